@@ -1,0 +1,403 @@
+/*
+ * cim22_cuda.h - C ABI of the B200 (sm_100a) execution backend for the
+ * software-simulated CIM22 path.
+ *
+ * Plain C types only: pointers, sizes, status integers and caller-owned error
+ * buffers. No exceptions cross this boundary. Every entry point that can fail
+ * returns 0 on success and nonzero on failure; when an error buffer is given,
+ * the diagnostic is copied into it NUL-terminated and truncated to the
+ * capacity, the same convention as the reference's copyError
+ * (runtime/Runtime.cpp:64-71).
+ *
+ * Three levels are exposed:
+ *   1. The transaction executor, a drop-in for the reference's CIMRunner
+ *      interface (include/CIM22/Execution/CIMRunner.h:75-154).
+ *   2. The tile dispatch ABI that compiled model libraries call
+ *      (_mlir_ciface_cim22_dispatch*, runtime/include/Session.h:52-66), routed
+ *      to a CUDA session instead of the software runner.
+ *   3. Layer-level entry points over device memory, which run whole CIM layers
+ *      (every column, every 16-lane N tile and 64-element K tile) in a few
+ *      launches. These replace the compiler-emitted Host glue around the
+ *      tile calls (lib/Conversion/LinalgToCIM/Passes.cpp:760-857,2304-2476).
+ */
+#ifndef CIM22_CUDA_H
+#define CIM22_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CIM22_CUDA_ABI_VERSION 1
+
+/* Crossbar geometry of target profile cim22-4x5-v1
+ * (include/CIM22/Execution/CIMRunner.h:19-22). */
+#define CIM22_TILE_K 64
+#define CIM22_TILE_N 16
+#define CIM22_CACHE_ROWS 8
+#define CIM22_MACRO_SLOTS 40
+
+/* ------------------------------------------------------------------------ */
+/* Transaction description. Field-for-field the data of
+ * cim22::execution::CIMTransaction (include/CIM22/Execution/CIMExecutable.h:21-148);
+ * the board-only `resource` string and flit stream are not needed to execute. */
+
+typedef enum cim22_data_type {
+  CIM22_DATA_INT8 = 0,
+  CIM22_DATA_BF16 = 1
+} cim22_data_type;
+
+/* Same order as CIMPacketKind (CIMExecutable.h:25-33). */
+typedef enum cim22_packet_kind {
+  CIM22_PACKET_CONTROL = 0,
+  CIM22_PACKET_WEIGHT = 1,
+  CIM22_PACKET_WEIGHT_EXPONENT = 2,
+  CIM22_PACKET_WORK = 3,
+  CIM22_PACKET_INPUT_CACHE_WRITE = 4,
+  CIM22_PACKET_RETURN_ROUTE = 5,
+  CIM22_PACKET_OUTPUT_CACHE_READ = 6
+} cim22_packet_kind;
+
+/* Same order as BF16Compensation (include/CIM22/Execution/BF16Compensation.h:8). */
+typedef enum cim22_bf16_compensation {
+  CIM22_BF16_NONE = 0,
+  CIM22_BF16_LEGACY = 1,
+  CIM22_BF16_SIGN_SPLIT = 2
+} cim22_bf16_compensation;
+
+typedef struct cim22_frame_packet {
+  int32_t kind; /* cim22_packet_kind */
+  int32_t route[6];
+  int64_t group_id;
+  int64_t work_id;
+  int64_t macro_slot;
+  int64_t cache_address;
+  int32_t test_core[3];
+  int32_t data_type; /* cim22_data_type */
+} cim22_frame_packet;
+
+/* StaticWeightSection: values is lane-major [16][64]; exponents holds one
+ * prealigned exponent per output lane (BF16 only). words are the board words,
+ * compared for weight identity only. */
+typedef struct cim22_static_weight {
+  int64_t group_id;
+  int64_t work_id;
+  int64_t core_slot;
+  int64_t macro_slot;
+  int32_t route[6];
+  const int32_t *words;
+  int64_t num_words;
+  int8_t values[16 * 64];
+  uint8_t exponents[16];
+  int32_t data_type;
+} cim22_static_weight;
+
+typedef struct cim22_input_binding {
+  int64_t group_id;
+  int64_t work_id;
+  int64_t macro_slot;
+  int64_t input_slot;
+  int32_t data_type;
+  int64_t input_cache_address;
+} cim22_input_binding;
+
+typedef struct cim22_readback_binding {
+  int64_t group_id;
+  int64_t work_id;
+  int64_t macro_slot;
+  int64_t output_cache_address;
+  int32_t route[6];
+  int32_t test_core[3];
+  int32_t data_type;
+} cim22_readback_binding;
+
+typedef struct cim22_work {
+  int64_t work_id;
+  int64_t core_slot;
+  int64_t macro_slot;
+  int32_t route[6];
+} cim22_work;
+
+typedef struct cim22_group {
+  int64_t group_id;
+  const cim22_work *works;
+  int64_t num_works;
+} cim22_group;
+
+typedef struct cim22_transaction {
+  const char *target_profile;
+  int64_t target_profile_version;
+  int64_t execution_plan_version;
+  const cim22_group *groups;
+  int64_t num_groups;
+  const cim22_static_weight *weights;
+  int64_t num_weights;
+  const cim22_frame_packet *packets;
+  int64_t num_packets;
+  const cim22_input_binding *inputs;
+  int64_t num_inputs;
+  const cim22_readback_binding *readbacks;
+  int64_t num_readbacks;
+} cim22_transaction;
+
+/* Trace events, same kinds and fields as CIMTraceEvent (CIMRunner.h:46-73). */
+typedef enum cim22_trace_kind {
+  CIM22_TRACE_BEGIN_RUN = 0,
+  CIM22_TRACE_CONFIGURE_WEIGHT = 1,
+  CIM22_TRACE_CONFIGURE_INPUT = 2,
+  CIM22_TRACE_SELECT_MACRO = 3,
+  CIM22_TRACE_START_WORK = 4,
+  CIM22_TRACE_CONFIGURE_RETURN_ROUTE = 5,
+  CIM22_TRACE_READ_OUTPUT = 6,
+  CIM22_TRACE_COMPLETE = 7,
+  CIM22_TRACE_ERROR = 8
+} cim22_trace_kind;
+
+typedef struct cim22_trace_event {
+  uint64_t sequence;
+  int32_t kind;
+  int64_t group_id;
+  int64_t work_id;
+  int64_t macro_slot;
+  int64_t packet_index;
+  int64_t cache_row_or_address;
+} cim22_trace_event;
+
+typedef void (*cim22_trace_callback)(void *context,
+                                     const cim22_trace_event *event);
+
+/* ------------------------------------------------------------------------ */
+/* 1. Transaction executor (replaces CIMSoftwareRunner behind CIMRunner,
+ *    include/CIM22/Execution/CIMRunner.h:75-154, lib/Execution/CIMSoftwareRunner.cpp). */
+
+typedef struct cim22_cuda_runner cim22_cuda_runner;
+typedef struct cim22_cuda_plan cim22_cuda_plan;
+
+/* Executor context on one CUDA device. It owns the weight catalog (exact
+ * payload interning, WeightResidency.h:28-50), the 40-slot residency table
+ * with its write/hit counters (WeightResidency.h:59-92) and the device copies
+ * of every interned weight tile. Calls on one runner must be serialized by the
+ * caller, as a Session serializes its runner (runtime/Runtime.cpp:297). */
+cim22_cuda_runner *cim22_cuda_runner_create(int device, char *error,
+                                            size_t error_capacity);
+void cim22_cuda_runner_destroy(cim22_cuda_runner *runner);
+
+/* Resolve bindings, waves and readback packets once
+ * (CIMSoftwareRunner::Plan, CIMSoftwareRunner.cpp:211-287) and upload the
+ * transaction's weight tiles. The transaction is copied; the caller may free
+ * it afterwards. batch_readbacks selects the batched-wave plan used by the
+ * session dispatch (runtime/Runtime.cpp:204). */
+cim22_cuda_plan *cim22_cuda_plan_create(cim22_cuda_runner *runner,
+                                        const cim22_transaction *transaction,
+                                        int batch_readbacks, char *error,
+                                        size_t error_capacity);
+void cim22_cuda_plan_destroy(cim22_cuda_plan *plan);
+
+/* Execute one transaction synchronously (CIMSoftwareRunner::run,
+ * CIMSoftwareRunner.cpp:289-482). inputs[i] is a host row of 64 int8 or 64
+ * raw BF16 (uint16) values in dynamic-input binding order; outputs[i] is a
+ * host row of 16 int32 or 16 uint16 values in readback binding order. Rows may
+ * alias one another; a row read after an earlier wave published into the same
+ * bytes sees the published values, as on the CPU. With use_residency, weights
+ * are matched per physical slot and the slots are cleared on failure
+ * (CIMRunner.h:133-145). Returns 0 or 1; outputs may be partially written on
+ * failure (CIMRunner.h:79-80). */
+int cim22_cuda_runner_run(cim22_cuda_runner *runner,
+                          const cim22_cuda_plan *plan,
+                          int32_t bf16_compensation, const void *const *inputs,
+                          int64_t num_inputs, void *const *outputs,
+                          int64_t num_outputs, int use_residency,
+                          cim22_trace_callback trace, void *trace_context,
+                          char *error, size_t error_capacity);
+
+/* Residency counters (CIMWeightStats, WeightResidency.h:52-57). */
+void cim22_cuda_runner_weight_stats(const cim22_cuda_runner *runner,
+                                    uint64_t *writes, uint64_t *hits);
+void cim22_cuda_runner_clear_residency(cim22_cuda_runner *runner);
+
+/* ------------------------------------------------------------------------ */
+/* 2. Session and the tile dispatch ABI of compiled model libraries.
+ *
+ * A CUDA session holds the model's transactions in id order (what
+ * cim22_session_load_shared decodes from the model artifact,
+ * runtime/Runtime.cpp:73-114) and executes them on one runner. Binding it to
+ * the calling thread routes the four _mlir_ciface_cim22_dispatch* symbols to
+ * it, as cim22_session_invoke binds activeSession (runtime/Runtime.cpp:333-336). */
+
+typedef struct cim22_cuda_session cim22_cuda_session;
+
+cim22_cuda_session *cim22_cuda_session_create(int device, char *error,
+                                              size_t error_capacity);
+void cim22_cuda_session_destroy(cim22_cuda_session *session);
+/* Appends a transaction; its id is the previous transaction count. kernel_name
+ * prefixes runner errors as "kernel: message" (runtime/Runtime.cpp:215-217). */
+int64_t cim22_cuda_session_add_transaction(cim22_cuda_session *session,
+                                           const cim22_transaction *transaction,
+                                           const char *kernel_name, char *error,
+                                           size_t error_capacity);
+int64_t cim22_cuda_session_num_transactions(const cim22_cuda_session *session);
+/* Starts an invocation on the calling thread: clears the error and the
+ * dispatch counter and makes the session the target of the dispatch symbols.
+ * end_invoke unbinds it, clears residency after an error
+ * (runtime/Runtime.cpp:337-338) and returns 0 when no dispatch failed. */
+void cim22_cuda_session_begin_invoke(cim22_cuda_session *session);
+int cim22_cuda_session_end_invoke(cim22_cuda_session *session);
+uint64_t cim22_cuda_session_dispatch_count(const cim22_cuda_session *session);
+/* Borrowed; valid until the next call on the session. */
+const char *cim22_cuda_session_error(const cim22_cuda_session *session);
+
+/* MLIR ranked memref descriptor of rank 2 (StridedMemRefType<T, 2>). */
+typedef struct cim22_memref2d {
+  void *allocated;
+  void *aligned;
+  int64_t offset;
+  int64_t sizes[2];
+  int64_t strides[2];
+} cim22_memref2d;
+
+/* Generated model code calls these with [R,64] input and [R,16] output
+ * memrefs (runtime/Runtime.cpp:221-247). Errors land in the bound session. */
+void _mlir_ciface_cim22_dispatch(int64_t id, cim22_memref2d *input,
+                                 cim22_memref2d *output);
+void _mlir_ciface_cim22_dispatch_sign_split(int64_t id, cim22_memref2d *input,
+                                            cim22_memref2d *output);
+void _mlir_ciface_cim22_dispatch_legacy(int64_t id, cim22_memref2d *input,
+                                        cim22_memref2d *output);
+void _mlir_ciface_cim22_dispatch_int8(int64_t id, cim22_memref2d *input,
+                                      cim22_memref2d *output);
+
+/* ------------------------------------------------------------------------ */
+/* 3. Layer level, device memory, stream ordered.
+ *
+ * A CIM layer is a contraction y[m, n] = sum_k W[n, k] x[m, k] executed as the
+ * compiler tiles it: 16-lane N tiles, 64-element K tiles with zero padding
+ * (Passes.cpp:760-826), one crossbar Work per (column m, N tile, K tile).
+ *
+ * Status words: kernels OR error bits (CIM22_STATUS_*) into a caller-owned
+ * device int32. The word is read after the stream is synchronized; the
+ * message of each bit is returned by cim22_cuda_status_message. */
+
+#define CIM22_STATUS_INPUT_NOT_FINITE 0x1   /* NaN/Inf reached a BF16 tile input */
+#define CIM22_STATUS_TILE_OVERFLOW 0x2      /* compensated tile exceeds BF16 */
+#define CIM22_STATUS_I21_RANGE 0x4          /* INT8 partial outside signed i21 */
+#define CIM22_STATUS_NORMALIZATION 0x8      /* sign-split prealign invariant broken */
+#define CIM22_STATUS_BAD_ARGUMENT 0x10      /* launch-time argument check failed */
+
+const char *cim22_cuda_status_message(int32_t status);
+
+typedef struct cim22_cuda_layer cim22_cuda_layer;
+
+/* BF16 sign-split weights. weight is a host f32 [n, k] matrix (row = output
+ * lane, k in the reduction order of the lowered op). Per Passes.cpp:2304-2476
+ * the weights are split into Wp = max(W, 0) and Wn = max(-W, 0), rounded to
+ * BF16 with round-to-nearest-even and prealigned per (16-lane, 64-K) tile and
+ * lane (BF16Support.cpp:56-70), then kept resident in device memory.
+ * Non-finite weights are rejected ("BF16 correction requires finite fixed
+ * weights", Passes.cpp:2349-2352). */
+cim22_cuda_layer *cim22_cuda_layer_create_bf16(int device, const float *weight,
+                                               int64_t n, int64_t k,
+                                               char *error,
+                                               size_t error_capacity);
+
+/* INT8 weights, host int8 [n, k]. The per-(lane, K tile) signed-i21 range
+ * proof over every int8 input (Passes.cpp:592-627) is evaluated at creation;
+ * cim22_cuda_layer_range_safe reports it. Proven layers accumulate the whole
+ * K range exactly in int32; unproven layers run the checked per-tile kernel
+ * that reports CIM22_STATUS_I21_RANGE. */
+cim22_cuda_layer *cim22_cuda_layer_create_int8(int device, const int8_t *weight,
+                                               int64_t n, int64_t k,
+                                               char *error,
+                                               size_t error_capacity);
+void cim22_cuda_layer_destroy(cim22_cuda_layer *layer);
+int cim22_cuda_layer_range_safe(const cim22_cuda_layer *layer);
+int64_t cim22_cuda_layer_n(const cim22_cuda_layer *layer);
+int64_t cim22_cuda_layer_k(const cim22_cuda_layer *layer);
+
+/* Epilogue activations fused into the layer kernel. */
+#define CIM22_ACT_NONE 0
+#define CIM22_ACT_RELU 1
+#define CIM22_ACT_GELU 2
+
+/* Gather descriptor of the K x columns operand. Linear: x is [m, k] row-major.
+ * Conv (im2col, Passes.cpp:1087-1385): x is an image batch; column m =
+ * (n, oh, ow), K index = c*kh*kw + i*kw + j (the FCHW weight order), zero
+ * padding inside 64-element groups. */
+#define CIM22_GATHER_ROWS 0
+#define CIM22_GATHER_CONV_NCHW 1
+#define CIM22_GATHER_CONV_NHWC 2
+
+typedef struct cim22_gather {
+  int32_t kind;
+  int32_t batch, channels, height, width; /* image geometry (conv only) */
+  int32_t kernel_h, kernel_w, stride_h, stride_w, pad_h, pad_w;
+  int32_t out_h, out_w;
+} cim22_gather;
+
+/* Scratch bytes needed by cim22_cuda_layer_forward_bf16 for m columns. */
+size_t cim22_cuda_layer_workspace_bf16(const cim22_cuda_layer *layer,
+                                       int64_t m, int32_t branches);
+
+/* BF16 sign-split layer: activation split into xp/xn, RNE to BF16, per-64
+ * group normalisation and prealignment (BF16Compensation.cpp:84-137), one
+ * 64x16 crossbar dot per (column, lane tile, K tile) with the per-tile
+ * truncating converter and binary64-exact scale recovery
+ * (BF16Compensation.cpp:33-51,149-164), f32 K accumulation in tile order,
+ * BF16 rounding when more than one K tile, branch merge
+ * ((pp - pn) - np) + nn in f32 (Passes.cpp:2405-2416), then + bias and the
+ * activation. branches is 4, or 2 when the input is known nonnegative
+ * (the xn branches are exactly +0 then). y is f32 [m, n] row-major; for conv
+ * gathers that is NHWC. */
+int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
+                                  const cim22_gather *gather, int64_t m,
+                                  const float *bias, int32_t activation,
+                                  int32_t branches, float *y, void *workspace,
+                                  size_t workspace_bytes, int32_t *status,
+                                  void *stream);
+
+/* INT8 layer: y[m, n] = sum over K tiles of the signed-i21 tile results,
+ * accumulated in wrapping int32 (Passes.cpp:1054-1059). x is int8 [m, k]. */
+int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,
+                                  const int8_t *x, int64_t m, int32_t *y,
+                                  int32_t *status, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Host glue the compiler emits around CIM layers (upstream Linalg lowering,
+ * lib/Compiler/Pipelines.cpp:61-72). All f32, device memory, NHWC images. */
+
+int cim22_cuda_relu(const float *x, float *y, int64_t count, void *stream);
+int cim22_cuda_add(const float *a, const float *b, float *y, int64_t count,
+                   int32_t activation, void *stream);
+int cim22_cuda_gelu(const float *x, float *y, int64_t count, void *stream);
+/* Max/average pooling over an NHWC batch (no padding when pad = 0; average
+ * pooling divides by the full window, count_include_pad semantics). */
+int cim22_cuda_maxpool2d_nhwc(const float *x, float *y, int32_t n, int32_t h,
+                              int32_t w, int32_t c, int32_t kernel,
+                              int32_t stride, int32_t pad, void *stream);
+int cim22_cuda_avgpool2d_nhwc(const float *x, float *y, int32_t n, int32_t h,
+                              int32_t w, int32_t c, int32_t kernel,
+                              int32_t stride, void *stream);
+/* Mean over H and W of an NHWC batch -> [n, c]. */
+int cim22_cuda_global_avgpool_nhwc(const float *x, float *y, int32_t n,
+                                   int32_t h, int32_t w, int32_t c,
+                                   void *stream);
+/* Per-channel affine y = x * scale[c] + shift[c] (+ activation), NHWC. */
+int cim22_cuda_channel_affine_nhwc(const float *x, const float *scale,
+                                   const float *shift, float *y, int64_t rows,
+                                   int32_t c, int32_t activation, void *stream);
+/* Row softmax over the last dimension of [rows, cols]. */
+int cim22_cuda_softmax(const float *x, float *y, int64_t rows, int32_t cols,
+                       void *stream);
+/* NHWC [n, h, w, c] -> NCHW-flattened [n, c*h*w] (torch.flatten order). */
+int cim22_cuda_nhwc_to_nchw(const float *x, float *y, int32_t n, int32_t h,
+                            int32_t w, int32_t c, void *stream);
+/* NCHW -> NHWC. */
+int cim22_cuda_nchw_to_nhwc(const float *x, float *y, int32_t n, int32_t c,
+                            int32_t h, int32_t w, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CIM22_CUDA_H */
