@@ -284,8 +284,18 @@ void _mlir_ciface_cim22_dispatch_int8(int64_t id, cim22_memref2d *input,
 #define CIM22_STATUS_I21_RANGE 0x4          /* INT8 partial outside signed i21 */
 #define CIM22_STATUS_NORMALIZATION 0x8      /* sign-split prealign invariant broken */
 #define CIM22_STATUS_BAD_ARGUMENT 0x10      /* launch-time argument check failed */
+#define CIM22_STATUS_NEGATIVE_INPUT 0x20    /* negative value in a nonnegative (2-branch) layer */
 
+/* Message of the lowest set status bit ("" for 0). */
 const char *cim22_cuda_status_message(int32_t status);
+
+/* Diagnostic of the last failing layer or glue call on this thread. */
+const char *cim22_cuda_last_error(void);
+
+/* sizeof of each structure above, in declaration order: frame_packet,
+ * static_weight, input_binding, readback_binding, work, group, transaction,
+ * trace_event, memref2d, gather. Returns the number of entries written. */
+int cim22_cuda_abi_sizes(int64_t *sizes, int capacity);
 
 typedef struct cim22_cuda_layer cim22_cuda_layer;
 
@@ -356,10 +366,15 @@ int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
                                   size_t workspace_bytes, int32_t *status,
                                   void *stream);
 
+/* Scratch bytes needed by cim22_cuda_layer_forward_int8 for m columns. */
+size_t cim22_cuda_layer_workspace_int8(const cim22_cuda_layer *layer,
+                                       int64_t m);
+
 /* INT8 layer: y[m, n] = sum over K tiles of the signed-i21 tile results,
  * accumulated in wrapping int32 (Passes.cpp:1054-1059). x is int8 [m, k]. */
 int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,
                                   const int8_t *x, int64_t m, int32_t *y,
+                                  void *workspace, size_t workspace_bytes,
                                   int32_t *status, void *stream);
 
 /* ------------------------------------------------------------------------ */

@@ -1,0 +1,50 @@
+// cim_internal.h - shared host-side definitions of the CUDA backend.
+#pragma once
+
+#include "../../include/cim22_cuda.h"
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+namespace cim {
+
+// Thread-local diagnostic of the last failing C-ABI call.
+void set_last_error(const std::string &message);
+const std::string &last_error();
+
+// Copy a message into a caller buffer (truncating, NUL-terminated), the
+// convention of runtime/Runtime.cpp:64-71.
+void copy_error(const std::string &message, char *buffer, size_t capacity);
+
+inline bool cuda_ok(cudaError_t e, const char *what) {
+  if (e == cudaSuccess)
+    return true;
+  set_last_error(std::string(what) + ": " + cudaGetErrorString(e));
+  return false;
+}
+
+inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+// Lane padding of resident weights: a multiple of every N tile width the
+// layer kernels use.
+constexpr int64_t kLanePad = 128;
+// Column padding of prepared activations: a multiple of the M tile.
+constexpr int64_t kColumnPad = 128;
+
+} // namespace cim
+
+// Prepared CIM layer weights resident in device memory.
+struct cim22_cuda_layer {
+  int device = 0;
+  bool bf16 = false;
+  int64_t n = 0, k = 0;         // logical output lanes and reduction length
+  int64_t n_pad = 0, k_pad = 0; // padded to kLanePad and 64
+  int64_t tiles = 0;            // K tiles (k_pad / 64)
+  bool range_safe = true;       // INT8 range proof result
+  // BF16: int8 mantissas [2][n_pad][k_pad] (Wp then Wn) and int32 lane
+  // exponents [2][tiles][n_pad]. INT8: int8 [n_pad][k_pad].
+  int8_t *weights = nullptr;
+  int32_t *exponents = nullptr;
+};

@@ -1,0 +1,28 @@
+// gemm_tc.h - tensor-core (tcgen05) CIM contraction kernels for sm_100a.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace cim::tc {
+
+// True when the tcgen05 kernels are compiled in and the current device is an
+// sm_100 part.
+bool signsplit_available();
+bool int8_available();
+
+// Launch the sign-split contraction over prepared operands (layout of
+// layers.cu). Returns false when the shape is not handled by the tensor-core
+// kernel, in which case nothing was launched.
+bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad,
+                      const int8_t *B, const int32_t *exB, int64_t n_pad,
+                      int64_t k_pad, int T, int64_t M, int64_t N,
+                      const float *bias, int act, int act_branches, float *y,
+                      int32_t *status, cudaStream_t stream);
+
+// INT8 contraction with whole-K int32 accumulation for range-proven layers.
+bool launch_int8(const int8_t *A, int64_t m_pad, const int8_t *B,
+                 int64_t n_pad, int64_t k_pad, int T, int64_t M, int64_t N,
+                 int32_t *y, int32_t *status, cudaStream_t stream);
+
+} // namespace cim::tc

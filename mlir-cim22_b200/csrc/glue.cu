@@ -1,0 +1,335 @@
+// glue.cu - the f32 Host glue the compiler emits around CIM layers
+// (ReLU, residual add, GELU, pooling, batch-norm affine, softmax, layout),
+// lowered by the reference through upstream Linalg to loops
+// (lib/Compiler/Pipelines.cpp:61-72). Memory-bound: grid-stride loops with
+// 128-bit accesses where the shape allows, images in NHWC.
+#include "cim_internal.h"
+
+#include <algorithm>
+#include <cfloat>
+
+namespace cim {
+namespace {
+
+unsigned grid_for(int64_t work, int threads = 256) {
+  const int64_t blocks = (work + threads - 1) / threads;
+  return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(blocks, 148 * 16)));
+}
+
+__device__ __forceinline__ float act_fn(float v, int act) {
+  if (act == CIM22_ACT_RELU)
+    return v > 0.0f ? v : 0.0f;
+  if (act == CIM22_ACT_GELU)
+    return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  return v;
+}
+
+template <int kAct>
+__global__ void unary_kernel(const float *__restrict__ x, float *__restrict__ y,
+                             int64_t count) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t vec = count / 4;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  if (aligned) {
+    for (int64_t i = i0; i < vec; i += stride) {
+      float4 v = reinterpret_cast<const float4 *>(x)[i];
+      v.x = act_fn(v.x, kAct);
+      v.y = act_fn(v.y, kAct);
+      v.z = act_fn(v.z, kAct);
+      v.w = act_fn(v.w, kAct);
+      reinterpret_cast<float4 *>(y)[i] = v;
+    }
+    for (int64_t i = vec * 4 + i0; i < count; i += stride)
+      y[i] = act_fn(x[i], kAct);
+  } else {
+    for (int64_t i = i0; i < count; i += stride)
+      y[i] = act_fn(x[i], kAct);
+  }
+}
+
+__global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b,
+                           float *__restrict__ y, int64_t count, int act) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < count; i += stride)
+    y[i] = act_fn(__fadd_rn(a[i], b[i]), act);
+}
+
+__global__ void maxpool_kernel(const float *__restrict__ x, float *__restrict__ y,
+                               int n, int h, int w, int c, int k, int s, int pad,
+                               int oh, int ow) {
+  const int64_t total = static_cast<int64_t>(n) * oh * ow * c;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < total; i += stride) {
+    const int ch = static_cast<int>(i % c);
+    int64_t r = i / c;
+    const int ox = static_cast<int>(r % ow);
+    r /= ow;
+    const int oy = static_cast<int>(r % oh);
+    const int b = static_cast<int>(r / oh);
+    float m = -FLT_MAX;
+    bool any = false;
+    for (int dy = 0; dy < k; ++dy)
+      for (int dx = 0; dx < k; ++dx) {
+        const int iy = oy * s - pad + dy, ix = ox * s - pad + dx;
+        if (iy < 0 || iy >= h || ix < 0 || ix >= w)
+          continue;
+        const float v = x[((static_cast<int64_t>(b) * h + iy) * w + ix) * c + ch];
+        // NaN propagates like torch.max_pool2d.
+        if (!any || v > m || v != v) {
+          m = v;
+          any = true;
+        }
+      }
+    y[i] = m;
+  }
+}
+
+__global__ void avgpool_kernel(const float *__restrict__ x, float *__restrict__ y,
+                               int n, int h, int w, int c, int k, int s, int oh,
+                               int ow) {
+  const int64_t total = static_cast<int64_t>(n) * oh * ow * c;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const float inv = 1.0f / static_cast<float>(k * k);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < total; i += stride) {
+    const int ch = static_cast<int>(i % c);
+    int64_t r = i / c;
+    const int ox = static_cast<int>(r % ow);
+    r /= ow;
+    const int oy = static_cast<int>(r % oh);
+    const int b = static_cast<int>(r / oh);
+    float sum = 0.0f;
+    for (int dy = 0; dy < k; ++dy)
+      for (int dx = 0; dx < k; ++dx)
+        sum += x[((static_cast<int64_t>(b) * h + oy * s + dy) * w + ox * s + dx) * c + ch];
+    y[i] = sum * inv;
+  }
+}
+
+// Mean over the spatial plane: one block per (image, 32-channel group),
+// warps stride the plane, shared-memory reduction.
+__global__ void gap_kernel(const float *__restrict__ x, float *__restrict__ y,
+                           int h, int w, int c) {
+  const int b = blockIdx.x;
+  const int c0 = blockIdx.y * 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int warps = blockDim.x >> 5;
+  const int ch = c0 + lane;
+  const int plane = h * w;
+  float sum = 0.0f;
+  if (ch < c)
+    for (int p = warp; p < plane; p += warps)
+      sum += x[(static_cast<int64_t>(b) * plane + p) * c + ch];
+  __shared__ float part[32][33];
+  part[warp][lane] = sum;
+  __syncthreads();
+  if (warp == 0) {
+    float total = 0.0f;
+    for (int i = 0; i < warps; ++i)
+      total += part[i][lane];
+    if (ch < c)
+      y[static_cast<int64_t>(b) * c + ch] = total / static_cast<float>(plane);
+  }
+}
+
+__global__ void affine_kernel(const float *__restrict__ x, const float *__restrict__ scale,
+                              const float *__restrict__ shift, float *__restrict__ y,
+                              int64_t rows, int c, int act) {
+  const int64_t total = rows * c;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < total; i += stride) {
+    const int ch = static_cast<int>(i % c);
+    y[i] = act_fn(fmaf(x[i], scale[ch], shift[ch]), act);
+  }
+}
+
+// One warp per row.
+__global__ void softmax_kernel(const float *__restrict__ x, float *__restrict__ y,
+                               int64_t rows, int cols) {
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows)
+    return;
+  const float *in = x + row * cols;
+  float *out = y + row * cols;
+  float m = -INFINITY;
+  for (int i = lane; i < cols; i += 32)
+    m = fmaxf(m, in[i]);
+  for (int o = 16; o; o >>= 1)
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float s = 0.0f;
+  for (int i = lane; i < cols; i += 32)
+    s += expf(in[i] - m);
+  for (int o = 16; o; o >>= 1)
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+  for (int i = lane; i < cols; i += 32)
+    out[i] = expf(in[i] - m) / s;
+}
+
+__global__ void nhwc_to_nchw_kernel(const float *__restrict__ x, float *__restrict__ y,
+                                    int n, int h, int w, int c) {
+  const int64_t total = static_cast<int64_t>(n) * h * w * c;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < total; i += stride) {
+    // i indexes the NCHW output.
+    const int xw = static_cast<int>(i % w);
+    int64_t r = i / w;
+    const int xh = static_cast<int>(r % h);
+    r /= h;
+    const int ch = static_cast<int>(r % c);
+    const int b = static_cast<int>(r / c);
+    y[i] = x[((static_cast<int64_t>(b) * h + xh) * w + xw) * c + ch];
+  }
+}
+
+__global__ void nchw_to_nhwc_kernel(const float *__restrict__ x, float *__restrict__ y,
+                                    int n, int c, int h, int w) {
+  const int64_t total = static_cast<int64_t>(n) * h * w * c;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < total; i += stride) {
+    // i indexes the NHWC output.
+    const int ch = static_cast<int>(i % c);
+    int64_t r = i / c;
+    const int xw = static_cast<int>(r % w);
+    r /= w;
+    const int xh = static_cast<int>(r % h);
+    const int b = static_cast<int>(r / h);
+    y[i] = x[((static_cast<int64_t>(b) * c + ch) * h + xh) * w + xw];
+  }
+}
+
+int launched(const char *what) {
+  return cuda_ok(cudaGetLastError(), what) ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+}
+
+int bad(const char *what) {
+  set_last_error(std::string("invalid arguments to ") + what);
+  return CIM22_STATUS_BAD_ARGUMENT;
+}
+
+} // namespace
+} // namespace cim
+
+using namespace cim;
+
+extern "C" {
+
+int cim22_cuda_relu(const float *x, float *y, int64_t count, void *stream) {
+  if (!x || !y || count < 0)
+    return bad("cim22_cuda_relu");
+  if (count == 0)
+    return 0;
+  unary_kernel<CIM22_ACT_RELU><<<grid_for((count + 3) / 4), 256, 0,
+                                 static_cast<cudaStream_t>(stream)>>>(x, y, count);
+  return launched("relu");
+}
+
+int cim22_cuda_gelu(const float *x, float *y, int64_t count, void *stream) {
+  if (!x || !y || count < 0)
+    return bad("cim22_cuda_gelu");
+  if (count == 0)
+    return 0;
+  unary_kernel<CIM22_ACT_GELU><<<grid_for((count + 3) / 4), 256, 0,
+                                 static_cast<cudaStream_t>(stream)>>>(x, y, count);
+  return launched("gelu");
+}
+
+int cim22_cuda_add(const float *a, const float *b, float *y, int64_t count,
+                   int32_t activation, void *stream) {
+  if (!a || !b || !y || count < 0 || activation < 0 || activation > 2)
+    return bad("cim22_cuda_add");
+  if (count == 0)
+    return 0;
+  add_kernel<<<grid_for(count), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      a, b, y, count, activation);
+  return launched("add");
+}
+
+int cim22_cuda_maxpool2d_nhwc(const float *x, float *y, int32_t n, int32_t h,
+                              int32_t w, int32_t c, int32_t kernel,
+                              int32_t stride, int32_t pad, void *stream) {
+  if (!x || !y || n <= 0 || h <= 0 || w <= 0 || c <= 0 || kernel <= 0 ||
+      stride <= 0 || pad < 0 || 2 * pad > kernel)
+    return bad("cim22_cuda_maxpool2d_nhwc");
+  const int oh = (h + 2 * pad - kernel) / stride + 1;
+  const int ow = (w + 2 * pad - kernel) / stride + 1;
+  if (oh <= 0 || ow <= 0)
+    return bad("cim22_cuda_maxpool2d_nhwc");
+  maxpool_kernel<<<grid_for(static_cast<int64_t>(n) * oh * ow * c), 256, 0,
+                   static_cast<cudaStream_t>(stream)>>>(x, y, n, h, w, c, kernel,
+                                                        stride, pad, oh, ow);
+  return launched("maxpool2d");
+}
+
+int cim22_cuda_avgpool2d_nhwc(const float *x, float *y, int32_t n, int32_t h,
+                              int32_t w, int32_t c, int32_t kernel,
+                              int32_t stride, void *stream) {
+  if (!x || !y || n <= 0 || h <= 0 || w <= 0 || c <= 0 || kernel <= 0 ||
+      stride <= 0 || kernel > h || kernel > w)
+    return bad("cim22_cuda_avgpool2d_nhwc");
+  const int oh = (h - kernel) / stride + 1, ow = (w - kernel) / stride + 1;
+  avgpool_kernel<<<grid_for(static_cast<int64_t>(n) * oh * ow * c), 256, 0,
+                   static_cast<cudaStream_t>(stream)>>>(x, y, n, h, w, c, kernel,
+                                                        stride, oh, ow);
+  return launched("avgpool2d");
+}
+
+int cim22_cuda_global_avgpool_nhwc(const float *x, float *y, int32_t n,
+                                   int32_t h, int32_t w, int32_t c,
+                                   void *stream) {
+  if (!x || !y || n <= 0 || h <= 0 || w <= 0 || c <= 0 || n > 65535 * 64)
+    return bad("cim22_cuda_global_avgpool_nhwc");
+  const dim3 grid(static_cast<unsigned>(n), static_cast<unsigned>((c + 31) / 32));
+  gap_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, h, w, c);
+  return launched("global_avgpool");
+}
+
+int cim22_cuda_channel_affine_nhwc(const float *x, const float *scale,
+                                   const float *shift, float *y, int64_t rows,
+                                   int32_t c, int32_t activation, void *stream) {
+  if (!x || !scale || !shift || !y || rows < 0 || c <= 0 || activation < 0 ||
+      activation > 2)
+    return bad("cim22_cuda_channel_affine_nhwc");
+  if (rows == 0)
+    return 0;
+  affine_kernel<<<grid_for(rows * c), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, scale, shift, y, rows, c, activation);
+  return launched("channel_affine");
+}
+
+int cim22_cuda_softmax(const float *x, float *y, int64_t rows, int32_t cols,
+                       void *stream) {
+  if (!x || !y || rows < 0 || cols <= 0)
+    return bad("cim22_cuda_softmax");
+  if (rows == 0)
+    return 0;
+  const unsigned blocks = static_cast<unsigned>((rows * 32 + 255) / 256);
+  softmax_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, rows, cols);
+  return launched("softmax");
+}
+
+int cim22_cuda_nhwc_to_nchw(const float *x, float *y, int32_t n, int32_t h,
+                            int32_t w, int32_t c, void *stream) {
+  if (!x || !y || n <= 0 || h <= 0 || w <= 0 || c <= 0)
+    return bad("cim22_cuda_nhwc_to_nchw");
+  nhwc_to_nchw_kernel<<<grid_for(static_cast<int64_t>(n) * h * w * c), 256, 0,
+                        static_cast<cudaStream_t>(stream)>>>(x, y, n, h, w, c);
+  return launched("nhwc_to_nchw");
+}
+
+int cim22_cuda_nchw_to_nhwc(const float *x, float *y, int32_t n, int32_t c,
+                            int32_t h, int32_t w, void *stream) {
+  if (!x || !y || n <= 0 || h <= 0 || w <= 0 || c <= 0)
+    return bad("cim22_cuda_nchw_to_nhwc");
+  nchw_to_nhwc_kernel<<<grid_for(static_cast<int64_t>(n) * h * w * c), 256, 0,
+                        static_cast<cudaStream_t>(stream)>>>(x, y, n, c, h, w);
+  return launched("nchw_to_nhwc");
+}
+
+} // extern "C"

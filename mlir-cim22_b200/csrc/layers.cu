@@ -1,0 +1,674 @@
+// layers.cu - CIM layers over device memory: weight preparation, the
+// activation prepare/im2col kernel and the CUDA-core contraction kernels.
+//
+// A CIM layer computes, for every column m and output lane n,
+//   BF16 sign-split: y = ((pp - pn) - np) + nn (+ bias, activation), where
+//     each branch is the f32 sum over 64-element K tiles, in tile order, of
+//     the restored tile values RNE_bf16(Q(p) * 2^(Ew + Ex - 266)), rounded to
+//     BF16 once more when there is more than one tile
+//     (lib/Conversion/LinalgToCIM/Passes.cpp:828-857,2304-2420 with
+//     lib/Execution/BF16Compensation.cpp:84-164);
+//   INT8: y = wrapping int32 sum of the signed-i21 tile partials
+//     (Passes.cpp:1054-1059, lib/Execution/CIMSoftwareRunner.cpp:406-420).
+//
+// Data layout in HBM (row-major, K innermost):
+//   prepared activations  int8 A[branch][m_pad][k_pad], int32 Ex[branch][T][m_pad]
+//   resident weights      int8 B[branch][n_pad][k_pad], int32 Ew[branch][T][n_pad]
+//   outputs               f32 / int32 y[m][n]
+#include "cim_internal.h"
+#include "cim_numeric.cuh"
+#include "gemm_tc.h"
+
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <vector>
+
+namespace cim {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+// ---------------------------------------------------------------------------
+// Gather of the K x columns operand (linear rows or conv im2col).
+
+__device__ __forceinline__ float gather_load(const float *__restrict__ x,
+                                             const cim22_gather &g, int64_t M,
+                                             int64_t K, int64_t m, int64_t k) {
+  if (m >= M || k >= K)
+    return 0.0f;
+  if (g.kind == CIM22_GATHER_ROWS)
+    return x[m * K + k];
+  const int ohw = g.out_h * g.out_w;
+  const int n = static_cast<int>(m / ohw);
+  const int r = static_cast<int>(m - static_cast<int64_t>(n) * ohw);
+  const int oh = r / g.out_w, ow = r - oh * g.out_w;
+  const int khw = g.kernel_h * g.kernel_w;
+  const int c = static_cast<int>(k / khw);
+  const int rk = static_cast<int>(k - static_cast<int64_t>(c) * khw);
+  const int i = rk / g.kernel_w, j = rk - i * g.kernel_w;
+  const int ih = oh * g.stride_h - g.pad_h + i;
+  const int iw = ow * g.stride_w - g.pad_w + j;
+  if (ih < 0 || ih >= g.height || iw < 0 || iw >= g.width)
+    return 0.0f; // explicit zero padding (tensor.pad)
+  if (g.kind == CIM22_GATHER_CONV_NCHW)
+    return x[((static_cast<int64_t>(n) * g.channels + c) * g.height + ih) *
+                 g.width + iw];
+  return x[((static_cast<int64_t>(n) * g.height + ih) * g.width + iw) *
+               g.channels + c];
+}
+
+// ---------------------------------------------------------------------------
+// Prepare: one warp per (column m, K tile t); lane l owns elements 2l, 2l+1.
+// Split x into xp/xn (Passes.cpp:2379-2399), RNE to BF16, then the
+// sign-split input preparation of prepareBF16Input (BF16Compensation.cpp:
+// 92-118): effective exponent of the group maximum, RNE scaling to put the
+// maximum in [1, 2), ExpPrealign at exponent 127. An all-zero group records
+// exponent 127 (its dots are zero, so any finite scale gives +0).
+template <int kActBranches>
+__global__ void __launch_bounds__(256)
+    prepare_kernel(const float *__restrict__ x, cim22_gather g, int64_t M,
+                   int64_t K, int T, int64_t m_pad, int64_t k_pad,
+                   int8_t *__restrict__ A, int32_t *__restrict__ ex,
+                   int32_t *status) {
+  const int64_t warp =
+      (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= m_pad * T)
+    return;
+  const int64_t m = warp / T;
+  const int t = static_cast<int>(warp - m * T);
+  const int64_t k0 = static_cast<int64_t>(t) * kTileK + 2 * lane;
+  float v[2] = {gather_load(x, g, M, K, m, k0), gather_load(x, g, M, K, m, k0 + 1)};
+  uint16_t bits[2][2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const float zero = 0.0f;
+    float p = v[e], n = zero;
+    if (kActBranches == 2) {
+      const bool negative = v[e] < zero;
+      p = negative ? zero : v[e];
+      n = negative ? -v[e] : zero;
+    }
+    p = (v[e] == zero) ? zero : p; // -0 becomes +0
+    bits[0][e] = f32_to_bf16(p);
+    bits[1][e] = f32_to_bf16(n);
+  }
+#pragma unroll
+  for (int b = 0; b < kActBranches; ++b) {
+    const uint16_t b0 = bits[b][0], b1 = bits[b][1];
+    const bool nonfinite =
+        ((b0 >> 7) & 0xff) == 0xff || ((b1 >> 7) & 0xff) == 0xff;
+    const bool any_nonfinite = __any_sync(kFull, nonfinite);
+    if (any_nonfinite && lane == 0)
+      atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
+    // A 2-branch layer asserts its input is nonnegative; the runtime check of
+    // prepareBF16Input (BF16Compensation.cpp:95-96) still applies.
+    const bool negative = ((b0 & 0x8000) && (b0 & 0x7fff)) || ((b1 & 0x8000) && (b1 & 0x7fff));
+    if (!any_nonfinite && __any_sync(kFull, negative) && lane == 0)
+      atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
+    const uint32_t mx = __reduce_max_sync(
+        kFull, static_cast<uint32_t>(max(b0 & 0x7fff, b1 & 0x7fff)));
+    int8_t a0 = 0, a1 = 0;
+    int exponent = 127;
+    if (mx != 0 && !any_nonfinite) {
+      exponent = effective_exponent(static_cast<uint16_t>(mx));
+      const int shift = 127 - exponent;
+      const uint16_t s0 = shift ? bf16_scalbn(b0 & 0x7fff, shift) : (b0 & 0x7fff);
+      const uint16_t s1 = shift ? bf16_scalbn(b1 & 0x7fff, shift) : (b1 & 0x7fff);
+      const uint32_t emax = __reduce_max_sync(
+          kFull, static_cast<uint32_t>(max((s0 >> 7) & 0xff, (s1 >> 7) & 0xff)));
+      a0 = prealign_element(s0, static_cast<int>(emax));
+      a1 = prealign_element(s1, static_cast<int>(emax));
+      if ((emax != 127 || a0 < 0 || a1 < 0))
+        atomicOr(status, CIM22_STATUS_NORMALIZATION);
+    }
+    uint16_t *row = reinterpret_cast<uint16_t *>(
+        A + (static_cast<int64_t>(b) * m_pad + m) * k_pad +
+        static_cast<int64_t>(t) * kTileK);
+    row[lane] = static_cast<uint16_t>(static_cast<uint8_t>(a0) |
+                                      (static_cast<uint16_t>(static_cast<uint8_t>(a1)) << 8));
+    if (lane == 0)
+      ex[(static_cast<int64_t>(b) * T + t) * m_pad + m] = exponent;
+  }
+}
+
+// 2^e as an exact f32 for e in [-149, 127].
+__device__ __forceinline__ float exp2i(int e) {
+  return e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23)
+                   : __uint_as_float(1u << (e + 149));
+}
+
+// Q(p) as an exact f32: the conversion is exact below 2^24 and clearing the
+// low 16 bits keeps the eight leading significant bits, truncating.
+__device__ __forceinline__ float trunc8f(int32_t p) {
+  const float f = __uint_as_float(static_cast<uint32_t>(p) | 0x4b000000u) - 8388608.0f;
+  return __uint_as_float(__float_as_uint(f) & 0xffff0000u);
+}
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  if (act == CIM22_ACT_RELU)
+    return v > 0.0f ? v : 0.0f;
+  if (act == CIM22_ACT_GELU)
+    return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Sign-split contraction on CUDA cores (dp4a). CTA tile 64 columns x 32
+// lanes, all branches. Thread (tr, tc) owns columns tr, tr + 32 and lanes
+// 4tc .. 4tc + 3.
+constexpr int kBM = 64, kBN = 32, kRowStride = 80;
+
+template <int kActBranches>
+__global__ void __launch_bounds__(256)
+    signsplit_simt_kernel(const int8_t *__restrict__ A,
+                          const int32_t *__restrict__ exA, int64_t m_pad,
+                          const int8_t *__restrict__ B,
+                          const int32_t *__restrict__ exB, int64_t n_pad,
+                          int64_t k_pad, int T, int64_t M, int64_t N,
+                          const float *__restrict__ bias, int act,
+                          float *__restrict__ y, int32_t *status) {
+  __shared__ __align__(16) int8_t As[kActBranches][kBM][kRowStride];
+  __shared__ __align__(16) int8_t Bs[2][kBN][kRowStride];
+  __shared__ int sExA[kActBranches][kBM];
+  __shared__ int sExB[2][kBN];
+  __shared__ int sFast;
+  const int tid = threadIdx.x;
+  const int tr = tid >> 3, tc = tid & 7;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * kBN;
+  float acc[kActBranches][2][2][4];
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a)
+#pragma unroll
+    for (int w = 0; w < 2; ++w)
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          acc[a][w][r][c] = 0.0f;
+
+  for (int t = 0; t < T; ++t) {
+    for (int i = tid; i < kActBranches * kBM * 4; i += 256) {
+      const int a = i / (kBM * 4), r = (i >> 2) % kBM, c = i & 3;
+      *reinterpret_cast<int4 *>(&As[a][r][c * 16]) = *reinterpret_cast<const int4 *>(
+          A + (static_cast<int64_t>(a) * m_pad + m0 + r) * k_pad +
+          static_cast<int64_t>(t) * kTileK + c * 16);
+    }
+    {
+      const int w = tid / (kBN * 4), r = (tid >> 2) % kBN, c = tid & 3;
+      *reinterpret_cast<int4 *>(&Bs[w][r][c * 16]) = *reinterpret_cast<const int4 *>(
+          B + (static_cast<int64_t>(w) * n_pad + n0 + r) * k_pad +
+          static_cast<int64_t>(t) * kTileK + c * 16);
+    }
+    if (tid < kActBranches * kBM)
+      sExA[tid / kBM][tid % kBM] =
+          exA[(static_cast<int64_t>(tid / kBM) * T + t) * m_pad + m0 + tid % kBM];
+    if (tid < 2 * kBN)
+      sExB[tid / kBN][tid % kBN] =
+          exB[(static_cast<int64_t>(tid / kBN) * T + t) * n_pad + n0 + tid % kBN];
+    __syncthreads();
+    if (tid < 32) {
+      int mnA = INT_MAX, mxA = INT_MIN, mnB = INT_MAX, mxB = INT_MIN;
+      for (int i = tid; i < kActBranches * kBM; i += 32) {
+        const int v = sExA[i / kBM][i % kBM];
+        mnA = min(mnA, v);
+        mxA = max(mxA, v);
+      }
+      for (int i = tid; i < 2 * kBN; i += 32) {
+        const int v = sExB[i / kBN][i % kBN];
+        mnB = min(mnB, v);
+        mxB = max(mxB, v);
+      }
+      mnA = __reduce_min_sync(kFull, mnA);
+      mxA = __reduce_max_sync(kFull, mxA);
+      mnB = __reduce_min_sync(kFull, mnB);
+      mxB = __reduce_max_sync(kFull, mxB);
+      if (tid == 0)
+        sFast = (mnA + mnB >= 140) && (mxA + mxB <= 374) && (mxA <= 240);
+    }
+    __syncthreads();
+    const bool fast = sFast != 0;
+    int p[kActBranches][2][2][4];
+#pragma unroll
+    for (int a = 0; a < kActBranches; ++a)
+#pragma unroll
+      for (int w = 0; w < 2; ++w)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            p[a][w][r][c] = 0;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      int4 av[kActBranches][2], bv[2][4];
+#pragma unroll
+      for (int a = 0; a < kActBranches; ++a)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+          av[a][r] = *reinterpret_cast<const int4 *>(&As[a][tr + 32 * r][kk * 16]);
+#pragma unroll
+      for (int w = 0; w < 2; ++w)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          bv[w][c] = *reinterpret_cast<const int4 *>(&Bs[w][tc * 4 + c][kk * 16]);
+#pragma unroll
+      for (int a = 0; a < kActBranches; ++a)
+#pragma unroll
+        for (int w = 0; w < 2; ++w)
+#pragma unroll
+          for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              int s = p[a][w][r][c];
+              s = __dp4a(av[a][r].x, bv[w][c].x, s);
+              s = __dp4a(av[a][r].y, bv[w][c].y, s);
+              s = __dp4a(av[a][r].z, bv[w][c].z, s);
+              s = __dp4a(av[a][r].w, bv[w][c].w, s);
+              p[a][w][r][c] = s;
+            }
+    }
+#pragma unroll
+    for (int a = 0; a < kActBranches; ++a)
+#pragma unroll
+      for (int w = 0; w < 2; ++w)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int ex = sExA[a][tr + 32 * r];
+            const int ew = sExB[w][tc * 4 + c];
+            if (fast) {
+              const float q = __fmul_rn(trunc8f(p[a][w][r][c]), exp2i(ex - 133));
+              acc[a][w][r][c] = fmaf(q, exp2i(ew - 133), acc[a][w][r][c]);
+            } else {
+              const uint16_t tile =
+                  signsplit_tile(static_cast<uint32_t>(p[a][w][r][c]), ew, ex);
+              if (tile == kBF16Inf)
+                atomicOr(status, CIM22_STATUS_TILE_OVERFLOW);
+              acc[a][w][r][c] = __fadd_rn(acc[a][w][r][c], bf16_to_f32(tile));
+            }
+          }
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int64_t row = m0 + tr + 32 * r;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int64_t lane = n0 + tc * 4 + c;
+      float br[kActBranches][2];
+#pragma unroll
+      for (int a = 0; a < kActBranches; ++a)
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          const float v = acc[a][w][r][c];
+          br[a][w] = T > 1 ? bf16_to_f32(f32_to_bf16(v)) : v;
+        }
+      float out = __fsub_rn(br[0][0], br[0][1]);
+      if (kActBranches == 2) {
+        out = __fsub_rn(out, br[1][0]);
+        out = __fadd_rn(out, br[1][1]);
+      }
+      if (bias != nullptr && lane < N)
+        out = __fadd_rn(out, bias[lane]);
+      out = apply_act(out, act);
+      if (row < M && lane < N)
+        y[row * N + lane] = out;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// INT8 on CUDA cores: CTA tile 64 x 64, thread owns 4 columns x 4 lanes.
+__global__ void pad_int8_kernel(const int8_t *__restrict__ x, int64_t M,
+                                int64_t K, int64_t m_pad, int64_t k_pad,
+                                int8_t *__restrict__ out) {
+  const int64_t total = m_pad * k_pad;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < total; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = i / k_pad, k = i - m * k_pad;
+    out[i] = (m < M && k < K) ? x[m * K + k] : int8_t{0};
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    int8_simt_kernel(const int8_t *__restrict__ A, const int8_t *__restrict__ B,
+                     int64_t k_pad, int T, int64_t M, int64_t N,
+                     int checked, int32_t *__restrict__ y, int32_t *status) {
+  __shared__ __align__(16) int8_t As[64][kRowStride];
+  __shared__ __align__(16) int8_t Bs[64][kRowStride];
+  const int tid = threadIdx.x;
+  const int tr = tid >> 4, tc = tid & 15;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * 64;
+  uint32_t acc[4][4] = {};
+  bool overflow = false;
+  for (int t = 0; t < T; ++t) {
+    {
+      const int r = tid >> 2, c = tid & 3;
+      *reinterpret_cast<int4 *>(&As[r][c * 16]) = *reinterpret_cast<const int4 *>(
+          A + (m0 + r) * k_pad + static_cast<int64_t>(t) * kTileK + c * 16);
+      *reinterpret_cast<int4 *>(&Bs[r][c * 16]) = *reinterpret_cast<const int4 *>(
+          B + (n0 + r) * k_pad + static_cast<int64_t>(t) * kTileK + c * 16);
+    }
+    __syncthreads();
+    int p[4][4] = {};
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      int4 av[4], bv[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        av[r] = *reinterpret_cast<const int4 *>(&As[tr + 16 * r][kk * 16]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        bv[c] = *reinterpret_cast<const int4 *>(&Bs[tc * 4 + c][kk * 16]);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          int s = p[r][c];
+          s = __dp4a(av[r].x, bv[c].x, s);
+          s = __dp4a(av[r].y, bv[c].y, s);
+          s = __dp4a(av[r].z, bv[c].z, s);
+          s = __dp4a(av[r].w, bv[c].w, s);
+          p[r][c] = s;
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (checked && (p[r][c] < -(1 << 20) || p[r][c] >= (1 << 20)))
+          overflow = true;
+        acc[r][c] += static_cast<uint32_t>(p[r][c]);
+      }
+    __syncthreads();
+  }
+  if (overflow)
+    atomicOr(status, CIM22_STATUS_I21_RANGE);
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int64_t row = m0 + tr + 16 * r;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int64_t lane = n0 + tc * 4 + c;
+      if (row < M && lane < N)
+        y[row * N + lane] = static_cast<int32_t>(acc[r][c]);
+    }
+  }
+}
+
+bool check_gather(const cim22_gather &g, int64_t m, int64_t k) {
+  if (g.kind == CIM22_GATHER_ROWS)
+    return true;
+  if (g.kind != CIM22_GATHER_CONV_NCHW && g.kind != CIM22_GATHER_CONV_NHWC)
+    return false;
+  if (g.batch <= 0 || g.channels <= 0 || g.height <= 0 || g.width <= 0 ||
+      g.kernel_h <= 0 || g.kernel_w <= 0 || g.stride_h <= 0 || g.stride_w <= 0 ||
+      g.pad_h < 0 || g.pad_w < 0)
+    return false;
+  const int oh = (g.height + 2 * g.pad_h - g.kernel_h) / g.stride_h + 1;
+  const int ow = (g.width + 2 * g.pad_w - g.kernel_w) / g.stride_w + 1;
+  return oh == g.out_h && ow == g.out_w &&
+         static_cast<int64_t>(g.batch) * oh * ow == m &&
+         static_cast<int64_t>(g.channels) * g.kernel_h * g.kernel_w == k;
+}
+
+} // namespace
+
+// Host-side BF16 weight preparation: split, RNE, prealign per lane and K tile.
+static void prepare_bf16_weights(const float *w, int64_t n, int64_t k,
+                                 int64_t n_pad, int64_t k_pad, int64_t T,
+                                 std::vector<int8_t> &mant,
+                                 std::vector<int32_t> &exps) {
+  mant.assign(2 * n_pad * k_pad, 0);
+  exps.assign(2 * T * n_pad, 127);
+  uint16_t group[kTileK];
+  for (int b = 0; b < 2; ++b)
+    for (int64_t lane = 0; lane < n; ++lane)
+      for (int64_t t = 0; t < T; ++t) {
+        int exp_max = 0;
+        for (int i = 0; i < kTileK; ++i) {
+          const int64_t col = t * kTileK + i;
+          uint16_t bits = 0;
+          if (col < k) {
+            const float v = w[lane * k + col];
+            const bool negative = std::signbit(v), zero = v == 0.0f;
+            if (b == 0)
+              bits = (negative || zero) ? 0 : f32_to_bf16(v);
+            else
+              bits = (!negative || zero) ? 0 : f32_to_bf16(-v);
+          }
+          group[i] = bits;
+          exp_max = std::max(exp_max, (bits >> 7) & 0xff);
+        }
+        bool any = false;
+        int8_t *dst = mant.data() + (b * n_pad + lane) * k_pad + t * kTileK;
+        for (int i = 0; i < kTileK; ++i) {
+          dst[i] = prealign_element(group[i], exp_max);
+          any |= dst[i] != 0;
+        }
+        // A lane whose prealigned tile is all zero contributes +0 for every
+        // input; keep its exponent at 127 so it never forces the exact
+        // (slow) restore path.
+        exps[(b * T + t) * n_pad + lane] = any ? exp_max : 127;
+      }
+}
+
+static bool int8_range_proof(const int8_t *w, int64_t n, int64_t k) {
+  for (int64_t o = 0; o < n; ++o)
+    for (int64_t r = 0; r < k; r += kTileK) {
+      int64_t lower = 0, upper = 0;
+      for (int64_t i = r; i < std::min<int64_t>(k, r + kTileK); ++i) {
+        const int64_t v = w[o * k + i];
+        upper += v >= 0 ? 127 * v : -128 * v;
+        lower += v >= 0 ? -128 * v : 127 * v;
+      }
+      if (lower < -(1 << 20) || lower >= (1 << 20) || upper < -(1 << 20) ||
+          upper >= (1 << 20))
+        return false;
+    }
+  return true;
+}
+
+} // namespace cim
+
+using namespace cim;
+
+extern "C" {
+
+cim22_cuda_layer *cim22_cuda_layer_create_bf16(int device, const float *weight,
+                                               int64_t n, int64_t k,
+                                               char *error,
+                                               size_t error_capacity) {
+  if (!weight || n <= 0 || k <= 0) {
+    copy_error("invalid CIM layer shape", error, error_capacity);
+    return nullptr;
+  }
+  for (int64_t i = 0; i < n * k; ++i)
+    if (!std::isfinite(weight[i])) {
+      copy_error("BF16 correction requires finite fixed weights", error,
+                 error_capacity);
+      return nullptr;
+    }
+  auto *layer = new cim22_cuda_layer();
+  layer->device = device;
+  layer->bf16 = true;
+  layer->n = n;
+  layer->k = k;
+  layer->n_pad = round_up(n, kLanePad);
+  layer->k_pad = round_up(k, kTileK);
+  layer->tiles = layer->k_pad / kTileK;
+  std::vector<int8_t> mant;
+  std::vector<int32_t> exps;
+  prepare_bf16_weights(weight, n, k, layer->n_pad, layer->k_pad, layer->tiles,
+                       mant, exps);
+  if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice") ||
+      !cuda_ok(cudaMalloc(&layer->weights, mant.size()), "cudaMalloc") ||
+      !cuda_ok(cudaMalloc(&layer->exponents, exps.size() * sizeof(int32_t)),
+               "cudaMalloc") ||
+      !cuda_ok(cudaMemcpy(layer->weights, mant.data(), mant.size(),
+                          cudaMemcpyHostToDevice),
+               "cudaMemcpy") ||
+      !cuda_ok(cudaMemcpy(layer->exponents, exps.data(),
+                          exps.size() * sizeof(int32_t), cudaMemcpyHostToDevice),
+               "cudaMemcpy")) {
+    copy_error(last_error(), error, error_capacity);
+    cim22_cuda_layer_destroy(layer);
+    return nullptr;
+  }
+  return layer;
+}
+
+cim22_cuda_layer *cim22_cuda_layer_create_int8(int device, const int8_t *weight,
+                                               int64_t n, int64_t k,
+                                               char *error,
+                                               size_t error_capacity) {
+  if (!weight || n <= 0 || k <= 0) {
+    copy_error("invalid CIM layer shape", error, error_capacity);
+    return nullptr;
+  }
+  auto *layer = new cim22_cuda_layer();
+  layer->device = device;
+  layer->bf16 = false;
+  layer->n = n;
+  layer->k = k;
+  layer->n_pad = round_up(n, kLanePad);
+  layer->k_pad = round_up(k, kTileK);
+  layer->tiles = layer->k_pad / kTileK;
+  layer->range_safe = int8_range_proof(weight, n, k);
+  std::vector<int8_t> padded(layer->n_pad * layer->k_pad, 0);
+  for (int64_t o = 0; o < n; ++o)
+    std::copy_n(weight + o * k, k, padded.data() + o * layer->k_pad);
+  if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice") ||
+      !cuda_ok(cudaMalloc(&layer->weights, padded.size()), "cudaMalloc") ||
+      !cuda_ok(cudaMemcpy(layer->weights, padded.data(), padded.size(),
+                          cudaMemcpyHostToDevice),
+               "cudaMemcpy")) {
+    copy_error(last_error(), error, error_capacity);
+    cim22_cuda_layer_destroy(layer);
+    return nullptr;
+  }
+  return layer;
+}
+
+void cim22_cuda_layer_destroy(cim22_cuda_layer *layer) {
+  if (!layer)
+    return;
+  cudaSetDevice(layer->device);
+  if (layer->weights)
+    cudaFree(layer->weights);
+  if (layer->exponents)
+    cudaFree(layer->exponents);
+  delete layer;
+}
+
+int cim22_cuda_layer_range_safe(const cim22_cuda_layer *layer) {
+  return layer && layer->range_safe ? 1 : 0;
+}
+int64_t cim22_cuda_layer_n(const cim22_cuda_layer *layer) { return layer ? layer->n : -1; }
+int64_t cim22_cuda_layer_k(const cim22_cuda_layer *layer) { return layer ? layer->k : -1; }
+
+size_t cim22_cuda_layer_workspace_bf16(const cim22_cuda_layer *layer,
+                                       int64_t m, int32_t branches) {
+  if (!layer || m <= 0)
+    return 0;
+  const int64_t m_pad = round_up(m, kColumnPad);
+  const int64_t ab = branches == 2 ? 1 : 2;
+  const int64_t a_bytes = round_up(ab * m_pad * layer->k_pad, 256);
+  return static_cast<size_t>(a_bytes + ab * layer->tiles * m_pad * 4);
+}
+
+size_t cim22_cuda_layer_workspace_int8(const cim22_cuda_layer *layer, int64_t m) {
+  if (!layer || m <= 0)
+    return 0;
+  return static_cast<size_t>(round_up(m, kColumnPad) * layer->k_pad);
+}
+
+int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
+                                  const cim22_gather *gather, int64_t m,
+                                  const float *bias, int32_t activation,
+                                  int32_t branches, float *y, void *workspace,
+                                  size_t workspace_bytes, int32_t *status,
+                                  void *stream) {
+  cim22_gather rows{};
+  rows.kind = CIM22_GATHER_ROWS;
+  const cim22_gather &g = gather ? *gather : rows;
+  if (!layer || !layer->bf16 || !x || !y || !status || m <= 0 ||
+      (branches != 2 && branches != 4) || activation < 0 || activation > 2 ||
+      !check_gather(g, m, layer->k) ||
+      workspace_bytes < cim22_cuda_layer_workspace_bf16(layer, m, branches) ||
+      !workspace) {
+    set_last_error("invalid arguments to cim22_cuda_layer_forward_bf16");
+    return CIM22_STATUS_BAD_ARGUMENT;
+  }
+  auto s = static_cast<cudaStream_t>(stream);
+  const int64_t m_pad = round_up(m, kColumnPad);
+  const int ab = branches == 2 ? 1 : 2;
+  const int T = static_cast<int>(layer->tiles);
+  int8_t *A = static_cast<int8_t *>(workspace);
+  int32_t *ex = reinterpret_cast<int32_t *>(
+      static_cast<char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
+  const int64_t warps = m_pad * T;
+  const unsigned prep_blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  if (ab == 1)
+    prepare_kernel<1><<<prep_blocks, 256, 0, s>>>(x, g, m, layer->k, T, m_pad,
+                                                  layer->k_pad, A, ex, status);
+  else
+    prepare_kernel<2><<<prep_blocks, 256, 0, s>>>(x, g, m, layer->k, T, m_pad,
+                                                  layer->k_pad, A, ex, status);
+  if (!cuda_ok(cudaGetLastError(), "prepare launch"))
+    return CIM22_STATUS_BAD_ARGUMENT;
+  if (tc::signsplit_available() &&
+      tc::launch_signsplit(A, ex, m_pad, layer->weights, layer->exponents,
+                           layer->n_pad, layer->k_pad, T, m, layer->n, bias,
+                           activation, ab, y, status, s))
+    return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+  const dim3 grid(static_cast<unsigned>(m_pad / kBM),
+                  static_cast<unsigned>((layer->n + kBN - 1) / kBN));
+  if (ab == 1)
+    signsplit_simt_kernel<1><<<grid, 256, 0, s>>>(
+        A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
+        layer->k_pad, T, m, layer->n, bias, activation, y, status);
+  else
+    signsplit_simt_kernel<2><<<grid, 256, 0, s>>>(
+        A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
+        layer->k_pad, T, m, layer->n, bias, activation, y, status);
+  return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+}
+
+int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,
+                                  const int8_t *x, int64_t m, int32_t *y,
+                                  void *workspace, size_t workspace_bytes,
+                                  int32_t *status, void *stream) {
+  if (!layer || layer->bf16 || !x || !y || !status || m <= 0 || !workspace ||
+      workspace_bytes < cim22_cuda_layer_workspace_int8(layer, m)) {
+    set_last_error("invalid arguments to cim22_cuda_layer_forward_int8");
+    return CIM22_STATUS_BAD_ARGUMENT;
+  }
+  auto s = static_cast<cudaStream_t>(stream);
+  const int64_t m_pad = round_up(m, kColumnPad);
+  int8_t *A = static_cast<int8_t *>(workspace);
+  const int64_t total = m_pad * layer->k_pad;
+  const unsigned blocks =
+      static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 32));
+  pad_int8_kernel<<<blocks, 256, 0, s>>>(x, m, layer->k, m_pad, layer->k_pad, A);
+  if (!cuda_ok(cudaGetLastError(), "pad launch"))
+    return CIM22_STATUS_BAD_ARGUMENT;
+  const int T = static_cast<int>(layer->tiles);
+  if (layer->range_safe && tc::int8_available() &&
+      tc::launch_int8(A, m_pad, layer->weights, layer->n_pad, layer->k_pad, T, m,
+                      layer->n, y, status, s))
+    return cuda_ok(cudaGetLastError(), "int8 launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+  const dim3 grid(static_cast<unsigned>(m_pad / 64),
+                  static_cast<unsigned>((layer->n + 63) / 64));
+  int8_simt_kernel<<<grid, 256, 0, s>>>(A, layer->weights, layer->k_pad, T, m,
+                                        layer->n, layer->range_safe ? 0 : 1, y,
+                                        status);
+  return cuda_ok(cudaGetLastError(), "int8 launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+}
+
+} // extern "C"

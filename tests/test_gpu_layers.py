@@ -1,0 +1,159 @@
+"""Layer-level CUDA kernels against the oracle (bit-exact) and glue against
+PyTorch CPU eager f32 (the reference's own float oracle, 1e-3 relative)."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def test_doc_example_on_gpu():
+    from cim22_b200.cim_ops import CimLayer
+
+    layer = CimLayer(np.full((16, 64), 0.5, np.float32))
+    y = layer.linear_bf16(torch.ones(1, 64, device=DEV))
+    assert torch.all(y == 32.0)
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 1, 1), (3, 64, 16), (37, 150, 20), (130, 400, 120),
+                                   (64, 784, 256), (5, 4096, 33), (200, 25, 6)])
+@pytest.mark.parametrize("branches", [2, 4])
+def test_linear_bf16_bit_exact(m, k, n, branches):
+    from cim22_b200.cim_ops import CimLayer
+
+    rng = np.random.default_rng(m * 1000 + k + n + branches)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    x[rng.random((m, k)) < 0.01] *= 20
+    if branches == 2:
+        x = np.maximum(x, 0)
+    w = (rng.standard_normal((n, k)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    expected = oracle.linear_bf16(x, w, b, branches=4, threads=8)
+    layer = CimLayer(w)
+    got = layer.linear_bf16(torch.from_numpy(x).to(DEV), bias=torch.from_numpy(b).to(DEV),
+                            branches=branches).cpu().numpy()
+    np.testing.assert_array_equal(bits(got), bits(expected))
+
+
+def test_linear_bf16_extreme_exponents_slow_path():
+    """Scales far from 2^0 force the exact subnormal/overflow restore path."""
+    from cim22_b200.cim_ops import CimLayer
+
+    rng = np.random.default_rng(3)
+    for scale_x, scale_w in ((1e-30, 1e-8), (1e-38, 1.0), (1e20, 1e-20), (1e-20, 1e-20)):
+        x = (rng.standard_normal((17, 130)) * scale_x).astype(np.float32)
+        w = (rng.standard_normal((19, 130)) * scale_w).astype(np.float32)
+        expected = oracle.linear_bf16(x, w, None, branches=4)
+        got = CimLayer(w).linear_bf16(torch.from_numpy(x).to(DEV)).cpu().numpy()
+        np.testing.assert_array_equal(bits(got), bits(expected))
+
+
+def test_linear_bf16_overflow_and_nan_status():
+    from cim22_b200.cim_ops import CimLayer
+
+    w = np.full((16, 64), 3e38, np.float32)
+    x = np.full((1, 64), 3e38, np.float32)
+    with pytest.raises(oracle.OracleError, match="exceeds BF16"):
+        oracle.linear_bf16(x, w)
+    with pytest.raises(RuntimeError, match="exceeds BF16"):
+        CimLayer(w).linear_bf16(torch.from_numpy(x).to(DEV))
+    x = np.ones((2, 64), np.float32)
+    x[1, 5] = np.nan
+    with pytest.raises(RuntimeError, match="NaN or infinity"):
+        CimLayer(np.ones((4, 64), np.float32)).linear_bf16(torch.from_numpy(x).to(DEV))
+
+
+@pytest.mark.parametrize("layout", ["nchw", "nhwc"])
+@pytest.mark.parametrize("c,h,f,kk,stride,pad", [(1, 32, 6, 5, 1, 0), (6, 14, 16, 5, 1, 0),
+                                                 (3, 9, 8, 3, 2, 1), (2, 16, 32, 3, 1, 1)])
+def test_conv_bf16_bit_exact(layout, c, h, f, kk, stride, pad):
+    from cim22_b200 import abi
+    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace, conv_gather
+
+    rng = np.random.default_rng(c * 100 + h + f)
+    n = 3
+    x = rng.standard_normal((n, c, h, h)).astype(np.float32)
+    w = (rng.standard_normal((f, c, kk, kk)) * 0.2).astype(np.float32)
+    b = rng.standard_normal(f).astype(np.float32)
+    expected = oracle.conv2d_bf16(x, w, b, stride, pad, branches=4)  # NCHW
+    layer = CimLayer(w.reshape(f, -1))
+    kind = abi.GATHER_CONV_NCHW if layout == "nchw" else abi.GATHER_CONV_NHWC
+    g = conv_gather(kind, n, c, h, h, kk, kk, stride, pad)
+    xt = torch.from_numpy(x if layout == "nchw" else x.transpose(0, 2, 3, 1).copy()).to(DEV)
+    m = n * g.out_h * g.out_w
+    out = torch.empty(m, f, device=DEV)
+    status = StatusWord(torch.device(DEV))
+    layer.forward_bf16(xt, out, m, gather=g, bias=torch.from_numpy(b).to(DEV),
+                       workspace=Workspace(torch.device(DEV)), status=status)
+    status.raise_if_set()
+    got = out.cpu().numpy().reshape(n, g.out_h, g.out_w, f).transpose(0, 3, 1, 2)
+    np.testing.assert_array_equal(bits(got), bits(expected))
+
+
+@pytest.mark.parametrize("m,k,n", [(2, 65, 17), (2, 128, 17), (33, 1000, 70), (300, 64, 16)])
+def test_linear_int8_exact(m, k, n):
+    from cim22_b200.cim_ops import CimLayer
+
+    rng = np.random.default_rng(k)
+    x = rng.integers(-128, 128, (m, k)).astype(np.int8)
+    w = rng.integers(-127, 128, (n, k)).astype(np.int8)
+    layer = CimLayer(w, kind="int8")
+    assert layer.range_safe == oracle.int8_range_safe(w)
+    got = layer.linear_int8(torch.from_numpy(x).to(DEV)).cpu().numpy()
+    np.testing.assert_array_equal(got, oracle.linear_int8(x, w))
+    np.testing.assert_array_equal(got, (x.astype(np.int64) @ w.T.astype(np.int64)).astype(np.int32))
+
+
+def test_linear_int8_unproven_weights_report_i21():
+    from cim22_b200.cim_ops import CimLayer
+
+    w = np.full((16, 64), -128, np.int8)
+    layer = CimLayer(w, kind="int8")
+    assert not layer.range_safe
+    ok = np.zeros((1, 64), np.int8)
+    ok[0, 0] = 3
+    np.testing.assert_array_equal(layer.linear_int8(torch.from_numpy(ok).to(DEV)).cpu().numpy(),
+                                  oracle.linear_int8(ok, w))
+    with pytest.raises(RuntimeError, match="signed i21"):
+        layer.linear_int8(torch.from_numpy(np.full((1, 64), -128, np.int8)).to(DEV))
+
+
+def test_glue_against_torch_cpu():
+    from cim22_b200 import cim_ops
+
+    rng = np.random.default_rng(5)
+    x = torch.from_numpy(rng.standard_normal((4, 10, 12, 7)).astype(np.float32))
+    y = torch.from_numpy(rng.standard_normal((4, 10, 12, 7)).astype(np.float32))
+    xd, yd = x.to(DEV), y.to(DEV)
+    tol = dict(rtol=1e-3, atol=1e-6)
+    torch.testing.assert_close(cim_ops.relu(xd).cpu(), torch.relu(x), **tol)
+    torch.testing.assert_close(cim_ops.gelu(xd).cpu(), torch.nn.functional.gelu(x), **tol)
+    torch.testing.assert_close(cim_ops.add(xd, yd, "relu").cpu(), torch.relu(x + y), **tol)
+    nchw = x.permute(0, 3, 1, 2)
+    torch.testing.assert_close(cim_ops.maxpool2d_nhwc(xd, 2, 2).cpu(),
+                               torch.nn.functional.max_pool2d(nchw, 2, 2).permute(0, 2, 3, 1), **tol)
+    torch.testing.assert_close(cim_ops.maxpool2d_nhwc(xd, 3, 2, 1).cpu(),
+                               torch.nn.functional.max_pool2d(nchw, 3, 2, 1).permute(0, 2, 3, 1),
+                               **tol)
+    torch.testing.assert_close(cim_ops.avgpool2d_nhwc(xd, 2, 2).cpu(),
+                               torch.nn.functional.avg_pool2d(nchw, 2, 2).permute(0, 2, 3, 1), **tol)
+    torch.testing.assert_close(cim_ops.global_avgpool_nhwc(xd).cpu(), nchw.mean((2, 3)), **tol)
+    scale = torch.rand(7) + 0.5
+    shift = torch.randn(7)
+    torch.testing.assert_close(
+        cim_ops.channel_affine_nhwc(xd, scale.to(DEV), shift.to(DEV), "relu").cpu(),
+        torch.relu(x * scale + shift), **tol)
+    flat = x.reshape(-1, 7)
+    torch.testing.assert_close(cim_ops.softmax(flat.to(DEV)).cpu(), torch.softmax(flat, -1), **tol)
+    torch.testing.assert_close(cim_ops.nhwc_to_nchw(xd).cpu(), nchw.contiguous(), rtol=0, atol=0)
+    torch.testing.assert_close(cim_ops.nchw_to_nhwc(nchw.contiguous().to(DEV)).cpu(), x,
+                               rtol=0, atol=0)
