@@ -1,0 +1,334 @@
+"""Benchmark: CIM-simulation inferences/s of the LeNet workload on B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload lenet]
+    python bench.py --impl reference ...      # the CPU reference arm
+
+One step is one inference pass of the whole CIM-simulated network over one
+batch (LeNet: 256 images of 1x32x32, U[0,1], He-normal weights; every
+Linear/Conv runs as BF16 sign-split crossbar tiles, bit-exact with the
+reference simulator). With N GPUs (torchrun, one process per GPU) each rank
+runs its own batch: the work shards by batch with no collective (weak
+scaling); ``value`` is the whole-job rate, timed on the device with CUDA
+events and taken as the maximum over ranks.
+
+Prints one JSON line (rank 0). ``e2e`` is the same metric through the public
+API (the torch.compile backend, runtime="cuda") with the batch in pinned host
+memory and the logits read back every step. ``roofline`` covers the kernel
+with the largest share of device time, timed per launch with CUDA events on
+its stream. ``cpu_baseline`` is the oracle port of the reference's software
+runner (oracle/), run on this host's cores over a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path[:0] = [str(REPO / "mlir-cim22_b200"), str(REPO / "oracle")]
+
+METRIC = "CIM-sim inferences/sec"
+UNIT = "inferences/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--workload", default="lenet")
+    p.add_argument("--batch", type=int, default=None)
+    p.add_argument("--cpu-sample", type=int, default=512,
+                   help="images in the CPU baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return data["hbm_gbs"], data["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, indices):
+        self.indices = set(indices)
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [s.strip() for s in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = [r for r in self.rows if r[0].isdigit() and int(r[0]) in self.indices]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_baseline(workload: str, sample: int, threads: int, batch_seed: int = 0):
+    """Oracle port of the reference's software runner on host cores."""
+    import oracle
+    from cim22_b200 import workloads
+
+    model, x = workloads.build(workload, sample, seed=batch_seed)
+    oracle.cim_forward(model, x[:2].numpy(), threads=threads, via_runner=True)  # warm
+    t0 = time.perf_counter()
+    oracle.cim_forward(model, x.numpy(), threads=threads, via_runner=True)
+    dt = time.perf_counter() - t0
+    return sample / dt, dt
+
+
+def reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    per_step = max(1, min(args.cpu_sample, 256))
+    for _ in range(args.warmup):
+        cpu_baseline(args.workload, max(2, per_step // 8), threads)
+    times = []
+    for _ in range(args.steps):
+        _, dt = cpu_baseline(args.workload, per_step, threads)
+        times.append(dt)
+    total = sum(times)
+    value = per_step * args.steps / total
+    from cim22_b200 import workloads
+
+    w = workloads.WORKLOADS[args.workload]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {w.description}",
+                   "batch_per_step": per_step, "parallelism": "host threads over columns"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{per_step} images per step through the oracle's "
+                                   "restated CIMSoftwareRunner (40-Work transactions, plan "
+                                   "reuse, weight residency) + PyTorch CPU glue"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from cim22_b200 import backend, program, workloads
+
+    w = workloads.WORKLOADS[args.workload]
+    batch = args.batch or w.batch
+    model, x = workloads.build(args.workload, batch, seed=0)
+    _, x = workloads.build(args.workload, batch, seed=1000 + rank)  # per-rank batch
+
+    prog = program.from_module(model, x, device=local, name=args.workload)
+    prog.inputs[0].tensor.copy_(x.to(dev))
+    prog.capture()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+
+    # Warm-up.
+    for _ in range(args.warmup):
+        flush.zero_()
+        prog.replay()
+    prog.check_status()
+    barrier()
+
+    stream = torch.cuda.current_stream(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler([local] if world == 1 else range(world)) as clocks:
+        barrier()
+        for i in range(args.steps):
+            flush.zero_()  # L2 flush between steps, outside the timed span
+            starts[i].record(stream)
+            prog.replay()
+            ends[i].record(stream)
+        barrier()
+    prog.check_status()
+    elapsed_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(t.item())
+    value = world * batch * args.steps / (elapsed_ms / 1000)
+
+    # Per-kernel device time (eager launches, one event pair per kernel).
+    names = [s.name for s in prog.steps]
+    per = {n: [] for n in names}
+    kernel_iters = max(3, min(args.steps, 20))
+    for _ in range(kernel_iters):
+        flush.zero_()
+        prog.status.reset()
+        evs = []
+        for step in prog.steps:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            step.fn()
+            b.record(stream)
+            evs.append((step.name, a, b))
+        torch.cuda.synchronize(dev)
+        for n, a, b in evs:
+            per[n].append(a.elapsed_time(b))
+    prog.check_status()
+    avg = {n: sum(v) / len(v) for n, v in per.items()}
+    total_kernel = sum(avg.values())
+    dominant = max(avg, key=avg.get)
+    hbm_peak, bf16_peak, peak_kind = peaks()
+    layer_of = {s.name: s for s in prog.steps}
+    step = layer_of[dominant]
+    info = next((l for l in prog.layers if dominant.startswith(l.name)), None)
+    dur_s = avg[dominant] / 1000
+    if step.cim and info is not None:
+        ops = 2 * info.macs
+        achieved = ops / dur_s / 1e12
+        int8_peak = 2 * bf16_peak
+        roof = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
+                "frac": achieved / int8_peak, "traffic": None, "kernel": dominant,
+                "ops_per_launch": ops, "launch_ms": avg[dominant],
+                "peak_note": f"int8 dense = 2 x {peak_kind} bf16 cuBLAS ({bf16_peak} TF/s); "
+                             "ops = 2 x branches x M x K x N (unpadded) as TOPS"}
+    else:
+        algo = None
+        if info is not None and dominant.endswith(".prepare"):
+            ab = 1 if info.branches == 2 else 2
+            t_tiles = -(-info.k // 64)
+            algo = 4 * info.m * info.k + ab * info.m * t_tiles * (64 + 4)
+        gbs = (algo / dur_s / 1e9) if algo else None
+        roof = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                "frac": (gbs / hbm_peak) if gbs else None, "traffic": None, "kernel": dominant,
+                "bytes_per_launch": algo, "launch_ms": avg[dominant],
+                "peak_note": f"{peak_kind} HBM copy bandwidth"}
+    kernel_table = {n: {"ms": round(avg[n], 5), "share": round(avg[n] / total_kernel, 4)}
+                    for n in names}
+
+    # End to end through the public API (torch.compile, runtime="cuda").
+    name = backend.register()
+    compiled = torch.compile(model, backend=name, fullgraph=True, dynamic=False,
+                             options={"runtime": "cuda", "device": local})
+    host = x.pin_memory()
+    with torch.inference_mode():
+        out = compiled(host)
+        for _ in range(args.warmup):
+            out = compiled(host)
+        barrier()
+        e_ms = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            out = compiled(host)
+            b.record(stream)
+            b.synchronize()
+            e_ms += a.elapsed_time(b)
+        barrier()
+    et = torch.tensor([e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e_value = world * batch * args.steps / (float(et.item()) / 1000)
+    h2d = host.numel() * host.element_size()
+    d2h = out.numel() * out.element_size() + 4  # logits + status word
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        rate, dt = cpu_baseline(args.workload, args.cpu_sample, threads)
+        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{args.cpu_sample} {args.workload} images through the oracle's "
+                         f"restated CIMSoftwareRunner (40-Work transactions, plan reuse, "
+                         f"residency) + PyTorch CPU glue, {dt:.1f} s wall"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{args.workload}: {w.description}", "batch_per_gpu": batch,
+                       "global_batch": batch * world, "parallelism": f"batch-sharded x{world}",
+                       "l2": "flushed between steps (256 MiB write, outside the timed span)",
+                       "graph": "CUDA graph replay", "cim_macs_per_batch": prog.macs,
+                       "arithmetic": "BF16 sign-split: int8 mantissa crossbar dots, BF16 "
+                                     "tiles, f32 K sums"},
+            "gpu_launches": len(prog.steps) * args.steps,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "roofline": roof,
+            "kernels": kernel_table,
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -370,6 +370,23 @@ int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
 size_t cim22_cuda_layer_workspace_int8(const cim22_cuda_layer *layer,
                                        int64_t m);
 
+/* The two kernels of cim22_cuda_layer_forward_bf16, callable separately:
+ * prepare gathers, splits and prealigns the activation columns into the
+ * workspace; contract runs the crossbar dots, restore, K accumulation, branch
+ * merge, bias and activation from that workspace. forward = prepare then
+ * contract on the same stream. */
+int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
+                                  const float *x, const cim22_gather *gather,
+                                  int64_t m, int32_t branches, void *workspace,
+                                  size_t workspace_bytes, int32_t *status,
+                                  void *stream);
+int cim22_cuda_layer_contract_bf16(const cim22_cuda_layer *layer, int64_t m,
+                                   const float *bias, int32_t activation,
+                                   int32_t branches, float *y,
+                                   const void *workspace,
+                                   size_t workspace_bytes, int32_t *status,
+                                   void *stream);
+
 /* INT8 layer: y[m, n] = sum over K tiles of the signed-i21 tile results,
  * accumulated in wrapping int32 (Passes.cpp:1054-1059). x is int8 [m, k]. */
 int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,

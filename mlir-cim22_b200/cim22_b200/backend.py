@@ -1,0 +1,106 @@
+"""torch.compile backend ``cim22`` with the CUDA execution runtime.
+
+Mirrors the reference's backend (python/cim22/backend.py:102-235 of mlir-cim22)
+and its options (python/cim22/compiler.py:28-93):
+
+  runtime="cuda"       new: lower the captured graph to CIM layers and glue
+                       kernels on a B200 (this package);
+  runtime="reference"  the captured graph with CPU PyTorch operators, exactly as
+                       the reference's reference mode.
+
+Read-only module parameters and buffers are frozen into the compiled program,
+as the reference freezes them (backend.py:161-196); Dynamo guards on their
+identity. Gradients must be disabled. bf16_compensation must be "sign-split"
+(the default and the only mode the layer kernels implement; the transaction
+runner in cim22_b200.native also executes "legacy" and "none").
+Inputs may be CPU or CUDA tensors; outputs are returned on the inputs' device.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Callable, Sequence, TypedDict
+
+import torch
+
+from .program import Program
+
+
+class BackendOptions(TypedDict, total=False):
+    runtime: str
+    bf16_compensation: str
+    device: int
+    cuda_graph: bool
+    artifact_dir: Any
+    debug_dir: Any
+
+
+def _validate(options: dict) -> None:
+    runtime = options.get("runtime", "cuda")
+    if runtime not in ("cuda", "reference"):
+        raise ValueError("CIM22 runtime must be one of ('reference', 'cuda') in this backend")
+    if options.get("bf16_compensation", "sign-split") != "sign-split":
+        raise ValueError("CIM22 CUDA layers implement bf16_compensation='sign-split'")
+    if options.get("usb_config") is not None or options.get("usb_session") is not None:
+        raise ValueError("CIM22 usb options require runtime='usb'")
+
+
+def _is_module_input(node: torch.fx.Node) -> bool:
+    grapharg = node.meta.get("grapharg")
+    if grapharg is None:
+        return False
+    from torch._dynamo.source import NNModuleSource, UnspecializedParamBufferSource
+
+    source = grapharg.source
+    while source is not None:
+        if isinstance(source, (NNModuleSource, UnspecializedParamBufferSource)):
+            return True
+        source = getattr(source, "base", None)
+    name = getattr(grapharg.source, "name", lambda: "")
+    text = name() if callable(name) else str(name)
+    return "_modules_" in text or "_parameters_" in text or "_buffers_" in text
+
+
+def backend(gm: torch.fx.GraphModule, example_inputs: Sequence[torch.Tensor], *,
+            options: BackendOptions | None = None) -> Callable:
+    """Compile a static inference graph for torch.compile."""
+    options = dict(options or {})
+    _validate(options)
+    if torch.is_grad_enabled():
+        raise ValueError("Use torch.no_grad() or torch.inference_mode() with CIM22")
+    runtime = options.get("runtime", "cuda")
+    if runtime == "reference":
+        if any(isinstance(v, torch.Tensor) and v.device.type != "cpu" for v in example_inputs):
+            raise ValueError("CIM22 reference requires CPU tensors")
+        return gm.forward
+    placeholders = list(gm.graph.find_nodes(op="placeholder"))
+    frozen = {i for i, node in enumerate(placeholders)
+              if isinstance(example_inputs[i], torch.Tensor) and _is_module_input(node)}
+    device = int(options.get("device", 0))
+    program = Program(gm, [e.detach() if isinstance(e, torch.Tensor) else e
+                           for e in example_inputs],
+                      frozen=frozen, device=device, name="cim22_cuda")
+    if options.get("cuda_graph", True):
+        program.capture()
+    inputs = [i for i in range(len(placeholders)) if i not in frozen]
+
+    def run(*values):
+        result = program(*(values[i] for i in inputs))
+        return result if isinstance(result, tuple) else (result,)
+
+    run.program = program  # type: ignore[attr-defined]
+    return run
+
+
+def register(name: str = "cim22") -> str:
+    """Register the backend with Dynamo under ``name`` (cim22 unless taken)."""
+    from torch._dynamo import list_backends, register_backend
+
+    def cim22(gm, example_inputs, options=None):
+        return backend(gm, example_inputs, options=options)
+
+    if name in list_backends(exclude_tags=()):
+        name = "cim22_cuda"
+        if name in list_backends(exclude_tags=()):
+            return name
+    register_backend(name=name)(cim22)
+    return name

@@ -123,6 +123,27 @@ class CimLayer:
         check(rc, "cim22_cuda_layer_forward_bf16")
         return out
 
+    def prepare_bf16(self, x: torch.Tensor, m: int, *, gather: abi.Gather | None = None,
+                     branches: int = 4, workspace: Workspace, status: StatusWord) -> None:
+        """First kernel of forward_bf16: gather, split and prealign into the workspace."""
+        _require(x, torch.float32, "x")
+        ws = workspace.get(self.workspace_bytes(m, branches))
+        check(lib().cim22_cuda_layer_prepare_bf16(
+            self._handle, _ptr(x), None if gather is None else ctypes.byref(gather), m,
+            branches, _ptr(ws), ws.numel(), _ptr(status.tensor), _stream(x.device)),
+            "cim22_cuda_layer_prepare_bf16")
+
+    def contract_bf16(self, out: torch.Tensor, m: int, *, bias: torch.Tensor | None = None,
+                      activation: str | None = None, branches: int = 4,
+                      workspace: Workspace, status: StatusWord) -> None:
+        """Second kernel of forward_bf16: crossbar dots, restore, accumulate, merge."""
+        _require(out, torch.float32, "out")
+        ws = workspace.get(self.workspace_bytes(m, branches))
+        check(lib().cim22_cuda_layer_contract_bf16(
+            self._handle, m, _ptr(bias), ACT[activation], branches, _ptr(out), _ptr(ws),
+            ws.numel(), _ptr(status.tensor), _stream(out.device)),
+            "cim22_cuda_layer_contract_bf16")
+
     def linear_bf16(self, x: torch.Tensor, bias=None, activation=None, branches: int = 4,
                     workspace: Workspace | None = None,
                     status: StatusWord | None = None) -> torch.Tensor:

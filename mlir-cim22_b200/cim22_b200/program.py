@@ -1,0 +1,575 @@
+"""Lower a captured inference graph to a CIM program on one CUDA device.
+
+This plays the role of the reference's compile pipeline for the CUDA runtime:
+Linear, Conv2d and torch._int_mm contractions with frozen weights become CIM
+layers (BF16 sign-split, or INT8 for _int_mm), with the same numerics the
+reference's lowering produces (lib/Conversion/LinalgToCIM/Passes.cpp:
+760-857,1087-1385,2304-2476); everything else becomes the Host glue kernels
+(ReLU, pooling, add, batch norm, GELU, softmax, flatten).
+
+Images are kept in NHWC internally, so a convolution's output matrix
+[N*OH*OW, F] is already the next layer's input image and no transposes are
+launched between layers. An activation that directly follows a CIM layer and
+is its only consumer is fused into the layer's epilogue. A layer whose input is
+provably nonnegative runs 2 branches instead of 4; the xn branches are exactly
++0 then, so the result is bit-identical (the reference proves the same
+invariance only for a narrower set of producers, Passes.cpp:2239-2303).
+
+All buffers are allocated once for the static input shapes, so a program can
+be captured into a CUDA graph and replayed.
+"""
+
+from __future__ import annotations
+
+import operator
+from dataclasses import dataclass, field
+from typing import Any, Callable
+
+import numpy as np
+import torch
+import torch.fx as fx
+import torch.nn.functional as F
+
+from . import abi, cim_ops
+from .cim_ops import CimLayer, StatusWord, Workspace
+
+IMAGE, MATRIX, TENSOR, CONST = "image", "matrix", "tensor", "const"
+
+
+@dataclass
+class Val:
+    kind: str
+    shape: tuple  # logical (torch) shape
+    tensor: torch.Tensor | None = None  # device storage (NHWC for images)
+    layout: str = "nhwc"  # images: "nhwc" storage or "nchw" (graph inputs)
+    nonneg: bool = False
+    value: Any = None  # constants
+    dtype: torch.dtype = torch.float32
+
+
+@dataclass
+class Step:
+    name: str
+    fn: Callable[[], None]
+    cim: bool = False
+    meta: dict = field(default_factory=dict)  # CIM layers: operands for parity checks
+
+
+@dataclass
+class LayerInfo:
+    name: str
+    kind: str  # "linear", "conv", "int8"
+    m: int
+    k: int
+    n: int
+    branches: int
+    macs: int
+
+
+_CONV = {torch.conv2d, F.conv2d}
+_LINEAR = {F.linear, torch._C._nn.linear}
+_RELU = {F.relu, torch.relu, torch.nn.functional.relu}
+_GELU = {F.gelu, torch._C._nn.gelu}
+_ADD = {operator.add, torch.add, operator.iadd}
+_FLATTEN = {torch.flatten}
+_MAXPOOL = {F.max_pool2d, torch.max_pool2d}
+_AVGPOOL = {F.avg_pool2d, torch._C._nn.avg_pool2d}
+_ADAPTIVE = {F.adaptive_avg_pool2d, torch._C._nn.adaptive_avg_pool2d}
+_BN = {F.batch_norm}
+_SOFTMAX = {F.softmax, torch.softmax}
+_INT_MM = {torch._int_mm}
+
+
+def _pair(v):
+    return tuple(v) if isinstance(v, (tuple, list)) else (v, v)
+
+
+class Program:
+    """A lowered graph: a list of kernel launches over preallocated buffers."""
+
+    def __init__(self, gm: fx.GraphModule, example_inputs, *, frozen: set[int] | None = None,
+                 device: int | torch.device = 0, name: str = "cim_program",
+                 fuse: bool = True) -> None:
+        self.device = torch.device("cuda", device) if isinstance(device, int) else device
+        self.name = name
+        self.fuse = fuse
+        self.workspace = Workspace(self.device)
+        self.status = StatusWord(self.device)
+        self.steps: list[Step] = []
+        self.layers: list[LayerInfo] = []
+        self._keep: list[Any] = []
+        self.inputs: list[Val] = []
+        self.input_shapes: list[tuple] = []
+        self.input_dtypes: list[torch.dtype] = []
+        self.graph = None
+        frozen = frozen or set()
+        env: dict[fx.Node, Val] = {}
+        users = {node: len(node.users) for node in gm.graph.nodes}
+        self._fused: set[fx.Node] = set()
+        placeholder_index = 0
+        modules = dict(gm.named_modules())
+        for node in gm.graph.nodes:
+            if node in self._fused:
+                continue
+            if node.op == "placeholder":
+                example = example_inputs[placeholder_index]
+                if placeholder_index in frozen:
+                    env[node] = Val(CONST, tuple(example.shape), value=example.detach())
+                else:
+                    t = torch.empty(tuple(example.shape), dtype=example.dtype, device=self.device)
+                    kind = IMAGE if example.dim() == 4 else (MATRIX if example.dim() == 2 else TENSOR)
+                    v = Val(kind, tuple(example.shape), t, layout="nchw", dtype=example.dtype)
+                    env[node] = v
+                    self.inputs.append(v)
+                    self.input_shapes.append(tuple(example.shape))
+                    self.input_dtypes.append(example.dtype)
+                placeholder_index += 1
+            elif node.op == "get_attr":
+                value = gm
+                for part in str(node.target).split("."):
+                    value = getattr(value, part)
+                env[node] = Val(CONST, tuple(getattr(value, "shape", ())), value=value)
+            elif node.op == "call_module":
+                self._lower(node, self._module_as_call(node, modules[str(node.target)]), env,
+                            users)
+            elif node.op == "call_method":
+                self._lower(node, self._method_as_call(node), env, users)
+            elif node.op == "call_function":
+                self._lower(node, (node.target, node.args, dict(node.kwargs)), env, users)
+            elif node.op == "output":
+                outs = node.args[0]
+                self._outputs = [env[o] for o in (outs if isinstance(outs, (tuple, list)) else (outs,))]
+                self._output_is_tuple = isinstance(outs, (tuple, list))
+        self.output_tensors = [self._materialize(v) for v in self._outputs]
+
+    # ------------------------------------------------------------------ lowering
+
+    def _module_as_call(self, node, module):
+        x = node.args[0]
+        if isinstance(module, torch.nn.Conv2d):
+            return (F.conv2d, (x, module.weight, module.bias, module.stride, module.padding,
+                               module.dilation, module.groups), {})
+        if isinstance(module, torch.nn.Linear):
+            return (F.linear, (x, module.weight, module.bias), {})
+        if isinstance(module, torch.nn.ReLU):
+            return (F.relu, (x,), {})
+        if isinstance(module, torch.nn.GELU):
+            return (F.gelu, (x,), {"approximate": module.approximate})
+        if isinstance(module, torch.nn.MaxPool2d):
+            return (F.max_pool2d, (x, module.kernel_size, module.stride, module.padding), {})
+        if isinstance(module, torch.nn.AvgPool2d):
+            return (F.avg_pool2d, (x, module.kernel_size, module.stride), {})
+        if isinstance(module, torch.nn.AdaptiveAvgPool2d):
+            return (F.adaptive_avg_pool2d, (x, module.output_size), {})
+        if isinstance(module, torch.nn.Flatten):
+            return (torch.flatten, (x, module.start_dim), {})
+        if isinstance(module, torch.nn.BatchNorm2d):
+            return (F.batch_norm, (x, module.running_mean, module.running_var, module.weight,
+                                   module.bias, False, 0.0, module.eps), {})
+        if isinstance(module, torch.nn.Softmax):
+            return (F.softmax, (x,), {"dim": module.dim})
+        if isinstance(module, torch.nn.Identity):
+            return ("identity", (x,), {})
+        raise NotImplementedError(f"CIM CUDA runtime does not lower module {type(module).__name__}")
+
+    def _method_as_call(self, node):
+        name = node.target
+        if name == "relu":
+            return (F.relu, node.args, {})
+        if name in ("flatten",):
+            return (torch.flatten, node.args, dict(node.kwargs))
+        if name in ("view", "reshape"):
+            return ("reshape", node.args, {})
+        if name in ("add",):
+            return (operator.add, node.args, {})
+        if name in ("contiguous",):
+            return ("identity", node.args[:1], {})
+        raise NotImplementedError(f"CIM CUDA runtime does not lower Tensor.{name}")
+
+    def _const(self, env, a):
+        if isinstance(a, fx.Node):
+            v = env[a]
+            if v.kind != CONST:
+                raise NotImplementedError("CIM layers need frozen (constant) weights")
+            return v.value
+        return a
+
+    def _single_fusable_user(self, node, users, targets) -> fx.Node | None:
+        if users[node] != 1:
+            return None
+        (user,) = node.users
+        if user.op == "call_function" and user.target in targets and user.args[0] is node:
+            return user
+        if user.op == "call_method" and user.target in ("relu",) and targets is _RELU:
+            return user
+        return None
+
+    def _lower(self, node, call, env, users) -> None:
+        target, args, kwargs = call
+        if target in _CONV:
+            self._lower_conv(node, args, kwargs, env, users)
+        elif target in _LINEAR:
+            self._lower_linear(node, args, env, users)
+        elif target in _INT_MM:
+            self._lower_int_mm(node, args, env)
+        elif target in _RELU:
+            self._lower_unary(node, env[args[0]], "relu", env)
+        elif target in _GELU:
+            if kwargs.get("approximate", "none") != "none":
+                raise NotImplementedError("only erf GELU is lowered")
+            self._lower_unary(node, env[args[0]], "gelu", env)
+        elif target in _ADD:
+            self._lower_add(node, args, kwargs, env, users)
+        elif target in _MAXPOOL:
+            self._lower_pool(node, args, kwargs, env, "max")
+        elif target in _AVGPOOL:
+            self._lower_pool(node, args, kwargs, env, "avg")
+        elif target in _ADAPTIVE:
+            size = _pair(args[1] if len(args) > 1 else kwargs["output_size"])
+            if size != (1, 1):
+                raise NotImplementedError("adaptive_avg_pool2d lowers output size 1 only")
+            self._lower_gap(node, env[args[0]], env)
+        elif target in _FLATTEN:
+            start = args[1] if len(args) > 1 else kwargs.get("start_dim", 0)
+            self._lower_flatten(node, env[args[0]], start, env)
+        elif target == "reshape":
+            shape = args[1:] if not isinstance(args[1], (tuple, list)) else tuple(args[1])
+            if len(shape) == 2 and env[args[0]].kind == IMAGE:
+                self._lower_flatten(node, env[args[0]], 1, env)
+            elif tuple(shape) == env[args[0]].shape:
+                env[node] = env[args[0]]
+            else:
+                raise NotImplementedError(f"reshape to {shape}")
+        elif target in _BN:
+            self._lower_bn(node, args, kwargs, env, users)
+        elif target in _SOFTMAX:
+            self._lower_softmax(node, args, kwargs, env)
+        elif target == "identity":
+            env[node] = env[args[0]]
+        elif target is operator.getitem:
+            env[node] = env[args[0]].value[args[1]]
+        else:
+            raise NotImplementedError(f"CIM CUDA runtime does not lower {target}")
+
+    def _new(self, shape, dtype=torch.float32) -> torch.Tensor:
+        return torch.empty(shape, dtype=dtype, device=self.device)
+
+    def _epilogue(self, node, users) -> tuple[str | None, fx.Node]:
+        if not self.fuse:
+            return None, node
+        fused = self._single_fusable_user(node, users, _RELU)
+        if fused is not None:
+            self._fused.add(fused)
+            return "relu", fused
+        fused = self._single_fusable_user(node, users, _GELU)
+        if fused is not None and fused.kwargs.get("approximate", "none") == "none":
+            self._fused.add(fused)
+            return "gelu", fused
+        return None, node
+
+    def _bias(self, b):
+        if b is None:
+            return None
+        t = torch.as_tensor(b).detach().float().contiguous().to(self.device)
+        self._keep.append(t)
+        return t
+
+    def _lower_conv(self, node, args, kwargs, env, users) -> None:
+        x = env[args[0]]
+        w = self._const(env, args[1])
+        b = self._const(env, args[2]) if len(args) > 2 else kwargs.get("bias")
+        stride = _pair(args[3] if len(args) > 3 else kwargs.get("stride", 1))
+        pad = _pair(args[4] if len(args) > 4 else kwargs.get("padding", 0))
+        dil = _pair(args[5] if len(args) > 5 else kwargs.get("dilation", 1))
+        groups = args[6] if len(args) > 6 else kwargs.get("groups", 1)
+        if groups != 1 or dil != (1, 1) or stride[0] != stride[1] or pad[0] != pad[1] \
+                or isinstance(pad[0], str):
+            raise NotImplementedError("conv2d lowers groups=1, dilation=1, square stride/pad")
+        if x.kind != IMAGE:
+            raise NotImplementedError("conv2d input must be an NCHW image")
+        n, c, h, wd = x.shape
+        f, c2, kh, kw = w.shape
+        assert c == c2
+        layer = CimLayer(torch.as_tensor(w).detach().float().reshape(f, -1), device=self.device)
+        self._keep.append(layer)
+        kind = abi.GATHER_CONV_NCHW if x.layout == "nchw" else abi.GATHER_CONV_NHWC
+        g = cim_ops.conv_gather(kind, n, c, h, wd, kh, kw, stride[0], pad[0])
+        self._keep.append(g)
+        m = n * g.out_h * g.out_w
+        act, out_node = self._epilogue(node, users)
+        out = self._new((n, g.out_h, g.out_w, f))
+        bias = self._bias(b)
+        branches = 2 if x.nonneg else 4
+        xt = x.tensor
+
+        def prepare():
+            layer.prepare_bf16(xt, m, gather=g, branches=branches, workspace=self.workspace,
+                               status=self.status)
+
+        def run():
+            layer.contract_bf16(out, m, bias=bias, activation=act, branches=branches,
+                                workspace=self.workspace, status=self.status)
+
+        name = f"conv{len(self.layers)}"
+        self.steps.append(Step(name + ".prepare", prepare))
+        self.steps.append(Step(name, run, cim=True, meta=dict(
+            kind="conv", x=xt, layout=x.layout, weight=torch.as_tensor(w).detach().float(),
+            bias=None if b is None else torch.as_tensor(b).detach().float(), stride=stride[0],
+            pad=pad[0], out=out, act=act, branches=branches)))
+        self.layers.append(LayerInfo(name, "conv", m, c * kh * kw, f, branches,
+                                     branches * m * c * kh * kw * f))
+        env[out_node] = Val(IMAGE, (n, f, g.out_h, g.out_w), out, "nhwc",
+                            nonneg=act == "relu")
+
+    def _lower_linear(self, node, args, env, users) -> None:
+        x = env[args[0]]
+        w = self._const(env, args[1])
+        b = self._const(env, args[2]) if len(args) > 2 else None
+        if x.kind not in (MATRIX, TENSOR) or len(x.shape) != 2:
+            raise NotImplementedError("linear lowers 2-D inputs")
+        m, k = x.shape
+        n = w.shape[0]
+        layer = CimLayer(torch.as_tensor(w).detach().float(), device=self.device)
+        self._keep.append(layer)
+        act, out_node = self._epilogue(node, users)
+        out = self._new((m, n))
+        bias = self._bias(b)
+        branches = 2 if x.nonneg else 4
+        xt = x.tensor
+
+        def prepare():
+            layer.prepare_bf16(xt, m, branches=branches, workspace=self.workspace,
+                               status=self.status)
+
+        def run():
+            layer.contract_bf16(out, m, bias=bias, activation=act, branches=branches,
+                                workspace=self.workspace, status=self.status)
+
+        name = f"linear{len(self.layers)}"
+        self.steps.append(Step(name + ".prepare", prepare))
+        self.steps.append(Step(name, run, cim=True, meta=dict(
+            kind="linear", x=xt, weight=torch.as_tensor(w).detach().float(),
+            bias=None if b is None else torch.as_tensor(b).detach().float(), out=out, act=act,
+            branches=branches)))
+        self.layers.append(LayerInfo(name, "linear", m, k, n, branches, branches * m * k * n))
+        env[out_node] = Val(MATRIX, (m, n), out, nonneg=act == "relu")
+
+    def _lower_int_mm(self, node, args, env) -> None:
+        x = env[args[0]]
+        w = self._const(env, args[1])  # [K, N]
+        if x.dtype != torch.int8 or len(x.shape) != 2:
+            raise NotImplementedError("_int_mm lowers int8 [M, K] inputs")
+        m, k = x.shape
+        wt = torch.as_tensor(w).detach().t().contiguous()
+        layer = CimLayer(wt, kind="int8", device=self.device)
+        self._keep.append(layer)
+        out = self._new((m, wt.shape[0]), torch.int32)
+        xt = x.tensor
+
+        def run():
+            from .native import check, lib
+
+            ws = self.workspace.get(layer.workspace_bytes(m))
+            check(lib().cim22_cuda_layer_forward_int8(
+                layer._handle, cim_ops._ptr(xt), m, cim_ops._ptr(out), cim_ops._ptr(ws),
+                ws.numel(), cim_ops._ptr(self.status.tensor), cim_ops._stream(self.device)),
+                "forward_int8")
+
+        name = f"int8_{len(self.layers)}"
+        self.steps.append(Step(name, run, cim=True))
+        self.layers.append(LayerInfo(name, "int8", m, k, wt.shape[0], 1, m * k * wt.shape[0]))
+        env[node] = Val(MATRIX, (m, wt.shape[0]), out, dtype=torch.int32)
+
+    def _lower_unary(self, node, x, op, env) -> None:
+        if x.kind == CONST:
+            raise NotImplementedError("activation of a constant")
+        out = self._new(x.tensor.shape)
+        xt = x.tensor
+        fn = cim_ops.relu if op == "relu" else cim_ops.gelu
+        self.steps.append(Step(op, lambda: fn(xt, out)))
+        env[node] = Val(x.kind, x.shape, out, x.layout, nonneg=op == "relu")
+
+    def _lower_add(self, node, args, kwargs, env, users) -> None:
+        a, b = args[0], args[1]
+        if kwargs.get("alpha", 1) != 1:
+            raise NotImplementedError("add with alpha")
+        va = env[a] if isinstance(a, fx.Node) else None
+        vb = env[b] if isinstance(b, fx.Node) else None
+        if va is None or vb is None or va.kind == CONST or vb.kind == CONST:
+            # x + scalar/constant: broadcast on the device once, then add.
+            v = va if va is not None and va.kind != CONST else vb
+            other = b if v is va else a
+            const = other.value if isinstance(other, Val) else (
+                env[other].value if isinstance(other, fx.Node) else other)
+            c = torch.as_tensor(const, dtype=torch.float32)
+            if v.kind == IMAGE and c.dim() > 0:
+                c = c.reshape(v.shape) if c.numel() == np.prod(v.shape) else c
+                c = c.permute(0, 2, 3, 1) if c.dim() == 4 else c
+            ct = c.expand(v.tensor.shape).contiguous().to(self.device)
+            self._keep.append(ct)
+            va, vb = v, Val(v.kind, v.shape, ct, v.layout)
+        if va.tensor.shape != vb.tensor.shape or va.layout != vb.layout:
+            raise NotImplementedError("add lowers same-shape, same-layout operands")
+        act, out_node = self._epilogue(node, users)
+        out = self._new(va.tensor.shape)
+        at, bt = va.tensor, vb.tensor
+        self.steps.append(Step("add", lambda: cim_ops.add(at, bt, act, out)))
+        env[out_node] = Val(va.kind, va.shape, out, va.layout,
+                            nonneg=act == "relu" or (va.nonneg and vb.nonneg))
+
+    def _nhwc(self, x: Val) -> torch.Tensor:
+        if x.layout == "nhwc":
+            return x.tensor
+        out = self._new((x.shape[0], x.shape[2], x.shape[3], x.shape[1]))
+        xt = x.tensor
+        self.steps.append(Step("nchw_to_nhwc", lambda: cim_ops.nchw_to_nhwc(xt, out)))
+        return out
+
+    def _lower_pool(self, node, args, kwargs, env, kind) -> None:
+        x = env[args[0]]
+        k = _pair(args[1] if len(args) > 1 else kwargs["kernel_size"])
+        s = args[2] if len(args) > 2 else kwargs.get("stride")
+        s = _pair(s if s not in (None, [], ()) else k)
+        p = _pair(args[3] if len(args) > 3 else kwargs.get("padding", 0))
+        if k[0] != k[1] or s[0] != s[1] or p[0] != p[1]:
+            raise NotImplementedError("pooling lowers square windows")
+        if kind == "max":
+            for key, default in (("dilation", 1), ("ceil_mode", False), ("return_indices", False)):
+                if kwargs.get(key, default) not in (default, (default, default)):
+                    raise NotImplementedError(f"max_pool2d {key}")
+        elif p[0] != 0:
+            raise NotImplementedError("avg_pool2d padding")
+        xt = self._nhwc(x)
+        n, c, h, w = x.shape
+        oh = (h + 2 * p[0] - k[0]) // s[0] + 1
+        ow = (w + 2 * p[0] - k[0]) // s[0] + 1
+        out = self._new((n, oh, ow, c))
+        if kind == "max":
+            self.steps.append(Step("maxpool", lambda: cim_ops.maxpool2d_nhwc(xt, k[0], s[0], p[0], out)))
+        else:
+            self.steps.append(Step("avgpool", lambda: cim_ops.avgpool2d_nhwc(xt, k[0], s[0], out)))
+        env[node] = Val(IMAGE, (n, c, oh, ow), out, "nhwc", nonneg=x.nonneg)
+
+    def _lower_gap(self, node, x, env) -> None:
+        xt = self._nhwc(x)
+        n, c, h, w = x.shape
+        out = self._new((n, 1, 1, c))
+        self.steps.append(Step("global_avgpool",
+                               lambda: cim_ops.global_avgpool_nhwc(xt, out.view(n, c))))
+        env[node] = Val(IMAGE, (n, c, 1, 1), out, "nhwc", nonneg=x.nonneg)
+
+    def _lower_flatten(self, node, x, start, env) -> None:
+        if start != 1:
+            raise NotImplementedError("flatten lowers start_dim=1")
+        if x.kind == IMAGE:
+            n, c, h, w = x.shape
+            if x.layout == "nhwc" and (h, w) != (1, 1):
+                out = self._new((n, c, h, w))
+                xt = x.tensor
+                self.steps.append(Step("flatten", lambda: cim_ops.nhwc_to_nchw(xt, out)))
+                t = out.view(n, c * h * w)
+            else:
+                t = x.tensor.view(n, c * h * w)
+            env[node] = Val(MATRIX, (n, c * h * w), t, nonneg=x.nonneg)
+        else:
+            env[node] = x
+
+    def _lower_bn(self, node, args, kwargs, env, users) -> None:
+        x = env[args[0]]
+        mean, var = self._const(env, args[1]), self._const(env, args[2])
+        weight = self._const(env, args[3]) if len(args) > 3 else kwargs.get("weight")
+        bias = self._const(env, args[4]) if len(args) > 4 else kwargs.get("bias")
+        training = args[5] if len(args) > 5 else kwargs.get("training", False)
+        eps = args[7] if len(args) > 7 else kwargs.get("eps", 1e-5)
+        if training:
+            raise NotImplementedError("batch_norm lowers inference mode only")
+        mean = torch.as_tensor(mean).float()
+        var = torch.as_tensor(var).float()
+        gamma = torch.ones_like(mean) if weight is None else torch.as_tensor(weight).float()
+        beta = torch.zeros_like(mean) if bias is None else torch.as_tensor(bias).float()
+        scale = (gamma / torch.sqrt(var + eps)).contiguous()
+        shift = (beta - mean * scale).contiguous()
+        st, sh = scale.to(self.device), shift.to(self.device)
+        self._keep += [st, sh]
+        xt = self._nhwc(x) if x.kind == IMAGE else x.tensor
+        act, out_node = self._epilogue(node, users)
+        out = self._new(xt.shape)
+        self.steps.append(Step("batch_norm",
+                               lambda: cim_ops.channel_affine_nhwc(xt, st, sh, act, out)))
+        env[out_node] = Val(x.kind, x.shape, out, "nhwc" if x.kind == IMAGE else x.layout,
+                            nonneg=act == "relu")
+
+    def _lower_softmax(self, node, args, kwargs, env) -> None:
+        x = env[args[0]]
+        dim = args[1] if len(args) > 1 else kwargs.get("dim")
+        if x.kind != MATRIX or dim not in (-1, 1):
+            raise NotImplementedError("softmax lowers the last dim of a matrix")
+        out = self._new(x.tensor.shape)
+        xt = x.tensor
+        self.steps.append(Step("softmax", lambda: cim_ops.softmax(xt, out)))
+        env[node] = Val(MATRIX, x.shape, out, nonneg=True)
+
+    def _materialize(self, v: Val) -> torch.Tensor:
+        if v.kind == IMAGE and v.layout == "nhwc":
+            n, c, h, w = v.shape
+            out = self._new((n, c, h, w))
+            xt = v.tensor
+            self.steps.append(Step("to_nchw", lambda: cim_ops.nhwc_to_nchw(xt, out)))
+            return out
+        if v.kind == CONST:
+            raise NotImplementedError("graph output is a constant")
+        return v.tensor
+
+    # ----------------------------------------------------------------- execution
+
+    def launch(self) -> None:
+        """Enqueue every step on the current stream (no synchronization)."""
+        for step in self.steps:
+            step.fn()
+
+    def capture(self) -> None:
+        """Record the program into a CUDA graph for replay."""
+        torch.cuda.synchronize(self.device)
+        self.launch()  # warm: allocates workspace, loads modules
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.status.tensor.zero_()
+            self.launch()
+        self.graph = graph
+
+    def replay(self) -> None:
+        if self.graph is None:
+            self.status.tensor.zero_()
+            self.launch()
+        else:
+            self.graph.replay()
+
+    def check_status(self) -> None:
+        self.status.raise_if_set(f"{self.name}: ")
+
+    def __call__(self, *values: torch.Tensor):
+        """Run on inputs (CPU or CUDA). Returns outputs on the inputs' device."""
+        if len(values) != len(self.inputs):
+            raise ValueError("Input count differs from compiled signature")
+        on_cpu = any(v.device.type == "cpu" for v in values)
+        for v, slot, shape, dtype in zip(values, self.inputs, self.input_shapes,
+                                         self.input_dtypes):
+            if tuple(v.shape) != shape or v.dtype != dtype:
+                raise ValueError(f"input must be {dtype} {shape}")
+            slot.tensor.copy_(v, non_blocking=True)
+        self.replay()
+        outs = [t.to("cpu") if on_cpu else t.clone() for t in self.output_tensors]
+        self.check_status()
+        return tuple(outs) if self._output_is_tuple else outs[0]
+
+    @property
+    def macs(self) -> int:
+        return sum(layer.macs for layer in self.layers)
+
+
+def from_module(model: torch.nn.Module, example: torch.Tensor, device: int = 0,
+                name: str = "cim_program", fuse: bool = True) -> Program:
+    """Lower an eval-mode module by symbolic tracing, freezing its parameters."""
+    gm = fx.symbolic_trace(model)
+    return Program(gm, [example], frozen=set(), device=device, name=name, fuse=fuse)

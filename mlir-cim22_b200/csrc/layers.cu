@@ -588,21 +588,19 @@ size_t cim22_cuda_layer_workspace_int8(const cim22_cuda_layer *layer, int64_t m)
   return static_cast<size_t>(round_up(m, kColumnPad) * layer->k_pad);
 }
 
-int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
-                                  const cim22_gather *gather, int64_t m,
-                                  const float *bias, int32_t activation,
-                                  int32_t branches, float *y, void *workspace,
+int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
+                                  const float *x, const cim22_gather *gather,
+                                  int64_t m, int32_t branches, void *workspace,
                                   size_t workspace_bytes, int32_t *status,
                                   void *stream) {
   cim22_gather rows{};
   rows.kind = CIM22_GATHER_ROWS;
   const cim22_gather &g = gather ? *gather : rows;
-  if (!layer || !layer->bf16 || !x || !y || !status || m <= 0 ||
-      (branches != 2 && branches != 4) || activation < 0 || activation > 2 ||
-      !check_gather(g, m, layer->k) ||
-      workspace_bytes < cim22_cuda_layer_workspace_bf16(layer, m, branches) ||
-      !workspace) {
-    set_last_error("invalid arguments to cim22_cuda_layer_forward_bf16");
+  if (!layer || !layer->bf16 || !x || !status || m <= 0 ||
+      (branches != 2 && branches != 4) || !check_gather(g, m, layer->k) ||
+      !workspace ||
+      workspace_bytes < cim22_cuda_layer_workspace_bf16(layer, m, branches)) {
+    set_last_error("invalid arguments to cim22_cuda_layer_prepare_bf16");
     return CIM22_STATUS_BAD_ARGUMENT;
   }
   auto s = static_cast<cudaStream_t>(stream);
@@ -613,15 +611,36 @@ int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
   int32_t *ex = reinterpret_cast<int32_t *>(
       static_cast<char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
   const int64_t warps = m_pad * T;
-  const unsigned prep_blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
   if (ab == 1)
-    prepare_kernel<1><<<prep_blocks, 256, 0, s>>>(x, g, m, layer->k, T, m_pad,
-                                                  layer->k_pad, A, ex, status);
+    prepare_kernel<1><<<blocks, 256, 0, s>>>(x, g, m, layer->k, T, m_pad,
+                                             layer->k_pad, A, ex, status);
   else
-    prepare_kernel<2><<<prep_blocks, 256, 0, s>>>(x, g, m, layer->k, T, m_pad,
-                                                  layer->k_pad, A, ex, status);
-  if (!cuda_ok(cudaGetLastError(), "prepare launch"))
+    prepare_kernel<2><<<blocks, 256, 0, s>>>(x, g, m, layer->k, T, m_pad,
+                                             layer->k_pad, A, ex, status);
+  return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+}
+
+int cim22_cuda_layer_contract_bf16(const cim22_cuda_layer *layer, int64_t m,
+                                   const float *bias, int32_t activation,
+                                   int32_t branches, float *y,
+                                   const void *workspace,
+                                   size_t workspace_bytes, int32_t *status,
+                                   void *stream) {
+  if (!layer || !layer->bf16 || !y || !status || m <= 0 ||
+      (branches != 2 && branches != 4) || activation < 0 || activation > 2 ||
+      !workspace ||
+      workspace_bytes < cim22_cuda_layer_workspace_bf16(layer, m, branches)) {
+    set_last_error("invalid arguments to cim22_cuda_layer_contract_bf16");
     return CIM22_STATUS_BAD_ARGUMENT;
+  }
+  auto s = static_cast<cudaStream_t>(stream);
+  const int64_t m_pad = round_up(m, kColumnPad);
+  const int ab = branches == 2 ? 1 : 2;
+  const int T = static_cast<int>(layer->tiles);
+  const int8_t *A = static_cast<const int8_t *>(workspace);
+  const int32_t *ex = reinterpret_cast<const int32_t *>(
+      static_cast<const char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
   if (tc::signsplit_available() &&
       tc::launch_signsplit(A, ex, m_pad, layer->weights, layer->exponents,
                            layer->n_pad, layer->k_pad, T, m, layer->n, bias,
@@ -638,6 +657,24 @@ int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
         A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
         layer->k_pad, T, m, layer->n, bias, activation, y, status);
   return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+}
+
+int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
+                                  const cim22_gather *gather, int64_t m,
+                                  const float *bias, int32_t activation,
+                                  int32_t branches, float *y, void *workspace,
+                                  size_t workspace_bytes, int32_t *status,
+                                  void *stream) {
+  if (!y || activation < 0 || activation > 2) {
+    set_last_error("invalid arguments to cim22_cuda_layer_forward_bf16");
+    return CIM22_STATUS_BAD_ARGUMENT;
+  }
+  const int rc = cim22_cuda_layer_prepare_bf16(layer, x, gather, m, branches, workspace,
+                                               workspace_bytes, status, stream);
+  if (rc)
+    return rc;
+  return cim22_cuda_layer_contract_bf16(layer, m, bias, activation, branches, y, workspace,
+                                        workspace_bytes, status, stream);
 }
 
 int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,

@@ -1,0 +1,154 @@
+"""Whole workloads on the GPU against the oracle.
+
+* MLP and LeNet use only exact glue (ReLU, max-pool, flatten), so the whole
+  network is bit-exact against the oracle's forward.
+* For ResNet-18, the BF16 4x4096 stack and the event CNN (batch norm, GELU,
+  average pooling in f32 glue), every CIM layer is checked bit-exact on the
+  very inputs the GPU produced for it, and the network output within the
+  reference's float tolerance (1e-3 relative to the output scale).
+* The torch.compile backend with runtime="cuda" returns the oracle's result
+  for CPU inputs and raises the reference's error text for NaN inputs.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def run_program(program, x):
+    program.inputs[0].tensor.copy_(x.to(DEV))
+    program.status.reset()
+    program.launch()
+    torch.cuda.synchronize()
+    program.check_status()
+    return [t.cpu().numpy() for t in program.output_tensors]
+
+
+@pytest.mark.parametrize("name,batch", [("mlp", 8), ("lenet", 6)])
+def test_exact_glue_networks_bit_exact(name, batch):
+    from cim22_b200 import program, workloads
+
+    model, x = workloads.build(name, batch)
+    prog = program.from_module(model, x)
+    (got,) = run_program(prog, x)
+    expected = oracle.cim_forward(model, x.numpy(), branches=4, threads=8)
+    np.testing.assert_array_equal(bits(got), bits(expected))
+    # Graph replay gives the same bits.
+    prog.capture()
+    prog.inputs[0].tensor.copy_(x.to(DEV))
+    prog.replay()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bits(prog.output_tensors[0].cpu().numpy()), bits(expected))
+
+
+def _check_layers(prog):
+    checked = 0
+    for step in prog.steps:
+        step.fn()
+        if not step.cim:
+            continue
+        torch.cuda.synchronize()
+        meta = step.meta
+        x = meta["x"].cpu().numpy()
+        w = meta["weight"].numpy()
+        b = None if meta["bias"] is None else meta["bias"].numpy()
+        got = meta["out"].cpu().numpy()
+        if meta["kind"] == "conv":
+            if meta["layout"] == "nhwc":
+                x = x.transpose(0, 3, 1, 2)
+            exp = oracle.conv2d_bf16(x, w, b, meta["stride"], meta["pad"], branches=4,
+                                     threads=8)
+            exp = exp.transpose(0, 2, 3, 1)
+        else:
+            exp = oracle.linear_bf16(x.reshape(x.shape[0], -1), w, b, branches=4, threads=8)
+        assert meta["act"] is None
+        np.testing.assert_array_equal(bits(got.reshape(exp.shape)), bits(exp),
+                                      err_msg=step.name)
+        checked += 1
+    return checked
+
+
+@pytest.mark.parametrize("name,batch,layers", [("resnet18", 1, 21), ("bf16_4x4096", 2, 4),
+                                               ("event_cnn", 1, 5)])
+def test_every_cim_layer_bit_exact_on_recorded_inputs(name, batch, layers):
+    from cim22_b200 import program, workloads
+
+    model, x = workloads.build(name, batch)
+    prog = program.from_module(model, x, fuse=False)
+    prog.inputs[0].tensor.copy_(x.to(DEV))
+    prog.status.reset()
+    assert _check_layers(prog) == layers
+    prog.check_status()
+
+
+@pytest.mark.parametrize("name,batch", [("resnet18", 2), ("bf16_4x4096", 3), ("event_cnn", 2)])
+def test_float_glue_networks_within_tolerance(name, batch):
+    from cim22_b200 import program, workloads
+
+    model, x = workloads.build(name, batch)
+    prog = program.from_module(model, x)
+    (got,) = run_program(prog, x)
+    expected = oracle.cim_forward(model, x.numpy(), branches=4, threads=8)
+    scale = np.max(np.abs(expected))
+    err = np.max(np.abs(got - expected))
+    assert err <= 1e-3 * scale, (err, scale)
+
+
+def test_torch_compile_cuda_runtime():
+    from cim22_b200 import backend, workloads
+
+    name = backend.register()
+    model, x = workloads.build("lenet", 4)
+    compiled = torch.compile(model, backend=name, fullgraph=True, dynamic=False,
+                             options={"runtime": "cuda"})
+    expected = oracle.cim_forward(model, x.numpy(), branches=4, threads=8)
+    with torch.inference_mode():
+        got = compiled(x)
+        assert got.device.type == "cpu"
+        np.testing.assert_array_equal(bits(got.numpy()), bits(expected))
+        got2 = compiled(x.to(DEV))
+        assert got2.device == DEV
+        np.testing.assert_array_equal(bits(got2.cpu().numpy()), bits(expected))
+        bad = x.clone()
+        bad[0, 0, 3, 3] = float("nan")
+        with pytest.raises(RuntimeError, match="NaN or infinity"):
+            compiled(bad)
+        # A failed call does not poison the next one.
+        np.testing.assert_array_equal(bits(compiled(x).numpy()), bits(expected))
+
+
+def test_torch_compile_int_mm():
+    from cim22_b200 import backend
+
+    name = backend.register()
+
+    class Int8Matmul(torch.nn.Module):
+        def __init__(self, k, n, fill=None):
+            super().__init__()
+            w = (torch.arange(k * n).reshape(k, n) % 15 - 7).to(torch.int8)
+            if fill is not None:
+                w.fill_(fill)
+            self.weight = torch.nn.Parameter(w, requires_grad=False)
+
+        def forward(self, v):
+            return torch._int_mm(v, self.weight)
+
+    for k, n, fill, value in ((128, 32, None, -128), (128, 32, 127, -128), (256, 64, None, 5)):
+        model = Int8Matmul(k, n, fill).eval()
+        compiled = torch.compile(model, backend=name, fullgraph=True, dynamic=False,
+                                 options={"runtime": "cuda"})
+        v = torch.full((32, k), value, dtype=torch.int8)
+        v[1] = (torch.arange(k) % 256 - 128).to(torch.int8)
+        with torch.inference_mode():
+            got = compiled(v)
+        exp = (v.to(torch.int64) @ model.weight.to(torch.int64)).to(torch.int32)
+        assert torch.equal(got, exp)
