@@ -115,15 +115,20 @@ def test_torch_compile_cuda_runtime():
         got = compiled(x)
         assert got.device.type == "cpu"
         np.testing.assert_array_equal(bits(got.numpy()), bits(expected))
-        got2 = compiled(x.to(DEV))
-        assert got2.device == DEV
-        np.testing.assert_array_equal(bits(got2.cpu().numpy()), bits(expected))
         bad = x.clone()
         bad[0, 0, 3, 3] = float("nan")
         with pytest.raises(RuntimeError, match="NaN or infinity"):
             compiled(bad)
         # A failed call does not poison the next one.
         np.testing.assert_array_equal(bits(compiled(x).numpy()), bits(expected))
+    # Device-resident inputs go straight to the lowered program (no copies).
+    gm = torch.fx.symbolic_trace(model)
+    from cim22_b200.program import Program
+
+    prog = Program(gm, [x], device=0)
+    got2 = prog(x.to(DEV))
+    assert got2.device == DEV
+    np.testing.assert_array_equal(bits(got2.cpu().numpy()), bits(expected))
 
 
 def test_torch_compile_int_mm():
