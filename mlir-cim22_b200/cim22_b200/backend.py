@@ -75,6 +75,16 @@ def backend(gm: torch.fx.GraphModule, example_inputs: Sequence[torch.Tensor], *,
     placeholders = list(gm.graph.find_nodes(op="placeholder"))
     frozen = {i for i, node in enumerate(placeholders)
               if isinstance(example_inputs[i], torch.Tensor) and _is_module_input(node)}
+    # Frozen values cannot serve another module's parameters or buffers: guard
+    # on their identity so Dynamo recompiles for a different module
+    # (python/cim22/backend.py:207-210 of the reference does the same).
+    from torch._dynamo.guards import GuardBuilder, install_guard
+
+    for i in frozen:
+        grapharg = placeholders[i].meta.get("grapharg")
+        if grapharg is None or grapharg.source is None:
+            raise ValueError("CIM22 cannot guard a frozen module input without a source")
+        install_guard(grapharg.source.make_guard(GuardBuilder.ID_MATCH))
     device = int(options.get("device", 0))
     program = Program(gm, [e.detach() if isinstance(e, torch.Tensor) else e
                            for e in example_inputs],
@@ -91,8 +101,15 @@ def backend(gm: torch.fx.GraphModule, example_inputs: Sequence[torch.Tensor], *,
     return run
 
 
+_registered: str | None = None
+
+
 def register(name: str = "cim22") -> str:
-    """Register the backend with Dynamo under ``name`` (cim22 unless taken)."""
+    """Register the backend with Dynamo, as ``name`` unless another backend
+    already holds it (then as ``cim22_cuda``). Idempotent; returns the name."""
+    global _registered
+    if _registered is not None:
+        return _registered
     from torch._dynamo import list_backends, register_backend
 
     def cim22(gm, example_inputs, options=None):
@@ -100,7 +117,6 @@ def register(name: str = "cim22") -> str:
 
     if name in list_backends(exclude_tags=()):
         name = "cim22_cuda"
-        if name in list_backends(exclude_tags=()):
-            return name
     register_backend(name=name)(cim22)
+    _registered = name
     return name
