@@ -37,17 +37,18 @@ sys.path[:0] = [str(REPO / "mlir-cim22_b200"), str(REPO / "oracle")]
 METRIC = "CIM-sim inferences/sec"
 UNIT = "inferences/s"
 L2_FLUSH_BYTES = 256 << 20
+REFERENCE_SECONDS = 90.0
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=50)
-    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--steps", type=int, default=3000)
+    p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="lenet")
     p.add_argument("--batch", type=int, default=None)
-    p.add_argument("--cpu-sample", type=int, default=512,
+    p.add_argument("--cpu-sample", type=int, default=2048,
                    help="images in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
@@ -129,9 +130,12 @@ def reference_arm(args) -> None:
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    per_step = max(1, min(args.cpu_sample, 256))
+    # Size each step's sample so the whole run takes about REFERENCE_SECONDS.
+    rate, _ = cpu_baseline(args.workload, 2 * threads, threads)
+    per_step = int(REFERENCE_SECONDS * rate / max(1, args.steps + args.warmup))
+    per_step = max(1, min(args.cpu_sample, 256, per_step))
     for _ in range(args.warmup):
-        cpu_baseline(args.workload, max(2, per_step // 8), threads)
+        cpu_baseline(args.workload, per_step, threads)
     times = []
     for _ in range(args.steps):
         _, dt = cpu_baseline(args.workload, per_step, threads)
