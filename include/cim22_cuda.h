@@ -366,6 +366,28 @@ int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
                                   size_t workspace_bytes, int32_t *status,
                                   void *stream);
 
+/* No counterpart in the reference. The same BF16 sign-split layer as
+ * cim22_cuda_layer_forward_bf16 for callers that cannot allocate device
+ * memory: code running while a stream is captured into a CUDA graph (where
+ * cudaMalloc/cudaFree are not allowed) and generated model code that owns only
+ * stack buffers. The prepared-column scratch lives in a library-owned 16 MiB
+ * __device__ array (held by every GPU that loads the library until exit);
+ * calls needing more (cim22_cuda_layer_workspace_bf16 > that size) are
+ * rejected with CIM22_STATUS_BAD_ARGUMENT and a message in
+ * cim22_cuda_last_error(). All calls on a device share the array: calls that
+ * overlap on the GPU race. The layer's device must be current; the first call
+ * on a device resolves the array's address and should precede any stream
+ * capture. Allocates nothing. */
+int cim22_cuda_layer_forward_bf16_noalloc(const cim22_cuda_layer *layer,
+                                          const float *x,
+                                          const cim22_gather *gather, int64_t m,
+                                          const float *bias,
+                                          int32_t activation, int32_t branches,
+                                          float *y, int32_t *status,
+                                          void *stream);
+/* Size of that static scratch in bytes. */
+size_t cim22_cuda_layer_noalloc_scratch_bytes(void);
+
 /* Scratch bytes needed by cim22_cuda_layer_forward_int8 for m columns. */
 size_t cim22_cuda_layer_workspace_int8(const cim22_cuda_layer *layer,
                                        int64_t m);

@@ -59,6 +59,8 @@ _SIGNATURES = {
     "cim22_cuda_layer_forward_int8": (c.c_int, [P, P, I64, P, P, SZ, P, P]),
     "cim22_cuda_layer_prepare_bf16": (c.c_int, [P, P, P, I64, I32, P, SZ, P, P]),
     "cim22_cuda_layer_contract_bf16": (c.c_int, [P, I64, P, I32, I32, P, P, SZ, P, P]),
+    "cim22_cuda_layer_forward_bf16_noalloc": (c.c_int, [P, P, P, I64, P, I32, I32, P, P, P]),
+    "cim22_cuda_layer_noalloc_scratch_bytes": (SZ, []),
     "cim22_cuda_relu": (c.c_int, [P, P, I64, P]),
     "cim22_cuda_add": (c.c_int, [P, P, P, I64, I32, P]),
     "cim22_cuda_gelu": (c.c_int, [P, P, I64, P]),
