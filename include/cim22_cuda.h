@@ -333,7 +333,9 @@ int64_t cim22_cuda_layer_k(const cim22_cuda_layer *layer);
 /* Gather descriptor of the K x columns operand. Linear: x is [m, k] row-major.
  * Conv (im2col, Passes.cpp:1087-1385): x is an image batch; column m =
  * (n, oh, ow), K index = c*kh*kw + i*kw + j (the FCHW weight order), zero
- * padding inside 64-element groups. */
+ * padding inside 64-element groups. A Linear applied to torch.flatten of an
+ * NHWC image is the conv gather whose kernel covers the whole image
+ * (out 1x1): K index c*H*W + h*W + w is exactly the NCHW flatten order. */
 #define CIM22_GATHER_ROWS 0
 #define CIM22_GATHER_CONV_NCHW 1
 #define CIM22_GATHER_CONV_NHWC 2
@@ -343,6 +345,11 @@ typedef struct cim22_gather {
   int32_t batch, channels, height, width; /* image geometry (conv only) */
   int32_t kernel_h, kernel_w, stride_h, stride_w, pad_h, pad_w;
   int32_t out_h, out_w;
+  /* Optional max pooling folded into the gather (NHWC only): when
+   * pool_kernel > 0, x is the pre-pool image of pool_src_h x pool_src_w and
+   * the conv reads max over each pool_kernel^2 window (stride pool_stride,
+   * no padding), with height/width the pooled size. */
+  int32_t pool_kernel, pool_stride, pool_src_h, pool_src_w;
 } cim22_gather;
 
 /* Scratch bytes needed by cim22_cuda_layer_forward_bf16 for m columns. */

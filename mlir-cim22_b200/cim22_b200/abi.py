@@ -171,6 +171,10 @@ class Gather(ctypes.Structure):
         ("pad_w", ctypes.c_int32),
         ("out_h", ctypes.c_int32),
         ("out_w", ctypes.c_int32),
+        ("pool_kernel", ctypes.c_int32),
+        ("pool_stride", ctypes.c_int32),
+        ("pool_src_h", ctypes.c_int32),
+        ("pool_src_w", ctypes.c_int32),
     ]
 
 

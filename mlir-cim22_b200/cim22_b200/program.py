@@ -45,6 +45,8 @@ class Val:
     nonneg: bool = False
     value: Any = None  # constants
     dtype: torch.dtype = torch.float32
+    pool: tuple | None = None  # pending max pool (kernel, stride, source Val)
+    flat_of: "Val | None" = None  # pending flatten of this NHWC image
 
 
 @dataclass
@@ -292,15 +294,12 @@ class Program:
         assert c == c2
         layer = CimLayer(torch.as_tensor(w).detach().float().reshape(f, -1), device=self.device)
         self._keep.append(layer)
-        kind = abi.GATHER_CONV_NCHW if x.layout == "nchw" else abi.GATHER_CONV_NHWC
-        g = cim_ops.conv_gather(kind, n, c, h, wd, kh, kw, stride[0], pad[0])
-        self._keep.append(g)
+        g, xt = self._image_gather(x, kh, kw, stride[0], pad[0])
         m = n * g.out_h * g.out_w
         act, out_node = self._epilogue(node, users)
         out = self._new((n, g.out_h, g.out_w, f))
         bias = self._bias(b)
         branches = 2 if x.nonneg else 4
-        xt = x.tensor
 
         def prepare():
             layer.prepare_bf16(xt, m, gather=g, branches=branches, workspace=self.workspace,
@@ -335,10 +334,17 @@ class Program:
         out = self._new((m, n))
         bias = self._bias(b)
         branches = 2 if x.nonneg else 4
-        xt = x.tensor
+        g = None
+        if x.flat_of is not None and x.tensor is None and x.flat_of.layout == "nhwc":
+            # flatten(NHWC image) -> Linear is the conv whose kernel covers the
+            # image: its K order c*H*W + h*W + w is the NCHW flatten order.
+            img = x.flat_of
+            g, xt = self._image_gather(img, img.shape[2], img.shape[3], 1, 0)
+        else:
+            xt = self._tensor(x)
 
         def prepare():
-            layer.prepare_bf16(xt, m, branches=branches, workspace=self.workspace,
+            layer.prepare_bf16(xt, m, gather=g, branches=branches, workspace=self.workspace,
                                status=self.status)
 
         def run():
@@ -364,7 +370,7 @@ class Program:
         layer = CimLayer(wt, kind="int8", device=self.device)
         self._keep.append(layer)
         out = self._new((m, wt.shape[0]), torch.int32)
-        xt = x.tensor
+        xt = self._tensor(x)
 
         def run():
             from .native import check, lib
@@ -383,8 +389,8 @@ class Program:
     def _lower_unary(self, node, x, op, env) -> None:
         if x.kind == CONST:
             raise NotImplementedError("activation of a constant")
-        out = self._new(x.tensor.shape)
-        xt = x.tensor
+        xt = self._tensor(x)
+        out = self._new(xt.shape)
         fn = cim_ops.relu if op == "relu" else cim_ops.gelu
         self.steps.append(Step(op, lambda: fn(xt, out)))
         env[node] = Val(x.kind, x.shape, out, x.layout, nonneg=op == "relu")
@@ -405,21 +411,59 @@ class Program:
             if v.kind == IMAGE and c.dim() > 0:
                 c = c.reshape(v.shape) if c.numel() == np.prod(v.shape) else c
                 c = c.permute(0, 2, 3, 1) if c.dim() == 4 else c
-            ct = c.expand(v.tensor.shape).contiguous().to(self.device)
+            ct = c.expand(self._tensor(v).shape).contiguous().to(self.device)
             self._keep.append(ct)
             va, vb = v, Val(v.kind, v.shape, ct, v.layout)
-        if va.tensor.shape != vb.tensor.shape or va.layout != vb.layout:
+        at, bt = self._tensor(va), self._tensor(vb)
+        if at.shape != bt.shape or va.layout != vb.layout:
             raise NotImplementedError("add lowers same-shape, same-layout operands")
         act, out_node = self._epilogue(node, users)
-        out = self._new(va.tensor.shape)
-        at, bt = va.tensor, vb.tensor
+        out = self._new(at.shape)
         self.steps.append(Step("add", lambda: cim_ops.add(at, bt, act, out)))
         env[out_node] = Val(va.kind, va.shape, out, va.layout,
                             nonneg=act == "relu" or (va.nonneg and vb.nonneg))
 
+    def _tensor(self, v: Val) -> torch.Tensor:
+        """Device storage of a value, launching a pending pool or flatten."""
+        if v.tensor is not None:
+            return v.tensor
+        if v.pool is not None:
+            k, s, src = v.pool
+            st = self._tensor(src)
+            n, c, oh, ow = v.shape
+            out = self._new((n, oh, ow, c))
+            self.steps.append(Step("maxpool", lambda: cim_ops.maxpool2d_nhwc(st, k, s, 0, out)))
+            v.tensor = out
+            return out
+        if v.flat_of is not None:
+            img = v.flat_of
+            it = self._tensor(img)
+            n, c, h, w = img.shape
+            out = self._new((n, c, h, w))
+            self.steps.append(Step("flatten", lambda: cim_ops.nhwc_to_nchw(it, out)))
+            v.tensor = out.view(n, c * h * w)
+            return v.tensor
+        raise RuntimeError("value has no storage")
+
+    def _image_gather(self, x: Val, kh: int, kw: int, stride: int, pad: int):
+        """Gather descriptor and source tensor for a CIM layer reading image x."""
+        n, c, h, w = x.shape
+        if x.pool is not None and x.tensor is None:
+            k, s, src = x.pool
+            st = self._tensor(src)
+            g = cim_ops.conv_gather(abi.GATHER_CONV_NHWC, n, c, h, w, kh, kw, stride, pad)
+            g.pool_kernel, g.pool_stride = k, s
+            g.pool_src_h, g.pool_src_w = src.shape[2], src.shape[3]
+        else:
+            st = self._tensor(x)
+            kind = abi.GATHER_CONV_NCHW if x.layout == "nchw" else abi.GATHER_CONV_NHWC
+            g = cim_ops.conv_gather(kind, n, c, h, w, kh, kw, stride, pad)
+        self._keep.append(g)
+        return g, st
+
     def _nhwc(self, x: Val) -> torch.Tensor:
         if x.layout == "nhwc":
-            return x.tensor
+            return self._tensor(x)
         out = self._new((x.shape[0], x.shape[2], x.shape[3], x.shape[1]))
         xt = x.tensor
         self.steps.append(Step("nchw_to_nhwc", lambda: cim_ops.nchw_to_nhwc(xt, out)))
@@ -439,10 +483,15 @@ class Program:
                     raise NotImplementedError(f"max_pool2d {key}")
         elif p[0] != 0:
             raise NotImplementedError("avg_pool2d padding")
-        xt = self._nhwc(x)
         n, c, h, w = x.shape
         oh = (h + 2 * p[0] - k[0]) // s[0] + 1
         ow = (w + 2 * p[0] - k[0]) // s[0] + 1
+        if self.fuse and kind == "max" and p[0] == 0 and x.layout == "nhwc" and x.pool is None:
+            # Pending: a following CIM layer reads the window max in its gather.
+            env[node] = Val(IMAGE, (n, c, oh, ow), None, "nhwc", nonneg=x.nonneg,
+                            pool=(k[0], s[0], x))
+            return
+        xt = self._nhwc(x)
         out = self._new((n, oh, ow, c))
         if kind == "max":
             self.steps.append(Step("maxpool", lambda: cim_ops.maxpool2d_nhwc(xt, k[0], s[0], p[0], out)))
@@ -464,13 +513,13 @@ class Program:
         if x.kind == IMAGE:
             n, c, h, w = x.shape
             if x.layout == "nhwc" and (h, w) != (1, 1):
-                out = self._new((n, c, h, w))
-                xt = x.tensor
-                self.steps.append(Step("flatten", lambda: cim_ops.nhwc_to_nchw(xt, out)))
-                t = out.view(n, c * h * w)
+                # Pending: a following Linear gathers the image directly.
+                env[node] = Val(MATRIX, (n, c * h * w), None, nonneg=x.nonneg, flat_of=x)
+                if not self.fuse:
+                    self._tensor(env[node])
             else:
-                t = x.tensor.view(n, c * h * w)
-            env[node] = Val(MATRIX, (n, c * h * w), t, nonneg=x.nonneg)
+                env[node] = Val(MATRIX, (n, c * h * w), self._tensor(x).view(n, c * h * w),
+                                nonneg=x.nonneg)
         else:
             env[node] = x
 
@@ -491,7 +540,7 @@ class Program:
         shift = (beta - mean * scale).contiguous()
         st, sh = scale.to(self.device), shift.to(self.device)
         self._keep += [st, sh]
-        xt = self._nhwc(x) if x.kind == IMAGE else x.tensor
+        xt = self._nhwc(x) if x.kind == IMAGE else self._tensor(x)
         act, out_node = self._epilogue(node, users)
         out = self._new(xt.shape)
         self.steps.append(Step("batch_norm",
@@ -504,8 +553,8 @@ class Program:
         dim = args[1] if len(args) > 1 else kwargs.get("dim")
         if x.kind != MATRIX or dim not in (-1, 1):
             raise NotImplementedError("softmax lowers the last dim of a matrix")
-        out = self._new(x.tensor.shape)
-        xt = x.tensor
+        xt = self._tensor(x)
+        out = self._new(xt.shape)
         self.steps.append(Step("softmax", lambda: cim_ops.softmax(xt, out)))
         env[node] = Val(MATRIX, x.shape, out, nonneg=True)
 
@@ -513,12 +562,12 @@ class Program:
         if v.kind == IMAGE and v.layout == "nhwc":
             n, c, h, w = v.shape
             out = self._new((n, c, h, w))
-            xt = v.tensor
+            xt = self._tensor(v)
             self.steps.append(Step("to_nchw", lambda: cim_ops.nhwc_to_nchw(xt, out)))
             return out
         if v.kind == CONST:
             raise NotImplementedError("graph output is a constant")
-        return v.tensor
+        return self._tensor(v)
 
     # ----------------------------------------------------------------- execution
 

@@ -30,106 +30,184 @@ namespace {
 constexpr unsigned kFull = 0xffffffffu;
 
 // ---------------------------------------------------------------------------
-// Gather of the K x columns operand (linear rows or conv im2col).
+// Gather of the K x columns operand (linear rows or conv im2col), with 32-bit
+// index arithmetic (checked on the host) and the K decomposition hoisted out
+// of the column loop.
 
-__device__ __forceinline__ float gather_load(const float *__restrict__ x,
-                                             const cim22_gather &g, int64_t M,
-                                             int64_t K, int64_t m, int64_t k) {
-  if (m >= M || k >= K)
-    return 0.0f;
-  if (g.kind == CIM22_GATHER_ROWS)
-    return x[m * K + k];
-  const int ohw = g.out_h * g.out_w;
-  const int n = static_cast<int>(m / ohw);
-  const int r = static_cast<int>(m - static_cast<int64_t>(n) * ohw);
-  const int oh = r / g.out_w, ow = r - oh * g.out_w;
-  const int khw = g.kernel_h * g.kernel_w;
-  const int c = static_cast<int>(k / khw);
-  const int rk = static_cast<int>(k - static_cast<int64_t>(c) * khw);
-  const int i = rk / g.kernel_w, j = rk - i * g.kernel_w;
-  const int ih = oh * g.stride_h - g.pad_h + i;
-  const int iw = ow * g.stride_w - g.pad_w + j;
-  if (ih < 0 || ih >= g.height || iw < 0 || iw >= g.width)
-    return 0.0f; // explicit zero padding (tensor.pad)
+struct Gather32 {
+  int kind, C, H, W, KH, KW, SH, SW, PH, PW, OH, OW;
+  int PK, PS, SRC_H, SRC_W; // fused max pool (NHWC), PK == 0 when absent
+  int M, K;
+  int pair_rows; // rows layout, even K and 8-byte aligned x: float2 loads
+};
+
+// One element of an NHWC image at (n, ih, iw, c), reading the max over the
+// pool window of the pre-pool image when a pool is fused (NaN propagates like
+// torch.max_pool2d).
+__device__ __forceinline__ float image_load(const float *__restrict__ x,
+                                            const Gather32 &g, int n, int ih,
+                                            int iw, int c) {
   if (g.kind == CIM22_GATHER_CONV_NCHW)
-    return x[((static_cast<int64_t>(n) * g.channels + c) * g.height + ih) *
-                 g.width + iw];
-  return x[((static_cast<int64_t>(n) * g.height + ih) * g.width + iw) *
-               g.channels + c];
+    return x[((static_cast<int64_t>(n) * g.C + c) * g.H + ih) * g.W + iw];
+  if (g.PK == 0)
+    return x[((static_cast<int64_t>(n) * g.H + ih) * g.W + iw) * g.C + c];
+  float m = 0.0f;
+  bool any = false;
+  for (int dy = 0; dy < g.PK; ++dy)
+    for (int dx = 0; dx < g.PK; ++dx) {
+      const float v = x[((static_cast<int64_t>(n) * g.SRC_H + ih * g.PS + dy) * g.SRC_W +
+                         iw * g.PS + dx) * g.C + c];
+      if (!any || v > m || v != v) {
+        m = v;
+        any = true;
+      }
+    }
+  return m;
 }
 
-// ---------------------------------------------------------------------------
-// Prepare: one warp per (column m, K tile t); lane l owns elements 2l, 2l+1.
-// Split x into xp/xn (Passes.cpp:2379-2399), RNE to BF16, then the
-// sign-split input preparation of prepareBF16Input (BF16Compensation.cpp:
-// 92-118): effective exponent of the group maximum, RNE scaling to put the
-// maximum in [1, 2), ExpPrealign at exponent 127. An all-zero group records
-// exponent 127 (its dots are zero, so any finite scale gives +0).
+// Sign-split preparation of one 64-element group held two elements per lane
+// (prepareBF16Input, BF16Compensation.cpp:92-118). Fast path: when the group
+// maximum is a normal BF16 with biased exponent Ex >= 8, scaling by
+// 2^(127-Ex) is exact for every element that stays normal and ExpPrealign
+// then gives (0x80 | m) >> (Ex - e + 1) for a gap Ex - e < 7; elements that
+// would become subnormal (or are subnormal) have gaps >= 7 and align to 0.
+// Other groups take the exact RNE scaling path.
+__device__ __forceinline__ int8_t fast_align(uint32_t p, int emax) {
+  const int e = static_cast<int>(p >> 7);
+  const int gap = emax - e;
+  return (e >= 1 && gap < 7)
+             ? static_cast<int8_t>((0x80u | (p & 0x7fu)) >> (gap + 1))
+             : int8_t{0};
+}
+
+__device__ __forceinline__ void prepare_pair(uint16_t b0, uint16_t b1, int lane,
+                                             int8_t &a0, int8_t &a1,
+                                             int &exponent, int32_t *status) {
+  const bool nonfinite = ((b0 >> 7) & 0xff) == 0xff || ((b1 >> 7) & 0xff) == 0xff;
+  const bool any_nonfinite = __any_sync(kFull, nonfinite);
+  const bool negative = ((b0 & 0x8000) && (b0 & 0x7fff)) || ((b1 & 0x8000) && (b1 & 0x7fff));
+  if (lane == 0 && any_nonfinite)
+    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
+  if (__any_sync(kFull, negative) && !any_nonfinite && lane == 0)
+    atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
+  const uint32_t p0 = b0 & 0x7fffu, p1 = b1 & 0x7fffu;
+  const uint32_t mx = __reduce_max_sync(kFull, max(p0, p1));
+  a0 = a1 = 0;
+  exponent = 127;
+  if (mx == 0 || any_nonfinite)
+    return;
+  const int emax = static_cast<int>(mx >> 7);
+  if (emax >= 8) {
+    exponent = emax;
+    a0 = fast_align(p0, emax);
+    a1 = fast_align(p1, emax);
+    return;
+  }
+  exponent = effective_exponent(static_cast<uint16_t>(mx));
+  const int shift = 127 - exponent;
+  const uint16_t s0 = shift ? bf16_scalbn(static_cast<uint16_t>(p0), shift) : static_cast<uint16_t>(p0);
+  const uint16_t s1 = shift ? bf16_scalbn(static_cast<uint16_t>(p1), shift) : static_cast<uint16_t>(p1);
+  const uint32_t e2 = __reduce_max_sync(
+      kFull, static_cast<uint32_t>(max((s0 >> 7) & 0xff, (s1 >> 7) & 0xff)));
+  a0 = prealign_element(s0, static_cast<int>(e2));
+  a1 = prealign_element(s1, static_cast<int>(e2));
+  if (lane == 0 && e2 != 127)
+    atomicOr(status, CIM22_STATUS_NORMALIZATION);
+}
+
+// Prepare: a warp owns kColsPerWarp consecutive columns of one K tile t; lane
+// l holds elements 2l and 2l + 1 of each 64-element group. Activation split
+// (Passes.cpp:2379-2399): xp = (x < 0 ? 0 : x) then (x == 0 ? +0 : xp),
+// xn = (x < 0 ? -x : 0); both rounded to BF16 (RNE); for a 2-branch layer
+// only the (x == 0 ? +0 : x) select applies. Padding columns (m >= M) and
+// padding K are zero; an all-zero group records exponent 127.
+constexpr int kColsPerWarp = 8;
+
 template <int kActBranches>
 __global__ void __launch_bounds__(256)
-    prepare_kernel(const float *__restrict__ x, cim22_gather g, int64_t M,
-                   int64_t K, int T, int64_t m_pad, int64_t k_pad,
-                   int8_t *__restrict__ A, int32_t *__restrict__ ex,
+    prepare_kernel(const float *__restrict__ x, Gather32 g, int T, int m_pad,
+                   int k_pad, int8_t *__restrict__ A, int32_t *__restrict__ ex,
                    int32_t *status) {
-  const int64_t warp =
-      (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (warp >= m_pad * T)
+  const int warp = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int col_blocks = m_pad / kColsPerWarp;
+  if (warp >= col_blocks * T)
     return;
-  const int64_t m = warp / T;
-  const int t = static_cast<int>(warp - m * T);
-  const int64_t k0 = static_cast<int64_t>(t) * kTileK + 2 * lane;
-  float v[2] = {gather_load(x, g, M, K, m, k0), gather_load(x, g, M, K, m, k0 + 1)};
-  uint16_t bits[2][2];
+  const int t = warp % T;
+  const int mb = warp / T;
+  const int k0 = t * kTileK + 2 * lane;
+  bool kval[2];
+  int kc[2], ki[2], kj[2];
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
-    const float zero = 0.0f;
-    float p = v[e], n = zero;
-    if (kActBranches == 2) {
-      const bool negative = v[e] < zero;
-      p = negative ? zero : v[e];
-      n = negative ? -v[e] : zero;
+    const int k = k0 + e;
+    kval[e] = k < g.K;
+    kc[e] = ki[e] = kj[e] = 0;
+    if (g.kind != CIM22_GATHER_ROWS && kval[e]) {
+      const int khw = g.KH * g.KW;
+      kc[e] = k / khw;
+      const int r = k - kc[e] * khw;
+      ki[e] = r / g.KW;
+      kj[e] = r - ki[e] * g.KW;
     }
-    p = (v[e] == zero) ? zero : p; // -0 becomes +0
-    bits[0][e] = f32_to_bf16(p);
-    bits[1][e] = f32_to_bf16(n);
   }
+  const bool pair_rows = g.pair_rows != 0;
+  const int ohw = g.OH * g.OW;
+  for (int col = 0; col < kColsPerWarp; ++col) {
+    const int m = mb * kColsPerWarp + col;
+    float v[2] = {0.0f, 0.0f};
+    if (m < g.M) {
+      if (g.kind == CIM22_GATHER_ROWS) {
+        const float *row = x + static_cast<int64_t>(m) * g.K;
+        if (pair_rows) {
+          if (kval[0]) {
+            const float2 pv = *reinterpret_cast<const float2 *>(row + k0);
+            v[0] = pv.x;
+            v[1] = pv.y;
+          }
+        } else {
+          v[0] = kval[0] ? row[k0] : 0.0f;
+          v[1] = kval[1] ? row[k0 + 1] : 0.0f;
+        }
+      } else {
+        const int n = m / ohw;
+        const int r = m - n * ohw;
+        const int oh = r / g.OW, ow = r - oh * g.OW;
 #pragma unroll
-  for (int b = 0; b < kActBranches; ++b) {
-    const uint16_t b0 = bits[b][0], b1 = bits[b][1];
-    const bool nonfinite =
-        ((b0 >> 7) & 0xff) == 0xff || ((b1 >> 7) & 0xff) == 0xff;
-    const bool any_nonfinite = __any_sync(kFull, nonfinite);
-    if (any_nonfinite && lane == 0)
-      atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-    // A 2-branch layer asserts its input is nonnegative; the runtime check of
-    // prepareBF16Input (BF16Compensation.cpp:95-96) still applies.
-    const bool negative = ((b0 & 0x8000) && (b0 & 0x7fff)) || ((b1 & 0x8000) && (b1 & 0x7fff));
-    if (!any_nonfinite && __any_sync(kFull, negative) && lane == 0)
-      atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
-    const uint32_t mx = __reduce_max_sync(
-        kFull, static_cast<uint32_t>(max(b0 & 0x7fff, b1 & 0x7fff)));
-    int8_t a0 = 0, a1 = 0;
-    int exponent = 127;
-    if (mx != 0 && !any_nonfinite) {
-      exponent = effective_exponent(static_cast<uint16_t>(mx));
-      const int shift = 127 - exponent;
-      const uint16_t s0 = shift ? bf16_scalbn(b0 & 0x7fff, shift) : (b0 & 0x7fff);
-      const uint16_t s1 = shift ? bf16_scalbn(b1 & 0x7fff, shift) : (b1 & 0x7fff);
-      const uint32_t emax = __reduce_max_sync(
-          kFull, static_cast<uint32_t>(max((s0 >> 7) & 0xff, (s1 >> 7) & 0xff)));
-      a0 = prealign_element(s0, static_cast<int>(emax));
-      a1 = prealign_element(s1, static_cast<int>(emax));
-      if ((emax != 127 || a0 < 0 || a1 < 0))
-        atomicOr(status, CIM22_STATUS_NORMALIZATION);
+        for (int e = 0; e < 2; ++e) {
+          const int ih = oh * g.SH - g.PH + ki[e];
+          const int iw = ow * g.SW - g.PW + kj[e];
+          if (kval[e] && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W)
+            v[e] = image_load(x, g, n, ih, iw, kc[e]);
+        }
+      }
     }
-    uint16_t *row = reinterpret_cast<uint16_t *>(
-        A + (static_cast<int64_t>(b) * m_pad + m) * k_pad +
-        static_cast<int64_t>(t) * kTileK);
-    row[lane] = static_cast<uint16_t>(static_cast<uint8_t>(a0) |
-                                      (static_cast<uint16_t>(static_cast<uint8_t>(a1)) << 8));
-    if (lane == 0)
-      ex[(static_cast<int64_t>(b) * T + t) * m_pad + m] = exponent;
+    uint16_t bits[2][2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float zero = 0.0f;
+      float p = v[e], q = zero;
+      if (kActBranches == 2) {
+        const bool negative = v[e] < zero;
+        p = negative ? zero : v[e];
+        q = negative ? -v[e] : zero;
+      }
+      p = (v[e] == zero) ? zero : p; // -0 becomes +0
+      bits[0][e] = f32_to_bf16(p);
+      bits[1][e] = f32_to_bf16(q);
+    }
+#pragma unroll
+    for (int b = 0; b < kActBranches; ++b) {
+      int8_t a0, a1;
+      int exponent;
+      prepare_pair(bits[b][0], bits[b][1], lane, a0, a1, exponent, status);
+      uint16_t *dst = reinterpret_cast<uint16_t *>(
+          A + (static_cast<int64_t>(b) * m_pad + m) * k_pad + static_cast<int64_t>(t) * kTileK);
+      dst[lane] = static_cast<uint16_t>(static_cast<uint8_t>(a0) |
+                                        (static_cast<uint16_t>(static_cast<uint8_t>(a1)) << 8));
+      if (lane == 0)
+        ex[(static_cast<int64_t>(b) * T + t) * m_pad + m] = exponent;
+    }
   }
 }
 
@@ -155,12 +233,12 @@ __device__ __forceinline__ float apply_act(float v, int act) {
 }
 
 // ---------------------------------------------------------------------------
-// Sign-split contraction on CUDA cores (dp4a). CTA tile 64 columns x 32
-// lanes, all branches. Thread (tr, tc) owns columns tr, tr + 32 and lanes
-// 4tc .. 4tc + 3.
-constexpr int kBM = 64, kBN = 32, kRowStride = 80;
+// Sign-split contraction on CUDA cores (dp4a). CTA tile kBM columns x kBN
+// lanes, all branches; thread (tr, tc) owns columns tr + i * kTR (i < kRM)
+// and lanes 4tc .. 4tc + 3.
+constexpr int kRowStride = 80;
 
-template <int kActBranches>
+template <int kActBranches, int kTC, int kRM>
 __global__ void __launch_bounds__(256)
     signsplit_simt_kernel(const int8_t *__restrict__ A,
                           const int32_t *__restrict__ exA, int64_t m_pad,
@@ -169,22 +247,23 @@ __global__ void __launch_bounds__(256)
                           int64_t k_pad, int T, int64_t M, int64_t N,
                           const float *__restrict__ bias, int act,
                           float *__restrict__ y, int32_t *status) {
+  constexpr int kBN = 4 * kTC, kTR = 256 / kTC, kBM = kTR * kRM;
   __shared__ __align__(16) int8_t As[kActBranches][kBM][kRowStride];
   __shared__ __align__(16) int8_t Bs[2][kBN][kRowStride];
   __shared__ int sExA[kActBranches][kBM];
   __shared__ int sExB[2][kBN];
   __shared__ int sFast;
   const int tid = threadIdx.x;
-  const int tr = tid >> 3, tc = tid & 7;
+  const int tr = tid / kTC, tc = tid % kTC;
   const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
   const int64_t n0 = static_cast<int64_t>(blockIdx.y) * kBN;
-  float acc[kActBranches][2][2][4];
+  float acc[kActBranches][2][kRM][4];
 #pragma unroll
   for (int a = 0; a < kActBranches; ++a)
 #pragma unroll
     for (int w = 0; w < 2; ++w)
 #pragma unroll
-      for (int r = 0; r < 2; ++r)
+      for (int r = 0; r < kRM; ++r)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           acc[a][w][r][c] = 0.0f;
@@ -196,18 +275,18 @@ __global__ void __launch_bounds__(256)
           A + (static_cast<int64_t>(a) * m_pad + m0 + r) * k_pad +
           static_cast<int64_t>(t) * kTileK + c * 16);
     }
-    {
-      const int w = tid / (kBN * 4), r = (tid >> 2) % kBN, c = tid & 3;
+    for (int i = tid; i < 2 * kBN * 4; i += 256) {
+      const int w = i / (kBN * 4), r = (i >> 2) % kBN, c = i & 3;
       *reinterpret_cast<int4 *>(&Bs[w][r][c * 16]) = *reinterpret_cast<const int4 *>(
           B + (static_cast<int64_t>(w) * n_pad + n0 + r) * k_pad +
           static_cast<int64_t>(t) * kTileK + c * 16);
     }
-    if (tid < kActBranches * kBM)
-      sExA[tid / kBM][tid % kBM] =
-          exA[(static_cast<int64_t>(tid / kBM) * T + t) * m_pad + m0 + tid % kBM];
-    if (tid < 2 * kBN)
-      sExB[tid / kBN][tid % kBN] =
-          exB[(static_cast<int64_t>(tid / kBN) * T + t) * n_pad + n0 + tid % kBN];
+    for (int i = tid; i < kActBranches * kBM; i += 256)
+      sExA[i / kBM][i % kBM] =
+          exA[(static_cast<int64_t>(i / kBM) * T + t) * m_pad + m0 + i % kBM];
+    for (int i = tid; i < 2 * kBN; i += 256)
+      sExB[i / kBN][i % kBN] =
+          exB[(static_cast<int64_t>(i / kBN) * T + t) * n_pad + n0 + i % kBN];
     __syncthreads();
     if (tid < 32) {
       int mnA = INT_MAX, mxA = INT_MIN, mnB = INT_MAX, mxB = INT_MIN;
@@ -230,24 +309,24 @@ __global__ void __launch_bounds__(256)
     }
     __syncthreads();
     const bool fast = sFast != 0;
-    int p[kActBranches][2][2][4];
+    int p[kActBranches][2][kRM][4];
 #pragma unroll
     for (int a = 0; a < kActBranches; ++a)
 #pragma unroll
       for (int w = 0; w < 2; ++w)
 #pragma unroll
-        for (int r = 0; r < 2; ++r)
+        for (int r = 0; r < kRM; ++r)
 #pragma unroll
           for (int c = 0; c < 4; ++c)
             p[a][w][r][c] = 0;
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      int4 av[kActBranches][2], bv[2][4];
+      int4 av[kActBranches][kRM], bv[2][4];
 #pragma unroll
       for (int a = 0; a < kActBranches; ++a)
 #pragma unroll
-        for (int r = 0; r < 2; ++r)
-          av[a][r] = *reinterpret_cast<const int4 *>(&As[a][tr + 32 * r][kk * 16]);
+        for (int r = 0; r < kRM; ++r)
+          av[a][r] = *reinterpret_cast<const int4 *>(&As[a][tr + kTR * r][kk * 16]);
 #pragma unroll
       for (int w = 0; w < 2; ++w)
 #pragma unroll
@@ -258,7 +337,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
         for (int w = 0; w < 2; ++w)
 #pragma unroll
-          for (int r = 0; r < 2; ++r)
+          for (int r = 0; r < kRM; ++r)
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               int s = p[a][w][r][c];
@@ -272,30 +351,32 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int a = 0; a < kActBranches; ++a)
 #pragma unroll
-      for (int w = 0; w < 2; ++w)
+      for (int r = 0; r < kRM; ++r) {
+        const int exr = sExA[a][tr + kTR * r];
+        const float sx = exp2i(exr - 133);
 #pragma unroll
-        for (int r = 0; r < 2; ++r)
+        for (int w = 0; w < 2; ++w)
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            const int ex = sExA[a][tr + 32 * r];
             const int ew = sExB[w][tc * 4 + c];
             if (fast) {
-              const float q = __fmul_rn(trunc8f(p[a][w][r][c]), exp2i(ex - 133));
+              const float q = __fmul_rn(trunc8f(p[a][w][r][c]), sx);
               acc[a][w][r][c] = fmaf(q, exp2i(ew - 133), acc[a][w][r][c]);
             } else {
               const uint16_t tile =
-                  signsplit_tile(static_cast<uint32_t>(p[a][w][r][c]), ew, ex);
+                  signsplit_tile(static_cast<uint32_t>(p[a][w][r][c]), ew, exr);
               if (tile == kBF16Inf)
                 atomicOr(status, CIM22_STATUS_TILE_OVERFLOW);
               acc[a][w][r][c] = __fadd_rn(acc[a][w][r][c], bf16_to_f32(tile));
             }
           }
+      }
     __syncthreads();
   }
 
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int64_t row = m0 + tr + 32 * r;
+  for (int r = 0; r < kRM; ++r) {
+    const int64_t row = m0 + tr + kTR * r;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const int64_t lane = n0 + tc * 4 + c;
@@ -318,6 +399,35 @@ __global__ void __launch_bounds__(256)
       if (row < M && lane < N)
         y[row * N + lane] = out;
     }
+  }
+}
+
+// Tile shape per layer: 16-lane tiles for layers of at most 16 lanes (a
+// single crossbar width), 32 otherwise; 2 column rows per thread when that
+// still gives every SM two CTAs.
+template <int kAB>
+void launch_signsplit_simt(const int8_t *A, const int32_t *exA, int64_t m_pad,
+                           const int8_t *B, const int32_t *exB, int64_t n_pad,
+                           int64_t k_pad, int T, int64_t M, int64_t N,
+                           const float *bias, int act, float *y, int32_t *status,
+                           cudaStream_t s) {
+  const int64_t target = 2 * 148;
+  if (N <= 16) {
+    const unsigned ny = static_cast<unsigned>((N + 15) / 16);
+    if ((m_pad / 128) * ny >= target)
+      signsplit_simt_kernel<kAB, 4, 2><<<dim3(static_cast<unsigned>(m_pad / 128), ny), 256, 0, s>>>(
+          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, act, y, status);
+    else
+      signsplit_simt_kernel<kAB, 4, 1><<<dim3(static_cast<unsigned>(m_pad / 64), ny), 256, 0, s>>>(
+          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, act, y, status);
+  } else {
+    const unsigned ny = static_cast<unsigned>((N + 31) / 32);
+    if ((m_pad / 64) * ny >= target)
+      signsplit_simt_kernel<kAB, 8, 2><<<dim3(static_cast<unsigned>(m_pad / 64), ny), 256, 0, s>>>(
+          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, act, y, status);
+    else
+      signsplit_simt_kernel<kAB, 8, 1><<<dim3(static_cast<unsigned>(m_pad / 32), ny), 256, 0, s>>>(
+          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, act, y, status);
   }
 }
 
@@ -402,8 +512,16 @@ __global__ void __launch_bounds__(256)
 }
 
 bool check_gather(const cim22_gather &g, int64_t m, int64_t k) {
+  if (m >= (int64_t{1} << 31) - kColumnPad || k >= (int64_t{1} << 30))
+    return false;
   if (g.kind == CIM22_GATHER_ROWS)
-    return true;
+    return m * k < (int64_t{1} << 40);
+  if (g.pool_kernel < 0 || (g.pool_kernel > 0 &&
+      (g.kind != CIM22_GATHER_CONV_NHWC || g.pool_stride <= 0 ||
+       (g.pool_src_h - g.pool_kernel) / g.pool_stride + 1 != g.height ||
+       (g.pool_src_w - g.pool_kernel) / g.pool_stride + 1 != g.width ||
+       g.pool_src_h < g.pool_kernel || g.pool_src_w < g.pool_kernel)))
+    return false;
   if (g.kind != CIM22_GATHER_CONV_NCHW && g.kind != CIM22_GATHER_CONV_NHWC)
     return false;
   if (g.batch <= 0 || g.channels <= 0 || g.height <= 0 || g.width <= 0 ||
@@ -415,6 +533,33 @@ bool check_gather(const cim22_gather &g, int64_t m, int64_t k) {
   return oh == g.out_h && ow == g.out_w &&
          static_cast<int64_t>(g.batch) * oh * ow == m &&
          static_cast<int64_t>(g.channels) * g.kernel_h * g.kernel_w == k;
+}
+
+Gather32 to_device_gather(const cim22_gather &g, int64_t m, int64_t k, const float *x) {
+  Gather32 d{};
+  d.kind = g.kind;
+  d.pair_rows = g.kind == CIM22_GATHER_ROWS && (k & 1) == 0 &&
+                (reinterpret_cast<uintptr_t>(x) & 7) == 0;
+  d.M = static_cast<int>(m);
+  d.K = static_cast<int>(k);
+  if (g.kind != CIM22_GATHER_ROWS) {
+    d.C = g.channels;
+    d.H = g.height;
+    d.W = g.width;
+    d.KH = g.kernel_h;
+    d.KW = g.kernel_w;
+    d.SH = g.stride_h;
+    d.SW = g.stride_w;
+    d.PH = g.pad_h;
+    d.PW = g.pad_w;
+    d.OH = g.out_h;
+    d.OW = g.out_w;
+    d.PK = g.pool_kernel;
+    d.PS = g.pool_stride;
+    d.SRC_H = g.pool_src_h;
+    d.SRC_W = g.pool_src_w;
+  }
+  return d;
 }
 
 } // namespace
@@ -610,14 +755,15 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
   int8_t *A = static_cast<int8_t *>(workspace);
   int32_t *ex = reinterpret_cast<int32_t *>(
       static_cast<char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
-  const int64_t warps = m_pad * T;
+  const Gather32 dg = to_device_gather(g, m, layer->k, x);
+  const int64_t warps = (m_pad / kColsPerWarp) * T;
   const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
   if (ab == 1)
-    prepare_kernel<1><<<blocks, 256, 0, s>>>(x, g, m, layer->k, T, m_pad,
-                                             layer->k_pad, A, ex, status);
+    prepare_kernel<1><<<blocks, 256, 0, s>>>(x, dg, T, static_cast<int>(m_pad),
+                                             static_cast<int>(layer->k_pad), A, ex, status);
   else
-    prepare_kernel<2><<<blocks, 256, 0, s>>>(x, g, m, layer->k, T, m_pad,
-                                             layer->k_pad, A, ex, status);
+    prepare_kernel<2><<<blocks, 256, 0, s>>>(x, dg, T, static_cast<int>(m_pad),
+                                             static_cast<int>(layer->k_pad), A, ex, status);
   return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
 }
 
@@ -646,16 +792,12 @@ int cim22_cuda_layer_contract_bf16(const cim22_cuda_layer *layer, int64_t m,
                            layer->n_pad, layer->k_pad, T, m, layer->n, bias,
                            activation, ab, y, status, s))
     return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
-  const dim3 grid(static_cast<unsigned>(m_pad / kBM),
-                  static_cast<unsigned>((layer->n + kBN - 1) / kBN));
   if (ab == 1)
-    signsplit_simt_kernel<1><<<grid, 256, 0, s>>>(
-        A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
-        layer->k_pad, T, m, layer->n, bias, activation, y, status);
+    launch_signsplit_simt<1>(A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
+                             layer->k_pad, T, m, layer->n, bias, activation, y, status, s);
   else
-    signsplit_simt_kernel<2><<<grid, 256, 0, s>>>(
-        A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
-        layer->k_pad, T, m, layer->n, bias, activation, y, status);
+    launch_signsplit_simt<2>(A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
+                             layer->k_pad, T, m, layer->n, bias, activation, y, status, s);
   return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
 }
 

@@ -157,3 +157,46 @@ def test_glue_against_torch_cpu():
     torch.testing.assert_close(cim_ops.nhwc_to_nchw(xd).cpu(), nchw.contiguous(), rtol=0, atol=0)
     torch.testing.assert_close(cim_ops.nchw_to_nhwc(nchw.contiguous().to(DEV)).cpu(), x,
                                rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("pool", [0, 2])
+def test_conv_with_fused_pool_and_flatten_gathers(pool):
+    """Max pool folded into the conv gather, and flatten->Linear as a conv whose
+    kernel covers the whole (pooled) NHWC image."""
+    from cim22_b200 import abi
+    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace, conv_gather
+
+    rng = np.random.default_rng(17 + pool)
+    n, c, src = 3, 6, 28
+    pre = rng.standard_normal((n, src, src, c)).astype(np.float32)  # NHWC, pre-pool
+    if pool:
+        pooled = pre.reshape(n, src // 2, 2, src // 2, 2, c).max(axis=(2, 4))
+    else:
+        pooled = pre
+    h = pooled.shape[1]
+    dev = torch.device(DEV)
+    status = StatusWord(dev)
+    # conv 5x5 on the pooled image
+    w = (rng.standard_normal((16, c, 5, 5)) * 0.2).astype(np.float32)
+    g = conv_gather(abi.GATHER_CONV_NHWC, n, c, h, h, 5, 5, 1, 0)
+    if pool:
+        g.pool_kernel, g.pool_stride, g.pool_src_h, g.pool_src_w = 2, 2, src, src
+    m = n * g.out_h * g.out_w
+    out = torch.empty(m, 16, device=dev)
+    CimLayer(w.reshape(16, -1)).forward_bf16(torch.from_numpy(pre).to(dev), out, m, gather=g,
+                                             workspace=Workspace(dev), status=status)
+    status.raise_if_set()
+    exp = oracle.conv2d_bf16(pooled.transpose(0, 3, 1, 2).copy(), w, None, 1, 0)
+    got = out.cpu().numpy().reshape(n, g.out_h, g.out_w, 16).transpose(0, 3, 1, 2)
+    np.testing.assert_array_equal(bits(got), bits(exp))
+    # flatten (NCHW order) -> Linear via the whole-image conv gather
+    wl = (rng.standard_normal((30, c * h * h)) * 0.05).astype(np.float32)
+    gf = conv_gather(abi.GATHER_CONV_NHWC, n, c, h, h, h, h, 1, 0)
+    if pool:
+        gf.pool_kernel, gf.pool_stride, gf.pool_src_h, gf.pool_src_w = 2, 2, src, src
+    outl = torch.empty(n, 30, device=dev)
+    CimLayer(wl).forward_bf16(torch.from_numpy(pre).to(dev), outl, n, gather=gf,
+                              workspace=Workspace(dev), status=status)
+    status.raise_if_set()
+    flat = pooled.transpose(0, 3, 1, 2).reshape(n, -1)
+    np.testing.assert_array_equal(bits(outl.cpu().numpy()), bits(oracle.linear_bf16(flat, wl)))
