@@ -51,6 +51,9 @@ def parse():
     p.add_argument("--cpu-sample", type=int, default=2048,
                    help="images in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--profile", action="store_true",
+                   help="only launch the program's kernels eagerly (warmup + steps passes); "
+                        "for capturing single kernels under a profiler")
     return p.parse_args()
 
 
@@ -189,6 +192,15 @@ def main() -> None:
 
     prog = program.from_module(model, x, device=local, name=args.workload)
     prog.inputs[0].tensor.copy_(x.to(dev))
+    if args.profile:
+        for _ in range(args.warmup + args.steps):
+            prog.status.reset()
+            prog.launch()
+        torch.cuda.synchronize(dev)
+        prog.check_status()
+        print(json.dumps({"profile": args.workload, "passes": args.warmup + args.steps,
+                          "kernels": [s.name for s in prog.steps]}))
+        return
     prog.capture()
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
