@@ -65,13 +65,14 @@ __device__ __forceinline__ float image_load(const float *__restrict__ x,
   return m;
 }
 
-// Sign-split preparation of one 64-element group held two elements per lane
-// (prepareBF16Input, BF16Compensation.cpp:92-118). Fast path: when the group
-// maximum is a normal BF16 with biased exponent Ex >= 8, scaling by
-// 2^(127-Ex) is exact for every element that stays normal and ExpPrealign
-// then gives (0x80 | m) >> (Ex - e + 1) for a gap Ex - e < 7; elements that
-// would become subnormal (or are subnormal) have gaps >= 7 and align to 0.
-// Other groups take the exact RNE scaling path.
+// Sign-split preparation of a 64-element group (prepareBF16Input,
+// BF16Compensation.cpp:92-118). Fast path: when the group maximum is a normal
+// BF16 with biased exponent Ex >= 8, scaling by 2^(127-Ex) is exact for every
+// element that stays normal, and ExpPrealign then yields (0x80 | m) >>
+// (Ex - e + 1) for a gap Ex - e < 7; elements that would turn subnormal (or
+// are subnormal) have gaps >= 7 and align to 0. Other groups take the exact
+// RNE scaling of bf16_scalbn. The scaled maximum lies in [1, 2), so the
+// prealign exponent is always 127.
 __device__ __forceinline__ int8_t fast_align(uint32_t p, int emax) {
   const int e = static_cast<int>(p >> 7);
   const int gap = emax - e;
@@ -80,134 +81,158 @@ __device__ __forceinline__ int8_t fast_align(uint32_t p, int emax) {
              : int8_t{0};
 }
 
-__device__ __forceinline__ void prepare_pair(uint16_t b0, uint16_t b1, int lane,
-                                             int8_t &a0, int8_t &a1,
-                                             int &exponent, int32_t *status) {
-  const bool nonfinite = ((b0 >> 7) & 0xff) == 0xff || ((b1 >> 7) & 0xff) == 0xff;
-  const bool any_nonfinite = __any_sync(kFull, nonfinite);
-  const bool negative = ((b0 & 0x8000) && (b0 & 0x7fff)) || ((b1 & 0x8000) && (b1 & 0x7fff));
-  if (lane == 0 && any_nonfinite)
-    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-  if (__any_sync(kFull, negative) && !any_nonfinite && lane == 0)
-    atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
-  const uint32_t p0 = b0 & 0x7fffu, p1 = b1 & 0x7fffu;
-  const uint32_t mx = __reduce_max_sync(kFull, max(p0, p1));
-  a0 = a1 = 0;
-  exponent = 127;
-  if (mx == 0 || any_nonfinite)
-    return;
-  const int emax = static_cast<int>(mx >> 7);
-  if (emax >= 8) {
-    exponent = emax;
-    a0 = fast_align(p0, emax);
-    a1 = fast_align(p1, emax);
-    return;
-  }
-  exponent = effective_exponent(static_cast<uint16_t>(mx));
-  const int shift = 127 - exponent;
-  const uint16_t s0 = shift ? bf16_scalbn(static_cast<uint16_t>(p0), shift) : static_cast<uint16_t>(p0);
-  const uint16_t s1 = shift ? bf16_scalbn(static_cast<uint16_t>(p1), shift) : static_cast<uint16_t>(p1);
-  const uint32_t e2 = __reduce_max_sync(
-      kFull, static_cast<uint32_t>(max((s0 >> 7) & 0xff, (s1 >> 7) & 0xff)));
-  a0 = prealign_element(s0, static_cast<int>(e2));
-  a1 = prealign_element(s1, static_cast<int>(e2));
-  if (lane == 0 && e2 != 127)
-    atomicOr(status, CIM22_STATUS_NORMALIZATION);
+__device__ __forceinline__ uint32_t align_byte(uint32_t p, int emax, int shift, bool fast) {
+  const int8_t a = fast ? fast_align(p, emax)
+                        : prealign_element(bf16_scalbn(static_cast<uint16_t>(p), shift), 127);
+  return static_cast<uint8_t>(a);
 }
 
-// Prepare: a warp owns kColsPerWarp consecutive columns of one K tile t; lane
-// l holds elements 2l and 2l + 1 of each 64-element group. Activation split
-// (Passes.cpp:2379-2399): xp = (x < 0 ? 0 : x) then (x == 0 ? +0 : xp),
-// xn = (x < 0 ? -x : 0); both rounded to BF16 (RNE); for a 2-branch layer
-// only the (x == 0 ? +0 : x) select applies. Padding columns (m >= M) and
-// padding K are zero; an all-zero group records exponent 127.
-constexpr int kColsPerWarp = 8;
-
+// Activation split (Passes.cpp:2379-2399): xp = (x < 0 ? 0 : x) then
+// (x == 0 ? +0 : xp), xn = (x < 0 ? -x : 0), each rounded to BF16 (RNE); a
+// 2-branch layer applies only the (x == 0 ? +0 : x) select.
 template <int kActBranches>
-__global__ void __launch_bounds__(256)
+__device__ __forceinline__ void split_bits(float v, uint32_t &bp, uint32_t &bn) {
+  const float zero = 0.0f;
+  float p = v, q = zero;
+  if (kActBranches == 2) {
+    const bool negative = v < zero;
+    p = negative ? zero : v;
+    q = negative ? -v : zero;
+  }
+  p = (v == zero) ? zero : p; // -0 becomes +0
+  bp = f32_to_bf16(p);
+  bn = f32_to_bf16(q);
+}
+
+// Element source of one group: consecutive K indices of one column, with the
+// conv (c, i, j) decomposition stepped incrementally.
+struct GroupCursor {
+  const float *row; // rows layout
+  int n, oh, ow;    // conv column
+  int c, i, j;      // conv position of the current k
+  int k;
+  bool column_valid;
+};
+
+__device__ __forceinline__ GroupCursor open_group(const float *__restrict__ x, const Gather32 &g,
+                                                  int m, int kbeg) {
+  GroupCursor cur{};
+  cur.k = kbeg;
+  cur.column_valid = m < g.M;
+  if (g.kind == CIM22_GATHER_ROWS) {
+    cur.row = x + static_cast<int64_t>(m) * g.K;
+  } else if (cur.column_valid) {
+    const int ohw = g.OH * g.OW;
+    cur.n = m / ohw;
+    const int r = m - cur.n * ohw;
+    cur.oh = r / g.OW;
+    cur.ow = r - cur.oh * g.OW;
+    const int khw = g.KH * g.KW;
+    cur.c = kbeg / khw;
+    const int rk = kbeg - cur.c * khw;
+    cur.i = rk / g.KW;
+    cur.j = rk - cur.i * g.KW;
+  }
+  return cur;
+}
+
+__device__ __forceinline__ float next_value(const float *__restrict__ x, const Gather32 &g,
+                                            GroupCursor &cur) {
+  float v = 0.0f;
+  if (cur.column_valid && cur.k < g.K) {
+    if (g.kind == CIM22_GATHER_ROWS) {
+      v = cur.row[cur.k];
+    } else {
+      const int ih = cur.oh * g.SH - g.PH + cur.i;
+      const int iw = cur.ow * g.SW - g.PW + cur.j;
+      if (ih >= 0 && ih < g.H && iw >= 0 && iw < g.W)
+        v = image_load(x, g, cur.n, ih, iw, cur.c);
+      if (++cur.j == g.KW) {
+        cur.j = 0;
+        if (++cur.i == g.KH) {
+          cur.i = 0;
+          ++cur.c;
+        }
+      }
+    }
+  }
+  ++cur.k;
+  return v;
+}
+
+// Prepare: one thread per (column m, K tile t) group; consecutive threads own
+// consecutive columns. Pass 1 finds each branch's group maximum (and the
+// error flags); pass 2 regenerates the elements, aligns them and writes the
+// group's 64 bytes per branch as four 16-byte stores. Padding columns
+// (m >= M) and padding K are zero; an all-zero group records exponent 127.
+template <int kActBranches>
+__global__ void __launch_bounds__(256, 3)
     prepare_kernel(const float *__restrict__ x, Gather32 g, int T, int m_pad,
                    int k_pad, int8_t *__restrict__ A, int32_t *__restrict__ ex,
                    int32_t *status) {
-  const int lane = threadIdx.x & 31;
-  const int warp = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
-  const int col_blocks = m_pad / kColsPerWarp;
-  if (warp >= col_blocks * T)
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (gid >= static_cast<int64_t>(m_pad) * T)
     return;
-  const int t = warp % T;
-  const int mb = warp / T;
-  const int k0 = t * kTileK + 2 * lane;
-  bool kval[2];
-  int kc[2], ki[2], kj[2];
+  const int m = static_cast<int>(gid % m_pad);
+  const int t = static_cast<int>(gid / m_pad);
+  const int kbeg = t * kTileK;
+  uint32_t mx[2] = {0, 0};
+  bool nonfinite = false, negative = false;
+  {
+    GroupCursor cur = open_group(x, g, m, kbeg);
+    const int kend = min(g.K, kbeg + kTileK);
+    for (int k = kbeg; k < kend; ++k) {
+      uint32_t b[2];
+      split_bits<kActBranches>(next_value(x, g, cur), b[0], b[1]);
 #pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const int k = k0 + e;
-    kval[e] = k < g.K;
-    kc[e] = ki[e] = kj[e] = 0;
-    if (g.kind != CIM22_GATHER_ROWS && kval[e]) {
-      const int khw = g.KH * g.KW;
-      kc[e] = k / khw;
-      const int r = k - kc[e] * khw;
-      ki[e] = r / g.KW;
-      kj[e] = r - ki[e] * g.KW;
+      for (int a = 0; a < kActBranches; ++a) {
+        nonfinite |= ((b[a] >> 7) & 0xffu) == 0xffu;
+        negative |= (b[a] & 0x8000u) && (b[a] & 0x7fffu);
+        mx[a] = max(mx[a], b[a] & 0x7fffu);
+      }
     }
   }
-  const bool pair_rows = g.pair_rows != 0;
-  const int ohw = g.OH * g.OW;
-  for (int col = 0; col < kColsPerWarp; ++col) {
-    const int m = mb * kColsPerWarp + col;
-    float v[2] = {0.0f, 0.0f};
-    if (m < g.M) {
-      if (g.kind == CIM22_GATHER_ROWS) {
-        const float *row = x + static_cast<int64_t>(m) * g.K;
-        if (pair_rows) {
-          if (kval[0]) {
-            const float2 pv = *reinterpret_cast<const float2 *>(row + k0);
-            v[0] = pv.x;
-            v[1] = pv.y;
-          }
-        } else {
-          v[0] = kval[0] ? row[k0] : 0.0f;
-          v[1] = kval[1] ? row[k0 + 1] : 0.0f;
-        }
-      } else {
-        const int n = m / ohw;
-        const int r = m - n * ohw;
-        const int oh = r / g.OW, ow = r - oh * g.OW;
+  if (nonfinite)
+    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
+  else if (negative)
+    atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
+  int emax[2], shift[2];
+  bool fast[2], zero[2];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int ih = oh * g.SH - g.PH + ki[e];
-          const int iw = ow * g.SW - g.PW + kj[e];
-          if (kval[e] && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W)
-            v[e] = image_load(x, g, n, ih, iw, kc[e]);
+  for (int a = 0; a < kActBranches; ++a) {
+    zero[a] = mx[a] == 0 || nonfinite;
+    emax[a] = zero[a] ? 127 : effective_exponent(static_cast<uint16_t>(mx[a]));
+    fast[a] = static_cast<int>(mx[a] >> 7) >= 8;
+    shift[a] = 127 - emax[a];
+    ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax[a];
+  }
+  GroupCursor cur = open_group(x, g, m, kbeg);
+#pragma unroll 1
+  for (int chunk = 0; chunk < 4; ++chunk) {
+    uint32_t words[kActBranches][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[2] = {0, 0};
+#pragma unroll
+      for (int byte = 0; byte < 4; ++byte) {
+        uint32_t b[2];
+        split_bits<kActBranches>(next_value(x, g, cur), b[0], b[1]);
+#pragma unroll
+        for (int a = 0; a < kActBranches; ++a) {
+          const uint32_t p = b[a] & 0x7fffu;
+          const uint32_t v = zero[a] ? 0u : align_byte(p, emax[a], shift[a], fast[a]);
+          w[a] |= v << (8 * byte);
         }
       }
-    }
-    uint16_t bits[2][2];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float zero = 0.0f;
-      float p = v[e], q = zero;
-      if (kActBranches == 2) {
-        const bool negative = v[e] < zero;
-        p = negative ? zero : v[e];
-        q = negative ? -v[e] : zero;
-      }
-      p = (v[e] == zero) ? zero : p; // -0 becomes +0
-      bits[0][e] = f32_to_bf16(p);
-      bits[1][e] = f32_to_bf16(q);
+      for (int a = 0; a < kActBranches; ++a)
+        words[a][q] = w[a];
     }
 #pragma unroll
-    for (int b = 0; b < kActBranches; ++b) {
-      int8_t a0, a1;
-      int exponent;
-      prepare_pair(bits[b][0], bits[b][1], lane, a0, a1, exponent, status);
-      uint16_t *dst = reinterpret_cast<uint16_t *>(
-          A + (static_cast<int64_t>(b) * m_pad + m) * k_pad + static_cast<int64_t>(t) * kTileK);
-      dst[lane] = static_cast<uint16_t>(static_cast<uint8_t>(a0) |
-                                        (static_cast<uint16_t>(static_cast<uint8_t>(a1)) << 8));
-      if (lane == 0)
-        ex[(static_cast<int64_t>(b) * T + t) * m_pad + m] = exponent;
-    }
+    for (int a = 0; a < kActBranches; ++a)
+      *reinterpret_cast<uint4 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad +
+                                 static_cast<int64_t>(t) * kTileK + chunk * 16) =
+          make_uint4(words[a][0], words[a][1], words[a][2], words[a][3]);
   }
 }
 
@@ -402,9 +427,9 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Tile shape per layer: 16-lane tiles for layers of at most 16 lanes (a
-// single crossbar width), 32 otherwise; 2 column rows per thread when that
-// still gives every SM two CTAs.
+// Tile shape per layer: 8 or 16-lane tiles for layers of at most 8 or 16
+// lanes, 32 otherwise; 2 column rows per thread when that still gives every
+// SM two CTAs.
 template <int kAB>
 void launch_signsplit_simt(const int8_t *A, const int32_t *exA, int64_t m_pad,
                            const int8_t *B, const int32_t *exB, int64_t n_pad,
@@ -412,7 +437,10 @@ void launch_signsplit_simt(const int8_t *A, const int32_t *exA, int64_t m_pad,
                            const float *bias, int act, float *y, int32_t *status,
                            cudaStream_t s) {
   const int64_t target = 2 * 148;
-  if (N <= 16) {
+  if (N <= 8) {
+    signsplit_simt_kernel<kAB, 2, 1><<<dim3(static_cast<unsigned>(m_pad / 128), 1), 256, 0, s>>>(
+        A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, act, y, status);
+  } else if (N <= 16) {
     const unsigned ny = static_cast<unsigned>((N + 15) / 16);
     if ((m_pad / 128) * ny >= target)
       signsplit_simt_kernel<kAB, 4, 2><<<dim3(static_cast<unsigned>(m_pad / 128), ny), 256, 0, s>>>(
@@ -756,8 +784,7 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
   int32_t *ex = reinterpret_cast<int32_t *>(
       static_cast<char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
   const Gather32 dg = to_device_gather(g, m, layer->k, x);
-  const int64_t warps = (m_pad / kColsPerWarp) * T;
-  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  const unsigned blocks = static_cast<unsigned>((m_pad * T + 255) / 256);
   if (ab == 1)
     prepare_kernel<1><<<blocks, 256, 0, s>>>(x, dg, T, static_cast<int>(m_pad),
                                              static_cast<int>(layer->k_pad), A, ex, status);
