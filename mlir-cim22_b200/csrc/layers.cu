@@ -38,7 +38,7 @@ struct Gather32 {
   int kind, C, H, W, KH, KW, SH, SW, PH, PW, OH, OW;
   int PK, PS, SRC_H, SRC_W; // fused max pool (NHWC), PK == 0 when absent
   int M, K;
-  int pair_rows; // rows layout, even K and 8-byte aligned x: float2 loads
+  int pair_rows; // rows layout: 2 when K % 4 == 0 and x is 16-byte aligned (float4 loads)
 };
 
 // One element of an NHWC image at (n, ih, iw, c), reading the max over the
@@ -160,79 +160,82 @@ __device__ __forceinline__ float next_value(const float *__restrict__ x, const G
   return v;
 }
 
-// Prepare: one thread per (column m, K tile t) group; consecutive threads own
-// consecutive columns. Pass 1 finds each branch's group maximum (and the
-// error flags); pass 2 regenerates the elements, aligns them and writes the
-// group's 64 bytes per branch as four 16-byte stores. Padding columns
-// (m >= M) and padding K are zero; an all-zero group records exponent 127.
+// Prepare: eight threads per (column m, K tile t) group, eight consecutive
+// elements each; groups are ordered t-fastest so a warp's four groups read
+// one contiguous stretch of a row. The group maximum of each branch is an
+// xor-shuffle reduction within the 8-lane subgroup; each thread then writes
+// its 8 aligned bytes per branch. Padding columns (m >= M) and padding K are
+// zero; an all-zero group records exponent 127.
+constexpr int kGroupThreads = 8;
+
 template <int kActBranches>
-__global__ void __launch_bounds__(256, 3)
+__global__ void __launch_bounds__(256)
     prepare_kernel(const float *__restrict__ x, Gather32 g, int T, int m_pad,
                    int k_pad, int8_t *__restrict__ A, int32_t *__restrict__ ex,
                    int32_t *status) {
-  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (gid >= static_cast<int64_t>(m_pad) * T)
-    return;
-  const int m = static_cast<int>(gid % m_pad);
-  const int t = static_cast<int>(gid / m_pad);
-  const int kbeg = t * kTileK;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t group = tid / kGroupThreads;
+  const int sub = static_cast<int>(threadIdx.x % kGroupThreads);
+  if (group >= static_cast<int64_t>(m_pad) * T)
+    return; // uniform per 8-lane subgroup (blockDim is a multiple of 8)
+  const unsigned mask = 0xffu << (threadIdx.x & 24);
+  const int m = static_cast<int>(group / T);
+  const int t = static_cast<int>(group - static_cast<int64_t>(m) * T);
+  const int kbeg = t * kTileK + sub * 8;
+  float v[8];
+  if (g.kind == CIM22_GATHER_ROWS && g.pair_rows == 2 && m < g.M && kbeg + 8 <= g.K) {
+    const float4 *src = reinterpret_cast<const float4 *>(x + static_cast<int64_t>(m) * g.K + kbeg);
+    const float4 lo = src[0], hi = src[1];
+    v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
+    v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+  } else {
+    GroupCursor cur = open_group(x, g, m, kbeg);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      v[e] = next_value(x, g, cur);
+  }
+  uint32_t bits[2][8];
   uint32_t mx[2] = {0, 0};
   bool nonfinite = false, negative = false;
-  {
-    GroupCursor cur = open_group(x, g, m, kbeg);
-    const int kend = min(g.K, kbeg + kTileK);
-    for (int k = kbeg; k < kend; ++k) {
-      uint32_t b[2];
-      split_bits<kActBranches>(next_value(x, g, cur), b[0], b[1]);
 #pragma unroll
-      for (int a = 0; a < kActBranches; ++a) {
-        nonfinite |= ((b[a] >> 7) & 0xffu) == 0xffu;
-        negative |= (b[a] & 0x8000u) && (b[a] & 0x7fffu);
-        mx[a] = max(mx[a], b[a] & 0x7fffu);
-      }
+  for (int e = 0; e < 8; ++e) {
+    split_bits<kActBranches>(v[e], bits[0][e], bits[1][e]);
+#pragma unroll
+    for (int a = 0; a < kActBranches; ++a) {
+      nonfinite |= ((bits[a][e] >> 7) & 0xffu) == 0xffu;
+      negative |= (bits[a][e] & 0x8000u) && (bits[a][e] & 0x7fffu);
+      bits[a][e] &= 0x7fffu;
+      mx[a] = max(mx[a], bits[a][e]);
     }
   }
-  if (nonfinite)
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a)
+#pragma unroll
+    for (int o = 4; o; o >>= 1)
+      mx[a] = max(mx[a], __shfl_xor_sync(mask, mx[a], o, kGroupThreads));
+  nonfinite = __any_sync(mask, nonfinite);
+  if (sub == 0 && nonfinite)
     atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-  else if (negative)
+  if (negative && !nonfinite)
     atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
-  int emax[2], shift[2];
-  bool fast[2], zero[2];
 #pragma unroll
   for (int a = 0; a < kActBranches; ++a) {
-    zero[a] = mx[a] == 0 || nonfinite;
-    emax[a] = zero[a] ? 127 : effective_exponent(static_cast<uint16_t>(mx[a]));
-    fast[a] = static_cast<int>(mx[a] >> 7) >= 8;
-    shift[a] = 127 - emax[a];
-    ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax[a];
-  }
-  GroupCursor cur = open_group(x, g, m, kbeg);
-#pragma unroll 1
-  for (int chunk = 0; chunk < 4; ++chunk) {
-    uint32_t words[kActBranches][4];
+    const bool zero = mx[a] == 0 || nonfinite;
+    const int emax = zero ? 127 : effective_exponent(static_cast<uint16_t>(mx[a]));
+    const bool fast = static_cast<int>(mx[a] >> 7) >= 8;
+    const int shift = 127 - emax;
+    uint32_t lo = 0, hi = 0;
+    if (!zero) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint32_t w[2] = {0, 0};
-#pragma unroll
-      for (int byte = 0; byte < 4; ++byte) {
-        uint32_t b[2];
-        split_bits<kActBranches>(next_value(x, g, cur), b[0], b[1]);
-#pragma unroll
-        for (int a = 0; a < kActBranches; ++a) {
-          const uint32_t p = b[a] & 0x7fffu;
-          const uint32_t v = zero[a] ? 0u : align_byte(p, emax[a], shift[a], fast[a]);
-          w[a] |= v << (8 * byte);
-        }
+      for (int e = 0; e < 4; ++e) {
+        lo |= align_byte(bits[a][e], emax, shift, fast) << (8 * e);
+        hi |= align_byte(bits[a][e + 4], emax, shift, fast) << (8 * e);
       }
-#pragma unroll
-      for (int a = 0; a < kActBranches; ++a)
-        words[a][q] = w[a];
     }
-#pragma unroll
-    for (int a = 0; a < kActBranches; ++a)
-      *reinterpret_cast<uint4 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad +
-                                 static_cast<int64_t>(t) * kTileK + chunk * 16) =
-          make_uint4(words[a][0], words[a][1], words[a][2], words[a][3]);
+    *reinterpret_cast<uint2 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) =
+        make_uint2(lo, hi);
+    if (sub == 0)
+      ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax;
   }
 }
 
@@ -566,8 +569,8 @@ bool check_gather(const cim22_gather &g, int64_t m, int64_t k) {
 Gather32 to_device_gather(const cim22_gather &g, int64_t m, int64_t k, const float *x) {
   Gather32 d{};
   d.kind = g.kind;
-  d.pair_rows = g.kind == CIM22_GATHER_ROWS && (k & 1) == 0 &&
-                (reinterpret_cast<uintptr_t>(x) & 7) == 0;
+  d.pair_rows = (g.kind == CIM22_GATHER_ROWS && (k & 3) == 0 &&
+                 (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 2 : 0;
   d.M = static_cast<int>(m);
   d.K = static_cast<int>(k);
   if (g.kind != CIM22_GATHER_ROWS) {
@@ -784,7 +787,7 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
   int32_t *ex = reinterpret_cast<int32_t *>(
       static_cast<char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
   const Gather32 dg = to_device_gather(g, m, layer->k, x);
-  const unsigned blocks = static_cast<unsigned>((m_pad * T + 255) / 256);
+  const unsigned blocks = static_cast<unsigned>((m_pad * T * kGroupThreads + 255) / 256);
   if (ab == 1)
     prepare_kernel<1><<<blocks, 256, 0, s>>>(x, dg, T, static_cast<int>(m_pad),
                                              static_cast<int>(layer->k_pad), A, ex, status);
