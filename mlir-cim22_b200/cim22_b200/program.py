@@ -310,14 +310,7 @@ class Program:
                                 workspace=self.workspace, status=self.status)
 
         name = f"conv{len(self.layers)}"
-        if layer.n <= 16:
-            # Narrow layers run as one fused kernel (no workspace round trip).
-            def run():
-                layer.forward_bf16(xt, out, m, gather=g, bias=bias, activation=act,
-                                   branches=branches, workspace=self.workspace,
-                                   status=self.status)
-        else:
-            self.steps.append(Step(name + ".prepare", prepare))
+        self.steps.append(Step(name + ".prepare", prepare))
         self.steps.append(Step(name, run, cim=True, meta=dict(
             kind="conv", x=xt, layout=x.layout, weight=torch.as_tensor(w).detach().float(),
             bias=None if b is None else torch.as_tensor(b).detach().float(), stride=stride[0],
@@ -359,13 +352,7 @@ class Program:
                                 workspace=self.workspace, status=self.status)
 
         name = f"linear{len(self.layers)}"
-        if layer.n <= 16:
-            def run():
-                layer.forward_bf16(xt, out, m, gather=g, bias=bias, activation=act,
-                                   branches=branches, workspace=self.workspace,
-                                   status=self.status)
-        else:
-            self.steps.append(Step(name + ".prepare", prepare))
+        self.steps.append(Step(name + ".prepare", prepare))
         self.steps.append(Step(name, run, cim=True, meta=dict(
             kind="linear", x=xt, weight=torch.as_tensor(w).detach().float(),
             bias=None if b is None else torch.as_tensor(b).detach().float(), out=out, act=act,
