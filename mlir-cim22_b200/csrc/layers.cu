@@ -463,177 +463,6 @@ void launch_signsplit_simt(const int8_t *A, const int32_t *exA, int64_t m_pad,
 }
 
 // ---------------------------------------------------------------------------
-// Narrow layers (at most 16 lanes): one fused kernel per layer, one thread per
-// column. For every K tile the thread gathers its 64-element group twice
-// (maximum, then alignment; the second pass hits L1), keeps the aligned
-// mantissas as 16 packed words per activation branch, takes the 16-word dp4a
-// dot with every lane of both weight branches (weights in shared memory, read
-// as broadcasts), restores and accumulates the tile values in f32 in tile
-// order, and finally rounds, merges, adds the bias and applies the
-// activation. Nothing is written to the workspace.
-constexpr int kNarrowThreads = 128;
-
-template <int kActBranches, int kNL>
-__global__ void __launch_bounds__(kNarrowThreads)
-    narrow_kernel(const float *__restrict__ x, Gather32 g, int T,
-                  const int8_t *__restrict__ B, const int32_t *__restrict__ exB,
-                  int64_t n_pad, int64_t k_pad, int N,
-                  const float *__restrict__ bias, int act,
-                  float *__restrict__ y, int32_t *status) {
-  __shared__ __align__(16) uint32_t sB[2][kNL][16];
-  __shared__ int sEw[2][kNL];
-  __shared__ int sEwMin, sEwMax;
-  // Each thread's aligned mantissas, 16 words per branch; stride 17 keeps the
-  // column-per-thread accesses free of bank conflicts.
-  __shared__ uint32_t sA[kActBranches][kNarrowThreads][17];
-  const int tid = static_cast<int>(threadIdx.x);
-  const int m = static_cast<int>(blockIdx.x) * kNarrowThreads + tid;
-  float acc[kActBranches][2][kNL];
-#pragma unroll
-  for (int a = 0; a < kActBranches; ++a)
-#pragma unroll
-    for (int w = 0; w < 2; ++w)
-#pragma unroll
-      for (int n = 0; n < kNL; ++n)
-        acc[a][w][n] = 0.0f;
-  bool nonfinite = false, negative = false;
-  GroupCursor cur = open_group(x, g, m, 0);
-  for (int t = 0; t < T; ++t) {
-    __syncthreads();
-    for (int i = tid; i < 2 * kNL * 16; i += kNarrowThreads) {
-      const int w = i / (kNL * 16), n = (i / 16) % kNL, q = i % 16;
-      sB[w][n][q] = *reinterpret_cast<const uint32_t *>(
-          B + (static_cast<int64_t>(w) * n_pad + n) * k_pad + static_cast<int64_t>(t) * kTileK + 4 * q);
-    }
-    if (tid < 2 * kNL)
-      sEw[tid / kNL][tid % kNL] = exB[(static_cast<int64_t>(tid / kNL) * T + t) * n_pad + tid % kNL];
-    __syncthreads();
-    if (tid == 0) {
-      int lo = sEw[0][0], hi = sEw[0][0];
-      for (int i = 0; i < 2 * kNL; ++i) {
-        lo = min(lo, sEw[i / kNL][i % kNL]);
-        hi = max(hi, sEw[i / kNL][i % kNL]);
-      }
-      sEwMin = lo;
-      sEwMax = hi;
-    }
-    // Pass 1: group maxima.
-    const GroupCursor start = cur;
-    uint32_t mx[2] = {0, 0};
-#pragma unroll 4
-    for (int e = 0; e < kTileK; ++e) {
-      uint32_t b[2];
-      split_bits<kActBranches>(next_value(x, g, cur), b[0], b[1]);
-#pragma unroll
-      for (int a = 0; a < kActBranches; ++a) {
-        nonfinite |= ((b[a] >> 7) & 0xffu) == 0xffu;
-        negative |= (b[a] & 0x8000u) && (b[a] & 0x7fffu);
-        mx[a] = max(mx[a], b[a] & 0x7fffu);
-      }
-    }
-    // Pass 2: aligned mantissas, 4 per word, into this thread's row.
-    int ex[2];
-    bool fast[2], zero[2];
-    int shift[2];
-#pragma unroll
-    for (int a = 0; a < kActBranches; ++a) {
-      zero[a] = mx[a] == 0;
-      ex[a] = zero[a] ? 127 : effective_exponent(static_cast<uint16_t>(mx[a]));
-      fast[a] = static_cast<int>(mx[a] >> 7) >= 8;
-      shift[a] = 127 - ex[a];
-    }
-    {
-      GroupCursor again = start;
-#pragma unroll 1
-      for (int q = 0; q < 16; ++q) {
-        uint32_t w[2] = {0, 0};
-#pragma unroll
-        for (int byte = 0; byte < 4; ++byte) {
-          uint32_t b[2];
-          split_bits<kActBranches>(next_value(x, g, again), b[0], b[1]);
-#pragma unroll
-          for (int a = 0; a < kActBranches; ++a)
-            if (!zero[a])
-              w[a] |= align_byte(b[a] & 0x7fffu, ex[a], shift[a], fast[a]) << (8 * byte);
-        }
-#pragma unroll
-        for (int a = 0; a < kActBranches; ++a)
-          sA[a][tid][q] = w[a];
-      }
-    }
-    __syncthreads();
-    const int ewlo = sEwMin, ewhi = sEwMax;
-#pragma unroll
-    for (int a = 0; a < kActBranches; ++a) {
-      if (zero[a])
-        continue; // every dot of an all-zero group is 0: the tile adds +0
-      const bool fa = ex[a] + ewlo >= 140 && ex[a] + ewhi <= 374 && ex[a] <= 240;
-      const float sx = exp2i(ex[a] - 133);
-      uint32_t wa[16];
-#pragma unroll
-      for (int q = 0; q < 16; ++q)
-        wa[q] = sA[a][tid][q];
-#pragma unroll
-      for (int w = 0; w < 2; ++w)
-#pragma unroll
-        for (int n = 0; n < kNL; ++n) {
-          int p = 0;
-#pragma unroll
-          for (int q = 0; q < 16; ++q)
-            p = __dp4a(static_cast<int>(wa[q]), static_cast<int>(sB[w][n][q]), p);
-          const int ew = sEw[w][n];
-          if (fa) {
-            acc[a][w][n] = fmaf(__fmul_rn(trunc8f(p), sx), exp2i(ew - 133), acc[a][w][n]);
-          } else {
-            const uint16_t tile = signsplit_tile(static_cast<uint32_t>(p), ew, ex[a]);
-            if (tile == kBF16Inf && n < N)
-              atomicOr(status, CIM22_STATUS_TILE_OVERFLOW);
-            acc[a][w][n] = __fadd_rn(acc[a][w][n], bf16_to_f32(tile));
-          }
-        }
-    }
-  }
-  if (nonfinite)
-    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-  else if (negative)
-    atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
-  if (m >= g.M)
-    return;
-#pragma unroll
-  for (int n = 0; n < kNL; ++n) {
-    if (n >= N)
-      break;
-    float br[kActBranches][2];
-#pragma unroll
-    for (int a = 0; a < kActBranches; ++a)
-#pragma unroll
-      for (int w = 0; w < 2; ++w)
-        br[a][w] = T > 1 ? bf16_to_f32(f32_to_bf16(acc[a][w][n])) : acc[a][w][n];
-    float out = __fsub_rn(br[0][0], br[0][1]);
-    if (kActBranches == 2) {
-      out = __fsub_rn(out, br[1][0]);
-      out = __fadd_rn(out, br[1][1]);
-    }
-    if (bias != nullptr)
-      out = __fadd_rn(out, bias[n]);
-    y[static_cast<int64_t>(m) * N + n] = apply_act(out, act);
-  }
-}
-
-template <int kAB>
-void launch_narrow(const float *x, const Gather32 &g, int T, const int8_t *B,
-                   const int32_t *exB, int64_t n_pad, int64_t k_pad, int N,
-                   const float *bias, int act, float *y, int32_t *status, cudaStream_t s) {
-  const unsigned blocks = static_cast<unsigned>((g.M + kNarrowThreads - 1) / kNarrowThreads);
-  if (N <= 8)
-    narrow_kernel<kAB, 8><<<blocks, kNarrowThreads, 0, s>>>(x, g, T, B, exB, n_pad, k_pad, N,
-                                                             bias, act, y, status);
-  else
-    narrow_kernel<kAB, 16><<<blocks, kNarrowThreads, 0, s>>>(x, g, T, B, exB, n_pad, k_pad, N,
-                                                              bias, act, y, status);
-}
-
-// ---------------------------------------------------------------------------
 // INT8 on CUDA cores: CTA tile 64 x 64, thread owns 4 columns x 4 lanes.
 __global__ void pad_int8_kernel(const int8_t *__restrict__ x, int64_t M,
                                 int64_t K, int64_t m_pad, int64_t k_pad,
@@ -1011,23 +840,6 @@ int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
   if (!y || activation < 0 || activation > 2) {
     set_last_error("invalid arguments to cim22_cuda_layer_forward_bf16");
     return CIM22_STATUS_BAD_ARGUMENT;
-  }
-  cim22_gather rows{};
-  rows.kind = CIM22_GATHER_ROWS;
-  const cim22_gather &g = gather ? *gather : rows;
-  if (layer && layer->bf16 && layer->n <= 16 && x && status && m > 0 &&
-      (branches == 2 || branches == 4) && check_gather(g, m, layer->k)) {
-    // Narrow layer: one fused kernel, no workspace traffic.
-    const Gather32 dg = to_device_gather(g, m, layer->k, x);
-    auto s = static_cast<cudaStream_t>(stream);
-    const int T = static_cast<int>(layer->tiles);
-    if (branches == 2)
-      launch_narrow<1>(x, dg, T, layer->weights, layer->exponents, layer->n_pad, layer->k_pad,
-                       static_cast<int>(layer->n), bias, activation, y, status, s);
-    else
-      launch_narrow<2>(x, dg, T, layer->weights, layer->exponents, layer->n_pad, layer->k_pad,
-                       static_cast<int>(layer->n), bias, activation, y, status, s);
-    return cuda_ok(cudaGetLastError(), "narrow launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
   }
   const int rc = cim22_cuda_layer_prepare_bf16(layer, x, gather, m, branches, workspace,
                                                workspace_bytes, status, stream);
