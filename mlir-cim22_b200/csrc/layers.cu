@@ -34,29 +34,51 @@ constexpr unsigned kFull = 0xffffffffu;
 // index arithmetic (checked on the host) and the K decomposition hoisted out
 // of the column loop.
 
+// Division by an invariant divisor as a multiply-high and shift (Granlund and
+// Montgomery, "Division by invariant integers using multiplication", 1994):
+// q = (umulhi(n, mul) + n) >> shift for 0 <= n < 2^31, with
+// shift = ceil(log2 d) and mul = floor(2^32 (2^shift - d) / d) + 1.
+struct FastDiv {
+  uint32_t d, mul, shift;
+};
+
+FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f{d, 0, 0};
+  uint32_t l = 0;
+  while ((uint64_t{1} << l) < d)
+    ++l;
+  f.shift = l;
+  f.mul = static_cast<uint32_t>(((uint64_t{1} << 32) * ((uint64_t{1} << l) - d)) / d + 1);
+  return f;
+}
+
+__device__ __forceinline__ int fdiv(int n, const FastDiv &f) {
+  return static_cast<int>((__umulhi(static_cast<uint32_t>(n), f.mul) + static_cast<uint32_t>(n)) >> f.shift);
+}
+
 struct Gather32 {
+  FastDiv div_ohw, div_ow, div_khw, div_kw;
   int kind, C, H, W, KH, KW, SH, SW, PH, PW, OH, OW;
   int PK, PS, SRC_H, SRC_W; // fused max pool (NHWC), PK == 0 when absent
   int M, K;
   int pair_rows; // rows layout: 2 when K % 4 == 0 and x is 16-byte aligned (float4 loads)
 };
 
-// One element of an NHWC image at (n, ih, iw, c), reading the max over the
-// pool window of the pre-pool image when a pool is fused (NaN propagates like
-// torch.max_pool2d).
-__device__ __forceinline__ float image_load(const float *__restrict__ x,
-                                            const Gather32 &g, int n, int ih,
-                                            int iw, int c) {
+// One element of image n at (ih, iw, c); `img` already points at image n.
+// With a fused max pool it reads the max over the pool window of the
+// pre-pool image (NaN propagates like torch.max_pool2d).
+__device__ __forceinline__ float image_load(const float *__restrict__ img,
+                                            const Gather32 &g, int ih, int iw,
+                                            int c) {
   if (g.kind == CIM22_GATHER_CONV_NCHW)
-    return x[((static_cast<int64_t>(n) * g.C + c) * g.H + ih) * g.W + iw];
+    return img[(c * g.H + ih) * g.W + iw];
   if (g.PK == 0)
-    return x[((static_cast<int64_t>(n) * g.H + ih) * g.W + iw) * g.C + c];
+    return img[(ih * g.W + iw) * g.C + c];
   float m = 0.0f;
   bool any = false;
   for (int dy = 0; dy < g.PK; ++dy)
     for (int dx = 0; dx < g.PK; ++dx) {
-      const float v = x[((static_cast<int64_t>(n) * g.SRC_H + ih * g.PS + dy) * g.SRC_W +
-                         iw * g.PS + dx) * g.C + c];
+      const float v = img[((ih * g.PS + dy) * g.SRC_W + iw * g.PS + dx) * g.C + c];
       if (!any || v > m || v != v) {
         m = v;
         any = true;
@@ -107,9 +129,9 @@ __device__ __forceinline__ void split_bits(float v, uint32_t &bp, uint32_t &bn) 
 // Element source of one group: consecutive K indices of one column, with the
 // conv (c, i, j) decomposition stepped incrementally.
 struct GroupCursor {
-  const float *row; // rows layout
-  int n, oh, ow;    // conv column
-  int c, i, j;      // conv position of the current k
+  const float *base; // rows: the column's row; conv: image n
+  int ih0, iw0;      // conv window origin (oh * SH - PH, ow * SW - PW)
+  int c, i, j;       // conv position of the current k
   int k;
   bool column_valid;
 };
@@ -120,17 +142,21 @@ __device__ __forceinline__ GroupCursor open_group(const float *__restrict__ x, c
   cur.k = kbeg;
   cur.column_valid = m < g.M;
   if (g.kind == CIM22_GATHER_ROWS) {
-    cur.row = x + static_cast<int64_t>(m) * g.K;
+    cur.base = x + static_cast<int64_t>(m) * g.K;
   } else if (cur.column_valid) {
-    const int ohw = g.OH * g.OW;
-    cur.n = m / ohw;
-    const int r = m - cur.n * ohw;
-    cur.oh = r / g.OW;
-    cur.ow = r - cur.oh * g.OW;
-    const int khw = g.KH * g.KW;
-    cur.c = kbeg / khw;
-    const int rk = kbeg - cur.c * khw;
-    cur.i = rk / g.KW;
+    const int n = fdiv(m, g.div_ohw);
+    const int r = m - n * g.OH * g.OW;
+    const int oh = fdiv(r, g.div_ow);
+    const int ow = r - oh * g.OW;
+    const int64_t image = g.kind == CIM22_GATHER_CONV_NCHW || g.PK == 0
+                              ? static_cast<int64_t>(g.C) * g.H * g.W
+                              : static_cast<int64_t>(g.C) * g.SRC_H * g.SRC_W;
+    cur.base = x + n * image;
+    cur.ih0 = oh * g.SH - g.PH;
+    cur.iw0 = ow * g.SW - g.PW;
+    cur.c = fdiv(kbeg, g.div_khw);
+    const int rk = kbeg - cur.c * g.KH * g.KW;
+    cur.i = fdiv(rk, g.div_kw);
     cur.j = rk - cur.i * g.KW;
   }
   return cur;
@@ -141,12 +167,13 @@ __device__ __forceinline__ float next_value(const float *__restrict__ x, const G
   float v = 0.0f;
   if (cur.column_valid && cur.k < g.K) {
     if (g.kind == CIM22_GATHER_ROWS) {
-      v = cur.row[cur.k];
+      v = cur.base[cur.k];
     } else {
-      const int ih = cur.oh * g.SH - g.PH + cur.i;
-      const int iw = cur.ow * g.SW - g.PW + cur.j;
-      if (ih >= 0 && ih < g.H && iw >= 0 && iw < g.W)
-        v = image_load(x, g, cur.n, ih, iw, cur.c);
+      const int ih = cur.ih0 + cur.i;
+      const int iw = cur.iw0 + cur.j;
+      if (static_cast<unsigned>(ih) < static_cast<unsigned>(g.H) &&
+          static_cast<unsigned>(iw) < static_cast<unsigned>(g.W))
+        v = image_load(cur.base, g, ih, iw, cur.c);
       if (++cur.j == g.KW) {
         cur.j = 0;
         if (++cur.i == g.KH) {
@@ -165,8 +192,11 @@ __device__ __forceinline__ float next_value(const float *__restrict__ x, const G
 // one contiguous stretch of a row. The group maximum of each branch is an
 // xor-shuffle reduction within the 8-lane subgroup; each thread then writes
 // its 8 aligned bytes per branch. Padding columns (m >= M) and padding K are
-// zero; an all-zero group records exponent 127.
+// zero; an all-zero group records the exponent kZeroGroup.
 constexpr int kGroupThreads = 8;
+// Exponent recorded for an all-zero group: every dot with it is 0, so its
+// tiles add +0 and the contraction skips it.
+constexpr int kZeroGroup = 0x7fff;
 
 template <int kActBranches>
 __global__ void __launch_bounds__(256)
@@ -183,7 +213,11 @@ __global__ void __launch_bounds__(256)
   const int t = static_cast<int>(group - static_cast<int64_t>(m) * T);
   const int kbeg = t * kTileK + sub * 8;
   float v[8];
-  if (g.kind == CIM22_GATHER_ROWS && g.pair_rows == 2 && m < g.M && kbeg + 8 <= g.K) {
+  if (kbeg >= g.K || m >= g.M) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      v[e] = 0.0f; // K or column padding
+  } else if (g.kind == CIM22_GATHER_ROWS && g.pair_rows == 2 && kbeg + 8 <= g.K) {
     const float4 *src = reinterpret_cast<const float4 *>(x + static_cast<int64_t>(m) * g.K + kbeg);
     const float4 lo = src[0], hi = src[1];
     v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
@@ -221,7 +255,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int a = 0; a < kActBranches; ++a) {
     const bool zero = mx[a] == 0 || nonfinite;
-    const int emax = zero ? 127 : effective_exponent(static_cast<uint16_t>(mx[a]));
+    const int emax = zero ? kZeroGroup : effective_exponent(static_cast<uint16_t>(mx[a]));
     const bool fast = static_cast<int>(mx[a] >> 7) >= 8;
     const int shift = 127 - emax;
     uint32_t lo = 0, hi = 0;
@@ -281,6 +315,7 @@ __global__ void __launch_bounds__(256)
   __shared__ int sExA[kActBranches][kBM];
   __shared__ int sExB[2][kBN];
   __shared__ int sFast;
+  __shared__ int sLive[kActBranches];
   const int tid = threadIdx.x;
   const int tr = tid / kTC, tc = tid % kTC;
   const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
@@ -318,10 +353,23 @@ __global__ void __launch_bounds__(256)
     __syncthreads();
     if (tid < 32) {
       int mnA = INT_MAX, mxA = INT_MIN, mnB = INT_MAX, mxB = INT_MIN;
+      int live[kActBranches];
+#pragma unroll
+      for (int a = 0; a < kActBranches; ++a)
+        live[a] = 0;
       for (int i = tid; i < kActBranches * kBM; i += 32) {
         const int v = sExA[i / kBM][i % kBM];
+        if (v == kZeroGroup)
+          continue;
+        live[i / kBM] = 1;
         mnA = min(mnA, v);
         mxA = max(mxA, v);
+      }
+#pragma unroll
+      for (int a = 0; a < kActBranches; ++a) {
+        live[a] = __any_sync(kFull, live[a]);
+        if (tid == 0)
+          sLive[a] = live[a];
       }
       for (int i = tid; i < 2 * kBN; i += 32) {
         const int v = sExB[i / kBN][i % kBN];
@@ -333,10 +381,14 @@ __global__ void __launch_bounds__(256)
       mnB = __reduce_min_sync(kFull, mnB);
       mxB = __reduce_max_sync(kFull, mxB);
       if (tid == 0)
-        sFast = (mnA + mnB >= 140) && (mxA + mxB <= 374) && (mxA <= 240);
+        sFast = mxA == INT_MIN || ((mnA + mnB >= 140) && (mxA + mxB <= 374) && (mxA <= 240));
     }
     __syncthreads();
     const bool fast = sFast != 0;
+    bool live[kActBranches];
+#pragma unroll
+    for (int a = 0; a < kActBranches; ++a)
+      live[a] = sLive[a] != 0;
     int p[kActBranches][2][kRM][4];
 #pragma unroll
     for (int a = 0; a < kActBranches; ++a)
@@ -362,6 +414,7 @@ __global__ void __launch_bounds__(256)
           bv[w][c] = *reinterpret_cast<const int4 *>(&Bs[w][tc * 4 + c][kk * 16]);
 #pragma unroll
       for (int a = 0; a < kActBranches; ++a)
+        if (live[a])
 #pragma unroll
         for (int w = 0; w < 2; ++w)
 #pragma unroll
@@ -377,11 +430,14 @@ __global__ void __launch_bounds__(256)
             }
     }
 #pragma unroll
-    for (int a = 0; a < kActBranches; ++a)
+    for (int a = 0; a < kActBranches; ++a) {
+      if (!live[a])
+        continue; // every group of this branch is zero: its tiles add +0
 #pragma unroll
       for (int r = 0; r < kRM; ++r) {
         const int exr = sExA[a][tr + kTR * r];
-        const float sx = exp2i(exr - 133);
+        const bool zr = exr == kZeroGroup;
+        const float sx = zr ? 1.0f : exp2i(exr - 133);
 #pragma unroll
         for (int w = 0; w < 2; ++w)
 #pragma unroll
@@ -390,7 +446,7 @@ __global__ void __launch_bounds__(256)
             if (fast) {
               const float q = __fmul_rn(trunc8f(p[a][w][r][c]), sx);
               acc[a][w][r][c] = fmaf(q, exp2i(ew - 133), acc[a][w][r][c]);
-            } else {
+            } else if (!zr) {
               const uint16_t tile =
                   signsplit_tile(static_cast<uint32_t>(p[a][w][r][c]), ew, exr);
               if (tile == kBF16Inf)
@@ -399,6 +455,7 @@ __global__ void __launch_bounds__(256)
             }
           }
       }
+    }
     __syncthreads();
   }
 
@@ -559,6 +616,11 @@ bool check_gather(const cim22_gather &g, int64_t m, int64_t k) {
       g.kernel_h <= 0 || g.kernel_w <= 0 || g.stride_h <= 0 || g.stride_w <= 0 ||
       g.pad_h < 0 || g.pad_w < 0)
     return false;
+  const int64_t image = static_cast<int64_t>(g.channels) *
+                        (g.pool_kernel > 0 ? static_cast<int64_t>(g.pool_src_h) * g.pool_src_w
+                                           : static_cast<int64_t>(g.height) * g.width);
+  if (image >= (int64_t{1} << 31))
+    return false;
   const int oh = (g.height + 2 * g.pad_h - g.kernel_h) / g.stride_h + 1;
   const int ow = (g.width + 2 * g.pad_w - g.kernel_w) / g.stride_w + 1;
   return oh == g.out_h && ow == g.out_w &&
@@ -589,6 +651,10 @@ Gather32 to_device_gather(const cim22_gather &g, int64_t m, int64_t k, const flo
     d.PS = g.pool_stride;
     d.SRC_H = g.pool_src_h;
     d.SRC_W = g.pool_src_w;
+    d.div_ohw = make_fastdiv(static_cast<uint32_t>(g.out_h * g.out_w));
+    d.div_ow = make_fastdiv(static_cast<uint32_t>(g.out_w));
+    d.div_khw = make_fastdiv(static_cast<uint32_t>(g.kernel_h * g.kernel_w));
+    d.div_kw = make_fastdiv(static_cast<uint32_t>(g.kernel_w));
   }
   return d;
 }
