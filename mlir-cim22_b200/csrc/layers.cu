@@ -200,17 +200,17 @@ constexpr int kZeroGroup = 0x7fff;
 
 template <int kActBranches>
 __global__ void __launch_bounds__(256)
-    prepare_kernel(const float *__restrict__ x, Gather32 g, int T, int m_pad,
+    prepare_kernel(const float *__restrict__ x, Gather32 g, FastDiv div_t, int m_pad,
                    int k_pad, int8_t *__restrict__ A, int32_t *__restrict__ ex,
                    int32_t *status) {
-  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t group = tid / kGroupThreads;
+  const int T = static_cast<int>(div_t.d);
+  const int group = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) / kGroupThreads);
   const int sub = static_cast<int>(threadIdx.x % kGroupThreads);
-  if (group >= static_cast<int64_t>(m_pad) * T)
+  if (group >= m_pad * T)
     return; // uniform per 8-lane subgroup (blockDim is a multiple of 8)
   const unsigned mask = 0xffu << (threadIdx.x & 24);
-  const int m = static_cast<int>(group / T);
-  const int t = static_cast<int>(group - static_cast<int64_t>(m) * T);
+  const int m = fdiv(group, div_t);
+  const int t = group - m * T;
   const int kbeg = t * kTileK + sub * 8;
   float v[8];
   if (kbeg >= g.K || m >= g.M) {
@@ -332,12 +332,6 @@ __global__ void __launch_bounds__(256)
           acc[a][w][r][c] = 0.0f;
 
   for (int t = 0; t < T; ++t) {
-    for (int i = tid; i < kActBranches * kBM * 4; i += 256) {
-      const int a = i / (kBM * 4), r = (i >> 2) % kBM, c = i & 3;
-      *reinterpret_cast<int4 *>(&As[a][r][c * 16]) = *reinterpret_cast<const int4 *>(
-          A + (static_cast<int64_t>(a) * m_pad + m0 + r) * k_pad +
-          static_cast<int64_t>(t) * kTileK + c * 16);
-    }
     for (int i = tid; i < 2 * kBN * 4; i += 256) {
       const int w = i / (kBN * 4), r = (i >> 2) % kBN, c = i & 3;
       *reinterpret_cast<int4 *>(&Bs[w][r][c * 16]) = *reinterpret_cast<const int4 *>(
@@ -389,6 +383,15 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int a = 0; a < kActBranches; ++a)
       live[a] = sLive[a] != 0;
+    // Activation tiles of live branches only (an all-zero branch is skipped).
+    for (int i = tid; i < kActBranches * kBM * 4; i += 256) {
+      const int a = i / (kBM * 4), r = (i >> 2) % kBM, c = i & 3;
+      if (live[a])
+        *reinterpret_cast<int4 *>(&As[a][r][c * 16]) = *reinterpret_cast<const int4 *>(
+            A + (static_cast<int64_t>(a) * m_pad + m0 + r) * k_pad +
+            static_cast<int64_t>(t) * kTileK + c * 16);
+    }
+    __syncthreads();
     int p[kActBranches][2][kRM][4];
 #pragma unroll
     for (int a = 0; a < kActBranches; ++a)
@@ -849,16 +852,21 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
   const int64_t m_pad = round_up(m, kColumnPad);
   const int ab = branches == 2 ? 1 : 2;
   const int T = static_cast<int>(layer->tiles);
+  if (m_pad * T * kGroupThreads >= (int64_t{1} << 31)) {
+    set_last_error("cim22_cuda_layer_prepare_bf16: columns x K tiles too large for one launch");
+    return CIM22_STATUS_BAD_ARGUMENT;
+  }
   int8_t *A = static_cast<int8_t *>(workspace);
   int32_t *ex = reinterpret_cast<int32_t *>(
       static_cast<char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
   const Gather32 dg = to_device_gather(g, m, layer->k, x);
   const unsigned blocks = static_cast<unsigned>((m_pad * T * kGroupThreads + 255) / 256);
+  const FastDiv div_t = make_fastdiv(static_cast<uint32_t>(T));
   if (ab == 1)
-    prepare_kernel<1><<<blocks, 256, 0, s>>>(x, dg, T, static_cast<int>(m_pad),
+    prepare_kernel<1><<<blocks, 256, 0, s>>>(x, dg, div_t, static_cast<int>(m_pad),
                                              static_cast<int>(layer->k_pad), A, ex, status);
   else
-    prepare_kernel<2><<<blocks, 256, 0, s>>>(x, dg, T, static_cast<int>(m_pad),
+    prepare_kernel<2><<<blocks, 256, 0, s>>>(x, dg, div_t, static_cast<int>(m_pad),
                                              static_cast<int>(layer->k_pad), A, ex, status);
   return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
 }
