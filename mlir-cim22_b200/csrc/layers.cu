@@ -103,10 +103,18 @@ __device__ __forceinline__ int8_t fast_align(uint32_t p, int emax) {
              : int8_t{0};
 }
 
-__device__ __forceinline__ uint32_t align_byte(uint32_t p, int emax, int shift, bool fast) {
-  const int8_t a = fast ? fast_align(p, emax)
-                        : prealign_element(bf16_scalbn(static_cast<uint16_t>(p), shift), 127);
-  return static_cast<uint8_t>(a);
+// Exact path for groups whose maximum is tiny (exponent < 8): RNE scaling of
+// every element, then ExpPrealign at exponent 127. Kept out of line so the
+// fast path is not predicated through it.
+__device__ __noinline__ void align8_slow(const uint32_t *bits, int shift, uint32_t &lo,
+                                         uint32_t &hi) {
+  lo = hi = 0;
+  for (int e = 0; e < 4; ++e) {
+    lo |= static_cast<uint32_t>(static_cast<uint8_t>(prealign_element(
+              bf16_scalbn(static_cast<uint16_t>(bits[e]), shift), 127))) << (8 * e);
+    hi |= static_cast<uint32_t>(static_cast<uint8_t>(prealign_element(
+              bf16_scalbn(static_cast<uint16_t>(bits[e + 4]), shift), 127))) << (8 * e);
+  }
 }
 
 // Activation split (Passes.cpp:2379-2399): xp = (x < 0 ? 0 : x) then
@@ -260,10 +268,15 @@ __global__ void __launch_bounds__(256)
     const int shift = 127 - emax;
     uint32_t lo = 0, hi = 0;
     if (!zero) {
+      if (fast) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        lo |= align_byte(bits[a][e], emax, shift, fast) << (8 * e);
-        hi |= align_byte(bits[a][e + 4], emax, shift, fast) << (8 * e);
+        for (int e = 0; e < 4; ++e) {
+          lo |= static_cast<uint32_t>(static_cast<uint8_t>(fast_align(bits[a][e], emax))) << (8 * e);
+          hi |= static_cast<uint32_t>(static_cast<uint8_t>(fast_align(bits[a][e + 4], emax)))
+                << (8 * e);
+        }
+      } else {
+        align8_slow(bits[a], shift, lo, hi);
       }
     }
     *reinterpret_cast<uint2 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) =
@@ -300,6 +313,18 @@ __device__ __forceinline__ float apply_act(float v, int act) {
 // and lanes 4tc .. 4tc + 3.
 constexpr int kRowStride = 80;
 
+// Exact restore of one tile value outside the fast exponent window (subnormal
+// or overflowing results), out of line so the fast path is not predicated
+// through it. Returns the updated f32 branch sum.
+__device__ __noinline__ float slow_tile_add(float acc, int p, int ew, int ex, int32_t *status) {
+  if (ex == kZeroGroup)
+    return acc;
+  const uint16_t tile = signsplit_tile(static_cast<uint32_t>(p), ew, ex);
+  if (tile == kBF16Inf)
+    atomicOr(status, CIM22_STATUS_TILE_OVERFLOW);
+  return __fadd_rn(acc, bf16_to_f32(tile));
+}
+
 template <int kActBranches, int kTC, int kRM>
 __global__ void __launch_bounds__(256)
     signsplit_simt_kernel(const int8_t *__restrict__ A,
@@ -314,6 +339,7 @@ __global__ void __launch_bounds__(256)
   __shared__ __align__(16) int8_t Bs[2][kBN][kRowStride];
   __shared__ int sExA[kActBranches][kBM];
   __shared__ int sExB[2][kBN];
+  __shared__ float sSw[2][kBN];
   __shared__ int sFast;
   __shared__ int sLive[kActBranches];
   const int tid = threadIdx.x;
@@ -341,9 +367,11 @@ __global__ void __launch_bounds__(256)
     for (int i = tid; i < kActBranches * kBM; i += 256)
       sExA[i / kBM][i % kBM] =
           exA[(static_cast<int64_t>(i / kBM) * T + t) * m_pad + m0 + i % kBM];
-    for (int i = tid; i < 2 * kBN; i += 256)
-      sExB[i / kBN][i % kBN] =
-          exB[(static_cast<int64_t>(i / kBN) * T + t) * n_pad + n0 + i % kBN];
+    for (int i = tid; i < 2 * kBN; i += 256) {
+      const int e = exB[(static_cast<int64_t>(i / kBN) * T + t) * n_pad + n0 + i % kBN];
+      sExB[i / kBN][i % kBN] = e;
+      sSw[i / kBN][i % kBN] = exp2i(e - 133);
+    }
     __syncthreads();
     if (tid < 32) {
       int mnA = INT_MAX, mxA = INT_MIN, mnB = INT_MAX, mxB = INT_MIN;
@@ -436,27 +464,30 @@ __global__ void __launch_bounds__(256)
     for (int a = 0; a < kActBranches; ++a) {
       if (!live[a])
         continue; // every group of this branch is zero: its tiles add +0
+      if (fast) {
 #pragma unroll
-      for (int r = 0; r < kRM; ++r) {
-        const int exr = sExA[a][tr + kTR * r];
-        const bool zr = exr == kZeroGroup;
-        const float sx = zr ? 1.0f : exp2i(exr - 133);
+        for (int r = 0; r < kRM; ++r) {
+          const int exr = sExA[a][tr + kTR * r];
+          const float sx = exr == kZeroGroup ? 1.0f : exp2i(exr - 133);
 #pragma unroll
-        for (int w = 0; w < 2; ++w)
+          for (int w = 0; w < 2; ++w)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int ew = sExB[w][tc * 4 + c];
-            if (fast) {
+            for (int c = 0; c < 4; ++c) {
               const float q = __fmul_rn(trunc8f(p[a][w][r][c]), sx);
-              acc[a][w][r][c] = fmaf(q, exp2i(ew - 133), acc[a][w][r][c]);
-            } else if (!zr) {
-              const uint16_t tile =
-                  signsplit_tile(static_cast<uint32_t>(p[a][w][r][c]), ew, exr);
-              if (tile == kBF16Inf)
-                atomicOr(status, CIM22_STATUS_TILE_OVERFLOW);
-              acc[a][w][r][c] = __fadd_rn(acc[a][w][r][c], bf16_to_f32(tile));
+              acc[a][w][r][c] = fmaf(q, sSw[w][tc * 4 + c], acc[a][w][r][c]);
             }
-          }
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < kRM; ++r) {
+          const int exr = sExA[a][tr + kTR * r];
+#pragma unroll
+          for (int w = 0; w < 2; ++w)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              acc[a][w][r][c] = slow_tile_add(acc[a][w][r][c], p[a][w][r][c],
+                                              sExB[w][tc * 4 + c], exr, status);
+        }
       }
     }
     __syncthreads();
