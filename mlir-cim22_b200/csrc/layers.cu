@@ -17,6 +17,8 @@
 //   outputs               f32 / int32 y[m][n]
 #include "cim_internal.h"
 #include "cim_numeric.cuh"
+
+#include <cuda_bf16.h>
 #include "gemm_tc.h"
 
 #include <algorithm>
@@ -104,17 +106,10 @@ __device__ __forceinline__ int8_t fast_align(uint32_t p, int emax) {
 }
 
 // Exact path for groups whose maximum is tiny (exponent < 8): RNE scaling of
-// every element, then ExpPrealign at exponent 127. Kept out of line so the
-// fast path is not predicated through it.
-__device__ __noinline__ void align8_slow(const uint32_t *bits, int shift, uint32_t &lo,
-                                         uint32_t &hi) {
-  lo = hi = 0;
-  for (int e = 0; e < 4; ++e) {
-    lo |= static_cast<uint32_t>(static_cast<uint8_t>(prealign_element(
-              bf16_scalbn(static_cast<uint16_t>(bits[e]), shift), 127))) << (8 * e);
-    hi |= static_cast<uint32_t>(static_cast<uint8_t>(prealign_element(
-              bf16_scalbn(static_cast<uint16_t>(bits[e + 4]), shift), 127))) << (8 * e);
-  }
+// the element, then ExpPrealign at exponent 127. Out of line so the fast path
+// is not predicated through it.
+__device__ __noinline__ uint32_t slow_align(uint32_t p, int shift) {
+  return static_cast<uint8_t>(prealign_element(bf16_scalbn(static_cast<uint16_t>(p), shift), 127));
 }
 
 // Activation split (Passes.cpp:2379-2399): xp = (x < 0 ? 0 : x) then
@@ -236,19 +231,42 @@ __global__ void __launch_bounds__(256)
     for (int e = 0; e < 8; ++e)
       v[e] = next_value(x, g, cur);
   }
+  // Split and round: xp = max(x, 0), xn = max(-x, 0) equal the reference's
+  // selects for every non-NaN x up to the sign of zero, which the preparation
+  // clears anyway (BF16Compensation.cpp:97); NaN, infinity and finite values
+  // that round to BF16 infinity (|x| >= 0x1.fep127) are caught on x itself.
+  // cvt.rn.bf16x2.f32 rounds to nearest even, as arith.truncf does.
   uint32_t bits[2][8];
   uint32_t mx[2] = {0, 0};
   bool nonfinite = false, negative = false;
+  uint32_t packed[2][4];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    split_bits<kActBranches>(v[e], bits[0][e], bits[1][e]);
-#pragma unroll
-    for (int a = 0; a < kActBranches; ++a) {
-      nonfinite |= ((bits[a][e] >> 7) & 0xffu) == 0xffu;
-      negative |= (bits[a][e] & 0x8000u) && (bits[a][e] & 0x7fffu);
-      bits[a][e] &= 0x7fffu;
-      mx[a] = max(mx[a], bits[a][e]);
+  for (int e = 0; e < 8; e += 2) {
+    float p0 = v[e], p1 = v[e + 1], q0 = 0.0f, q1 = 0.0f;
+    nonfinite |= !(fabsf(p0) < 3.3961548e38f) || !(fabsf(p1) < 3.3961548e38f);
+    if (kActBranches == 2) {
+      q0 = fmaxf(-p0, 0.0f);
+      q1 = fmaxf(-p1, 0.0f);
+      p0 = fmaxf(p0, 0.0f);
+      p1 = fmaxf(p1, 0.0f);
+    } else {
+      negative |= p0 < 0.0f || p1 < 0.0f;
     }
+    const __nv_bfloat162 hp = __floats2bfloat162_rn(p0, p1);
+    packed[0][e / 2] = *reinterpret_cast<const uint32_t *>(&hp) & 0x7fff7fffu;
+    if (kActBranches == 2) {
+      const __nv_bfloat162 hn = __floats2bfloat162_rn(q0, q1);
+      packed[1][e / 2] = *reinterpret_cast<const uint32_t *>(&hn) & 0x7fff7fffu;
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a) {
+    const uint32_t m2 = __vmaxu2(__vmaxu2(packed[a][0], packed[a][1]),
+                                 __vmaxu2(packed[a][2], packed[a][3]));
+    mx[a] = max(m2 & 0xffffu, m2 >> 16);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      bits[a][e] = (packed[a][e / 2] >> (16 * (e & 1))) & 0xffffu;
   }
 #pragma unroll
   for (int a = 0; a < kActBranches; ++a)
@@ -276,7 +294,11 @@ __global__ void __launch_bounds__(256)
                 << (8 * e);
         }
       } else {
-        align8_slow(bits[a], shift, lo, hi);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          lo |= slow_align(bits[a][e], shift) << (8 * e);
+          hi |= slow_align(bits[a][e + 4], shift) << (8 * e);
+        }
       }
     }
     *reinterpret_cast<uint2 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) =
