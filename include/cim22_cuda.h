@@ -285,6 +285,7 @@ void _mlir_ciface_cim22_dispatch_int8(int64_t id, cim22_memref2d *input,
 #define CIM22_STATUS_NORMALIZATION 0x8      /* sign-split prealign invariant broken */
 #define CIM22_STATUS_BAD_ARGUMENT 0x10      /* launch-time argument check failed */
 #define CIM22_STATUS_NEGATIVE_INPUT 0x20    /* negative value in a nonnegative (2-branch) layer */
+#define CIM22_STATUS_TIMEOUT 0x40           /* a bounded on-device wait gave up (results invalid) */
 
 /* Message of the lowest set status bit ("" for 0). */
 const char *cim22_cuda_status_message(int32_t status);

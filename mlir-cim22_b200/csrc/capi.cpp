@@ -38,6 +38,8 @@ const char *cim22_cuda_status_message(int32_t status) {
     return "invalid CIM layer launch arguments";
   if (status & CIM22_STATUS_NEGATIVE_INPUT)
     return "CIM nonnegative BF16 mode rejects negative inputs";
+  if (status & CIM22_STATUS_TIMEOUT)
+    return "CIM tensor-core pipeline wait timed out";
   return "";
 }
 

@@ -1,10 +1,286 @@
-// gemm_tc.cu - tcgen05 contraction kernels (sm_100a).
+// gemm_tc.cu - tcgen05 (5th-generation tensor core) CIM contractions, sm_100a.
+//
+// INT8 layers whose weights pass the signed-i21 range proof
+// (lib/Conversion/LinalgToCIM/Passes.cpp:592-627) accumulate every 64-K
+// crossbar partial exactly in int32, so the whole K range of a 128x128 output
+// tile accumulates in one TMEM accumulator:
+//
+//   warp 0 (one thread)   TMA producer: A and B K-blocks of 128 bytes into a
+//                          4-stage ring of 128B-swizzled shared-memory tiles
+//   warp 1 (one thread)   tcgen05.mma.cta_group::1.kind::i8, M=128 N=128 K=32,
+//                          4 MMAs per K-block, tcgen05.commit frees a stage
+//   warps 2-5             epilogue: tcgen05.ld 32x32b from TMEM, int32 stores
+//
+// Every mbarrier wait is bounded; a wait that runs out sets
+// CIM22_STATUS_TIMEOUT, the CTA stops issuing work, waits (bounded) for the
+// copies it has in flight, frees its TMEM and returns. Loads never use
+// cluster multicast.
 #include "gemm_tc.h"
 
+#include "cim_internal.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 namespace cim::tc {
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 128, kStages = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kSpinLimit = 1u << 24;
+constexpr uint32_t kTileBytes = kBM * kBK; // A and B tiles are the same size
+
+struct alignas(1024) SmemInt8 {
+  int8_t a[kStages][kBM * kBK];
+  int8_t b[kStages][kBN * kBK];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t done;
+  uint32_t tmem;
+  int failed;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Wait for the phase with the given parity to complete, at most kSpinLimit
+// polls. Returns false when the limit was reached.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    uint32_t done;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                 " selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(done)
+                 : "r"(addr), "r"(parity)
+                 : "memory");
+    if (done)
+      return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128
+// bytes in 8-row (1024-byte) atoms. Bits [0,14) address >> 4, [32,46) stride
+// byte offset >> 4, [46,48) = 1, [61,64) layout (2 = SWIZZLE_128B).
+__device__ __forceinline__ uint64_t sw128_desc(const void *tile) {
+  const uint64_t addr = smem_u32(tile);
+  return ((addr & 0x3ffffull) >> 4) | (uint64_t{1024 >> 4} << 32) | (uint64_t{1} << 46) |
+         (uint64_t{2} << 61);
+}
+
+// Instruction descriptor of tcgen05.mma .kind::i8: D s32 (bits [4,6) = 2),
+// A and B signed 8-bit (bits [7,10), [10,13) = 1), both K-major, N >> 3 at
+// bit 17, M >> 4 at bit 24.
+constexpr uint32_t idesc_i8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+               " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+               "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, "
+               "%9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, "
+               "%24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                 "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]),
+                 "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                 "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+                 "=r"(r[30]), "=r"(r[31])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    int8_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                   const __grid_constant__ CUtensorMap tmB, int num_kb, int64_t M, int64_t N,
+                   int32_t *__restrict__ y, int32_t *status) {
+  extern __shared__ uint8_t smem_raw[];
+  SmemInt8 &s = *reinterpret_cast<SmemInt8 *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m0 = static_cast<int>(blockIdx.x) * kBM;
+  const int n0 = static_cast<int>(blockIdx.y) * kBN;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    mbar_init(&s.done, 1);
+    s.failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s.tmem)),
+                 "r"(kBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = s.tmem;
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer.
+    int issued = 0;
+    for (int kb = 0; kb < num_kb; ++kb) {
+      const int stage = kb % kStages;
+      const uint32_t parity = ((kb / kStages) & 1) ^ 1;
+      if (!mbar_wait(&s.empty[stage], parity)) {
+        s.failed = 1;
+        break;
+      }
+      if (*reinterpret_cast<volatile int *>(&s.failed))
+        break;
+      mbar_expect_tx(&s.full[stage], 2 * kTileBytes);
+      tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * kBK, m0);
+      tma_load_2d(s.b[stage], &tmB, &s.full[stage], kb * kBK, n0);
+      issued = kb + 1;
+    }
+    // Never leave with copies in flight: wait (bounded) for the stages this
+    // thread filled but the MMA thread may not have consumed.
+    for (int kb = issued > kStages ? issued - kStages : 0; kb < issued; ++kb)
+      mbar_wait(&s.full[kb % kStages], (kb / kStages) & 1);
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer.
+    constexpr uint32_t idesc = idesc_i8(kBM, kBN);
+    bool ok = true;
+    for (int kb = 0; kb < num_kb && ok; ++kb) {
+      const int stage = kb % kStages;
+      if (!mbar_wait(&s.full[stage], (kb / kStages) & 1) ||
+          *reinterpret_cast<volatile int *>(&s.failed)) {
+        s.failed = 1;
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint64_t adesc = sw128_desc(s.a[stage]);
+      const uint64_t bdesc = sw128_desc(s.b[stage]);
+#pragma unroll
+      for (int kk = 0; kk < kBK / 32; ++kk)
+        mma_i8(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+      mma_commit(&s.empty[stage]);
+    }
+    mma_commit(&s.done);
+  } else if (warp >= 2) {
+    // Epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 (= tile rows).
+    const int quad = warp % 4;
+    const bool ok = mbar_wait(&s.done, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (!ok || *reinterpret_cast<volatile int *>(&s.failed)) {
+      if (lane == 0)
+        atomicOr(status, CIM22_STATUS_TIMEOUT);
+    } else {
+      const int64_t row = m0 + quad * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + c * 32, r);
+        if (row < M) {
+          int32_t *dst = y + row * N + n0 + c * 32;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + c * 32 + j < N)
+              dst[j] = static_cast<int32_t>(r[j]);
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D int8 tensor [rows][cols] (cols contiguous), box 128 x 128, 128B swizzle.
+bool encode_int8_2d(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                    uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn)
+    return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols};
+  const cuuint32_t box[2] = {kBK, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box,
+            elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool sm100(cudaStream_t) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess)
+    return false;
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  return major == 10 && minor == 0;
+}
+
+constexpr size_t kSmemInt8 = sizeof(SmemInt8) + 1024;
+
+} // namespace
 
 bool signsplit_available() { return false; }
-bool int8_available() { return false; }
+
+bool int8_available() { return sm100(nullptr) && encode_fn() != nullptr; }
 
 bool launch_signsplit(const int8_t *, const int32_t *, int64_t, const int8_t *,
                       const int32_t *, int64_t, int64_t, int, int64_t, int64_t,
@@ -12,9 +288,23 @@ bool launch_signsplit(const int8_t *, const int32_t *, int64_t, const int8_t *,
   return false;
 }
 
-bool launch_int8(const int8_t *, int64_t, const int8_t *, int64_t, int64_t, int,
-                 int64_t, int64_t, int32_t *, int32_t *, cudaStream_t) {
-  return false;
+bool launch_int8(const int8_t *A, int64_t m_pad, const int8_t *B, int64_t n_pad,
+                 int64_t k_pad, int T, int64_t M, int64_t N, int32_t *y, int32_t *status,
+                 cudaStream_t stream) {
+  (void)T;
+  if (m_pad % kBM || n_pad % kBN || k_pad % 64 || m_pad >= (int64_t{1} << 31) ||
+      (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+    return false;
+  CUtensorMap ta, tb;
+  if (!encode_int8_2d(&ta, A, m_pad, k_pad, kBM) || !encode_int8_2d(&tb, B, n_pad, k_pad, kBN))
+    return false;
+  if (cudaFuncSetAttribute(int8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kSmemInt8)) != cudaSuccess)
+    return false;
+  const int num_kb = static_cast<int>((k_pad + kBK - 1) / kBK);
+  const dim3 grid(static_cast<unsigned>(m_pad / kBM), static_cast<unsigned>((N + kBN - 1) / kBN));
+  int8_tc_kernel<<<grid, kThreads, kSmemInt8, stream>>>(ta, tb, num_kb, M, N, y, status);
+  return true;
 }
 
 } // namespace cim::tc

@@ -200,3 +200,18 @@ def test_conv_with_fused_pool_and_flatten_gathers(pool):
     status.raise_if_set()
     flat = pooled.transpose(0, 3, 1, 2).reshape(n, -1)
     np.testing.assert_array_equal(bits(outl.cpu().numpy()), bits(oracle.linear_bf16(flat, wl)))
+
+
+@pytest.mark.parametrize("m,k,n", [(1000, 4096, 1000), (4096, 256, 256), (129, 8192, 130)])
+def test_linear_int8_tensor_core_shapes(m, k, n):
+    """Range-proven INT8 layers run whole-K int32 accumulation on tcgen05."""
+    from cim22_b200.cim_ops import CimLayer
+
+    rng = np.random.default_rng(m + k + n)
+    x = rng.integers(-128, 128, (m, k)).astype(np.int8)
+    w = rng.integers(-8, 8, (n, k)).astype(np.int8)  # provably in range
+    layer = CimLayer(w, kind="int8")
+    assert layer.range_safe
+    got = layer.linear_int8(torch.from_numpy(x).to(DEV)).cpu().numpy()
+    exp = (x.astype(np.int64) @ w.T.astype(np.int64)).astype(np.int32)
+    np.testing.assert_array_equal(got, exp)
