@@ -51,6 +51,10 @@ def parse():
     p.add_argument("--cpu-sample", type=int, default=2048,
                    help="images in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--int8-sweep", action="store_true",
+                   help="INT8 CIM MVM sweep (M x K=N grid): TOPS vs the int8 tensor peak")
+    p.add_argument("--sweep-m", default="1,16,128,1024,8192")
+    p.add_argument("--sweep-kn", default="256,1024,4096,8192")
     p.add_argument("--profile", action="store_true",
                    help="only launch the program's kernels eagerly (warmup + steps passes); "
                         "for capturing single kernels under a profiler")
@@ -164,10 +168,78 @@ def reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def int8_sweep(args) -> None:
+    """INT8 CIM MVM layers y = x W^T (int8 x int8 -> int32, exact), timed per
+    launch with CUDA events on the current stream, L2 flushed in between."""
+    import numpy as np
+    import torch
+
+    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace
+    from cim22_b200.native import lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _, bf16_peak, peak_kind = peaks()
+    int8_peak = 2 * bf16_peak
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    ws, status = Workspace(dev), StatusWord(dev)
+    stream = torch.cuda.current_stream(dev)
+    rng = np.random.default_rng(1)
+    rows = []
+    for kn in [int(v) for v in args.sweep_kn.split(",")]:
+        w = rng.integers(-127, 128, (kn, kn)).astype(np.int8)
+        layer = CimLayer(w, kind="int8", device=dev)
+        for m in [int(v) for v in args.sweep_m.split(",")]:
+            x = torch.from_numpy(np.random.default_rng(0).integers(-128, 128, (m, kn))
+                                 .astype(np.int8)).to(dev)
+            out = torch.empty(m, kn, dtype=torch.int32, device=dev)
+            tc0 = lib().cim22_cuda_tensor_core_launches()
+            for _ in range(3):
+                layer_launch(layer, x, out, m, ws, status)
+            times = []
+            for _ in range(max(3, min(args.steps, 20))):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                layer_launch(layer, x, out, m, ws, status)
+                b.record(stream)
+                b.synchronize()
+                times.append(a.elapsed_time(b))
+            status.raise_if_set()
+            tc = lib().cim22_cuda_tensor_core_launches() - tc0
+            ms = sorted(times)[len(times) // 2]
+            tops = 2.0 * m * kn * kn / (ms / 1e3) / 1e12
+            row = {"m": m, "k": kn, "n": kn, "ms": ms, "tops": tops,
+                   "frac_int8_peak": tops / int8_peak, "tensor_core": tc > 0}
+            rows.append(row)
+            print(json.dumps(row), flush=True)
+    best = max(rows, key=lambda r: r["tops"])
+    print(json.dumps({"metric": "int8 CIM MVM TOPS", "best": best,
+                      "int8_peak_tops": int8_peak,
+                      "peak_note": f"2 x {peak_kind} bf16 cuBLAS ({bf16_peak} TF/s)"}), flush=True)
+
+
+def layer_launch(layer, x, out, m, ws, status):
+    import ctypes
+
+    import torch
+
+    from cim22_b200.native import check, lib
+
+    buf = ws.get(layer.workspace_bytes(m))
+    check(lib().cim22_cuda_layer_forward_int8(
+        layer._handle, ctypes.c_void_p(x.data_ptr()), m, ctypes.c_void_p(out.data_ptr()),
+        ctypes.c_void_p(buf.data_ptr()), buf.numel(), ctypes.c_void_p(status.tensor.data_ptr()),
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "forward_int8")
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.int8_sweep:
+        int8_sweep(args)
         return
 
     import torch

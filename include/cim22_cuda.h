@@ -293,6 +293,10 @@ const char *cim22_cuda_status_message(int32_t status);
 /* Diagnostic of the last failing layer or glue call on this thread. */
 const char *cim22_cuda_last_error(void);
 
+/* Number of tcgen05 tensor-core kernel launches issued by this process so
+ * far (diagnostics: shows which contraction path a layer took). */
+int64_t cim22_cuda_tensor_core_launches(void);
+
 /* sizeof of each structure above, in declaration order: frame_packet,
  * static_weight, input_binding, readback_binding, work, group, transaction,
  * trace_event, memref2d, gather. Returns the number of entries written. */

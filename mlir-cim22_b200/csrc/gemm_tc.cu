@@ -22,6 +22,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 namespace cim::tc {
@@ -278,6 +279,8 @@ constexpr size_t kSmemInt8 = sizeof(SmemInt8) + 1024;
 
 } // namespace
 
+std::atomic<int64_t> g_tc_launches{0};
+
 bool signsplit_available() { return false; }
 
 bool int8_available() { return sm100(nullptr) && encode_fn() != nullptr; }
@@ -288,23 +291,30 @@ bool launch_signsplit(const int8_t *, const int32_t *, int64_t, const int8_t *,
   return false;
 }
 
-bool launch_int8(const int8_t *A, int64_t m_pad, const int8_t *B, int64_t n_pad,
-                 int64_t k_pad, int T, int64_t M, int64_t N, int32_t *y, int32_t *status,
-                 cudaStream_t stream) {
-  (void)T;
-  if (m_pad % kBM || n_pad % kBN || k_pad % 64 || m_pad >= (int64_t{1} << 31) ||
-      (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+bool launch_int8(const int8_t *A, int64_t a_rows, int64_t a_cols, const int8_t *B,
+                 int64_t n_pad, int64_t k_pad, int64_t M, int64_t N, int32_t *y,
+                 int32_t *status, cudaStream_t stream) {
+  if (n_pad % kBN || k_pad % 64 || a_cols % 16 || a_cols > k_pad || a_rows < M ||
+      M >= (int64_t{1} << 31) - kBM || (reinterpret_cast<uintptr_t>(A) & 15) ||
+      (reinterpret_cast<uintptr_t>(B) & 15))
     return false;
+  // Columns beyond a_cols (to k_pad) and rows beyond a_rows read TMA's zero fill.
   CUtensorMap ta, tb;
-  if (!encode_int8_2d(&ta, A, m_pad, k_pad, kBM) || !encode_int8_2d(&tb, B, n_pad, k_pad, kBN))
+  if (!encode_int8_2d(&ta, A, a_rows, a_cols, kBM) || !encode_int8_2d(&tb, B, n_pad, k_pad, kBN))
     return false;
+  const int64_t m_pad = (M + kBM - 1) / kBM * kBM;
   if (cudaFuncSetAttribute(int8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(kSmemInt8)) != cudaSuccess)
     return false;
   const int num_kb = static_cast<int>((k_pad + kBK - 1) / kBK);
   const dim3 grid(static_cast<unsigned>(m_pad / kBM), static_cast<unsigned>((N + kBN - 1) / kBN));
   int8_tc_kernel<<<grid, kThreads, kSmemInt8, stream>>>(ta, tb, num_kb, M, N, y, status);
+  g_tc_launches.fetch_add(1, std::memory_order_relaxed);
   return true;
 }
 
 } // namespace cim::tc
+
+extern "C" int64_t cim22_cuda_tensor_core_launches(void) {
+  return cim::tc::g_tc_launches.load(std::memory_order_relaxed);
+}

@@ -987,6 +987,10 @@ int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,
   }
   auto s = static_cast<cudaStream_t>(stream);
   const int64_t m_pad = round_up(m, kColumnPad);
+  if (layer->range_safe && tc::int8_available() && layer->k % 16 == 0 &&
+      tc::launch_int8(x, m, layer->k, layer->weights, layer->n_pad, layer->k_pad, m, layer->n,
+                      y, status, s))
+    return cuda_ok(cudaGetLastError(), "int8 launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
   int8_t *A = static_cast<int8_t *>(workspace);
   const int64_t total = m_pad * layer->k_pad;
   const unsigned blocks =
@@ -996,7 +1000,7 @@ int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,
     return CIM22_STATUS_BAD_ARGUMENT;
   const int T = static_cast<int>(layer->tiles);
   if (layer->range_safe && tc::int8_available() &&
-      tc::launch_int8(A, m_pad, layer->weights, layer->n_pad, layer->k_pad, T, m,
+      tc::launch_int8(A, m_pad, layer->k_pad, layer->weights, layer->n_pad, layer->k_pad, m,
                       layer->n, y, status, s))
     return cuda_ok(cudaGetLastError(), "int8 launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
   const dim3 grid(static_cast<unsigned>(m_pad / 64),

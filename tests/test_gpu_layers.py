@@ -210,8 +210,12 @@ def test_linear_int8_tensor_core_shapes(m, k, n):
     rng = np.random.default_rng(m + k + n)
     x = rng.integers(-128, 128, (m, k)).astype(np.int8)
     w = rng.integers(-8, 8, (n, k)).astype(np.int8)  # provably in range
+    from cim22_b200.native import lib
+
     layer = CimLayer(w, kind="int8")
     assert layer.range_safe
+    before = lib().cim22_cuda_tensor_core_launches()
     got = layer.linear_int8(torch.from_numpy(x).to(DEV)).cpu().numpy()
+    assert lib().cim22_cuda_tensor_core_launches() == before + 1
     exp = (x.astype(np.int64) @ w.T.astype(np.int64)).astype(np.int32)
     np.testing.assert_array_equal(got, exp)
