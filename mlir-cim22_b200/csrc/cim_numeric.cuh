@@ -220,4 +220,23 @@ CIM_HD uint16_t signsplit_tile(uint32_t p, int ew, int ex) {
   return bf16_round_scaled(truncate8(p), ew + ex - 266);
 }
 
+// Exponent recorded for an all-zero activation group: every dot with it is
+// 0, so its tiles add +0 and the contractions skip it.
+constexpr int kZeroGroup = 0x7fff;
+
+#if defined(__CUDACC__)
+// 2^e as an exact f32 for e in [-149, 127].
+__device__ __forceinline__ float exp2i(int e) {
+  return e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23)
+                   : __uint_as_float(1u << (e + 149));
+}
+
+// Q(p) as an exact f32 for 0 <= p < 2^23: the magic-number conversion is exact
+// and clearing the low 16 bits keeps the eight leading significant bits.
+__device__ __forceinline__ float trunc8f(int32_t p) {
+  const float f = __uint_as_float(static_cast<uint32_t>(p) | 0x4b000000u) - 8388608.0f;
+  return __uint_as_float(__float_as_uint(f) & 0xffff0000u);
+}
+#endif
+
 } // namespace cim

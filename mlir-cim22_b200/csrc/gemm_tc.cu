@@ -18,6 +18,7 @@
 #include "gemm_tc.h"
 
 #include "cim_internal.h"
+#include "cim_numeric.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -233,6 +234,260 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// BF16 sign-split contraction. Per 64-K crossbar tile t the two MMAs of each
+// activation branch (xp, xn) produce 128 columns x 64 lanes of int32 dots in
+// TMEM: the B tile stacks the CTA's 32 Wp lanes over its 32 Wn lanes, so one
+// N=64 MMA covers both weight branches. Tile results alternate between two
+// TMEM buffers so the MMA of tile t+1 overlaps the epilogue of tile t. The
+// epilogue (8 warps; warp w reads TMEM lanes 32 * (w % 4) and half of the
+// lanes) restores each dot as RNE_bf16(Q(p) * 2^(Ew + Ex - 266)) and adds it
+// to its f32 branch sum in tile order - exactly through an FMA inside the
+// normal window, through the integer path otherwise - then rounds, merges
+// ((pp - pn) - np) + nn, adds the bias and applies the activation.
+constexpr int kSBM = 128, kSBL = 32, kSN = 2 * kSBL, kSBK = 128, kSStages = 4;
+constexpr int kSThreads = 320; // producer warp, MMA warp, 8 epilogue warps
+constexpr int kEpiWarps = 8;
+
+struct alignas(1024) SmemSS {
+  int8_t a[kSStages][2][kSBM * kSBK];
+  int8_t b[kSStages][kSN * kSBK];
+  uint64_t full[kSStages];
+  uint64_t empty[kSStages];
+  uint64_t dfull[2];
+  uint64_t dempty[2];
+  uint32_t tmem;
+  int failed;
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, "
+               "%9, %10, %11, %12, %13, %14, %15}, [%16];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                 "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Exact restore of one tile value outside the fast window (out of line).
+__device__ __noinline__ float tc_slow_tile_add(float acc, int p, int ew, int ex,
+                                               int32_t *status) {
+  const uint16_t tile = signsplit_tile(static_cast<uint32_t>(p), ew, ex);
+  if (tile == kBF16Inf)
+    atomicOr(status, CIM22_STATUS_TILE_OVERFLOW);
+  return __fadd_rn(acc, bf16_to_f32(tile));
+}
+
+__device__ __forceinline__ float act_tc(float v, int act) {
+  if (act == CIM22_ACT_RELU)
+    return v > 0.0f ? v : 0.0f;
+  if (act == CIM22_ACT_GELU)
+    return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  return v;
+}
+
+template <int kAB>
+__global__ void __launch_bounds__(kSThreads, 1)
+    signsplit_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const int32_t *__restrict__ exA,
+                        int m_pad, const int32_t *__restrict__ exB, int n_pad, int T, int M,
+                        int N, const float *__restrict__ bias, int act, float *__restrict__ y,
+                        int32_t *status) {
+  extern __shared__ uint8_t smem_raw[];
+  SmemSS &s = *reinterpret_cast<SmemSS *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m0 = static_cast<int>(blockIdx.x) * kSBM;
+  const int n0 = static_cast<int>(blockIdx.y) * kSBL;
+  const int num_kb = (T + 1) / 2;
+  constexpr uint32_t kBufCols = kAB * kSN;
+  constexpr uint32_t kTmemCols = 2 * kBufCols < 32 ? 32 : 2 * kBufCols;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.dfull[i], 1);
+      mbar_init(&s.dempty[i], kEpiWarps);
+    }
+    s.failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s.tmem)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = s.tmem;
+  volatile int *failed = &s.failed;
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer: per K-block, the activation tile of each branch and the
+    // stacked Wp/Wn weight tile.
+    int issued = 0;
+    for (int kb = 0; kb < num_kb; ++kb) {
+      const int stage = kb % kSStages;
+      if (!mbar_wait(&s.empty[stage], ((kb / kSStages) & 1) ^ 1) || *failed) {
+        *failed = 1;
+        break;
+      }
+      mbar_expect_tx(&s.full[stage], kAB * kSBM * kSBK + kSN * kSBK);
+#pragma unroll
+      for (int a = 0; a < kAB; ++a)
+        tma_load_2d(s.a[stage][a], &tmA, &s.full[stage], kb * kSBK, a * m_pad + m0);
+      tma_load_2d(s.b[stage], &tmB, &s.full[stage], kb * kSBK, n0);
+      tma_load_2d(s.b[stage] + kSBL * kSBK, &tmB, &s.full[stage], kb * kSBK, n_pad + n0);
+      issued = kb + 1;
+    }
+    for (int kb = issued > kSStages ? issued - kSStages : 0; kb < issued; ++kb)
+      mbar_wait(&s.full[kb % kSStages], (kb / kSStages) & 1);
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer: two K=32 MMAs per branch per crossbar tile.
+    constexpr uint32_t idesc = idesc_i8(kSBM, kSN);
+    for (int t = 0; t < T; ++t) {
+      const int kb = t / 2, half = t % 2, stage = kb % kSStages, buf = t % 2;
+      if (half == 0 && (!mbar_wait(&s.full[stage], (kb / kSStages) & 1) || *failed)) {
+        *failed = 1;
+        break;
+      }
+      if (!mbar_wait(&s.dempty[buf], ((t / 2) & 1) ^ 1) || *failed) {
+        *failed = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint64_t bdesc = sw128_desc(s.b[stage]) + half * 4;
+#pragma unroll
+      for (int a = 0; a < kAB; ++a) {
+        const uint64_t adesc = sw128_desc(s.a[stage][a]) + half * 4;
+        const uint32_t d = tmem + buf * kBufCols + a * kSN;
+        mma_i8(d, adesc, bdesc, idesc, 0u);
+        mma_i8(d, adesc + 2, bdesc + 2, idesc, 1u);
+      }
+      mma_commit(&s.dfull[buf]);
+      if (half == 1 || t == T - 1)
+        mma_commit(&s.empty[stage]);
+    }
+  } else if (warp >= 2) {
+    // Epilogue.
+    const int quad = warp % 4, sub = (warp - 2) / 4;
+    const int row_local = quad * 32 + lane;
+    const int row = m0 + row_local;
+    const int lane0 = n0 + sub * 16;
+    float acc[kAB][2][16];
+#pragma unroll
+    for (int a = 0; a < kAB; ++a)
+#pragma unroll
+      for (int w = 0; w < 2; ++w)
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          acc[a][w][j] = 0.0f;
+    bool ok = true;
+    for (int t = 0; t < T; ++t) {
+      const int buf = t % 2;
+      int ex[kAB];
+#pragma unroll
+      for (int a = 0; a < kAB; ++a)
+        ex[a] = exA[(static_cast<int64_t>(a) * T + t) * m_pad + m0 + row_local];
+      float sw[2][16];
+      int ewlo = 1 << 30, ewhi = -(1 << 30);
+#pragma unroll
+      for (int w = 0; w < 2; ++w) {
+        const int4 *src = reinterpret_cast<const int4 *>(
+            exB + (static_cast<int64_t>(w) * T + t) * n_pad + lane0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int4 e4 = src[q];
+          const int e[4] = {e4.x, e4.y, e4.z, e4.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            sw[w][4 * q + i] = exp2i(e[i] - 133);
+            ewlo = min(ewlo, e[i]);
+            ewhi = max(ewhi, e[i]);
+          }
+        }
+      }
+      if (!mbar_wait(&s.dfull[buf], (t / 2) & 1) || *failed) {
+        ok = false;
+        *failed = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+      for (int a = 0; a < kAB; ++a) {
+        const bool zero = ex[a] == kZeroGroup;
+        const bool fast = ex[a] + ewlo >= 140 && ex[a] + ewhi <= 374 && ex[a] <= 240;
+        const float sx = zero ? 1.0f : exp2i(ex[a] - 133);
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          uint32_t p[16];
+          tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * kBufCols +
+                        a * kSN + w * kSBL + sub * 16,
+                    p);
+          if (zero)
+            continue;
+          if (fast) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              acc[a][w][j] = fmaf(__fmul_rn(trunc8f(static_cast<int>(p[j])), sx), sw[w][j],
+                                  acc[a][w][j]);
+          } else {
+            for (int j = 0; j < 16; ++j)
+              acc[a][w][j] = tc_slow_tile_add(
+                  acc[a][w][j], static_cast<int>(p[j]),
+                  exB[(static_cast<int64_t>(w) * T + t) * n_pad + lane0 + j], ex[a], status);
+          }
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0)
+        mbar_arrive(&s.dempty[buf]);
+    }
+    if (!ok) {
+      if (lane == 0)
+        atomicOr(status, CIM22_STATUS_TIMEOUT);
+    } else if (row < M) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int col = lane0 + j;
+        if (col >= N)
+          break;
+        float br[kAB][2];
+#pragma unroll
+        for (int a = 0; a < kAB; ++a)
+#pragma unroll
+          for (int w = 0; w < 2; ++w)
+            br[a][w] = T > 1 ? bf16_to_f32(f32_to_bf16(acc[a][w][j])) : acc[a][w][j];
+        float out = __fsub_rn(br[0][0], br[0][1]);
+        if (kAB == 2) {
+          out = __fsub_rn(out, br[1][0]);
+          out = __fadd_rn(out, br[1][1]);
+        }
+        if (bias != nullptr)
+          out = __fadd_rn(out, bias[col]);
+        y[static_cast<int64_t>(row) * N + col] = act_tc(out, act);
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols));
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side.
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -281,14 +536,44 @@ constexpr size_t kSmemInt8 = sizeof(SmemInt8) + 1024;
 
 std::atomic<int64_t> g_tc_launches{0};
 
-bool signsplit_available() { return false; }
+constexpr size_t kSmemSS = sizeof(SmemSS) + 1024;
+
+bool signsplit_available() { return sm100(nullptr) && encode_fn() != nullptr; }
 
 bool int8_available() { return sm100(nullptr) && encode_fn() != nullptr; }
 
-bool launch_signsplit(const int8_t *, const int32_t *, int64_t, const int8_t *,
-                      const int32_t *, int64_t, int64_t, int, int64_t, int64_t,
-                      const float *, int, int, float *, int32_t *, cudaStream_t) {
-  return false;
+bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const int8_t *B,
+                      const int32_t *exB, int64_t n_pad, int64_t k_pad, int T, int64_t M,
+                      int64_t N, const float *bias, int act, int act_branches, float *y,
+                      int32_t *status, cudaStream_t stream) {
+  // Worth it only when the crossbar tiles are wide enough to feed the MMA.
+  if (N < 32 || M < 512 || m_pad % kSBM || n_pad % kSBL || k_pad % 64 ||
+      static_cast<int64_t>(act_branches) * m_pad >= (int64_t{1} << 31) ||
+      (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
+      (reinterpret_cast<uintptr_t>(exB) & 15))
+    return false;
+  CUtensorMap ta, tb;
+  if (!encode_int8_2d(&ta, A, act_branches * m_pad, k_pad, kSBM) ||
+      !encode_int8_2d(&tb, B, 2 * n_pad, k_pad, kSBL))
+    return false;
+  const dim3 grid(static_cast<unsigned>(m_pad / kSBM), static_cast<unsigned>((N + kSBL - 1) / kSBL));
+  if (act_branches == 2) {
+    if (cudaFuncSetAttribute(signsplit_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemSS)) != cudaSuccess)
+      return false;
+    signsplit_tc_kernel<2><<<grid, kSThreads, kSmemSS, stream>>>(
+        ta, tb, exA, static_cast<int>(m_pad), exB, static_cast<int>(n_pad), T,
+        static_cast<int>(M), static_cast<int>(N), bias, act, y, status);
+  } else {
+    if (cudaFuncSetAttribute(signsplit_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemSS)) != cudaSuccess)
+      return false;
+    signsplit_tc_kernel<1><<<grid, kSThreads, kSmemSS, stream>>>(
+        ta, tb, exA, static_cast<int>(m_pad), exB, static_cast<int>(n_pad), T,
+        static_cast<int>(M), static_cast<int>(N), bias, act, y, status);
+  }
+  g_tc_launches.fetch_add(1, std::memory_order_relaxed);
+  return true;
 }
 
 bool launch_int8(const int8_t *A, int64_t a_rows, int64_t a_cols, const int8_t *B,

@@ -197,9 +197,6 @@ __device__ __forceinline__ float next_value(const float *__restrict__ x, const G
 // its 8 aligned bytes per branch. Padding columns (m >= M) and padding K are
 // zero; an all-zero group records the exponent kZeroGroup.
 constexpr int kGroupThreads = 8;
-// Exponent recorded for an all-zero group: every dot with it is 0, so its
-// tiles add +0 and the contraction skips it.
-constexpr int kZeroGroup = 0x7fff;
 
 template <int kActBranches>
 __global__ void __launch_bounds__(256)
@@ -308,18 +305,6 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// 2^e as an exact f32 for e in [-149, 127].
-__device__ __forceinline__ float exp2i(int e) {
-  return e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23)
-                   : __uint_as_float(1u << (e + 149));
-}
-
-// Q(p) as an exact f32: the conversion is exact below 2^24 and clearing the
-// low 16 bits keeps the eight leading significant bits, truncating.
-__device__ __forceinline__ float trunc8f(int32_t p) {
-  const float f = __uint_as_float(static_cast<uint32_t>(p) | 0x4b000000u) - 8388608.0f;
-  return __uint_as_float(__float_as_uint(f) & 0xffff0000u);
-}
 
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == CIM22_ACT_RELU)

@@ -219,3 +219,28 @@ def test_linear_int8_tensor_core_shapes(m, k, n):
     assert lib().cim22_cuda_tensor_core_launches() == before + 1
     exp = (x.astype(np.int64) @ w.T.astype(np.int64)).astype(np.int32)
     np.testing.assert_array_equal(got, exp)
+
+
+@pytest.mark.parametrize("m,k,n,branches,scale", [
+    (1024, 4096, 512, 4, 1.0), (2000, 150, 40, 2, 1.0), (777, 640, 96, 4, 1.0),
+    (600, 200, 64, 4, 1e-30), (512, 64, 32, 4, 1e18)])
+def test_linear_bf16_tensor_core_bit_exact(m, k, n, branches, scale):
+    """Wide layers run the tcgen05 sign-split kernel (launch counter checked)."""
+    from cim22_b200.cim_ops import CimLayer
+    from cim22_b200.native import lib
+
+    rng = np.random.default_rng(m + k + n)
+    x = (rng.standard_normal((m, k)) * scale).astype(np.float32)
+    x[rng.random((m, k)) < 0.01] *= 20
+    if branches == 2:
+        x = np.maximum(x, 0)
+    x[rng.random((m, k)) < 0.3] = 0  # zero groups and sparse inputs
+    w = (rng.standard_normal((n, k)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    expected = oracle.linear_bf16(x, w, b, branches=4, threads=8)
+    layer = CimLayer(w)
+    before = lib().cim22_cuda_tensor_core_launches()
+    got = layer.linear_bf16(torch.from_numpy(x).to(DEV), bias=torch.from_numpy(b).to(DEV),
+                            branches=branches).cpu().numpy()
+    assert lib().cim22_cuda_tensor_core_launches() == before + 1
+    np.testing.assert_array_equal(bits(got), bits(expected))
