@@ -21,8 +21,10 @@
 #include "cim_numeric.cuh"
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 
@@ -236,25 +238,54 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // BF16 sign-split contraction. Per 64-K crossbar tile t the two MMAs of each
 // activation branch (xp, xn) produce 128 columns x 64 lanes of int32 dots in
-// TMEM: the B tile stacks the CTA's 32 Wp lanes over its 32 Wn lanes, so one
-// N=64 MMA covers both weight branches. Tile results alternate between two
-// TMEM buffers so the MMA of tile t+1 overlaps the epilogue of tile t. The
-// epilogue (8 warps; warp w reads TMEM lanes 32 * (w % 4) and half of the
-// lanes) restores each dot as RNE_bf16(Q(p) * 2^(Ew + Ex - 266)) and adds it
-// to its f32 branch sum in tile order - exactly through an FMA inside the
-// normal window, through the integer path otherwise - then rounds, merges
-// ((pp - pn) - np) + nn, adds the bias and applies the activation.
+// TMEM: one N=64 MMA covers both weight branches (Wp rows, then Wn rows).
+// The kernel is persistent: each CTA walks output tiles (128 columns x 32
+// lanes) blockIdx.x, blockIdx.x + gridDim.x, ... and every crossbar tile of
+// every output tile flows through the same three rings:
+//
+//   warp 0 (one thread)   TMA producer: per K-block of 128 bytes (two
+//                          crossbar tiles) the activation tile of each branch
+//                          and the stacked Wp/Wn tile into a 4-stage ring;
+//                          per crossbar tile the activation exponents of the
+//                          128 columns, the 2 x 32 weight exponents and the
+//                          tile's weight-exponent range into a 16-slot ring
+//                          (cp.async.bulk, no multicast)
+//   warp 1 (one thread)   tcgen05.mma kind::i8 into one of 4 TMEM buffers
+//   warps 2-17            epilogue: warp w reads TMEM lanes 32 * (w % 4) and
+//                          8 of the 32 lanes; it restores each dot as
+//                          RNE_bf16(Q(p) * 2^(Ew + Ex - 266)) and adds it to
+//                          its f32 branch sum in tile order, then rounds,
+//                          merges ((pp - pn) - np) + nn, adds the bias and
+//                          applies the activation
+//
+// Inside the normal window (7 <= Ex <= 237, 140 <= Ex + Ew <= 374 for every
+// weight exponent of the tile) the restore is exact in three f32 operations:
+// fma(2^23 + p, 2^(Ex-133), -2^23 * 2^(Ex-133)) = p * 2^(Ex-133) is a normal
+// f32, clearing its low 16 bits keeps Q(p), and the product with 2^(Ew-133)
+// is the exactly representable tile value, so one FMA adds it with the single
+// rounding of the reference's f32 add. Outside the window the integer path
+// (signsplit_tile) restores the tile.
 constexpr int kSBM = 128, kSBL = 32, kSN = 2 * kSBL, kSBK = 128, kSStages = 4;
-constexpr int kSThreads = 320; // producer warp, MMA warp, 8 epilogue warps
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
+constexpr int kSThreads = 64 + 32 * kEpiWarps;
+constexpr int kExpSlots = 16, kTmemBufs = 4;
 
-struct alignas(1024) SmemSS {
-  int8_t a[kSStages][2][kSBM * kSBK];
+struct alignas(16) ExpSlot {
+  int32_t a[2][kSBM];  // activation group exponents per branch
+  float w[2][kSBL];    // weight scales 2^(Ew - 133), Wp then Wn
+  int32_t range[4];    // min and max weight exponent of the tile, 2 pad words
+};
+
+template <int kAB> struct alignas(1024) SmemSS {
+  int8_t a[kSStages][kAB][kSBM * kSBK];
   int8_t b[kSStages][kSN * kSBK];
+  ExpSlot ex[kExpSlots];
   uint64_t full[kSStages];
   uint64_t empty[kSStages];
-  uint64_t dfull[2];
-  uint64_t dempty[2];
+  uint64_t exfull[kExpSlots];
+  uint64_t exempty[kExpSlots];
+  uint64_t dfull[kTmemBufs];
+  uint64_t dempty[kTmemBufs];
   uint32_t tmem;
   int failed;
 };
@@ -263,14 +294,28 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, "
-               "%9, %10, %11, %12, %13, %14, %15}, [%16];"
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], "
+               "%2, [%3];" ::"r"(smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Issue a 32x32b.x8 TMEM load; the values are valid after tmem_wait8.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-                 "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
-                 "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Wait for the outstanding TMEM loads. The registers are in/out operands so
+// no use of them is scheduled before the wait.
+__device__ __forceinline__ void tmem_wait8(uint32_t (&r)[8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7])::"memory");
 }
 
 // Exact restore of one tile value outside the fast window (out of line).
@@ -298,20 +343,26 @@ __global__ void __launch_bounds__(kSThreads, 1)
                         int N, const float *__restrict__ bias, int act, float *__restrict__ y,
                         int32_t *status) {
   extern __shared__ uint8_t smem_raw[];
-  SmemSS &s = *reinterpret_cast<SmemSS *>(
+  SmemSS<kAB> &s = *reinterpret_cast<SmemSS<kAB> *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int m0 = static_cast<int>(blockIdx.x) * kSBM;
-  const int n0 = static_cast<int>(blockIdx.y) * kSBL;
   const int num_kb = (T + 1) / 2;
+  const int num_nb = (N + kSBL - 1) / kSBL;
+  const int num_tiles = ((M + kSBM - 1) / kSBM) * num_nb;
+  const int32_t *ranges = exB + int64_t{2} * T * n_pad; // [n_pad / 32][T][4]
+  const int32_t *scales = ranges + int64_t{n_pad / 32} * T * 4; // f32 [2][T][n_pad]
   constexpr uint32_t kBufCols = kAB * kSN;
-  constexpr uint32_t kTmemCols = 2 * kBufCols < 32 ? 32 : 2 * kBufCols;
+  constexpr uint32_t kTmemCols = kTmemBufs * kBufCols;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSStages; ++i) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kExpSlots; ++i) {
+      mbar_init(&s.exfull[i], 1);
+      mbar_init(&s.exempty[i], kEpiWarps);
+    }
+    for (int i = 0; i < kTmemBufs; ++i) {
       mbar_init(&s.dfull[i], 1);
       mbar_init(&s.dempty[i], kEpiWarps);
     }
@@ -331,151 +382,211 @@ __global__ void __launch_bounds__(kSThreads, 1)
   volatile int *failed = &s.failed;
 
   if (warp == 0 && lane == 0) {
-    // TMA producer: per K-block, the activation tile of each branch and the
-    // stacked Wp/Wn weight tile.
-    int issued = 0;
-    for (int kb = 0; kb < num_kb; ++kb) {
-      const int stage = kb % kSStages;
-      if (!mbar_wait(&s.empty[stage], ((kb / kSStages) & 1) ^ 1) || *failed) {
-        *failed = 1;
-        break;
-      }
-      mbar_expect_tx(&s.full[stage], kAB * kSBM * kSBK + kSN * kSBK);
+    uint32_t kbi = 0, gi = 0;
+    bool ok = true;
+    for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
+      const int m0 = (ot / num_nb) * kSBM, nb = ot % num_nb, n0 = nb * kSBL;
+      for (int kb = 0; kb < num_kb; ++kb, ++kbi) {
+        const int stage = kbi % kSStages;
+        if (!mbar_wait(&s.empty[stage], ((kbi / kSStages) & 1) ^ 1) || *failed) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&s.full[stage], kAB * kSBM * kSBK + kSN * kSBK);
 #pragma unroll
-      for (int a = 0; a < kAB; ++a)
-        tma_load_2d(s.a[stage][a], &tmA, &s.full[stage], kb * kSBK, a * m_pad + m0);
-      tma_load_2d(s.b[stage], &tmB, &s.full[stage], kb * kSBK, n0);
-      tma_load_2d(s.b[stage] + kSBL * kSBK, &tmB, &s.full[stage], kb * kSBK, n_pad + n0);
-      issued = kb + 1;
+        for (int a = 0; a < kAB; ++a)
+          tma_load_2d(s.a[stage][a], &tmA, &s.full[stage], kb * kSBK, a * m_pad + m0);
+        tma_load_2d(s.b[stage], &tmB, &s.full[stage], kb * kSBK, n0);
+        tma_load_2d(s.b[stage] + kSBL * kSBK, &tmB, &s.full[stage], kb * kSBK, n_pad + n0);
+        for (int t = 2 * kb; t < 2 * kb + 2 && t < T; ++t, ++gi) {
+          const int slot = gi % kExpSlots;
+          if (!mbar_wait(&s.exempty[slot], ((gi / kExpSlots) & 1) ^ 1) || *failed) {
+            ok = false;
+            break;
+          }
+          ExpSlot &e = s.ex[slot];
+          mbar_expect_tx(&s.exfull[slot], kAB * kSBM * 4 + 2 * kSBL * 4 + 16);
+#pragma unroll
+          for (int a = 0; a < kAB; ++a)
+            bulk_load(e.a[a], exA + (static_cast<int64_t>(a) * T + t) * m_pad + m0, kSBM * 4,
+                      &s.exfull[slot]);
+#pragma unroll
+          for (int w = 0; w < 2; ++w)
+            bulk_load(e.w[w], scales + (static_cast<int64_t>(w) * T + t) * n_pad + n0, kSBL * 4,
+                      &s.exfull[slot]);
+          bulk_load(e.range, ranges + (static_cast<int64_t>(nb) * T + t) * 4, 16,
+                    &s.exfull[slot]);
+        }
+        if (!ok) {
+          ++kbi;
+          break;
+        }
+      }
     }
-    for (int kb = issued > kSStages ? issued - kSStages : 0; kb < issued; ++kb)
-      mbar_wait(&s.full[kb % kSStages], (kb / kSStages) & 1);
+    if (!ok)
+      *failed = 1;
+    // Never leave with copies in flight: wait (bounded) for the stages and
+    // exponent slots this thread filled but the consumers may not have used.
+    for (uint32_t i = kbi > kSStages ? kbi - kSStages : 0; i < kbi; ++i)
+      mbar_wait(&s.full[i % kSStages], (i / kSStages) & 1);
+    for (uint32_t i = gi > kExpSlots ? gi - kExpSlots : 0; i < gi; ++i)
+      mbar_wait(&s.exfull[i % kExpSlots], (i / kExpSlots) & 1);
   } else if (warp == 1 && lane == 0) {
     // MMA issuer: two K=32 MMAs per branch per crossbar tile.
     constexpr uint32_t idesc = idesc_i8(kSBM, kSN);
-    for (int t = 0; t < T; ++t) {
-      const int kb = t / 2, half = t % 2, stage = kb % kSStages, buf = t % 2;
-      if (half == 0 && (!mbar_wait(&s.full[stage], (kb / kSStages) & 1) || *failed)) {
-        *failed = 1;
-        break;
-      }
-      if (!mbar_wait(&s.dempty[buf], ((t / 2) & 1) ^ 1) || *failed) {
-        *failed = 1;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint64_t bdesc = sw128_desc(s.b[stage]) + half * 4;
+    uint32_t kbi = 0, gi = 0;
+    bool ok = true;
+    for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
+      for (int t = 0; t < T; ++t, ++gi) {
+        const int half = t % 2, stage = kbi % kSStages, buf = gi % kTmemBufs;
+        if ((half == 0 && !mbar_wait(&s.full[stage], (kbi / kSStages) & 1)) ||
+            !mbar_wait(&s.dempty[buf], ((gi / kTmemBufs) & 1) ^ 1) || *failed) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t bdesc = sw128_desc(s.b[stage]) + half * 4;
 #pragma unroll
-      for (int a = 0; a < kAB; ++a) {
-        const uint64_t adesc = sw128_desc(s.a[stage][a]) + half * 4;
-        const uint32_t d = tmem + buf * kBufCols + a * kSN;
-        mma_i8(d, adesc, bdesc, idesc, 0u);
-        mma_i8(d, adesc + 2, bdesc + 2, idesc, 1u);
+        for (int a = 0; a < kAB; ++a) {
+          const uint64_t adesc = sw128_desc(s.a[stage][a]) + half * 4;
+          const uint32_t d = tmem + buf * kBufCols + a * kSN;
+          mma_i8(d, adesc, bdesc, idesc, 0u);
+          mma_i8(d, adesc + 2, bdesc + 2, idesc, 1u);
+        }
+        mma_commit(&s.dfull[buf]);
+        if (half == 1 || t == T - 1) {
+          mma_commit(&s.empty[stage]);
+          ++kbi;
+        }
       }
-      mma_commit(&s.dfull[buf]);
-      if (half == 1 || t == T - 1)
-        mma_commit(&s.empty[stage]);
     }
+    if (!ok)
+      *failed = 1;
+    // Let the last MMAs land before TMEM is freed.
+    if (gi > 0)
+      mbar_wait(&s.dfull[(gi - 1) % kTmemBufs], ((gi - 1) / kTmemBufs) & 1);
   } else if (warp >= 2) {
     // Epilogue.
     const int quad = warp % 4, sub = (warp - 2) / 4;
     const int row_local = quad * 32 + lane;
-    const int row = m0 + row_local;
-    const int lane0 = n0 + sub * 16;
-    float acc[kAB][2][16];
-#pragma unroll
-    for (int a = 0; a < kAB; ++a)
-#pragma unroll
-      for (int w = 0; w < 2; ++w)
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          acc[a][w][j] = 0.0f;
+    const uint32_t tlane = static_cast<uint32_t>(quad * 32) << 16;
+    uint32_t gi = 0;
     bool ok = true;
-    for (int t = 0; t < T; ++t) {
-      const int buf = t % 2;
-      int ex[kAB];
+    for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
+      const int m0 = (ot / num_nb) * kSBM, n0 = (ot % num_nb) * kSBL;
+      const int lane0 = n0 + sub * 8;
+      float acc[kAB][2][8];
 #pragma unroll
       for (int a = 0; a < kAB; ++a)
-        ex[a] = exA[(static_cast<int64_t>(a) * T + t) * m_pad + m0 + row_local];
-      float sw[2][16];
-      int ewlo = 1 << 30, ewhi = -(1 << 30);
 #pragma unroll
-      for (int w = 0; w < 2; ++w) {
-        const int4 *src = reinterpret_cast<const int4 *>(
-            exB + (static_cast<int64_t>(w) * T + t) * n_pad + lane0);
+        for (int w = 0; w < 2; ++w)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int4 e4 = src[q];
-          const int e[4] = {e4.x, e4.y, e4.z, e4.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            sw[w][4 * q + i] = exp2i(e[i] - 133);
-            ewlo = min(ewlo, e[i]);
-            ewhi = max(ewhi, e[i]);
-          }
+          for (int j = 0; j < 8; ++j)
+            acc[a][w][j] = 0.0f;
+      for (int t = 0; t < T; ++t, ++gi) {
+        const int slot = gi % kExpSlots, buf = gi % kTmemBufs;
+        if (!mbar_wait(&s.exfull[slot], (gi / kExpSlots) & 1) || *failed) {
+          ok = false;
+          break;
         }
-      }
-      if (!mbar_wait(&s.dfull[buf], (t / 2) & 1) || *failed) {
-        ok = false;
-        *failed = 1;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const ExpSlot &e = s.ex[slot];
+        const int2 range = *reinterpret_cast<const int2 *>(e.range);
+        float sx[kAB], nsx[kAB];
+        bool fast[kAB];
+        int ex[kAB];
 #pragma unroll
-      for (int a = 0; a < kAB; ++a) {
-        const bool zero = ex[a] == kZeroGroup;
-        const bool fast = ex[a] + ewlo >= 140 && ex[a] + ewhi <= 374 && ex[a] <= 240;
-        const float sx = zero ? 1.0f : exp2i(ex[a] - 133);
+        for (int a = 0; a < kAB; ++a) {
+          ex[a] = e.a[a][row_local];
+          const bool zero = ex[a] == kZeroGroup;
+          fast[a] = zero || (ex[a] >= 7 && ex[a] <= 237 && ex[a] + range.x >= 140 &&
+                             ex[a] + range.y <= 374);
+          sx[a] = zero || !fast[a] ? 0.0f : exp2i(ex[a] - 133);
+          nsx[a] = -8388608.0f * sx[a];
+        }
+        float sw[2][8];
 #pragma unroll
         for (int w = 0; w < 2; ++w) {
-          uint32_t p[16];
-          tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * kBufCols +
-                        a * kSN + w * kSBL + sub * 16,
-                    p);
-          if (zero)
-            continue;
-          if (fast) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              acc[a][w][j] = fmaf(__fmul_rn(trunc8f(static_cast<int>(p[j])), sx), sw[w][j],
-                                  acc[a][w][j]);
-          } else {
-            for (int j = 0; j < 16; ++j)
-              acc[a][w][j] = tc_slow_tile_add(
-                  acc[a][w][j], static_cast<int>(p[j]),
-                  exB[(static_cast<int64_t>(w) * T + t) * n_pad + lane0 + j], ex[a], status);
-          }
+          const float4 e0 = *reinterpret_cast<const float4 *>(&e.w[w][sub * 8]);
+          const float4 e1 = *reinterpret_cast<const float4 *>(&e.w[w][sub * 8 + 4]);
+          sw[w][0] = e0.x; sw[w][1] = e0.y; sw[w][2] = e0.z; sw[w][3] = e0.w;
+          sw[w][4] = e1.x; sw[w][5] = e1.y; sw[w][6] = e1.z; sw[w][7] = e1.w;
         }
-      }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0)
-        mbar_arrive(&s.dempty[buf]);
-    }
-    if (!ok) {
-      if (lane == 0)
-        atomicOr(status, CIM22_STATUS_TIMEOUT);
-    } else if (row < M) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int col = lane0 + j;
-        if (col >= N)
+        if (!mbar_wait(&s.dfull[buf], (gi / kTmemBufs) & 1) || *failed) {
+          ok = false;
           break;
-        float br[kAB][2];
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        // One activation branch at a time keeps 16 dots in registers.
 #pragma unroll
-        for (int a = 0; a < kAB; ++a)
+        for (int a = 0; a < kAB; ++a) {
+          uint32_t p[2][8];
 #pragma unroll
           for (int w = 0; w < 2; ++w)
-            br[a][w] = T > 1 ? bf16_to_f32(f32_to_bf16(acc[a][w][j])) : acc[a][w][j];
-        float out = __fsub_rn(br[0][0], br[0][1]);
-        if (kAB == 2) {
-          out = __fsub_rn(out, br[1][0]);
-          out = __fadd_rn(out, br[1][1]);
+            tmem_ld8(tmem + tlane + buf * kBufCols + a * kSN + w * kSBL + sub * 8, p[w]);
+          tmem_wait8(p[0]);
+          tmem_wait8(p[1]);
+          if (a == kAB - 1) {
+            // The dots are in registers: hand the TMEM buffer back.
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0)
+              mbar_arrive(&s.dempty[buf]);
+          }
+          if (fast[a]) {
+#pragma unroll
+            for (int w = 0; w < 2; ++w)
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float v =
+                    __fmaf_rn(__uint_as_float(p[w][j] | 0x4b000000u), sx[a], nsx[a]);
+                acc[a][w][j] = __fmaf_rn(__uint_as_float(__float_as_uint(v) & 0xffff0000u),
+                                         sw[w][j], acc[a][w][j]);
+              }
+          } else {
+            for (int w = 0; w < 2; ++w)
+              for (int j = 0; j < 8; ++j)
+                acc[a][w][j] = tc_slow_tile_add(
+                    acc[a][w][j], static_cast<int>(p[w][j]),
+                    exB[(static_cast<int64_t>(w) * T + t) * n_pad + lane0 + j], ex[a], status);
+          }
         }
-        if (bias != nullptr)
-          out = __fadd_rn(out, bias[col]);
-        y[static_cast<int64_t>(row) * N + col] = act_tc(out, act);
+        __syncwarp();
+        if (lane == 0)
+          mbar_arrive(&s.exempty[slot]);
       }
+      if (!ok)
+        break;
+      const int row = m0 + row_local;
+      if (row < M) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int col = lane0 + j;
+          if (col >= N)
+            break;
+          // Branch sums are finite or infinite, never NaN: the hardware
+          // RNE conversion rounds them as the reference's truncf does.
+          float br[kAB][2];
+#pragma unroll
+          for (int a = 0; a < kAB; ++a)
+#pragma unroll
+            for (int w = 0; w < 2; ++w)
+              br[a][w] = T > 1 ? __bfloat162float(__float2bfloat16_rn(acc[a][w][j]))
+                               : acc[a][w][j];
+          float out = __fsub_rn(br[0][0], br[0][1]);
+          if (kAB == 2) {
+            out = __fsub_rn(out, br[1][0]);
+            out = __fadd_rn(out, br[1][1]);
+          }
+          if (bias != nullptr)
+            out = __fadd_rn(out, bias[col]);
+          y[static_cast<int64_t>(row) * N + col] = act_tc(out, act);
+        }
+      }
+    }
+    if (!ok) {
+      *failed = 1;
+      if (lane == 0)
+        atomicOr(status, CIM22_STATUS_TIMEOUT);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -532,11 +643,25 @@ bool sm100(cudaStream_t) {
 
 constexpr size_t kSmemInt8 = sizeof(SmemInt8) + 1024;
 
+int sm_count() {
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return 148;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      return 148;
+    cached[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
 } // namespace
 
 std::atomic<int64_t> g_tc_launches{0};
 
-constexpr size_t kSmemSS = sizeof(SmemSS) + 1024;
+template <int kAB> constexpr size_t smem_ss() { return sizeof(SmemSS<kAB>) + 1024; }
 
 bool signsplit_available() { return sm100(nullptr) && encode_fn() != nullptr; }
 
@@ -547,28 +672,31 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
                       int64_t N, const float *bias, int act, int act_branches, float *y,
                       int32_t *status, cudaStream_t stream) {
   // Worth it only when the crossbar tiles are wide enough to feed the MMA.
+  // The exponent copies need 16-byte aligned rows: m_pad and n_pad are
+  // multiples of 128 and both exponent arrays start 16-byte aligned.
   if (N < 32 || M < 512 || m_pad % kSBM || n_pad % kSBL || k_pad % 64 ||
       static_cast<int64_t>(act_branches) * m_pad >= (int64_t{1} << 31) ||
       (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
-      (reinterpret_cast<uintptr_t>(exB) & 15))
+      (reinterpret_cast<uintptr_t>(exA) & 15) || (reinterpret_cast<uintptr_t>(exB) & 15))
     return false;
   CUtensorMap ta, tb;
   if (!encode_int8_2d(&ta, A, act_branches * m_pad, k_pad, kSBM) ||
       !encode_int8_2d(&tb, B, 2 * n_pad, k_pad, kSBL))
     return false;
-  const dim3 grid(static_cast<unsigned>(m_pad / kSBM), static_cast<unsigned>((N + kSBL - 1) / kSBL));
+  const int64_t tiles = ((M + kSBM - 1) / kSBM) * ((N + kSBL - 1) / kSBL);
+  const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, sm_count())));
   if (act_branches == 2) {
     if (cudaFuncSetAttribute(signsplit_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemSS)) != cudaSuccess)
+                             static_cast<int>(smem_ss<2>())) != cudaSuccess)
       return false;
-    signsplit_tc_kernel<2><<<grid, kSThreads, kSmemSS, stream>>>(
+    signsplit_tc_kernel<2><<<grid, kSThreads, smem_ss<2>(), stream>>>(
         ta, tb, exA, static_cast<int>(m_pad), exB, static_cast<int>(n_pad), T,
         static_cast<int>(M), static_cast<int>(N), bias, act, y, status);
   } else {
     if (cudaFuncSetAttribute(signsplit_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemSS)) != cudaSuccess)
+                             static_cast<int>(smem_ss<1>())) != cudaSuccess)
       return false;
-    signsplit_tc_kernel<1><<<grid, kSThreads, kSmemSS, stream>>>(
+    signsplit_tc_kernel<1><<<grid, kSThreads, smem_ss<1>(), stream>>>(
         ta, tb, exA, static_cast<int>(m_pad), exB, static_cast<int>(n_pad), T,
         static_cast<int>(M), static_cast<int>(N), bias, act, y, status);
   }

@@ -24,6 +24,7 @@
 #include <algorithm>
 #include <climits>
 #include <cmath>
+#include <cstring>
 #include <vector>
 
 namespace cim {
@@ -61,48 +62,46 @@ __device__ __forceinline__ int fdiv(int n, const FastDiv &f) {
 struct Gather32 {
   FastDiv div_ohw, div_ow, div_khw, div_kw;
   int kind, C, H, W, KH, KW, SH, SW, PH, PW, OH, OW;
-  int PK, PS, SRC_H, SRC_W; // fused max pool (NHWC), PK == 0 when absent
+  int PK;         // fused max pool window (NHWC), 0 when absent
+  int sC, sH, sW; // element strides of a channel, row and column of the gathered image
+  int pdy, pdx;   // strides of the pool window rows and columns in the pre-pool image
+  int image;      // elements per image
   int M, K;
   int pair_rows; // rows layout: 2 when K % 4 == 0 and x is 16-byte aligned (float4 loads)
 };
 
-// One element of image n at (ih, iw, c); `img` already points at image n.
-// With a fused max pool it reads the max over the pool window of the
-// pre-pool image (NaN propagates like torch.max_pool2d).
-__device__ __forceinline__ float image_load(const float *__restrict__ img,
-                                            const Gather32 &g, int ih, int iw,
-                                            int c) {
-  if (g.kind == CIM22_GATHER_CONV_NCHW)
-    return img[(c * g.H + ih) * g.W + iw];
-  if (g.PK == 0)
-    return img[(ih * g.W + iw) * g.C + c];
+// Prepare kernels by gather: linear rows, convolution windows, convolution
+// windows over a fused max pool.
+enum PrepareMode { kPrepRows = 0, kPrepConv = 1, kPrepConvPool = 2 };
+
+// One element at offset `off` of image `img`; with a fused max pool the max
+// over the pool window of the pre-pool image (NaN propagates like
+// torch.max_pool2d).
+template <int kMode>
+__device__ __forceinline__ float window_load(const float *__restrict__ img, const Gather32 &g,
+                                             int off) {
+  if (kMode != kPrepConvPool)
+    return __ldg(img + off);
+  if (g.PK == 2) {
+    // The common 2x2 window: four independent loads, then the ordered max.
+    const float v0 = __ldg(img + off), v1 = __ldg(img + off + g.pdx);
+    const float v2 = __ldg(img + off + g.pdy), v3 = __ldg(img + off + g.pdy + g.pdx);
+    float m = v0;
+    m = (v1 > m || v1 != v1) ? v1 : m;
+    m = (v2 > m || v2 != v2) ? v2 : m;
+    return (v3 > m || v3 != v3) ? v3 : m;
+  }
   float m = 0.0f;
   bool any = false;
   for (int dy = 0; dy < g.PK; ++dy)
     for (int dx = 0; dx < g.PK; ++dx) {
-      const float v = img[((ih * g.PS + dy) * g.SRC_W + iw * g.PS + dx) * g.C + c];
+      const float v = __ldg(img + off + dy * g.pdy + dx * g.pdx);
       if (!any || v > m || v != v) {
         m = v;
         any = true;
       }
     }
   return m;
-}
-
-// Sign-split preparation of a 64-element group (prepareBF16Input,
-// BF16Compensation.cpp:92-118). Fast path: when the group maximum is a normal
-// BF16 with biased exponent Ex >= 8, scaling by 2^(127-Ex) is exact for every
-// element that stays normal, and ExpPrealign then yields (0x80 | m) >>
-// (Ex - e + 1) for a gap Ex - e < 7; elements that would turn subnormal (or
-// are subnormal) have gaps >= 7 and align to 0. Other groups take the exact
-// RNE scaling of bf16_scalbn. The scaled maximum lies in [1, 2), so the
-// prealign exponent is always 127.
-__device__ __forceinline__ int8_t fast_align(uint32_t p, int emax) {
-  const int e = static_cast<int>(p >> 7);
-  const int gap = emax - e;
-  return (e >= 1 && gap < 7)
-             ? static_cast<int8_t>((0x80u | (p & 0x7fu)) >> (gap + 1))
-             : int8_t{0};
 }
 
 // Exact path for groups whose maximum is tiny (exponent < 8): RNE scaling of
@@ -112,196 +111,205 @@ __device__ __noinline__ uint32_t slow_align(uint32_t p, int shift) {
   return static_cast<uint8_t>(prealign_element(bf16_scalbn(static_cast<uint16_t>(p), shift), 127));
 }
 
-// Activation split (Passes.cpp:2379-2399): xp = (x < 0 ? 0 : x) then
-// (x == 0 ? +0 : xp), xn = (x < 0 ? -x : 0), each rounded to BF16 (RNE); a
-// 2-branch layer applies only the (x == 0 ? +0 : x) select.
-template <int kActBranches>
-__device__ __forceinline__ void split_bits(float v, uint32_t &bp, uint32_t &bn) {
-  const float zero = 0.0f;
-  float p = v, q = zero;
-  if (kActBranches == 2) {
-    const bool negative = v < zero;
-    p = negative ? zero : v;
-    q = negative ? -v : zero;
-  }
-  p = (v == zero) ? zero : p; // -0 becomes +0
-  bp = f32_to_bf16(p);
-  bn = f32_to_bf16(q);
+// Low bytes of four words, in order, as one word.
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c,
+                                                   uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-// Element source of one group: consecutive K indices of one column, with the
-// conv (c, i, j) decomposition stepped incrementally.
-struct GroupCursor {
-  const float *base; // rows: the column's row; conv: image n
-  int ih0, iw0;      // conv window origin (oh * SH - PH, ow * SW - PW)
-  int c, i, j;       // conv position of the current k
-  int k;
-  bool column_valid;
-};
-
-__device__ __forceinline__ GroupCursor open_group(const float *__restrict__ x, const Gather32 &g,
-                                                  int m, int kbeg) {
-  GroupCursor cur{};
-  cur.k = kbeg;
-  cur.column_valid = m < g.M;
-  if (g.kind == CIM22_GATHER_ROWS) {
-    cur.base = x + static_cast<int64_t>(m) * g.K;
-  } else if (cur.column_valid) {
-    const int n = fdiv(m, g.div_ohw);
-    const int r = m - n * g.OH * g.OW;
-    const int oh = fdiv(r, g.div_ow);
-    const int ow = r - oh * g.OW;
-    const int64_t image = g.kind == CIM22_GATHER_CONV_NCHW || g.PK == 0
-                              ? static_cast<int64_t>(g.C) * g.H * g.W
-                              : static_cast<int64_t>(g.C) * g.SRC_H * g.SRC_W;
-    cur.base = x + n * image;
-    cur.ih0 = oh * g.SH - g.PH;
-    cur.iw0 = ow * g.SW - g.PW;
-    cur.c = fdiv(kbeg, g.div_khw);
-    const int rk = kbeg - cur.c * g.KH * g.KW;
-    cur.i = fdiv(rk, g.div_kw);
-    cur.j = rk - cur.i * g.KW;
-  }
-  return cur;
-}
-
-__device__ __forceinline__ float next_value(const float *__restrict__ x, const Gather32 &g,
-                                            GroupCursor &cur) {
-  float v = 0.0f;
-  if (cur.column_valid && cur.k < g.K) {
-    if (g.kind == CIM22_GATHER_ROWS) {
-      v = cur.base[cur.k];
-    } else {
-      const int ih = cur.ih0 + cur.i;
-      const int iw = cur.iw0 + cur.j;
-      if (static_cast<unsigned>(ih) < static_cast<unsigned>(g.H) &&
-          static_cast<unsigned>(iw) < static_cast<unsigned>(g.W))
-        v = image_load(cur.base, g, ih, iw, cur.c);
-      if (++cur.j == g.KW) {
-        cur.j = 0;
-        if (++cur.i == g.KH) {
-          cur.i = 0;
-          ++cur.c;
-        }
-      }
-    }
-  }
-  ++cur.k;
-  return v;
-}
-
-// Prepare: eight threads per (column m, K tile t) group, eight consecutive
-// elements each; groups are ordered t-fastest so a warp's four groups read
-// one contiguous stretch of a row. The group maximum of each branch is an
-// xor-shuffle reduction within the 8-lane subgroup; each thread then writes
-// its 8 aligned bytes per branch. Padding columns (m >= M) and padding K are
-// zero; an all-zero group records the exponent kZeroGroup.
+// Sign-split preparation of 64-element groups (prepareBF16Input,
+// BF16Compensation.cpp:92-118, on the gathered operand of the reference's
+// im2col / row layout). Eight threads share a (column m, K tile t) group,
+// eight consecutive K elements each; the group maximum of each branch is an
+// xor-shuffle reduction within the 8-lane subgroup, then each thread writes
+// its 8 aligned bytes per branch. A block serves one K tile and 32 * cols
+// columns, so every thread decomposes its eight K indices into
+// (channel, kernel row, kernel column) offsets once and reuses them for
+// `cols` columns. Padding columns (m >= M) and padding K are zero; an
+// all-zero group records the exponent kZeroGroup.
+//
+// Alignment fast path: when the group maximum is a normal BF16 with biased
+// exponent Ex >= 8, scaling by 2^(127-Ex) is exact for every element that
+// stays normal and ExpPrealign yields (0x80 | m) >> (Ex - e + 1), i.e.
+// floor(v * 2^(133 - Ex)) for the BF16 value v, which is 0 for gaps >= 7 and
+// subnormal elements; fma(v, 2^(133 - Ex), 2^23) rounded toward zero holds
+// that floor in its low mantissa bits. Other groups take the exact RNE
+// scaling of bf16_scalbn. The scaled maximum lies in [1, 2), so the prealign
+// exponent is always 127.
 constexpr int kGroupThreads = 8;
 
-template <int kActBranches>
+template <int kActBranches, int kMode>
 __global__ void __launch_bounds__(256)
-    prepare_kernel(const float *__restrict__ x, Gather32 g, FastDiv div_t, int m_pad,
-                   int k_pad, int8_t *__restrict__ A, int32_t *__restrict__ ex,
+    prepare_kernel(const float *__restrict__ x, Gather32 g, FastDiv div_chunks, int T, int cols,
+                   int m_pad, int k_pad, int8_t *__restrict__ A, int32_t *__restrict__ ex,
                    int32_t *status) {
-  const int T = static_cast<int>(div_t.d);
-  const int group = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) / kGroupThreads);
+  const int blk = static_cast<int>(blockIdx.x);
+  const int t = fdiv(blk, div_chunks);
+  const int chunk = blk - t * static_cast<int>(div_chunks.d);
+  const int grp = static_cast<int>(threadIdx.x / kGroupThreads);
   const int sub = static_cast<int>(threadIdx.x % kGroupThreads);
-  if (group >= m_pad * T)
-    return; // uniform per 8-lane subgroup (blockDim is a multiple of 8)
   const unsigned mask = 0xffu << (threadIdx.x & 24);
-  const int m = fdiv(group, div_t);
-  const int t = group - m * T;
   const int kbeg = t * kTileK + sub * 8;
-  float v[8];
-  if (kbeg >= g.K || m >= g.M) {
+  unsigned kvalid = 0;
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      v[e] = 0.0f; // K or column padding
-  } else if (g.kind == CIM22_GATHER_ROWS && g.pair_rows == 2 && kbeg + 8 <= g.K) {
-    const float4 *src = reinterpret_cast<const float4 *>(x + static_cast<int64_t>(m) * g.K + kbeg);
-    const float4 lo = src[0], hi = src[1];
-    v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
-    v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
-  } else {
-    GroupCursor cur = open_group(x, g, m, kbeg);
+  for (int e = 0; e < 8; ++e)
+    kvalid |= (kbeg + e < g.K ? 1u : 0u) << e;
+  int rel[8], di[8], dj[8];
+  if (kMode != kPrepRows) {
+    int c = fdiv(kbeg, g.div_khw);
+    const int rk = kbeg - c * g.KH * g.KW;
+    int i = fdiv(rk, g.div_kw);
+    int j = rk - i * g.KW;
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      v[e] = next_value(x, g, cur);
-  }
-  // Split and round: xp = max(x, 0), xn = max(-x, 0) equal the reference's
-  // selects for every non-NaN x up to the sign of zero, which the preparation
-  // clears anyway (BF16Compensation.cpp:97); NaN, infinity and finite values
-  // that round to BF16 infinity (|x| >= 0x1.fep127) are caught on x itself.
-  // cvt.rn.bf16x2.f32 rounds to nearest even, as arith.truncf does.
-  uint32_t bits[2][8];
-  uint32_t mx[2] = {0, 0};
-  bool nonfinite = false, negative = false;
-  uint32_t packed[2][4];
-#pragma unroll
-  for (int e = 0; e < 8; e += 2) {
-    float p0 = v[e], p1 = v[e + 1], q0 = 0.0f, q1 = 0.0f;
-    nonfinite |= !(fabsf(p0) < 3.3961548e38f) || !(fabsf(p1) < 3.3961548e38f);
-    if (kActBranches == 2) {
-      q0 = fmaxf(-p0, 0.0f);
-      q1 = fmaxf(-p1, 0.0f);
-      p0 = fmaxf(p0, 0.0f);
-      p1 = fmaxf(p1, 0.0f);
-    } else {
-      negative |= p0 < 0.0f || p1 < 0.0f;
-    }
-    const __nv_bfloat162 hp = __floats2bfloat162_rn(p0, p1);
-    packed[0][e / 2] = *reinterpret_cast<const uint32_t *>(&hp) & 0x7fff7fffu;
-    if (kActBranches == 2) {
-      const __nv_bfloat162 hn = __floats2bfloat162_rn(q0, q1);
-      packed[1][e / 2] = *reinterpret_cast<const uint32_t *>(&hn) & 0x7fff7fffu;
-    }
-  }
-#pragma unroll
-  for (int a = 0; a < kActBranches; ++a) {
-    const uint32_t m2 = __vmaxu2(__vmaxu2(packed[a][0], packed[a][1]),
-                                 __vmaxu2(packed[a][2], packed[a][3]));
-    mx[a] = max(m2 & 0xffffu, m2 >> 16);
-#pragma unroll
-    for (int e = 0; e < 8; ++e)
-      bits[a][e] = (packed[a][e / 2] >> (16 * (e & 1))) & 0xffffu;
-  }
-#pragma unroll
-  for (int a = 0; a < kActBranches; ++a)
-#pragma unroll
-    for (int o = 4; o; o >>= 1)
-      mx[a] = max(mx[a], __shfl_xor_sync(mask, mx[a], o, kGroupThreads));
-  nonfinite = __any_sync(mask, nonfinite);
-  if (sub == 0 && nonfinite)
-    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-  if (negative && !nonfinite)
-    atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
-#pragma unroll
-  for (int a = 0; a < kActBranches; ++a) {
-    const bool zero = mx[a] == 0 || nonfinite;
-    const int emax = zero ? kZeroGroup : effective_exponent(static_cast<uint16_t>(mx[a]));
-    const bool fast = static_cast<int>(mx[a] >> 7) >= 8;
-    const int shift = 127 - emax;
-    uint32_t lo = 0, hi = 0;
-    if (!zero) {
-      if (fast) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          lo |= static_cast<uint32_t>(static_cast<uint8_t>(fast_align(bits[a][e], emax))) << (8 * e);
-          hi |= static_cast<uint32_t>(static_cast<uint8_t>(fast_align(bits[a][e + 4], emax)))
-                << (8 * e);
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          lo |= slow_align(bits[a][e], shift) << (8 * e);
-          hi |= slow_align(bits[a][e + 4], shift) << (8 * e);
+    for (int e = 0; e < 8; ++e) {
+      rel[e] = c * g.sC + i * g.sH + j * g.sW;
+      di[e] = i;
+      dj[e] = j;
+      if (++j == g.KW) {
+        j = 0;
+        if (++i == g.KH) {
+          i = 0;
+          ++c;
         }
       }
     }
-    *reinterpret_cast<uint2 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) =
-        make_uint2(lo, hi);
-    if (sub == 0)
-      ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax;
+  }
+  for (int r = 0; r < cols; ++r) {
+    const int m = (chunk * cols + r) * 32 + grp;
+    if (m >= m_pad)
+      break; // uniform per 8-lane subgroup
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      v[e] = 0.0f;
+    if (m < g.M && kvalid) {
+      if (kMode == kPrepRows) {
+        const float *row = x + static_cast<int64_t>(m) * g.K;
+        if (g.pair_rows == 2 && kvalid == 0xffu) {
+          const float4 *src = reinterpret_cast<const float4 *>(row + kbeg);
+          const float4 lo = __ldg(src), hi = __ldg(src + 1);
+          v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
+          v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if ((kvalid >> e) & 1u)
+              v[e] = __ldg(row + kbeg + e);
+        }
+      } else {
+        const int n = fdiv(m, g.div_ohw);
+        const int rm = m - n * g.OH * g.OW;
+        const int oh = fdiv(rm, g.div_ow);
+        const int ow = rm - oh * g.OW;
+        const int ih0 = oh * g.SH - g.PH, iw0 = ow * g.SW - g.PW;
+        const float *img = x + static_cast<int64_t>(n) * g.image;
+        const int org = ih0 * g.sH + iw0 * g.sW;
+        if (kvalid == 0xffu && ih0 >= 0 && iw0 >= 0 && ih0 + g.KH <= g.H &&
+            iw0 + g.KW <= g.W) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            v[e] = window_load<kMode>(img, g, org + rel[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (((kvalid >> e) & 1u) &&
+                static_cast<unsigned>(ih0 + di[e]) < static_cast<unsigned>(g.H) &&
+                static_cast<unsigned>(iw0 + dj[e]) < static_cast<unsigned>(g.W))
+              v[e] = window_load<kMode>(img, g, org + rel[e]);
+        }
+      }
+    }
+    // Split and round: xp = max(x, 0), xn = max(-x, 0) equal the reference's
+    // selects for every non-NaN x up to the sign of zero, which the
+    // preparation clears anyway (BF16Compensation.cpp:97). cvt.rn.bf16x2.f32
+    // rounds to nearest even, as arith.truncf does. NaN, infinity and finite
+    // values that round to BF16 infinity (|x| >= 0x1.fep127) mark the group
+    // non-finite: through the BF16 exponent 0xff of the maximum for a
+    // 2-branch layer, through |x| of the raw inputs otherwise (the max with 0
+    // drops NaN).
+    uint32_t packed[2][4];
+    uint32_t mx[2] = {0, 0};
+    bool negative = false;
+    if (kActBranches == 2) {
+      uint32_t amax = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        amax = max(amax, __float_as_uint(v[e]) & 0x7fffffffu);
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const __nv_bfloat162 hp =
+            __floats2bfloat162_rn(fmaxf(v[e], 0.0f), fmaxf(v[e + 1], 0.0f));
+        const __nv_bfloat162 hn =
+            __floats2bfloat162_rn(fmaxf(-v[e], 0.0f), fmaxf(-v[e + 1], 0.0f));
+        packed[0][e / 2] = *reinterpret_cast<const uint32_t *>(&hp) & 0x7fff7fffu;
+        packed[1][e / 2] = *reinterpret_cast<const uint32_t *>(&hn) & 0x7fff7fffu;
+      }
+#pragma unroll
+      for (int a = 0; a < 2; ++a) {
+        const uint32_t m2 = __vmaxu2(__vmaxu2(packed[a][0], packed[a][1]),
+                                     __vmaxu2(packed[a][2], packed[a][3]));
+        mx[a] = max(m2 & 0xffffu, m2 >> 16);
+      }
+      if (amax >= 0x7f7f8000u)
+        mx[0] = 0xffffu;
+    } else {
+      uint32_t umax = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        umax = max(umax, __float_as_uint(v[e]));
+      negative = umax > 0x80000000u;
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const __nv_bfloat162 hp = __floats2bfloat162_rn(v[e], v[e + 1]);
+        packed[0][e / 2] = *reinterpret_cast<const uint32_t *>(&hp) & 0x7fff7fffu;
+      }
+      const uint32_t m2 = __vmaxu2(__vmaxu2(packed[0][0], packed[0][1]),
+                                   __vmaxu2(packed[0][2], packed[0][3]));
+      mx[0] = max(m2 & 0xffffu, m2 >> 16);
+    }
+#pragma unroll
+    for (int a = 0; a < kActBranches; ++a)
+#pragma unroll
+      for (int o = 4; o; o >>= 1)
+        mx[a] = max(mx[a], __shfl_xor_sync(mask, mx[a], o, kGroupThreads));
+    const bool nonfinite = mx[0] >= 0x7f80u;
+    if (sub == 0 && nonfinite)
+      atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
+    if (negative && !nonfinite)
+      atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
+#pragma unroll
+    for (int a = 0; a < kActBranches; ++a) {
+      const bool zero = mx[a] == 0 || nonfinite;
+      const int emax = zero ? kZeroGroup : effective_exponent(static_cast<uint16_t>(mx[a]));
+      uint32_t lo = 0, hi = 0;
+      if (!zero) {
+        if ((mx[a] >> 7) >= 8) {
+          const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax) << 23);
+          uint32_t q[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            q[2 * e] = __float_as_uint(
+                __fmaf_rz(__uint_as_float(packed[a][e] << 16), scale, 8388608.0f));
+            q[2 * e + 1] = __float_as_uint(
+                __fmaf_rz(__uint_as_float(packed[a][e] & 0xffff0000u), scale, 8388608.0f));
+          }
+          lo = pack_low_bytes(q[0], q[1], q[2], q[3]);
+          hi = pack_low_bytes(q[4], q[5], q[6], q[7]);
+        } else {
+          const int shift = 127 - emax;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            lo |= slow_align((packed[a][e / 2] >> (16 * (e & 1))) & 0xffffu, shift) << (8 * e);
+            hi |= slow_align((packed[a][2 + e / 2] >> (16 * (e & 1))) & 0xffffu, shift)
+                  << (8 * e);
+          }
+        }
+      }
+      *reinterpret_cast<uint2 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) =
+          make_uint2(lo, hi);
+      if (sub == 0)
+        ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax;
+    }
   }
 }
 
@@ -660,7 +668,17 @@ bool check_gather(const cim22_gather &g, int64_t m, int64_t k) {
   const int64_t image = static_cast<int64_t>(g.channels) *
                         (g.pool_kernel > 0 ? static_cast<int64_t>(g.pool_src_h) * g.pool_src_w
                                            : static_cast<int64_t>(g.height) * g.width);
-  if (image >= (int64_t{1} << 31))
+  // The prepare kernel forms element offsets within an image, window
+  // origins included, in 32-bit arithmetic: bound every term.
+  const int64_t ps = g.pool_kernel > 0 ? g.pool_stride : 1;
+  const int64_t reach =
+      (static_cast<int64_t>(g.height) + g.pad_h + g.kernel_h) * ps *
+          (g.pool_kernel > 0 ? g.pool_src_w : g.width) * g.channels +
+      (static_cast<int64_t>(g.width) + g.pad_w + g.kernel_w) * ps * g.channels +
+      static_cast<int64_t>(g.channels + 1) *
+          (g.kind == CIM22_GATHER_CONV_NCHW ? static_cast<int64_t>(g.height) * g.width : 1) +
+      static_cast<int64_t>(g.pool_kernel) * (g.pool_src_w + 1) * g.channels;
+  if (image >= (int64_t{1} << 30) || reach >= (int64_t{1} << 30))
     return false;
   const int oh = (g.height + 2 * g.pad_h - g.kernel_h) / g.stride_h + 1;
   const int ow = (g.width + 2 * g.pad_w - g.kernel_w) / g.stride_w + 1;
@@ -689,9 +707,25 @@ Gather32 to_device_gather(const cim22_gather &g, int64_t m, int64_t k, const flo
     d.OH = g.out_h;
     d.OW = g.out_w;
     d.PK = g.pool_kernel;
-    d.PS = g.pool_stride;
-    d.SRC_H = g.pool_src_h;
-    d.SRC_W = g.pool_src_w;
+    if (g.kind == CIM22_GATHER_CONV_NCHW) {
+      d.sC = g.height * g.width;
+      d.sH = g.width;
+      d.sW = 1;
+      d.image = g.channels * g.height * g.width;
+    } else if (g.pool_kernel == 0) {
+      d.sC = 1;
+      d.sH = g.width * g.channels;
+      d.sW = g.channels;
+      d.image = g.channels * g.height * g.width;
+    } else {
+      // Pooled (ih, iw) starts at pre-pool (ih * PS, iw * PS).
+      d.sC = 1;
+      d.sH = g.pool_stride * g.pool_src_w * g.channels;
+      d.sW = g.pool_stride * g.channels;
+      d.pdy = g.pool_src_w * g.channels;
+      d.pdx = g.channels;
+      d.image = g.channels * g.pool_src_h * g.pool_src_w;
+    }
     d.div_ohw = make_fastdiv(static_cast<uint32_t>(g.out_h * g.out_w));
     d.div_ow = make_fastdiv(static_cast<uint32_t>(g.out_w));
     d.div_khw = make_fastdiv(static_cast<uint32_t>(g.kernel_h * g.kernel_w));
@@ -708,7 +742,7 @@ static void prepare_bf16_weights(const float *w, int64_t n, int64_t k,
                                  std::vector<int8_t> &mant,
                                  std::vector<int32_t> &exps) {
   mant.assign(2 * n_pad * k_pad, 0);
-  exps.assign(2 * T * n_pad, 127);
+  exps.assign(2 * T * n_pad + (n_pad / 32) * T * 4 + 2 * T * n_pad, 127);
   uint16_t group[kTileK];
   for (int b = 0; b < 2; ++b)
     for (int64_t lane = 0; lane < n; ++lane)
@@ -739,6 +773,30 @@ static void prepare_bf16_weights(const float *w, int64_t n, int64_t k,
         // (slow) restore path.
         exps[(b * T + t) * n_pad + lane] = any ? exp_max : 127;
       }
+  // Per 32-lane block and tile: the range of the weight exponents of both
+  // signs, which decides the tensor-core epilogue's exact-FMA window.
+  int32_t *ranges = exps.data() + 2 * T * n_pad;
+  for (int64_t nb = 0; nb < n_pad / 32; ++nb)
+    for (int64_t t = 0; t < T; ++t) {
+      int lo = 1 << 30, hi = -(1 << 30);
+      for (int b = 0; b < 2; ++b)
+        for (int64_t lane = nb * 32; lane < nb * 32 + 32; ++lane) {
+          const int e = exps[(b * T + t) * n_pad + lane];
+          lo = std::min(lo, e);
+          hi = std::max(hi, e);
+        }
+      int32_t *r = ranges + (nb * T + t) * 4;
+      r[0] = lo;
+      r[1] = hi;
+      r[2] = r[3] = 0;
+    }
+  // The weight scales 2^(Ew - 133) as f32 bit patterns (exact: Ew - 133 lies
+  // in [-133, 121], inside f32's normal and subnormal range).
+  int32_t *scales = ranges + (n_pad / 32) * T * 4;
+  for (int64_t i = 0; i < 2 * T * n_pad; ++i) {
+    const float f = std::ldexp(1.0f, exps[i] - 133);
+    std::memcpy(&scales[i], &f, 4);
+  }
 }
 
 static bool int8_range_proof(const int8_t *w, int64_t n, int64_t k) {
@@ -898,14 +956,29 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
   int32_t *ex = reinterpret_cast<int32_t *>(
       static_cast<char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
   const Gather32 dg = to_device_gather(g, m, layer->k, x);
-  const unsigned blocks = static_cast<unsigned>((m_pad * T * kGroupThreads + 255) / 256);
-  const FastDiv div_t = make_fastdiv(static_cast<uint32_t>(T));
+  // Columns per group thread: as many as still give four waves of 256-thread
+  // blocks on a B200 (148 SMs, four resident blocks each).
+  int cols = 4;
+  while (cols > 1 && ((m_pad + 32 * cols - 1) / (32 * cols)) * T < 148 * 4 * 4)
+    cols /= 2;
+  const int64_t chunks = (m_pad + 32 * cols - 1) / (32 * cols);
+  const unsigned blocks = static_cast<unsigned>(chunks * T);
+  const FastDiv div_chunks = make_fastdiv(static_cast<uint32_t>(chunks));
+  const int mode = g.kind == CIM22_GATHER_ROWS ? kPrepRows
+                   : g.pool_kernel > 0         ? kPrepConvPool
+                                               : kPrepConv;
+  auto launch = [&](auto kernel) {
+    kernel<<<blocks, 256, 0, s>>>(x, dg, div_chunks, T, cols, static_cast<int>(m_pad),
+                                  static_cast<int>(layer->k_pad), A, ex, status);
+  };
   if (ab == 1)
-    prepare_kernel<1><<<blocks, 256, 0, s>>>(x, dg, div_t, static_cast<int>(m_pad),
-                                             static_cast<int>(layer->k_pad), A, ex, status);
+    launch(mode == kPrepRows   ? prepare_kernel<1, kPrepRows>
+           : mode == kPrepConv ? prepare_kernel<1, kPrepConv>
+                               : prepare_kernel<1, kPrepConvPool>);
   else
-    prepare_kernel<2><<<blocks, 256, 0, s>>>(x, dg, div_t, static_cast<int>(m_pad),
-                                             static_cast<int>(layer->k_pad), A, ex, status);
+    launch(mode == kPrepRows   ? prepare_kernel<2, kPrepRows>
+           : mode == kPrepConv ? prepare_kernel<2, kPrepConv>
+                               : prepare_kernel<2, kPrepConvPool>);
   return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
 }
 

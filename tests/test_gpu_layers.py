@@ -99,6 +99,45 @@ def test_conv_bf16_bit_exact(layout, c, h, f, kk, stride, pad):
     np.testing.assert_array_equal(bits(got), bits(expected))
 
 
+@pytest.mark.parametrize("layout,n,c,h,f,kk,stride,pad,branches,pool", [
+    ("nhwc", 64, 16, 32, 64, 3, 1, 1, 4, 0),   # several columns per prepare thread
+    ("nhwc", 64, 16, 32, 64, 3, 1, 1, 2, 0),
+    ("nchw", 48, 3, 40, 32, 5, 2, 2, 4, 0),    # K = 75: ragged K tail inside a thread
+    ("nhwc", 32, 8, 34, 48, 3, 2, 0, 2, 0),
+    ("nhwc", 64, 32, 16, 32, 3, 1, 1, 4, 2)])  # fused 2x2 max pool over 32x32
+def test_conv_bf16_large_batch_bit_exact(layout, n, c, h, f, kk, stride, pad, branches, pool):
+    """Batches large enough that each prepare thread serves several columns
+    and the tensor-core contraction runs, for both layouts, both branch
+    counts, ragged K and a fused max pool."""
+    from cim22_b200 import abi
+    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace, conv_gather
+
+    rng = np.random.default_rng(n * 7 + c + h + f + pool)
+    src = h * 2 if pool else h
+    x = rng.standard_normal((n, c, src, src)).astype(np.float32)
+    if branches == 2:
+        x = np.maximum(x, 0)
+    x[rng.random(x.shape) < 0.2] = 0
+    pooled = x.reshape(n, c, h, 2, h, 2).max(axis=(3, 5)) if pool else x
+    w = (rng.standard_normal((f, c, kk, kk)) * 0.2).astype(np.float32)
+    b = rng.standard_normal(f).astype(np.float32)
+    expected = oracle.conv2d_bf16(pooled, w, b, stride, pad, branches=4, threads=8)
+    layer = CimLayer(w.reshape(f, -1))
+    kind = abi.GATHER_CONV_NCHW if layout == "nchw" else abi.GATHER_CONV_NHWC
+    g = conv_gather(kind, n, c, h, h, kk, kk, stride, pad)
+    if pool:
+        g.pool_kernel, g.pool_stride, g.pool_src_h, g.pool_src_w = 2, 2, src, src
+    xt = torch.from_numpy(x if layout == "nchw" else x.transpose(0, 2, 3, 1).copy()).to(DEV)
+    m = n * g.out_h * g.out_w
+    out = torch.empty(m, f, device=DEV)
+    status = StatusWord(torch.device(DEV))
+    layer.forward_bf16(xt, out, m, gather=g, bias=torch.from_numpy(b).to(DEV),
+                       branches=branches, workspace=Workspace(torch.device(DEV)), status=status)
+    status.raise_if_set()
+    got = out.cpu().numpy().reshape(n, g.out_h, g.out_w, f).transpose(0, 3, 1, 2)
+    np.testing.assert_array_equal(bits(got), bits(expected))
+
+
 @pytest.mark.parametrize("m,k,n", [(2, 65, 17), (2, 128, 17), (33, 1000, 70), (300, 64, 16)])
 def test_linear_int8_exact(m, k, n):
     from cim22_b200.cim_ops import CimLayer
@@ -223,14 +262,27 @@ def test_linear_int8_tensor_core_shapes(m, k, n):
 
 @pytest.mark.parametrize("m,k,n,branches,scale", [
     (1024, 4096, 512, 4, 1.0), (2000, 150, 40, 2, 1.0), (777, 640, 96, 4, 1.0),
-    (600, 200, 64, 4, 1e-30), (512, 64, 32, 4, 1e18)])
+    (600, 200, 64, 4, 1e-30), (512, 64, 32, 4, 1e18),
+    # one crossbar tile, hundreds of output tiles per persistent CTA
+    (40000, 18, 64, 4, 1.0), (30000, 27, 32, 2, 1.0),
+    # odd tile count, several output tiles per CTA
+    (5000, 300, 160, 4, 1.0),
+    # per-row scales from 1e-38 to 1e30: fast and exact-path rows share a
+    # CTA, and whole rows of zero groups
+    (3000, 256, 96, 4, "rows"), (2048, 130, 64, 2, "rows")])
 def test_linear_bf16_tensor_core_bit_exact(m, k, n, branches, scale):
     """Wide layers run the tcgen05 sign-split kernel (launch counter checked)."""
     from cim22_b200.cim_ops import CimLayer
     from cim22_b200.native import lib
 
     rng = np.random.default_rng(m + k + n)
-    x = (rng.standard_normal((m, k)) * scale).astype(np.float32)
+    if scale == "rows":
+        x = rng.standard_normal((m, k)).astype(np.float64)
+        x *= 10.0 ** rng.uniform(-38, 30, (m, 1))
+        x[rng.random(m) < 0.1] = 0
+        x = x.astype(np.float32)
+    else:
+        x = (rng.standard_normal((m, k)) * scale).astype(np.float32)
     x[rng.random((m, k)) < 0.01] *= 20
     if branches == 2:
         x = np.maximum(x, 0)
