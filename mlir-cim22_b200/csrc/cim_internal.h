@@ -44,8 +44,8 @@ struct cim22_cuda_layer {
   int64_t tiles = 0;            // K tiles (k_pad / 64)
   bool range_safe = true;       // INT8 range proof result
   // BF16: int8 mantissas [2][n_pad][k_pad] (Wp then Wn) and int32 lane
-  // exponents [2][tiles][n_pad], the per-32-lane-block, per-tile
-  // weight-exponent ranges [n_pad / 32][tiles][4] and the f32 weight scales
+  // exponents [2][tiles][n_pad], the per-tile, per-32-lane-block
+  // weight-exponent ranges [tiles][n_pad / 32][4] and the f32 weight scales
   // 2^(Ew - 133) [2][tiles][n_pad]. INT8: int8 [n_pad][k_pad].
   int8_t *weights = nullptr;
   int32_t *exponents = nullptr;

@@ -237,22 +237,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------------------
 // BF16 sign-split contraction. Per 64-K crossbar tile t the two MMAs of each
-// activation branch (xp, xn) produce 128 columns x 64 lanes of int32 dots in
-// TMEM: one N=64 MMA covers both weight branches (Wp rows, then Wn rows).
-// The kernel is persistent: each CTA walks output tiles (128 columns x 32
-// lanes) blockIdx.x, blockIdx.x + gridDim.x, ... and every crossbar tile of
-// every output tile flows through the same three rings:
+// activation branch (xp, xn) produce 128 columns x 2L lanes of int32 dots in
+// TMEM: one N=2L MMA covers both weight branches (L Wp rows, then L Wn rows).
+// L = 32 lanes for 4-branch layers and 64 for 2-branch layers, so a TMEM
+// buffer is 128 columns wide and every epilogue thread restores 32 dots per
+// crossbar tile in both cases. The kernel is persistent: each CTA walks the
+// output tiles (128 columns x L lanes) blockIdx.x, blockIdx.x + gridDim.x, ...
+// and every crossbar tile of every output tile flows through three rings:
 //
 //   warp 0 (one thread)   TMA producer: per K-block of 128 bytes (two
 //                          crossbar tiles) the activation tile of each branch
 //                          and the stacked Wp/Wn tile into a 4-stage ring;
 //                          per crossbar tile the activation exponents of the
-//                          128 columns, the 2 x 32 weight exponents and the
-//                          tile's weight-exponent range into a 16-slot ring
+//                          128 columns, the 2 x L weight scales and the tile's
+//                          weight-exponent range into a 16-slot ring
 //                          (cp.async.bulk, no multicast)
 //   warp 1 (one thread)   tcgen05.mma kind::i8 into one of 4 TMEM buffers
 //   warps 2-17            epilogue: warp w reads TMEM lanes 32 * (w % 4) and
-//                          8 of the 32 lanes; it restores each dot as
+//                          L / 4 of the L lanes; it restores each dot as
 //                          RNE_bf16(Q(p) * 2^(Ew + Ex - 266)) and adds it to
 //                          its f32 branch sum in tile order, then rounds,
 //                          merges ((pp - pn) - np) + nn, adds the bias and
@@ -265,20 +267,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 // is the exactly representable tile value, so one FMA adds it with the single
 // rounding of the reference's f32 add. Outside the window the integer path
 // (signsplit_tile) restores the tile.
-constexpr int kSBM = 128, kSBL = 32, kSN = 2 * kSBL, kSBK = 128, kSStages = 4;
+constexpr int kSBM = 128, kSBK = 128, kSStages = 4;
 constexpr int kEpiWarps = 16;
 constexpr int kSThreads = 64 + 32 * kEpiWarps;
 constexpr int kExpSlots = 16, kTmemBufs = 4;
+constexpr uint32_t kBufCols = 128;
+
+template <int kAB> struct SSShape {
+  static constexpr int L = kAB == 1 ? 64 : 32; // lanes per output tile
+  static constexpr int LT = L / 4;             // lanes per epilogue thread
+  static constexpr int N = 2 * L;              // MMA N: Wp and Wn rows
+};
 
 struct alignas(16) ExpSlot {
-  int32_t a[2][kSBM];  // activation group exponents per branch
-  float w[2][kSBL];    // weight scales 2^(Ew - 133), Wp then Wn
-  int32_t range[4];    // min and max weight exponent of the tile, 2 pad words
+  int32_t a[2][kSBM]; // activation group exponents per branch
+  float w[2][64];     // weight scales 2^(Ew - 133), Wp then Wn
+  int32_t range[8];   // {min, max, 0, 0} weight exponent per 32-lane block
 };
 
 template <int kAB> struct alignas(1024) SmemSS {
   int8_t a[kSStages][kAB][kSBM * kSBK];
-  int8_t b[kSStages][kSN * kSBK];
+  int8_t b[kSStages][SSShape<kAB>::N * kSBK];
   ExpSlot ex[kExpSlots];
   uint64_t full[kSStages];
   uint64_t empty[kSStages];
@@ -302,20 +311,37 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
                : "memory");
 }
 
-// Issue a 32x32b.x8 TMEM load; the values are valid after tmem_wait8.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+// Issue a 32x32b TMEM load of 8 or 16 columns; the values are valid after
+// tmem_wait.
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
                  "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, "
+               "%9, %10, %11, %12, %13, %14, %15}, [%16];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                 "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+               : "r"(taddr));
+}
+
 // Wait for the outstanding TMEM loads. The registers are in/out operands so
 // no use of them is scheduled before the wait.
-__device__ __forceinline__ void tmem_wait8(uint32_t (&r)[8]) {
+__device__ __forceinline__ void tmem_wait(uint32_t (&r)[8]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
                : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
                  "+r"(r[6]), "+r"(r[7])::"memory");
+}
+
+__device__ __forceinline__ void tmem_wait(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])::"memory");
 }
 
 // Exact restore of one tile value outside the fast window (out of line).
@@ -335,23 +361,52 @@ __device__ __forceinline__ float act_tc(float v, int act) {
   return v;
 }
 
+// Add the restored dots of one (activation branch, weight branch) pair of a
+// crossbar tile to the branch sums: the exact three-operation form inside
+// the window (scales read from the exponent slot four at a time), the
+// integer path otherwise.
+template <int kLT>
+__device__ __forceinline__ void restore_add(float (&acc)[kLT], const uint32_t (&p)[kLT],
+                                            bool fast, float sx, float nsx,
+                                            const float *__restrict__ sw,
+                                            const int32_t *__restrict__ ew, int ex,
+                                            int32_t *status) {
+  if (fast) {
+#pragma unroll
+    for (int j4 = 0; j4 < kLT; j4 += 4) {
+      const float4 s4 = *reinterpret_cast<const float4 *>(sw + j4);
+      const float s[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float v = __fmaf_rn(__uint_as_float(p[j4 + j] | 0x4b000000u), sx, nsx);
+        acc[j4 + j] =
+            __fmaf_rn(__uint_as_float(__float_as_uint(v) & 0xffff0000u), s[j], acc[j4 + j]);
+      }
+    }
+  } else {
+    for (int j = 0; j < kLT; ++j)
+      acc[j] = tc_slow_tile_add(acc[j], static_cast<int>(p[j]), ew[j], ex, status);
+  }
+}
+
 template <int kAB>
 __global__ void __launch_bounds__(kSThreads, 1)
     signsplit_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const int32_t *__restrict__ exA,
                         int m_pad, const int32_t *__restrict__ exB, int n_pad, int T, int M,
-                        int N, const float *__restrict__ bias, int act, float *__restrict__ y,
-                        int32_t *status) {
+                        int N, const float *__restrict__ bias, int act, int vec,
+                        float *__restrict__ y, int32_t *status) {
+  using S = SSShape<kAB>;
+  constexpr int L = S::L, LT = S::LT, SN = S::N;
   extern __shared__ uint8_t smem_raw[];
   SmemSS<kAB> &s = *reinterpret_cast<SmemSS<kAB> *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int num_kb = (T + 1) / 2;
-  const int num_nb = (N + kSBL - 1) / kSBL;
+  const int num_nb = (N + L - 1) / L;
   const int num_tiles = ((M + kSBM - 1) / kSBM) * num_nb;
-  const int32_t *ranges = exB + int64_t{2} * T * n_pad; // [n_pad / 32][T][4]
-  const int32_t *scales = ranges + int64_t{n_pad / 32} * T * 4; // f32 [2][T][n_pad]
-  constexpr uint32_t kBufCols = kAB * kSN;
+  const int32_t *ranges = exB + int64_t{2} * T * n_pad; // [T][n_pad / 32][4]
+  const float *scales = reinterpret_cast<const float *>(ranges + int64_t{n_pad / 32} * T * 4);
   constexpr uint32_t kTmemCols = kTmemBufs * kBufCols;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSStages; ++i) {
@@ -385,19 +440,19 @@ __global__ void __launch_bounds__(kSThreads, 1)
     uint32_t kbi = 0, gi = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
-      const int m0 = (ot / num_nb) * kSBM, nb = ot % num_nb, n0 = nb * kSBL;
+      const int m0 = (ot / num_nb) * kSBM, n0 = (ot % num_nb) * L;
       for (int kb = 0; kb < num_kb; ++kb, ++kbi) {
         const int stage = kbi % kSStages;
         if (!mbar_wait(&s.empty[stage], ((kbi / kSStages) & 1) ^ 1) || *failed) {
           ok = false;
           break;
         }
-        mbar_expect_tx(&s.full[stage], kAB * kSBM * kSBK + kSN * kSBK);
+        mbar_expect_tx(&s.full[stage], kAB * kSBM * kSBK + SN * kSBK);
 #pragma unroll
         for (int a = 0; a < kAB; ++a)
           tma_load_2d(s.a[stage][a], &tmA, &s.full[stage], kb * kSBK, a * m_pad + m0);
         tma_load_2d(s.b[stage], &tmB, &s.full[stage], kb * kSBK, n0);
-        tma_load_2d(s.b[stage] + kSBL * kSBK, &tmB, &s.full[stage], kb * kSBK, n_pad + n0);
+        tma_load_2d(s.b[stage] + L * kSBK, &tmB, &s.full[stage], kb * kSBK, n_pad + n0);
         for (int t = 2 * kb; t < 2 * kb + 2 && t < T; ++t, ++gi) {
           const int slot = gi % kExpSlots;
           if (!mbar_wait(&s.exempty[slot], ((gi / kExpSlots) & 1) ^ 1) || *failed) {
@@ -405,17 +460,17 @@ __global__ void __launch_bounds__(kSThreads, 1)
             break;
           }
           ExpSlot &e = s.ex[slot];
-          mbar_expect_tx(&s.exfull[slot], kAB * kSBM * 4 + 2 * kSBL * 4 + 16);
+          mbar_expect_tx(&s.exfull[slot], kAB * kSBM * 4 + 2 * L * 4 + (L / 32) * 16);
 #pragma unroll
           for (int a = 0; a < kAB; ++a)
             bulk_load(e.a[a], exA + (static_cast<int64_t>(a) * T + t) * m_pad + m0, kSBM * 4,
                       &s.exfull[slot]);
 #pragma unroll
           for (int w = 0; w < 2; ++w)
-            bulk_load(e.w[w], scales + (static_cast<int64_t>(w) * T + t) * n_pad + n0, kSBL * 4,
+            bulk_load(e.w[w], scales + (static_cast<int64_t>(w) * T + t) * n_pad + n0, L * 4,
                       &s.exfull[slot]);
-          bulk_load(e.range, ranges + (static_cast<int64_t>(nb) * T + t) * 4, 16,
-                    &s.exfull[slot]);
+          bulk_load(e.range, ranges + (static_cast<int64_t>(t) * (n_pad / 32) + n0 / 32) * 4,
+                    (L / 32) * 16, &s.exfull[slot]);
         }
         if (!ok) {
           ++kbi;
@@ -433,7 +488,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
       mbar_wait(&s.exfull[i % kExpSlots], (i / kExpSlots) & 1);
   } else if (warp == 1 && lane == 0) {
     // MMA issuer: two K=32 MMAs per branch per crossbar tile.
-    constexpr uint32_t idesc = idesc_i8(kSBM, kSN);
+    constexpr uint32_t idesc = idesc_i8(kSBM, SN);
     uint32_t kbi = 0, gi = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
@@ -449,7 +504,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
 #pragma unroll
         for (int a = 0; a < kAB; ++a) {
           const uint64_t adesc = sw128_desc(s.a[stage][a]) + half * 4;
-          const uint32_t d = tmem + buf * kBufCols + a * kSN;
+          const uint32_t d = tmem + buf * kBufCols + a * SN;
           mma_i8(d, adesc, bdesc, idesc, 0u);
           mma_i8(d, adesc + 2, bdesc + 2, idesc, 1u);
         }
@@ -473,15 +528,15 @@ __global__ void __launch_bounds__(kSThreads, 1)
     uint32_t gi = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
-      const int m0 = (ot / num_nb) * kSBM, n0 = (ot % num_nb) * kSBL;
-      const int lane0 = n0 + sub * 8;
-      float acc[kAB][2][8];
+      const int m0 = (ot / num_nb) * kSBM, n0 = (ot % num_nb) * L;
+      const int lane0 = n0 + sub * LT;
+      float acc[kAB][2][LT];
 #pragma unroll
       for (int a = 0; a < kAB; ++a)
 #pragma unroll
         for (int w = 0; w < 2; ++w)
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
+          for (int j = 0; j < LT; ++j)
             acc[a][w][j] = 0.0f;
       for (int t = 0; t < T; ++t, ++gi) {
         const int slot = gi % kExpSlots, buf = gi % kTmemBufs;
@@ -490,7 +545,11 @@ __global__ void __launch_bounds__(kSThreads, 1)
           break;
         }
         const ExpSlot &e = s.ex[slot];
-        const int2 range = *reinterpret_cast<const int2 *>(e.range);
+        int lo = e.range[0], hi = e.range[1];
+        if (L == 64) {
+          lo = min(lo, e.range[4]);
+          hi = max(hi, e.range[5]);
+        }
         float sx[kAB], nsx[kAB];
         bool fast[kAB];
         int ex[kAB];
@@ -498,33 +557,27 @@ __global__ void __launch_bounds__(kSThreads, 1)
         for (int a = 0; a < kAB; ++a) {
           ex[a] = e.a[a][row_local];
           const bool zero = ex[a] == kZeroGroup;
-          fast[a] = zero || (ex[a] >= 7 && ex[a] <= 237 && ex[a] + range.x >= 140 &&
-                             ex[a] + range.y <= 374);
+          fast[a] = zero ||
+                    (ex[a] >= 7 && ex[a] <= 237 && ex[a] + lo >= 140 && ex[a] + hi <= 374);
           sx[a] = zero || !fast[a] ? 0.0f : exp2i(ex[a] - 133);
           nsx[a] = -8388608.0f * sx[a];
-        }
-        float sw[2][8];
-#pragma unroll
-        for (int w = 0; w < 2; ++w) {
-          const float4 e0 = *reinterpret_cast<const float4 *>(&e.w[w][sub * 8]);
-          const float4 e1 = *reinterpret_cast<const float4 *>(&e.w[w][sub * 8 + 4]);
-          sw[w][0] = e0.x; sw[w][1] = e0.y; sw[w][2] = e0.z; sw[w][3] = e0.w;
-          sw[w][4] = e1.x; sw[w][5] = e1.y; sw[w][6] = e1.z; sw[w][7] = e1.w;
         }
         if (!mbar_wait(&s.dfull[buf], (gi / kTmemBufs) & 1) || *failed) {
           ok = false;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        // One activation branch at a time keeps 16 dots in registers.
+        const uint32_t col0 = tmem + tlane + buf * kBufCols + sub * LT;
+        const int32_t *ew0 = exB + static_cast<int64_t>(t) * n_pad + lane0;
+        const int32_t *ew1 = exB + (static_cast<int64_t>(T) + t) * n_pad + lane0;
+        // One activation branch at a time: 2 x LT dots in registers.
 #pragma unroll
         for (int a = 0; a < kAB; ++a) {
-          uint32_t p[2][8];
-#pragma unroll
-          for (int w = 0; w < 2; ++w)
-            tmem_ld8(tmem + tlane + buf * kBufCols + a * kSN + w * kSBL + sub * 8, p[w]);
-          tmem_wait8(p[0]);
-          tmem_wait8(p[1]);
+          uint32_t p0[LT], p1[LT];
+          tmem_ld(col0 + a * SN, p0);
+          tmem_ld(col0 + a * SN + L, p1);
+          tmem_wait(p0);
+          tmem_wait(p1);
           if (a == kAB - 1) {
             // The dots are in registers: hand the TMEM buffer back.
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -532,23 +585,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
             if (lane == 0)
               mbar_arrive(&s.dempty[buf]);
           }
-          if (fast[a]) {
-#pragma unroll
-            for (int w = 0; w < 2; ++w)
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float v =
-                    __fmaf_rn(__uint_as_float(p[w][j] | 0x4b000000u), sx[a], nsx[a]);
-                acc[a][w][j] = __fmaf_rn(__uint_as_float(__float_as_uint(v) & 0xffff0000u),
-                                         sw[w][j], acc[a][w][j]);
-              }
-          } else {
-            for (int w = 0; w < 2; ++w)
-              for (int j = 0; j < 8; ++j)
-                acc[a][w][j] = tc_slow_tile_add(
-                    acc[a][w][j], static_cast<int>(p[w][j]),
-                    exB[(static_cast<int64_t>(w) * T + t) * n_pad + lane0 + j], ex[a], status);
-          }
+          restore_add<LT>(acc[a][0], p0, fast[a], sx[a], nsx[a], &e.w[0][sub * LT], ew0, ex[a],
+                          status);
+          restore_add<LT>(acc[a][1], p1, fast[a], sx[a], nsx[a], &e.w[1][sub * LT], ew1, ex[a],
+                          status);
         }
         __syncwarp();
         if (lane == 0)
@@ -558,28 +598,51 @@ __global__ void __launch_bounds__(kSThreads, 1)
         break;
       const int row = m0 + row_local;
       if (row < M) {
+        float *dst = y + static_cast<int64_t>(row) * N + lane0;
+        const bool full = vec && lane0 + LT <= N;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int col = lane0 + j;
-          if (col >= N)
-            break;
-          // Branch sums are finite or infinite, never NaN: the hardware
-          // RNE conversion rounds them as the reference's truncf does.
-          float br[kAB][2];
+        for (int j4 = 0; j4 < LT; j4 += 4) {
+          float b4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          if (bias != nullptr) {
+            if (full) {
+              const float4 v = __ldg(reinterpret_cast<const float4 *>(bias + lane0 + j4));
+              b4[0] = v.x; b4[1] = v.y; b4[2] = v.z; b4[3] = v.w;
+            } else {
 #pragma unroll
-          for (int a = 0; a < kAB; ++a)
-#pragma unroll
-            for (int w = 0; w < 2; ++w)
-              br[a][w] = T > 1 ? __bfloat162float(__float2bfloat16_rn(acc[a][w][j]))
-                               : acc[a][w][j];
-          float out = __fsub_rn(br[0][0], br[0][1]);
-          if (kAB == 2) {
-            out = __fsub_rn(out, br[1][0]);
-            out = __fadd_rn(out, br[1][1]);
+              for (int j = 0; j < 4; ++j)
+                if (lane0 + j4 + j < N)
+                  b4[j] = __ldg(bias + lane0 + j4 + j);
+            }
           }
-          if (bias != nullptr)
-            out = __fadd_rn(out, bias[col]);
-          y[static_cast<int64_t>(row) * N + col] = act_tc(out, act);
+          float o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            // Branch sums are finite or infinite, never NaN: the hardware
+            // RNE conversion rounds them as the reference's truncf does.
+            float br[kAB][2];
+#pragma unroll
+            for (int a = 0; a < kAB; ++a)
+#pragma unroll
+              for (int w = 0; w < 2; ++w)
+                br[a][w] = T > 1 ? __bfloat162float(__float2bfloat16_rn(acc[a][w][j4 + j]))
+                                 : acc[a][w][j4 + j];
+            float out = __fsub_rn(br[0][0], br[0][1]);
+            if (kAB == 2) {
+              out = __fsub_rn(out, br[1][0]);
+              out = __fadd_rn(out, br[1][1]);
+            }
+            if (bias != nullptr)
+              out = __fadd_rn(out, b4[j]);
+            o[j] = act_tc(out, act);
+          }
+          if (full) {
+            *reinterpret_cast<float4 *>(dst + j4) = make_float4(o[0], o[1], o[2], o[3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              if (lane0 + j4 + j < N)
+                dst[j4 + j] = o[j];
+          }
         }
       }
     }
@@ -674,32 +737,36 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
   // Worth it only when the crossbar tiles are wide enough to feed the MMA.
   // The exponent copies need 16-byte aligned rows: m_pad and n_pad are
   // multiples of 128 and both exponent arrays start 16-byte aligned.
-  if (N < 32 || M < 512 || m_pad % kSBM || n_pad % kSBL || k_pad % 64 ||
+  const int L = act_branches == 2 ? SSShape<2>::L : SSShape<1>::L;
+  if (N < 32 || M < 512 || m_pad % kSBM || n_pad % 128 || k_pad % 64 ||
       static_cast<int64_t>(act_branches) * m_pad >= (int64_t{1} << 31) ||
       (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
       (reinterpret_cast<uintptr_t>(exA) & 15) || (reinterpret_cast<uintptr_t>(exB) & 15))
     return false;
   CUtensorMap ta, tb;
   if (!encode_int8_2d(&ta, A, act_branches * m_pad, k_pad, kSBM) ||
-      !encode_int8_2d(&tb, B, 2 * n_pad, k_pad, kSBL))
+      !encode_int8_2d(&tb, B, 2 * n_pad, k_pad, static_cast<uint32_t>(L)))
     return false;
-  const int64_t tiles = ((M + kSBM - 1) / kSBM) * ((N + kSBL - 1) / kSBL);
+  // Vector bias and output access when every row and the bias start 16-byte
+  // aligned.
+  const int vec = (N % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(bias) & 15) == 0)
+                      ? 1
+                      : 0;
+  const int64_t tiles = ((M + kSBM - 1) / kSBM) * ((N + L - 1) / L);
   const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, sm_count())));
-  if (act_branches == 2) {
-    if (cudaFuncSetAttribute(signsplit_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem_ss<2>())) != cudaSuccess)
+  auto launch = [&](auto kernel, size_t smem) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
       return false;
-    signsplit_tc_kernel<2><<<grid, kSThreads, smem_ss<2>(), stream>>>(
-        ta, tb, exA, static_cast<int>(m_pad), exB, static_cast<int>(n_pad), T,
-        static_cast<int>(M), static_cast<int>(N), bias, act, y, status);
-  } else {
-    if (cudaFuncSetAttribute(signsplit_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem_ss<1>())) != cudaSuccess)
-      return false;
-    signsplit_tc_kernel<1><<<grid, kSThreads, smem_ss<1>(), stream>>>(
-        ta, tb, exA, static_cast<int>(m_pad), exB, static_cast<int>(n_pad), T,
-        static_cast<int>(M), static_cast<int>(N), bias, act, y, status);
-  }
+    kernel<<<grid, kSThreads, smem, stream>>>(ta, tb, exA, static_cast<int>(m_pad), exB,
+                                              static_cast<int>(n_pad), T, static_cast<int>(M),
+                                              static_cast<int>(N), bias, act, vec, y, status);
+    return true;
+  };
+  if (!(act_branches == 2 ? launch(signsplit_tc_kernel<2>, smem_ss<2>())
+                          : launch(signsplit_tc_kernel<1>, smem_ss<1>())))
+    return false;
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
   return true;
 }

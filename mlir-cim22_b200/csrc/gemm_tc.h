@@ -15,8 +15,8 @@ bool int8_available();
 // layers.cu): A int8 [act_branches * m_pad][k_pad], exA int32
 // [act_branches][T][m_pad], B int8 [2 * n_pad][k_pad] (Wp rows, then Wn),
 // exB int32 [2][T][n_pad] followed by the weight-exponent ranges
-// [n_pad / 32][T][4] = {min, max, 0, 0} over both signs of each 32-lane block
-// and tile, and by the f32 weight scales 2^(Ew - 133) [2][T][n_pad]. Returns false when the shape is not handled by the tensor-core
+// [T][n_pad / 32][4] = {min, max, 0, 0} over both signs of each tile and
+// 32-lane block, and by the f32 weight scales 2^(Ew - 133) [2][T][n_pad]. Returns false when the shape is not handled by the tensor-core
 // kernel, in which case nothing was launched.
 bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad,
                       const int8_t *B, const int32_t *exB, int64_t n_pad,

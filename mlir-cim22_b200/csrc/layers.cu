@@ -773,11 +773,11 @@ static void prepare_bf16_weights(const float *w, int64_t n, int64_t k,
         // (slow) restore path.
         exps[(b * T + t) * n_pad + lane] = any ? exp_max : 127;
       }
-  // Per 32-lane block and tile: the range of the weight exponents of both
+  // Per tile and 32-lane block: the range of the weight exponents of both
   // signs, which decides the tensor-core epilogue's exact-FMA window.
   int32_t *ranges = exps.data() + 2 * T * n_pad;
-  for (int64_t nb = 0; nb < n_pad / 32; ++nb)
-    for (int64_t t = 0; t < T; ++t) {
+  for (int64_t t = 0; t < T; ++t)
+    for (int64_t nb = 0; nb < n_pad / 32; ++nb) {
       int lo = 1 << 30, hi = -(1 << 30);
       for (int b = 0; b < 2; ++b)
         for (int64_t lane = nb * 32; lane < nb * 32 + 32; ++lane) {
@@ -785,7 +785,7 @@ static void prepare_bf16_weights(const float *w, int64_t n, int64_t k,
           lo = std::min(lo, e);
           hi = std::max(hi, e);
         }
-      int32_t *r = ranges + (nb * T + t) * 4;
+      int32_t *r = ranges + (t * (n_pad / 32) + nb) * 4;
       r[0] = lo;
       r[1] = hi;
       r[2] = r[3] = 0;
