@@ -350,7 +350,7 @@ typedef struct cim22_gather {
   int32_t batch, channels, height, width; /* image geometry (conv only) */
   int32_t kernel_h, kernel_w, stride_h, stride_w, pad_h, pad_w;
   int32_t out_h, out_w;
-  /* Optional max pooling folded into the gather (NHWC only): when
+  /* Optional max pooling folded into a conv gather (either layout): when
    * pool_kernel > 0, x is the pre-pool image of pool_src_h x pool_src_w and
    * the conv reads max over each pool_kernel^2 window (stride pool_stride,
    * no padding), with height/width the pooled size. */
@@ -421,6 +421,29 @@ int cim22_cuda_layer_contract_bf16(const cim22_cuda_layer *layer, int64_t m,
                                    size_t workspace_bytes, int32_t *status,
                                    void *stream);
 
+/* No counterpart in the reference's C interface: the same layer with two
+ * options for the code around it. y is written as NCHW images,
+ * y[m / out_pixels][n][out_pixels], column m being (image, pixel) =
+ * (m / out_pixels, m % out_pixels) - the layout of the conv output the
+ * reference hands to the next torch op - when out_pixels > 0 (it must divide
+ * m), or as [m, n] rows when out_pixels = 0. When post_scale and post_shift
+ * are given (both or neither), each output becomes
+ * fma(out, post_scale[n], post_shift[n]) after the bias and before the
+ * activation: an inference batch norm that follows the layer, computed
+ * exactly as cim22_cuda_channel_affine_* computes it. */
+int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float *x,
+                                     const cim22_gather *gather, int64_t m, int64_t out_pixels,
+                                     const float *bias, const float *post_scale,
+                                     const float *post_shift, int32_t activation,
+                                     int32_t branches, float *y, void *workspace,
+                                     size_t workspace_bytes, int32_t *status, void *stream);
+int cim22_cuda_layer_contract_bf16_ex(const cim22_cuda_layer *layer, int64_t m,
+                                      int64_t out_pixels, const float *bias,
+                                      const float *post_scale, const float *post_shift,
+                                      int32_t activation, int32_t branches, float *y,
+                                      const void *workspace, size_t workspace_bytes,
+                                      int32_t *status, void *stream);
+
 /* INT8 layer: y[m, n] = sum over K tiles of the signed-i21 tile results,
  * accumulated in wrapping int32 (Passes.cpp:1054-1059). x is int8 [m, k]. */
 int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,
@@ -430,7 +453,8 @@ int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,
 
 /* ------------------------------------------------------------------------ */
 /* Host glue the compiler emits around CIM layers (upstream Linalg lowering,
- * lib/Compiler/Pipelines.cpp:61-72). All f32, device memory, NHWC images. */
+ * lib/Compiler/Pipelines.cpp:61-72). All f32, device memory; image layout
+ * in the function name. */
 
 int cim22_cuda_relu(const float *x, float *y, int64_t count, void *stream);
 int cim22_cuda_add(const float *a, const float *b, float *y, int64_t count,
@@ -461,6 +485,22 @@ int cim22_cuda_nhwc_to_nchw(const float *x, float *y, int32_t n, int32_t h,
 /* NCHW -> NHWC. */
 int cim22_cuda_nchw_to_nhwc(const float *x, float *y, int32_t n, int32_t c,
                             int32_t h, int32_t w, void *stream);
+/* The pooling and affine glue on NCHW batches [n, c, h, w]. */
+int cim22_cuda_maxpool2d_nchw(const float *x, float *y, int32_t n, int32_t c,
+                              int32_t h, int32_t w, int32_t kernel,
+                              int32_t stride, int32_t pad, void *stream);
+int cim22_cuda_avgpool2d_nchw(const float *x, float *y, int32_t n, int32_t c,
+                              int32_t h, int32_t w, int32_t kernel,
+                              int32_t stride, void *stream);
+/* Mean over H and W -> [n, c]. */
+int cim22_cuda_global_avgpool_nchw(const float *x, float *y, int32_t n,
+                                   int32_t c, int32_t h, int32_t w,
+                                   void *stream);
+/* y = x * scale[c] + shift[c] (+ activation) for planes of hw elements. */
+int cim22_cuda_channel_affine_nchw(const float *x, const float *scale,
+                                   const float *shift, float *y, int32_t n,
+                                   int32_t c, int64_t hw, int32_t activation,
+                                   void *stream);
 
 #ifdef __cplusplus
 }

@@ -109,17 +109,22 @@ class CimLayer:
     def forward_bf16(self, x: torch.Tensor, out: torch.Tensor, m: int, *,
                      gather: abi.Gather | None = None, bias: torch.Tensor | None = None,
                      activation: str | None = None, branches: int = 4,
+                     out_pixels: int = 0, post_scale: torch.Tensor | None = None,
+                     post_shift: torch.Tensor | None = None,
                      workspace: Workspace, status: StatusWord) -> torch.Tensor:
+        """out is [m, n] rows, or NCHW images [m / out_pixels, n, out_pixels]
+        when out_pixels > 0; post_scale/post_shift fold a following per-lane
+        affine (inference batch norm) into the epilogue."""
         _require(x, torch.float32, "x")
         _require(out, torch.float32, "out")
         if bias is not None:
             _require(bias, torch.float32, "bias")
         nbytes = self.workspace_bytes(m, branches)
         ws = workspace.get(nbytes)
-        rc = lib().cim22_cuda_layer_forward_bf16(
+        rc = lib().cim22_cuda_layer_forward_bf16_ex(
             self._handle, _ptr(x), None if gather is None else ctypes.byref(gather), m,
-            _ptr(bias), ACT[activation], branches, _ptr(out), _ptr(ws), ws.numel(),
-            _ptr(status.tensor), _stream(x.device))
+            out_pixels, _ptr(bias), _ptr(post_scale), _ptr(post_shift), ACT[activation],
+            branches, _ptr(out), _ptr(ws), ws.numel(), _ptr(status.tensor), _stream(x.device))
         check(rc, "cim22_cuda_layer_forward_bf16")
         return out
 
@@ -135,13 +140,16 @@ class CimLayer:
 
     def contract_bf16(self, out: torch.Tensor, m: int, *, bias: torch.Tensor | None = None,
                       activation: str | None = None, branches: int = 4,
+                      out_pixels: int = 0, post_scale: torch.Tensor | None = None,
+                      post_shift: torch.Tensor | None = None,
                       workspace: Workspace, status: StatusWord) -> None:
         """Second kernel of forward_bf16: crossbar dots, restore, accumulate, merge."""
         _require(out, torch.float32, "out")
         ws = workspace.get(self.workspace_bytes(m, branches))
-        check(lib().cim22_cuda_layer_contract_bf16(
-            self._handle, m, _ptr(bias), ACT[activation], branches, _ptr(out), _ptr(ws),
-            ws.numel(), _ptr(status.tensor), _stream(out.device)),
+        check(lib().cim22_cuda_layer_contract_bf16_ex(
+            self._handle, m, out_pixels, _ptr(bias), _ptr(post_scale), _ptr(post_shift),
+            ACT[activation], branches, _ptr(out), _ptr(ws), ws.numel(), _ptr(status.tensor),
+            _stream(out.device)),
             "cim22_cuda_layer_contract_bf16")
 
     def linear_bf16(self, x: torch.Tensor, bias=None, activation=None, branches: int = 4,
@@ -250,6 +258,47 @@ def channel_affine_nhwc(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tenso
     check(lib().cim22_cuda_channel_affine_nhwc(_ptr(x), _ptr(scale), _ptr(shift), _ptr(out),
                                                x.numel() // c, c, ACT[activation],
                                                _stream(x.device)), "channel_affine")
+    return out
+
+
+def maxpool2d_nchw(x: torch.Tensor, kernel: int, stride: int, pad: int = 0,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    n, c, h, w = x.shape
+    oh, ow = (h + 2 * pad - kernel) // stride + 1, (w + 2 * pad - kernel) // stride + 1
+    out = torch.empty(n, c, oh, ow, dtype=x.dtype, device=x.device) if out is None else out
+    check(lib().cim22_cuda_maxpool2d_nchw(_ptr(x), _ptr(out), n, c, h, w, kernel, stride, pad,
+                                          _stream(x.device)), "maxpool2d")
+    return out
+
+
+def avgpool2d_nchw(x: torch.Tensor, kernel: int, stride: int,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    n, c, h, w = x.shape
+    oh, ow = (h - kernel) // stride + 1, (w - kernel) // stride + 1
+    out = torch.empty(n, c, oh, ow, dtype=x.dtype, device=x.device) if out is None else out
+    check(lib().cim22_cuda_avgpool2d_nchw(_ptr(x), _ptr(out), n, c, h, w, kernel, stride,
+                                          _stream(x.device)), "avgpool2d")
+    return out
+
+
+def global_avgpool_nchw(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    n, c, h, w = x.shape
+    out = torch.empty(n, c, dtype=x.dtype, device=x.device) if out is None else out
+    check(lib().cim22_cuda_global_avgpool_nchw(_ptr(x), _ptr(out), n, c, h, w,
+                                               _stream(x.device)), "global_avgpool")
+    return out
+
+
+def channel_affine_nchw(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
+                        activation: str | None = None,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-channel affine over [n, c, ...] (every trailing element of a channel)."""
+    n, c = x.shape[0], x.shape[1]
+    hw = x.numel() // max(1, n * c)
+    out = torch.empty_like(x) if out is None else out
+    check(lib().cim22_cuda_channel_affine_nchw(_ptr(x), _ptr(scale), _ptr(shift), _ptr(out),
+                                               n, c, hw, ACT[activation], _stream(x.device)),
+          "channel_affine")
     return out
 
 

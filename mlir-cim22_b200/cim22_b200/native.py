@@ -60,6 +60,10 @@ _SIGNATURES = {
     "cim22_cuda_layer_forward_int8": (c.c_int, [P, P, I64, P, P, SZ, P, P]),
     "cim22_cuda_layer_prepare_bf16": (c.c_int, [P, P, P, I64, I32, P, SZ, P, P]),
     "cim22_cuda_layer_contract_bf16": (c.c_int, [P, I64, P, I32, I32, P, P, SZ, P, P]),
+    "cim22_cuda_layer_forward_bf16_ex": (c.c_int, [P, P, P, I64, I64, P, P, P, I32, I32, P, P,
+                                                   SZ, P, P]),
+    "cim22_cuda_layer_contract_bf16_ex": (c.c_int, [P, I64, I64, P, P, P, I32, I32, P, P, SZ, P,
+                                                    P]),
     "cim22_cuda_layer_forward_bf16_noalloc": (c.c_int, [P, P, P, I64, P, I32, I32, P, P, P]),
     "cim22_cuda_layer_noalloc_scratch_bytes": (SZ, []),
     "cim22_cuda_relu": (c.c_int, [P, P, I64, P]),
@@ -72,6 +76,10 @@ _SIGNATURES = {
     "cim22_cuda_softmax": (c.c_int, [P, P, I64, I32, P]),
     "cim22_cuda_nhwc_to_nchw": (c.c_int, [P, P, I32, I32, I32, I32, P]),
     "cim22_cuda_nchw_to_nhwc": (c.c_int, [P, P, I32, I32, I32, I32, P]),
+    "cim22_cuda_maxpool2d_nchw": (c.c_int, [P, P, I32, I32, I32, I32, I32, I32, I32, P]),
+    "cim22_cuda_avgpool2d_nchw": (c.c_int, [P, P, I32, I32, I32, I32, I32, I32, P]),
+    "cim22_cuda_global_avgpool_nchw": (c.c_int, [P, P, I32, I32, I32, I32, P]),
+    "cim22_cuda_channel_affine_nchw": (c.c_int, [P, P, P, P, I32, I32, I64, I32, P]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

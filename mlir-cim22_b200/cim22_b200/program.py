@@ -7,13 +7,19 @@ reference's lowering produces (lib/Conversion/LinalgToCIM/Passes.cpp:
 760-857,1087-1385,2304-2476); everything else becomes the Host glue kernels
 (ReLU, pooling, add, batch norm, GELU, softmax, flatten).
 
-Images are kept in NHWC internally, so a convolution's output matrix
-[N*OH*OW, F] is already the next layer's input image and no transposes are
-launched between layers. An activation that directly follows a CIM layer and
-is its only consumer is fused into the layer's epilogue. A layer whose input is
-provably nonnegative runs 2 branches instead of 4; the xn branches are exactly
-+0 then, so the result is bit-identical (the reference proves the same
-invariance only for a narrower set of producers, Passes.cpp:2239-2303).
+Images are kept in NCHW, the layout torch hands between the ops: the
+contraction epilogue writes each convolution's output planes directly (a
+warp stores 32 neighbouring pixels of one channel), the next layer's gather
+reads a kernel tap of 32 neighbouring pixels per warp load, flatten is a
+view, and no transposes are launched between layers. (layout="nhwc" keeps
+images channel-minor instead: the output matrix [N*OH*OW, F] itself.)
+
+An inference batch norm and an activation that directly follow a CIM layer
+as its only consumers are fused into the layer's epilogue (the same
+per-channel fma and activation the glue kernels compute). A layer whose
+input is provably nonnegative runs 2 branches instead of 4; the xn branches
+are exactly +0 then, so the result is bit-identical (the reference proves the
+same invariance only for a narrower set of producers, Passes.cpp:2239-2303).
 
 All buffers are allocated once for the static input shapes, so a program can
 be captured into a CUDA graph and replayed.
@@ -40,13 +46,13 @@ IMAGE, MATRIX, TENSOR, CONST = "image", "matrix", "tensor", "const"
 class Val:
     kind: str
     shape: tuple  # logical (torch) shape
-    tensor: torch.Tensor | None = None  # device storage (NHWC for images)
-    layout: str = "nhwc"  # images: "nhwc" storage or "nchw" (graph inputs)
+    tensor: torch.Tensor | None = None  # device storage
+    layout: str = "nchw"  # images: "nchw" or "nhwc" storage
     nonneg: bool = False
     value: Any = None  # constants
     dtype: torch.dtype = torch.float32
     pool: tuple | None = None  # pending max pool (kernel, stride, source Val)
-    flat_of: "Val | None" = None  # pending flatten of this NHWC image
+    flat_of: "Val | None" = None  # pending flatten of this image
 
 
 @dataclass
@@ -91,10 +97,13 @@ class Program:
 
     def __init__(self, gm: fx.GraphModule, example_inputs, *, frozen: set[int] | None = None,
                  device: int | torch.device = 0, name: str = "cim_program",
-                 fuse: bool = True) -> None:
+                 fuse: bool = True, layout: str = "nchw") -> None:
+        if layout not in ("nchw", "nhwc"):
+            raise ValueError(f"unknown image layout {layout!r}")
         self.device = torch.device("cuda", device) if isinstance(device, int) else device
         self.name = name
         self.fuse = fuse
+        self.layout = layout
         self.workspace = Workspace(self.device)
         self.status = StatusWord(self.device)
         self.steps: list[Step] = []
@@ -110,6 +119,7 @@ class Program:
         self._fused: set[fx.Node] = set()
         placeholder_index = 0
         modules = dict(gm.named_modules())
+        self._modules = modules
         for node in gm.graph.nodes:
             if node in self._fused:
                 continue
@@ -269,6 +279,42 @@ class Program:
             return "gelu", fused
         return None, node
 
+    def _fusable_bn(self, node, users):
+        """The inference batch norm that is node's only user, as (bn node,
+        its (target, args, kwargs)), or None."""
+        if not self.fuse or users[node] != 1:
+            return None
+        (user,) = node.users
+        if user.op == "call_module":
+            module = self._modules[str(user.target)]
+            if isinstance(module, torch.nn.BatchNorm2d) and not module.training:
+                call = self._module_as_call(user, module)
+                return user, call
+        elif user.op == "call_function" and user.target in _BN and user.args[0] is node:
+            training = user.args[5] if len(user.args) > 5 else user.kwargs.get("training", False)
+            if not training:
+                return user, (user.target, user.args, dict(user.kwargs))
+        return None
+
+    def _bn_affine(self, args, kwargs, env):
+        """Device (scale, shift) of an inference batch norm: y = x * scale + shift."""
+        mean, var = self._const(env, args[1]), self._const(env, args[2])
+        weight = self._const(env, args[3]) if len(args) > 3 else kwargs.get("weight")
+        bias = self._const(env, args[4]) if len(args) > 4 else kwargs.get("bias")
+        training = args[5] if len(args) > 5 else kwargs.get("training", False)
+        eps = args[7] if len(args) > 7 else kwargs.get("eps", 1e-5)
+        if training:
+            raise NotImplementedError("batch_norm lowers inference mode only")
+        mean = torch.as_tensor(mean).float()
+        var = torch.as_tensor(var).float()
+        gamma = torch.ones_like(mean) if weight is None else torch.as_tensor(weight).float()
+        beta = torch.zeros_like(mean) if bias is None else torch.as_tensor(bias).float()
+        scale = (gamma / torch.sqrt(var + eps)).contiguous()
+        shift = (beta - mean * scale).contiguous()
+        st, sh = scale.to(self.device), shift.to(self.device)
+        self._keep += [st, sh]
+        return st, sh
+
     def _bias(self, b):
         if b is None:
             return None
@@ -296,8 +342,20 @@ class Program:
         self._keep.append(layer)
         g, xt = self._image_gather(x, kh, kw, stride[0], pad[0])
         m = n * g.out_h * g.out_w
-        act, out_node = self._epilogue(node, users)
-        out = self._new((n, g.out_h, g.out_w, f))
+        # A following inference batch norm folds into the epilogue as the
+        # same per-channel fma the glue would compute.
+        post_scale = post_shift = None
+        tail = node
+        bn = self._fusable_bn(node, users)
+        if bn is not None:
+            bn_node, (_, bn_args, bn_kwargs) = bn
+            post_scale, post_shift = self._bn_affine(bn_args, bn_kwargs, env)
+            self._fused.add(bn_node)
+            tail = bn_node
+        act, out_node = self._epilogue(tail, users)
+        nchw = self.layout == "nchw"
+        out = self._new((n, f, g.out_h, g.out_w) if nchw else (n, g.out_h, g.out_w, f))
+        pixels = g.out_h * g.out_w if nchw else 0
         bias = self._bias(b)
         branches = 2 if x.nonneg else 4
 
@@ -307,17 +365,21 @@ class Program:
 
         def run():
             layer.contract_bf16(out, m, bias=bias, activation=act, branches=branches,
-                                workspace=self.workspace, status=self.status)
+                                out_pixels=pixels, post_scale=post_scale,
+                                post_shift=post_shift, workspace=self.workspace,
+                                status=self.status)
 
         name = f"conv{len(self.layers)}"
         self.steps.append(Step(name + ".prepare", prepare))
         self.steps.append(Step(name, run, cim=True, meta=dict(
-            kind="conv", x=xt, layout=x.layout, weight=torch.as_tensor(w).detach().float(),
+            kind="conv", x=xt, layout=x.layout, out_layout=self.layout,
+            post=None if post_scale is None else (post_scale, post_shift),
+            weight=torch.as_tensor(w).detach().float(),
             bias=None if b is None else torch.as_tensor(b).detach().float(), stride=stride[0],
             pad=pad[0], out=out, act=act, branches=branches)))
         self.layers.append(LayerInfo(name, "conv", m, c * kh * kw, f, branches,
                                      branches * m * c * kh * kw * f))
-        env[out_node] = Val(IMAGE, (n, f, g.out_h, g.out_w), out, "nhwc",
+        env[out_node] = Val(IMAGE, (n, f, g.out_h, g.out_w), out, self.layout,
                             nonneg=act == "relu")
 
     def _lower_linear(self, node, args, env, users) -> None:
@@ -335,9 +397,10 @@ class Program:
         bias = self._bias(b)
         branches = 2 if x.nonneg else 4
         g = None
-        if x.flat_of is not None and x.tensor is None and x.flat_of.layout == "nhwc":
-            # flatten(NHWC image) -> Linear is the conv whose kernel covers the
-            # image: its K order c*H*W + h*W + w is the NCHW flatten order.
+        if x.flat_of is not None and x.tensor is None:
+            # flatten(image) -> Linear is the conv whose kernel covers the
+            # image: its K order c*H*W + h*W + w is the NCHW flatten order, so
+            # an NHWC image or a pending max pool is read in place.
             img = x.flat_of
             g, xt = self._image_gather(img, img.shape[2], img.shape[3], 1, 0)
         else:
@@ -410,7 +473,8 @@ class Program:
             c = torch.as_tensor(const, dtype=torch.float32)
             if v.kind == IMAGE and c.dim() > 0:
                 c = c.reshape(v.shape) if c.numel() == np.prod(v.shape) else c
-                c = c.permute(0, 2, 3, 1) if c.dim() == 4 else c
+                if v.layout == "nhwc" and c.dim() == 4:
+                    c = c.permute(0, 2, 3, 1)
             ct = c.expand(self._tensor(v).shape).contiguous().to(self.device)
             self._keep.append(ct)
             va, vb = v, Val(v.kind, v.shape, ct, v.layout)
@@ -431,14 +495,23 @@ class Program:
             k, s, src = v.pool
             st = self._tensor(src)
             n, c, oh, ow = v.shape
-            out = self._new((n, oh, ow, c))
-            self.steps.append(Step("maxpool", lambda: cim_ops.maxpool2d_nhwc(st, k, s, 0, out)))
+            if v.layout == "nchw":
+                out = self._new((n, c, oh, ow))
+                self.steps.append(Step("maxpool",
+                                       lambda: cim_ops.maxpool2d_nchw(st, k, s, 0, out)))
+            else:
+                out = self._new((n, oh, ow, c))
+                self.steps.append(Step("maxpool",
+                                       lambda: cim_ops.maxpool2d_nhwc(st, k, s, 0, out)))
             v.tensor = out
             return out
         if v.flat_of is not None:
             img = v.flat_of
             it = self._tensor(img)
             n, c, h, w = img.shape
+            if img.layout == "nchw":
+                v.tensor = it.view(n, c * h * w)
+                return v.tensor
             out = self._new((n, c, h, w))
             self.steps.append(Step("flatten", lambda: cim_ops.nhwc_to_nchw(it, out)))
             v.tensor = out.view(n, c * h * w)
@@ -451,7 +524,8 @@ class Program:
         if x.pool is not None and x.tensor is None:
             k, s, src = x.pool
             st = self._tensor(src)
-            g = cim_ops.conv_gather(abi.GATHER_CONV_NHWC, n, c, h, w, kh, kw, stride, pad)
+            kind = abi.GATHER_CONV_NCHW if x.layout == "nchw" else abi.GATHER_CONV_NHWC
+            g = cim_ops.conv_gather(kind, n, c, h, w, kh, kw, stride, pad)
             g.pool_kernel, g.pool_stride = k, s
             g.pool_src_h, g.pool_src_w = src.shape[2], src.shape[3]
         else:
@@ -461,12 +535,18 @@ class Program:
         self._keep.append(g)
         return g, st
 
-    def _nhwc(self, x: Val) -> torch.Tensor:
-        if x.layout == "nhwc":
-            return self._tensor(x)
-        out = self._new((x.shape[0], x.shape[2], x.shape[3], x.shape[1]))
-        xt = x.tensor
-        self.steps.append(Step("nchw_to_nhwc", lambda: cim_ops.nchw_to_nhwc(xt, out)))
+    def _in_layout(self, x: Val) -> torch.Tensor:
+        """Storage of image x in the program's layout, converting once if needed."""
+        xt = self._tensor(x)
+        if x.layout == self.layout:
+            return xt
+        n, c, h, w = x.shape
+        if self.layout == "nhwc":
+            out = self._new((n, h, w, c))
+            self.steps.append(Step("nchw_to_nhwc", lambda: cim_ops.nchw_to_nhwc(xt, out)))
+        else:
+            out = self._new((n, c, h, w))
+            self.steps.append(Step("nhwc_to_nchw", lambda: cim_ops.nhwc_to_nchw(xt, out)))
         return out
 
     def _lower_pool(self, node, args, kwargs, env, kind) -> None:
@@ -486,34 +566,40 @@ class Program:
         n, c, h, w = x.shape
         oh = (h + 2 * p[0] - k[0]) // s[0] + 1
         ow = (w + 2 * p[0] - k[0]) // s[0] + 1
-        if self.fuse and kind == "max" and p[0] == 0 and x.layout == "nhwc" and x.pool is None:
+        if (self.fuse and kind == "max" and p[0] == 0 and x.pool is None
+                and x.tensor is not None):
             # Pending: a following CIM layer reads the window max in its gather.
-            env[node] = Val(IMAGE, (n, c, oh, ow), None, "nhwc", nonneg=x.nonneg,
+            env[node] = Val(IMAGE, (n, c, oh, ow), None, x.layout, nonneg=x.nonneg,
                             pool=(k[0], s[0], x))
             return
-        xt = self._nhwc(x)
-        out = self._new((n, oh, ow, c))
+        xt = self._in_layout(x)
+        nchw = self.layout == "nchw"
+        out = self._new((n, c, oh, ow) if nchw else (n, oh, ow, c))
         if kind == "max":
-            self.steps.append(Step("maxpool", lambda: cim_ops.maxpool2d_nhwc(xt, k[0], s[0], p[0], out)))
+            fn = cim_ops.maxpool2d_nchw if nchw else cim_ops.maxpool2d_nhwc
+            self.steps.append(Step("maxpool", lambda: fn(xt, k[0], s[0], p[0], out)))
         else:
-            self.steps.append(Step("avgpool", lambda: cim_ops.avgpool2d_nhwc(xt, k[0], s[0], out)))
-        env[node] = Val(IMAGE, (n, c, oh, ow), out, "nhwc", nonneg=x.nonneg)
+            fn = cim_ops.avgpool2d_nchw if nchw else cim_ops.avgpool2d_nhwc
+            self.steps.append(Step("avgpool", lambda: fn(xt, k[0], s[0], out)))
+        env[node] = Val(IMAGE, (n, c, oh, ow), out, self.layout, nonneg=x.nonneg)
 
     def _lower_gap(self, node, x, env) -> None:
-        xt = self._nhwc(x)
+        xt = self._in_layout(x)
         n, c, h, w = x.shape
-        out = self._new((n, 1, 1, c))
-        self.steps.append(Step("global_avgpool",
-                               lambda: cim_ops.global_avgpool_nhwc(xt, out.view(n, c))))
-        env[node] = Val(IMAGE, (n, c, 1, 1), out, "nhwc", nonneg=x.nonneg)
+        nchw = self.layout == "nchw"
+        out = self._new((n, c, 1, 1) if nchw else (n, 1, 1, c))
+        fn = cim_ops.global_avgpool_nchw if nchw else cim_ops.global_avgpool_nhwc
+        self.steps.append(Step("global_avgpool", lambda: fn(xt, out.view(n, c))))
+        env[node] = Val(IMAGE, (n, c, 1, 1), out, self.layout, nonneg=x.nonneg)
 
     def _lower_flatten(self, node, x, start, env) -> None:
         if start != 1:
             raise NotImplementedError("flatten lowers start_dim=1")
         if x.kind == IMAGE:
             n, c, h, w = x.shape
-            if x.layout == "nhwc" and (h, w) != (1, 1):
-                # Pending: a following Linear gathers the image directly.
+            if (x.layout == "nhwc" and (h, w) != (1, 1)) or x.tensor is None:
+                # Pending: a following Linear gathers the image directly
+                # (channel-minor storage or a pending max pool).
                 env[node] = Val(MATRIX, (n, c * h * w), None, nonneg=x.nonneg, flat_of=x)
                 if not self.fuse:
                     self._tensor(env[node])
@@ -525,27 +611,15 @@ class Program:
 
     def _lower_bn(self, node, args, kwargs, env, users) -> None:
         x = env[args[0]]
-        mean, var = self._const(env, args[1]), self._const(env, args[2])
-        weight = self._const(env, args[3]) if len(args) > 3 else kwargs.get("weight")
-        bias = self._const(env, args[4]) if len(args) > 4 else kwargs.get("bias")
-        training = args[5] if len(args) > 5 else kwargs.get("training", False)
-        eps = args[7] if len(args) > 7 else kwargs.get("eps", 1e-5)
-        if training:
-            raise NotImplementedError("batch_norm lowers inference mode only")
-        mean = torch.as_tensor(mean).float()
-        var = torch.as_tensor(var).float()
-        gamma = torch.ones_like(mean) if weight is None else torch.as_tensor(weight).float()
-        beta = torch.zeros_like(mean) if bias is None else torch.as_tensor(bias).float()
-        scale = (gamma / torch.sqrt(var + eps)).contiguous()
-        shift = (beta - mean * scale).contiguous()
-        st, sh = scale.to(self.device), shift.to(self.device)
-        self._keep += [st, sh]
-        xt = self._nhwc(x) if x.kind == IMAGE else self._tensor(x)
+        st, sh = self._bn_affine(args, kwargs, env)
+        image = x.kind == IMAGE
+        xt = self._in_layout(x) if image else self._tensor(x)
         act, out_node = self._epilogue(node, users)
         out = self._new(xt.shape)
-        self.steps.append(Step("batch_norm",
-                               lambda: cim_ops.channel_affine_nhwc(xt, st, sh, act, out)))
-        env[out_node] = Val(x.kind, x.shape, out, "nhwc" if x.kind == IMAGE else x.layout,
+        fn = (cim_ops.channel_affine_nchw if image and self.layout == "nchw"
+              else cim_ops.channel_affine_nhwc)
+        self.steps.append(Step("batch_norm", lambda: fn(xt, st, sh, act, out)))
+        env[out_node] = Val(x.kind, x.shape, out, self.layout if image else x.layout,
                             nonneg=act == "relu")
 
     def _lower_softmax(self, node, args, kwargs, env) -> None:
@@ -618,7 +692,9 @@ class Program:
 
 
 def from_module(model: torch.nn.Module, example: torch.Tensor, device: int = 0,
-                name: str = "cim_program", fuse: bool = True) -> Program:
+                name: str = "cim_program", fuse: bool = True,
+                layout: str = "nchw") -> Program:
     """Lower an eval-mode module by symbolic tracing, freezing its parameters."""
     gm = fx.symbolic_trace(model)
-    return Program(gm, [example], frozen=set(), device=device, name=name, fuse=fuse)
+    return Program(gm, [example], frozen=set(), device=device, name=name, fuse=fuse,
+                   layout=layout)

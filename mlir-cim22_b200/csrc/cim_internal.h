@@ -33,6 +33,30 @@ constexpr int64_t kLanePad = 128;
 // Column padding of prepared activations: a multiple of the M tile.
 constexpr int64_t kColumnPad = 128;
 
+// Division by an invariant divisor as a multiply-high and shift (Granlund and
+// Montgomery, "Division by invariant integers using multiplication", 1994):
+// q = (umulhi(n, mul) + n) >> shift for 0 <= n < 2^31, with
+// shift = ceil(log2 d) and mul = floor(2^32 (2^shift - d) / d) + 1.
+struct FastDiv {
+  uint32_t d, mul, shift;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f{d, 0, 0};
+  uint32_t l = 0;
+  while ((uint64_t{1} << l) < d)
+    ++l;
+  f.shift = l;
+  f.mul = static_cast<uint32_t>(((uint64_t{1} << 32) * ((uint64_t{1} << l) - d)) / d + 1);
+  return f;
+}
+
+#if defined(__CUDACC__)
+__device__ __forceinline__ int fdiv(int n, const FastDiv &f) {
+  return static_cast<int>((__umulhi(static_cast<uint32_t>(n), f.mul) + static_cast<uint32_t>(n)) >> f.shift);
+}
+#endif
+
 } // namespace cim
 
 // Prepared CIM layer weights resident in device memory.

@@ -394,8 +394,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
     signsplit_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const int32_t *__restrict__ exA,
                         int m_pad, const int32_t *__restrict__ exB, int n_pad, int T, int M,
-                        int N, const float *__restrict__ bias, int act, int vec,
-                        float *__restrict__ y, int32_t *status) {
+                        int N, const float *__restrict__ bias,
+                        const float *__restrict__ post_scale,
+                        const float *__restrict__ post_shift, int act, int vec,
+                        int out_pixels, float *__restrict__ y, int32_t *status) {
   using S = SSShape<kAB>;
   constexpr int L = S::L, LT = S::LT, SN = S::N;
   extern __shared__ uint8_t smem_raw[];
@@ -598,13 +600,24 @@ __global__ void __launch_bounds__(kSThreads, 1)
         break;
       const int row = m0 + row_local;
       if (row < M) {
-        float *dst = y + static_cast<int64_t>(row) * N + lane0;
-        const bool full = vec && lane0 + LT <= N;
+        // Rows layout: y[row][lane]. NCHW layout: y[image][lane][pixel] with
+        // row = image * out_pixels + pixel, so a warp's 32 consecutive rows
+        // store 32 consecutive floats of one lane.
+        int64_t base = static_cast<int64_t>(row) * N + lane0, lane_stride = 1;
+        if (out_pixels > 0) {
+          const int image = row / out_pixels;
+          base = (static_cast<int64_t>(image) * N + lane0) * out_pixels + (row - image * out_pixels);
+          lane_stride = out_pixels;
+        }
+        float *dst = y + base;
+        const bool full = lane0 + LT <= N;
+        const bool bias_vec = full && (vec & 1);
+        const bool store_vec = full && (vec & 2) && out_pixels == 0;
 #pragma unroll
         for (int j4 = 0; j4 < LT; j4 += 4) {
           float b4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
           if (bias != nullptr) {
-            if (full) {
+            if (bias_vec) {
               const float4 v = __ldg(reinterpret_cast<const float4 *>(bias + lane0 + j4));
               b4[0] = v.x; b4[1] = v.y; b4[2] = v.z; b4[3] = v.w;
             } else {
@@ -633,15 +646,18 @@ __global__ void __launch_bounds__(kSThreads, 1)
             }
             if (bias != nullptr)
               out = __fadd_rn(out, b4[j]);
+            if (post_scale != nullptr && lane0 + j4 + j < N)
+              out = __fmaf_rn(out, __ldg(post_scale + lane0 + j4 + j),
+                              __ldg(post_shift + lane0 + j4 + j));
             o[j] = act_tc(out, act);
           }
-          if (full) {
+          if (store_vec) {
             *reinterpret_cast<float4 *>(dst + j4) = make_float4(o[0], o[1], o[2], o[3]);
           } else {
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               if (lane0 + j4 + j < N)
-                dst[j4 + j] = o[j];
+                dst[(j4 + j) * lane_stride] = o[j];
           }
         }
       }
@@ -732,8 +748,9 @@ bool int8_available() { return sm100(nullptr) && encode_fn() != nullptr; }
 
 bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const int8_t *B,
                       const int32_t *exB, int64_t n_pad, int64_t k_pad, int T, int64_t M,
-                      int64_t N, const float *bias, int act, int act_branches, float *y,
-                      int32_t *status, cudaStream_t stream) {
+                      int64_t N, const float *bias, const float *post_scale,
+                      const float *post_shift, int act, int act_branches,
+                      int64_t out_pixels, float *y, int32_t *status, cudaStream_t stream) {
   // Worth it only when the crossbar tiles are wide enough to feed the MMA.
   // The exponent copies need 16-byte aligned rows: m_pad and n_pad are
   // multiples of 128 and both exponent arrays start 16-byte aligned.
@@ -747,12 +764,10 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
   if (!encode_int8_2d(&ta, A, act_branches * m_pad, k_pad, kSBM) ||
       !encode_int8_2d(&tb, B, 2 * n_pad, k_pad, static_cast<uint32_t>(L)))
     return false;
-  // Vector bias and output access when every row and the bias start 16-byte
-  // aligned.
-  const int vec = (N % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 &&
-                   (reinterpret_cast<uintptr_t>(bias) & 15) == 0)
-                      ? 1
-                      : 0;
+  // Vector bias loads (bit 0) and row stores (bit 1) where the bias and the
+  // output rows start 16-byte aligned.
+  const int vec = (N % 4 == 0 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0 ? 1 : 0) |
+                  (N % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 ? 2 : 0);
   const int64_t tiles = ((M + kSBM - 1) / kSBM) * ((N + L - 1) / L);
   const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, sm_count())));
   auto launch = [&](auto kernel, size_t smem) {
@@ -761,7 +776,9 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
       return false;
     kernel<<<grid, kSThreads, smem, stream>>>(ta, tb, exA, static_cast<int>(m_pad), exB,
                                               static_cast<int>(n_pad), T, static_cast<int>(M),
-                                              static_cast<int>(N), bias, act, vec, y, status);
+                                              static_cast<int>(N), bias, post_scale,
+                                              post_shift, act, vec,
+                                              static_cast<int>(out_pixels), y, status);
     return true;
   };
   if (!(act_branches == 2 ? launch(signsplit_tc_kernel<2>, smem_ss<2>())

@@ -17,12 +17,17 @@ bool int8_available();
 // exB int32 [2][T][n_pad] followed by the weight-exponent ranges
 // [T][n_pad / 32][4] = {min, max, 0, 0} over both signs of each tile and
 // 32-lane block, and by the f32 weight scales 2^(Ew - 133) [2][T][n_pad]. Returns false when the shape is not handled by the tensor-core
-// kernel, in which case nothing was launched.
+// kernel, in which case nothing was launched. out_pixels = 0 writes y as
+// rows [M][N]; out_pixels > 0 writes NCHW images [M / out_pixels][N][out_pixels].
+// A non-null post_scale applies fma(out, post_scale[n], post_shift[n]) after
+// the bias and before the activation.
 bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad,
                       const int8_t *B, const int32_t *exB, int64_t n_pad,
                       int64_t k_pad, int T, int64_t M, int64_t N,
-                      const float *bias, int act, int act_branches, float *y,
-                      int32_t *status, cudaStream_t stream);
+                      const float *bias, const float *post_scale,
+                      const float *post_shift, int act, int act_branches,
+                      int64_t out_pixels, float *y, int32_t *status,
+                      cudaStream_t stream);
 
 // INT8 contraction with whole-K int32 accumulation for range-proven layers.
 // A is int8 [a_rows][a_cols] (a_cols <= k_pad, a multiple of 16; rows >= M),

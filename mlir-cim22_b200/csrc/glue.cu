@@ -2,7 +2,7 @@
 // (ReLU, residual add, GELU, pooling, batch-norm affine, softmax, layout),
 // lowered by the reference through upstream Linalg to loops
 // (lib/Compiler/Pipelines.cpp:61-72). Memory-bound: grid-stride loops with
-// 128-bit accesses where the shape allows, images in NHWC.
+// 128-bit accesses where the shape allows, images in NHWC or NCHW as named.
 #include "cim_internal.h"
 
 #include <algorithm>
@@ -204,6 +204,111 @@ __global__ void nchw_to_nhwc_kernel(const float *__restrict__ x, float *__restri
   }
 }
 
+// NCHW pooling: output index i = ((b * c + ch) * oh + oy) * ow + ox, so a
+// warp's threads read neighbouring pixels of one plane.
+__global__ void maxpool_nchw_kernel(const float *__restrict__ x, float *__restrict__ y,
+                                    int64_t planes, int h, int w, int k, int s, int pad,
+                                    int oh, int ow) {
+  const int64_t total = planes * oh * ow;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < total; i += stride) {
+    const int ox = static_cast<int>(i % ow);
+    const int64_t r = i / ow;
+    const int oy = static_cast<int>(r % oh);
+    const float *plane = x + (r / oh) * h * w;
+    float m = -FLT_MAX;
+    bool any = false;
+    for (int dy = 0; dy < k; ++dy)
+      for (int dx = 0; dx < k; ++dx) {
+        const int iy = oy * s - pad + dy, ix = ox * s - pad + dx;
+        if (iy < 0 || iy >= h || ix < 0 || ix >= w)
+          continue;
+        const float v = plane[iy * w + ix];
+        // NaN propagates like torch.max_pool2d.
+        if (!any || v > m || v != v) {
+          m = v;
+          any = true;
+        }
+      }
+    y[i] = m;
+  }
+}
+
+__global__ void avgpool_nchw_kernel(const float *__restrict__ x, float *__restrict__ y,
+                                    int64_t planes, int h, int w, int k, int s, int oh,
+                                    int ow) {
+  const int64_t total = planes * oh * ow;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const float inv = 1.0f / static_cast<float>(k * k);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < total; i += stride) {
+    const int ox = static_cast<int>(i % ow);
+    const int64_t r = i / ow;
+    const int oy = static_cast<int>(r % oh);
+    const float *plane = x + (r / oh) * h * w;
+    float sum = 0.0f;
+    for (int dy = 0; dy < k; ++dy)
+      for (int dx = 0; dx < k; ++dx)
+        sum += plane[(oy * s + dy) * w + ox * s + dx];
+    y[i] = sum * inv;
+  }
+}
+
+// Mean of each plane: one warp per (image, channel) plane.
+__global__ void gap_nchw_kernel(const float *__restrict__ x, float *__restrict__ y,
+                                int64_t planes, int64_t hw) {
+  const int64_t plane = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (plane >= planes)
+    return;
+  const float *p = x + plane * hw;
+  float sum = 0.0f;
+  for (int64_t i = lane; i < hw; i += 32)
+    sum += p[i];
+  for (int o = 16; o; o >>= 1)
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0)
+    y[plane] = sum / static_cast<float>(hw);
+}
+
+// Per-channel affine over NCHW planes, 128-bit accesses: planes of a
+// multiple of 4 elements, flat index below 2^31 quads.
+__global__ void affine_nchw_vec_kernel(const float4 *__restrict__ x,
+                                       const float *__restrict__ scale,
+                                       const float *__restrict__ shift, float4 *__restrict__ y,
+                                       int quads, FastDiv div_plane, FastDiv div_c, int act) {
+  const int stride = static_cast<int>(gridDim.x * blockDim.x);
+  for (int i = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x); i < quads; i += stride) {
+    const int plane = fdiv(i, div_plane);
+    const int ch = plane - fdiv(plane, div_c) * static_cast<int>(div_c.d);
+    const float sc = __ldg(scale + ch), sh = __ldg(shift + ch);
+    float4 v = x[i];
+    v.x = act_fn(fmaf(v.x, sc, sh), act);
+    v.y = act_fn(fmaf(v.y, sc, sh), act);
+    v.z = act_fn(fmaf(v.z, sc, sh), act);
+    v.w = act_fn(fmaf(v.w, sc, sh), act);
+    y[i] = v;
+  }
+}
+
+// Per-channel affine over NCHW planes: block (x, plane) strides one plane.
+__global__ void affine_nchw_kernel(const float *__restrict__ x, const float *__restrict__ scale,
+                                   const float *__restrict__ shift, float *__restrict__ y,
+                                   int64_t planes, int c, int64_t hw, int act) {
+  const int64_t plane = blockIdx.y + static_cast<int64_t>(blockIdx.z) * gridDim.y;
+  if (plane >= planes)
+    return;
+  const int ch = static_cast<int>(plane % c);
+  const float sc = scale[ch], sh = shift[ch];
+  const float *src = x + plane * hw;
+  float *dst = y + plane * hw;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < hw;
+       i += stride)
+    dst[i] = act_fn(fmaf(src[i], sc, sh), act);
+}
+
 int launched(const char *what) {
   return cuda_ok(cudaGetLastError(), what) ? 0 : CIM22_STATUS_BAD_ARGUMENT;
 }
@@ -330,6 +435,79 @@ int cim22_cuda_nchw_to_nhwc(const float *x, float *y, int32_t n, int32_t c,
   nchw_to_nhwc_kernel<<<grid_for(static_cast<int64_t>(n) * h * w * c), 256, 0,
                         static_cast<cudaStream_t>(stream)>>>(x, y, n, c, h, w);
   return launched("nchw_to_nhwc");
+}
+
+int cim22_cuda_maxpool2d_nchw(const float *x, float *y, int32_t n, int32_t c,
+                              int32_t h, int32_t w, int32_t kernel,
+                              int32_t stride, int32_t pad, void *stream) {
+  if (!x || !y || n <= 0 || h <= 0 || w <= 0 || c <= 0 || kernel <= 0 ||
+      stride <= 0 || pad < 0 || 2 * pad > kernel)
+    return bad("cim22_cuda_maxpool2d_nchw");
+  const int oh = (h + 2 * pad - kernel) / stride + 1;
+  const int ow = (w + 2 * pad - kernel) / stride + 1;
+  if (oh <= 0 || ow <= 0)
+    return bad("cim22_cuda_maxpool2d_nchw");
+  const int64_t planes = static_cast<int64_t>(n) * c;
+  maxpool_nchw_kernel<<<grid_for(planes * oh * ow), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, y, planes, h, w, kernel, stride, pad, oh, ow);
+  return launched("maxpool2d");
+}
+
+int cim22_cuda_avgpool2d_nchw(const float *x, float *y, int32_t n, int32_t c,
+                              int32_t h, int32_t w, int32_t kernel,
+                              int32_t stride, void *stream) {
+  if (!x || !y || n <= 0 || h <= 0 || w <= 0 || c <= 0 || kernel <= 0 ||
+      stride <= 0 || kernel > h || kernel > w)
+    return bad("cim22_cuda_avgpool2d_nchw");
+  const int oh = (h - kernel) / stride + 1, ow = (w - kernel) / stride + 1;
+  const int64_t planes = static_cast<int64_t>(n) * c;
+  avgpool_nchw_kernel<<<grid_for(planes * oh * ow), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, y, planes, h, w, kernel, stride, oh, ow);
+  return launched("avgpool2d");
+}
+
+int cim22_cuda_global_avgpool_nchw(const float *x, float *y, int32_t n,
+                                   int32_t c, int32_t h, int32_t w,
+                                   void *stream) {
+  if (!x || !y || n <= 0 || h <= 0 || w <= 0 || c <= 0)
+    return bad("cim22_cuda_global_avgpool_nchw");
+  const int64_t planes = static_cast<int64_t>(n) * c;
+  const unsigned blocks = static_cast<unsigned>((planes * 32 + 255) / 256);
+  gap_nchw_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, y, planes, static_cast<int64_t>(h) * w);
+  return launched("global_avgpool");
+}
+
+int cim22_cuda_channel_affine_nchw(const float *x, const float *scale,
+                                   const float *shift, float *y, int32_t n,
+                                   int32_t c, int64_t hw, int32_t activation,
+                                   void *stream) {
+  if (!x || !scale || !shift || !y || n < 0 || c <= 0 || hw < 0 || activation < 0 ||
+      activation > 2)
+    return bad("cim22_cuda_channel_affine_nchw");
+  const int64_t planes = static_cast<int64_t>(n) * c;
+  if (planes == 0 || hw == 0)
+    return 0;
+  const int64_t quads = planes * hw / 4;
+  if (hw % 4 == 0 && quads < (int64_t{1} << 31) && planes < (int64_t{1} << 31) &&
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0) {
+    affine_nchw_vec_kernel<<<grid_for(quads), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const float4 *>(x), scale, shift, reinterpret_cast<float4 *>(y),
+        static_cast<int>(quads), make_fastdiv(static_cast<uint32_t>(hw / 4)),
+        make_fastdiv(static_cast<uint32_t>(c)), activation);
+    return launched("channel_affine");
+  }
+  // Planes over grid.y and grid.z (blocks past the last plane return), the
+  // plane itself over grid.x.
+  const int64_t gy = std::min<int64_t>(planes, 65535);
+  const int64_t gz = (planes + gy - 1) / gy;
+  if (gz > 65535)
+    return bad("cim22_cuda_channel_affine_nchw");
+  const unsigned gx = static_cast<unsigned>(std::min<int64_t>((hw + 255) / 256, 64));
+  affine_nchw_kernel<<<dim3(gx, static_cast<unsigned>(gy), static_cast<unsigned>(gz)), 256, 0,
+                       static_cast<cudaStream_t>(stream)>>>(x, scale, shift, y, planes, c, hw,
+                                                            activation);
+  return launched("channel_affine");
 }
 
 } // extern "C"

@@ -37,28 +37,6 @@ constexpr unsigned kFull = 0xffffffffu;
 // index arithmetic (checked on the host) and the K decomposition hoisted out
 // of the column loop.
 
-// Division by an invariant divisor as a multiply-high and shift (Granlund and
-// Montgomery, "Division by invariant integers using multiplication", 1994):
-// q = (umulhi(n, mul) + n) >> shift for 0 <= n < 2^31, with
-// shift = ceil(log2 d) and mul = floor(2^32 (2^shift - d) / d) + 1.
-struct FastDiv {
-  uint32_t d, mul, shift;
-};
-
-FastDiv make_fastdiv(uint32_t d) {
-  FastDiv f{d, 0, 0};
-  uint32_t l = 0;
-  while ((uint64_t{1} << l) < d)
-    ++l;
-  f.shift = l;
-  f.mul = static_cast<uint32_t>(((uint64_t{1} << 32) * ((uint64_t{1} << l) - d)) / d + 1);
-  return f;
-}
-
-__device__ __forceinline__ int fdiv(int n, const FastDiv &f) {
-  return static_cast<int>((__umulhi(static_cast<uint32_t>(n), f.mul) + static_cast<uint32_t>(n)) >> f.shift);
-}
-
 struct Gather32 {
   FastDiv div_ohw, div_ow, div_khw, div_kw;
   int kind, C, H, W, KH, KW, SH, SW, PH, PW, OH, OW;
@@ -77,12 +55,12 @@ enum PrepareMode { kPrepRows = 0, kPrepConv = 1, kPrepConvPool = 2 };
 // One element at offset `off` of image `img`; with a fused max pool the max
 // over the pool window of the pre-pool image (NaN propagates like
 // torch.max_pool2d).
-template <int kMode>
+template <int kMode, bool kPool2 = false>
 __device__ __forceinline__ float window_load(const float *__restrict__ img, const Gather32 &g,
                                              int off) {
   if (kMode != kPrepConvPool)
     return __ldg(img + off);
-  if (g.PK == 2) {
+  if (kPool2 || g.PK == 2) {
     // The common 2x2 window: four independent loads, then the ordered max.
     const float v0 = __ldg(img + off), v1 = __ldg(img + off + g.pdx);
     const float v2 = __ldg(img + off + g.pdy), v3 = __ldg(img + off + g.pdy + g.pdx);
@@ -313,6 +291,165 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// NCHW convolution gathers: one thread per (column m, K tile t) group. A
+// block serves one K tile and 256 consecutive columns, so a warp's 32 threads
+// read the same kernel tap of 32 neighbouring output pixels - contiguous (or
+// pool-stride spaced) floats of one channel row - and every thread owns its
+// whole 64-element group: the maximum needs no shuffles and the 64 aligned
+// bytes leave as four 16-byte stores. The K decomposition depends on the tile
+// only: the block tabulates its 64 taps (image offset, kernel row, kernel
+// column) in shared memory once, and each thread issues its loads sixteen at
+// a time before converting them. A 4-branch layer keeps the signed BF16 pairs
+// and splits them into the xp/xn branches when aligning: RNE commutes with
+// max(., 0) and negation. The fused-pool form handles 2x2 windows.
+struct Tap {
+  int rel, i, j, valid;
+};
+
+// Branch a of two signed BF16 halves, sign cleared: for a 2-branch layer the
+// value itself (its sign is flagged separately); for a 4-branch layer xp =
+// max(v, 0) (a = 0) or xn = max(-v, 0) (a = 1).
+template <int kActBranches>
+__device__ __forceinline__ uint32_t branch_pair(uint32_t pair, int a) {
+  if (kActBranches == 1)
+    return pair & 0x7fff7fffu;
+  const uint32_t neg = ((pair >> 15) & 0x00010001u) * 0xffffu; // halves with the sign set
+  return (a == 0 ? pair & ~neg : pair & neg) & 0x7fff7fffu;
+}
+
+template <int kActBranches, bool kPool>
+__global__ void __launch_bounds__(256)
+    prepare_nchw_kernel(const float *__restrict__ x, Gather32 g, FastDiv div_chunks, int T,
+                        int m_pad, int k_pad, int8_t *__restrict__ A,
+                        int32_t *__restrict__ ex, int32_t *status) {
+  constexpr int kMode = kPool ? kPrepConvPool : kPrepConv;
+  __shared__ Tap taps[kTileK];
+  const int blk = static_cast<int>(blockIdx.x);
+  const int t = fdiv(blk, div_chunks);
+  const int m = (blk - t * static_cast<int>(div_chunks.d)) * 256 + static_cast<int>(threadIdx.x);
+  const int kbeg = t * kTileK;
+  if (threadIdx.x < kTileK) {
+    const int k = kbeg + static_cast<int>(threadIdx.x);
+    const int c = fdiv(k, g.div_khw);
+    const int rk = k - c * g.KH * g.KW;
+    const int i = fdiv(rk, g.div_kw);
+    const int j = rk - i * g.KW;
+    const bool valid = k < g.K;
+    taps[threadIdx.x] = Tap{valid ? c * g.sC + i * g.sH + j * g.sW : 0, i, j, valid ? 1 : 0};
+  }
+  __syncthreads();
+  if (m >= m_pad)
+    return; // whole warps: m_pad is a multiple of 128
+  const float *img = x;
+  int ih0 = 0, iw0 = 0, org = 0;
+  const bool col_valid = m < g.M;
+  if (col_valid) {
+    const int n = fdiv(m, g.div_ohw);
+    const int rm = m - n * g.OH * g.OW;
+    const int oh = fdiv(rm, g.div_ow);
+    const int ow = rm - oh * g.OW;
+    ih0 = oh * g.SH - g.PH;
+    iw0 = ow * g.SW - g.PW;
+    img = x + static_cast<int64_t>(n) * g.image;
+    org = ih0 * g.sH + iw0 * g.sW;
+  }
+  const bool interior = col_valid && kbeg + kTileK <= g.K && ih0 >= 0 && iw0 >= 0 &&
+                        ih0 + g.KH <= g.H && iw0 + g.KW <= g.W;
+  const bool all_interior = __all_sync(kFull, interior);
+  // Pass 1: gather, round to signed BF16 pairs, track the raw maximum.
+  uint32_t signed_pairs[32];
+  uint32_t raw_max = 0;
+#pragma unroll
+  for (int chunk = 0; chunk < kTileK; chunk += 16) {
+    float v[16];
+    if (all_interior) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        v[e] = window_load<kMode, kPool>(img, g, org + taps[chunk + e].rel);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const Tap tap = taps[chunk + e];
+        v[e] = 0.0f;
+        if (col_valid && tap.valid &&
+            static_cast<unsigned>(ih0 + tap.i) < static_cast<unsigned>(g.H) &&
+            static_cast<unsigned>(iw0 + tap.j) < static_cast<unsigned>(g.W))
+          v[e] = window_load<kMode, kPool>(img, g, org + tap.rel);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+      const int q = (chunk + e) / 2;
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[e], v[e + 1]);
+      signed_pairs[q] = *reinterpret_cast<const uint32_t *>(&h);
+      if (kActBranches == 2)
+        raw_max = max(raw_max, max(__float_as_uint(v[e]) & 0x7fffffffu,
+                                   __float_as_uint(v[e + 1]) & 0x7fffffffu));
+      else
+        raw_max = max(raw_max, max(__float_as_uint(v[e]), __float_as_uint(v[e + 1])));
+    }
+  }
+  uint32_t mx[2] = {0, 0};
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a) {
+    uint32_t m2 = 0;
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      m2 = __vmaxu2(m2, branch_pair<kActBranches>(signed_pairs[e], a));
+    mx[a] = max(m2 & 0xffffu, m2 >> 16);
+  }
+  // Non-finite groups: BF16 exponent 0xff in the 2-branch maximum, |x| of
+  // the raw inputs otherwise (the max with 0 drops NaN).
+  const bool nonfinite = kActBranches == 2 ? raw_max >= 0x7f7f8000u : mx[0] >= 0x7f80u;
+  if (nonfinite)
+    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
+  else if (kActBranches == 1 && raw_max > 0x80000000u)
+    atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
+  // Pass 2: align and store.
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a) {
+    const bool zero = mx[a] == 0 || nonfinite;
+    const int emax = zero ? kZeroGroup : effective_exponent(static_cast<uint16_t>(mx[a]));
+    uint32_t out[16];
+    if (zero) {
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        out[q] = 0;
+    } else if ((mx[a] >> 7) >= 8) {
+      const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax) << 23);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        uint32_t r[4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t pk = branch_pair<kActBranches>(signed_pairs[2 * q + h], a);
+          r[2 * h] = __float_as_uint(__fmaf_rz(__uint_as_float(pk << 16), scale, 8388608.0f));
+          r[2 * h + 1] =
+              __float_as_uint(__fmaf_rz(__uint_as_float(pk & 0xffff0000u), scale, 8388608.0f));
+        }
+        out[q] = pack_low_bytes(r[0], r[1], r[2], r[3]);
+      }
+    } else {
+      const int shift = 127 - emax;
+      for (int q = 0; q < 16; ++q) {
+        uint32_t word = 0;
+        for (int h = 0; h < 4; ++h)
+          word |= slow_align((branch_pair<kActBranches>(signed_pairs[2 * q + h / 2], a) >>
+                              (16 * (h & 1))) & 0xffffu,
+                             shift)
+                  << (8 * h);
+        out[q] = word;
+      }
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad +
+                                           kbeg);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      dst[q] = make_uint4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+    ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax;
+  }
+}
+
 
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == CIM22_ACT_RELU)
@@ -347,7 +484,9 @@ __global__ void __launch_bounds__(256)
                           const int8_t *__restrict__ B,
                           const int32_t *__restrict__ exB, int64_t n_pad,
                           int64_t k_pad, int T, int64_t M, int64_t N,
-                          const float *__restrict__ bias, int act,
+                          const float *__restrict__ bias,
+                          const float *__restrict__ post_scale,
+                          const float *__restrict__ post_shift, int act, int64_t out_pixels,
                           float *__restrict__ y, int32_t *status) {
   constexpr int kBN = 4 * kTC, kTR = 256 / kTC, kBM = kTR * kRM;
   __shared__ __align__(16) int8_t As[kActBranches][kBM][kRowStride];
@@ -511,6 +650,13 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int r = 0; r < kRM; ++r) {
     const int64_t row = m0 + tr + kTR * r;
+    // Rows layout y[row][lane], or NCHW images y[image][lane][pixel].
+    int64_t base = row * N, lane_stride = 1;
+    if (out_pixels > 0) {
+      const int64_t image = row / out_pixels;
+      base = image * N * out_pixels + (row - image * out_pixels);
+      lane_stride = out_pixels;
+    }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const int64_t lane = n0 + tc * 4 + c;
@@ -529,9 +675,11 @@ __global__ void __launch_bounds__(256)
       }
       if (bias != nullptr && lane < N)
         out = __fadd_rn(out, bias[lane]);
+      if (post_scale != nullptr && lane < N)
+        out = __fmaf_rn(out, post_scale[lane], post_shift[lane]);
       out = apply_act(out, act);
       if (row < M && lane < N)
-        y[row * N + lane] = out;
+        y[base + lane * lane_stride] = out;
     }
   }
 }
@@ -543,28 +691,34 @@ template <int kAB>
 void launch_signsplit_simt(const int8_t *A, const int32_t *exA, int64_t m_pad,
                            const int8_t *B, const int32_t *exB, int64_t n_pad,
                            int64_t k_pad, int T, int64_t M, int64_t N,
-                           const float *bias, int act, float *y, int32_t *status,
-                           cudaStream_t s) {
+                           const float *bias, const float *post_scale,
+                           const float *post_shift, int act, int64_t out_pixels, float *y,
+                           int32_t *status, cudaStream_t s) {
   const int64_t target = 2 * 148;
   if (N <= 8) {
     signsplit_simt_kernel<kAB, 2, 1><<<dim3(static_cast<unsigned>(m_pad / 128), 1), 256, 0, s>>>(
-        A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, act, y, status);
+        A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
+          out_pixels, y, status);
   } else if (N <= 16) {
     const unsigned ny = static_cast<unsigned>((N + 15) / 16);
     if ((m_pad / 128) * ny >= target)
       signsplit_simt_kernel<kAB, 4, 2><<<dim3(static_cast<unsigned>(m_pad / 128), ny), 256, 0, s>>>(
-          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, act, y, status);
+          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
+          out_pixels, y, status);
     else
       signsplit_simt_kernel<kAB, 4, 1><<<dim3(static_cast<unsigned>(m_pad / 64), ny), 256, 0, s>>>(
-          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, act, y, status);
+          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
+          out_pixels, y, status);
   } else {
     const unsigned ny = static_cast<unsigned>((N + 31) / 32);
     if ((m_pad / 64) * ny >= target)
       signsplit_simt_kernel<kAB, 8, 2><<<dim3(static_cast<unsigned>(m_pad / 64), ny), 256, 0, s>>>(
-          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, act, y, status);
+          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
+          out_pixels, y, status);
     else
       signsplit_simt_kernel<kAB, 8, 1><<<dim3(static_cast<unsigned>(m_pad / 32), ny), 256, 0, s>>>(
-          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, act, y, status);
+          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
+          out_pixels, y, status);
   }
 }
 
@@ -654,7 +808,7 @@ bool check_gather(const cim22_gather &g, int64_t m, int64_t k) {
   if (g.kind == CIM22_GATHER_ROWS)
     return m * k < (int64_t{1} << 40);
   if (g.pool_kernel < 0 || (g.pool_kernel > 0 &&
-      (g.kind != CIM22_GATHER_CONV_NHWC || g.pool_stride <= 0 ||
+      (g.kind == CIM22_GATHER_ROWS || g.pool_stride <= 0 ||
        (g.pool_src_h - g.pool_kernel) / g.pool_stride + 1 != g.height ||
        (g.pool_src_w - g.pool_kernel) / g.pool_stride + 1 != g.width ||
        g.pool_src_h < g.pool_kernel || g.pool_src_w < g.pool_kernel)))
@@ -671,13 +825,13 @@ bool check_gather(const cim22_gather &g, int64_t m, int64_t k) {
   // The prepare kernel forms element offsets within an image, window
   // origins included, in 32-bit arithmetic: bound every term.
   const int64_t ps = g.pool_kernel > 0 ? g.pool_stride : 1;
+  const int64_t src_h = g.pool_kernel > 0 ? g.pool_src_h : g.height;
+  const int64_t src_w = g.pool_kernel > 0 ? g.pool_src_w : g.width;
   const int64_t reach =
-      (static_cast<int64_t>(g.height) + g.pad_h + g.kernel_h) * ps *
-          (g.pool_kernel > 0 ? g.pool_src_w : g.width) * g.channels +
+      (static_cast<int64_t>(g.height) + g.pad_h + g.kernel_h) * ps * src_w * g.channels +
       (static_cast<int64_t>(g.width) + g.pad_w + g.kernel_w) * ps * g.channels +
-      static_cast<int64_t>(g.channels + 1) *
-          (g.kind == CIM22_GATHER_CONV_NCHW ? static_cast<int64_t>(g.height) * g.width : 1) +
-      static_cast<int64_t>(g.pool_kernel) * (g.pool_src_w + 1) * g.channels;
+      static_cast<int64_t>(g.channels + 1) * src_h * src_w +
+      static_cast<int64_t>(g.pool_kernel) * (src_w + 1) * g.channels;
   if (image >= (int64_t{1} << 30) || reach >= (int64_t{1} << 30))
     return false;
   const int oh = (g.height + 2 * g.pad_h - g.kernel_h) / g.stride_h + 1;
@@ -707,11 +861,19 @@ Gather32 to_device_gather(const cim22_gather &g, int64_t m, int64_t k, const flo
     d.OH = g.out_h;
     d.OW = g.out_w;
     d.PK = g.pool_kernel;
-    if (g.kind == CIM22_GATHER_CONV_NCHW) {
+    if (g.kind == CIM22_GATHER_CONV_NCHW && g.pool_kernel == 0) {
       d.sC = g.height * g.width;
       d.sH = g.width;
       d.sW = 1;
       d.image = g.channels * g.height * g.width;
+    } else if (g.kind == CIM22_GATHER_CONV_NCHW) {
+      // Pooled (ih, iw) starts at pre-pool (ih * PS, iw * PS) of its plane.
+      d.sC = g.pool_src_h * g.pool_src_w;
+      d.sH = g.pool_stride * g.pool_src_w;
+      d.sW = g.pool_stride;
+      d.pdy = g.pool_src_w;
+      d.pdx = 1;
+      d.image = g.channels * g.pool_src_h * g.pool_src_w;
     } else if (g.pool_kernel == 0) {
       d.sC = 1;
       d.sH = g.width * g.channels;
@@ -956,6 +1118,25 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
   int32_t *ex = reinterpret_cast<int32_t *>(
       static_cast<char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
   const Gather32 dg = to_device_gather(g, m, layer->k, x);
+  // The thread-per-group NCHW kernel needs enough columns to fill the GPU;
+  // short column counts (a flatten -> Linear over a small batch) go to the
+  // eight-threads-per-group kernel below.
+  if (g.kind == CIM22_GATHER_CONV_NCHW && (g.pool_kernel == 0 || g.pool_kernel == 2) &&
+      ((m_pad + 255) / 256) * T >= 148 * 2) {
+    const int64_t chunks = (m_pad + 255) / 256;
+    const FastDiv div_chunks = make_fastdiv(static_cast<uint32_t>(chunks));
+    const unsigned blocks = static_cast<unsigned>(chunks * T);
+    auto launch = [&](auto kernel) {
+      kernel<<<blocks, 256, 0, s>>>(x, dg, div_chunks, T, static_cast<int>(m_pad),
+                                    static_cast<int>(layer->k_pad), A, ex, status);
+    };
+    const bool pool = g.pool_kernel > 0;
+    if (ab == 1)
+      launch(pool ? prepare_nchw_kernel<1, true> : prepare_nchw_kernel<1, false>);
+    else
+      launch(pool ? prepare_nchw_kernel<2, true> : prepare_nchw_kernel<2, false>);
+    return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+  }
   // Columns per group thread: as many as still give four waves of 256-thread
   // blocks on a B200 (148 SMs, four resident blocks each).
   int cols = 4;
@@ -982,15 +1163,16 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
   return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
 }
 
-int cim22_cuda_layer_contract_bf16(const cim22_cuda_layer *layer, int64_t m,
-                                   const float *bias, int32_t activation,
-                                   int32_t branches, float *y,
-                                   const void *workspace,
-                                   size_t workspace_bytes, int32_t *status,
-                                   void *stream) {
+int cim22_cuda_layer_contract_bf16_ex(const cim22_cuda_layer *layer, int64_t m,
+                                      int64_t out_pixels, const float *bias,
+                                      const float *post_scale, const float *post_shift,
+                                      int32_t activation, int32_t branches, float *y,
+                                      const void *workspace, size_t workspace_bytes,
+                                      int32_t *status, void *stream) {
   if (!layer || !layer->bf16 || !y || !status || m <= 0 ||
       (branches != 2 && branches != 4) || activation < 0 || activation > 2 ||
-      !workspace ||
+      !workspace || out_pixels < 0 || (out_pixels > 0 && m % out_pixels != 0) ||
+      (post_scale == nullptr) != (post_shift == nullptr) ||
       workspace_bytes < cim22_cuda_layer_workspace_bf16(layer, m, branches)) {
     set_last_error("invalid arguments to cim22_cuda_layer_contract_bf16");
     return CIM22_STATUS_BAD_ARGUMENT;
@@ -1004,16 +1186,50 @@ int cim22_cuda_layer_contract_bf16(const cim22_cuda_layer *layer, int64_t m,
       static_cast<const char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
   if (tc::signsplit_available() &&
       tc::launch_signsplit(A, ex, m_pad, layer->weights, layer->exponents,
-                           layer->n_pad, layer->k_pad, T, m, layer->n, bias,
-                           activation, ab, y, status, s))
+                           layer->n_pad, layer->k_pad, T, m, layer->n, bias, post_scale,
+                           post_shift, activation, ab, out_pixels, y, status, s))
     return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
   if (ab == 1)
     launch_signsplit_simt<1>(A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
-                             layer->k_pad, T, m, layer->n, bias, activation, y, status, s);
+                             layer->k_pad, T, m, layer->n, bias, post_scale, post_shift,
+                             activation, out_pixels, y, status, s);
   else
     launch_signsplit_simt<2>(A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
-                             layer->k_pad, T, m, layer->n, bias, activation, y, status, s);
+                             layer->k_pad, T, m, layer->n, bias, post_scale, post_shift,
+                             activation, out_pixels, y, status, s);
   return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+}
+
+int cim22_cuda_layer_contract_bf16(const cim22_cuda_layer *layer, int64_t m,
+                                   const float *bias, int32_t activation,
+                                   int32_t branches, float *y,
+                                   const void *workspace,
+                                   size_t workspace_bytes, int32_t *status,
+                                   void *stream) {
+  return cim22_cuda_layer_contract_bf16_ex(layer, m, 0, bias, nullptr, nullptr, activation,
+                                           branches, y, workspace, workspace_bytes, status,
+                                           stream);
+}
+
+int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float *x,
+                                     const cim22_gather *gather, int64_t m, int64_t out_pixels,
+                                     const float *bias, const float *post_scale,
+                                     const float *post_shift, int32_t activation,
+                                     int32_t branches, float *y, void *workspace,
+                                     size_t workspace_bytes, int32_t *status, void *stream) {
+  if (!y || activation < 0 || activation > 2 || out_pixels < 0 ||
+      (out_pixels > 0 && m % out_pixels != 0) ||
+      (post_scale == nullptr) != (post_shift == nullptr)) {
+    set_last_error("invalid arguments to cim22_cuda_layer_forward_bf16");
+    return CIM22_STATUS_BAD_ARGUMENT;
+  }
+  const int rc = cim22_cuda_layer_prepare_bf16(layer, x, gather, m, branches, workspace,
+                                               workspace_bytes, status, stream);
+  if (rc)
+    return rc;
+  return cim22_cuda_layer_contract_bf16_ex(layer, m, out_pixels, bias, post_scale, post_shift,
+                                           activation, branches, y, workspace, workspace_bytes,
+                                           status, stream);
 }
 
 int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
@@ -1022,16 +1238,9 @@ int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
                                   int32_t branches, float *y, void *workspace,
                                   size_t workspace_bytes, int32_t *status,
                                   void *stream) {
-  if (!y || activation < 0 || activation > 2) {
-    set_last_error("invalid arguments to cim22_cuda_layer_forward_bf16");
-    return CIM22_STATUS_BAD_ARGUMENT;
-  }
-  const int rc = cim22_cuda_layer_prepare_bf16(layer, x, gather, m, branches, workspace,
-                                               workspace_bytes, status, stream);
-  if (rc)
-    return rc;
-  return cim22_cuda_layer_contract_bf16(layer, m, bias, activation, branches, y, workspace,
-                                        workspace_bytes, status, stream);
+  return cim22_cuda_layer_forward_bf16_ex(layer, x, gather, m, 0, bias, nullptr, nullptr,
+                                          activation, branches, y, workspace, workspace_bytes,
+                                          status, stream);
 }
 
 int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,

@@ -102,13 +102,19 @@ def test_conv_bf16_bit_exact(layout, c, h, f, kk, stride, pad):
 @pytest.mark.parametrize("layout,n,c,h,f,kk,stride,pad,branches,pool", [
     ("nhwc", 64, 16, 32, 64, 3, 1, 1, 4, 0),   # several columns per prepare thread
     ("nhwc", 64, 16, 32, 64, 3, 1, 1, 2, 0),
-    ("nchw", 48, 3, 40, 32, 5, 2, 2, 4, 0),    # K = 75: ragged K tail inside a thread
+    ("nchw", 64, 16, 32, 64, 3, 1, 1, 2, 0),
+    ("nchw", 48, 3, 40, 32, 5, 2, 2, 4, 0),    # K = 75: ragged K tail
     ("nhwc", 32, 8, 34, 48, 3, 2, 0, 2, 0),
+    ("nchw", 40, 6, 14, 16, 5, 1, 0, 2, 2),    # LeNet conv2 shape over a fused pool
+    ("nchw", 64, 32, 16, 32, 3, 1, 1, 4, 2),
     ("nhwc", 64, 32, 16, 32, 3, 1, 1, 4, 2)])  # fused 2x2 max pool over 32x32
-def test_conv_bf16_large_batch_bit_exact(layout, n, c, h, f, kk, stride, pad, branches, pool):
+@pytest.mark.parametrize("out_layout", ["rows", "nchw"])
+def test_conv_bf16_large_batch_bit_exact(layout, n, c, h, f, kk, stride, pad, branches, pool,
+                                         out_layout):
     """Batches large enough that each prepare thread serves several columns
-    and the tensor-core contraction runs, for both layouts, both branch
-    counts, ragged K and a fused max pool."""
+    and the tensor-core contraction runs, for both input layouts, both
+    branch counts, ragged K and a fused max pool, with the output as [m, n]
+    rows or as NCHW planes."""
     from cim22_b200 import abi
     from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace, conv_gather
 
@@ -131,10 +137,15 @@ def test_conv_bf16_large_batch_bit_exact(layout, n, c, h, f, kk, stride, pad, br
     m = n * g.out_h * g.out_w
     out = torch.empty(m, f, device=DEV)
     status = StatusWord(torch.device(DEV))
+    pixels = g.out_h * g.out_w if out_layout == "nchw" else 0
     layer.forward_bf16(xt, out, m, gather=g, bias=torch.from_numpy(b).to(DEV),
-                       branches=branches, workspace=Workspace(torch.device(DEV)), status=status)
+                       branches=branches, out_pixels=pixels,
+                       workspace=Workspace(torch.device(DEV)), status=status)
     status.raise_if_set()
-    got = out.cpu().numpy().reshape(n, g.out_h, g.out_w, f).transpose(0, 3, 1, 2)
+    if out_layout == "nchw":
+        got = out.cpu().numpy().reshape(n, f, g.out_h, g.out_w)
+    else:
+        got = out.cpu().numpy().reshape(n, g.out_h, g.out_w, f).transpose(0, 3, 1, 2)
     np.testing.assert_array_equal(bits(got), bits(expected))
 
 
@@ -196,6 +207,24 @@ def test_glue_against_torch_cpu():
     torch.testing.assert_close(cim_ops.nhwc_to_nchw(xd).cpu(), nchw.contiguous(), rtol=0, atol=0)
     torch.testing.assert_close(cim_ops.nchw_to_nhwc(nchw.contiguous().to(DEV)).cpu(), x,
                                rtol=0, atol=0)
+    # NCHW variants, exact where torch's CPU result is exact.
+    nd = nchw.contiguous().to(DEV)
+    torch.testing.assert_close(cim_ops.maxpool2d_nchw(nd, 2, 2).cpu(),
+                               torch.nn.functional.max_pool2d(nchw, 2, 2), rtol=0, atol=0)
+    torch.testing.assert_close(cim_ops.maxpool2d_nchw(nd, 3, 2, 1).cpu(),
+                               torch.nn.functional.max_pool2d(nchw, 3, 2, 1), rtol=0, atol=0)
+    torch.testing.assert_close(cim_ops.avgpool2d_nchw(nd, 2, 2).cpu(),
+                               torch.nn.functional.avg_pool2d(nchw, 2, 2), **tol)
+    torch.testing.assert_close(cim_ops.global_avgpool_nchw(nd).cpu(), nchw.mean((2, 3)), **tol)
+    torch.testing.assert_close(
+        cim_ops.channel_affine_nchw(nd, scale.to(DEV), shift.to(DEV), "relu").cpu(),
+        torch.relu(nchw * scale[:, None, None] + shift[:, None, None]), **tol)
+    # More planes than one grid dimension holds.
+    big = torch.randn(1100, 64, 2, 2)
+    bs, bb = torch.rand(64) + 0.5, torch.randn(64)
+    torch.testing.assert_close(
+        cim_ops.channel_affine_nchw(big.to(DEV), bs.to(DEV), bb.to(DEV)).cpu(),
+        big * bs[:, None, None] + bb[:, None, None], **tol)
 
 
 @pytest.mark.parametrize("pool", [0, 2])

@@ -33,12 +33,13 @@ def run_program(program, x):
     return [t.cpu().numpy() for t in program.output_tensors]
 
 
+@pytest.mark.parametrize("layout", ["nchw", "nhwc"])
 @pytest.mark.parametrize("name,batch", [("mlp", 8), ("lenet", 6)])
-def test_exact_glue_networks_bit_exact(name, batch):
+def test_exact_glue_networks_bit_exact(name, batch, layout):
     from cim22_b200 import program, workloads
 
     model, x = workloads.build(name, batch)
-    prog = program.from_module(model, x)
+    prog = program.from_module(model, x, layout=layout)
     (got,) = run_program(prog, x)
     expected = oracle.cim_forward(model, x.numpy(), branches=4, threads=8)
     np.testing.assert_array_equal(bits(got), bits(expected))
@@ -67,7 +68,8 @@ def _check_layers(prog):
                 x = x.transpose(0, 3, 1, 2)
             exp = oracle.conv2d_bf16(x, w, b, meta["stride"], meta["pad"], branches=4,
                                      threads=8)
-            exp = exp.transpose(0, 2, 3, 1)
+            if meta["out_layout"] == "nhwc":
+                exp = exp.transpose(0, 2, 3, 1)
         else:
             exp = oracle.linear_bf16(x.reshape(x.shape[0], -1), w, b, branches=4, threads=8)
         assert meta["act"] is None
@@ -77,30 +79,49 @@ def _check_layers(prog):
     return checked
 
 
+@pytest.mark.parametrize("layout", ["nchw", "nhwc"])
 @pytest.mark.parametrize("name,batch,layers", [("resnet18", 1, 21), ("bf16_4x4096", 2, 4),
                                                ("event_cnn", 1, 5)])
-def test_every_cim_layer_bit_exact_on_recorded_inputs(name, batch, layers):
+def test_every_cim_layer_bit_exact_on_recorded_inputs(name, batch, layers, layout):
     from cim22_b200 import program, workloads
 
     model, x = workloads.build(name, batch)
-    prog = program.from_module(model, x, fuse=False)
+    prog = program.from_module(model, x, fuse=False, layout=layout)
     prog.inputs[0].tensor.copy_(x.to(DEV))
     prog.status.reset()
     assert _check_layers(prog) == layers
     prog.check_status()
 
 
+@pytest.mark.parametrize("layout", ["nchw", "nhwc"])
 @pytest.mark.parametrize("name,batch", [("resnet18", 2), ("bf16_4x4096", 3), ("event_cnn", 2)])
-def test_float_glue_networks_within_tolerance(name, batch):
+def test_float_glue_networks_within_tolerance(name, batch, layout):
     from cim22_b200 import program, workloads
 
     model, x = workloads.build(name, batch)
-    prog = program.from_module(model, x)
+    prog = program.from_module(model, x, layout=layout)
     (got,) = run_program(prog, x)
     expected = oracle.cim_forward(model, x.numpy(), branches=4, threads=8)
     scale = np.max(np.abs(expected))
     err = np.max(np.abs(got - expected))
     assert err <= 1e-3 * scale, (err, scale)
+
+
+@pytest.mark.parametrize("layout", ["nchw", "nhwc"])
+def test_fused_epilogues_match_separate_glue(layout):
+    """Batch norm + ReLU folded into the conv epilogues (and pools into the
+    gathers) give the same bits as the separate glue kernels."""
+    from cim22_b200 import program, workloads
+
+    model, x = workloads.build("resnet18", 2)
+    fused = program.from_module(model, x, layout=layout)
+    plain = program.from_module(model, x, fuse=False, layout=layout)
+    names = [s.name for s in fused.steps]
+    assert "batch_norm" not in names, names
+    assert sum(s.name == "batch_norm" for s in plain.steps) == 20
+    (a,) = run_program(fused, x)
+    (b,) = run_program(plain, x)
+    np.testing.assert_array_equal(bits(a), bits(b))
 
 
 def test_torch_compile_cuda_runtime():
