@@ -136,17 +136,23 @@ def reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    import oracle
+    from cim22_b200 import workloads as wl
+
     threads = os.cpu_count() or 1
     # Size each step's sample so the whole run takes about REFERENCE_SECONDS.
     rate, _ = cpu_baseline(args.workload, 2 * threads, threads)
     per_step = int(REFERENCE_SECONDS * rate / max(1, args.steps + args.warmup))
     per_step = max(1, min(args.cpu_sample, 256, per_step))
+    model, x = wl.build(args.workload, per_step, seed=0)
+    xs = x.numpy()
     for _ in range(args.warmup):
-        cpu_baseline(args.workload, per_step, threads)
+        oracle.cim_forward(model, xs, threads=threads, via_runner=True)
     times = []
     for _ in range(args.steps):
-        _, dt = cpu_baseline(args.workload, per_step, threads)
-        times.append(dt)
+        t0 = time.perf_counter()
+        oracle.cim_forward(model, xs, threads=threads, via_runner=True)
+        times.append(time.perf_counter() - t0)
     total = sum(times)
     value = per_step * args.steps / total
     from cim22_b200 import workloads
@@ -307,20 +313,24 @@ def main() -> None:
     elapsed_ms = float(t.item())
     value = world * batch * args.steps / (elapsed_ms / 1000)
 
-    # Per-kernel device time (eager launches, one event pair per kernel).
-    names = [s.name for s in prog.steps]
+    # Per-kernel device time (eager launches, one event pair per kernel);
+    # repeated glue names get an ordinal ("add", "add#2", ...).
+    names, seen = [], {}
+    for s in prog.steps:
+        seen[s.name] = seen.get(s.name, 0) + 1
+        names.append(s.name if seen[s.name] == 1 else f"{s.name}#{seen[s.name]}")
     per = {n: [] for n in names}
     kernel_iters = max(3, min(args.steps, 20))
     for _ in range(kernel_iters):
         flush.zero_()
         prog.status.reset()
         evs = []
-        for step in prog.steps:
+        for n, step in zip(names, prog.steps):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
             step.fn()
             b.record(stream)
-            evs.append((step.name, a, b))
+            evs.append((n, a, b))
         torch.cuda.synchronize(dev)
         for n, a, b in evs:
             per[n].append(a.elapsed_time(b))
@@ -329,8 +339,7 @@ def main() -> None:
     total_kernel = sum(avg.values())
     dominant = max(avg, key=avg.get)
     hbm_peak, bf16_peak, peak_kind = peaks()
-    layer_of = {s.name: s for s in prog.steps}
-    step = layer_of[dominant]
+    step = prog.steps[names.index(dominant)]
     info = next((l for l in prog.layers if dominant.startswith(l.name)), None)
     dur_s = avg[dominant] / 1000
     if step.cim and info is not None:

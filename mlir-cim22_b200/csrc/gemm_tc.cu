@@ -13,8 +13,8 @@
 //
 // Every mbarrier wait is bounded; a wait that runs out sets
 // CIM22_STATUS_TIMEOUT, the CTA stops issuing work, waits (bounded) for the
-// copies it has in flight, frees its TMEM and returns. Loads never use
-// cluster multicast.
+// copies it has in flight, frees its TMEM and returns. Every load is a plain
+// per-CTA copy into this CTA's shared memory.
 #include "gemm_tc.h"
 
 #include "cim_internal.h"
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 //                          per crossbar tile the activation exponents of the
 //                          128 columns, the 2 x L weight scales and the tile's
 //                          weight-exponent range into a 16-slot ring
-//                          (cp.async.bulk, no multicast)
+//                          (cp.async.bulk, per CTA)
 //   warp 1 (one thread)   tcgen05.mma kind::i8 into one of 4 TMEM buffers
 //   warps 2-17            epilogue: warp w reads TMEM lanes 32 * (w % 4) and
 //                          L / 4 of the L lanes; it restores each dot as
@@ -751,11 +751,12 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
                       int64_t N, const float *bias, const float *post_scale,
                       const float *post_shift, int act, int act_branches,
                       int64_t out_pixels, float *y, int32_t *status, cudaStream_t stream) {
-  // Worth it only when the crossbar tiles are wide enough to feed the MMA.
-  // The exponent copies need 16-byte aligned rows: m_pad and n_pad are
-  // multiples of 128 and both exponent arrays start 16-byte aligned.
+  // Layers of at most 8 lanes leave most of a 32- or 64-lane tile idle; the
+  // CUDA-core kernel serves them. The exponent copies need 16-byte aligned
+  // rows: m_pad and n_pad are multiples of 128 and both exponent arrays
+  // start 16-byte aligned.
   const int L = act_branches == 2 ? SSShape<2>::L : SSShape<1>::L;
-  if (N < 32 || M < 512 || m_pad % kSBM || n_pad % 128 || k_pad % 64 ||
+  if (M < 1 || N <= 8 || m_pad % kSBM || n_pad % 128 || k_pad % 64 ||
       static_cast<int64_t>(act_branches) * m_pad >= (int64_t{1} << 31) ||
       (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
       (reinterpret_cast<uintptr_t>(exA) & 15) || (reinterpret_cast<uintptr_t>(exB) & 15))

@@ -318,7 +318,7 @@ __device__ __forceinline__ uint32_t branch_pair(uint32_t pair, int a) {
 }
 
 template <int kActBranches, bool kPool>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, kActBranches == 2 ? 3 : 1)
     prepare_nchw_kernel(const float *__restrict__ x, Gather32 g, FastDiv div_chunks, int T,
                         int m_pad, int k_pad, int8_t *__restrict__ A,
                         int32_t *__restrict__ ex, int32_t *status) {
@@ -362,7 +362,12 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int chunk = 0; chunk < kTileK; chunk += 16) {
     float v[16];
-    if (all_interior) {
+    if (kbeg + chunk >= g.K) {
+      // K padding: zeros, no loads.
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        v[e] = 0.0f;
+    } else if (all_interior) {
 #pragma unroll
       for (int e = 0; e < 16; ++e)
         v[e] = window_load<kMode, kPool>(img, g, org + taps[chunk + e].rel);
