@@ -365,12 +365,14 @@ __device__ __forceinline__ float act_tc(float v, int act) {
 // crossbar tile to the branch sums: the exact three-operation form inside
 // the window (scales read from the exponent slot four at a time), the
 // integer path otherwise.
-template <int kLT>
+// kInit marks the first crossbar tile of an output tile: the sums start at
+// +0, and q * s (exact, nonnegative) is what fma(q, s, +0) gives.
+template <int kLT, bool kInit>
 __device__ __forceinline__ void restore_add(float (&acc)[kLT], const uint32_t (&p)[kLT],
                                             bool fast, float sx, float nsx,
                                             const float *__restrict__ sw,
-                                            const int32_t *__restrict__ ew, int ex,
-                                            int32_t *status) {
+                                            const int32_t *__restrict__ exB, int64_t ew_index,
+                                            int ex, int32_t *status) {
   if (fast) {
 #pragma unroll
     for (int j4 = 0; j4 < kLT; j4 += 4) {
@@ -379,13 +381,104 @@ __device__ __forceinline__ void restore_add(float (&acc)[kLT], const uint32_t (&
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float v = __fmaf_rn(__uint_as_float(p[j4 + j] | 0x4b000000u), sx, nsx);
-        acc[j4 + j] =
-            __fmaf_rn(__uint_as_float(__float_as_uint(v) & 0xffff0000u), s[j], acc[j4 + j]);
+        const float q = __uint_as_float(__float_as_uint(v) & 0xffff0000u);
+        acc[j4 + j] = kInit ? __fmul_rn(q, s[j]) : __fmaf_rn(q, s[j], acc[j4 + j]);
       }
     }
   } else {
     for (int j = 0; j < kLT; ++j)
-      acc[j] = tc_slow_tile_add(acc[j], static_cast<int>(p[j]), ew[j], ex, status);
+      acc[j] = tc_slow_tile_add(kInit ? 0.0f : acc[j], static_cast<int>(p[j]),
+                                exB[ew_index + j], ex, status);
+  }
+}
+
+// Final merge of one output row's LT lanes: BF16 rounding of each branch sum
+// when there is more than one K tile, ((pp - pn) - np) + nn, bias, the
+// optional per-lane fma, the activation, then the store - rows, or NCHW
+// planes where a warp's 32 consecutive rows store 32 consecutive floats of a
+// lane. The branch sums are finite or infinite, never NaN, so the hardware
+// RNE conversion rounds them as the reference's truncf does.
+template <int kAB, int LT>
+__device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, int lane0, int M,
+                                           int N, int T, const float *__restrict__ bias,
+                                           const float *__restrict__ post_scale,
+                                           const float *__restrict__ post_shift, int act,
+                                           int vec, int out_pixels, FastDiv div_pix,
+                                           float *__restrict__ y) {
+  if (row >= M)
+    return;
+  if (T > 1) {
+#pragma unroll
+    for (int a = 0; a < kAB; ++a)
+#pragma unroll
+      for (int w = 0; w < 2; ++w)
+#pragma unroll
+        for (int j = 0; j < LT; j += 2) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(acc[a][w][j], acc[a][w][j + 1]);
+          acc[a][w][j] = __low2float(h);
+          acc[a][w][j + 1] = __high2float(h);
+        }
+  }
+  float o[LT];
+#pragma unroll
+  for (int j = 0; j < LT; ++j) {
+    o[j] = __fsub_rn(acc[0][0][j], acc[0][1][j]);
+    if (kAB == 2)
+      o[j] = __fadd_rn(__fsub_rn(o[j], acc[kAB - 1][0][j]), acc[kAB - 1][1][j]);
+  }
+  const bool full = lane0 + LT <= N;
+  if (bias != nullptr) {
+    if (full && (vec & 1)) {
+#pragma unroll
+      for (int j4 = 0; j4 < LT; j4 += 4) {
+        const float4 b = __ldg(reinterpret_cast<const float4 *>(bias + lane0 + j4));
+        o[j4] = __fadd_rn(o[j4], b.x);
+        o[j4 + 1] = __fadd_rn(o[j4 + 1], b.y);
+        o[j4 + 2] = __fadd_rn(o[j4 + 2], b.z);
+        o[j4 + 3] = __fadd_rn(o[j4 + 3], b.w);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < LT; ++j)
+        if (lane0 + j < N)
+          o[j] = __fadd_rn(o[j], __ldg(bias + lane0 + j));
+    }
+  }
+  if (post_scale != nullptr) {
+#pragma unroll
+    for (int j = 0; j < LT; ++j)
+      if (lane0 + j < N)
+        o[j] = __fmaf_rn(o[j], __ldg(post_scale + lane0 + j), __ldg(post_shift + lane0 + j));
+  }
+  if (act == CIM22_ACT_RELU) {
+#pragma unroll
+    for (int j = 0; j < LT; ++j)
+      o[j] = o[j] > 0.0f ? o[j] : 0.0f;
+  } else if (act == CIM22_ACT_GELU) {
+#pragma unroll
+    for (int j = 0; j < LT; ++j)
+      o[j] = act_tc(o[j], CIM22_ACT_GELU);
+  }
+  if (out_pixels > 0) {
+    const int image = fdiv(row, div_pix);
+    float *dst = y + (static_cast<int64_t>(image) * N + lane0) * out_pixels +
+                 (row - image * out_pixels);
+#pragma unroll
+    for (int j = 0; j < LT; ++j)
+      if (lane0 + j < N)
+        dst[static_cast<int64_t>(j) * out_pixels] = o[j];
+  } else {
+    float *dst = y + static_cast<int64_t>(row) * N + lane0;
+    if (full && (vec & 2)) {
+#pragma unroll
+      for (int j4 = 0; j4 < LT; j4 += 4)
+        *reinterpret_cast<float4 *>(dst + j4) = make_float4(o[j4], o[j4 + 1], o[j4 + 2], o[j4 + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < LT; ++j)
+        if (lane0 + j < N)
+          dst[j] = o[j];
+    }
   }
 }
 
@@ -394,10 +487,11 @@ __global__ void __launch_bounds__(kSThreads, 1)
     signsplit_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const int32_t *__restrict__ exA,
                         int m_pad, const int32_t *__restrict__ exB, int n_pad, int T, int M,
-                        int N, const float *__restrict__ bias,
+                        int N, FastDiv div_nb, const float *__restrict__ bias,
                         const float *__restrict__ post_scale,
                         const float *__restrict__ post_shift, int act, int vec,
-                        int out_pixels, float *__restrict__ y, int32_t *status) {
+                        int out_pixels, FastDiv div_pix, float *__restrict__ y,
+                        int32_t *status) {
   using S = SSShape<kAB>;
   constexpr int L = S::L, LT = S::LT, SN = S::N;
   extern __shared__ uint8_t smem_raw[];
@@ -442,7 +536,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
     uint32_t kbi = 0, gi = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
-      const int m0 = (ot / num_nb) * kSBM, n0 = (ot % num_nb) * L;
+      const int mb = fdiv(ot, div_nb);
+      const int m0 = mb * kSBM, nb = ot - mb * num_nb, n0 = nb * L;
       for (int kb = 0; kb < num_kb; ++kb, ++kbi) {
         const int stage = kbi % kSStages;
         if (!mbar_wait(&s.empty[stage], ((kbi / kSStages) & 1) ^ 1) || *failed) {
@@ -530,16 +625,11 @@ __global__ void __launch_bounds__(kSThreads, 1)
     uint32_t gi = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
-      const int m0 = (ot / num_nb) * kSBM, n0 = (ot % num_nb) * L;
+      const int mb = fdiv(ot, div_nb);
+      const int m0 = mb * kSBM, n0 = (ot - mb * num_nb) * L;
       const int lane0 = n0 + sub * LT;
+      // Written by the first crossbar tile (restore with kInit).
       float acc[kAB][2][LT];
-#pragma unroll
-      for (int a = 0; a < kAB; ++a)
-#pragma unroll
-        for (int w = 0; w < 2; ++w)
-#pragma unroll
-          for (int j = 0; j < LT; ++j)
-            acc[a][w][j] = 0.0f;
       for (int t = 0; t < T; ++t, ++gi) {
         const int slot = gi % kExpSlots, buf = gi % kTmemBufs;
         if (!mbar_wait(&s.exfull[slot], (gi / kExpSlots) & 1) || *failed) {
@@ -552,6 +642,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
           lo = min(lo, e.range[4]);
           hi = max(hi, e.range[5]);
         }
+        // Fast window for this tile's weights: ex_lo <= Ex <= ex_hi.
+        const int ex_lo = max(7, 140 - lo), ex_hi = min(237, 374 - hi);
         float sx[kAB], nsx[kAB];
         bool fast[kAB];
         int ex[kAB];
@@ -559,9 +651,11 @@ __global__ void __launch_bounds__(kSThreads, 1)
         for (int a = 0; a < kAB; ++a) {
           ex[a] = e.a[a][row_local];
           const bool zero = ex[a] == kZeroGroup;
-          fast[a] = zero ||
-                    (ex[a] >= 7 && ex[a] <= 237 && ex[a] + lo >= 140 && ex[a] + hi <= 374);
-          sx[a] = zero || !fast[a] ? 0.0f : exp2i(ex[a] - 133);
+          const bool window = ex[a] >= ex_lo && ex[a] <= ex_hi;
+          fast[a] = zero || window;
+          // 2^(Ex - 133), a normal f32 inside the window (Ex >= 7).
+          sx[a] = window && !zero ? __uint_as_float(static_cast<uint32_t>(ex[a] - 6) << 23)
+                                  : 0.0f;
           nsx[a] = -8388608.0f * sx[a];
         }
         if (!mbar_wait(&s.dfull[buf], (gi / kTmemBufs) & 1) || *failed) {
@@ -570,8 +664,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t col0 = tmem + tlane + buf * kBufCols + sub * LT;
-        const int32_t *ew0 = exB + static_cast<int64_t>(t) * n_pad + lane0;
-        const int32_t *ew1 = exB + (static_cast<int64_t>(T) + t) * n_pad + lane0;
+        // Index of this thread's weight exponents exB[w][t][lane0] (exact path).
+        const int64_t ew0 = static_cast<int64_t>(t) * n_pad + lane0;
+        const int64_t ew1 = ew0 + static_cast<int64_t>(T) * n_pad;
         // One activation branch at a time: 2 x LT dots in registers.
 #pragma unroll
         for (int a = 0; a < kAB; ++a) {
@@ -587,10 +682,17 @@ __global__ void __launch_bounds__(kSThreads, 1)
             if (lane == 0)
               mbar_arrive(&s.dempty[buf]);
           }
-          restore_add<LT>(acc[a][0], p0, fast[a], sx[a], nsx[a], &e.w[0][sub * LT], ew0, ex[a],
-                          status);
-          restore_add<LT>(acc[a][1], p1, fast[a], sx[a], nsx[a], &e.w[1][sub * LT], ew1, ex[a],
-                          status);
+          if (t == 0) {
+            restore_add<LT, true>(acc[a][0], p0, fast[a], sx[a], nsx[a], &e.w[0][sub * LT],
+                                  exB, ew0, ex[a], status);
+            restore_add<LT, true>(acc[a][1], p1, fast[a], sx[a], nsx[a], &e.w[1][sub * LT],
+                                  exB, ew1, ex[a], status);
+          } else {
+            restore_add<LT, false>(acc[a][0], p0, fast[a], sx[a], nsx[a], &e.w[0][sub * LT],
+                                   exB, ew0, ex[a], status);
+            restore_add<LT, false>(acc[a][1], p1, fast[a], sx[a], nsx[a], &e.w[1][sub * LT],
+                                   exB, ew1, ex[a], status);
+          }
         }
         __syncwarp();
         if (lane == 0)
@@ -598,69 +700,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
       }
       if (!ok)
         break;
-      const int row = m0 + row_local;
-      if (row < M) {
-        // Rows layout: y[row][lane]. NCHW layout: y[image][lane][pixel] with
-        // row = image * out_pixels + pixel, so a warp's 32 consecutive rows
-        // store 32 consecutive floats of one lane.
-        int64_t base = static_cast<int64_t>(row) * N + lane0, lane_stride = 1;
-        if (out_pixels > 0) {
-          const int image = row / out_pixels;
-          base = (static_cast<int64_t>(image) * N + lane0) * out_pixels + (row - image * out_pixels);
-          lane_stride = out_pixels;
-        }
-        float *dst = y + base;
-        const bool full = lane0 + LT <= N;
-        const bool bias_vec = full && (vec & 1);
-        const bool store_vec = full && (vec & 2) && out_pixels == 0;
-#pragma unroll
-        for (int j4 = 0; j4 < LT; j4 += 4) {
-          float b4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-          if (bias != nullptr) {
-            if (bias_vec) {
-              const float4 v = __ldg(reinterpret_cast<const float4 *>(bias + lane0 + j4));
-              b4[0] = v.x; b4[1] = v.y; b4[2] = v.z; b4[3] = v.w;
-            } else {
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                if (lane0 + j4 + j < N)
-                  b4[j] = __ldg(bias + lane0 + j4 + j);
-            }
-          }
-          float o[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            // Branch sums are finite or infinite, never NaN: the hardware
-            // RNE conversion rounds them as the reference's truncf does.
-            float br[kAB][2];
-#pragma unroll
-            for (int a = 0; a < kAB; ++a)
-#pragma unroll
-              for (int w = 0; w < 2; ++w)
-                br[a][w] = T > 1 ? __bfloat162float(__float2bfloat16_rn(acc[a][w][j4 + j]))
-                                 : acc[a][w][j4 + j];
-            float out = __fsub_rn(br[0][0], br[0][1]);
-            if (kAB == 2) {
-              out = __fsub_rn(out, br[1][0]);
-              out = __fadd_rn(out, br[1][1]);
-            }
-            if (bias != nullptr)
-              out = __fadd_rn(out, b4[j]);
-            if (post_scale != nullptr && lane0 + j4 + j < N)
-              out = __fmaf_rn(out, __ldg(post_scale + lane0 + j4 + j),
-                              __ldg(post_shift + lane0 + j4 + j));
-            o[j] = act_tc(out, act);
-          }
-          if (store_vec) {
-            *reinterpret_cast<float4 *>(dst + j4) = make_float4(o[0], o[1], o[2], o[3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              if (lane0 + j4 + j < N)
-                dst[(j4 + j) * lane_stride] = o[j];
-          }
-        }
-      }
+      store_tile<kAB, LT>(acc, m0 + row_local, lane0, M, N, T, bias, post_scale, post_shift,
+                          act, vec, out_pixels, div_pix, y);
     }
     if (!ok) {
       *failed = 1;
@@ -775,11 +816,12 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
       return false;
-    kernel<<<grid, kSThreads, smem, stream>>>(ta, tb, exA, static_cast<int>(m_pad), exB,
-                                              static_cast<int>(n_pad), T, static_cast<int>(M),
-                                              static_cast<int>(N), bias, post_scale,
-                                              post_shift, act, vec,
-                                              static_cast<int>(out_pixels), y, status);
+    kernel<<<grid, kSThreads, smem, stream>>>(
+        ta, tb, exA, static_cast<int>(m_pad), exB, static_cast<int>(n_pad), T,
+        static_cast<int>(M), static_cast<int>(N),
+        make_fastdiv(static_cast<uint32_t>((N + L - 1) / L)), bias, post_scale, post_shift, act,
+        vec, static_cast<int>(out_pixels),
+        make_fastdiv(static_cast<uint32_t>(out_pixels > 0 ? out_pixels : 1)), y, status);
     return true;
   };
   if (!(act_branches == 2 ? launch(signsplit_tc_kernel<2>, smem_ss<2>())

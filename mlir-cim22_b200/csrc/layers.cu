@@ -362,15 +362,15 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 3 : 1)
 #pragma unroll
   for (int chunk = 0; chunk < kTileK; chunk += 16) {
     float v[16];
-    if (kbeg + chunk >= g.K) {
+    if (all_interior) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        v[e] = window_load<kMode, kPool>(img, g, org + taps[chunk + e].rel);
+    } else if (kbeg + chunk >= g.K) {
       // K padding: zeros, no loads.
 #pragma unroll
       for (int e = 0; e < 16; ++e)
         v[e] = 0.0f;
-    } else if (all_interior) {
-#pragma unroll
-      for (int e = 0; e < 16; ++e)
-        v[e] = window_load<kMode, kPool>(img, g, org + taps[chunk + e].rel);
     } else {
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
