@@ -119,6 +119,17 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
+def ncu_traffic(workload: str, batch: int, step: str):
+    """DRAM bytes per launch (read + write) of a step's kernel from a committed
+    ncu launch-list summary (profiles/traffic.json), or (None, None)."""
+    try:
+        table = json.loads((REPO / "profiles" / "traffic.json").read_text())
+        entry = table[f"{workload}_b{batch}"]
+        return entry["kernels"][step], entry["source"]
+    except (OSError, KeyError, ValueError):
+        return None, None
+
+
 def cpu_baseline(workload: str, sample: int, threads: int, batch_seed: int = 0):
     """Oracle port of the reference's software runner on host cores."""
     import oracle
@@ -354,14 +365,18 @@ def main() -> None:
     else:
         algo = None
         if info is not None and dominant.endswith(".prepare"):
+            # Read the source tensor once; write the prepared int8 columns and
+            # their group exponents (m_pad x (k_pad + 4 T) per activation branch).
             ab = 1 if info.branches == 2 else 2
             t_tiles = -(-info.k // 64)
-            algo = 4 * info.m * info.k + ab * info.m * t_tiles * (64 + 4)
+            m_pad = -(-info.m // 128) * 128
+            algo = info.in_bytes + ab * m_pad * t_tiles * (64 + 4)
         gbs = (algo / dur_s / 1e9) if algo else None
         roof = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
                 "frac": (gbs / hbm_peak) if gbs else None, "traffic": None, "kernel": dominant,
                 "bytes_per_launch": algo, "launch_ms": avg[dominant],
                 "peak_note": f"{peak_kind} HBM copy bandwidth"}
+    roof["traffic"], roof["traffic_source"] = ncu_traffic(args.workload, batch, dominant)
     kernel_table = {n: {"ms": round(avg[n], 5), "share": round(avg[n] / total_kernel, 4)}
                     for n in names}
 

@@ -72,6 +72,7 @@ class LayerInfo:
     n: int
     branches: int
     macs: int
+    in_bytes: int = 0  # bytes of the source tensor the prepare kernel gathers from
 
 
 _CONV = {torch.conv2d, F.conv2d}
@@ -378,7 +379,8 @@ class Program:
             bias=None if b is None else torch.as_tensor(b).detach().float(), stride=stride[0],
             pad=pad[0], out=out, act=act, branches=branches)))
         self.layers.append(LayerInfo(name, "conv", m, c * kh * kw, f, branches,
-                                     branches * m * c * kh * kw * f))
+                                     branches * m * c * kh * kw * f,
+                                     xt.numel() * xt.element_size()))
         env[out_node] = Val(IMAGE, (n, f, g.out_h, g.out_w), out, self.layout,
                             nonneg=act == "relu")
 
@@ -420,7 +422,8 @@ class Program:
             kind="linear", x=xt, weight=torch.as_tensor(w).detach().float(),
             bias=None if b is None else torch.as_tensor(b).detach().float(), out=out, act=act,
             branches=branches)))
-        self.layers.append(LayerInfo(name, "linear", m, k, n, branches, branches * m * k * n))
+        self.layers.append(LayerInfo(name, "linear", m, k, n, branches, branches * m * k * n,
+                                     xt.numel() * xt.element_size()))
         env[out_node] = Val(MATRIX, (m, n), out, nonneg=act == "relu")
 
     def _lower_int_mm(self, node, args, env) -> None:
