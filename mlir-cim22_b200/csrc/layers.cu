@@ -1123,11 +1123,13 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
   int32_t *ex = reinterpret_cast<int32_t *>(
       static_cast<char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
   const Gather32 dg = to_device_gather(g, m, layer->k, x);
-  // The thread-per-group NCHW kernel needs enough columns to fill the GPU;
-  // short column counts (a flatten -> Linear over a small batch) go to the
-  // eight-threads-per-group kernel below.
+  // The thread-per-group NCHW kernel serves layers of few K tiles (small
+  // channel counts, K padding) over enough columns to fill the GPU; layers of
+  // nine or more tiles and short column counts (a flatten -> Linear over a
+  // small batch) go to the eight-threads-per-group kernel below, which was
+  // measured faster there.
   if (g.kind == CIM22_GATHER_CONV_NCHW && (g.pool_kernel == 0 || g.pool_kernel == 2) &&
-      ((m_pad + 255) / 256) * T >= 148 * 2) {
+      T < 9 && ((m_pad + 255) / 256) * T >= 148 * 2) {
     const int64_t chunks = (m_pad + 255) / 256;
     const FastDiv div_chunks = make_fastdiv(static_cast<uint32_t>(chunks));
     const unsigned blocks = static_cast<unsigned>(chunks * T);
