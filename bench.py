@@ -55,6 +55,10 @@ def parse():
                    help="INT8 CIM MVM sweep (M x K=N grid): TOPS vs the int8 tensor peak")
     p.add_argument("--sweep-m", default="1,16,128,1024,8192")
     p.add_argument("--sweep-kn", default="256,1024,4096,8192")
+    p.add_argument("--parallel", default="batch", choices=["batch", "columns"],
+                   help="batch: every rank runs its own batch (weak scaling); columns: every "
+                        "Linear layer's output lanes are split over the ranks, outputs "
+                        "all-gathered (strong scaling; Linear stacks such as bf16_4x4096)")
     p.add_argument("--profile", action="store_true",
                    help="only launch the program's kernels eagerly (warmup + steps passes); "
                         "for capturing single kernels under a profiler")
@@ -250,6 +254,121 @@ def layer_launch(layer, x, out, m, ws, status):
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "forward_int8")
 
 
+def column_bench(args, world: int, rank: int, local: int, dev) -> None:
+    """Column-sharded Linear stack: every rank computes 1/world of each layer's
+    lanes for all rows; outputs are all-gathered over NCCL. One step = one
+    forward of the whole batch; value = rows per second for the whole job."""
+    import torch
+    import torch.distributed as dist
+
+    from cim22_b200 import workloads
+    from cim22_b200.sharding import ColumnShardedStack
+
+    w = workloads.WORKLOADS[args.workload]
+    rows = args.batch or w.batch
+    model, x = workloads.build(args.workload, rows, seed=0)
+    if args.workload != "bf16_4x4096":
+        raise SystemExit("--parallel columns is defined for the bf16_4x4096 Linear stack")
+    linears = [m for m in model.modules() if isinstance(m, torch.nn.Linear)]
+    acts = ["gelu"] * (len(linears) - 1) + [None]  # GELU between the layers
+    stack = ColumnShardedStack([l.weight.detach() for l in linears],
+                               [None if l.bias is None else l.bias.detach() for l in linears],
+                               acts, rows, device=local)
+    xd = x.to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        stack(xd)
+    stack.check_status()
+    barrier()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler([local] if world == 1 else range(world)) as clocks:
+        barrier()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            stack(xd)
+            ends[i].record(stream)
+        barrier()
+    stack.check_status()
+    t = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts, ends))], device=dev,
+                     dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(t.item())
+    value = rows * args.steps / (elapsed_ms / 1000)
+
+    # End to end: rows from pinned host memory, the output read back each step.
+    host = x.pin_memory()
+    e_ms = 0.0
+    out = None
+    barrier()
+    for _ in range(args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        out = stack(host.to(dev, non_blocking=True)).cpu()
+        b.record(stream)
+        b.synchronize()
+        e_ms += a.elapsed_time(b)
+    stack.check_status()
+    et = torch.tensor([e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e_value = rows * args.steps / (float(et.item()) / 1000)
+
+    # Per-rank contraction of the first layer, timed alone (tensor roofline).
+    layer = stack.layers[0]
+    per = []
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        layer.prepare_bf16(xd, rows, branches=4, workspace=stack.workspace, status=stack.status)
+        a.record(stream)
+        layer.contract_bf16(stack.local[0], rows, activation="gelu", branches=4,
+                            workspace=stack.workspace, status=stack.status)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        per.append(a.elapsed_time(b))
+    stack.check_status()
+    launch_ms = sorted(per)[len(per) // 2]
+    ops = 2 * 4 * rows * layer.k * stack.plans[0].block
+    hbm_peak, bf16_peak, peak_kind = peaks()
+    achieved = ops / (launch_ms / 1000) / 1e12
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{args.workload}: {w.description}", "global_batch": rows,
+                       "parallelism": f"column-sharded x{world} (lanes split, NCCL all-gather "
+                                      f"per layer)",
+                       "l2": "flushed between steps (256 MiB write, outside the timed span)",
+                       "graph": "eager launches"},
+            "gpu_launches": 3 * len(stack.layers) * args.steps,
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": host.numel() * host.element_size(),
+                    "d2h_bytes_per_step": out.numel() * out.element_size()},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": 2 * bf16_peak,
+                         "unit": "TFLOP/s", "frac": achieved / (2 * bf16_peak), "traffic": None,
+                         "kernel": "linear0 (local lanes)", "launch_ms": launch_ms,
+                         "peak_note": f"int8 dense = 2 x {peak_kind} bf16 cuBLAS"},
+            "cpu_baseline": None,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
@@ -273,6 +392,10 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     from cim22_b200 import backend, program, workloads
+
+    if args.parallel == "columns":
+        column_bench(args, world, rank, local, dev)
+        return
 
     w = workloads.WORKLOADS[args.workload]
     batch = args.batch or w.batch

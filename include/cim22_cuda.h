@@ -485,6 +485,13 @@ int cim22_cuda_nhwc_to_nchw(const float *x, float *y, int32_t n, int32_t h,
 /* NCHW -> NHWC. */
 int cim22_cuda_nchw_to_nhwc(const float *x, float *y, int32_t n, int32_t c,
                             int32_t h, int32_t w, void *stream);
+/* No counterpart in the reference (it runs on one host): reassembles a
+ * layer whose output lanes are split over `ranks` devices. src is what an
+ * all-gather of the per-rank [rows][cols] outputs stacks, [ranks][rows][cols];
+ * dst is [rows][total] with rank r's block in columns r*cols .. r*cols+cols-1
+ * (trailing blocks may be padded: columns at or past total are dropped). */
+int cim22_cuda_unshard_columns(const float *src, float *dst, int32_t ranks, int64_t rows,
+                               int64_t cols, int64_t total, void *stream);
 /* The pooling and affine glue on NCHW batches [n, c, h, w]. */
 int cim22_cuda_maxpool2d_nchw(const float *x, float *y, int32_t n, int32_t c,
                               int32_t h, int32_t w, int32_t kernel,

@@ -302,6 +302,16 @@ def channel_affine_nchw(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tenso
     return out
 
 
+def unshard_columns(src: torch.Tensor, total: int,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """[ranks, rows, cols] blocks (an all-gather's stacking) -> [rows, total]."""
+    ranks, rows, cols = src.shape
+    out = torch.empty(rows, total, dtype=src.dtype, device=src.device) if out is None else out
+    check(lib().cim22_cuda_unshard_columns(_ptr(src), _ptr(out), ranks, rows, cols, total,
+                                           _stream(src.device)), "unshard_columns")
+    return out
+
+
 def softmax(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     cols = x.shape[-1]
     out = torch.empty_like(x) if out is None else out

@@ -309,6 +309,22 @@ __global__ void affine_nchw_kernel(const float *__restrict__ x, const float *__r
     dst[i] = act_fn(fmaf(src[i], sc, sh), act);
 }
 
+// Column-shard reassembly: src holds `ranks` blocks [rank][rows][cols] as an
+// all-gather stacks them; dst is [rows][total] with block r in columns
+// [r * cols, r * cols + cols) (columns at or past `total` are the last
+// block's padding and are dropped).
+__global__ void unshard_columns_kernel(const float *__restrict__ src, float *__restrict__ dst,
+                                       int ranks, int64_t rows, int64_t cols, int64_t total) {
+  const int64_t count = rows * total;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += stride) {
+    const int64_t row = i / total, col = i - row * total;
+    const int64_t r = col / cols, j = col - r * cols;
+    dst[i] = src[(r * rows + row) * cols + j];
+  }
+}
+
 int launched(const char *what) {
   return cuda_ok(cudaGetLastError(), what) ? 0 : CIM22_STATUS_BAD_ARGUMENT;
 }
@@ -435,6 +451,18 @@ int cim22_cuda_nchw_to_nhwc(const float *x, float *y, int32_t n, int32_t c,
   nchw_to_nhwc_kernel<<<grid_for(static_cast<int64_t>(n) * h * w * c), 256, 0,
                         static_cast<cudaStream_t>(stream)>>>(x, y, n, c, h, w);
   return launched("nchw_to_nhwc");
+}
+
+int cim22_cuda_unshard_columns(const float *src, float *dst, int32_t ranks, int64_t rows,
+                               int64_t cols, int64_t total, void *stream) {
+  if (!src || !dst || ranks <= 0 || rows < 0 || cols <= 0 || total <= 0 ||
+      total > static_cast<int64_t>(ranks) * cols)
+    return bad("cim22_cuda_unshard_columns");
+  if (rows == 0)
+    return 0;
+  unshard_columns_kernel<<<grid_for(rows * total), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      src, dst, ranks, rows, cols, total);
+  return launched("unshard_columns");
 }
 
 int cim22_cuda_maxpool2d_nchw(const float *x, float *y, int32_t n, int32_t c,
