@@ -66,10 +66,14 @@ class ColumnShardPlan:
 
 
 def gather_blocks(local: torch.Tensor, gathered: torch.Tensor, group=None) -> None:
-    """All-gather each rank's [rows, block] output into gathered [world, rows, block]."""
+    """All-gather each rank's [rows, block] output into gathered [world, rows, block]
+    (a copy when there is one rank and no process group)."""
     world, rows, block = gathered.shape
     if tuple(local.shape) != (rows, block):
         raise ValueError(f"local block {tuple(local.shape)} does not match {(rows, block)}")
+    if world == 1 and not dist.is_initialized():
+        gathered[0].copy_(local)
+        return
     dist.all_gather_into_tensor(gathered.view(world * rows, block), local, group=group)
 
 
@@ -86,8 +90,10 @@ class ColumnShardedStack:
         if not (len(weights) == len(biases) == len(activations)) or not weights:
             raise ValueError("one bias and one activation per weight")
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        if dist.is_initialized():
+            self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        else:
+            self.rank, self.world = 0, 1
         self.device = torch.device("cuda", device) if isinstance(device, int) else device
         self.rows = rows
         self.workspace = Workspace(self.device)
