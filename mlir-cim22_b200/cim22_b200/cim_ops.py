@@ -98,6 +98,11 @@ class CimLayer:
             pass
 
     @property
+    def fused_forward(self) -> bool:
+        """forward_bf16 runs as one kernel (gather + prealign + contraction)."""
+        return bool(lib().cim22_cuda_layer_fused_forward(self._handle))
+
+    @property
     def range_safe(self) -> bool:
         return bool(lib().cim22_cuda_layer_range_safe(self._handle))
 

@@ -370,8 +370,17 @@ class Program:
                                 post_shift=post_shift, workspace=self.workspace,
                                 status=self.status)
 
+        def fused():
+            layer.forward_bf16(xt, out, m, gather=g, bias=bias, activation=act,
+                               branches=branches, out_pixels=pixels, post_scale=post_scale,
+                               post_shift=post_shift, workspace=self.workspace,
+                               status=self.status)
+
         name = f"conv{len(self.layers)}"
-        self.steps.append(Step(name + ".prepare", prepare))
+        if layer.fused_forward and self.fuse:
+            run = fused  # one kernel: gather, prealign and contraction
+        else:
+            self.steps.append(Step(name + ".prepare", prepare))
         self.steps.append(Step(name, run, cim=True, meta=dict(
             kind="conv", x=xt, layout=x.layout, out_layout=self.layout,
             post=None if post_scale is None else (post_scale, post_shift),
@@ -416,8 +425,15 @@ class Program:
             layer.contract_bf16(out, m, bias=bias, activation=act, branches=branches,
                                 workspace=self.workspace, status=self.status)
 
+        def fused():
+            layer.forward_bf16(xt, out, m, gather=g, bias=bias, activation=act,
+                               branches=branches, workspace=self.workspace, status=self.status)
+
         name = f"linear{len(self.layers)}"
-        self.steps.append(Step(name + ".prepare", prepare))
+        if layer.fused_forward and self.fuse:
+            run = fused  # one kernel: gather, prealign and contraction
+        else:
+            self.steps.append(Step(name + ".prepare", prepare))
         self.steps.append(Step(name, run, cim=True, meta=dict(
             kind="linear", x=xt, weight=torch.as_tensor(w).detach().float(),
             bias=None if b is None else torch.as_tensor(b).detach().float(), out=out, act=act,

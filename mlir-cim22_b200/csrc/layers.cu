@@ -25,6 +25,7 @@
 #include <climits>
 #include <cmath>
 #include <cstring>
+#include <type_traits>
 #include <vector>
 
 namespace cim {
@@ -116,6 +117,184 @@ __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint3
 // exponent is always 127.
 constexpr int kGroupThreads = 8;
 
+// The eight K indices kbeg .. kbeg+7 of one thread: image offsets (channel,
+// kernel row, kernel column) relative to a window origin, and which are < K.
+struct Taps8 {
+  int rel[8], di[8], dj[8];
+  unsigned kvalid;
+};
+
+template <int kMode>
+__device__ __forceinline__ Taps8 make_taps8(const Gather32 &g, int kbeg) {
+  Taps8 tp;
+  tp.kvalid = 0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    tp.kvalid |= (kbeg + e < g.K ? 1u : 0u) << e;
+  if (kMode != kPrepRows) {
+    int c = fdiv(kbeg, g.div_khw);
+    const int rk = kbeg - c * g.KH * g.KW;
+    int i = fdiv(rk, g.div_kw);
+    int j = rk - i * g.KW;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      tp.rel[e] = c * g.sC + i * g.sH + j * g.sW;
+      tp.di[e] = i;
+      tp.dj[e] = j;
+      if (++j == g.KW) {
+        j = 0;
+        if (++i == g.KH) {
+          i = 0;
+          ++c;
+        }
+      }
+    }
+  }
+  return tp;
+}
+
+// The eight gathered values of column m at the thread's taps (zero for
+// padding columns, padding K and conv padding).
+template <int kMode>
+__device__ __forceinline__ void gather8(const float *__restrict__ x, const Gather32 &g,
+                                        const Taps8 &tp, int m, int kbeg, float (&v)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    v[e] = 0.0f;
+  if (m >= g.M || !tp.kvalid)
+    return;
+  if (kMode == kPrepRows) {
+    const float *row = x + static_cast<int64_t>(m) * g.K;
+    if (g.pair_rows == 2 && tp.kvalid == 0xffu) {
+      const float4 *src = reinterpret_cast<const float4 *>(row + kbeg);
+      const float4 lo = __ldg(src), hi = __ldg(src + 1);
+      v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
+      v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if ((tp.kvalid >> e) & 1u)
+          v[e] = __ldg(row + kbeg + e);
+    }
+    return;
+  }
+  const int n = fdiv(m, g.div_ohw);
+  const int rm = m - n * g.OH * g.OW;
+  const int oh = fdiv(rm, g.div_ow);
+  const int ow = rm - oh * g.OW;
+  const int ih0 = oh * g.SH - g.PH, iw0 = ow * g.SW - g.PW;
+  const float *img = x + static_cast<int64_t>(n) * g.image;
+  const int org = ih0 * g.sH + iw0 * g.sW;
+  if (tp.kvalid == 0xffu && ih0 >= 0 && iw0 >= 0 && ih0 + g.KH <= g.H && iw0 + g.KW <= g.W) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      v[e] = window_load<kMode>(img, g, org + tp.rel[e]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (((tp.kvalid >> e) & 1u) &&
+          static_cast<unsigned>(ih0 + tp.di[e]) < static_cast<unsigned>(g.H) &&
+          static_cast<unsigned>(iw0 + tp.dj[e]) < static_cast<unsigned>(g.W))
+        v[e] = window_load<kMode>(img, g, org + tp.rel[e]);
+  }
+}
+
+// Split, round and prealign the thread's eight values of a group shared by
+// the eight lanes of `mask` (sub = lane within them): out[a] holds the eight
+// aligned bytes of activation branch a, emax[a] the group exponent
+// (kZeroGroup for an all-zero group).
+//
+// Split and round: xp = max(x, 0), xn = max(-x, 0) equal the reference's
+// selects for every non-NaN x up to the sign of zero, which the preparation
+// clears anyway (BF16Compensation.cpp:97). cvt.rn.bf16x2.f32 rounds to
+// nearest even, as arith.truncf does. NaN, infinity and finite values that
+// round to BF16 infinity (|x| >= 0x1.fep127) mark the group non-finite:
+// through the BF16 exponent 0xff of the maximum for a 2-branch layer, through
+// |x| of the raw inputs otherwise (the max with 0 drops NaN).
+template <int kActBranches>
+__device__ __forceinline__ void convert8(const float (&v)[8], unsigned mask, int sub,
+                                         int32_t *status, uint2 (&out)[2], int (&emax)[2]) {
+  uint32_t packed[2][4];
+  uint32_t mx[2] = {0, 0};
+  bool negative = false;
+  if (kActBranches == 2) {
+    uint32_t amax = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      amax = max(amax, __float_as_uint(v[e]) & 0x7fffffffu);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const __nv_bfloat162 hp = __floats2bfloat162_rn(fmaxf(v[e], 0.0f), fmaxf(v[e + 1], 0.0f));
+      const __nv_bfloat162 hn =
+          __floats2bfloat162_rn(fmaxf(-v[e], 0.0f), fmaxf(-v[e + 1], 0.0f));
+      packed[0][e / 2] = *reinterpret_cast<const uint32_t *>(&hp) & 0x7fff7fffu;
+      packed[kActBranches - 1][e / 2] = *reinterpret_cast<const uint32_t *>(&hn) & 0x7fff7fffu;
+    }
+#pragma unroll
+    for (int a = 0; a < kActBranches; ++a) {
+      const uint32_t m2 = __vmaxu2(__vmaxu2(packed[a][0], packed[a][1]),
+                                   __vmaxu2(packed[a][2], packed[a][3]));
+      mx[a] = max(m2 & 0xffffu, m2 >> 16);
+    }
+    if (amax >= 0x7f7f8000u)
+      mx[0] = 0xffffu;
+  } else {
+    uint32_t umax = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      umax = max(umax, __float_as_uint(v[e]));
+    negative = umax > 0x80000000u;
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const __nv_bfloat162 hp = __floats2bfloat162_rn(v[e], v[e + 1]);
+      packed[0][e / 2] = *reinterpret_cast<const uint32_t *>(&hp) & 0x7fff7fffu;
+    }
+    const uint32_t m2 = __vmaxu2(__vmaxu2(packed[0][0], packed[0][1]),
+                                 __vmaxu2(packed[0][2], packed[0][3]));
+    mx[0] = max(m2 & 0xffffu, m2 >> 16);
+  }
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a)
+#pragma unroll
+    for (int o = 4; o; o >>= 1)
+      mx[a] = max(mx[a], __shfl_xor_sync(mask, mx[a], o, kGroupThreads));
+  const bool nonfinite = mx[0] >= 0x7f80u;
+  if (sub == 0 && nonfinite)
+    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
+  if (negative && !nonfinite)
+    atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a) {
+    const bool zero = mx[a] == 0 || nonfinite;
+    emax[a] = zero ? kZeroGroup : effective_exponent(static_cast<uint16_t>(mx[a]));
+    uint32_t lo = 0, hi = 0;
+    if (!zero) {
+      if ((mx[a] >> 7) >= 8) {
+        const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax[a]) << 23);
+        uint32_t q[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          q[2 * e] = __float_as_uint(
+              __fmaf_rz(__uint_as_float(packed[a][e] << 16), scale, 8388608.0f));
+          q[2 * e + 1] = __float_as_uint(
+              __fmaf_rz(__uint_as_float(packed[a][e] & 0xffff0000u), scale, 8388608.0f));
+        }
+        lo = pack_low_bytes(q[0], q[1], q[2], q[3]);
+        hi = pack_low_bytes(q[4], q[5], q[6], q[7]);
+      } else {
+        const int shift = 127 - emax[a];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          lo |= slow_align((packed[a][e / 2] >> (16 * (e & 1))) & 0xffffu, shift) << (8 * e);
+          hi |= slow_align((packed[a][2 + e / 2] >> (16 * (e & 1))) & 0xffffu, shift)
+                << (8 * e);
+        }
+      }
+    }
+    out[a] = make_uint2(lo, hi);
+  }
+}
+
 template <int kActBranches, int kMode>
 __global__ void __launch_bounds__(256)
     prepare_kernel(const float *__restrict__ x, Gather32 g, FastDiv div_chunks, int T, int cols,
@@ -128,165 +307,22 @@ __global__ void __launch_bounds__(256)
   const int sub = static_cast<int>(threadIdx.x % kGroupThreads);
   const unsigned mask = 0xffu << (threadIdx.x & 24);
   const int kbeg = t * kTileK + sub * 8;
-  unsigned kvalid = 0;
-#pragma unroll
-  for (int e = 0; e < 8; ++e)
-    kvalid |= (kbeg + e < g.K ? 1u : 0u) << e;
-  int rel[8], di[8], dj[8];
-  if (kMode != kPrepRows) {
-    int c = fdiv(kbeg, g.div_khw);
-    const int rk = kbeg - c * g.KH * g.KW;
-    int i = fdiv(rk, g.div_kw);
-    int j = rk - i * g.KW;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      rel[e] = c * g.sC + i * g.sH + j * g.sW;
-      di[e] = i;
-      dj[e] = j;
-      if (++j == g.KW) {
-        j = 0;
-        if (++i == g.KH) {
-          i = 0;
-          ++c;
-        }
-      }
-    }
-  }
+  const Taps8 tp = make_taps8<kMode>(g, kbeg);
   for (int r = 0; r < cols; ++r) {
     const int m = (chunk * cols + r) * 32 + grp;
     if (m >= m_pad)
       break; // uniform per 8-lane subgroup
     float v[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e)
-      v[e] = 0.0f;
-    if (m < g.M && kvalid) {
-      if (kMode == kPrepRows) {
-        const float *row = x + static_cast<int64_t>(m) * g.K;
-        if (g.pair_rows == 2 && kvalid == 0xffu) {
-          const float4 *src = reinterpret_cast<const float4 *>(row + kbeg);
-          const float4 lo = __ldg(src), hi = __ldg(src + 1);
-          v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
-          v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if ((kvalid >> e) & 1u)
-              v[e] = __ldg(row + kbeg + e);
-        }
-      } else {
-        const int n = fdiv(m, g.div_ohw);
-        const int rm = m - n * g.OH * g.OW;
-        const int oh = fdiv(rm, g.div_ow);
-        const int ow = rm - oh * g.OW;
-        const int ih0 = oh * g.SH - g.PH, iw0 = ow * g.SW - g.PW;
-        const float *img = x + static_cast<int64_t>(n) * g.image;
-        const int org = ih0 * g.sH + iw0 * g.sW;
-        if (kvalid == 0xffu && ih0 >= 0 && iw0 >= 0 && ih0 + g.KH <= g.H &&
-            iw0 + g.KW <= g.W) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            v[e] = window_load<kMode>(img, g, org + rel[e]);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if (((kvalid >> e) & 1u) &&
-                static_cast<unsigned>(ih0 + di[e]) < static_cast<unsigned>(g.H) &&
-                static_cast<unsigned>(iw0 + dj[e]) < static_cast<unsigned>(g.W))
-              v[e] = window_load<kMode>(img, g, org + rel[e]);
-        }
-      }
-    }
-    // Split and round: xp = max(x, 0), xn = max(-x, 0) equal the reference's
-    // selects for every non-NaN x up to the sign of zero, which the
-    // preparation clears anyway (BF16Compensation.cpp:97). cvt.rn.bf16x2.f32
-    // rounds to nearest even, as arith.truncf does. NaN, infinity and finite
-    // values that round to BF16 infinity (|x| >= 0x1.fep127) mark the group
-    // non-finite: through the BF16 exponent 0xff of the maximum for a
-    // 2-branch layer, through |x| of the raw inputs otherwise (the max with 0
-    // drops NaN).
-    uint32_t packed[2][4];
-    uint32_t mx[2] = {0, 0};
-    bool negative = false;
-    if (kActBranches == 2) {
-      uint32_t amax = 0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        amax = max(amax, __float_as_uint(v[e]) & 0x7fffffffu);
-#pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        const __nv_bfloat162 hp =
-            __floats2bfloat162_rn(fmaxf(v[e], 0.0f), fmaxf(v[e + 1], 0.0f));
-        const __nv_bfloat162 hn =
-            __floats2bfloat162_rn(fmaxf(-v[e], 0.0f), fmaxf(-v[e + 1], 0.0f));
-        packed[0][e / 2] = *reinterpret_cast<const uint32_t *>(&hp) & 0x7fff7fffu;
-        packed[1][e / 2] = *reinterpret_cast<const uint32_t *>(&hn) & 0x7fff7fffu;
-      }
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        const uint32_t m2 = __vmaxu2(__vmaxu2(packed[a][0], packed[a][1]),
-                                     __vmaxu2(packed[a][2], packed[a][3]));
-        mx[a] = max(m2 & 0xffffu, m2 >> 16);
-      }
-      if (amax >= 0x7f7f8000u)
-        mx[0] = 0xffffu;
-    } else {
-      uint32_t umax = 0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        umax = max(umax, __float_as_uint(v[e]));
-      negative = umax > 0x80000000u;
-#pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        const __nv_bfloat162 hp = __floats2bfloat162_rn(v[e], v[e + 1]);
-        packed[0][e / 2] = *reinterpret_cast<const uint32_t *>(&hp) & 0x7fff7fffu;
-      }
-      const uint32_t m2 = __vmaxu2(__vmaxu2(packed[0][0], packed[0][1]),
-                                   __vmaxu2(packed[0][2], packed[0][3]));
-      mx[0] = max(m2 & 0xffffu, m2 >> 16);
-    }
-#pragma unroll
-    for (int a = 0; a < kActBranches; ++a)
-#pragma unroll
-      for (int o = 4; o; o >>= 1)
-        mx[a] = max(mx[a], __shfl_xor_sync(mask, mx[a], o, kGroupThreads));
-    const bool nonfinite = mx[0] >= 0x7f80u;
-    if (sub == 0 && nonfinite)
-      atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-    if (negative && !nonfinite)
-      atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
+    gather8<kMode>(x, g, tp, m, kbeg, v);
+    uint2 out[2];
+    int emax[2];
+    convert8<kActBranches>(v, mask, sub, status, out, emax);
 #pragma unroll
     for (int a = 0; a < kActBranches; ++a) {
-      const bool zero = mx[a] == 0 || nonfinite;
-      const int emax = zero ? kZeroGroup : effective_exponent(static_cast<uint16_t>(mx[a]));
-      uint32_t lo = 0, hi = 0;
-      if (!zero) {
-        if ((mx[a] >> 7) >= 8) {
-          const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax) << 23);
-          uint32_t q[8];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            q[2 * e] = __float_as_uint(
-                __fmaf_rz(__uint_as_float(packed[a][e] << 16), scale, 8388608.0f));
-            q[2 * e + 1] = __float_as_uint(
-                __fmaf_rz(__uint_as_float(packed[a][e] & 0xffff0000u), scale, 8388608.0f));
-          }
-          lo = pack_low_bytes(q[0], q[1], q[2], q[3]);
-          hi = pack_low_bytes(q[4], q[5], q[6], q[7]);
-        } else {
-          const int shift = 127 - emax;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            lo |= slow_align((packed[a][e / 2] >> (16 * (e & 1))) & 0xffffu, shift) << (8 * e);
-            hi |= slow_align((packed[a][2 + e / 2] >> (16 * (e & 1))) & 0xffffu, shift)
-                  << (8 * e);
-          }
-        }
-      }
       *reinterpret_cast<uint2 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) =
-          make_uint2(lo, hi);
+          out[a];
       if (sub == 0)
-        ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax;
+        ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax[a];
     }
   }
 }
@@ -482,7 +518,12 @@ __device__ __noinline__ float slow_tile_add(float acc, int p, int ew, int ex, in
   return __fadd_rn(acc, bf16_to_f32(tile));
 }
 
-template <int kActBranches, int kTC, int kRM>
+// kFuse < 0: A and Ex come from the prepare kernel's workspace. kFuse =
+// kPrepRows / kPrepConv / kPrepConvPool: the CTA gathers and prealigns its own
+// activation tiles from x (eight threads per 64-element group, as
+// prepare_kernel does) into shared memory, so a narrow layer is one launch
+// and its prepared columns never travel through HBM.
+template <int kActBranches, int kTC, int kRM, int kFuse>
 __global__ void __launch_bounds__(256)
     signsplit_simt_kernel(const int8_t *__restrict__ A,
                           const int32_t *__restrict__ exA, int64_t m_pad,
@@ -492,7 +533,8 @@ __global__ void __launch_bounds__(256)
                           const float *__restrict__ bias,
                           const float *__restrict__ post_scale,
                           const float *__restrict__ post_shift, int act, int64_t out_pixels,
-                          float *__restrict__ y, int32_t *status) {
+                          float *__restrict__ y, int32_t *status,
+                          const float *__restrict__ x, Gather32 g, int k_logical) {
   constexpr int kBN = 4 * kTC, kTR = 256 / kTC, kBM = kTR * kRM;
   __shared__ __align__(16) int8_t As[kActBranches][kBM][kRowStride];
   __shared__ __align__(16) int8_t Bs[2][kBN][kRowStride];
@@ -523,9 +565,33 @@ __global__ void __launch_bounds__(256)
           B + (static_cast<int64_t>(w) * n_pad + n0 + r) * k_pad +
           static_cast<int64_t>(t) * kTileK + c * 16);
     }
-    for (int i = tid; i < kActBranches * kBM; i += 256)
-      sExA[i / kBM][i % kBM] =
-          exA[(static_cast<int64_t>(i / kBM) * T + t) * m_pad + m0 + i % kBM];
+    if (kFuse < 0) {
+      for (int i = tid; i < kActBranches * kBM; i += 256)
+        sExA[i / kBM][i % kBM] =
+            exA[(static_cast<int64_t>(i / kBM) * T + t) * m_pad + m0 + i % kBM];
+    } else {
+      // 32 groups per pass: eight threads each own eight K elements.
+      constexpr int kPrepMode = kFuse < 0 ? kPrepRows : kFuse;
+      const int grp = tid / kGroupThreads, sub = tid % kGroupThreads;
+      const unsigned mask = 0xffu << (tid & 24);
+      const int kbeg = t * kTileK + sub * 8;
+      const Taps8 tp = make_taps8<kPrepMode>(g, kbeg);
+#pragma unroll 1
+      for (int r0 = 0; r0 < kBM; r0 += 32) {
+        const int row = r0 + grp;
+        float v[8];
+        gather8<kPrepMode>(x, g, tp, static_cast<int>(m0) + row, kbeg, v);
+        uint2 out[2];
+        int emax[2];
+        convert8<kActBranches>(v, mask, sub, status, out, emax);
+#pragma unroll
+        for (int a = 0; a < kActBranches; ++a) {
+          *reinterpret_cast<uint2 *>(&As[a][row][sub * 8]) = out[a];
+          if (sub == 0)
+            sExA[a][row] = emax[a];
+        }
+      }
+    }
     for (int i = tid; i < 2 * kBN; i += 256) {
       const int e = exB[(static_cast<int64_t>(i / kBN) * T + t) * n_pad + n0 + i % kBN];
       sExB[i / kBN][i % kBN] = e;
@@ -571,14 +637,16 @@ __global__ void __launch_bounds__(256)
     for (int a = 0; a < kActBranches; ++a)
       live[a] = sLive[a] != 0;
     // Activation tiles of live branches only (an all-zero branch is skipped).
-    for (int i = tid; i < kActBranches * kBM * 4; i += 256) {
-      const int a = i / (kBM * 4), r = (i >> 2) % kBM, c = i & 3;
-      if (live[a])
-        *reinterpret_cast<int4 *>(&As[a][r][c * 16]) = *reinterpret_cast<const int4 *>(
-            A + (static_cast<int64_t>(a) * m_pad + m0 + r) * k_pad +
-            static_cast<int64_t>(t) * kTileK + c * 16);
+    if (kFuse < 0) {
+      for (int i = tid; i < kActBranches * kBM * 4; i += 256) {
+        const int a = i / (kBM * 4), r = (i >> 2) % kBM, c = i & 3;
+        if (live[a])
+          *reinterpret_cast<int4 *>(&As[a][r][c * 16]) = *reinterpret_cast<const int4 *>(
+              A + (static_cast<int64_t>(a) * m_pad + m0 + r) * k_pad +
+              static_cast<int64_t>(t) * kTileK + c * 16);
+      }
+      __syncthreads();
     }
-    __syncthreads();
     int p[kActBranches][2][kRM][4];
 #pragma unroll
     for (int a = 0; a < kActBranches; ++a)
@@ -589,8 +657,12 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
           for (int c = 0; c < 4; ++c)
             p[a][w][r][c] = 0;
+    // 16-element chunks past K hold zeros in both operands: skip them.
+    const int kk_end = min(4, (k_logical - t * kTileK + 15) / 16);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
+      if (kk >= kk_end)
+        break;
       int4 av[kActBranches][kRM], bv[2][4];
 #pragma unroll
       for (int a = 0; a < kActBranches; ++a)
@@ -692,38 +764,34 @@ __global__ void __launch_bounds__(256)
 // Tile shape per layer: 8 or 16-lane tiles for layers of at most 8 or 16
 // lanes, 32 otherwise; 2 column rows per thread when that still gives every
 // SM two CTAs.
-template <int kAB>
+template <int kAB, int kFuse = -1>
 void launch_signsplit_simt(const int8_t *A, const int32_t *exA, int64_t m_pad,
                            const int8_t *B, const int32_t *exB, int64_t n_pad,
                            int64_t k_pad, int T, int64_t M, int64_t N,
                            const float *bias, const float *post_scale,
                            const float *post_shift, int act, int64_t out_pixels, float *y,
-                           int32_t *status, cudaStream_t s) {
+                           int32_t *status, cudaStream_t s, int k_logical,
+                           const float *x = nullptr, Gather32 g = Gather32{}) {
   const int64_t target = 2 * 148;
-  if (N <= 8) {
-    signsplit_simt_kernel<kAB, 2, 1><<<dim3(static_cast<unsigned>(m_pad / 128), 1), 256, 0, s>>>(
+  auto go = [&](auto kernel, int64_t rows_per_cta, unsigned ny) {
+    kernel<<<dim3(static_cast<unsigned>(m_pad / rows_per_cta), ny), 256, 0, s>>>(
         A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
-          out_pixels, y, status);
+        out_pixels, y, status, x, g, k_logical);
+  };
+  if (N <= 8) {
+    go(signsplit_simt_kernel<kAB, 2, 1, kFuse>, 128, 1);
   } else if (N <= 16) {
     const unsigned ny = static_cast<unsigned>((N + 15) / 16);
     if ((m_pad / 128) * ny >= target)
-      signsplit_simt_kernel<kAB, 4, 2><<<dim3(static_cast<unsigned>(m_pad / 128), ny), 256, 0, s>>>(
-          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
-          out_pixels, y, status);
+      go(signsplit_simt_kernel<kAB, 4, 2, kFuse>, 128, ny);
     else
-      signsplit_simt_kernel<kAB, 4, 1><<<dim3(static_cast<unsigned>(m_pad / 64), ny), 256, 0, s>>>(
-          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
-          out_pixels, y, status);
+      go(signsplit_simt_kernel<kAB, 4, 1, kFuse>, 64, ny);
   } else {
     const unsigned ny = static_cast<unsigned>((N + 31) / 32);
     if ((m_pad / 64) * ny >= target)
-      signsplit_simt_kernel<kAB, 8, 2><<<dim3(static_cast<unsigned>(m_pad / 64), ny), 256, 0, s>>>(
-          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
-          out_pixels, y, status);
+      go(signsplit_simt_kernel<kAB, 8, 2, kFuse>, 64, ny);
     else
-      signsplit_simt_kernel<kAB, 8, 1><<<dim3(static_cast<unsigned>(m_pad / 32), ny), 256, 0, s>>>(
-          A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
-          out_pixels, y, status);
+      go(signsplit_simt_kernel<kAB, 8, 1, kFuse>, 32, ny);
   }
 }
 
@@ -1199,11 +1267,11 @@ int cim22_cuda_layer_contract_bf16_ex(const cim22_cuda_layer *layer, int64_t m,
   if (ab == 1)
     launch_signsplit_simt<1>(A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
                              layer->k_pad, T, m, layer->n, bias, post_scale, post_shift,
-                             activation, out_pixels, y, status, s);
+                             activation, out_pixels, y, status, s, static_cast<int>(layer->k));
   else
     launch_signsplit_simt<2>(A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
                              layer->k_pad, T, m, layer->n, bias, post_scale, post_shift,
-                             activation, out_pixels, y, status, s);
+                             activation, out_pixels, y, status, s, static_cast<int>(layer->k));
   return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
 }
 
@@ -1230,6 +1298,47 @@ int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float 
     set_last_error("invalid arguments to cim22_cuda_layer_forward_bf16");
     return CIM22_STATUS_BAD_ARGUMENT;
   }
+  if (cim22_cuda_layer_fused_forward(layer)) {
+    // Narrow layer: one CUDA-core kernel gathers, prealigns and contracts.
+    cim22_gather rows{};
+    rows.kind = CIM22_GATHER_ROWS;
+    const cim22_gather &g = gather ? *gather : rows;
+    const int64_t m_pad = round_up(m, kColumnPad);
+    const int T = static_cast<int>(layer->tiles);
+    if (!x || !status || m <= 0 || (branches != 2 && branches != 4) ||
+        !check_gather(g, m, layer->k) || !workspace ||
+        workspace_bytes < cim22_cuda_layer_workspace_bf16(layer, m, branches) ||
+        m_pad * T * kGroupThreads >= (int64_t{1} << 31)) {
+      set_last_error("invalid arguments to cim22_cuda_layer_forward_bf16");
+      return CIM22_STATUS_BAD_ARGUMENT;
+    }
+    auto s = static_cast<cudaStream_t>(stream);
+    const Gather32 dg = to_device_gather(g, m, layer->k, x);
+    const int mode = g.kind == CIM22_GATHER_ROWS ? kPrepRows
+                     : g.pool_kernel > 0         ? kPrepConvPool
+                                                 : kPrepConv;
+    auto launch = [&](auto ab_tag, auto mode_tag) {
+      launch_signsplit_simt<decltype(ab_tag)::value, decltype(mode_tag)::value>(
+          nullptr, nullptr, m_pad, layer->weights, layer->exponents, layer->n_pad,
+          layer->k_pad, T, m, layer->n, bias, post_scale, post_shift, activation, out_pixels, y,
+          status, s, static_cast<int>(layer->k), x, dg);
+    };
+    using R = std::integral_constant<int, kPrepRows>;
+    using C = std::integral_constant<int, kPrepConv>;
+    using P = std::integral_constant<int, kPrepConvPool>;
+    using B1 = std::integral_constant<int, 1>;
+    using B2 = std::integral_constant<int, 2>;
+    if (branches == 2) {
+      if (mode == kPrepRows) launch(B1{}, R{});
+      else if (mode == kPrepConv) launch(B1{}, C{});
+      else launch(B1{}, P{});
+    } else {
+      if (mode == kPrepRows) launch(B2{}, R{});
+      else if (mode == kPrepConv) launch(B2{}, C{});
+      else launch(B2{}, P{});
+    }
+    return cuda_ok(cudaGetLastError(), "fused layer launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+  }
   const int rc = cim22_cuda_layer_prepare_bf16(layer, x, gather, m, branches, workspace,
                                                workspace_bytes, status, stream);
   if (rc)
@@ -1237,6 +1346,10 @@ int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float 
   return cim22_cuda_layer_contract_bf16_ex(layer, m, out_pixels, bias, post_scale, post_shift,
                                            activation, branches, y, workspace, workspace_bytes,
                                            status, stream);
+}
+
+int cim22_cuda_layer_fused_forward(const cim22_cuda_layer *layer) {
+  return layer && layer->bf16 && layer->n <= 16 ? 1 : 0;
 }
 
 int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
