@@ -438,9 +438,9 @@ int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float 
                                      int32_t branches, float *y, void *workspace,
                                      size_t workspace_bytes, int32_t *status, void *stream);
 /* 1 when cim22_cuda_layer_forward_bf16{,_ex} runs the layer as one kernel
- * that gathers, prealigns and contracts (layers of at most 16 lanes, where
- * the prepared columns then never leave the SM), 0 when it runs the prepare
- * and contract kernels. */
+ * that gathers, prealigns and contracts (layers of at most 16 lanes and at
+ * most two K tiles, whose prepared columns then never leave the SM), 0 when
+ * it runs the prepare and contract kernels. */
 int cim22_cuda_layer_fused_forward(const cim22_cuda_layer *layer);
 int cim22_cuda_layer_contract_bf16_ex(const cim22_cuda_layer *layer, int64_t m,
                                       int64_t out_pixels, const float *bias,

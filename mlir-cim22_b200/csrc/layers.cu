@@ -576,7 +576,7 @@ __global__ void __launch_bounds__(256)
       const unsigned mask = 0xffu << (tid & 24);
       const int kbeg = t * kTileK + sub * 8;
       const Taps8 tp = make_taps8<kPrepMode>(g, kbeg);
-#pragma unroll 1
+#pragma unroll
       for (int r0 = 0; r0 < kBM; r0 += 32) {
         const int row = r0 + grp;
         float v[8];
@@ -1317,11 +1317,14 @@ int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float 
     const int mode = g.kind == CIM22_GATHER_ROWS ? kPrepRows
                      : g.pool_kernel > 0         ? kPrepConvPool
                                                  : kPrepConv;
+    // The CUDA-core contraction builds its own activation tiles.
     auto launch = [&](auto ab_tag, auto mode_tag) {
-      launch_signsplit_simt<decltype(ab_tag)::value, decltype(mode_tag)::value>(
-          nullptr, nullptr, m_pad, layer->weights, layer->exponents, layer->n_pad,
-          layer->k_pad, T, m, layer->n, bias, post_scale, post_shift, activation, out_pixels, y,
-          status, s, static_cast<int>(layer->k), x, dg);
+      constexpr int kAB = decltype(ab_tag)::value, kMode = decltype(mode_tag)::value;
+      launch_signsplit_simt<kAB, kMode>(nullptr, nullptr, m_pad, layer->weights,
+                                        layer->exponents, layer->n_pad, layer->k_pad, T, m,
+                                        layer->n, bias, post_scale, post_shift, activation,
+                                        out_pixels, y, status, s, static_cast<int>(layer->k), x,
+                                        dg);
     };
     using R = std::integral_constant<int, kPrepRows>;
     using C = std::integral_constant<int, kPrepConv>;
@@ -1349,7 +1352,7 @@ int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float 
 }
 
 int cim22_cuda_layer_fused_forward(const cim22_cuda_layer *layer) {
-  return layer && layer->bf16 && layer->n <= 16 ? 1 : 0;
+  return layer && layer->bf16 && layer->n <= 16 && layer->tiles <= 2 ? 1 : 0;
 }
 
 int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,

@@ -325,3 +325,71 @@ def test_linear_bf16_tensor_core_bit_exact(m, k, n, branches, scale):
                             branches=branches).cpu().numpy()
     assert lib().cim22_cuda_tensor_core_launches() == before + 1
     np.testing.assert_array_equal(bits(got), bits(expected))
+
+
+@pytest.mark.parametrize("layout,n,c,h,f,kk,stride,pad,branches,pool", [
+    ("nchw", 64, 1, 32, 6, 5, 1, 0, 4, 0),    # LeNet conv1: K = 25, 6 lanes
+    ("nchw", 16, 3, 20, 8, 3, 2, 1, 2, 0),
+    ("nhwc", 16, 2, 18, 5, 3, 1, 1, 4, 0),
+    ("nchw", 16, 4, 10, 7, 3, 1, 0, 2, 2),    # fused 2x2 pool, K = 36
+    ("nhwc", 8, 1, 12, 1, 7, 1, 3, 4, 2),     # K = 49, one lane
+    ("nchw", 32, 2, 16, 12, 5, 1, 2, 4, 0),   # 12 lanes, K = 50: fused CUDA-core kernel
+    ("nchw", 32, 4, 12, 16, 5, 1, 2, 2, 0)])  # 16 lanes, K = 100: two tiles, fused
+@pytest.mark.parametrize("out_layout", ["rows", "nchw"])
+def test_narrow_fused_layers_bit_exact(layout, n, c, h, f, kk, stride, pad, branches, pool,
+                                       out_layout):
+    """Layers of at most 16 lanes and two K tiles run as one kernel (the
+    CUDA-core contraction building its own activation tiles): bit-exact
+    against the oracle."""
+    from cim22_b200 import abi
+    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace, conv_gather
+
+    rng = np.random.default_rng(n + c * 7 + h + f * 3 + pool)
+    src = h * 2 if pool else h
+    x = rng.standard_normal((n, c, src, src)).astype(np.float32)
+    x *= (10.0 ** rng.uniform(-30, 30, (n, 1, 1, 1))).astype(np.float32)  # exact-path images
+    if branches == 2:
+        x = np.maximum(x, 0)
+    x[rng.random(x.shape) < 0.2] = 0
+    pooled = x.reshape(n, c, h, 2, h, 2).max(axis=(3, 5)) if pool else x
+    w = (rng.standard_normal((f, c, kk, kk)) * 0.2).astype(np.float32)
+    b = rng.standard_normal(f).astype(np.float32)
+    expected = oracle.conv2d_bf16(pooled, w, b, stride, pad, branches=4, threads=8)
+    layer = CimLayer(w.reshape(f, -1))
+    assert layer.fused_forward
+    kind = abi.GATHER_CONV_NCHW if layout == "nchw" else abi.GATHER_CONV_NHWC
+    g = conv_gather(kind, n, c, h, h, kk, kk, stride, pad)
+    if pool:
+        g.pool_kernel, g.pool_stride, g.pool_src_h, g.pool_src_w = 2, 2, src, src
+    xt = torch.from_numpy(x if layout == "nchw" else x.transpose(0, 2, 3, 1).copy()).to(DEV)
+    m = n * g.out_h * g.out_w
+    out = torch.empty(m, f, device=DEV)
+    status = StatusWord(torch.device(DEV))
+    pixels = g.out_h * g.out_w if out_layout == "nchw" else 0
+    layer.forward_bf16(xt, out, m, gather=g, bias=torch.from_numpy(b).to(DEV),
+                       branches=branches, out_pixels=pixels,
+                       workspace=Workspace(torch.device(DEV)), status=status)
+    status.raise_if_set()
+    if out_layout == "nchw":
+        got = out.cpu().numpy().reshape(n, f, g.out_h, g.out_w)
+    else:
+        got = out.cpu().numpy().reshape(n, g.out_h, g.out_w, f).transpose(0, 3, 1, 2)
+    np.testing.assert_array_equal(bits(got), bits(expected))
+
+
+@pytest.mark.parametrize("m,k,n,branches", [(300, 25, 6, 4), (129, 64, 8, 2), (77, 100, 10, 4),
+                                            (1000, 3, 1, 2)])
+def test_narrow_fused_linear_bit_exact(m, k, n, branches):
+    from cim22_b200.cim_ops import CimLayer
+
+    rng = np.random.default_rng(m + k + n)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    if branches == 2:
+        x = np.maximum(x, 0)
+    w = (rng.standard_normal((n, k)) * 0.1).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    layer = CimLayer(w)
+    assert layer.fused_forward
+    got = layer.linear_bf16(torch.from_numpy(x).to(DEV), bias=torch.from_numpy(b).to(DEV),
+                            branches=branches).cpu().numpy()
+    np.testing.assert_array_equal(bits(got), bits(oracle.linear_bf16(x, w, b)))
