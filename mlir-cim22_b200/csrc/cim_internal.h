@@ -57,6 +57,37 @@ __device__ __forceinline__ int fdiv(int n, const FastDiv &f) {
 }
 #endif
 
+// Programmatic dependent launch. Layer and glue kernels are launched with
+// launch_pdl, so the next kernel in the stream (or CUDA graph) is scheduled
+// while the current one drains; each kernel calls pdl_launch_dependents()
+// once its CTAs run and pdl_wait() before its first access to memory that
+// another kernel reads or writes (only barrier setup, TMEM allocation and
+// reads of resident weights come earlier). griddepcontrol.wait returns once
+// every earlier grid has completed and its writes are visible; without the
+// launch attribute both instructions are no-ops.
+#if defined(__CUDACC__)
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+#endif
+
 } // namespace cim
 
 // Prepared CIM layer weights resident in device memory.

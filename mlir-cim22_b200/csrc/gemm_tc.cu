@@ -551,6 +551,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = s.tmem;
   volatile int *failed = &s.failed;
+  // Barriers and TMEM are set up; everything below touches memory that
+  // earlier kernels write.
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == 0 && lane == 0) {
     uint32_t kbi = 0, gi = 0;
@@ -858,8 +862,7 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
       return false;
-    kernel<<<grid, kSThreads, smem, stream>>>(
-        ta, tb, exA, static_cast<int>(m_pad), exB, static_cast<int>(n_pad), T,
+    launch_pdl(kernel, grid, kSThreads, smem, stream, ta, tb, exA, static_cast<int>(m_pad), exB, static_cast<int>(n_pad), T,
         static_cast<int>(M), static_cast<int>(N),
         make_fastdiv(static_cast<uint32_t>((N + L - 1) / L)), bias, post_scale, post_shift, act,
         vec, static_cast<int>(out_pixels),

@@ -27,6 +27,8 @@ __device__ __forceinline__ float act_fn(float v, int act) {
 template <int kAct>
 __global__ void unary_kernel(const float *__restrict__ x, float *__restrict__ y,
                              int64_t count) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t vec = count / 4;
@@ -50,6 +52,8 @@ __global__ void unary_kernel(const float *__restrict__ x, float *__restrict__ y,
 
 __global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b,
                            float *__restrict__ y, int64_t count, int act) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
        i < count; i += stride)
@@ -59,6 +63,8 @@ __global__ void add_kernel(const float *__restrict__ a, const float *__restrict_
 __global__ void maxpool_kernel(const float *__restrict__ x, float *__restrict__ y,
                                int n, int h, int w, int c, int k, int s, int pad,
                                int oh, int ow) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t total = static_cast<int64_t>(n) * oh * ow * c;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -90,6 +96,8 @@ __global__ void maxpool_kernel(const float *__restrict__ x, float *__restrict__ 
 __global__ void avgpool_kernel(const float *__restrict__ x, float *__restrict__ y,
                                int n, int h, int w, int c, int k, int s, int oh,
                                int ow) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t total = static_cast<int64_t>(n) * oh * ow * c;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const float inv = 1.0f / static_cast<float>(k * k);
@@ -113,6 +121,8 @@ __global__ void avgpool_kernel(const float *__restrict__ x, float *__restrict__ 
 // warps stride the plane, shared-memory reduction.
 __global__ void gap_kernel(const float *__restrict__ x, float *__restrict__ y,
                            int h, int w, int c) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.x;
   const int c0 = blockIdx.y * 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -138,6 +148,8 @@ __global__ void gap_kernel(const float *__restrict__ x, float *__restrict__ y,
 __global__ void affine_kernel(const float *__restrict__ x, const float *__restrict__ scale,
                               const float *__restrict__ shift, float *__restrict__ y,
                               int64_t rows, int c, int act) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t total = rows * c;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -150,6 +162,8 @@ __global__ void affine_kernel(const float *__restrict__ x, const float *__restri
 // One warp per row.
 __global__ void softmax_kernel(const float *__restrict__ x, float *__restrict__ y,
                                int64_t rows, int cols) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows)
@@ -172,6 +186,8 @@ __global__ void softmax_kernel(const float *__restrict__ x, float *__restrict__ 
 
 __global__ void nhwc_to_nchw_kernel(const float *__restrict__ x, float *__restrict__ y,
                                     int n, int h, int w, int c) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t total = static_cast<int64_t>(n) * h * w * c;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -189,6 +205,8 @@ __global__ void nhwc_to_nchw_kernel(const float *__restrict__ x, float *__restri
 
 __global__ void nchw_to_nhwc_kernel(const float *__restrict__ x, float *__restrict__ y,
                                     int n, int c, int h, int w) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t total = static_cast<int64_t>(n) * h * w * c;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -209,6 +227,8 @@ __global__ void nchw_to_nhwc_kernel(const float *__restrict__ x, float *__restri
 __global__ void maxpool_nchw_kernel(const float *__restrict__ x, float *__restrict__ y,
                                     int64_t planes, int h, int w, int k, int s, int pad,
                                     int oh, int ow) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t total = planes * oh * ow;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -238,6 +258,8 @@ __global__ void maxpool_nchw_kernel(const float *__restrict__ x, float *__restri
 __global__ void avgpool_nchw_kernel(const float *__restrict__ x, float *__restrict__ y,
                                     int64_t planes, int h, int w, int k, int s, int oh,
                                     int ow) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t total = planes * oh * ow;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const float inv = 1.0f / static_cast<float>(k * k);
@@ -258,6 +280,8 @@ __global__ void avgpool_nchw_kernel(const float *__restrict__ x, float *__restri
 // Mean of each plane: one warp per (image, channel) plane.
 __global__ void gap_nchw_kernel(const float *__restrict__ x, float *__restrict__ y,
                                 int64_t planes, int64_t hw) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t plane = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (plane >= planes)
@@ -278,6 +302,8 @@ __global__ void affine_nchw_vec_kernel(const float4 *__restrict__ x,
                                        const float *__restrict__ scale,
                                        const float *__restrict__ shift, float4 *__restrict__ y,
                                        int quads, FastDiv div_plane, FastDiv div_c, int act) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int stride = static_cast<int>(gridDim.x * blockDim.x);
   for (int i = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x); i < quads; i += stride) {
     const int plane = fdiv(i, div_plane);
@@ -296,6 +322,8 @@ __global__ void affine_nchw_vec_kernel(const float4 *__restrict__ x,
 __global__ void affine_nchw_kernel(const float *__restrict__ x, const float *__restrict__ scale,
                                    const float *__restrict__ shift, float *__restrict__ y,
                                    int64_t planes, int c, int64_t hw, int act) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t plane = blockIdx.y + static_cast<int64_t>(blockIdx.z) * gridDim.y;
   if (plane >= planes)
     return;
@@ -315,6 +343,8 @@ __global__ void affine_nchw_kernel(const float *__restrict__ x, const float *__r
 // block's padding and are dropped).
 __global__ void unshard_columns_kernel(const float *__restrict__ src, float *__restrict__ dst,
                                        int ranks, int64_t rows, int64_t cols, int64_t total) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t count = rows * total;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
@@ -346,8 +376,7 @@ int cim22_cuda_relu(const float *x, float *y, int64_t count, void *stream) {
     return bad("cim22_cuda_relu");
   if (count == 0)
     return 0;
-  unary_kernel<CIM22_ACT_RELU><<<grid_for((count + 3) / 4), 256, 0,
-                                 static_cast<cudaStream_t>(stream)>>>(x, y, count);
+  launch_pdl(unary_kernel<CIM22_ACT_RELU>, grid_for((count + 3) / 4), 256, 0, static_cast<cudaStream_t>(stream), x, y, count);
   return launched("relu");
 }
 
@@ -356,8 +385,7 @@ int cim22_cuda_gelu(const float *x, float *y, int64_t count, void *stream) {
     return bad("cim22_cuda_gelu");
   if (count == 0)
     return 0;
-  unary_kernel<CIM22_ACT_GELU><<<grid_for((count + 3) / 4), 256, 0,
-                                 static_cast<cudaStream_t>(stream)>>>(x, y, count);
+  launch_pdl(unary_kernel<CIM22_ACT_GELU>, grid_for((count + 3) / 4), 256, 0, static_cast<cudaStream_t>(stream), x, y, count);
   return launched("gelu");
 }
 
@@ -367,8 +395,7 @@ int cim22_cuda_add(const float *a, const float *b, float *y, int64_t count,
     return bad("cim22_cuda_add");
   if (count == 0)
     return 0;
-  add_kernel<<<grid_for(count), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      a, b, y, count, activation);
+  launch_pdl(add_kernel, grid_for(count), 256, 0, static_cast<cudaStream_t>(stream), a, b, y, count, activation);
   return launched("add");
 }
 
@@ -382,8 +409,7 @@ int cim22_cuda_maxpool2d_nhwc(const float *x, float *y, int32_t n, int32_t h,
   const int ow = (w + 2 * pad - kernel) / stride + 1;
   if (oh <= 0 || ow <= 0)
     return bad("cim22_cuda_maxpool2d_nhwc");
-  maxpool_kernel<<<grid_for(static_cast<int64_t>(n) * oh * ow * c), 256, 0,
-                   static_cast<cudaStream_t>(stream)>>>(x, y, n, h, w, c, kernel,
+  launch_pdl(maxpool_kernel, grid_for(static_cast<int64_t>(n) * oh * ow * c), 256, 0, static_cast<cudaStream_t>(stream), x, y, n, h, w, c, kernel,
                                                         stride, pad, oh, ow);
   return launched("maxpool2d");
 }
@@ -395,8 +421,7 @@ int cim22_cuda_avgpool2d_nhwc(const float *x, float *y, int32_t n, int32_t h,
       stride <= 0 || kernel > h || kernel > w)
     return bad("cim22_cuda_avgpool2d_nhwc");
   const int oh = (h - kernel) / stride + 1, ow = (w - kernel) / stride + 1;
-  avgpool_kernel<<<grid_for(static_cast<int64_t>(n) * oh * ow * c), 256, 0,
-                   static_cast<cudaStream_t>(stream)>>>(x, y, n, h, w, c, kernel,
+  launch_pdl(avgpool_kernel, grid_for(static_cast<int64_t>(n) * oh * ow * c), 256, 0, static_cast<cudaStream_t>(stream), x, y, n, h, w, c, kernel,
                                                         stride, oh, ow);
   return launched("avgpool2d");
 }
@@ -407,7 +432,7 @@ int cim22_cuda_global_avgpool_nhwc(const float *x, float *y, int32_t n,
   if (!x || !y || n <= 0 || h <= 0 || w <= 0 || c <= 0 || n > 65535 * 64)
     return bad("cim22_cuda_global_avgpool_nhwc");
   const dim3 grid(static_cast<unsigned>(n), static_cast<unsigned>((c + 31) / 32));
-  gap_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, h, w, c);
+  launch_pdl(gap_kernel, grid, 256, 0, static_cast<cudaStream_t>(stream), x, y, h, w, c);
   return launched("global_avgpool");
 }
 
@@ -419,8 +444,7 @@ int cim22_cuda_channel_affine_nhwc(const float *x, const float *scale,
     return bad("cim22_cuda_channel_affine_nhwc");
   if (rows == 0)
     return 0;
-  affine_kernel<<<grid_for(rows * c), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, scale, shift, y, rows, c, activation);
+  launch_pdl(affine_kernel, grid_for(rows * c), 256, 0, static_cast<cudaStream_t>(stream), x, scale, shift, y, rows, c, activation);
   return launched("channel_affine");
 }
 
@@ -431,7 +455,7 @@ int cim22_cuda_softmax(const float *x, float *y, int64_t rows, int32_t cols,
   if (rows == 0)
     return 0;
   const unsigned blocks = static_cast<unsigned>((rows * 32 + 255) / 256);
-  softmax_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, rows, cols);
+  launch_pdl(softmax_kernel, blocks, 256, 0, static_cast<cudaStream_t>(stream), x, y, rows, cols);
   return launched("softmax");
 }
 
@@ -439,8 +463,7 @@ int cim22_cuda_nhwc_to_nchw(const float *x, float *y, int32_t n, int32_t h,
                             int32_t w, int32_t c, void *stream) {
   if (!x || !y || n <= 0 || h <= 0 || w <= 0 || c <= 0)
     return bad("cim22_cuda_nhwc_to_nchw");
-  nhwc_to_nchw_kernel<<<grid_for(static_cast<int64_t>(n) * h * w * c), 256, 0,
-                        static_cast<cudaStream_t>(stream)>>>(x, y, n, h, w, c);
+  launch_pdl(nhwc_to_nchw_kernel, grid_for(static_cast<int64_t>(n) * h * w * c), 256, 0, static_cast<cudaStream_t>(stream), x, y, n, h, w, c);
   return launched("nhwc_to_nchw");
 }
 
@@ -448,8 +471,7 @@ int cim22_cuda_nchw_to_nhwc(const float *x, float *y, int32_t n, int32_t c,
                             int32_t h, int32_t w, void *stream) {
   if (!x || !y || n <= 0 || h <= 0 || w <= 0 || c <= 0)
     return bad("cim22_cuda_nchw_to_nhwc");
-  nchw_to_nhwc_kernel<<<grid_for(static_cast<int64_t>(n) * h * w * c), 256, 0,
-                        static_cast<cudaStream_t>(stream)>>>(x, y, n, c, h, w);
+  launch_pdl(nchw_to_nhwc_kernel, grid_for(static_cast<int64_t>(n) * h * w * c), 256, 0, static_cast<cudaStream_t>(stream), x, y, n, c, h, w);
   return launched("nchw_to_nhwc");
 }
 
@@ -460,8 +482,7 @@ int cim22_cuda_unshard_columns(const float *src, float *dst, int32_t ranks, int6
     return bad("cim22_cuda_unshard_columns");
   if (rows == 0)
     return 0;
-  unshard_columns_kernel<<<grid_for(rows * total), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      src, dst, ranks, rows, cols, total);
+  launch_pdl(unshard_columns_kernel, grid_for(rows * total), 256, 0, static_cast<cudaStream_t>(stream), src, dst, ranks, rows, cols, total);
   return launched("unshard_columns");
 }
 
@@ -476,8 +497,7 @@ int cim22_cuda_maxpool2d_nchw(const float *x, float *y, int32_t n, int32_t c,
   if (oh <= 0 || ow <= 0)
     return bad("cim22_cuda_maxpool2d_nchw");
   const int64_t planes = static_cast<int64_t>(n) * c;
-  maxpool_nchw_kernel<<<grid_for(planes * oh * ow), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, y, planes, h, w, kernel, stride, pad, oh, ow);
+  launch_pdl(maxpool_nchw_kernel, grid_for(planes * oh * ow), 256, 0, static_cast<cudaStream_t>(stream), x, y, planes, h, w, kernel, stride, pad, oh, ow);
   return launched("maxpool2d");
 }
 
@@ -489,8 +509,7 @@ int cim22_cuda_avgpool2d_nchw(const float *x, float *y, int32_t n, int32_t c,
     return bad("cim22_cuda_avgpool2d_nchw");
   const int oh = (h - kernel) / stride + 1, ow = (w - kernel) / stride + 1;
   const int64_t planes = static_cast<int64_t>(n) * c;
-  avgpool_nchw_kernel<<<grid_for(planes * oh * ow), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, y, planes, h, w, kernel, stride, oh, ow);
+  launch_pdl(avgpool_nchw_kernel, grid_for(planes * oh * ow), 256, 0, static_cast<cudaStream_t>(stream), x, y, planes, h, w, kernel, stride, oh, ow);
   return launched("avgpool2d");
 }
 
@@ -501,8 +520,7 @@ int cim22_cuda_global_avgpool_nchw(const float *x, float *y, int32_t n,
     return bad("cim22_cuda_global_avgpool_nchw");
   const int64_t planes = static_cast<int64_t>(n) * c;
   const unsigned blocks = static_cast<unsigned>((planes * 32 + 255) / 256);
-  gap_nchw_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, y, planes, static_cast<int64_t>(h) * w);
+  launch_pdl(gap_nchw_kernel, blocks, 256, 0, static_cast<cudaStream_t>(stream), x, y, planes, static_cast<int64_t>(h) * w);
   return launched("global_avgpool");
 }
 
@@ -519,8 +537,7 @@ int cim22_cuda_channel_affine_nchw(const float *x, const float *scale,
   const int64_t quads = planes * hw / 4;
   if (hw % 4 == 0 && quads < (int64_t{1} << 31) && planes < (int64_t{1} << 31) &&
       ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0) {
-    affine_nchw_vec_kernel<<<grid_for(quads), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        reinterpret_cast<const float4 *>(x), scale, shift, reinterpret_cast<float4 *>(y),
+    launch_pdl(affine_nchw_vec_kernel, grid_for(quads), 256, 0, static_cast<cudaStream_t>(stream), reinterpret_cast<const float4 *>(x), scale, shift, reinterpret_cast<float4 *>(y),
         static_cast<int>(quads), make_fastdiv(static_cast<uint32_t>(hw / 4)),
         make_fastdiv(static_cast<uint32_t>(c)), activation);
     return launched("channel_affine");
@@ -532,8 +549,7 @@ int cim22_cuda_channel_affine_nchw(const float *x, const float *scale,
   if (gz > 65535)
     return bad("cim22_cuda_channel_affine_nchw");
   const unsigned gx = static_cast<unsigned>(std::min<int64_t>((hw + 255) / 256, 64));
-  affine_nchw_kernel<<<dim3(gx, static_cast<unsigned>(gy), static_cast<unsigned>(gz)), 256, 0,
-                       static_cast<cudaStream_t>(stream)>>>(x, scale, shift, y, planes, c, hw,
+  launch_pdl(affine_nchw_kernel, dim3(gx, static_cast<unsigned>(gy), static_cast<unsigned>(gz)), 256, 0, static_cast<cudaStream_t>(stream), x, scale, shift, y, planes, c, hw,
                                                             activation);
   return launched("channel_affine");
 }

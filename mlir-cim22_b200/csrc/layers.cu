@@ -300,6 +300,8 @@ __global__ void __launch_bounds__(256)
     prepare_kernel(const float *__restrict__ x, Gather32 g, FastDiv div_chunks, int T, int cols,
                    int m_pad, int k_pad, int8_t *__restrict__ A, int32_t *__restrict__ ex,
                    int32_t *status) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int blk = static_cast<int>(blockIdx.x);
   const int t = fdiv(blk, div_chunks);
   const int chunk = blk - t * static_cast<int>(div_chunks.d);
@@ -358,6 +360,8 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 3 : 1)
     prepare_nchw_kernel(const float *__restrict__ x, Gather32 g, FastDiv div_chunks, int T,
                         int m_pad, int k_pad, int8_t *__restrict__ A,
                         int32_t *__restrict__ ex, int32_t *status) {
+  pdl_launch_dependents();
+  pdl_wait();
   constexpr int kMode = kPool ? kPrepConvPool : kPrepConv;
   __shared__ Tap taps[kTileK];
   const int blk = static_cast<int>(blockIdx.x);
@@ -535,6 +539,8 @@ __global__ void __launch_bounds__(256)
                           const float *__restrict__ post_shift, int act, int64_t out_pixels,
                           float *__restrict__ y, int32_t *status,
                           const float *__restrict__ x, Gather32 g, int k_logical) {
+  pdl_launch_dependents();
+  pdl_wait();
   constexpr int kBN = 4 * kTC, kTR = 256 / kTC, kBM = kTR * kRM;
   __shared__ __align__(16) int8_t As[kActBranches][kBM][kRowStride];
   __shared__ __align__(16) int8_t Bs[2][kBN][kRowStride];
@@ -774,8 +780,7 @@ void launch_signsplit_simt(const int8_t *A, const int32_t *exA, int64_t m_pad,
                            const float *x = nullptr, Gather32 g = Gather32{}) {
   const int64_t target = 2 * 148;
   auto go = [&](auto kernel, int64_t rows_per_cta, unsigned ny) {
-    kernel<<<dim3(static_cast<unsigned>(m_pad / rows_per_cta), ny), 256, 0, s>>>(
-        A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
+    launch_pdl(kernel, dim3(static_cast<unsigned>(m_pad / rows_per_cta), ny), 256, 0, s, A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
         out_pixels, y, status, x, g, k_logical);
   };
   if (N <= 8) {
@@ -1202,7 +1207,7 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
     const FastDiv div_chunks = make_fastdiv(static_cast<uint32_t>(chunks));
     const unsigned blocks = static_cast<unsigned>(chunks * T);
     auto launch = [&](auto kernel) {
-      kernel<<<blocks, 256, 0, s>>>(x, dg, div_chunks, T, static_cast<int>(m_pad),
+      launch_pdl(kernel, blocks, 256, 0, s, x, dg, div_chunks, T, static_cast<int>(m_pad),
                                     static_cast<int>(layer->k_pad), A, ex, status);
     };
     const bool pool = g.pool_kernel > 0;
@@ -1224,7 +1229,7 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
                    : g.pool_kernel > 0         ? kPrepConvPool
                                                : kPrepConv;
   auto launch = [&](auto kernel) {
-    kernel<<<blocks, 256, 0, s>>>(x, dg, div_chunks, T, cols, static_cast<int>(m_pad),
+    launch_pdl(kernel, blocks, 256, 0, s, x, dg, div_chunks, T, cols, static_cast<int>(m_pad),
                                   static_cast<int>(layer->k_pad), A, ex, status);
   };
   if (ab == 1)
