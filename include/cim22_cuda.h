@@ -286,6 +286,9 @@ void _mlir_ciface_cim22_dispatch_int8(int64_t id, cim22_memref2d *input,
 #define CIM22_STATUS_BAD_ARGUMENT 0x10      /* launch-time argument check failed */
 #define CIM22_STATUS_NEGATIVE_INPUT 0x20    /* negative value in a nonnegative (2-branch) layer */
 #define CIM22_STATUS_TIMEOUT 0x40           /* a bounded on-device wait gave up (results invalid) */
+#define CIM22_STATUS_CHIP_NOT_FINITE 0x80   /* Legacy: a chip output to compensate is not finite */
+#define CIM22_STATUS_LEGACY_SCALING 0x100   /* Legacy group scaling changed prealigned mantissas */
+#define CIM22_STATUS_LEGACY_I21 0x200       /* Legacy: all -128 input group and weight lane */
 
 /* Message of the lowest set status bit ("" for 0). */
 const char *cim22_cuda_status_message(int32_t status);
@@ -356,6 +359,18 @@ typedef struct cim22_gather {
    * no padding), with height/width the pooled size. */
   int32_t pool_kernel, pool_stride, pool_src_h, pool_src_w;
 } cim22_gather;
+
+/* A BF16 layer in a given compensation mode (CIM22_BF16_SIGN_SPLIT is
+ * cim22_cuda_layer_create_bf16). CIM22_BF16_LEGACY and CIM22_BF16_NONE are
+ * the reference's diagnostic modes (compiler.py:25, bf16_compensation): no
+ * sign split, signed prealigned tiles, the mode's input preparation and
+ * restore (BF16Compensation.cpp:84-164); the branches argument of the
+ * forward calls is ignored for them. */
+cim22_cuda_layer *cim22_cuda_layer_create_bf16_mode(int device, const float *weight,
+                                                    int64_t n, int64_t k, int32_t compensation,
+                                                    char *error, size_t error_capacity);
+/* The layer's CIM22_BF16_* compensation mode (-1 for a null layer). */
+int32_t cim22_cuda_layer_compensation(const cim22_cuda_layer *layer);
 
 /* Scratch bytes needed by cim22_cuda_layer_forward_bf16 for m columns. */
 size_t cim22_cuda_layer_workspace_bf16(const cim22_cuda_layer *layer,

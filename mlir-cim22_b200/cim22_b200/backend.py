@@ -10,9 +10,9 @@ and its options (python/cim22/compiler.py:28-93):
 
 Read-only module parameters and buffers are frozen into the compiled program,
 as the reference freezes them (backend.py:161-196); Dynamo guards on their
-identity. Gradients must be disabled. bf16_compensation must be "sign-split"
-(the default and the only mode the layer kernels implement; the transaction
-runner in cim22_b200.native also executes "legacy" and "none").
+identity. Gradients must be disabled. bf16_compensation selects "sign-split"
+(the default), or the reference's diagnostic "legacy" and "none" modes
+(compiler.py:25,34-36).
 Inputs may be CPU or CUDA tensors; outputs are returned on the inputs' device.
 """
 
@@ -38,8 +38,9 @@ def _validate(options: dict) -> None:
     runtime = options.get("runtime", "cuda")
     if runtime not in ("cuda", "reference"):
         raise ValueError("CIM22 runtime must be one of ('reference', 'cuda') in this backend")
-    if options.get("bf16_compensation", "sign-split") != "sign-split":
-        raise ValueError("CIM22 CUDA layers implement bf16_compensation='sign-split'")
+    if options.get("bf16_compensation", "sign-split") not in ("sign-split", "legacy", "none"):
+        raise ValueError(
+            "CIM22 bf16_compensation must be 'sign-split', 'legacy' or 'none'")
     if options.get("usb_config") is not None or options.get("usb_session") is not None:
         raise ValueError("CIM22 usb options require runtime='usb'")
 
@@ -88,7 +89,8 @@ def backend(gm: torch.fx.GraphModule, example_inputs: Sequence[torch.Tensor], *,
     device = int(options.get("device", 0))
     program = Program(gm, [e.detach() if isinstance(e, torch.Tensor) else e
                            for e in example_inputs],
-                      frozen=frozen, device=device, name="cim22_cuda")
+                      frozen=frozen, device=device, name="cim22_cuda",
+                      bf16_compensation=options.get("bf16_compensation", "sign-split"))
     if options.get("cuda_graph", True):
         program.capture()
     inputs = [i for i in range(len(placeholders)) if i not in frozen]

@@ -54,17 +54,23 @@ class StatusWord:
         self.tensor.zero_()
 
     def raise_if_set(self, prefix: str = "") -> None:
-        value = int(self.tensor.item())
-        if value:
-            message = lib().cim22_cuda_status_message(value).decode()
-            raise RuntimeError(f"{prefix}{message}")
+        raise_status(int(self.tensor.item()), prefix)
+
+
+def raise_status(value: int, prefix: str = "") -> None:
+    """Raise the reference's error text for a nonzero status word."""
+    if value:
+        message = lib().cim22_cuda_status_message(value).decode()
+        raise RuntimeError(f"{prefix}{message}")
 
 
 class CimLayer:
     """Resident CIM weights of one Linear/Conv contraction (W[n, k])."""
 
     def __init__(self, weight: np.ndarray | torch.Tensor, *, kind: str = "bf16",
-                 device: int | torch.device = 0) -> None:
+                 device: int | torch.device = 0, compensation: str = "sign-split") -> None:
+        """compensation: the BF16 mode, "sign-split" (default), or the
+        reference's diagnostic "legacy" and "none" (no sign split)."""
         dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         self.device = dev
         index = dev.index if dev.index is not None else torch.cuda.current_device()
@@ -73,10 +79,14 @@ class CimLayer:
         self.n, self.k = w.shape
         self.kind = kind
         err = ctypes.create_string_buffer(512)
+        self.compensation = compensation
         if kind == "bf16":
+            if compensation not in abi.COMPENSATION:
+                raise ValueError("BF16 compensation must be sign-split, legacy or none")
             w = np.ascontiguousarray(w, dtype=np.float32)
-            self._handle = lib().cim22_cuda_layer_create_bf16(index, w.ctypes.data, self.n,
-                                                              self.k, err, len(err))
+            self._handle = lib().cim22_cuda_layer_create_bf16_mode(
+                index, w.ctypes.data, self.n, self.k, abi.COMPENSATION[compensation], err,
+                len(err))
         elif kind == "int8":
             w = np.ascontiguousarray(w, dtype=np.int8)
             self._handle = lib().cim22_cuda_layer_create_int8(index, w.ctypes.data, self.n,

@@ -63,6 +63,8 @@ _SIGNATURES = {
     "cim22_cuda_layer_forward_bf16_ex": (c.c_int, [P, P, P, I64, I64, P, P, P, I32, I32, P, P,
                                                    SZ, P, P]),
     "cim22_cuda_layer_fused_forward": (c.c_int, [P]),
+    "cim22_cuda_layer_create_bf16_mode": (c.c_void_p, [c.c_int, P, I64, I64, I32, c.c_char_p, SZ]),
+    "cim22_cuda_layer_compensation": (I32, [P]),
     "cim22_cuda_layer_contract_bf16_ex": (c.c_int, [P, I64, I64, P, P, P, I32, I32, P, P, SZ, P,
                                                     P]),
     "cim22_cuda_layer_forward_bf16_noalloc": (c.c_int, [P, P, P, I64, P, I32, I32, P, P, P]),

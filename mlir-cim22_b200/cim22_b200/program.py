@@ -98,9 +98,13 @@ class Program:
 
     def __init__(self, gm: fx.GraphModule, example_inputs, *, frozen: set[int] | None = None,
                  device: int | torch.device = 0, name: str = "cim_program",
-                 fuse: bool = True, layout: str = "nchw") -> None:
+                 fuse: bool = True, layout: str = "nchw",
+                 bf16_compensation: str = "sign-split") -> None:
         if layout not in ("nchw", "nhwc"):
             raise ValueError(f"unknown image layout {layout!r}")
+        if bf16_compensation not in abi.COMPENSATION:
+            raise ValueError("bf16_compensation must be sign-split, legacy or none")
+        self.compensation = bf16_compensation
         self.device = torch.device("cuda", device) if isinstance(device, int) else device
         self.name = name
         self.fuse = fuse
@@ -114,6 +118,8 @@ class Program:
         self.input_shapes: list[tuple] = []
         self.input_dtypes: list[torch.dtype] = []
         self.graph = None
+        self._host = None  # pinned output staging for CPU callers
+        self._host_status = None
         frozen = frozen or set()
         env: dict[fx.Node, Val] = {}
         users = {node: len(node.users) for node in gm.graph.nodes}
@@ -339,7 +345,8 @@ class Program:
         n, c, h, wd = x.shape
         f, c2, kh, kw = w.shape
         assert c == c2
-        layer = CimLayer(torch.as_tensor(w).detach().float().reshape(f, -1), device=self.device)
+        layer = CimLayer(torch.as_tensor(w).detach().float().reshape(f, -1), device=self.device,
+                         compensation=self.compensation)
         self._keep.append(layer)
         g, xt = self._image_gather(x, kh, kw, stride[0], pad[0])
         m = n * g.out_h * g.out_w
@@ -401,7 +408,8 @@ class Program:
             raise NotImplementedError("linear lowers 2-D inputs")
         m, k = x.shape
         n = w.shape[0]
-        layer = CimLayer(torch.as_tensor(w).detach().float(), device=self.device)
+        layer = CimLayer(torch.as_tensor(w).detach().float(), device=self.device,
+                         compensation=self.compensation)
         self._keep.append(layer)
         act, out_node = self._epilogue(node, users)
         out = self._new((m, n))
@@ -701,8 +709,22 @@ class Program:
                 raise ValueError(f"input must be {dtype} {shape}")
             slot.tensor.copy_(v, non_blocking=True)
         self.replay()
-        outs = [t.to("cpu") if on_cpu else t.clone() for t in self.output_tensors]
-        self.check_status()
+        if on_cpu:
+            # Outputs and the status word come back in one pinned staging
+            # area with a single synchronization.
+            if self._host is None:
+                self._host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                              for t in self.output_tensors]
+                self._host_status = torch.empty(1, dtype=torch.int32, pin_memory=True)
+            for h, t in zip(self._host, self.output_tensors):
+                h.copy_(t, non_blocking=True)
+            self._host_status.copy_(self.status.tensor, non_blocking=True)
+            torch.cuda.current_stream(self.device).synchronize()
+            cim_ops.raise_status(int(self._host_status[0]), f"{self.name}: ")
+            outs = [h.clone() for h in self._host]
+        else:
+            outs = [t.clone() for t in self.output_tensors]
+            self.check_status()
         return tuple(outs) if self._output_is_tuple else outs[0]
 
     @property
@@ -712,8 +734,8 @@ class Program:
 
 def from_module(model: torch.nn.Module, example: torch.Tensor, device: int = 0,
                 name: str = "cim_program", fuse: bool = True,
-                layout: str = "nchw") -> Program:
+                layout: str = "nchw", bf16_compensation: str = "sign-split") -> Program:
     """Lower an eval-mode module by symbolic tracing, freezing its parameters."""
     gm = fx.symbolic_trace(model)
     return Program(gm, [example], frozen=set(), device=device, name=name, fuse=fuse,
-                   layout=layout)
+                   layout=layout, bf16_compensation=bf16_compensation)

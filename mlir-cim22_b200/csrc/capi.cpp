@@ -40,6 +40,12 @@ const char *cim22_cuda_status_message(int32_t status) {
     return "CIM nonnegative BF16 mode rejects negative inputs";
   if (status & CIM22_STATUS_TIMEOUT)
     return "CIM tensor-core pipeline wait timed out";
+  if (status & CIM22_STATUS_LEGACY_SCALING)
+    return "CIM legacy BF16 group scaling changed prealigned input mantissas";
+  if (status & CIM22_STATUS_LEGACY_I21)
+    return "CIM BF16 result exceeds signed i21 range";
+  if (status & CIM22_STATUS_CHIP_NOT_FINITE)
+    return "CIM BF16 chip output is not finite";
   return "";
 }
 

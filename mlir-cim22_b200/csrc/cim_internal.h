@@ -94,6 +94,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 struct cim22_cuda_layer {
   int device = 0;
   bool bf16 = false;
+  int mode = CIM22_BF16_SIGN_SPLIT; // BF16 compensation (Legacy / None: signed, unsplit)
   int64_t n = 0, k = 0;         // logical output lanes and reduction length
   int64_t n_pad = 0, k_pad = 0; // padded to kLanePad and 64
   int64_t tiles = 0;            // K tiles (k_pad / 64)
@@ -101,7 +102,9 @@ struct cim22_cuda_layer {
   // BF16: int8 mantissas [2][n_pad][k_pad] (Wp then Wn) and int32 lane
   // exponents [2][tiles][n_pad], the per-tile, per-32-lane-block
   // weight-exponent ranges [tiles][n_pad / 32][4] and the f32 weight scales
-  // 2^(Ew - 133) [2][tiles][n_pad]. INT8: int8 [n_pad][k_pad].
+  // 2^(Ew - 133) [2][tiles][n_pad]. BF16 Legacy / None: int8 [n_pad][k_pad]
+  // signed, int32 exponents [tiles][n_pad] then per (tile, 16-lane tile) a
+  // flag for a lane of all -128 mantissas. INT8: int8 [n_pad][k_pad].
   int8_t *weights = nullptr;
   int32_t *exponents = nullptr;
 };

@@ -974,6 +974,198 @@ Gather32 to_device_gather(const cim22_gather &g, int64_t m, int64_t k, const flo
   return d;
 }
 
+
+// ---------------------------------------------------------------------------
+// Legacy and None BF16 compensation (diagnostic modes, no sign split): the
+// BF16-rounded signed activations and weights go through one contraction.
+// Per 64-element group: prepareBF16Input (BF16Compensation.cpp:84-137) -
+// non-finite inputs rejected, prealignment at the raw maximum exponent, and
+// for Legacy the group scaling by 2^-scaleDelta with scaleDelta =
+// max(0, Eprealigned - 240) that must leave the mantissas unchanged. Per
+// (column, lane, tile): the signed dot with its i21 gate, int21ToBF16 with
+// the weight exponent only in None mode, the mode's restore
+// (BF16Compensation.cpp:149-164), then the Host f32 sum in tile order with a
+// final BF16 rounding when T > 1 (Passes.cpp:828-857), + bias.
+//
+// Workspace: int8 A[m_pad][k_pad], int32 ie[T][m_pad] (the prealign
+// exponent), int32 sd[T][m_pad] (Legacy scaleDelta in bits 0-7, bit 8 set
+// when every prealigned mantissa of the group is -128).
+
+constexpr int kAllMinus128 = 0x100;
+
+template <int kMode>
+__global__ void __launch_bounds__(256)
+    prepare_mode_kernel(const float *__restrict__ x, Gather32 g, int T, int m_pad, int k_pad,
+                        int compensation, int8_t *__restrict__ A, int32_t *__restrict__ ie,
+                        int32_t *__restrict__ sd, int32_t *status) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t group = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (group >= static_cast<int64_t>(m_pad) * T)
+    return;
+  const int m = static_cast<int>(group / T), t = static_cast<int>(group % T);
+  uint16_t bits[kTileK];
+  int exp_max = 0;
+  bool nonfinite = false;
+#pragma unroll 1
+  for (int s8 = 0; s8 < 8; ++s8) {
+    const int kbeg = t * kTileK + s8 * 8;
+    const Taps8 tp = make_taps8<kMode>(g, kbeg);
+    float v[8];
+    gather8<kMode>(x, g, tp, m, kbeg, v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint16_t b = f32_to_bf16(v[e]);
+      bits[s8 * 8 + e] = b;
+      const int ex = (b >> 7) & 0xff;
+      nonfinite |= ex == 0xff;
+      exp_max = max(exp_max, ex);
+    }
+  }
+  int8_t *dst = A + static_cast<int64_t>(m) * k_pad + t * kTileK;
+  int delta = 0;
+  bool all_min = true;
+  if (nonfinite) {
+    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
+    exp_max = 0;
+    for (int i = 0; i < kTileK; ++i)
+      dst[i] = 0;
+    all_min = false;
+  } else {
+    for (int i = 0; i < kTileK; ++i) {
+      dst[i] = prealign_element(bits[i], exp_max);
+      all_min &= dst[i] == -128;
+    }
+    if (compensation == CIM22_BF16_LEGACY) {
+      delta = max(0, exp_max - 240);
+      if (delta) {
+        int scaled_max = 0;
+        uint16_t scaled[kTileK];
+        for (int i = 0; i < kTileK; ++i) {
+          scaled[i] = bf16_scalbn(bits[i], -delta);
+          scaled_max = max(scaled_max, (scaled[i] >> 7) & 0xff);
+        }
+        bool same = scaled_max <= 240;
+        for (int i = 0; i < kTileK && same; ++i)
+          same = prealign_element(scaled[i], scaled_max) == dst[i];
+        if (!same)
+          atomicOr(status, CIM22_STATUS_LEGACY_SCALING);
+        exp_max = scaled_max;
+      }
+    }
+  }
+  ie[static_cast<int64_t>(t) * m_pad + m] = exp_max;
+  sd[static_cast<int64_t>(t) * m_pad + m] = delta | (all_min ? kAllMinus128 : 0);
+}
+
+// CTA tile 64 columns x 32 lanes; thread (tr, tc) owns columns tr, tr + 32
+// and lanes 4 tc .. 4 tc + 3.
+__global__ void __launch_bounds__(256)
+    mode_simt_kernel(const int8_t *__restrict__ A, const int32_t *__restrict__ ie,
+                     const int32_t *__restrict__ sd, int m_pad, const int8_t *__restrict__ B,
+                     const int32_t *__restrict__ exB, const int32_t *__restrict__ wmin,
+                     int n_pad, int k_pad, int T, int M, int N, int compensation,
+                     const float *__restrict__ bias, const float *__restrict__ post_scale,
+                     const float *__restrict__ post_shift, int act, int out_pixels,
+                     float *__restrict__ y, int32_t *status) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ __align__(16) int8_t As[64][kRowStride];
+  __shared__ __align__(16) int8_t Bs[32][kRowStride];
+  __shared__ int sIe[64], sSd[64], sEw[32], sMin[2];
+  const int tid = static_cast<int>(threadIdx.x);
+  const int tr = tid / 8, tc = tid % 8;
+  const int m0 = static_cast<int>(blockIdx.x) * 64, n0 = static_cast<int>(blockIdx.y) * 32;
+  float acc[2][4];
+  for (int t = 0; t < T; ++t) {
+    for (int i = tid; i < 64 * 4; i += 256) {
+      const int r = i / 4, c = i % 4;
+      *reinterpret_cast<int4 *>(&As[r][c * 16]) = *reinterpret_cast<const int4 *>(
+          A + static_cast<int64_t>(m0 + r) * k_pad + t * kTileK + c * 16);
+    }
+    for (int i = tid; i < 32 * 4; i += 256) {
+      const int r = i / 4, c = i % 4;
+      *reinterpret_cast<int4 *>(&Bs[r][c * 16]) = *reinterpret_cast<const int4 *>(
+          B + static_cast<int64_t>(n0 + r) * k_pad + t * kTileK + c * 16);
+    }
+    if (tid < 64) {
+      sIe[tid] = ie[static_cast<int64_t>(t) * m_pad + m0 + tid];
+      sSd[tid] = sd[static_cast<int64_t>(t) * m_pad + m0 + tid];
+    } else if (tid < 96) {
+      sEw[tid - 64] = exB[static_cast<int64_t>(t) * n_pad + n0 + tid - 64];
+    } else if (tid < 98) {
+      // Some lane of this 16-lane weight tile is all -128 (Legacy validation).
+      sMin[tid - 96] = wmin[static_cast<int64_t>(t) * (n_pad / 16) + n0 / 16 + tid - 96];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = tr + 32 * r;
+      const int ie_r = sIe[row], sd_r = sSd[row];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int lane = 4 * tc + c;
+        int p = 0;
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          p = __dp4a(*reinterpret_cast<const int *>(&As[row][q * 4]),
+                     *reinterpret_cast<const int *>(&Bs[lane][q * 4]), p);
+        const bool live = m0 + row < M && n0 + lane < N;
+        if (compensation == CIM22_BF16_LEGACY && (sd_r & kAllMinus128) && sMin[lane / 16]) {
+          // validateBF16Group rejects the Work before its dots are formed.
+          if (live)
+            atomicOr(status, CIM22_STATUS_LEGACY_I21);
+          p = 0;
+        } else if (p < -(1 << 20) || p >= (1 << 20)) {
+          if (live)
+            atomicOr(status, CIM22_STATUS_I21_RANGE);
+          p = 0;
+        }
+        const int ew = sEw[lane];
+        const uint16_t chip =
+            int21_to_bf16(p, compensation == CIM22_BF16_NONE ? ew : 0, ie_r);
+        uint16_t tile = chip;
+        if (compensation == CIM22_BF16_LEGACY) {
+          int error = 0;
+          if (!compensate(chip, ew + (sd_r & 0xff) - 133, tile, error)) {
+            if (live)
+              atomicOr(status, error == 1 ? CIM22_STATUS_CHIP_NOT_FINITE
+                                          : CIM22_STATUS_TILE_OVERFLOW);
+            tile = 0;
+          }
+        }
+        const float v = bf16_to_f32(tile);
+        acc[r][c] = t == 0 ? v : __fadd_rn(acc[r][c], v);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = m0 + tr + 32 * r;
+    if (row >= M)
+      continue;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int lane = n0 + 4 * tc + c;
+      if (lane >= N)
+        continue;
+      float out = T > 1 ? bf16_to_f32(f32_to_bf16(acc[r][c])) : acc[r][c];
+      if (bias != nullptr)
+        out = __fadd_rn(out, bias[lane]);
+      if (post_scale != nullptr)
+        out = __fmaf_rn(out, post_scale[lane], post_shift[lane]);
+      out = apply_act(out, act);
+      if (out_pixels > 0) {
+        const int image = row / out_pixels;
+        y[(static_cast<int64_t>(image) * N + lane) * out_pixels + (row - image * out_pixels)] =
+            out;
+      } else {
+        y[static_cast<int64_t>(row) * N + lane] = out;
+      }
+    }
+  }
+}
 } // namespace
 
 // Host-side BF16 weight preparation: split, RNE, prealign per lane and K tile.
@@ -1104,6 +1296,77 @@ cim22_cuda_layer *cim22_cuda_layer_create_bf16(int device, const float *weight,
   return layer;
 }
 
+cim22_cuda_layer *cim22_cuda_layer_create_bf16_mode(int device, const float *weight,
+                                                    int64_t n, int64_t k, int32_t compensation,
+                                                    char *error, size_t error_capacity) {
+  if (compensation == CIM22_BF16_SIGN_SPLIT)
+    return cim22_cuda_layer_create_bf16(device, weight, n, k, error, error_capacity);
+  if (compensation != CIM22_BF16_LEGACY && compensation != CIM22_BF16_NONE) {
+    copy_error("BF16 compensation must be sign-split, legacy or none", error, error_capacity);
+    return nullptr;
+  }
+  if (!weight || n <= 0 || k <= 0) {
+    copy_error("invalid CIM layer shape", error, error_capacity);
+    return nullptr;
+  }
+  for (int64_t i = 0; i < n * k; ++i)
+    if (!std::isfinite(weight[i])) {
+      copy_error("BF16 correction requires finite fixed weights", error, error_capacity);
+      return nullptr;
+    }
+  auto *layer = new cim22_cuda_layer();
+  layer->device = device;
+  layer->bf16 = true;
+  layer->mode = compensation;
+  layer->n = n;
+  layer->k = k;
+  layer->n_pad = round_up(n, kLanePad);
+  layer->k_pad = round_up(k, kTileK);
+  layer->tiles = layer->k_pad / kTileK;
+  const int64_t T = layer->tiles, n_pad = layer->n_pad, k_pad = layer->k_pad;
+  // Signed BF16 weights prealigned per (lane, K tile) at the lane's raw
+  // maximum exponent (prealignBF16WeightTile, BF16Support.cpp:56-70), then
+  // per (K tile, 16-lane tile) whether some lane is all -128.
+  std::vector<int8_t> mant(n_pad * k_pad, 0);
+  std::vector<int32_t> exps(T * n_pad + T * (n_pad / 16), 0);
+  uint16_t group[kTileK];
+  for (int64_t lane = 0; lane < n; ++lane)
+    for (int64_t t = 0; t < T; ++t) {
+      int exp_max = 0;
+      for (int i = 0; i < kTileK; ++i) {
+        const int64_t col = t * kTileK + i;
+        group[i] = col < k ? f32_to_bf16(weight[lane * k + col]) : 0;
+        exp_max = std::max(exp_max, (group[i] >> 7) & 0xff);
+      }
+      bool all_min = true;
+      for (int i = 0; i < kTileK; ++i) {
+        const int8_t v = prealign_element(group[i], exp_max);
+        mant[lane * k_pad + t * kTileK + i] = v;
+        all_min &= v == -128;
+      }
+      exps[t * n_pad + lane] = exp_max;
+      if (all_min)
+        exps[T * n_pad + t * (n_pad / 16) + lane / 16] = 1;
+    }
+  if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice") ||
+      !cuda_ok(cudaMalloc(&layer->weights, mant.size()), "cudaMalloc") ||
+      !cuda_ok(cudaMalloc(&layer->exponents, exps.size() * sizeof(int32_t)), "cudaMalloc") ||
+      !cuda_ok(cudaMemcpy(layer->weights, mant.data(), mant.size(), cudaMemcpyHostToDevice),
+               "cudaMemcpy") ||
+      !cuda_ok(cudaMemcpy(layer->exponents, exps.data(), exps.size() * sizeof(int32_t),
+                          cudaMemcpyHostToDevice),
+               "cudaMemcpy")) {
+    copy_error(last_error(), error, error_capacity);
+    cim22_cuda_layer_destroy(layer);
+    return nullptr;
+  }
+  return layer;
+}
+
+int32_t cim22_cuda_layer_compensation(const cim22_cuda_layer *layer) {
+  return layer ? layer->mode : -1;
+}
+
 cim22_cuda_layer *cim22_cuda_layer_create_int8(int device, const int8_t *weight,
                                                int64_t n, int64_t k,
                                                char *error,
@@ -1158,6 +1421,9 @@ size_t cim22_cuda_layer_workspace_bf16(const cim22_cuda_layer *layer,
   if (!layer || m <= 0)
     return 0;
   const int64_t m_pad = round_up(m, kColumnPad);
+  if (layer->mode != CIM22_BF16_SIGN_SPLIT)
+    return static_cast<size_t>(round_up(m_pad * layer->k_pad, 256) +
+                               2 * layer->tiles * m_pad * 4);
   const int64_t ab = branches == 2 ? 1 : 2;
   const int64_t a_bytes = round_up(ab * m_pad * layer->k_pad, 256);
   return static_cast<size_t>(a_bytes + ab * layer->tiles * m_pad * 4);
@@ -1196,6 +1462,27 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
   int32_t *ex = reinterpret_cast<int32_t *>(
       static_cast<char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
   const Gather32 dg = to_device_gather(g, m, layer->k, x);
+  if (layer->mode != CIM22_BF16_SIGN_SPLIT) {
+    // Legacy / None: one thread per (column, K tile) group.
+    int32_t *ie = reinterpret_cast<int32_t *>(static_cast<char *>(workspace) +
+                                              round_up(m_pad * layer->k_pad, 256));
+    int32_t *sd = ie + T * m_pad;
+    const unsigned blocks = static_cast<unsigned>((m_pad * T + 255) / 256);
+    const int mode = g.kind == CIM22_GATHER_ROWS ? kPrepRows
+                     : g.pool_kernel > 0         ? kPrepConvPool
+                                                 : kPrepConv;
+    auto go = [&](auto kernel) {
+      launch_pdl(kernel, blocks, 256, 0, s, x, dg, T, static_cast<int>(m_pad),
+                 static_cast<int>(layer->k_pad), layer->mode, A, ie, sd, status);
+    };
+    if (mode == kPrepRows)
+      go(prepare_mode_kernel<kPrepRows>);
+    else if (mode == kPrepConv)
+      go(prepare_mode_kernel<kPrepConv>);
+    else
+      go(prepare_mode_kernel<kPrepConvPool>);
+    return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+  }
   // The thread-per-group NCHW kernel serves layers of few K tiles (small
   // channel counts, K padding) over enough columns to fill the GPU; layers of
   // nine or more tiles and short column counts (a flatten -> Linear over a
@@ -1243,6 +1530,27 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
   return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
 }
 
+// Legacy / None layers: the CUDA-core contraction over the mode's workspace.
+static int contract_mode(const cim22_cuda_layer *layer, int64_t m, int64_t out_pixels,
+                         const float *bias, const float *post_scale, const float *post_shift,
+                         int32_t activation, float *y, const void *workspace, int32_t *status,
+                         cudaStream_t s) {
+  const int64_t m_pad = round_up(m, kColumnPad);
+  const int T = static_cast<int>(layer->tiles);
+  const int8_t *A = static_cast<const int8_t *>(workspace);
+  const int32_t *ie = reinterpret_cast<const int32_t *>(
+      static_cast<const char *>(workspace) + round_up(m_pad * layer->k_pad, 256));
+  const int32_t *sd = ie + T * m_pad;
+  const int32_t *wmin = layer->exponents + T * layer->n_pad;
+  const dim3 grid(static_cast<unsigned>(m_pad / 64), static_cast<unsigned>((layer->n + 31) / 32));
+  launch_pdl(mode_simt_kernel, grid, 256, 0, s, A, ie, sd, static_cast<int>(m_pad),
+             layer->weights, layer->exponents, wmin, static_cast<int>(layer->n_pad),
+             static_cast<int>(layer->k_pad), T, static_cast<int>(m), static_cast<int>(layer->n),
+             layer->mode, bias, post_scale, post_shift, activation,
+             static_cast<int>(out_pixels), y, status);
+  return cuda_ok(cudaGetLastError(), "mode contraction launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+}
+
 int cim22_cuda_layer_contract_bf16_ex(const cim22_cuda_layer *layer, int64_t m,
                                       int64_t out_pixels, const float *bias,
                                       const float *post_scale, const float *post_shift,
@@ -1258,6 +1566,9 @@ int cim22_cuda_layer_contract_bf16_ex(const cim22_cuda_layer *layer, int64_t m,
     return CIM22_STATUS_BAD_ARGUMENT;
   }
   auto s = static_cast<cudaStream_t>(stream);
+  if (layer->mode != CIM22_BF16_SIGN_SPLIT)
+    return contract_mode(layer, m, out_pixels, bias, post_scale, post_shift, activation, y,
+                         workspace, status, s);
   const int64_t m_pad = round_up(m, kColumnPad);
   const int ab = branches == 2 ? 1 : 2;
   const int T = static_cast<int>(layer->tiles);
@@ -1357,7 +1668,10 @@ int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float 
 }
 
 int cim22_cuda_layer_fused_forward(const cim22_cuda_layer *layer) {
-  return layer && layer->bf16 && layer->n <= 16 && layer->tiles <= 2 ? 1 : 0;
+  return layer && layer->bf16 && layer->mode == CIM22_BF16_SIGN_SPLIT && layer->n <= 16 &&
+                 layer->tiles <= 2
+             ? 1
+             : 0;
 }
 
 int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,

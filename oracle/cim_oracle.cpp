@@ -1192,6 +1192,88 @@ int oracle_linear_bf16(const float *x, int64_t m, int64_t k, const float *w,
   return 0;
 }
 
+// BF16 CIM layer in the Legacy or None compensation mode (mode = 1 or 0):
+// no sign split (the SplitCIMBF16Signs pass returns early for these modes,
+// Passes.cpp:2343-2344), so the BF16-rounded signed weights and activations
+// go through one contraction. Per (column, 16-lane N tile, K tile) Work the
+// runner's arithmetic applies (CIMSoftwareRunner.cpp:357-365,406-430):
+// prepareBF16Input in the mode, the Legacy all -128 validation, the signed
+// dot with its i21 gate, int21ToBF16 with the weight exponent only in None
+// mode, and the mode's restore; then the Host f32 sum in tile order with a
+// final truncf when T > 1 (Passes.cpp:828-857), then + bias.
+int oracle_linear_bf16_mode(const float *x, int64_t m, int64_t k, const float *w, int64_t n,
+                            const float *bias, int mode, float *y, char *error,
+                            size_t capacity) {
+  if (mode != kNone && mode != kLegacy) {
+    copyError("oracle_linear_bf16_mode handles the legacy and none modes", error, capacity);
+    return 1;
+  }
+  for (int64_t i = 0; i < n * k; ++i)
+    if (!std::isfinite(w[i])) {
+      copyError("BF16 correction requires finite fixed weights", error, capacity);
+      return 1;
+    }
+  const int64_t T = (k + kIn - 1) / kIn, J = (n + kOut - 1) / kOut;
+  std::vector<int8_t> values(J * T * kOut * kIn);
+  std::vector<uint8_t> exps(J * T * kOut);
+  std::vector<uint16_t> bits(kOut * kIn);
+  for (int64_t j = 0; j < J; ++j)
+    for (int64_t t = 0; t < T; ++t) {
+      std::fill(bits.begin(), bits.end(), 0);
+      for (int lane = 0; lane < kOut; ++lane)
+        for (int i = 0; i < kIn; ++i) {
+          const int64_t row = j * kOut + lane, col = t * kIn + i;
+          if (row < n && col < k)
+            bits[lane * kIn + i] = floatToBF16(w[row * k + col]);
+        }
+      prealignTile(bits.data(), values.data() + (j * T + t) * kOut * kIn,
+                   exps.data() + (j * T + t) * kOut);
+    }
+  std::vector<uint16_t> row(T * kIn);
+  std::vector<std::array<uint16_t, kOut>> tiles(T);
+  std::array<float, kOut> sums;
+  for (int64_t col = 0; col < m; ++col) {
+    std::fill(row.begin(), row.end(), 0);
+    for (int64_t i = 0; i < k; ++i)
+      row[i] = floatToBF16(x[col * k + i]);
+    for (int64_t j = 0; j < J; ++j) {
+      for (int64_t t = 0; t < T; ++t) {
+        Prepared p;
+        std::string message;
+        const int8_t *vals = values.data() + (j * T + t) * kOut * kIn;
+        const uint8_t *ew = exps.data() + (j * T + t) * kOut;
+        if (!prepareInput(row.data() + t * kIn, mode, p, message) ||
+            !validateGroup(vals, ew, p, mode, message)) {
+          copyError(message, error, capacity);
+          return 1;
+        }
+        for (int lane = 0; lane < kOut; ++lane) {
+          int32_t sum = 0;
+          for (int i = 0; i < kIn; ++i)
+            sum += static_cast<int32_t>(vals[lane * kIn + i]) * p.aligned.mantissas[i];
+          if (sum < kI21Min || sum >= kI21MaxExclusive) {
+            copyError("CIM software result exceeds signed i21 range", error, capacity);
+            return 1;
+          }
+          const uint16_t chip =
+              int21ToBF16(sum, mode == kNone ? ew[lane] : 0, p.aligned.exponent);
+          if (!restoreOutput(chip, ew[lane], true, p, mode, tiles[t][lane], message)) {
+            copyError(message, error, capacity);
+            return 1;
+          }
+        }
+      }
+      accumulate(tiles, sums.data());
+      for (int lane = 0; lane < kOut; ++lane) {
+        const int64_t o = j * kOut + lane;
+        if (o < n)
+          y[col * n + o] = bias ? sums[lane] + bias[o] : sums[lane];
+      }
+    }
+  }
+  return 0;
+}
+
 // The same layer driven through the restated runner exactly as compiled
 // models drive the software runner: per column, every (branch, N tile,
 // K tile) Work is packed into transactions of at most 40 Works (20 Cores x 2

@@ -78,6 +78,9 @@ def lib() -> ctypes.CDLL:
         L.oracle_int8_range_safe.argtypes = [c.c_void_p, c.c_int64, c.c_int64]
         L.oracle_linear_int8.argtypes = [c.c_void_p, c.c_int64, c.c_int64, c.c_void_p,
                                          c.c_int64, c.c_void_p, c.c_char_p, c.c_size_t]
+        L.oracle_linear_bf16_mode.argtypes = [c.c_void_p, c.c_int64, c.c_int64, c.c_void_p,
+                                              c.c_int64, c.c_void_p, c.c_int, c.c_void_p,
+                                              c.c_char_p, c.c_size_t]
         for name in ("oracle_linear_bf16", "oracle_linear_bf16_runner"):
             getattr(L, name).argtypes = [c.c_void_p, c.c_int64, c.c_int64, c.c_void_p,
                                          c.c_int64, c.c_void_p, c.c_int, c.c_void_p,
@@ -263,6 +266,26 @@ def linear_bf16(x: np.ndarray, w: np.ndarray, bias: np.ndarray | None = None,
     return y
 
 
+MODES = {"none": 0, "legacy": 1}
+
+
+def linear_bf16_mode(x: np.ndarray, w: np.ndarray, bias: np.ndarray | None = None,
+                     mode: str = "legacy") -> np.ndarray:
+    """BF16 CIM layer in the Legacy or None compensation mode (no sign split)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    m, k = x.shape
+    n = w.shape[0]
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    y = np.zeros((m, n), np.float32)
+    err = _err()
+    if lib().oracle_linear_bf16_mode(x.ctypes.data, m, k, w.ctypes.data, n,
+                                     None if b is None else b.ctypes.data, MODES[mode],
+                                     y.ctypes.data, err, len(err)):
+        raise OracleError(err.value.decode())
+    return y
+
+
 def im2col(x: np.ndarray, kh: int, kw: int, stride: int, pad: int) -> tuple[np.ndarray, int, int]:
     """Columns (n, oh, ow) x K (c, i, j) of an NCHW batch (Passes.cpp:1185-1191)."""
     n, c, h, w = x.shape
@@ -288,22 +311,28 @@ def conv2d_bf16(x: np.ndarray, weight: np.ndarray, bias: np.ndarray | None, stri
     return y.reshape(n, oh, ow, f).transpose(0, 3, 1, 2).copy()
 
 
-def cim_forward(model, x, *, branches: int = 4, threads: int = 1, via_runner: bool = False):
+def cim_forward(model, x, *, branches: int = 4, threads: int = 1, via_runner: bool = False,
+                compensation: str = "sign-split"):
     """Run a torch model on CPU with every Linear/Conv2d computed by the oracle.
 
     Everything else runs as PyTorch CPU eager in f32, which is the reference's
-    own oracle for the float glue. Returns a NumPy array.
+    own oracle for the float glue. compensation "legacy" / "none" computes the
+    layers in those diagnostic modes. Returns a NumPy array.
     """
     import torch
 
     saved = {}
 
+    def contract(cols, weight, bias):
+        if compensation == "sign-split":
+            return linear_bf16(cols, weight, bias, branches, threads, via_runner)
+        return linear_bf16_mode(cols, weight, bias, compensation)
+
     def linear_forward(module):
         def fn(inp):
             flat = inp.detach().float().reshape(-1, inp.shape[-1]).numpy()
             bias = None if module.bias is None else module.bias.detach().float().numpy()
-            y = linear_bf16(flat, module.weight.detach().float().numpy(), bias,
-                            branches, threads, via_runner)
+            y = contract(flat, module.weight.detach().float().numpy(), bias)
             return torch.from_numpy(y).reshape(*inp.shape[:-1], y.shape[-1])
         return fn
 
@@ -313,10 +342,13 @@ def cim_forward(model, x, *, branches: int = 4, threads: int = 1, via_runner: bo
             assert module.stride[0] == module.stride[1]
             assert module.padding[0] == module.padding[1]
             bias = None if module.bias is None else module.bias.detach().float().numpy()
-            y = conv2d_bf16(inp.detach().float().numpy(), module.weight.detach().float().numpy(),
-                            bias, module.stride[0], module.padding[0], branches, threads,
-                            via_runner)
-            return torch.from_numpy(y)
+            weight = module.weight.detach().float().numpy()
+            f, c, kh, kw = weight.shape
+            cols, oh, ow = im2col(inp.detach().float().numpy(), kh, kw, module.stride[0],
+                                  module.padding[0])
+            y = contract(cols, weight.reshape(f, -1), bias)
+            n = inp.shape[0]
+            return torch.from_numpy(y.reshape(n, oh, ow, f).transpose(0, 3, 1, 2).copy())
         return fn
 
     for module in model.modules():

@@ -21,7 +21,9 @@ def test_rejects_unknown_runtime_and_grad():
     with pytest.raises(ValueError, match="runtime"):
         backend._validate({"runtime": "usb"})
     with pytest.raises(ValueError, match="sign-split"):
-        backend._validate({"bf16_compensation": "legacy"})
+        backend._validate({"bf16_compensation": "exact"})
+    for mode in ("sign-split", "legacy", "none"):
+        backend._validate({"bf16_compensation": mode})
     gm = torch.fx.symbolic_trace(torch.nn.ReLU())
     with torch.enable_grad(), pytest.raises(ValueError, match="no_grad"):
         backend.backend(gm, [torch.ones(2)], options={"runtime": "cuda"})
@@ -32,7 +34,7 @@ def test_frozen_parameters_are_identity_guarded(monkeypatch):
     module's frozen weights (python/cim22/backend.py:207-210)."""
 
     class FakeProgram:
-        def __init__(self, gm, example, frozen, device, name):
+        def __init__(self, gm, example, frozen, device, name, bf16_compensation):
             self.gm, self.example, self.frozen = gm, example, frozen
 
         def capture(self):

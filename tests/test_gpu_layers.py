@@ -393,3 +393,54 @@ def test_narrow_fused_linear_bit_exact(m, k, n, branches):
     got = layer.linear_bf16(torch.from_numpy(x).to(DEV), bias=torch.from_numpy(b).to(DEV),
                             branches=branches).cpu().numpy()
     np.testing.assert_array_equal(bits(got), bits(oracle.linear_bf16(x, w, b)))
+
+
+def nan_equal_bits(a, b):
+    """Bit equality with every NaN treated alike (the None mode returns raw
+    chip bits, and NaN payloads after f32 adds are not specified)."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    both_nan = np.isnan(a) & np.isnan(b)
+    return np.array_equal(np.where(both_nan, 0, a.view(np.uint32)),
+                          np.where(both_nan, 0, b.view(np.uint32)))
+
+
+@pytest.mark.parametrize("mode", ["legacy", "none"])
+@pytest.mark.parametrize("m,k,n,scale", [(70, 150, 40, 1.0), (300, 64, 16, 1e-3),
+                                         (33, 400, 130, 1e20), (5, 7, 3, 1e-25)])
+def test_linear_bf16_legacy_none_modes(mode, m, k, n, scale):
+    """The reference's diagnostic BF16 modes at layer level, vs the oracle."""
+    from cim22_b200.cim_ops import CimLayer
+
+    rng = np.random.default_rng(m + k + n)
+    x = (rng.standard_normal((m, k)) * scale).astype(np.float32)
+    x[rng.random((m, k)) < 0.2] = 0
+    w = (rng.standard_normal((n, k)) * 0.1).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    layer = CimLayer(w, compensation=mode)
+    try:
+        expected = oracle.linear_bf16_mode(x, w, b, mode)
+    except oracle.OracleError as e:
+        with pytest.raises(RuntimeError, match=str(e)):
+            layer.linear_bf16(torch.from_numpy(x).to(DEV), bias=torch.from_numpy(b).to(DEV))
+        return
+    got = layer.linear_bf16(torch.from_numpy(x).to(DEV), bias=torch.from_numpy(b).to(DEV))
+    assert nan_equal_bits(got.cpu().numpy(), expected)
+
+
+def test_legacy_mode_errors_match_reference_texts():
+    from cim22_b200.cim_ops import CimLayer
+
+    # All -128 prealigned input and weight lane: validateBF16Group rejects it.
+    x = np.full((2, 64), -1.0, np.float32)
+    w = np.full((3, 64), -1.0, np.float32)
+    with pytest.raises(RuntimeError, match="exceeds signed i21 range"):
+        oracle.linear_bf16_mode(x, w, None, "legacy")
+    with pytest.raises(RuntimeError, match="CIM BF16 result exceeds signed i21 range"):
+        CimLayer(w, compensation="legacy").linear_bf16(torch.from_numpy(x).to(DEV))
+    # NaN input.
+    x = np.ones((2, 64), np.float32)
+    x[1, 3] = np.nan
+    with pytest.raises(RuntimeError, match="NaN or infinity"):
+        CimLayer(np.ones((4, 64), np.float32), compensation="none").linear_bf16(
+            torch.from_numpy(x).to(DEV))

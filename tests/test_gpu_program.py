@@ -178,3 +178,27 @@ def test_torch_compile_int_mm():
             got = compiled(v)
         exp = (v.to(torch.int64) @ model.weight.to(torch.int64)).to(torch.int32)
         assert torch.equal(got, exp)
+
+
+@pytest.mark.parametrize("mode", ["legacy", "none"])
+def test_torch_compile_diagnostic_compensation_modes(mode):
+    """bf16_compensation="legacy" / "none" through torch.compile runtime="cuda"
+    against the oracle's layers in the same mode (exact glue: MLP)."""
+    from cim22_b200 import backend, workloads
+
+    name = backend.register()
+    model, x = workloads.build("mlp", 4)
+    compiled = torch.compile(model, backend=name, fullgraph=True, dynamic=False,
+                             options={"runtime": "cuda", "bf16_compensation": mode})
+    try:
+        expected = oracle.cim_forward(model, x.numpy(), compensation=mode)
+    except oracle.OracleError as e:
+        # None mode hands raw chip bits (non-finite here) to the next layer.
+        with torch.inference_mode(), pytest.raises(RuntimeError, match=str(e)):
+            compiled(x)
+        return
+    with torch.inference_mode():
+        got = compiled(x).numpy()
+    both_nan = np.isnan(got) & np.isnan(expected)
+    np.testing.assert_array_equal(np.where(both_nan, 0, bits(got)),
+                                  np.where(both_nan, 0, bits(expected)))
