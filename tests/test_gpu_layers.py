@@ -431,9 +431,10 @@ def test_linear_bf16_legacy_none_modes(mode, m, k, n, scale):
 def test_legacy_mode_errors_match_reference_texts():
     from cim22_b200.cim_ops import CimLayer
 
-    # All -128 prealigned input and weight lane: validateBF16Group rejects it.
-    x = np.full((2, 64), -1.0, np.float32)
-    w = np.full((3, 64), -1.0, np.float32)
+    # All -128 prealigned input and weight lane (-1.9921875 = BF16 0xbfff,
+    # mantissa 0xff at the group exponent): validateBF16Group rejects it.
+    x = np.full((2, 64), -1.9921875, np.float32)
+    w = np.full((3, 64), -1.9921875, np.float32)
     with pytest.raises(RuntimeError, match="exceeds signed i21 range"):
         oracle.linear_bf16_mode(x, w, None, "legacy")
     with pytest.raises(RuntimeError, match="CIM BF16 result exceeds signed i21 range"):
