@@ -374,7 +374,7 @@ __device__ __noinline__ float tc_slow_tile_add(float acc, int p, int ew, int ex,
 
 __device__ __forceinline__ float act_tc(float v, int act) {
   if (act == CIM22_ACT_RELU)
-    return v > 0.0f ? v : 0.0f;
+    return (v > 0.0f || v != v) ? v : 0.0f; // NaN propagates, as torch.relu
   if (act == CIM22_ACT_GELU)
     return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
   return v;
@@ -473,7 +473,7 @@ __device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, in
   if (act == CIM22_ACT_RELU) {
 #pragma unroll
     for (int j = 0; j < LT; ++j)
-      o[j] = o[j] > 0.0f ? o[j] : 0.0f;
+      o[j] = (o[j] > 0.0f || o[j] != o[j]) ? o[j] : 0.0f; // NaN propagates
   } else if (act == CIM22_ACT_GELU) {
 #pragma unroll
     for (int j = 0; j < LT; ++j)

@@ -18,7 +18,7 @@ unsigned grid_for(int64_t work, int threads = 256) {
 
 __device__ __forceinline__ float act_fn(float v, int act) {
   if (act == CIM22_ACT_RELU)
-    return v > 0.0f ? v : 0.0f;
+    return (v > 0.0f || v != v) ? v : 0.0f; // NaN propagates, as torch.relu
   if (act == CIM22_ACT_GELU)
     return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
   return v;

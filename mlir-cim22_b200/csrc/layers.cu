@@ -498,7 +498,7 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 3 : 1)
 
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == CIM22_ACT_RELU)
-    return v > 0.0f ? v : 0.0f;
+    return (v > 0.0f || v != v) ? v : 0.0f; // NaN propagates, as torch.relu
   if (act == CIM22_ACT_GELU)
     return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
   return v;

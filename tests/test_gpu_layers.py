@@ -445,3 +445,11 @@ def test_legacy_mode_errors_match_reference_texts():
     with pytest.raises(RuntimeError, match="NaN or infinity"):
         CimLayer(np.ones((4, 64), np.float32), compensation="none").linear_bf16(
             torch.from_numpy(x).to(DEV))
+
+
+def test_relu_propagates_nan_like_torch():
+    from cim22_b200 import cim_ops
+
+    x = torch.tensor([float("nan"), -1.0, 2.0, float("-inf"), float("inf"), -0.0])
+    got = cim_ops.relu(x.to(DEV)).cpu()
+    torch.testing.assert_close(got, torch.relu(x), equal_nan=True, rtol=0, atol=0)
