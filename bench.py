@@ -477,14 +477,26 @@ def main() -> None:
     info = next((l for l in prog.layers if dominant.startswith(l.name)), None)
     dur_s = avg[dominant] / 1000
     if step.cim and info is not None:
+        # Both roofs of a CIM layer step: the MMA work on the int8 tensor
+        # peak, and the bytes it must move (its source read once, int8
+        # weights of both signs, the f32 output) on HBM; the binding one is
+        # the one with the larger fraction.
         ops = 2 * info.macs
         achieved = ops / dur_s / 1e12
         int8_peak = 2 * bf16_peak
-        roof = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
-                "frac": achieved / int8_peak, "traffic": None, "kernel": dominant,
-                "ops_per_launch": ops, "launch_ms": avg[dominant],
-                "peak_note": f"int8 dense = 2 x {peak_kind} bf16 cuBLAS ({bf16_peak} TF/s); "
-                             "ops = 2 x branches x M x K x N (unpadded) as TOPS"}
+        layer_bytes = info.in_bytes + 2 * info.n * info.k + 4 * info.m * info.n
+        gbs = layer_bytes / dur_s / 1e9
+        tensor = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
+                  "frac": achieved / int8_peak, "ops_per_launch": ops,
+                  "peak_note": f"int8 dense = 2 x {peak_kind} bf16 cuBLAS ({bf16_peak} TF/s); "
+                               "ops = 2 x branches x M x K x N (unpadded) as TOPS"}
+        hbm = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+               "frac": gbs / hbm_peak, "bytes_per_launch": layer_bytes,
+               "peak_note": f"{peak_kind} HBM copy bandwidth"}
+        first, other = (tensor, hbm) if tensor["frac"] >= hbm["frac"] else (hbm, tensor)
+        roof = dict(first, traffic=None, kernel=dominant, launch_ms=avg[dominant],
+                    other_roof={k: other[k] for k in ("bound", "achieved", "peak", "unit",
+                                                       "frac")})
     else:
         algo = None
         if info is not None and dominant.endswith(".prepare"):
