@@ -269,6 +269,52 @@ void _mlir_ciface_cim22_dispatch_int8(int64_t id, cim22_memref2d *input,
                                       cim22_memref2d *output);
 
 /* ------------------------------------------------------------------------ */
+/* 2b. Compiled model libraries on a CUDA session.
+ *
+ * A model library exports `const CIM22ModelV1 *cim22_model_v1(void)`
+ * (include/CIM22/Runtime/ModelABI.h): ABI version 1, the Protobuf model
+ * artifact (schema/cim22_model.proto) and the MLIR packed-argument entry
+ * point. These functions replace cim22_session_* of runtime/Runtime.cpp
+ * with the same arguments, return values and error texts; the artifact's
+ * transactions run on a CUDA session instead of the software runner. */
+
+typedef struct cim22_cuda_model cim22_cuda_model;
+
+/* Decode and check an artifact (runtime/src/ModelArtifact.cpp:101-266,
+ * 444-478) without loading anything. Returns 0 when it is valid, else 1 with
+ * "invalid CIM22 Protobuf model: <reason>; recompile the model". */
+int cim22_cuda_model_validate(const uint8_t *data, uint64_t size, char *error,
+                              size_t error_capacity);
+/* Replaces cim22_session_load_shared (runtime/Runtime.cpp:73-114): dlopen
+ * (RTLD_NOW | RTLD_LOCAL), cim22_model_v1 ABI check ("incompatible CIM22
+ * model ABI"), artifact decode and check, then every kernel's transaction
+ * planned on a CUDA session on `device`. This library is promoted to global
+ * symbol scope first, so the model's _mlir_ciface_cim22_dispatch* references
+ * resolve to the CUDA dispatch above. */
+cim22_cuda_model *cim22_cuda_model_load_shared(const char *path, int device, char *error,
+                                               size_t error_capacity);
+void cim22_cuda_model_destroy(cim22_cuda_model *model);
+/* runtime/Runtime.cpp:252-291: -1 (or 0 for the count, "null session" for the
+ * error) on a null model or an index out of range. dtype is the artifact's
+ * DataType: 1 INT8, 3 FP32, 4 INT32. */
+int64_t cim22_cuda_model_num_inputs(const cim22_cuda_model *model);
+int64_t cim22_cuda_model_num_outputs(const cim22_cuda_model *model);
+int64_t cim22_cuda_model_rank(const cim22_cuda_model *model, int64_t tensor);
+int64_t cim22_cuda_model_dim(const cim22_cuda_model *model, int64_t tensor, int64_t axis);
+int64_t cim22_cuda_model_dtype(const cim22_cuda_model *model, int64_t tensor);
+int64_t cim22_cuda_model_num_transactions(const cim22_cuda_model *model);
+uint64_t cim22_cuda_model_dispatch_count(const cim22_cuda_model *model);
+const char *cim22_cuda_model_error(const cim22_cuda_model *model);
+/* Replaces cim22_session_invoke (runtime/Runtime.cpp:292-340): buffers are
+ * host pointers to contiguous row-major tensors, inputs then outputs, with
+ * counts[i] elements each; they are passed as MLIR ranked descriptors. Calls
+ * on one model are serialized. Returns 0, or 1 with the diagnostic in
+ * cim22_cuda_model_error ("runtime buffer count mismatch", "runtime buffer
+ * element count mismatch", or "kernel: <runner error>"). */
+int cim22_cuda_model_invoke(cim22_cuda_model *model, void **buffers, const int64_t *counts,
+                            int64_t num_buffers);
+
+/* ------------------------------------------------------------------------ */
 /* 3. Layer level, device memory, stream ordered.
  *
  * A CIM layer is a contraction y[m, n] = sum_k W[n, k] x[m, k] executed as the

@@ -67,7 +67,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     newest = max(o.stat().st_mtime for o in objs)
     if force or not OUT.exists() or OUT.stat().st_mtime < max(newest, EXPORTS.stat().st_mtime):
         cmd = [nvcc(), *ARCH, "-shared", "-o", str(OUT), *map(str, objs),
-               "-Xlinker", f"--version-script={EXPORTS}", "-lpthread"]
+               "-Xlinker", f"--version-script={EXPORTS}", "-lpthread", "-ldl"]
         subprocess.run(cmd, check=True)
     return OUT
 

@@ -44,6 +44,18 @@ _SIGNATURES = {
     "cim22_cuda_session_end_invoke": (c.c_int, [P]),
     "cim22_cuda_session_dispatch_count": (c.c_uint64, [P]),
     "cim22_cuda_session_error": (CHARP, [P]),
+    "cim22_cuda_model_validate": (c.c_int, [P, c.c_uint64, CHARP, SZ]),
+    "cim22_cuda_model_load_shared": (P, [CHARP, c.c_int, CHARP, SZ]),
+    "cim22_cuda_model_destroy": (None, [P]),
+    "cim22_cuda_model_num_inputs": (I64, [P]),
+    "cim22_cuda_model_num_outputs": (I64, [P]),
+    "cim22_cuda_model_rank": (I64, [P, I64]),
+    "cim22_cuda_model_dim": (I64, [P, I64, I64]),
+    "cim22_cuda_model_dtype": (I64, [P, I64]),
+    "cim22_cuda_model_num_transactions": (I64, [P]),
+    "cim22_cuda_model_dispatch_count": (c.c_uint64, [P]),
+    "cim22_cuda_model_error": (CHARP, [P]),
+    "cim22_cuda_model_invoke": (c.c_int, [P, c.POINTER(P), c.POINTER(I64), I64]),
     "_mlir_ciface_cim22_dispatch": (None, [I64, P, P]),
     "_mlir_ciface_cim22_dispatch_sign_split": (None, [I64, P, P]),
     "_mlir_ciface_cim22_dispatch_legacy": (None, [I64, P, P]),

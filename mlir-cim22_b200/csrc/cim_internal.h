@@ -18,6 +18,11 @@ const std::string &last_error();
 // convention of runtime/Runtime.cpp:64-71.
 void copy_error(const std::string &message, char *buffer, size_t capacity);
 
+// Makes every later dispatch on the session fail with `message` after the
+// descriptor checks and the output zero fill, as a USB-backend model without
+// a configured board does (runtime/Runtime.cpp:175-179).
+void session_refuse_dispatch(cim22_cuda_session *session, const std::string &message);
+
 inline bool cuda_ok(cudaError_t e, const char *what) {
   if (e == cudaSuccess)
     return true;

@@ -1041,9 +1041,17 @@ struct cim22_cuda_session {
   };
   std::vector<Entry> transactions;
   std::string error;
+  std::string refusal;
   uint64_t dispatches = 0;
   cim22_cuda_session *previous = nullptr;
 };
+
+namespace cim {
+void session_refuse_dispatch(cim22_cuda_session *session, const std::string &message) {
+  if (session)
+    session->refusal = message;
+}
+} // namespace cim
 
 namespace {
 thread_local cim22_cuda_session *active_session = nullptr;
@@ -1074,6 +1082,10 @@ void dispatch(int64_t id, cim22_memref2d *input, cim22_memref2d *output,
   std::fill_n(out, output->sizes[0] * 16, Output{0});
   if (!s.error.empty())
     return;
+  if (!s.refusal.empty()) {
+    s.error = s.refusal;
+    return;
+  }
   std::vector<const void *> rows(input->sizes[0]);
   std::vector<void *> outs(output->sizes[0]);
   for (int64_t i = 0; i < input->sizes[0]; ++i)
