@@ -517,6 +517,33 @@ int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,
                                   void *workspace, size_t workspace_bytes,
                                   int32_t *status, void *stream);
 
+/* INT8 layer with the compiler's INT8 Conv and bias lowerings
+ * (Passes.cpp:1402-1557, 1863-2012, 2049-2155):
+ *   gather      NULL or CIM22_GATHER_ROWS: x is int8 [m, k]. A conv gather
+ *               (NCHW or NHWC, no fused pool): x is an int8 image batch and
+ *               m = batch * out_h * out_w columns in (image, oh, ow) order,
+ *               K in (channel, kh, kw) order (weights [F][C][KH][KW]).
+ *   pad_bottom, pad_right
+ *               bottom/right zero padding of a conv gather when it differs
+ *               from pad_h/pad_w (ONNX ConvInteger pads); -1 = symmetric.
+ *   bias        optional int32 [n], added with int32 wraparound. The
+ *               compiler folds an int8-range bias into the crossbar as one
+ *               more K column (weight = bias, input = 1) when the range proof
+ *               allows, and leaves it as a Host add otherwise; both give this
+ *               exact sum.
+ *   out_pixels  0: y is [m, n]; > 0: y is NCHW [m / out_pixels][n][out_pixels].
+ *   exact_unproven
+ *               for weights that fail the i21 range proof: nonzero computes
+ *               the exact wrapping int32 sum, as the compiler keeps such an
+ *               op on the Host (Passes.cpp:592-627); zero runs the checked
+ *               per-tile kernel that reports CIM22_STATUS_I21_RANGE.
+ * Workspace: cim22_cuda_layer_workspace_int8(layer, m) bytes. */
+int cim22_cuda_layer_forward_int8_ex(const cim22_cuda_layer *layer, const int8_t *x,
+                                     const cim22_gather *gather, int64_t m, int32_t pad_bottom,
+                                     int32_t pad_right, const int32_t *bias, int64_t out_pixels,
+                                     int32_t exact_unproven, int32_t *y, void *workspace,
+                                     size_t workspace_bytes, int32_t *status, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Host glue the compiler emits around CIM layers (upstream Linalg lowering,
  * lib/Compiler/Pipelines.cpp:61-72). All f32, device memory; image layout

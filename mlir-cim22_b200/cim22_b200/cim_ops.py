@@ -182,6 +182,64 @@ class CimLayer:
             status.raise_if_set()
         return out
 
+    def forward_int8(self, x: torch.Tensor, out: torch.Tensor, m: int, *,
+                     gather: abi.Gather | None = None, pad_bottom: int = -1,
+                     pad_right: int = -1, bias: torch.Tensor | None = None,
+                     out_pixels: int = 0, exact_unproven: bool = True,
+                     workspace: Workspace, status: StatusWord) -> torch.Tensor:
+        """INT8 layer over int8 rows [m, k] or a conv gather of an int8 image
+        batch; out is int32 [m, n] rows, or NCHW [m / out_pixels, n,
+        out_pixels]. bias is int32 [n] (wrapping add). exact_unproven computes
+        weights that fail the i21 range proof exactly, as the compiler's Host
+        does; otherwise their tiles are checked (CIM22_STATUS_I21_RANGE)."""
+        _require(x, torch.int8, "x")
+        _require(out, torch.int32, "out")
+        if bias is not None:
+            _require(bias, torch.int32, "bias")
+        ws = workspace.get(self.workspace_bytes(m))
+        rc = lib().cim22_cuda_layer_forward_int8_ex(
+            self._handle, _ptr(x), None if gather is None else ctypes.byref(gather), m,
+            pad_bottom, pad_right, _ptr(bias), out_pixels, int(exact_unproven), _ptr(out),
+            _ptr(ws), ws.numel(), _ptr(status.tensor), _stream(x.device))
+        check(rc, "cim22_cuda_layer_forward_int8_ex")
+        return out
+
+    def conv2d_int8(self, x: torch.Tensor, kernel: tuple[int, int], stride=(1, 1),
+                    pads=(0, 0, 0, 0), bias: torch.Tensor | None = None, *,
+                    layout: str = "nchw", exact_unproven: bool = True,
+                    workspace: Workspace | None = None,
+                    status: StatusWord | None = None) -> torch.Tensor:
+        """ConvInteger of an int8 image batch (NCHW, or NHWC with layout="nhwc")
+        with this layer's [F, C * KH * KW] weights; pads are ONNX's (top, left,
+        bottom, right). Returns int32 NCHW [N, F, OH, OW]."""
+        kh, kw = kernel
+        sh, sw = (stride, stride) if isinstance(stride, int) else stride
+        top, left, bottom, right = pads
+        if layout == "nchw":
+            n, c, h, w = x.shape
+            kind = abi.GATHER_CONV_NCHW
+        else:
+            n, h, w, c = x.shape
+            kind = abi.GATHER_CONV_NHWC
+        g = abi.Gather()
+        g.kind = kind
+        g.batch, g.channels, g.height, g.width = n, c, h, w
+        g.kernel_h, g.kernel_w, g.stride_h, g.stride_w = kh, kw, sh, sw
+        g.pad_h, g.pad_w = top, left
+        g.out_h = (h + top + bottom - kh) // sh + 1
+        g.out_w = (w + left + right - kw) // sw + 1
+        pixels = g.out_h * g.out_w
+        out = torch.empty(n, self.n, g.out_h, g.out_w, dtype=torch.int32, device=x.device)
+        own_status = status is None
+        status = status or StatusWord(x.device)
+        self.forward_int8(x.contiguous(), out, n * pixels, gather=g, pad_bottom=bottom,
+                          pad_right=right, bias=bias, out_pixels=pixels,
+                          exact_unproven=exact_unproven,
+                          workspace=workspace or Workspace(x.device), status=status)
+        if own_status:
+            status.raise_if_set()
+        return out
+
     def linear_int8(self, x: torch.Tensor, workspace: Workspace | None = None,
                     status: StatusWord | None = None) -> torch.Tensor:
         _require(x, torch.int8, "x")

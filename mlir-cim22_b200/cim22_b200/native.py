@@ -70,6 +70,8 @@ _SIGNATURES = {
     "cim22_cuda_layer_workspace_int8": (SZ, [P, I64]),
     "cim22_cuda_layer_forward_bf16": (c.c_int, [P, P, P, I64, P, I32, I32, P, P, SZ, P, P]),
     "cim22_cuda_layer_forward_int8": (c.c_int, [P, P, I64, P, P, SZ, P, P]),
+    "cim22_cuda_layer_forward_int8_ex": (c.c_int, [P, P, P, I64, I32, I32, P, I64, I32, P, P,
+                                                   SZ, P, P]),
     "cim22_cuda_layer_prepare_bf16": (c.c_int, [P, P, P, I64, I32, P, SZ, P, P]),
     "cim22_cuda_layer_contract_bf16": (c.c_int, [P, I64, P, I32, I32, P, P, SZ, P, P]),
     "cim22_cuda_layer_forward_bf16_ex": (c.c_int, [P, P, P, I64, I64, P, P, P, I32, I32, P, P,

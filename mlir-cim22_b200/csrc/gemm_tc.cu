@@ -134,6 +134,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __global__ void __launch_bounds__(kThreads, 1)
     int8_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB, int num_kb, int64_t M, int64_t N,
+                   const int32_t *__restrict__ bias, int64_t out_pixels, FastDiv div_pix,
                    int32_t *__restrict__ y, int32_t *status) {
   extern __shared__ uint8_t smem_raw[];
   SmemInt8 &s = *reinterpret_cast<SmemInt8 *>(
@@ -212,17 +213,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0)
         atomicOr(status, CIM22_STATUS_TIMEOUT);
     } else {
+      // Row r of the tile is column m0 + r; with out_pixels the output is
+      // NCHW: column = image * out_pixels + pixel, lane = channel. The bias is
+      // an exact wrapping int32 add, as the Host adds it.
       const int64_t row = m0 + quad * 32 + lane;
+      int64_t base = row * N, step = 1;
+      if (out_pixels > 0 && row < M) {
+        const int64_t img = fdiv(static_cast<int>(row), div_pix);
+        base = img * N * out_pixels + (row - img * out_pixels);
+        step = out_pixels;
+      }
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + c * 32, r);
         if (row < M) {
-          int32_t *dst = y + row * N + n0 + c * 32;
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + c * 32 + j < N)
-              dst[j] = static_cast<int32_t>(r[j]);
+          for (int j = 0; j < 32; ++j) {
+            const int64_t n = n0 + c * 32 + j;
+            if (n < N)
+              y[base + n * step] =
+                  static_cast<int32_t>(r[j] + (bias ? static_cast<uint32_t>(bias[n]) : 0u));
+          }
         }
       }
     }
@@ -877,12 +889,14 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
 }
 
 bool launch_int8(const int8_t *A, int64_t a_rows, int64_t a_cols, const int8_t *B,
-                 int64_t n_pad, int64_t k_pad, int64_t M, int64_t N, int32_t *y,
-                 int32_t *status, cudaStream_t stream) {
+                 int64_t n_pad, int64_t k_pad, int64_t M, int64_t N, const int32_t *bias,
+                 int64_t out_pixels, int32_t *y, int32_t *status, cudaStream_t stream) {
   if (n_pad % kBN || k_pad % 64 || a_cols % 16 || a_cols > k_pad || a_rows < M ||
       M >= (int64_t{1} << 31) - kBM || (reinterpret_cast<uintptr_t>(A) & 15) ||
-      (reinterpret_cast<uintptr_t>(B) & 15))
+      (reinterpret_cast<uintptr_t>(B) & 15) || out_pixels < 0 ||
+      (out_pixels > 0 && M % out_pixels))
     return false;
+  const FastDiv div_pix = make_fastdiv(static_cast<uint32_t>(out_pixels > 0 ? out_pixels : 1));
   // Columns beyond a_cols (to k_pad) and rows beyond a_rows read TMA's zero fill.
   CUtensorMap ta, tb;
   if (!encode_int8_2d(&ta, A, a_rows, a_cols, kBM) || !encode_int8_2d(&tb, B, n_pad, k_pad, kBN))
@@ -893,7 +907,8 @@ bool launch_int8(const int8_t *A, int64_t a_rows, int64_t a_cols, const int8_t *
     return false;
   const int num_kb = static_cast<int>((k_pad + kBK - 1) / kBK);
   const dim3 grid(static_cast<unsigned>(m_pad / kBM), static_cast<unsigned>((N + kBN - 1) / kBN));
-  int8_tc_kernel<<<grid, kThreads, kSmemInt8, stream>>>(ta, tb, num_kb, M, N, y, status);
+  int8_tc_kernel<<<grid, kThreads, kSmemInt8, stream>>>(ta, tb, num_kb, M, N, bias,
+                                                        out_pixels, div_pix, y, status);
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
   return true;
 }

@@ -29,11 +29,14 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad,
                       int64_t out_pixels, float *y, int32_t *status,
                       cudaStream_t stream);
 
-// INT8 contraction with whole-K int32 accumulation for range-proven layers.
+// INT8 contraction with whole-K int32 accumulation (exact: range-proven
+// layers, or unproven ones computed as the Host computes them).
 // A is int8 [a_rows][a_cols] (a_cols <= k_pad, a multiple of 16; rows >= M),
-// B is the resident [n_pad][k_pad] weight matrix.
+// B is the resident [n_pad][k_pad] weight matrix. bias (optional) is a
+// wrapping int32 add per lane; out_pixels > 0 writes NCHW images
+// [M / out_pixels][N][out_pixels] instead of rows [M][N].
 bool launch_int8(const int8_t *A, int64_t a_rows, int64_t a_cols, const int8_t *B,
-                 int64_t n_pad, int64_t k_pad, int64_t M, int64_t N, int32_t *y,
-                 int32_t *status, cudaStream_t stream);
+                 int64_t n_pad, int64_t k_pad, int64_t M, int64_t N, const int32_t *bias,
+                 int64_t out_pixels, int32_t *y, int32_t *status, cudaStream_t stream);
 
 } // namespace cim::tc

@@ -813,10 +813,60 @@ __global__ void pad_int8_kernel(const int8_t *__restrict__ x, int64_t M,
   }
 }
 
+// Columns of an INT8 convolution (the im2col of normalizeCIMInt8Conv,
+// Passes.cpp:1511-1552): A[m][k] for column m = (image, oh, ow) and
+// k = (c * KH + i) * KW + j is the input at row oh * SH - PH + i, column
+// ow * SW - PW + j of channel c, zero outside the image (padding), for
+// k >= K and for m >= M. One thread writes 16 consecutive bytes of a row.
+__global__ void __launch_bounds__(256)
+    im2col_int8_kernel(const int8_t *__restrict__ x, Gather32 g, int64_t m_pad, int64_t k_pad,
+                       int8_t *__restrict__ A) {
+  pdl_wait();
+  const int chunks = static_cast<int>(k_pad / 16);
+  const int64_t total = m_pad * chunks;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(i / chunks);
+    const int kb = static_cast<int>(i - static_cast<int64_t>(m) * chunks) * 16;
+    uint32_t word[4] = {0, 0, 0, 0};
+    if (m < g.M && kb < g.K) {
+      const int n = fdiv(m, g.div_ohw);
+      const int rm = m - n * g.OH * g.OW;
+      const int oh = fdiv(rm, g.div_ow);
+      const int ow = rm - oh * g.OW;
+      const int ih0 = oh * g.SH - g.PH, iw0 = ow * g.SW - g.PW;
+      const int8_t *img = x + static_cast<int64_t>(n) * g.image;
+      int c = fdiv(kb, g.div_khw);
+      const int rk = kb - c * g.KH * g.KW;
+      int ki = fdiv(rk, g.div_kw);
+      int kj = rk - ki * g.KW;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int ih = ih0 + ki, iw = iw0 + kj;
+        if (kb + e < g.K && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W) {
+          const uint32_t b = static_cast<uint8_t>(__ldg(img + c * g.sC + ih * g.sH + iw * g.sW));
+          word[e >> 2] |= b << (8 * (e & 3));
+        }
+        if (++kj == g.KW) {
+          kj = 0;
+          if (++ki == g.KH) {
+            ki = 0;
+            ++c;
+          }
+        }
+      }
+    }
+    *reinterpret_cast<uint4 *>(A + static_cast<int64_t>(m) * k_pad + kb) =
+        make_uint4(word[0], word[1], word[2], word[3]);
+  }
+  pdl_launch_dependents();
+}
+
 __global__ void __launch_bounds__(256)
     int8_simt_kernel(const int8_t *__restrict__ A, const int8_t *__restrict__ B,
                      int64_t k_pad, int T, int64_t M, int64_t N,
-                     int checked, int32_t *__restrict__ y, int32_t *status) {
+                     int checked, const int32_t *__restrict__ bias, int64_t out_pixels,
+                     FastDiv div_pix, int32_t *__restrict__ y, int32_t *status) {
   __shared__ __align__(16) int8_t As[64][kRowStride];
   __shared__ __align__(16) int8_t Bs[64][kRowStride];
   const int tid = threadIdx.x;
@@ -871,11 +921,21 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     const int64_t row = m0 + tr + 16 * r;
+    if (row >= M)
+      continue;
+    // Rows [M][N], or NCHW images [M / out_pixels][N][out_pixels].
+    int64_t base = row * N, step = 1;
+    if (out_pixels > 0) {
+      const int64_t img = fdiv(static_cast<int>(row), div_pix);
+      base = img * N * out_pixels + (row - img * out_pixels);
+      step = out_pixels;
+    }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const int64_t lane = n0 + tc * 4 + c;
-      if (row < M && lane < N)
-        y[row * N + lane] = static_cast<int32_t>(acc[r][c]);
+      if (lane < N)
+        y[base + lane * step] =
+            static_cast<int32_t>(acc[r][c] + (bias ? static_cast<uint32_t>(bias[lane]) : 0u));
     }
   }
 }
@@ -916,6 +976,37 @@ bool check_gather(const cim22_gather &g, int64_t m, int64_t k) {
   const int ow = (g.width + 2 * g.pad_w - g.kernel_w) / g.stride_w + 1;
   return oh == g.out_h && ow == g.out_w &&
          static_cast<int64_t>(g.batch) * oh * ow == m &&
+         static_cast<int64_t>(g.channels) * g.kernel_h * g.kernel_w == k;
+}
+
+// Gathers of INT8 layers: rows, or a convolution without a fused pool whose
+// bottom/right padding may differ from the top/left padding (pad_h, pad_w),
+// as ONNX ConvInteger pads allow; a negative pad_bottom/pad_right means the
+// same as the top/left one.
+bool check_gather_int8(const cim22_gather &g, int64_t m, int64_t k, int32_t pad_bottom,
+                       int32_t pad_right) {
+  if (m >= (int64_t{1} << 31) - kColumnPad || k >= (int64_t{1} << 30))
+    return false;
+  if (g.kind == CIM22_GATHER_ROWS)
+    return m * k < (int64_t{1} << 40);
+  if ((g.kind != CIM22_GATHER_CONV_NCHW && g.kind != CIM22_GATHER_CONV_NHWC) ||
+      g.pool_kernel != 0 || g.batch <= 0 || g.channels <= 0 || g.height <= 0 ||
+      g.width <= 0 || g.kernel_h <= 0 || g.kernel_w <= 0 || g.stride_h <= 0 ||
+      g.stride_w <= 0 || g.pad_h < 0 || g.pad_w < 0)
+    return false;
+  const int64_t pb = pad_bottom < 0 ? g.pad_h : pad_bottom;
+  const int64_t pr = pad_right < 0 ? g.pad_w : pad_right;
+  const int64_t span_h = g.height + g.pad_h + pb, span_w = g.width + g.pad_w + pr;
+  const int64_t image = static_cast<int64_t>(g.channels) * g.height * g.width;
+  const int64_t reach = (span_h + g.kernel_h) * g.width * g.channels +
+                        (span_w + g.kernel_w) * g.channels +
+                        static_cast<int64_t>(g.channels + 1) * g.height * g.width;
+  if (image >= (int64_t{1} << 30) || reach >= (int64_t{1} << 30) || span_h < g.kernel_h ||
+      span_w < g.kernel_w)
+    return false;
+  const int64_t oh = (span_h - g.kernel_h) / g.stride_h + 1;
+  const int64_t ow = (span_w - g.kernel_w) / g.stride_w + 1;
+  return oh == g.out_h && ow == g.out_w && static_cast<int64_t>(g.batch) * oh * ow == m &&
          static_cast<int64_t>(g.channels) * g.kernel_h * g.kernel_w == k;
 }
 
@@ -1685,39 +1776,66 @@ int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
                                           status, stream);
 }
 
-int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,
-                                  const int8_t *x, int64_t m, int32_t *y,
-                                  void *workspace, size_t workspace_bytes,
-                                  int32_t *status, void *stream) {
+int cim22_cuda_layer_forward_int8_ex(const cim22_cuda_layer *layer, const int8_t *x,
+                                     const cim22_gather *gather, int64_t m, int32_t pad_bottom,
+                                     int32_t pad_right, const int32_t *bias, int64_t out_pixels,
+                                     int32_t exact_unproven, int32_t *y, void *workspace,
+                                     size_t workspace_bytes, int32_t *status, void *stream) {
+  cim22_gather rows{};
+  rows.kind = CIM22_GATHER_ROWS;
+  const cim22_gather &g = gather ? *gather : rows;
   if (!layer || layer->bf16 || !x || !y || !status || m <= 0 || !workspace ||
-      workspace_bytes < cim22_cuda_layer_workspace_int8(layer, m)) {
+      workspace_bytes < cim22_cuda_layer_workspace_int8(layer, m) ||
+      !check_gather_int8(g, m, layer->k, pad_bottom, pad_right) || out_pixels < 0 ||
+      (out_pixels > 0 && (m % out_pixels || out_pixels >= (int64_t{1} << 31)))) {
     set_last_error("invalid arguments to cim22_cuda_layer_forward_int8");
     return CIM22_STATUS_BAD_ARGUMENT;
   }
   auto s = static_cast<cudaStream_t>(stream);
   const int64_t m_pad = round_up(m, kColumnPad);
-  if (layer->range_safe && tc::int8_available() && layer->k % 16 == 0 &&
+  // Proven layers cannot leave i21 on any tile, so whole-K accumulation is
+  // exact; unproven ones either run the checked per-tile kernel or, with
+  // exact_unproven, are computed as the Host computes them.
+  const bool exact = layer->range_safe || exact_unproven;
+  const bool conv = g.kind != CIM22_GATHER_ROWS;
+  if (!conv && exact && tc::int8_available() && layer->k % 16 == 0 &&
       tc::launch_int8(x, m, layer->k, layer->weights, layer->n_pad, layer->k_pad, m, layer->n,
-                      y, status, s))
+                      bias, out_pixels, y, status, s))
     return cuda_ok(cudaGetLastError(), "int8 launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
   int8_t *A = static_cast<int8_t *>(workspace);
-  const int64_t total = m_pad * layer->k_pad;
-  const unsigned blocks =
-      static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 32));
-  pad_int8_kernel<<<blocks, 256, 0, s>>>(x, m, layer->k, m_pad, layer->k_pad, A);
-  if (!cuda_ok(cudaGetLastError(), "pad launch"))
+  if (conv) {
+    const Gather32 dg = to_device_gather(g, m, layer->k, nullptr);
+    const int64_t total = m_pad * (layer->k_pad / 16);
+    const unsigned blocks =
+        static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+    im2col_int8_kernel<<<blocks, 256, 0, s>>>(x, dg, m_pad, layer->k_pad, A);
+  } else {
+    const int64_t total = m_pad * layer->k_pad;
+    const unsigned blocks =
+        static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 32));
+    pad_int8_kernel<<<blocks, 256, 0, s>>>(x, m, layer->k, m_pad, layer->k_pad, A);
+  }
+  if (!cuda_ok(cudaGetLastError(), "int8 gather launch"))
     return CIM22_STATUS_BAD_ARGUMENT;
   const int T = static_cast<int>(layer->tiles);
-  if (layer->range_safe && tc::int8_available() &&
+  if (exact && tc::int8_available() &&
       tc::launch_int8(A, m_pad, layer->k_pad, layer->weights, layer->n_pad, layer->k_pad, m,
-                      layer->n, y, status, s))
+                      layer->n, bias, out_pixels, y, status, s))
     return cuda_ok(cudaGetLastError(), "int8 launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
   const dim3 grid(static_cast<unsigned>(m_pad / 64),
                   static_cast<unsigned>((layer->n + 63) / 64));
-  int8_simt_kernel<<<grid, 256, 0, s>>>(A, layer->weights, layer->k_pad, T, m,
-                                        layer->n, layer->range_safe ? 0 : 1, y,
-                                        status);
+  const FastDiv div_pix = make_fastdiv(static_cast<uint32_t>(out_pixels > 0 ? out_pixels : 1));
+  int8_simt_kernel<<<grid, 256, 0, s>>>(A, layer->weights, layer->k_pad, T, m, layer->n,
+                                        exact ? 0 : 1, bias, out_pixels, div_pix, y, status);
   return cuda_ok(cudaGetLastError(), "int8 launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+}
+
+int cim22_cuda_layer_forward_int8(const cim22_cuda_layer *layer,
+                                  const int8_t *x, int64_t m, int32_t *y,
+                                  void *workspace, size_t workspace_bytes,
+                                  int32_t *status, void *stream) {
+  return cim22_cuda_layer_forward_int8_ex(layer, x, nullptr, m, -1, -1, nullptr, 0, 0, y,
+                                          workspace, workspace_bytes, status, stream);
 }
 
 } // extern "C"

@@ -311,6 +311,93 @@ def conv2d_bf16(x: np.ndarray, weight: np.ndarray, bias: np.ndarray | None, stri
     return y.reshape(n, oh, ow, f).transpose(0, 3, 1, 2).copy()
 
 
+# ---------------------------------------------------------------------------
+# INT8 Conv / MatMulInteger with bias, as the compiler lowers them.
+
+
+def prove_int8_ranges(w: np.ndarray, input_ranges) -> bool:
+    """proveMatMulIntegerRanges (Passes.cpp:593-627): every 64-wide K tile of
+    every output lane keeps its lowest and highest possible partial sum, given
+    per-K input ranges [lo, hi], inside signed i21."""
+    w = np.asarray(w, np.int64)
+    lo = np.array([r[0] for r in input_ranges], np.int64)
+    hi = np.array([r[1] for r in input_ranges], np.int64)
+    upper = np.where(w >= 0, w * hi, w * lo)
+    lower = np.where(w >= 0, w * lo, w * hi)
+    for t in range(0, w.shape[1], 64):
+        for part in (upper[:, t:t + 64].sum(1), lower[:, t:t + 64].sum(1)):
+            if np.any(part < -(1 << 20)) or np.any(part >= (1 << 20)):
+                return False
+    return True
+
+
+def wrap_i32(values: np.ndarray) -> np.ndarray:
+    """Two's-complement int32 of an int64 array."""
+    return ((np.asarray(values, np.int64) + (1 << 31)) % (1 << 32) - (1 << 31)).astype(np.int32)
+
+
+def im2col_int8(x: np.ndarray, kh: int, kw: int, strides=(1, 1),
+                pads=(0, 0, 0, 0)) -> tuple[np.ndarray, int, int]:
+    """Columns (n, oh, ow) x K (c, i, j) of an int8 NCHW batch with ONNX pads
+    (top, left, bottom, right); the im2col of normalizeCIMInt8Conv
+    (Passes.cpp:1511-1552) after the importer's zero padding."""
+    n, c, h, w = x.shape
+    top, left, bottom, right = pads
+    xp = np.pad(np.asarray(x, np.int8), ((0, 0), (0, 0), (top, bottom), (left, right)))
+    sh, sw = strides
+    oh = (h + top + bottom - kh) // sh + 1
+    ow = (w + left + right - kw) // sw + 1
+    cols = np.empty((n, oh, ow, c, kh, kw), np.int8)
+    for i in range(kh):
+        for j in range(kw):
+            patch = xp[:, :, i:i + sh * (oh - 1) + 1:sh, j:j + sw * (ow - 1) + 1:sw]
+            cols[:, :, :, :, i, j] = patch.transpose(0, 2, 3, 1)
+    return cols.reshape(n * oh * ow, c * kh * kw), oh, ow
+
+
+def linear_int8_bias(x: np.ndarray, w: np.ndarray, bias: np.ndarray | None = None, *,
+                     allow_extra_k_tile: bool = True) -> np.ndarray:
+    """An INT8 contraction plus optional int32 bias, as the compiler lowers it.
+
+    Weights that fail the range proof stay on the Host: exact wrapping int32
+    (Passes.cpp:1402-1450, 2075-2155). Otherwise the layer runs as CIM tiles
+    (linear_int8). A bias whose values all fit int8 is folded into the tiles
+    as one more K column (weight = bias, input = 1), inserted before the last
+    column when K is a multiple of 64, if the folded weights pass the proof
+    with that column's input range [1, 1] (FoldCIMInt8BiasPattern,
+    Passes.cpp:1863-2012); any other bias is a wrapping Host add."""
+    x = np.ascontiguousarray(x, np.int8)
+    w = np.ascontiguousarray(w, np.int8)
+    k = w.shape[1]
+    if not int8_range_safe(w):
+        y = wrap_i32(x.astype(np.int64) @ w.T.astype(np.int64))
+        return y if bias is None else wrap_i32(y.astype(np.int64) + np.asarray(bias, np.int64))
+    if bias is not None:
+        b = np.asarray(bias, np.int64)
+        exact_k = k % 64 == 0
+        if np.all((b >= -128) & (b <= 127)) and (not exact_k or allow_extra_k_tile):
+            lane = k - 1 if exact_k else k
+            wf = np.insert(w, lane, b.astype(np.int8), axis=1)
+            xf = np.insert(x, lane, np.int8(1), axis=1)
+            ranges = [(-128, 127)] * (k + 1)
+            ranges[lane] = (1, 1)
+            if prove_int8_ranges(wf, ranges):
+                return linear_int8(xf, wf)
+        return wrap_i32(linear_int8(x, w).astype(np.int64) + b)
+    return linear_int8(x, w)
+
+
+def conv2d_int8(x: np.ndarray, weight: np.ndarray, bias: np.ndarray | None = None,
+                strides=(1, 1), pads=(0, 0, 0, 0), **kw) -> np.ndarray:
+    """INT8 convolution (ConvInteger with zero zero-points, or a marked
+    linalg conv) of an int8 NCHW batch with int8 [F, C, KH, KW] weights,
+    returned as int32 NCHW."""
+    f, c, kh, kwid = weight.shape
+    cols, oh, ow = im2col_int8(x, kh, kwid, strides, pads)
+    y = linear_int8_bias(cols, np.asarray(weight, np.int8).reshape(f, -1), bias, **kw)
+    return y.reshape(x.shape[0], oh, ow, f).transpose(0, 3, 1, 2).copy()
+
+
 def cim_forward(model, x, *, branches: int = 4, threads: int = 1, via_runner: bool = False,
                 compensation: str = "sign-split"):
     """Run a torch model on CPU with every Linear/Conv2d computed by the oracle.

@@ -5,6 +5,8 @@ CPU only. Sources of the expectations:
     tests/golden/supplier_int8.json by tests/golden/make_golden.py);
   * the reference's compiled lib/Support/BF16Support.cpp
     (tests/golden/bf16_support_ref.npz);
+  * the reference's INT8 lowering helpers (test/python/ONNX/int8_lowering.py)
+    on its ConvInteger and integer-bias corpus (tests/golden/int8_conv_ref.npz);
   * known answers of test/Unit/Support/BF16SupportTest.cpp,
     test/Unit/Execution/CIMSoftwareRunnerTest.cpp (runner_scenarios.py),
     test/python/CIM22/bf16_reference_case.py and docs/BF16.md.
@@ -160,3 +162,52 @@ def test_int8_layer_exact_and_range_proof():
     assert not oracle.int8_range_safe(np.full((16, 64), -128, np.int8))
     with pytest.raises(oracle.OracleError, match="signed i21"):
         oracle.linear_int8(np.full((1, 64), -128, np.int8), np.full((16, 64), -128, np.int8))
+
+
+INT8_CONV_CASES = ("canonical", "odd", "pointwise", "rectangular", "conv_bias", "conv_bias_fold",
+                   "conv_bias_exact", "compile_tool0", "compile_tool1")
+
+
+@pytest.mark.parametrize("name", INT8_CONV_CASES)
+def test_int8_conv_golden(name):
+    """INT8 Conv (+ bias) against outputs of the reference's own lowering
+    helpers on its ConvInteger / integer-bias corpus and compile-tool case."""
+    g = np.load(GOLDEN / "int8_conv_ref.npz")
+    sh, sw, *pads = (int(v) for v in g[f"{name}.geom"])
+    bias = g[f"{name}.bias"] if f"{name}.bias" in g.files else None
+    y = oracle.conv2d_int8(g[f"{name}.x"], g[f"{name}.w"], bias, (sh, sw), tuple(pads))
+    np.testing.assert_array_equal(y, g[f"{name}.y"])
+    # The bias fold and the Host add agree (integer sums are exact).
+    if bias is not None:
+        y2 = oracle.conv2d_int8(g[f"{name}.x"], g[f"{name}.w"], bias, (sh, sw), tuple(pads),
+                                allow_extra_k_tile=False)
+        np.testing.assert_array_equal(y2, g[f"{name}.y"])
+
+
+@pytest.mark.parametrize("name", ("linear_bias", "linear_bias_fold", "linear_bias_exact"))
+def test_int8_linear_bias_golden(name):
+    """MatMulInteger + Add: int32 wraparound (bias near 2^31) and the folded
+    bias column, against the reference's lowering helpers."""
+    g = np.load(GOLDEN / "int8_conv_ref.npz")
+    y = oracle.linear_int8_bias(g[f"{name}.x"], g[f"{name}.w"].T, g[f"{name}.bias"])
+    np.testing.assert_array_equal(y, g[f"{name}.y"])
+
+
+def test_int8_conv_work_counts_and_proof():
+    """Work counts of the reference's corpus checks (verify_conv_integer.py:
+    canonical 256, odd 9, pointwise 12, rectangular 18) from the same
+    geometry, and the Host fallback for weights that fail the proof."""
+    g = np.load(GOLDEN / "int8_conv_ref.npz")
+    counts = {}
+    for name in ("canonical", "odd", "pointwise", "rectangular"):
+        x, w = g[f"{name}.x"], g[f"{name}.w"]
+        sh, sw, *pads = (int(v) for v in g[f"{name}.geom"])
+        cols, oh, ow = oracle.im2col_int8(x, w.shape[2], w.shape[3], (sh, sw), pads)
+        counts[name] = oh * ow * -(-w.shape[0] // 16) * -(-cols.shape[1] // 64)
+    assert counts == {"canonical": 256, "odd": 9, "pointwise": 12, "rectangular": 18}
+    w = np.full((16, 64), -128, np.int8)
+    x = np.full((2, 64), -128, np.int8)
+    assert not oracle.int8_range_safe(w)
+    np.testing.assert_array_equal(oracle.linear_int8_bias(x, w), np.full((2, 16), 1 << 20))
+    with pytest.raises(oracle.OracleError, match="signed i21"):
+        oracle.linear_int8(x, w)
