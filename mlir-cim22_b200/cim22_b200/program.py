@@ -42,6 +42,15 @@ from .cim_ops import CimLayer, StatusWord, Workspace
 IMAGE, MATRIX, TENSOR, CONST = "image", "matrix", "tensor", "const"
 
 
+# Operations evaluated at compile time when every tensor operand is frozen.
+_FOLD_METHODS = {"t", "transpose", "permute", "reshape", "view", "contiguous", "flatten",
+                 "squeeze", "unsqueeze", "to", "float", "int", "detach"}
+_FOLD_FUNCTIONS = {torch.t, torch.transpose, torch.permute, torch.reshape, torch.flatten,
+                   torch.squeeze, torch.unsqueeze, torch.ops.aten.t.default,
+                   torch.ops.aten.transpose.int, torch.ops.aten.permute.default,
+                   torch.ops.aten.view.default, torch.ops.aten.reshape.default}
+
+
 @dataclass
 class Val:
     kind: str
@@ -53,6 +62,7 @@ class Val:
     dtype: torch.dtype = torch.float32
     pool: tuple | None = None  # pending max pool (kernel, stride, source Val)
     flat_of: "Val | None" = None  # pending flatten of this image
+    int8_epilogue: dict | None = None  # INT8 layer output: its {"bias": tensor} slot
 
 
 @dataclass
@@ -151,6 +161,8 @@ class Program:
             elif node.op == "call_module":
                 self._lower(node, self._module_as_call(node, modules[str(node.target)]), env,
                             users)
+            elif self._fold_constant(node, env):
+                pass
             elif node.op == "call_method":
                 self._lower(node, self._method_as_call(node), env, users)
             elif node.op == "call_function":
@@ -162,6 +174,32 @@ class Program:
         self.output_tensors = [self._materialize(v) for v in self._outputs]
 
     # ------------------------------------------------------------------ lowering
+
+    def _fold_constant(self, node, env) -> bool:
+        """Layout and dtype operations on frozen weights (a transpose of an
+        _int_mm weight, a reshape) are evaluated once at compile time, as the
+        reference compiler evaluates dense constants (evaluateDenseTensor)."""
+        if node.op == "call_method":
+            if node.target not in _FOLD_METHODS:
+                return False
+        elif node.op != "call_function" or node.target not in _FOLD_FUNCTIONS:
+            return False
+        nodes = [a for a in (*node.args, *node.kwargs.values()) if isinstance(a, fx.Node)]
+        if not nodes or any(env[a].kind != CONST for a in nodes):
+            return False
+
+        def value(a):
+            return env[a].value if isinstance(a, fx.Node) else a
+
+        args = [value(a) for a in node.args]
+        kwargs = {k: value(v) for k, v in node.kwargs.items()}
+        with torch.no_grad():
+            if node.op == "call_method":
+                result = getattr(torch.as_tensor(args[0]), node.target)(*args[1:], **kwargs)
+            else:
+                result = node.target(*args, **kwargs)
+        env[node] = Val(CONST, tuple(getattr(result, "shape", ())), value=result)
+        return True
 
     def _module_as_call(self, node, module):
         x = node.args[0]
@@ -451,6 +489,10 @@ class Program:
         env[out_node] = Val(MATRIX, (m, n), out, nonneg=act == "relu")
 
     def _lower_int_mm(self, node, args, env) -> None:
+        """torch._int_mm as an INT8 CIM layer. Weights that fail the i21 range
+        proof are computed exactly, as the compiler keeps them on the Host
+        (Passes.cpp:592-627); a following int32 bias add folds into the
+        epilogue (_lower_add)."""
         x = env[args[0]]
         w = self._const(env, args[1])  # [K, N]
         if x.dtype != torch.int8 or len(x.shape) != 2:
@@ -461,20 +503,41 @@ class Program:
         self._keep.append(layer)
         out = self._new((m, wt.shape[0]), torch.int32)
         xt = self._tensor(x)
+        epilogue = {"bias": None}
 
         def run():
-            from .native import check, lib
-
-            ws = self.workspace.get(layer.workspace_bytes(m))
-            check(lib().cim22_cuda_layer_forward_int8(
-                layer._handle, cim_ops._ptr(xt), m, cim_ops._ptr(out), cim_ops._ptr(ws),
-                ws.numel(), cim_ops._ptr(self.status.tensor), cim_ops._stream(self.device)),
-                "forward_int8")
+            layer.forward_int8(xt, out, m, bias=epilogue["bias"], exact_unproven=True,
+                               workspace=self.workspace, status=self.status)
 
         name = f"int8_{len(self.layers)}"
         self.steps.append(Step(name, run, cim=True))
         self.layers.append(LayerInfo(name, "int8", m, k, wt.shape[0], 1, m * k * wt.shape[0]))
-        env[node] = Val(MATRIX, (m, wt.shape[0]), out, dtype=torch.int32)
+        env[node] = Val(MATRIX, (m, wt.shape[0]), out, dtype=torch.int32, int8_epilogue=epilogue)
+
+    def _lower_int_bias(self, node, args, env, users) -> None:
+        """INT8 layer output + int32 constant bias over the lanes: the exact
+        wrapping add of the compiler's Host (or of its folded bias column,
+        Passes.cpp:1863-2012), done in the layer's epilogue."""
+        a, b = args[0], args[1]
+        computed = [t for t in (a, b) if isinstance(t, fx.Node) and env[t].kind != CONST]
+        if len(computed) != 1:
+            raise NotImplementedError("integer add of two computed tensors")
+        v = computed[0]
+        other = b if v is a else a
+        val = env[v]
+        const = env[other].value if isinstance(other, fx.Node) else other
+        # A Python int keeps the tensor's int32 type, as in torch.
+        bias = torch.tensor(const, dtype=torch.int32) if isinstance(const, int) \
+            else torch.as_tensor(const)
+        n = val.shape[-1]
+        if val.int8_epilogue is None or val.int8_epilogue["bias"] is not None or \
+                users[v] != 1 or bias.dtype != torch.int32 or \
+                bias.numel() not in (1, n) or (bias.dim() > 0 and bias.shape[-1] != bias.numel()):
+            raise NotImplementedError("integer add other than an int32 bias on an INT8 layer")
+        bt = bias.reshape(-1).expand(n).contiguous().to(self.device)
+        self._keep.append(bt)
+        val.int8_epilogue["bias"] = bt
+        env[node] = Val(val.kind, val.shape, val.tensor, val.layout, dtype=torch.int32)
 
     def _lower_unary(self, node, x, op, env) -> None:
         if x.kind == CONST:
@@ -489,6 +552,9 @@ class Program:
         a, b = args[0], args[1]
         if kwargs.get("alpha", 1) != 1:
             raise NotImplementedError("add with alpha")
+        if any(isinstance(t, fx.Node) and env[t].dtype == torch.int32 for t in (a, b)):
+            self._lower_int_bias(node, args, env, users)
+            return
         va = env[a] if isinstance(a, fx.Node) else None
         vb = env[b] if isinstance(b, fx.Node) else None
         if va is None or vb is None or va.kind == CONST or vb.kind == CONST:

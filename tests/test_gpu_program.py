@@ -10,6 +10,8 @@
   for CPU inputs and raises the reference's error text for NaN inputs.
 """
 
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -152,32 +154,74 @@ def test_torch_compile_cuda_runtime():
     np.testing.assert_array_equal(bits(got2.cpu().numpy()), bits(expected))
 
 
-def test_torch_compile_int_mm():
+@pytest.mark.parametrize(("transpose_weight", "overflow", "wide_sum"),
+                         [(False, False, False), (True, False, False), (False, True, False),
+                          (False, False, True)])
+def test_torch_compile_int_mm(transpose_weight, overflow, wide_sum):
+    """python/tests/test_backend.py:225-330 of the reference: tiled INT8, or
+    range-unsafe weights (all -128) computed exactly as the Host does, and
+    sums beyond the i21 range of one tile."""
     from cim22_b200 import backend
 
     name = backend.register()
+    reduction, output = (64, 16) if overflow else (128, 17) if wide_sum else (65, 17)
 
     class Int8Matmul(torch.nn.Module):
-        def __init__(self, k, n, fill=None):
+        def __init__(self):
             super().__init__()
-            w = (torch.arange(k * n).reshape(k, n) % 15 - 7).to(torch.int8)
-            if fill is not None:
-                w.fill_(fill)
+            shape = (output, reduction) if transpose_weight else (reduction, output)
+            w = (torch.arange(reduction * output).reshape(shape) % 15 - 7).to(torch.int8)
+            if overflow:
+                w.fill_(-128)
+            elif wide_sum:
+                w.fill_(127)
             self.weight = torch.nn.Parameter(w, requires_grad=False)
 
         def forward(self, v):
-            return torch._int_mm(v, self.weight)
+            return torch._int_mm(v, self.weight.t() if transpose_weight else self.weight)
 
-    for k, n, fill, value in ((128, 32, None, -128), (128, 32, 127, -128), (256, 64, None, 5)):
-        model = Int8Matmul(k, n, fill).eval()
-        compiled = torch.compile(model, backend=name, fullgraph=True, dynamic=False,
-                                 options={"runtime": "cuda"})
-        v = torch.full((32, k), value, dtype=torch.int8)
-        v[1] = (torch.arange(k) % 256 - 128).to(torch.int8)
+    model = Int8Matmul().eval()
+    compiled = torch.compile(model, backend=name, fullgraph=True, dynamic=False,
+                             options={"runtime": "cuda"})
+    values = [torch.full((2, reduction), 127 if wide_sum else -128, dtype=torch.int8),
+              (torch.arange(2 * reduction).reshape(2, reduction) % 256 - 128).to(torch.int8)]
+    if wide_sum:
+        values[1].fill_(-128)
+    weight = model.weight.t() if transpose_weight else model.weight
+    for value in (*values, values[0]):
         with torch.inference_mode():
-            got = compiled(v)
-        exp = (v.to(torch.int64) @ model.weight.to(torch.int64)).to(torch.int32)
-        assert torch.equal(got, exp)
+            got = compiled(value)
+        assert got.dtype == torch.int32
+        exp = (value.to(torch.int64) @ weight.to(torch.int64)).to(torch.int32)
+        assert torch.equal(got.cpu(), exp)
+        if wide_sum:
+            assert torch.all(exp.abs() > 2**20)
+
+
+def test_torch_compile_int_mm_bias():
+    """MatMulInteger + Add (generate_integer_bias_onnx.py): the int32 bias,
+    including one that wraps past 2^31, folds into the INT8 epilogue."""
+    from cim22_b200 import backend
+
+    name = backend.register()
+    g = np.load(Path(__file__).resolve().parent / "golden" / "int8_conv_ref.npz")
+    for case in ("linear_bias", "linear_bias_fold", "linear_bias_exact"):
+        w, b, x = g[f"{case}.w"], g[f"{case}.bias"], g[f"{case}.x"]
+
+        class Biased(torch.nn.Module):
+            def __init__(self):
+                super().__init__()
+                self.weight = torch.nn.Parameter(torch.from_numpy(w), requires_grad=False)
+                self.register_buffer("bias", torch.from_numpy(b))
+
+            def forward(self, v):
+                return torch._int_mm(v, self.weight) + self.bias
+
+        compiled = torch.compile(Biased().eval(), backend=name, fullgraph=True, dynamic=False,
+                                 options={"runtime": "cuda"})
+        with torch.inference_mode():
+            got = compiled(torch.from_numpy(x))
+        np.testing.assert_array_equal(got.cpu().numpy(), g[f"{case}.y"])
 
 
 @pytest.mark.parametrize("mode", ["legacy", "none"])
