@@ -578,6 +578,37 @@ int cim22_cuda_nhwc_to_nchw(const float *x, float *y, int32_t n, int32_t h,
 /* NCHW -> NHWC. */
 int cim22_cuda_nchw_to_nhwc(const float *x, float *y, int32_t n, int32_t c,
                             int32_t h, int32_t w, void *stream);
+/* Elementwise f32 glue (Host arithmetic around the layers, e.g. the LIF
+ * membrane updates of spiking models, python/tests/test_backend.py:502-545):
+ * y[i] = a[i] op b[i], where a NULL a or b stands for the scalar a_scalar /
+ * b_scalar. One IEEE round-to-nearest operation per element, as PyTorch's
+ * CPU kernels compute it; comparisons give 1.0f or 0.0f (0 for NaN); max/min
+ * propagate NaN like torch.maximum/minimum. y may alias a or b. */
+#define CIM22_BINARY_ADD 0
+#define CIM22_BINARY_SUB 1
+#define CIM22_BINARY_MUL 2
+#define CIM22_BINARY_DIV 3
+#define CIM22_BINARY_GE 4
+#define CIM22_BINARY_GT 5
+#define CIM22_BINARY_LE 6
+#define CIM22_BINARY_LT 7
+#define CIM22_BINARY_EQ 8
+#define CIM22_BINARY_NE 9
+#define CIM22_BINARY_MAX 10
+#define CIM22_BINARY_MIN 11
+int cim22_cuda_binary(const float *a, const float *b, float *y, int64_t count, int32_t op,
+                      float a_scalar, float b_scalar, void *stream);
+/* y[i] = value. */
+int cim22_cuda_fill(float *y, int64_t count, float value, void *stream);
+/* Copies `words` 32-bit words (slice writes and state updates). */
+int cim22_cuda_copy(const void *src, void *dst, int64_t words, void *stream);
+/* Copies `blocks` runs of `inner` 32-bit words; run b is read at
+ * src + b * src_stride and written at dst + b * dst_stride (words). Selecting
+ * index i of axis d of a contiguous tensor is blocks = prod(shape[:d]),
+ * inner = prod(shape[d+1:]), src offset i * inner, src_stride =
+ * shape[d] * inner; select_scatter writes the same runs the other way. */
+int cim22_cuda_slice_copy(const void *src, void *dst, int64_t blocks, int64_t inner,
+                          int64_t src_stride, int64_t dst_stride, void *stream);
 /* No counterpart in the reference (it runs on one host): reassembles a
  * layer whose output lanes are split over `ranks` devices. src is what an
  * all-gather of the per-rank [rows][cols] outputs stacks, [ranks][rows][cols];

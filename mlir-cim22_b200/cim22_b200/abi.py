@@ -179,6 +179,10 @@ class Gather(ctypes.Structure):
 
 
 GATHER_ROWS = 0
+
+# cim22_cuda_binary operations (include/cim22_cuda.h).
+(BINARY_ADD, BINARY_SUB, BINARY_MUL, BINARY_DIV, BINARY_GE, BINARY_GT, BINARY_LE, BINARY_LT,
+ BINARY_EQ, BINARY_NE, BINARY_MAX, BINARY_MIN) = range(12)
 GATHER_CONV_NCHW = 1
 GATHER_CONV_NHWC = 2
 

@@ -61,6 +61,19 @@ def _is_module_input(node: torch.fx.Node) -> bool:
     return "_modules_" in text or "_parameters_" in text or "_buffers_" in text
 
 
+def _is_mutated(node: torch.fx.Node) -> bool:
+    import operator
+
+    from .program import MUTATING_METHODS
+
+    for user in node.users:
+        if user.args and user.args[0] is node and (
+                (user.op == "call_method" and user.target in MUTATING_METHODS) or
+                (user.op == "call_function" and user.target is operator.setitem)):
+            return True
+    return False
+
+
 def backend(gm: torch.fx.GraphModule, example_inputs: Sequence[torch.Tensor], *,
             options: BackendOptions | None = None) -> Callable:
     """Compile a static inference graph for torch.compile."""
@@ -74,8 +87,14 @@ def backend(gm: torch.fx.GraphModule, example_inputs: Sequence[torch.Tensor], *,
             raise ValueError("CIM22 reference requires CPU tensors")
         return gm.forward
     placeholders = list(gm.graph.find_nodes(op="placeholder"))
+    # Module state the forward writes (a LIF membrane buffer updated with
+    # copy_ or slice writes) stays a runtime input and is written back after
+    # each call, as the reference keeps mutated inputs out of its frozen set
+    # (python/cim22/backend.py:171-185).
+    mutated = {i for i, node in enumerate(placeholders) if _is_mutated(node)}
     frozen = {i for i, node in enumerate(placeholders)
-              if isinstance(example_inputs[i], torch.Tensor) and _is_module_input(node)}
+              if isinstance(example_inputs[i], torch.Tensor) and _is_module_input(node)
+              and i not in mutated}
     # Frozen values cannot serve another module's parameters or buffers: guard
     # on their identity so Dynamo recompiles for a different module
     # (python/cim22/backend.py:207-210 of the reference does the same).

@@ -94,6 +94,10 @@ _SIGNATURES = {
     "cim22_cuda_nhwc_to_nchw": (c.c_int, [P, P, I32, I32, I32, I32, P]),
     "cim22_cuda_nchw_to_nhwc": (c.c_int, [P, P, I32, I32, I32, I32, P]),
     "cim22_cuda_unshard_columns": (c.c_int, [P, P, I32, I64, I64, I64, P]),
+    "cim22_cuda_binary": (c.c_int, [P, P, P, I64, I32, c.c_float, c.c_float, P]),
+    "cim22_cuda_fill": (c.c_int, [P, I64, c.c_float, P]),
+    "cim22_cuda_copy": (c.c_int, [P, P, I64, P]),
+    "cim22_cuda_slice_copy": (c.c_int, [P, P, I64, I64, I64, I64, P]),
     "cim22_cuda_maxpool2d_nchw": (c.c_int, [P, P, I32, I32, I32, I32, I32, I32, I32, P]),
     "cim22_cuda_avgpool2d_nchw": (c.c_int, [P, P, I32, I32, I32, I32, I32, I32, P]),
     "cim22_cuda_global_avgpool_nchw": (c.c_int, [P, P, I32, I32, I32, I32, P]),

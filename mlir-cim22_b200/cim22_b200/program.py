@@ -97,6 +97,25 @@ _ADAPTIVE = {F.adaptive_avg_pool2d, torch._C._nn.adaptive_avg_pool2d}
 _BN = {F.batch_norm}
 _SOFTMAX = {F.softmax, torch.softmax}
 _INT_MM = {torch._int_mm}
+_BINARY = {
+    operator.sub: abi.BINARY_SUB, torch.sub: abi.BINARY_SUB, operator.isub: abi.BINARY_SUB,
+    operator.mul: abi.BINARY_MUL, torch.mul: abi.BINARY_MUL, operator.imul: abi.BINARY_MUL,
+    operator.truediv: abi.BINARY_DIV, torch.div: abi.BINARY_DIV,
+    torch.true_divide: abi.BINARY_DIV, operator.itruediv: abi.BINARY_DIV,
+    operator.ge: abi.BINARY_GE, torch.ge: abi.BINARY_GE, operator.gt: abi.BINARY_GT,
+    torch.gt: abi.BINARY_GT, operator.le: abi.BINARY_LE, torch.le: abi.BINARY_LE,
+    operator.lt: abi.BINARY_LT, torch.lt: abi.BINARY_LT, operator.eq: abi.BINARY_EQ,
+    torch.eq: abi.BINARY_EQ, operator.ne: abi.BINARY_NE, torch.ne: abi.BINARY_NE,
+    torch.maximum: abi.BINARY_MAX, torch.minimum: abi.BINARY_MIN,
+}
+_COMPARISONS = {abi.BINARY_GE, abi.BINARY_GT, abi.BINARY_LE, abi.BINARY_LT, abi.BINARY_EQ,
+                abi.BINARY_NE}
+_FILL_LIKE = {torch.zeros_like: 0.0, torch.ones_like: 1.0}
+# Value-preserving calls on inference tensors (Tensor.data, detach).
+_IDENTITY = {getattr(torch._C._autograd, "_get_data_attr", None), torch.detach}
+_IDENTITY.discard(None)
+# In-place methods whose first operand is written (state updates).
+MUTATING_METHODS = {"copy_", "add_", "sub_", "mul_", "div_", "fill_", "zero_"}
 
 
 def _pair(v):
@@ -130,6 +149,7 @@ class Program:
         self.graph = None
         self._host = None  # pinned output staging for CPU callers
         self._host_status = None
+        self.mutated_inputs: set[int] = set()  # inputs the graph writes (state)
         frozen = frozen or set()
         env: dict[fx.Node, Val] = {}
         users = {node: len(node.users) for node in gm.graph.nodes}
@@ -239,8 +259,18 @@ class Program:
             return ("reshape", node.args, {})
         if name in ("add",):
             return (operator.add, node.args, {})
-        if name in ("contiguous",):
+        if name in ("contiguous", "detach"):
             return ("identity", node.args[:1], {})
+        if name in ("to", "float", "type"):
+            args = node.args if name != "float" else (node.args[0], torch.float32)
+            return ("to_dtype", args, dict(node.kwargs))
+        if name == "copy_":
+            return ("copy_", node.args, {})
+        methods = {"sub": torch.sub, "mul": torch.mul, "div": torch.div, "ge": torch.ge,
+                   "gt": torch.gt, "le": torch.le, "lt": torch.lt, "eq": torch.eq,
+                   "ne": torch.ne}
+        if name in methods:
+            return (methods[name], node.args, dict(node.kwargs))
         raise NotImplementedError(f"CIM CUDA runtime does not lower Tensor.{name}")
 
     def _const(self, env, a):
@@ -275,8 +305,38 @@ class Program:
             if kwargs.get("approximate", "none") != "none":
                 raise NotImplementedError("only erf GELU is lowered")
             self._lower_unary(node, env[args[0]], "gelu", env)
+        elif target in _ADD and self._has_scalar(args, env):
+            self._lower_binary(node, abi.BINARY_ADD, args[0], args[1], env)
         elif target in _ADD:
             self._lower_add(node, args, kwargs, env, users)
+        elif target in _BINARY:
+            if kwargs.get("rounding_mode") is not None or kwargs.get("alpha", 1) != 1:
+                raise NotImplementedError(f"{target} with {kwargs}")
+            self._lower_binary(node, _BINARY[target], args[0], args[1], env)
+        elif target in _FILL_LIKE or target is torch.full_like:
+            value = _FILL_LIKE.get(target, args[1] if len(args) > 1 else kwargs.get("fill_value"))
+            self._lower_fill(node, env[args[0]], value, kwargs, env)
+        elif target == "to_dtype":
+            self._lower_to(node, env[args[0]], args[1:], kwargs, env)
+        elif target == "copy_":
+            self._lower_copy(node, args[0], args[1], env)
+        elif target is operator.setitem:
+            self._lower_setitem(args[0], args[1], args[2], env)
+        elif target is torch.select:
+            x = env[args[0]]
+            base_shape = tuple(self._tensor(x).shape)
+            dim = args[1] % len(base_shape)
+            index = args[2]
+            if not -base_shape[dim] <= index < base_shape[dim]:
+                raise IndexError(f"index {index} out of range")
+            self._lower_select(node, x, None, env, axis_index=(dim, index % base_shape[dim]))
+        elif target is torch.select_scatter:
+            dim = args[2] if len(args) > 2 else kwargs["dim"]
+            index = args[3] if len(args) > 3 else kwargs["index"]
+            self._lower_select_scatter(node, env[args[0]], env[args[1]], dim, index, env)
+        elif target is torch.stack:
+            self._lower_stack(node, args[0], args[1] if len(args) > 1 else kwargs.get("dim", 0),
+                              env)
         elif target in _MAXPOOL:
             self._lower_pool(node, args, kwargs, env, "max")
         elif target in _AVGPOOL:
@@ -301,8 +361,10 @@ class Program:
             self._lower_bn(node, args, kwargs, env, users)
         elif target in _SOFTMAX:
             self._lower_softmax(node, args, kwargs, env)
-        elif target == "identity":
+        elif target == "identity" or target in _IDENTITY:
             env[node] = env[args[0]]
+        elif target is operator.getitem and env[args[0]].kind != CONST:
+            self._lower_select(node, env[args[0]], args[1], env)
         elif target is operator.getitem:
             env[node] = env[args[0]].value[args[1]]
         else:
@@ -442,9 +504,12 @@ class Program:
         x = env[args[0]]
         w = self._const(env, args[1])
         b = self._const(env, args[2]) if len(args) > 2 else None
-        if x.kind not in (MATRIX, TENSOR) or len(x.shape) != 2:
-            raise NotImplementedError("linear lowers 2-D inputs")
-        m, k = x.shape
+        lead = tuple(x.shape[:-1])
+        if len(x.shape) < 2 or x.kind == CONST or \
+                (len(x.shape) != 2 and (x.layout != "nchw" or x.flat_of is not None)):
+            raise NotImplementedError("linear lowers inputs of rank 2 or more")
+        k = x.shape[-1]
+        m = int(np.prod(lead))
         n = w.shape[0]
         layer = CimLayer(torch.as_tensor(w).detach().float(), device=self.device,
                          compensation=self.compensation)
@@ -461,7 +526,9 @@ class Program:
             img = x.flat_of
             g, xt = self._image_gather(img, img.shape[2], img.shape[3], 1, 0)
         else:
-            xt = self._tensor(x)
+            # Leading dimensions are columns, as torch.nn.functional.linear
+            # treats them.
+            xt = self._tensor(x).reshape(m, k)
 
         def prepare():
             layer.prepare_bf16(xt, m, gather=g, branches=branches, workspace=self.workspace,
@@ -486,7 +553,12 @@ class Program:
             branches=branches)))
         self.layers.append(LayerInfo(name, "linear", m, k, n, branches, branches * m * k * n,
                                      xt.numel() * xt.element_size()))
-        env[out_node] = Val(MATRIX, (m, n), out, nonneg=act == "relu")
+        if len(lead) == 1:
+            env[out_node] = Val(MATRIX, (m, n), out, nonneg=act == "relu")
+        else:
+            shape = (*lead, n)
+            kind = IMAGE if len(shape) == 4 else TENSOR
+            env[out_node] = Val(kind, shape, out.view(shape), nonneg=act == "relu")
 
     def _lower_int_mm(self, node, args, env) -> None:
         """torch._int_mm as an INT8 CIM layer. Weights that fail the i21 range
@@ -538,6 +610,247 @@ class Program:
         self._keep.append(bt)
         val.int8_epilogue["bias"] = bt
         env[node] = Val(val.kind, val.shape, val.tensor, val.layout, dtype=torch.int32)
+
+    # Elementwise state glue (LIF membrane updates, python/tests/test_backend.py:
+    # 502-545 of the reference): f32 tensors, Python scalars, comparisons held
+    # as float 0/1 with a bool dtype, slices along the leading axis.
+
+    @staticmethod
+    def _has_scalar(args, env) -> bool:
+        return any(isinstance(a, (int, float)) and not isinstance(a, bool) for a in args[:2])
+
+    def _lower_binary(self, node, op, a, b, env) -> None:
+        def operand(x):
+            if isinstance(x, fx.Node):
+                v = env[x]
+                if v.kind == CONST:
+                    value = v.value
+                    if isinstance(value, torch.Tensor) and value.numel() == 1:
+                        return None, float(value.item()), v
+                    raise NotImplementedError("elementwise op on a non-scalar constant")
+                return v, None, v
+            if isinstance(x, (int, float)) and not isinstance(x, bool):
+                return None, float(x), None
+            raise NotImplementedError(f"elementwise operand {x!r}")
+
+        va, sa, _ = operand(a)
+        vb, sb, _ = operand(b)
+        tensors = [v for v in (va, vb) if v is not None]
+        if not tensors:
+            raise NotImplementedError("elementwise op of two scalars")
+        # f32 results need an f32 tensor operand (a bool one is 0/1 under f32
+        # promotion); comparisons compare f32 tensors and scalars.
+        dtypes = [v.dtype for v in tensors]
+        if any(d not in (torch.float32, torch.bool) for d in dtypes) or \
+                torch.float32 not in dtypes or \
+                (op in _COMPARISONS and torch.bool in dtypes):
+            raise NotImplementedError("elementwise glue computes on f32 tensors")
+        if len(tensors) == 2 and (va.shape != vb.shape or va.layout != vb.layout):
+            raise NotImplementedError("elementwise op of tensors of different shapes")
+        ref = tensors[0]
+        at = None if va is None else self._tensor(va)
+        bt = None if vb is None else self._tensor(vb)
+        out = self._new(tuple((at if at is not None else bt).shape))
+        a_s = 0.0 if sa is None else sa
+        b_s = 0.0 if sb is None else sb
+
+        def run():
+            from .native import check, lib
+
+            check(lib().cim22_cuda_binary(cim_ops._ptr(at), cim_ops._ptr(bt), cim_ops._ptr(out),
+                                          out.numel(), op, a_s, b_s, cim_ops._stream(out.device)),
+                  "binary")
+
+        self.steps.append(Step("binary", run))
+        env[node] = Val(ref.kind, ref.shape, out, ref.layout,
+                        dtype=torch.bool if op in _COMPARISONS else torch.float32)
+
+    def _lower_fill(self, node, x: Val, value, kwargs, env) -> None:
+        dtype = kwargs.get("dtype") or x.dtype
+        if dtype != torch.float32 or not isinstance(value, (int, float)):
+            raise NotImplementedError("fill of f32 tensors with a scalar")
+        out = self._new(tuple(self._tensor(x).shape))
+        fill = float(value)
+
+        def run():
+            from .native import check, lib
+
+            check(lib().cim22_cuda_fill(cim_ops._ptr(out), out.numel(), fill,
+                                        cim_ops._stream(out.device)), "fill")
+
+        self.steps.append(Step("fill", run))
+        env[node] = Val(x.kind, x.shape, out, x.layout)
+
+    def _lower_to(self, node, x: Val, args, kwargs, env) -> None:
+        dtype = kwargs.get("dtype", args[0] if args else None)
+        if isinstance(dtype, torch.Tensor):
+            dtype = dtype.dtype
+        if dtype not in (torch.float32, x.dtype) or x.dtype not in (torch.float32, torch.bool):
+            raise NotImplementedError(f"conversion {x.dtype} -> {dtype}")
+        # Comparisons are already stored as 0.0 / 1.0.
+        env[node] = Val(x.kind, x.shape, self._tensor(x), x.layout, nonneg=x.nonneg,
+                        dtype=dtype)
+
+    @staticmethod
+    def _axis_index(shape, index):
+        """(axis, i) of x[index] for an int, or a tuple of full slices and one
+        int; None for other indexing."""
+        if isinstance(index, int):
+            items = (index,)
+        elif isinstance(index, tuple):
+            items = index
+        else:
+            return None
+        ints = [d for d, it in enumerate(items) if isinstance(it, int)]
+        full = all(isinstance(it, int) or (isinstance(it, slice) and it == slice(None))
+                   for it in items)
+        if len(ints) != 1 or not full or len(items) > len(shape):
+            return None
+        axis = ints[0]
+        i = items[axis]
+        if not -shape[axis] <= i < shape[axis]:
+            raise IndexError(f"index {i} out of range for axis {axis} of {shape}")
+        return axis, i % shape[axis]
+
+    def _select_runs(self, t: torch.Tensor, axis: int):
+        shape = tuple(t.shape)
+        outer = int(np.prod(shape[:axis]))
+        inner = int(np.prod(shape[axis + 1:]))
+        return outer, inner, shape[axis] * inner
+
+    def _lower_select(self, node, x: Val, index, env, axis_index=None) -> None:
+        """x[i] (or torch.select): along the leading axis a view, no launch;
+        along an inner axis one strided copy."""
+        if x.kind == IMAGE and x.layout != "nchw":
+            raise NotImplementedError("indexing an NHWC image")
+        base = self._tensor(x)
+        ai = axis_index or self._axis_index(tuple(base.shape), index)
+        if ai is None:
+            raise NotImplementedError(f"indexing with {index!r}")
+        axis, i = ai
+        if axis == 0:
+            t = base[i]
+        else:
+            outer, inner, stride = self._select_runs(base, axis)
+            t = self._new(tuple(base.shape[:axis]) + tuple(base.shape[axis + 1:]), base.dtype)
+            src = base.view(-1)[i * inner:]
+            out = t
+
+            def run():
+                from .native import check, lib
+
+                check(lib().cim22_cuda_slice_copy(cim_ops._ptr(src), cim_ops._ptr(out), outer,
+                                                  inner, stride, inner,
+                                                  cim_ops._stream(out.device)), "select")
+
+            self.steps.append(Step("select", run))
+        kind = IMAGE if t.dim() == 4 else MATRIX if t.dim() == 2 else TENSOR
+        env[node] = Val(kind, tuple(t.shape), t, "nchw", nonneg=x.nonneg, dtype=x.dtype)
+
+    def _lower_select_scatter(self, node, x: Val, src: Val, dim: int, index: int, env) -> None:
+        """torch.select_scatter: a copy of x with src written at index of dim,
+        the single-slice insert the reference decomposes it to
+        (python/cim22/backend.py:58-99)."""
+        if x.kind == CONST or src.kind == CONST or x.dtype != src.dtype or \
+                x.kind == IMAGE and x.layout != "nchw" or src.kind == IMAGE and src.layout != "nchw":
+            raise NotImplementedError("select_scatter of computed tensors of one dtype")
+        base = self._tensor(x)
+        st = self._tensor(src)
+        nd = base.dim()
+        if not -nd <= dim < nd:
+            raise IndexError(f"dim {dim} out of range")
+        axis = dim % nd
+        if tuple(st.shape) != tuple(base.shape[:axis]) + tuple(base.shape[axis + 1:]) or \
+                not -base.shape[axis] <= index < base.shape[axis]:
+            raise NotImplementedError("select_scatter source shape or index")
+        i = index % base.shape[axis]
+        out = self._new(tuple(base.shape), base.dtype)
+        self._copy_step(base, out)
+        outer, inner, stride = self._select_runs(out, axis)
+        dst = out.view(-1)[i * inner:]
+
+        def run():
+            from .native import check, lib
+
+            check(lib().cim22_cuda_slice_copy(cim_ops._ptr(st), cim_ops._ptr(dst), outer, inner,
+                                              inner, stride, cim_ops._stream(out.device)),
+                  "select_scatter")
+
+        self.steps.append(Step("select_scatter", run))
+        kind = IMAGE if out.dim() == 4 else MATRIX if out.dim() == 2 else TENSOR
+        env[node] = Val(kind, tuple(out.shape), out, dtype=x.dtype)
+
+    def _copy_step(self, src: torch.Tensor, dst: torch.Tensor) -> None:
+        def run():
+            from .native import check, lib
+
+            check(lib().cim22_cuda_copy(cim_ops._ptr(src), cim_ops._ptr(dst), dst.numel(),
+                                        cim_ops._stream(dst.device)), "copy")
+
+        self.steps.append(Step("copy", run))
+
+    def _note_mutation(self, v: Val) -> None:
+        for i, slot in enumerate(self.inputs):
+            if slot.tensor is not None and v.tensor is not None and \
+                    slot.tensor.data_ptr() <= v.tensor.data_ptr() < \
+                    slot.tensor.data_ptr() + slot.tensor.numel() * slot.tensor.element_size():
+                self.mutated_inputs.add(i)
+
+    def _lower_setitem(self, target, index, value, env) -> None:
+        """target[i] = value on the leading axis (a select_scatter written in
+        place, as the reference lowers it to one slice insert)."""
+        tv = env[target]
+        if tv.kind == CONST or not isinstance(index, int):
+            raise NotImplementedError("slice write into a constant or with a non-integer index")
+        if tv.kind == IMAGE and tv.layout != "nchw":
+            raise NotImplementedError("slice write into an NHWC image")
+        dst = self._tensor(tv)[index]
+        if isinstance(value, fx.Node):
+            sv = env[value]
+            src = self._tensor(sv)
+            same = sv.dtype == tv.dtype or (tv.dtype == torch.float32 and sv.dtype == torch.bool)
+            if tuple(src.shape) != tuple(dst.shape) or src.dtype != dst.dtype or not same:
+                raise NotImplementedError("slice write of a different shape or type")
+            self._copy_step(src, dst)
+        elif isinstance(value, (int, float)) and tv.dtype == torch.float32:
+            fill = float(value)
+
+            def run():
+                from .native import check, lib
+
+                check(lib().cim22_cuda_fill(cim_ops._ptr(dst), dst.numel(), fill,
+                                            cim_ops._stream(dst.device)), "fill")
+
+            self.steps.append(Step("fill", run))
+        else:
+            raise NotImplementedError(f"slice write of {value!r}")
+        tv.nonneg = False
+        self._note_mutation(tv)
+
+    def _lower_copy(self, node, target, source, env) -> None:
+        """State write-back: dst.copy_(src) on a graph input (a module buffer
+        the forward updates); the input is copied back after each call."""
+        tv, sv = env[target], env[source]
+        if tv.kind == CONST:
+            raise NotImplementedError("copy_ into a frozen constant")
+        dst, src = self._tensor(tv), self._tensor(sv)
+        if tuple(dst.shape) != tuple(src.shape) or dst.dtype != src.dtype:
+            raise NotImplementedError("copy_ between different shapes or types")
+        self._copy_step(src, dst)
+        self._note_mutation(tv)
+        env[node] = tv
+
+    def _lower_stack(self, node, items, dim, env) -> None:
+        vals = [env[i] for i in items]
+        if dim != 0 or not vals or any(v.kind == CONST for v in vals) or \
+                any(v.shape != vals[0].shape or v.dtype != vals[0].dtype for v in vals):
+            raise NotImplementedError("stack of equal computed tensors on axis 0")
+        srcs = [self._tensor(v) for v in vals]
+        out = self._new((len(vals), *srcs[0].shape))
+        for i, src in enumerate(srcs):
+            self._copy_step(src, out[i])
+        kind = IMAGE if out.dim() == 4 else MATRIX if out.dim() == 2 else TENSOR
+        env[node] = Val(kind, tuple(out.shape), out, dtype=vals[0].dtype)
 
     def _lower_unary(self, node, x, op, env) -> None:
         if x.kind == CONST:
@@ -775,6 +1088,9 @@ class Program:
                 raise ValueError(f"input must be {dtype} {shape}")
             slot.tensor.copy_(v, non_blocking=True)
         self.replay()
+        for i in sorted(self.mutated_inputs):
+            # Write the updated state back into the caller's tensor.
+            values[i].copy_(self.inputs[i].tensor)
         if on_cpu:
             # Outputs and the status word come back in one pinned staging
             # area with a single synchronization.

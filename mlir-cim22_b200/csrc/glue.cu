@@ -60,6 +60,74 @@ __global__ void add_kernel(const float *__restrict__ a, const float *__restrict_
     y[i] = act_fn(__fadd_rn(a[i], b[i]), act);
 }
 
+// Elementwise arithmetic and comparisons of the Host glue (stateful LIF
+// updates and other f32 elementwise code the compiler leaves on the Host).
+// Each operation rounds once, as PyTorch's CPU kernels do; comparisons give
+// 1.0f / 0.0f (false for NaN operands, as in IEEE). Operands may alias y.
+__device__ __forceinline__ float binary_op(float x, float z, int op) {
+  switch (op) {
+  case CIM22_BINARY_ADD: return __fadd_rn(x, z);
+  case CIM22_BINARY_SUB: return __fsub_rn(x, z);
+  case CIM22_BINARY_MUL: return __fmul_rn(x, z);
+  case CIM22_BINARY_DIV: return __fdiv_rn(x, z);
+  case CIM22_BINARY_GE: return x >= z ? 1.0f : 0.0f;
+  case CIM22_BINARY_GT: return x > z ? 1.0f : 0.0f;
+  case CIM22_BINARY_LE: return x <= z ? 1.0f : 0.0f;
+  case CIM22_BINARY_LT: return x < z ? 1.0f : 0.0f;
+  case CIM22_BINARY_EQ: return x == z ? 1.0f : 0.0f;
+  case CIM22_BINARY_NE: return x != z ? 1.0f : 0.0f;
+  case CIM22_BINARY_MAX: return (x != x || z != z) ? __int_as_float(0x7fc00000) : fmaxf(x, z);
+  default: return (x != x || z != z) ? __int_as_float(0x7fc00000) : fminf(x, z);
+  }
+}
+
+__global__ void binary_kernel(const float *a, const float *b, float *y, int64_t count, int op,
+                              float a_scalar, float b_scalar) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += stride)
+    y[i] = binary_op(a ? a[i] : a_scalar, b ? b[i] : b_scalar, op);
+}
+
+__global__ void fill_kernel(float *__restrict__ y, int64_t count, float value) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += stride)
+    y[i] = value;
+}
+
+// 32-bit word copy (f32, int32, or float-coded bool data).
+__global__ void copy_kernel(const uint32_t *__restrict__ src, uint32_t *__restrict__ dst,
+                            int64_t count) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += stride)
+    dst[i] = src[i];
+}
+
+// Strided block copy: `blocks` runs of `inner` 32-bit words, run b read at
+// src + b * src_stride and written at dst + b * dst_stride (a select along an
+// inner axis, or the slice insert of select_scatter).
+__global__ void slice_copy_kernel(const uint32_t *__restrict__ src, uint32_t *__restrict__ dst,
+                                  int64_t blocks, int64_t inner, int64_t src_stride,
+                                  int64_t dst_stride) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t count = blocks * inner;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += stride) {
+    const int64_t b = i / inner, j = i - b * inner;
+    dst[b * dst_stride + j] = src[b * src_stride + j];
+  }
+}
+
 __global__ void maxpool_kernel(const float *__restrict__ x, float *__restrict__ y,
                                int n, int h, int w, int c, int k, int s, int pad,
                                int oh, int ow) {
@@ -397,6 +465,49 @@ int cim22_cuda_add(const float *a, const float *b, float *y, int64_t count,
     return 0;
   launch_pdl(add_kernel, grid_for(count), 256, 0, static_cast<cudaStream_t>(stream), a, b, y, count, activation);
   return launched("add");
+}
+
+int cim22_cuda_binary(const float *a, const float *b, float *y, int64_t count, int32_t op,
+                      float a_scalar, float b_scalar, void *stream) {
+  if (!y || count < 0 || op < CIM22_BINARY_ADD || op > CIM22_BINARY_MIN)
+    return bad("cim22_cuda_binary");
+  if (count == 0)
+    return 0;
+  launch_pdl(binary_kernel, grid_for(count), 256, 0, static_cast<cudaStream_t>(stream), a, b, y,
+             count, static_cast<int>(op), a_scalar, b_scalar);
+  return launched("binary");
+}
+
+int cim22_cuda_fill(float *y, int64_t count, float value, void *stream) {
+  if (!y || count < 0)
+    return bad("cim22_cuda_fill");
+  if (count == 0)
+    return 0;
+  launch_pdl(fill_kernel, grid_for(count), 256, 0, static_cast<cudaStream_t>(stream), y, count,
+             value);
+  return launched("fill");
+}
+
+int cim22_cuda_copy(const void *src, void *dst, int64_t words, void *stream) {
+  if (!src || !dst || words < 0)
+    return bad("cim22_cuda_copy");
+  if (words == 0 || src == dst)
+    return 0;
+  launch_pdl(copy_kernel, grid_for(words), 256, 0, static_cast<cudaStream_t>(stream),
+             static_cast<const uint32_t *>(src), static_cast<uint32_t *>(dst), words);
+  return launched("copy");
+}
+
+int cim22_cuda_slice_copy(const void *src, void *dst, int64_t blocks, int64_t inner,
+                          int64_t src_stride, int64_t dst_stride, void *stream) {
+  if (!src || !dst || blocks < 0 || inner < 0 || src_stride < 0 || dst_stride < 0)
+    return bad("cim22_cuda_slice_copy");
+  if (blocks == 0 || inner == 0)
+    return 0;
+  launch_pdl(slice_copy_kernel, grid_for(blocks * inner), 256, 0,
+             static_cast<cudaStream_t>(stream), static_cast<const uint32_t *>(src),
+             static_cast<uint32_t *>(dst), blocks, inner, src_stride, dst_stride);
+  return launched("slice_copy");
 }
 
 int cim22_cuda_maxpool2d_nhwc(const float *x, float *y, int32_t n, int32_t h,
