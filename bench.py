@@ -476,7 +476,29 @@ def main() -> None:
     step = prog.steps[names.index(dominant)]
     info = next((l for l in prog.layers if dominant.startswith(l.name)), None)
     dur_s = avg[dominant] / 1000
-    if step.cim and info is not None:
+    if step.cim and step.meta and step.meta.get("kind") == "chain":
+        # The whole network in one kernel: the MMA-equivalent work of every
+        # layer on the int8 tensor peak (the chain computes it with dp4a on
+        # CUDA cores), and on HBM the input images, the logits and each
+        # layer's int8 weights of both signs.
+        ops = 2 * prog.macs
+        achieved = ops / dur_s / 1e12
+        int8_peak = 2 * bf16_peak
+        chain_bytes = (4 * step.meta["x"].numel() + 4 * step.meta["out"].numel()
+                       + sum(2 * l.n * l.k for l in prog.layers))
+        gbs = chain_bytes / dur_s / 1e9
+        tensor = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
+                  "frac": achieved / int8_peak, "ops_per_launch": ops,
+                  "peak_note": f"int8 dense = 2 x {peak_kind} bf16 cuBLAS ({bf16_peak} TF/s); "
+                               "ops = 2 x branches x M x K x N of every layer (unpadded)"}
+        hbm = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+               "frac": gbs / hbm_peak, "bytes_per_launch": chain_bytes,
+               "peak_note": f"{peak_kind} HBM copy bandwidth"}
+        first, other = (tensor, hbm) if tensor["frac"] >= hbm["frac"] else (hbm, tensor)
+        roof = dict(first, traffic=None, kernel=dominant, launch_ms=avg[dominant],
+                    other_roof={k: other[k] for k in ("bound", "achieved", "peak", "unit",
+                                                       "frac")})
+    elif step.cim and info is not None:
         # Both roofs of a CIM layer step: the MMA work on the int8 tensor
         # peak, and the bytes it must move (its source read once, int8
         # weights of both signs, the f32 output) on HBM; the binding one is
@@ -561,6 +583,8 @@ def main() -> None:
                        "global_batch": batch * world, "parallelism": f"batch-sharded x{world}",
                        "l2": "flushed between steps (256 MiB write, outside the timed span)",
                        "graph": "CUDA graph replay", "cim_macs_per_batch": prog.macs,
+                       "lowering": "fused layer chain (one persistent kernel)" if prog.chained
+                                   else "per-layer kernels",
                        "arithmetic": "BF16 sign-split: int8 mantissa crossbar dots, BF16 "
                                      "tiles, f32 K sums"},
             "gpu_launches": len(prog.steps) * args.steps,

@@ -544,6 +544,33 @@ int cim22_cuda_layer_forward_int8_ex(const cim22_cuda_layer *layer, const int8_t
                                      int32_t exact_unproven, int32_t *y, void *workspace,
                                      size_t workspace_bytes, int32_t *status, void *stream);
 
+/* A chain of small BF16 sign-split layers in one persistent kernel (no
+ * counterpart in the reference's interface; the numerics are those of
+ * cim22_cuda_layer_forward_bf16 layer by layer). Each CTA carries whole
+ * images through every layer with the activations in shared memory: per
+ * layer the im2col gather, split, prealign, crossbar dots, restore, tile
+ * sums, merge, bias and activation, then an optional 2x2 stride-2 max pool.
+ * Meant for networks whose per-image activations fit in shared memory
+ * (LeNet-5, the MNIST MLP), where per-layer launches are latency-bound. */
+#define CIM22_CHAIN_LINEAR 0
+#define CIM22_CHAIN_CONV 1
+typedef struct cim22_chain_layer {
+  int32_t kind;                     /* CIM22_CHAIN_CONV or CIM22_CHAIN_LINEAR */
+  const cim22_cuda_layer *layer;    /* sign-split weights [n][c * kh * kw] */
+  const float *bias;                /* device [n] or NULL */
+  /* First layer only: the input image [channels][height][width] (a vector
+   * input is [k][1][1]); later layers take the previous output. A Linear
+   * layer flattens its input in NCHW order. */
+  int32_t channels, height, width;
+  int32_t kernel_h, kernel_w, stride, pad; /* conv only */
+  int32_t branches;                 /* 4, or 2 when the input is nonnegative */
+  int32_t activation;               /* CIM22_ACT_* */
+  int32_t pool;                     /* 0, or 2: 2x2 stride-2 max pool after it */
+} cim22_chain_layer;
+/* x: f32 [batch][input image]; y: f32 [batch][last output, NCHW order]. */
+int cim22_cuda_chain_forward(const cim22_chain_layer *layers, int32_t n_layers, const float *x,
+                             int64_t batch, float *y, int32_t *status, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Host glue the compiler emits around CIM layers (upstream Linalg lowering,
  * lib/Compiler/Pipelines.cpp:61-72). All f32, device memory; image layout

@@ -179,12 +179,36 @@ class Gather(ctypes.Structure):
 
 
 GATHER_ROWS = 0
+GATHER_CONV_NCHW = 1
+GATHER_CONV_NHWC = 2
 
 # cim22_cuda_binary operations (include/cim22_cuda.h).
 (BINARY_ADD, BINARY_SUB, BINARY_MUL, BINARY_DIV, BINARY_GE, BINARY_GT, BINARY_LE, BINARY_LT,
  BINARY_EQ, BINARY_NE, BINARY_MAX, BINARY_MIN) = range(12)
-GATHER_CONV_NCHW = 1
-GATHER_CONV_NHWC = 2
+
+
+class ChainLayer(ctypes.Structure):
+    """cim22_chain_layer: one layer of cim22_cuda_chain_forward."""
+
+    _fields_ = [
+        ("kind", ctypes.c_int32),
+        ("layer", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("channels", ctypes.c_int32),
+        ("height", ctypes.c_int32),
+        ("width", ctypes.c_int32),
+        ("kernel_h", ctypes.c_int32),
+        ("kernel_w", ctypes.c_int32),
+        ("stride", ctypes.c_int32),
+        ("pad", ctypes.c_int32),
+        ("branches", ctypes.c_int32),
+        ("activation", ctypes.c_int32),
+        ("pool", ctypes.c_int32),
+    ]
+
+
+CHAIN_LINEAR = 0
+CHAIN_CONV = 1
 
 ABI_STRUCTS = (
     FramePacket,
@@ -197,6 +221,7 @@ ABI_STRUCTS = (
     TraceEvent,
     Memref2D,
     Gather,
+    ChainLayer,
 )
 
 

@@ -98,6 +98,7 @@ _SIGNATURES = {
     "cim22_cuda_fill": (c.c_int, [P, I64, c.c_float, P]),
     "cim22_cuda_copy": (c.c_int, [P, P, I64, P]),
     "cim22_cuda_slice_copy": (c.c_int, [P, P, I64, I64, I64, I64, P]),
+    "cim22_cuda_chain_forward": (c.c_int, [P, I32, P, I64, P, P, P]),
     "cim22_cuda_maxpool2d_nchw": (c.c_int, [P, P, I32, I32, I32, I32, I32, I32, I32, P]),
     "cim22_cuda_avgpool2d_nchw": (c.c_int, [P, P, I32, I32, I32, I32, I32, I32, P]),
     "cim22_cuda_global_avgpool_nchw": (c.c_int, [P, P, I32, I32, I32, I32, P]),

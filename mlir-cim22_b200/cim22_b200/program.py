@@ -128,7 +128,7 @@ class Program:
     def __init__(self, gm: fx.GraphModule, example_inputs, *, frozen: set[int] | None = None,
                  device: int | torch.device = 0, name: str = "cim_program",
                  fuse: bool = True, layout: str = "nchw",
-                 bf16_compensation: str = "sign-split") -> None:
+                 bf16_compensation: str = "sign-split", chain: bool | str = "auto") -> None:
         if layout not in ("nchw", "nhwc"):
             raise ValueError(f"unknown image layout {layout!r}")
         if bf16_compensation not in abi.COMPENSATION:
@@ -151,6 +151,22 @@ class Program:
         self._host_status = None
         self.mutated_inputs: set[int] = set()  # inputs the graph writes (state)
         frozen = frozen or set()
+        self.chained = False
+        if chain and fuse and layout == "nchw" and bf16_compensation == "sign-split":
+            plan = self._match_chain(gm, example_inputs, frozen)
+            if plan is not None and self._build_chain(plan, example_inputs, frozen):
+                if chain != "auto":
+                    return
+                # Both lowerings give the same bits: keep the faster one.
+                alt = Program(gm, example_inputs, frozen=frozen, device=self.device, name=name,
+                              fuse=fuse, layout=layout, bf16_compensation=bf16_compensation,
+                              chain=False)
+                example = example_inputs[plan["source"]]
+                for prog in (self, alt):
+                    prog.inputs[0].tensor.copy_(example)
+                if alt.time_launch() < self.time_launch():
+                    self.__dict__.update(alt.__dict__)
+                return
         env: dict[fx.Node, Val] = {}
         users = {node: len(node.users) for node in gm.graph.nodes}
         self._fused: set[fx.Node] = set()
@@ -192,6 +208,199 @@ class Program:
                 self._outputs = [env[o] for o in (outs if isinstance(outs, (tuple, list)) else (outs,))]
                 self._output_is_tuple = isinstance(outs, (tuple, list))
         self.output_tensors = [self._materialize(v) for v in self._outputs]
+
+    # ------------------------------------------------------- fused layer chain
+
+    def _match_chain(self, gm, example_inputs, frozen):
+        """The layers of a graph that is one chain of Conv2d / Linear layers,
+        each optionally followed by ReLU or GELU and a 2x2 stride-2 max pool,
+        with flattens between them; None for any other graph. Such a network
+        runs as one persistent kernel (cim22_cuda_chain_forward)."""
+        modules = dict(gm.named_modules())
+        self._modules = modules
+        consts: dict[fx.Node, Any] = {}
+        plan: list[dict] = []
+        cur = None
+        source = None
+        index = 0
+        out = None
+        for node in gm.graph.nodes:
+            if node.op == "placeholder":
+                example = example_inputs[index]
+                if index in frozen:
+                    consts[node] = example
+                elif source is None and isinstance(example, torch.Tensor) and \
+                        example.dtype == torch.float32 and example.dim() in (2, 4):
+                    source, cur = (node, index), node
+                else:
+                    return None
+                index += 1
+                continue
+            if node.op == "get_attr":
+                value = gm
+                for part in str(node.target).split("."):
+                    value = getattr(value, part)
+                consts[node] = value
+                continue
+            if node.op == "output":
+                outs = node.args[0]
+                if isinstance(outs, (tuple, list)):
+                    if len(outs) != 1:
+                        return None
+                    outs = outs[0]
+                out = outs
+                continue
+            try:
+                if node.op == "call_module":
+                    target, args, kwargs = self._module_as_call(node, modules[str(node.target)])
+                elif node.op == "call_method":
+                    target, args, kwargs = self._method_as_call(node)
+                else:
+                    target, args, kwargs = node.target, node.args, dict(node.kwargs)
+            except NotImplementedError:
+                return None
+            if not args or args[0] is not cur or len(cur.users) != 1:
+                return None
+
+            def const(a):
+                return consts.get(a) if isinstance(a, fx.Node) else a
+
+            if target in _CONV:
+                w, b = const(args[1]), const(args[2]) if len(args) > 2 else None
+                stride = _pair(args[3] if len(args) > 3 else kwargs.get("stride", 1))
+                pad = _pair(args[4] if len(args) > 4 else kwargs.get("padding", 0))
+                dil = _pair(args[5] if len(args) > 5 else kwargs.get("dilation", 1))
+                groups = args[6] if len(args) > 6 else kwargs.get("groups", 1)
+                if not isinstance(w, torch.Tensor) or w.dim() != 4 or \
+                        (args[2] if len(args) > 2 else None) is not None and b is None or \
+                        stride[0] != stride[1] or pad[0] != pad[1] or dil != (1, 1) or \
+                        groups != 1 or isinstance(pad[0], str):
+                    return None
+                plan.append(dict(kind=abi.CHAIN_CONV, weight=w, bias=b, stride=stride[0],
+                                 pad=pad[0], act=None, pool=0))
+            elif target in _LINEAR:
+                w, b = const(args[1]), const(args[2]) if len(args) > 2 else None
+                if not isinstance(w, torch.Tensor) or w.dim() != 2 or \
+                        (args[2] if len(args) > 2 else None) is not None and b is None:
+                    return None
+                plan.append(dict(kind=abi.CHAIN_LINEAR, weight=w, bias=b, act=None, pool=0))
+            elif target in _RELU or target in _GELU:
+                if not plan or plan[-1]["act"] is not None or plan[-1]["pool"] or \
+                        target in _GELU and kwargs.get("approximate", "none") != "none":
+                    return None
+                plan[-1]["act"] = "relu" if target in _RELU else "gelu"
+            elif target in _MAXPOOL:
+                k = _pair(args[1] if len(args) > 1 else kwargs.get("kernel_size"))
+                st = args[2] if len(args) > 2 else kwargs.get("stride")
+                st = k if st is None or st == [] or st == () else _pair(st)
+                pd = _pair(args[3] if len(args) > 3 else kwargs.get("padding", 0))
+                dl = _pair(args[4] if len(args) > 4 else kwargs.get("dilation", 1))
+                ceil = args[5] if len(args) > 5 else kwargs.get("ceil_mode", False)
+                idx = args[6] if len(args) > 6 else kwargs.get("return_indices", False)
+                if not plan or plan[-1]["kind"] != abi.CHAIN_CONV or plan[-1]["pool"] or \
+                        k != (2, 2) or st != (2, 2) or pd != (0, 0) or dl != (1, 1) or ceil or idx:
+                    return None
+                plan[-1]["pool"] = 2
+            elif target in _FLATTEN:
+                start = args[1] if len(args) > 1 else kwargs.get("start_dim", 0)
+                end = args[2] if len(args) > 2 else kwargs.get("end_dim", -1)
+                if start != 1 or end != -1:
+                    return None
+            elif target == "reshape":
+                shape = args[1:] if not isinstance(args[1], (tuple, list)) else tuple(args[1])
+                if len(shape) != 2 or shape[1] != -1:
+                    return None
+            elif target != "identity":
+                return None
+            cur = node
+        if source is None or not plan or out is not cur:
+            return None
+        return dict(plan=plan, source=source[1], output_tuple=isinstance(
+            list(gm.graph.find_nodes(op="output"))[0].args[0], (tuple, list)))
+
+    def _build_chain(self, match, example_inputs, frozen) -> bool:
+        """One chain step for a matched network, if its layers fit the
+        kernel (shared memory, geometry); False leaves the normal lowering."""
+        from .native import lib
+
+        plan = match["plan"]
+        x = example_inputs[match["source"]]
+        batch = x.shape[0]
+        shape = tuple(x.shape[1:]) if x.dim() == 4 else (x.shape[1], 1, 1)
+        specs = (abi.ChainLayer * len(plan))()
+        layers, infos, keep = [], [], []
+        c, h, w = shape
+        nonneg = False
+        for i, ly in enumerate(plan):
+            weight = torch.as_tensor(ly["weight"]).detach().float()
+            n = weight.shape[0]
+            layer = CimLayer(weight.reshape(n, -1), device=self.device)
+            layers.append(layer)
+            bias = None
+            if ly["bias"] is not None:
+                bias = torch.as_tensor(ly["bias"]).detach().float().contiguous().to(self.device)
+                keep.append(bias)
+            sp = specs[i]
+            sp.kind = ly["kind"]
+            sp.layer = layer._handle
+            sp.bias = None if bias is None else bias.data_ptr()
+            sp.channels, sp.height, sp.width = c, h, w
+            branches = 2 if nonneg else 4
+            sp.branches = branches
+            sp.activation = cim_ops.ACT[ly["act"]]
+            sp.pool = ly["pool"]
+            if ly["kind"] == abi.CHAIN_CONV:
+                kh, kw = weight.shape[2], weight.shape[3]
+                sp.kernel_h, sp.kernel_w, sp.stride, sp.pad = kh, kw, ly["stride"], ly["pad"]
+                if weight.shape[1] != c:
+                    return False
+                oh = (h + 2 * ly["pad"] - kh) // ly["stride"] + 1
+                ow = (w + 2 * ly["pad"] - kw) // ly["stride"] + 1
+                k = c * kh * kw
+            else:
+                k = c * h * w
+                oh = ow = 1
+                if weight.shape[1] != k:
+                    return False
+            m = batch * oh * ow
+            infos.append(LayerInfo(f"chain.{'conv' if ly['kind'] else 'linear'}{i}",
+                                   "conv" if ly["kind"] else "linear", m, k, n, branches,
+                                   branches * m * k * n, 4 * batch * c * h * w))
+            c = n
+            h, w = (oh // 2, ow // 2) if ly["pool"] else (oh, ow)
+            nonneg = ly["act"] == "relu"
+        out_shape = (batch, c, h, w) if plan[-1]["kind"] == abi.CHAIN_CONV or h * w > 1 \
+            else (batch, c)
+        slot = torch.empty(tuple(x.shape), dtype=torch.float32, device=self.device)
+        out = torch.empty(out_shape, dtype=torch.float32, device=self.device)
+        status = self.status
+
+        def run():
+            from .native import check
+
+            check(lib().cim22_cuda_chain_forward(specs, len(plan), slot.data_ptr(), batch,
+                                                 out.data_ptr(), status.tensor.data_ptr(),
+                                                 cim_ops._stream(out.device)),
+                  "cim22_cuda_chain_forward")
+
+        try:
+            run()
+            torch.cuda.synchronize(self.device)
+        except RuntimeError:
+            return False  # does not fit the kernel: lower layer by layer
+        self.status.reset()
+        self._keep += layers + keep + [specs]
+        self.steps = [Step("chain", run, cim=True, meta=dict(kind="chain", x=slot, out=out))]
+        self.layers = infos
+        v = Val(IMAGE if x.dim() == 4 else MATRIX, tuple(x.shape), slot, dtype=torch.float32)
+        self.inputs = [v]
+        self.input_shapes = [tuple(x.shape)]
+        self.input_dtypes = [torch.float32]
+        self._outputs = [Val(IMAGE if len(out_shape) == 4 else MATRIX, out_shape, out)]
+        self._output_is_tuple = match["output_tuple"]
+        self.output_tensors = [out]
+        self.chained = True
+        return True
 
     # ------------------------------------------------------------------ lowering
 
@@ -1056,6 +1265,24 @@ class Program:
         for step in self.steps:
             step.fn()
 
+    def time_launch(self, iters: int = 10) -> float:
+        """Median device time (ms) of one eager launch of every step, on the
+        inputs currently in the input slots."""
+        torch.cuda.synchronize(self.device)
+        for _ in range(3):
+            self.launch()
+        times = []
+        for _ in range(iters):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            self.launch()
+            b.record()
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        self.status.reset()
+        return sorted(times)[len(times) // 2]
+
     def capture(self) -> None:
         """Record the program into a CUDA graph for replay."""
         torch.cuda.synchronize(self.device)
@@ -1116,8 +1343,12 @@ class Program:
 
 def from_module(model: torch.nn.Module, example: torch.Tensor, device: int = 0,
                 name: str = "cim_program", fuse: bool = True,
-                layout: str = "nchw", bf16_compensation: str = "sign-split") -> Program:
-    """Lower an eval-mode module by symbolic tracing, freezing its parameters."""
+                layout: str = "nchw", bf16_compensation: str = "sign-split",
+                chain: bool | str = "auto") -> Program:
+    """Lower an eval-mode module by symbolic tracing, freezing its parameters.
+    chain: "auto" times the fused layer chain against the per-layer kernels
+    for a network the chain can run and keeps the faster (the outputs are the
+    same bits); True forces the chain, False the per-layer kernels."""
     gm = fx.symbolic_trace(model)
     return Program(gm, [example], frozen=set(), device=device, name=name, fuse=fuse,
-                   layout=layout, bf16_compensation=bf16_compensation)
+                   layout=layout, bf16_compensation=bf16_compensation, chain=chain)

@@ -20,6 +20,7 @@
 
 #include <cuda_bf16.h>
 #include "gemm_tc.h"
+#include "signsplit_prep.cuh"
 
 #include <algorithm>
 #include <climits>
@@ -31,7 +32,6 @@
 namespace cim {
 namespace {
 
-constexpr unsigned kFull = 0xffffffffu;
 
 // ---------------------------------------------------------------------------
 // Gather of the K x columns operand (linear rows or conv im2col), with 32-bit
@@ -83,18 +83,6 @@ __device__ __forceinline__ float window_load(const float *__restrict__ img, cons
   return m;
 }
 
-// Exact path for groups whose maximum is tiny (exponent < 8): RNE scaling of
-// the element, then ExpPrealign at exponent 127. Out of line so the fast path
-// is not predicated through it.
-__device__ __noinline__ uint32_t slow_align(uint32_t p, int shift) {
-  return static_cast<uint8_t>(prealign_element(bf16_scalbn(static_cast<uint16_t>(p), shift), 127));
-}
-
-// Low bytes of four words, in order, as one word.
-__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c,
-                                                   uint32_t d) {
-  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
-}
 
 // Sign-split preparation of 64-element groups (prepareBF16Input,
 // BF16Compensation.cpp:92-118, on the gathered operand of the reference's
@@ -115,7 +103,6 @@ __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint3
 // that floor in its low mantissa bits. Other groups take the exact RNE
 // scaling of bf16_scalbn. The scaled maximum lies in [1, 2), so the prealign
 // exponent is always 127.
-constexpr int kGroupThreads = 8;
 
 // The eight K indices kbeg .. kbeg+7 of one thread: image offsets (channel,
 // kernel row, kernel column) relative to a window origin, and which are < K.
@@ -199,101 +186,6 @@ __device__ __forceinline__ void gather8(const float *__restrict__ x, const Gathe
   }
 }
 
-// Split, round and prealign the thread's eight values of a group shared by
-// the eight lanes of `mask` (sub = lane within them): out[a] holds the eight
-// aligned bytes of activation branch a, emax[a] the group exponent
-// (kZeroGroup for an all-zero group).
-//
-// Split and round: xp = max(x, 0), xn = max(-x, 0) equal the reference's
-// selects for every non-NaN x up to the sign of zero, which the preparation
-// clears anyway (BF16Compensation.cpp:97). cvt.rn.bf16x2.f32 rounds to
-// nearest even, as arith.truncf does. NaN, infinity and finite values that
-// round to BF16 infinity (|x| >= 0x1.fep127) mark the group non-finite:
-// through the BF16 exponent 0xff of the maximum for a 2-branch layer, through
-// |x| of the raw inputs otherwise (the max with 0 drops NaN).
-template <int kActBranches>
-__device__ __forceinline__ void convert8(const float (&v)[8], unsigned mask, int sub,
-                                         int32_t *status, uint2 (&out)[2], int (&emax)[2]) {
-  uint32_t packed[2][4];
-  uint32_t mx[2] = {0, 0};
-  bool negative = false;
-  if (kActBranches == 2) {
-    uint32_t amax = 0;
-#pragma unroll
-    for (int e = 0; e < 8; ++e)
-      amax = max(amax, __float_as_uint(v[e]) & 0x7fffffffu);
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const __nv_bfloat162 hp = __floats2bfloat162_rn(fmaxf(v[e], 0.0f), fmaxf(v[e + 1], 0.0f));
-      const __nv_bfloat162 hn =
-          __floats2bfloat162_rn(fmaxf(-v[e], 0.0f), fmaxf(-v[e + 1], 0.0f));
-      packed[0][e / 2] = *reinterpret_cast<const uint32_t *>(&hp) & 0x7fff7fffu;
-      packed[kActBranches - 1][e / 2] = *reinterpret_cast<const uint32_t *>(&hn) & 0x7fff7fffu;
-    }
-#pragma unroll
-    for (int a = 0; a < kActBranches; ++a) {
-      const uint32_t m2 = __vmaxu2(__vmaxu2(packed[a][0], packed[a][1]),
-                                   __vmaxu2(packed[a][2], packed[a][3]));
-      mx[a] = max(m2 & 0xffffu, m2 >> 16);
-    }
-    if (amax >= 0x7f7f8000u)
-      mx[0] = 0xffffu;
-  } else {
-    uint32_t umax = 0;
-#pragma unroll
-    for (int e = 0; e < 8; ++e)
-      umax = max(umax, __float_as_uint(v[e]));
-    negative = umax > 0x80000000u;
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const __nv_bfloat162 hp = __floats2bfloat162_rn(v[e], v[e + 1]);
-      packed[0][e / 2] = *reinterpret_cast<const uint32_t *>(&hp) & 0x7fff7fffu;
-    }
-    const uint32_t m2 = __vmaxu2(__vmaxu2(packed[0][0], packed[0][1]),
-                                 __vmaxu2(packed[0][2], packed[0][3]));
-    mx[0] = max(m2 & 0xffffu, m2 >> 16);
-  }
-#pragma unroll
-  for (int a = 0; a < kActBranches; ++a)
-#pragma unroll
-    for (int o = 4; o; o >>= 1)
-      mx[a] = max(mx[a], __shfl_xor_sync(mask, mx[a], o, kGroupThreads));
-  const bool nonfinite = mx[0] >= 0x7f80u;
-  if (sub == 0 && nonfinite)
-    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-  if (negative && !nonfinite)
-    atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
-#pragma unroll
-  for (int a = 0; a < kActBranches; ++a) {
-    const bool zero = mx[a] == 0 || nonfinite;
-    emax[a] = zero ? kZeroGroup : effective_exponent(static_cast<uint16_t>(mx[a]));
-    uint32_t lo = 0, hi = 0;
-    if (!zero) {
-      if ((mx[a] >> 7) >= 8) {
-        const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax[a]) << 23);
-        uint32_t q[8];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          q[2 * e] = __float_as_uint(
-              __fmaf_rz(__uint_as_float(packed[a][e] << 16), scale, 8388608.0f));
-          q[2 * e + 1] = __float_as_uint(
-              __fmaf_rz(__uint_as_float(packed[a][e] & 0xffff0000u), scale, 8388608.0f));
-        }
-        lo = pack_low_bytes(q[0], q[1], q[2], q[3]);
-        hi = pack_low_bytes(q[4], q[5], q[6], q[7]);
-      } else {
-        const int shift = 127 - emax[a];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          lo |= slow_align((packed[a][e / 2] >> (16 * (e & 1))) & 0xffffu, shift) << (8 * e);
-          hi |= slow_align((packed[a][2 + e / 2] >> (16 * (e & 1))) & 0xffffu, shift)
-                << (8 * e);
-        }
-      }
-    }
-    out[a] = make_uint2(lo, hi);
-  }
-}
 
 template <int kActBranches, int kMode>
 __global__ void __launch_bounds__(256)
@@ -496,13 +388,6 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 3 : 1)
 }
 
 
-__device__ __forceinline__ float apply_act(float v, int act) {
-  if (act == CIM22_ACT_RELU)
-    return (v > 0.0f || v != v) ? v : 0.0f; // NaN propagates, as torch.relu
-  if (act == CIM22_ACT_GELU)
-    return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
-  return v;
-}
 
 // ---------------------------------------------------------------------------
 // Sign-split contraction on CUDA cores (dp4a). CTA tile kBM columns x kBN
@@ -510,17 +395,6 @@ __device__ __forceinline__ float apply_act(float v, int act) {
 // and lanes 4tc .. 4tc + 3.
 constexpr int kRowStride = 80;
 
-// Exact restore of one tile value outside the fast exponent window (subnormal
-// or overflowing results), out of line so the fast path is not predicated
-// through it. Returns the updated f32 branch sum.
-__device__ __noinline__ float slow_tile_add(float acc, int p, int ew, int ex, int32_t *status) {
-  if (ex == kZeroGroup)
-    return acc;
-  const uint16_t tile = signsplit_tile(static_cast<uint32_t>(p), ew, ex);
-  if (tile == kBF16Inf)
-    atomicOr(status, CIM22_STATUS_TILE_OVERFLOW);
-  return __fadd_rn(acc, bf16_to_f32(tile));
-}
 
 // kFuse < 0: A and Ex come from the prepare kernel's workspace. kFuse =
 // kPrepRows / kPrepConv / kPrepConvPool: the CTA gathers and prealigns its own
