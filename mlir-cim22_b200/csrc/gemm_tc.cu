@@ -777,6 +777,203 @@ __global__ void __launch_bounds__(kSThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// INT8 contraction, persistent: 128 x 256 output tiles (one tcgen05.mma
+// kind::i8 of M=128, N=256, K=32 per 32 bytes of K), a 4-stage TMA ring of
+// 128-byte K blocks (16 KB of A and 32 KB of B per stage), and two 256-column
+// TMEM accumulators so the epilogue of one tile overlaps the MMAs of the next.
+//
+//   warp 0 (one thread)  TMA producer over every tile of the CTA
+//   warp 1 (one thread)  MMA issuer; commits each stage back to the producer
+//                        and each finished accumulator to the epilogue
+//   warps 2-9            epilogue: warp w reads TMEM lanes 32 * (w % 4) (tile
+//                        rows) and one 128-column half of the accumulator,
+//                        adds the bias and stores rows or NCHW planes
+//
+// Tiles are walked column-major (consecutive CTAs take consecutive row
+// blocks of the same weight block), so a weight block is read from HBM once
+// per wave and the activations stay in L2. Every wait is bounded; a wait
+// that runs out stops the CTA, which waits (bounded) for its copies in flight
+// and frees its TMEM.
+constexpr int kIBM = 128, kIBN = 256, kIBK = 128, kIStages = 4;
+constexpr int kIEpiWarps = 8;
+constexpr int kIThreads = 64 + 32 * kIEpiWarps;
+constexpr uint32_t kIBufCols = kIBN;
+constexpr uint32_t kIStageBytes = (kIBM + kIBN) * kIBK;
+
+struct alignas(1024) SmemI8P {
+  int8_t a[kIStages][kIBM * kIBK];
+  int8_t b[kIStages][kIBN * kIBK];
+  uint64_t full[kIStages];
+  uint64_t empty[kIStages];
+  uint64_t dfull[2];
+  uint64_t dempty[2];
+  uint32_t tmem;
+  int failed;
+};
+
+__global__ void __launch_bounds__(kIThreads, 1)
+    int8_persistent_kernel(const __grid_constant__ CUtensorMap tmA,
+                           const __grid_constant__ CUtensorMap tmB, int num_kb, int M, int N,
+                           int num_mb, FastDiv div_mb, const int32_t *__restrict__ bias,
+                           int out_pixels, FastDiv div_pix, int vec, int32_t *__restrict__ y,
+                           int32_t *status) {
+  extern __shared__ uint8_t smem_raw[];
+  SmemI8P &s = *reinterpret_cast<SmemI8P *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                            ~uintptr_t{1023});
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int num_tiles = num_mb * ((N + kIBN - 1) / kIBN);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kIStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.dfull[i], 1);
+      mbar_init(&s.dempty[i], kIEpiWarps);
+    }
+    s.failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s.tmem)),
+                 "r"(2 * kIBufCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = s.tmem;
+  volatile int *failed = &s.failed;
+  pdl_launch_dependents();
+  pdl_wait();
+
+  if (warp == 0 && lane == 0) {
+    uint32_t kbi = 0;
+    bool ok = true;
+    for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
+      const int nb = fdiv(ot, div_mb);
+      const int m0 = (ot - nb * num_mb) * kIBM, n0 = nb * kIBN;
+      for (int kb = 0; kb < num_kb; ++kb, ++kbi) {
+        const int stage = kbi % kIStages;
+        if (!mbar_wait(&s.empty[stage], ((kbi / kIStages) & 1) ^ 1) || *failed) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&s.full[stage], kIStageBytes);
+        tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * kIBK, m0);
+        tma_load_2d(s.b[stage], &tmB, &s.full[stage], kb * kIBK, n0);
+      }
+    }
+    if (!ok)
+      *failed = 1;
+    // Never leave with copies in flight.
+    for (uint32_t i = kbi > kIStages ? kbi - kIStages : 0; i < kbi; ++i)
+      mbar_wait(&s.full[i % kIStages], (i / kIStages) & 1);
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = idesc_i8(kIBM, kIBN);
+    uint32_t kbi = 0, ti = 0;
+    bool ok = true;
+    for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
+      const int buf = ti & 1;
+      if (!mbar_wait(&s.dempty[buf], ((ti >> 1) & 1) ^ 1) || *failed) {
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t d = tmem + buf * kIBufCols;
+      for (int kb = 0; kb < num_kb; ++kb, ++kbi) {
+        const int stage = kbi % kIStages;
+        if (!mbar_wait(&s.full[stage], (kbi / kIStages) & 1) || *failed) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t adesc = sw128_desc(s.a[stage]);
+        const uint64_t bdesc = sw128_desc(s.b[stage]);
+#pragma unroll
+        for (int kk = 0; kk < kIBK / 32; ++kk)
+          mma_i8(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&s.empty[stage]);
+      }
+      // Commit the accumulator (also after a failed wait, so every MMA
+      // issued is tracked before TMEM is freed).
+      mma_commit(&s.dfull[buf]);
+      ++ti;
+    }
+    if (!ok)
+      *failed = 1;
+    // Let the last MMAs land before TMEM is freed.
+    if (ti > 0)
+      mbar_wait(&s.dfull[(ti - 1) & 1], ((ti - 1) >> 1) & 1);
+  } else if (warp >= 2) {
+    const int quad = warp % 4, half = (warp - 2) / 4;
+    const uint32_t tlane = static_cast<uint32_t>(quad * 32) << 16;
+    uint32_t ti = 0;
+    bool ok = true;
+    for (int ot = blockIdx.x; ot < num_tiles; ot += gridDim.x, ++ti) {
+      const int buf = ti & 1;
+      const int nb = fdiv(ot, div_mb);
+      const int row = (ot - nb * num_mb) * kIBM + quad * 32 + lane;
+      const int n_half = nb * kIBN + half * (kIBN / 2);
+      if (!mbar_wait(&s.dfull[buf], (ti >> 1) & 1) || *failed) {
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      int64_t base = static_cast<int64_t>(row) * N, step = 1;
+      if (out_pixels > 0 && row < M) {
+        const int64_t img = fdiv(row, div_pix);
+        base = img * N * out_pixels + (row - img * out_pixels);
+        step = out_pixels;
+      }
+#pragma unroll 1
+      for (int c = 0; c < kIBN / 2 / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + tlane + buf * kIBufCols + half * (kIBN / 2) + c * 32, r);
+        const int n0 = n_half + c * 32;
+        if (row >= M)
+          continue;
+        if (bias != nullptr)
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < N)
+              r[j] += static_cast<uint32_t>(bias[n0 + j]);
+        if (step == 1 && vec && n0 + 32 <= N) {
+          int4 *dst = reinterpret_cast<int4 *>(y + base + n0);
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            dst[j / 4] = make_int4(static_cast<int>(r[j]), static_cast<int>(r[j + 1]),
+                                   static_cast<int>(r[j + 2]), static_cast<int>(r[j + 3]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < N)
+              y[base + static_cast<int64_t>(n0 + j) * step] = static_cast<int32_t>(r[j]);
+        }
+      }
+      // The accumulator is free once every epilogue warp has read it.
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0)
+        mbar_arrive(&s.dempty[buf]);
+    }
+    if (!ok) {
+      *failed = 1;
+      if (lane == 0)
+        atomicOr(status, CIM22_STATUS_TIMEOUT);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(2 * kIBufCols));
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side.
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -897,6 +1094,30 @@ bool launch_int8(const int8_t *A, int64_t a_rows, int64_t a_cols, const int8_t *
       (out_pixels > 0 && M % out_pixels))
     return false;
   const FastDiv div_pix = make_fastdiv(static_cast<uint32_t>(out_pixels > 0 ? out_pixels : 1));
+  // Enough 128 x 256 tiles for every SM: the persistent kernel.
+  const int64_t num_mb = (M + kIBM - 1) / kIBM;
+  const int64_t p_tiles = num_mb * ((N + kIBN - 1) / kIBN);
+  if (p_tiles >= sm_count() && p_tiles < (int64_t{1} << 31)) {
+    CUtensorMap ta, tb;
+    if (!encode_int8_2d(&ta, A, a_rows, a_cols, kIBM) ||
+        !encode_int8_2d(&tb, B, n_pad, k_pad, kIBN))
+      return false;
+    constexpr size_t smem = sizeof(SmemI8P) + 1024;
+    if (cudaFuncSetAttribute(int8_persistent_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return false;
+    const int vec = (N % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) ? 1 : 0;
+    const int grid = static_cast<int>(std::min<int64_t>(p_tiles, sm_count()));
+    if (launch_pdl(int8_persistent_kernel, dim3(grid), kIThreads, smem, stream, ta, tb,
+                   static_cast<int>((k_pad + kIBK - 1) / kIBK), static_cast<int>(M),
+                   static_cast<int>(N), static_cast<int>(num_mb),
+                   make_fastdiv(static_cast<uint32_t>(num_mb)), bias,
+                   static_cast<int>(out_pixels), div_pix, vec, y, status) != cudaSuccess)
+      return false;
+    g_tc_launches.fetch_add(1, std::memory_order_relaxed);
+    return true;
+  }
   // Columns beyond a_cols (to k_pad) and rows beyond a_rows read TMA's zero fill.
   CUtensorMap ta, tb;
   if (!encode_int8_2d(&ta, A, a_rows, a_cols, kBM) || !encode_int8_2d(&tb, B, n_pad, k_pad, kBN))

@@ -114,3 +114,36 @@ def test_int8_rows_out_pixels_and_argument_checks():
     with pytest.raises(RuntimeError, match="invalid arguments"):
         layer.forward_int8(dev(np.zeros((1, 8, 10, 10), np.int8)), out, 1, gather=g,
                            workspace=Workspace(DEV), status=status)
+
+
+def test_int8_persistent_kernel_large_linear():
+    """Shapes with enough 128 x 256 tiles for every SM take the persistent
+    kernel (two TMEM accumulators, ragged M, N and K): exact int32 sums."""
+    from cim22_b200.native import lib
+
+    rng = np.random.default_rng(21)
+    m, k, n = 4133, 1000, 2053
+    x = rng.integers(-128, 128, (m, k)).astype(np.int8)
+    w = rng.integers(-127, 128, (n, k)).astype(np.int8)
+    bias = rng.integers(-1000, 1000, n).astype(np.int32)
+    layer = CimLayer(w, kind="int8", device=DEV)
+    assert layer.range_safe
+    out = torch.empty(m, n, dtype=torch.int32, device=DEV)
+    before = lib().cim22_cuda_tensor_core_launches()
+    status = StatusWord(DEV)
+    layer.forward_int8(dev(x), out, m, bias=dev(bias), workspace=Workspace(DEV), status=status)
+    status.raise_if_set()
+    assert lib().cim22_cuda_tensor_core_launches() == before + 1
+    exact = (x.astype(np.float64) @ w.T.astype(np.float64)).astype(np.int64) + bias
+    np.testing.assert_array_equal(out.cpu().numpy(), exact.astype(np.int32))
+
+
+def test_int8_persistent_kernel_conv_nchw():
+    rng = np.random.default_rng(22)
+    x = rng.integers(-128, 128, (64, 16, 32, 32)).astype(np.int8)
+    wt = rng.integers(-20, 21, (64, 16, 3, 3)).astype(np.int8)
+    bias = rng.integers(-(1 << 20), 1 << 20, 64).astype(np.int32)
+    layer = CimLayer(wt.reshape(64, -1), kind="int8", device=DEV)
+    y = layer.conv2d_int8(dev(x), (3, 3), 1, (1, 1, 1, 1), dev(bias))
+    np.testing.assert_array_equal(y.cpu().numpy(),
+                                  oracle.conv2d_int8(x, wt, bias, (1, 1), (1, 1, 1, 1)))
