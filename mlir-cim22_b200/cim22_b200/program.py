@@ -375,13 +375,19 @@ class Program:
         out = torch.empty(out_shape, dtype=torch.float32, device=self.device)
         status = self.status
 
-        def run():
+        in_bytes = slot[0].numel() * 4
+        out_bytes = out[0].numel() * 4
+
+        def run_part(lo: int, hi: int, stream) -> None:
             from .native import check
 
-            check(lib().cim22_cuda_chain_forward(specs, len(plan), slot.data_ptr(), batch,
-                                                 out.data_ptr(), status.tensor.data_ptr(),
-                                                 cim_ops._stream(out.device)),
+            check(lib().cim22_cuda_chain_forward(specs, len(plan), slot.data_ptr() + lo * in_bytes,
+                                                 hi - lo, out.data_ptr() + lo * out_bytes,
+                                                 status.tensor.data_ptr(), stream),
                   "cim22_cuda_chain_forward")
+
+        def run():
+            run_part(0, batch, cim_ops._stream(out.device))
 
         try:
             run()
@@ -1304,15 +1310,16 @@ class Program:
     def check_status(self) -> None:
         self.status.raise_if_set(f"{self.name}: ")
 
+
     def __call__(self, *values: torch.Tensor):
         """Run on inputs (CPU or CUDA). Returns outputs on the inputs' device."""
         if len(values) != len(self.inputs):
             raise ValueError("Input count differs from compiled signature")
         on_cpu = any(v.device.type == "cpu" for v in values)
-        for v, slot, shape, dtype in zip(values, self.inputs, self.input_shapes,
-                                         self.input_dtypes):
+        for v, shape, dtype in zip(values, self.input_shapes, self.input_dtypes):
             if tuple(v.shape) != shape or v.dtype != dtype:
                 raise ValueError(f"input must be {dtype} {shape}")
+        for v, slot in zip(values, self.inputs):
             slot.tensor.copy_(v, non_blocking=True)
         self.replay()
         for i in sorted(self.mutated_inputs):

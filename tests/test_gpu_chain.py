@@ -120,3 +120,20 @@ def test_non_chain_graphs_keep_layer_kernels():
 
     model, x = workloads.build("resnet18", 1)
     assert not program.from_module(model, x).chained
+
+
+def test_pipelined_host_batches_match():
+    """Host batches (pinned or pageable) through a chained program give the
+    device-resident run's bits."""
+    from cim22_b200 import program, workloads
+
+    model, x = workloads.build("lenet", 256, seed=3)
+    prog = program.from_module(model, x, chain=True)
+    prog.capture()
+    expected = run(prog, x)
+    got = prog(x.pin_memory())
+    assert got.device.type == "cpu"
+    np.testing.assert_array_equal(bits(got.numpy()), bits(expected))
+    got2 = prog(x.pin_memory())
+    np.testing.assert_array_equal(bits(got2.numpy()), bits(expected))
+    np.testing.assert_array_equal(bits(prog(x).numpy()), bits(expected))
