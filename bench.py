@@ -540,7 +540,8 @@ def main() -> None:
     # End to end through the public API (torch.compile, runtime="cuda").
     name = backend.register()
     compiled = torch.compile(model, backend=name, fullgraph=True, dynamic=False,
-                             options={"runtime": "cuda", "device": local})
+                             options={"runtime": "cuda", "device": local,
+                                      "chain": prog.chained})
     host = x.pin_memory()
     with torch.inference_mode():
         out = compiled(host)

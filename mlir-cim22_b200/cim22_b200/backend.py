@@ -7,6 +7,11 @@ and its options (python/cim22/compiler.py:28-93):
                        kernels on a B200 (this package);
   runtime="reference"  the captured graph with CPU PyTorch operators, exactly as
                        the reference's reference mode.
+  chain                "auto" (default): a network that is one chain of Conv2d /
+                       Linear layers with ReLU/GELU and 2x2 max pools runs either
+                       as one fused persistent kernel or layer by layer, whichever
+                       a timed launch finds faster (same bits); True / False force
+                       one of them.
 
 Read-only module parameters and buffers are frozen into the compiled program,
 as the reference freezes them (backend.py:161-196); Dynamo guards on their
@@ -30,6 +35,7 @@ class BackendOptions(TypedDict, total=False):
     bf16_compensation: str
     device: int
     cuda_graph: bool
+    chain: Any  # "auto" (default), True or False: the fused layer chain lowering
     artifact_dir: Any
     debug_dir: Any
 
@@ -109,7 +115,8 @@ def backend(gm: torch.fx.GraphModule, example_inputs: Sequence[torch.Tensor], *,
     program = Program(gm, [e.detach() if isinstance(e, torch.Tensor) else e
                            for e in example_inputs],
                       frozen=frozen, device=device, name="cim22_cuda",
-                      bf16_compensation=options.get("bf16_compensation", "sign-split"))
+                      bf16_compensation=options.get("bf16_compensation", "sign-split"),
+                      chain=options.get("chain", "auto"))
     if options.get("cuda_graph", True):
         program.capture()
     inputs = [i for i in range(len(placeholders)) if i not in frozen]

@@ -34,7 +34,7 @@ def test_frozen_parameters_are_identity_guarded(monkeypatch):
     module's frozen weights (python/cim22/backend.py:207-210)."""
 
     class FakeProgram:
-        def __init__(self, gm, example, frozen, device, name, bf16_compensation):
+        def __init__(self, gm, example, frozen, device, name, bf16_compensation, chain):
             self.gm, self.example, self.frozen = gm, example, frozen
 
         def capture(self):
