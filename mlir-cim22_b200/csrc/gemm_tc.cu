@@ -356,24 +356,10 @@ __device__ __forceinline__ void tmem_wait(uint32_t (&r)[16]) {
                  "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])::"memory");
 }
 
-// Every TMEM accumulator of the sign-split kernel starts at the bit pattern
-// of 2^23: dots are below 2^21, so the int32 sum 2^23-bits + dot is the f32
-// 2^23 + dot, ready for the exact restore without a further integer step.
+// A crossbar dot of the sign-split kernel is a nonnegative int32 below 2^21
+// (prealigned magnitudes of at most 127 over 64 elements), so OR-ing in the
+// bit pattern of 2^23 gives the f32 2^23 + dot, ready for the exact restore.
 constexpr uint32_t kDotBias = 0x4b000000u;
-
-// Write v into kCols (8 or 16) consecutive TMEM columns of the warp's lanes.
-template <int kCols>
-__device__ __forceinline__ void tmem_fill(uint32_t taddr, uint32_t v) {
-  if (kCols == 16)
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, "
-                 "%1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-                 "r"(v)
-                 : "memory");
-  else
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};"
-                 ::"r"(taddr), "r"(v)
-                 : "memory");
-}
 
 // Exact restore of one tile value outside the fast window (out of line).
 __device__ __noinline__ float tc_slow_tile_add(float acc, int p, int ew, int ex,
@@ -396,7 +382,7 @@ __device__ __forceinline__ float act_tc(float v, int act) {
 // crossbar tile to the branch sums: the exact three-operation form inside
 // the window (scales read from the exponent slot four at a time), the
 // integer path otherwise.
-// p holds 2^23 + dot as f32 bits (the TMEM accumulator starts at kDotBias).
+// p holds the dots as read from TMEM.
 // kInit marks the first crossbar tile of an output tile: the sums start at
 // +0, and q * s (exact, nonnegative) is what fma(q, s, +0) gives.
 template <int kLT, bool kInit>
@@ -412,14 +398,14 @@ __device__ __forceinline__ void restore_add(float (&acc)[kLT], const uint32_t (&
       const float s[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float v = __fmaf_rn(__uint_as_float(p[j4 + j]), sx, nsx);
+        const float v = __fmaf_rn(__uint_as_float(p[j4 + j] | kDotBias), sx, nsx);
         const float q = __uint_as_float(__float_as_uint(v) & 0xffff0000u);
         acc[j4 + j] = kInit ? __fmul_rn(q, s[j]) : __fmaf_rn(q, s[j], acc[j4 + j]);
       }
     }
   } else {
     for (int j = 0; j < kLT; ++j)
-      acc[j] = tc_slow_tile_add(kInit ? 0.0f : acc[j], static_cast<int>(p[j] - kDotBias),
+      acc[j] = tc_slow_tile_add(kInit ? 0.0f : acc[j], static_cast<int>(p[j]),
                                 exB[ew_index + j], ex, status);
   }
 }
@@ -628,7 +614,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
       for (int t = 0; t < T; ++t, ++gi) {
         const int half = t % 2, stage = kbi % kSStages, buf = gi % kTmemBufs;
         if ((half == 0 && !mbar_wait(&s.full[stage], (kbi / kSStages) & 1)) ||
-            !mbar_wait(&s.dempty[buf], (gi / kTmemBufs) & 1) || *failed) {
+            !mbar_wait(&s.dempty[buf], ((gi / kTmemBufs) & 1) ^ 1) || *failed) {
           ok = false;
           break;
         }
@@ -638,8 +624,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
         for (int a = 0; a < kAB; ++a) {
           const uint64_t adesc = sw128_desc(s.a[stage][a]) + half * 4;
           const uint32_t d = tmem + buf * kBufCols + a * SN;
-          // Accumulate onto the 2^23 preset the epilogue left in the buffer.
-          mma_i8(d, adesc, bdesc, idesc, 1u);
+          mma_i8(d, adesc, bdesc, idesc, 0u);
           mma_i8(d, adesc + 2, bdesc + 2, idesc, 1u);
         }
         mma_commit(&s.dfull[buf]);
@@ -659,25 +644,6 @@ __global__ void __launch_bounds__(kSThreads, 1)
     const int quad = warp % 4, sub = (warp - 2) / 4;
     const int row_local = quad * 32 + lane;
     const uint32_t tlane = static_cast<uint32_t>(quad * 32) << 16;
-    // Preset the TMEM buffers this CTA will use (one per crossbar tile, at
-    // most all four) to 2^23 in this thread's columns and release them to the
-    // MMA thread (phase 0 of each dempty barrier).
-    const int my_tiles = blockIdx.x < num_tiles
-                             ? (num_tiles - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
-                             : 0;
-    const int used_bufs = min(kTmemBufs, my_tiles * T);
-    for (int b = 0; b < used_bufs; ++b)
-#pragma unroll
-      for (int a = 0; a < kAB; ++a)
-#pragma unroll
-        for (int w = 0; w < 2; ++w)
-          tmem_fill<LT>(tmem + tlane + b * kBufCols + a * SN + w * L + sub * LT, kDotBias);
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncwarp();
-    if (lane == 0)
-      for (int b = 0; b < used_bufs; ++b)
-        mbar_arrive(&s.dempty[b]);
     uint32_t gi = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
@@ -742,13 +708,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
             restore_add<LT, false>(acc[a][1], p1, fast[a], sx[a], nsx[a], &e.w[1][sub * LT],
                                    exB, ew1, ex[a], status);
           }
-          // Preset the columns just read for their next use.
-          tmem_fill<LT>(col0 + a * SN, kDotBias);
-          tmem_fill<LT>(col0 + a * SN + L, kDotBias);
         }
-        // Hand the TMEM buffer back once the presets have landed, and the
-        // exponent slot once every lane has used it.
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        // Hand the TMEM buffer and the exponent slot back once every lane
+        // has read them.
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
