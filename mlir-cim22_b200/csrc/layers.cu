@@ -675,6 +675,409 @@ void launch_signsplit_simt(const int8_t *A, const int32_t *exA, int64_t m_pad,
 }
 
 // ---------------------------------------------------------------------------
+// One-tile sign-split layers (K <= 64) of at most kDirectLanes lanes, such as
+// the first convolution of an image network. Each thread owns kCols columns
+// 256 apart: per column it gathers the group through the block's tap table
+// (a warp reads one tap of 32 neighbouring output pixels), splits, rounds and
+// prealigns it in registers (the thread owns the whole group: no shuffles);
+// then, lane by lane, every weight word read from shared memory (a broadcast)
+// is dotted with all of the thread's columns. The prepared operand never
+// leaves the registers, and a warp's outputs of one lane and column slot are
+// 32 consecutive columns (128-byte stores into NCHW planes). kWords (even) is
+// the number of 4-byte K words holding the layer's K elements. With one K tile
+// there is no K sum: each branch value is its restored tile added to +0, as
+// in the multi-tile kernels.
+constexpr int kDirectLanes = 64;
+
+// Columns per thread: the aligned operand of all of them stays within 32
+// registers.
+template <int kActBranches, int kWords>
+constexpr int direct_columns() {
+  return 32 / (kActBranches * kWords) >= 4 ? 4 : 32 / (kActBranches * kWords) >= 1 ? 32 / (kActBranches * kWords) : 1;
+}
+
+// The K elements of a one-tile layer as seen from a column's window origin,
+// passed in kernel parameter space so that the unrolled gather reads each
+// offset as an instruction operand. rows[t] (cols[t]) is the bit set of the K
+// elements whose kernel row (column) is below t; a column's valid elements are
+// those of its in-bounds kernel rows and columns. A rows gather has one
+// "kernel row" of K elements at offsets 0 .. K-1.
+struct DirectTaps {
+  int rel[kTileK];
+  unsigned long long rows[kTileK + 1], cols[kTileK + 1];
+};
+
+DirectTaps make_direct_taps(const Gather32 &g) {
+  DirectTaps t{};
+  const bool conv = g.kind != CIM22_GATHER_ROWS;
+  const int KH = conv ? g.KH : 1, KW = conv ? g.KW : 1;
+  unsigned long long rowbits[kTileK] = {}, colbits[kTileK] = {};
+  for (int k = 0; k < g.K; ++k) {
+    int i = 0, j = 0;
+    if (conv) {
+      const int c = k / (KH * KW), r = k % (KH * KW);
+      i = r / KW;
+      j = r % KW;
+      t.rel[k] = c * g.sC + i * g.sH + j * g.sW;
+    } else {
+      t.rel[k] = k;
+    }
+    rowbits[i] |= 1ull << k;
+    colbits[j] |= 1ull << k;
+  }
+  for (int r = 0; r < KH; ++r)
+    t.rows[r + 1] = t.rows[r] | rowbits[r];
+  for (int c = 0; c < KW; ++c)
+    t.cols[c + 1] = t.cols[c] | colbits[c];
+  return t;
+}
+
+// Gather, split, round and prealign the group of column m: aw[a] holds the
+// aligned bytes of activation branch a, ex[a] its group exponent (kZeroGroup
+// for an all-zero branch). Returns whether the column can take the fast
+// restore for weight exponents in [win_lo, win_hi]: every branch is a zero
+// group or has 7 <= ex <= 230 and 140 <= ex + ew <= 374 (then p * 2^(ex-133)
+// is a normal f32 that one FMA against -2^23 * 2^(ex-133) yields exactly, and
+// the tile Q(p) * 2^(ex+ew-266) is a normal BF16).
+template <int kActBranches, int kMode, int kWords>
+__device__ __forceinline__ bool direct_prepare(const float *__restrict__ x, const Gather32 &g,
+                                               const DirectTaps &tp, int m, bool col_valid,
+                                               int win_lo, int win_hi, int32_t *status,
+                                               uint32_t (&aw)[kActBranches][kWords],
+                                               int (&ex)[kActBranches]) {
+  static_assert(kMode != kPrepConvPool, "direct layers gather without a fused pool");
+  constexpr int kE = 4 * kWords; // gathered elements (a multiple of 8)
+  uint32_t signed_pairs[kE / 2];
+  uint32_t raw_max = 0;
+  const float *src = x;
+  unsigned long long valid = 0;
+  if (col_valid) {
+    if (kMode == kPrepRows) {
+      src = x + static_cast<int64_t>(m) * g.K;
+      valid = tp.rows[1];
+    } else {
+      const int n = fdiv(m, g.div_ohw);
+      const int rm = m - n * g.OH * g.OW;
+      const int oh = fdiv(rm, g.div_ow);
+      const int ow = rm - oh * g.OW;
+      const int ih0 = oh * g.SH - g.PH, iw0 = ow * g.SW - g.PW;
+      src = x + static_cast<int64_t>(n) * g.image + (ih0 * g.sH + iw0 * g.sW);
+      // In-bounds kernel rows [rlo, rhi) and columns [clo, chi).
+      const int rlo = min(max(-ih0, 0), g.KH), rhi = max(min(g.H - ih0, g.KH), rlo);
+      const int clo = min(max(-iw0, 0), g.KW), chi = max(min(g.W - iw0, g.KW), clo);
+      valid = (tp.rows[rhi] & ~tp.rows[rlo]) & (tp.cols[chi] & ~tp.cols[clo]);
+    }
+  }
+#pragma unroll
+  for (int chunk = 0; chunk < kE; chunk += 8) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      v[e] = (valid >> (chunk + e)) & 1ull ? __ldg(src + tp.rel[chunk + e]) : 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[e], v[e + 1]);
+      signed_pairs[(chunk + e) / 2] = *reinterpret_cast<const uint32_t *>(&h);
+      if (kActBranches == 2)
+        raw_max = max(raw_max, max(__float_as_uint(v[e]) & 0x7fffffffu,
+                                   __float_as_uint(v[e + 1]) & 0x7fffffffu));
+      else
+        raw_max = max(raw_max, max(__float_as_uint(v[e]), __float_as_uint(v[e + 1])));
+    }
+  }
+  uint32_t mx[2] = {0, 0};
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a) {
+    uint32_t m2 = 0;
+#pragma unroll
+    for (int e = 0; e < kE / 2; ++e)
+      m2 = __vmaxu2(m2, branch_pair<kActBranches>(signed_pairs[e], a));
+    mx[a] = max(m2 & 0xffffu, m2 >> 16);
+  }
+  // Non-finite groups: BF16 exponent 0xff in the 2-branch maximum, |x| of
+  // the raw inputs otherwise (the max with 0 drops NaN).
+  const bool nonfinite = kActBranches == 2 ? raw_max >= 0x7f7f8000u : mx[0] >= 0x7f80u;
+  if (nonfinite)
+    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
+  else if (kActBranches == 1 && raw_max > 0x80000000u)
+    atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
+  bool fast = true;
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a) {
+    const bool zero = mx[a] == 0 || nonfinite;
+    ex[a] = zero ? kZeroGroup : effective_exponent(static_cast<uint16_t>(mx[a]));
+    fast &= zero || (ex[a] >= 7 && ex[a] <= 230 && ex[a] + win_lo >= 140 &&
+                     ex[a] + win_hi <= 374);
+#pragma unroll
+    for (int q = 0; q < kWords; ++q)
+      aw[a][q] = zero ? 0u
+                      : align4(branch_pair<kActBranches>(signed_pairs[2 * q], a),
+                               branch_pair<kActBranches>(signed_pairs[2 * q + 1], a), mx[a],
+                               ex[a]);
+  }
+  return fast;
+}
+
+// Dots of one weight row (kWords words, pairs in shared memory) with the
+// first kBr activation branches of every column.
+template <int kBr, int kCols, int kAB, int kWords>
+__device__ __forceinline__ void direct_dots(const uint2 *row,
+                                            const uint32_t (&aw)[kCols][kAB][kWords],
+                                            int (&p)[kCols][kAB]) {
+#pragma unroll
+  for (int c = 0; c < kCols; ++c)
+#pragma unroll
+    for (int a = 0; a < kBr; ++a)
+      p[c][a] = 0;
+#pragma unroll
+  for (int h = 0; h < kWords / 2; ++h) {
+    const uint2 b = row[h];
+#pragma unroll
+    for (int c = 0; c < kCols; ++c)
+#pragma unroll
+      for (int a = 0; a < kBr; ++a) {
+        p[c][a] = __dp4a(static_cast<int>(aw[c][a][2 * h]), static_cast<int>(b.x), p[c][a]);
+        p[c][a] = __dp4a(static_cast<int>(aw[c][a][2 * h + 1]), static_cast<int>(b.y), p[c][a]);
+      }
+  }
+}
+
+// The lane loop of the direct kernel when every column of the warp lies in
+// the fast-restore window, over the first kBr activation branches.
+template <int kBr, int kCols, int kAB, int kWords>
+__device__ __forceinline__ void direct_fast_lanes(
+    int N, const uint2 (*Bs)[kDirectLanes][kWords / 2], const float (*sSw)[kDirectLanes],
+    const float *sBias, const float *sScale, const float *sShift,
+    const uint32_t (&aw)[kCols][kAB][kWords], const float (&sx)[kCols][kAB],
+    const float (&nsx)[kCols][kAB], float floor_v, float *const (&yp)[kCols],
+    const bool (&valid)[kCols], int64_t lane_stride) {
+  for (int n = 0; n < N; ++n) {
+    float br[kCols][kAB][2];
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      int p[kCols][kAB];
+      direct_dots<kBr>(Bs[w][n], aw, p);
+      const float sw = sSw[w][n];
+#pragma unroll
+      for (int c = 0; c < kCols; ++c)
+#pragma unroll
+        for (int a = 0; a < kBr; ++a) {
+          const float v =
+              __fmaf_rn(__uint_as_float(static_cast<uint32_t>(p[c][a]) | 0x4b000000u),
+                        sx[c][a], nsx[c][a]);
+          br[c][a][w] = __fmaf_rn(__uint_as_float(__float_as_uint(v) & 0xffff0000u), sw, 0.0f);
+        }
+    }
+    const float bn = sBias[n], sn = sScale[n], hn = sShift[n];
+    const int64_t off = static_cast<int64_t>(n) * lane_stride;
+#pragma unroll
+    for (int c = 0; c < kCols; ++c) {
+      float out = __fsub_rn(br[c][0][0], br[c][0][1]);
+      if (kBr == 2) {
+        out = __fsub_rn(out, br[c][1][0]);
+        out = __fadd_rn(out, br[c][1][1]);
+      }
+      out = fmaxf(__fmaf_rn(__fadd_rn(out, bn), sn, hn), floor_v);
+      if (valid[c])
+        yp[c][off] = out;
+    }
+  }
+}
+
+template <int kActBranches, int kMode, int kWords>
+__global__ void __launch_bounds__(256, 2)
+    signsplit_direct_kernel(const float *__restrict__ x, Gather32 g,
+                            const __grid_constant__ DirectTaps tp,
+                            const int8_t *__restrict__ B, const int32_t *__restrict__ exB,
+                            int n_pad, int k_pad, int N, const float *__restrict__ bias,
+                            const float *__restrict__ post_scale,
+                            const float *__restrict__ post_shift, int act, int out_pixels,
+                            float *__restrict__ y, int32_t *status) {
+  constexpr int kCols = direct_columns<kActBranches, kWords>();
+  __shared__ __align__(16) uint2 Bs[2][kDirectLanes][kWords / 2];
+  __shared__ float sSw[2][kDirectLanes];
+  __shared__ int sExB[2][kDirectLanes];
+  __shared__ float sBias[kDirectLanes], sScale[kDirectLanes], sShift[kDirectLanes];
+  __shared__ int sWin[2];
+  const int tid = static_cast<int>(threadIdx.x);
+  // Resident weights first: no earlier kernel writes them.
+  for (int i = tid; i < 2 * N * (kWords / 2); i += 256) {
+    const int c = i % (kWords / 2), r = (i / (kWords / 2)) % N, w = i / ((kWords / 2) * N);
+    Bs[w][r][c] = __ldg(reinterpret_cast<const uint2 *>(
+        B + (static_cast<int64_t>(w) * n_pad + r) * k_pad + c * 8));
+  }
+  if (tid < 2 * N) {
+    const int w = tid / N, r = tid - w * N;
+    const int e = __ldg(exB + w * n_pad + r); // Ew[w][tile 0][lane]
+    sExB[w][r] = e;
+    sSw[w][r] = exp2i(e - 133);
+  }
+  if (tid >= 128 && tid < 160) {
+    // Range of the weight exponents: the fast-restore window of the block.
+    int lo = INT_MAX, hi = INT_MIN;
+    for (int i = tid - 128; i < 2 * N; i += 32) {
+      const int e = __ldg(exB + (i / N) * n_pad + i % N);
+      lo = min(lo, e);
+      hi = max(hi, e);
+    }
+    lo = __reduce_min_sync(kFull, lo);
+    hi = __reduce_max_sync(kFull, hi);
+    if (tid == 128) {
+      sWin[0] = lo;
+      sWin[1] = hi;
+    }
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+  if (tid < N) {
+    // Neutral values where the epilogue has no bias or scale: the merged
+    // branch sum is never -0, so adding +0 and fma(v, 1, +0) leave it as it is.
+    sBias[tid] = bias != nullptr ? bias[tid] : 0.0f;
+    sScale[tid] = post_scale != nullptr ? post_scale[tid] : 1.0f;
+    sShift[tid] = post_scale != nullptr ? post_shift[tid] : 0.0f;
+  }
+  __syncthreads();
+  const int win_lo = sWin[0], win_hi = sWin[1];
+  uint32_t aw[kCols][kActBranches][kWords];
+  int ex[kCols][kActBranches];
+  int m[kCols];
+  bool valid[kCols];
+  bool fast = true;
+#pragma unroll
+  for (int c = 0; c < kCols; ++c) {
+    m[c] = (static_cast<int>(blockIdx.x) * kCols + c) * 256 + tid;
+    valid[c] = m[c] < g.M;
+    fast &= direct_prepare<kActBranches, kMode, kWords>(x, g, tp, m[c], valid[c], win_lo,
+                                                        win_hi, status, aw[c], ex[c]) ||
+            !valid[c];
+  }
+  // Output of lane n: y[m][n] (rows) or y[image][n][pixel] (NCHW planes).
+  float *yp[kCols];
+  const int64_t lane_stride = out_pixels > 0 ? out_pixels : 1;
+#pragma unroll
+  for (int c = 0; c < kCols; ++c) {
+    int64_t base = static_cast<int64_t>(m[c]) * N;
+    if (out_pixels > 0) {
+      const int image = m[c] / out_pixels;
+      base = static_cast<int64_t>(image) * N * out_pixels + (m[c] - image * out_pixels);
+    }
+    yp[c] = y + base;
+  }
+  if (__all_sync(kFull, fast) && act != CIM22_ACT_GELU) {
+    // Every column of the warp in the fast window: the tile of dot p is
+    // (fma(2^23 + p, sx, -2^23 sx) with the low 16 bits cleared) * sw, exact.
+    float sx[kCols][kActBranches], nsx[kCols][kActBranches];
+    bool neg_live = false; // some column's xn branch is not a zero group
+#pragma unroll
+    for (int c = 0; c < kCols; ++c)
+#pragma unroll
+      for (int a = 0; a < kActBranches; ++a) {
+        const bool zero = ex[c][a] == kZeroGroup;
+        sx[c][a] = zero ? 0.0f : exp2i(ex[c][a] - 133);
+        nsx[c][a] = -8388608.0f * sx[c][a];
+        neg_live |= a == 1 && !zero;
+      }
+    // ReLU as max(v, 0): v is finite and never -0 here; -inf leaves v as is.
+    const float floor_v = act == CIM22_ACT_RELU ? 0.0f : -INFINITY;
+    // Where the warp's xn branches are all zero groups their tiles are +0 and
+    // ((pp - pn) - 0) + 0 == pp - pn (never -0): the 2-branch merge.
+    if (kActBranches == 2 && !__any_sync(kFull, neg_live))
+      direct_fast_lanes<1>(N, Bs, sSw, sBias, sScale, sShift, aw, sx, nsx, floor_v, yp, valid,
+                           lane_stride);
+    else
+      direct_fast_lanes<kActBranches>(N, Bs, sSw, sBias, sScale, sShift, aw, sx, nsx, floor_v,
+                                      yp, valid, lane_stride);
+    return;
+  }
+  for (int n = 0; n < N; ++n) {
+    float br[kCols][kActBranches][2];
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      int p[kCols][kActBranches];
+      direct_dots<kActBranches>(Bs[w][n], aw, p);
+      const int ew = sExB[w][n];
+      const float sw = sSw[w][n];
+#pragma unroll
+      for (int c = 0; c < kCols; ++c)
+#pragma unroll
+        for (int a = 0; a < kActBranches; ++a) {
+          const int e = ex[c][a], s = e + ew;
+          if (e == kZeroGroup)
+            br[c][a][w] = 0.0f;
+          else if (e <= 240 && s >= 140 && s <= 374)
+            br[c][a][w] = fmaf(__fmul_rn(trunc8f(p[c][a]), exp2i(e - 133)), sw, 0.0f);
+          else
+            br[c][a][w] = slow_tile_add(0.0f, p[c][a], ew, e, status);
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < kCols; ++c) {
+      float out = __fsub_rn(br[c][0][0], br[c][0][1]);
+      if (kActBranches == 2) {
+        out = __fsub_rn(out, br[c][1][0]);
+        out = __fadd_rn(out, br[c][1][1]);
+      }
+      if (bias != nullptr)
+        out = __fadd_rn(out, sBias[n]);
+      if (post_scale != nullptr)
+        out = __fmaf_rn(out, sScale[n], sShift[n]);
+      out = apply_act(out, act);
+      if (valid[c])
+        yp[c][static_cast<int64_t>(n) * lane_stride] = out;
+    }
+  }
+}
+
+// Whether cim22_cuda_layer_forward_bf16 may run a layer through
+// signsplit_direct_kernel (one K tile, at most kDirectLanes lanes).
+bool direct_layer(const cim22_cuda_layer *layer) {
+  return layer->tiles == 1 && layer->n <= kDirectLanes;
+}
+
+// Whether the direct kernel beats the prepare and tensor-core contract
+// kernels for this layer (crossovers measured on B200 over one-tile 3x3
+// convolutions and linear layers of 2^20 columns). Its cost grows with lanes
+// x K words x activation branches; NCHW planes take coalesced stores, rows
+// outputs (one column's lanes contiguous) do not.
+bool direct_preferred(const cim22_cuda_layer *layer, int branches, int64_t out_pixels) {
+  const int64_t words = (layer->k + 7) / 8 * 2, n = layer->n;
+  if (out_pixels <= 0)
+    return n <= 16 && words <= 8;
+  if (branches == 4)
+    return words * n <= 512 && !(words >= 16 && n >= 32);
+  return words * n <= 1024;
+}
+
+template <int kAB, int kMode>
+void launch_signsplit_direct(const cim22_cuda_layer *layer, const float *x, const Gather32 &g,
+                             int64_t m, const float *bias, const float *post_scale,
+                             const float *post_shift, int act, int64_t out_pixels, float *y,
+                             int32_t *status, cudaStream_t s) {
+  const int words = static_cast<int>((layer->k + 7) / 8) * 2; // even, K <= 4 * words
+  const DirectTaps taps = make_direct_taps(g);
+  auto go = [&](auto words_tag) {
+    constexpr int kWords = decltype(words_tag)::value;
+    constexpr int kCols = direct_columns<kAB, kWords>();
+    const unsigned grid = static_cast<unsigned>((m + 256 * kCols - 1) / (256 * kCols));
+    launch_pdl(signsplit_direct_kernel<kAB, kMode, kWords>, dim3(grid), 256, 0, s, x, g, taps,
+               static_cast<const int8_t *>(layer->weights),
+               static_cast<const int32_t *>(layer->exponents), static_cast<int>(layer->n_pad),
+               static_cast<int>(layer->k_pad), static_cast<int>(layer->n), bias, post_scale,
+               post_shift, act, static_cast<int>(out_pixels), y, status);
+  };
+  switch (words) {
+  case 2: go(std::integral_constant<int, 2>{}); break;
+  case 4: go(std::integral_constant<int, 4>{}); break;
+  case 6: go(std::integral_constant<int, 6>{}); break;
+  case 8: go(std::integral_constant<int, 8>{}); break;
+  case 10: go(std::integral_constant<int, 10>{}); break;
+  case 12: go(std::integral_constant<int, 12>{}); break;
+  case 14: go(std::integral_constant<int, 14>{}); break;
+  default: go(std::integral_constant<int, 16>{}); break;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // INT8 on CUDA cores: CTA tile 64 x 64, thread owns 4 columns x 4 lanes.
 __global__ void pad_int8_kernel(const int8_t *__restrict__ x, int64_t M,
                                 int64_t K, int64_t m_pad, int64_t k_pad,
@@ -1598,6 +2001,27 @@ int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float 
     const int mode = g.kind == CIM22_GATHER_ROWS ? kPrepRows
                      : g.pool_kernel > 0         ? kPrepConvPool
                                                  : kPrepConv;
+    if (direct_layer(layer) && mode != kPrepConvPool &&
+        direct_preferred(layer, branches, out_pixels)) {
+      auto direct = [&](auto ab_tag, auto mode_tag) {
+        launch_signsplit_direct<decltype(ab_tag)::value, decltype(mode_tag)::value>(
+            layer, x, dg, m, bias, post_scale, post_shift, activation, out_pixels, y, status,
+            s);
+      };
+      using R = std::integral_constant<int, kPrepRows>;
+      using C = std::integral_constant<int, kPrepConv>;
+      using B1 = std::integral_constant<int, 1>;
+      using B2 = std::integral_constant<int, 2>;
+      if (branches == 2) {
+        if (mode == kPrepRows) direct(B1{}, R{});
+        else direct(B1{}, C{});
+      } else {
+        if (mode == kPrepRows) direct(B2{}, R{});
+        else direct(B2{}, C{});
+      }
+      return cuda_ok(cudaGetLastError(), "fused layer launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+    }
+    if (layer->n <= 16 && layer->tiles <= 2) {
     // The CUDA-core contraction builds its own activation tiles.
     auto launch = [&](auto ab_tag, auto mode_tag) {
       constexpr int kAB = decltype(ab_tag)::value, kMode = decltype(mode_tag)::value;
@@ -1622,6 +2046,8 @@ int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float 
       else launch(B2{}, P{});
     }
     return cuda_ok(cudaGetLastError(), "fused layer launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+    }
+    // Other one-tile layers: the prepare and contract kernels below.
   }
   const int rc = cim22_cuda_layer_prepare_bf16(layer, x, gather, m, branches, workspace,
                                                workspace_bytes, status, stream);
@@ -1633,8 +2059,8 @@ int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float 
 }
 
 int cim22_cuda_layer_fused_forward(const cim22_cuda_layer *layer) {
-  return layer && layer->bf16 && layer->mode == CIM22_BF16_SIGN_SPLIT && layer->n <= 16 &&
-                 layer->tiles <= 2
+  return layer && layer->bf16 && layer->mode == CIM22_BF16_SIGN_SPLIT &&
+                 (direct_layer(layer) || (layer->n <= 16 && layer->tiles <= 2))
              ? 1
              : 0;
 }

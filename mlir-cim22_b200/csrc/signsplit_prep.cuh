@@ -102,10 +102,13 @@ __device__ __forceinline__ void group_exponents(uint32_t (&mx)[2], uint32_t flag
 }
 
 // ExpPrealign of eight BF16 magnitudes (packed in pairs) against a group of
-// maximum mx and exponent emax (not a zero group).
+// maximum mx and exponent emax; zeros for a zero group (emax == kZeroGroup),
+// which never enters the exact path (a caller's select on the zero case may
+// be if-converted into evaluating this function for it).
 __device__ __forceinline__ uint2 align8(const uint32_t (&packed)[4], uint32_t mx, int emax) {
   uint32_t lo = 0, hi = 0;
-  if ((mx >> 7) >= 8) {
+  const bool zero = emax == kZeroGroup;
+  if (zero || (mx >> 7) >= 8) {
     const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax) << 23);
     uint32_t q[8];
 #pragma unroll
@@ -115,8 +118,8 @@ __device__ __forceinline__ uint2 align8(const uint32_t (&packed)[4], uint32_t mx
       q[2 * e + 1] = __float_as_uint(
           __fmaf_rz(__uint_as_float(packed[e] & 0xffff0000u), scale, 8388608.0f));
     }
-    lo = pack_low_bytes(q[0], q[1], q[2], q[3]);
-    hi = pack_low_bytes(q[4], q[5], q[6], q[7]);
+    lo = zero ? 0u : pack_low_bytes(q[0], q[1], q[2], q[3]);
+    hi = zero ? 0u : pack_low_bytes(q[4], q[5], q[6], q[7]);
   } else {
     const int shift = 127 - emax;
 #pragma unroll
@@ -129,9 +132,11 @@ __device__ __forceinline__ uint2 align8(const uint32_t (&packed)[4], uint32_t mx
 }
 
 // ExpPrealign of four BF16 magnitudes (packed in pairs) against a group of
-// maximum mx and exponent emax (not a zero group), as bytes of one word.
+// maximum mx and exponent emax, as bytes of one word; 0 for a zero group
+// (emax == kZeroGroup), which never enters the exact path.
 __device__ __forceinline__ uint32_t align4(uint32_t p0, uint32_t p1, uint32_t mx, int emax) {
-  if ((mx >> 7) >= 8) {
+  const bool zero = emax == kZeroGroup;
+  if (zero || (mx >> 7) >= 8) {
     const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax) << 23);
     const uint32_t q0 = __float_as_uint(__fmaf_rz(__uint_as_float(p0 << 16), scale, 8388608.0f));
     const uint32_t q1 =
@@ -139,7 +144,7 @@ __device__ __forceinline__ uint32_t align4(uint32_t p0, uint32_t p1, uint32_t mx
     const uint32_t q2 = __float_as_uint(__fmaf_rz(__uint_as_float(p1 << 16), scale, 8388608.0f));
     const uint32_t q3 =
         __float_as_uint(__fmaf_rz(__uint_as_float(p1 & 0xffff0000u), scale, 8388608.0f));
-    return pack_low_bytes(q0, q1, q2, q3);
+    return zero ? 0u : pack_low_bytes(q0, q1, q2, q3);
   }
   const int shift = 127 - emax;
   return slow_align(p0 & 0xffffu, shift) | (slow_align(p0 >> 16, shift) << 8) |

@@ -1,6 +1,8 @@
 """Layer-level CUDA kernels against the oracle (bit-exact) and glue against
 PyTorch CPU eager f32 (the reference's own float oracle, 1e-3 relative)."""
 
+import itertools
+
 import numpy as np
 import pytest
 import torch
@@ -49,9 +51,10 @@ def test_linear_bf16_extreme_exponents_slow_path():
     from cim22_b200.cim_ops import CimLayer
 
     rng = np.random.default_rng(3)
-    for scale_x, scale_w in ((1e-30, 1e-8), (1e-38, 1.0), (1e20, 1e-20), (1e-20, 1e-20)):
-        x = (rng.standard_normal((17, 130)) * scale_x).astype(np.float32)
-        w = (rng.standard_normal((19, 130)) * scale_w).astype(np.float32)
+    for (scale_x, scale_w), k in itertools.product(
+            ((1e-30, 1e-8), (1e-38, 1.0), (1e20, 1e-20), (1e-20, 1e-20)), (130, 50)):
+        x = (rng.standard_normal((17, k)) * scale_x).astype(np.float32)
+        w = (rng.standard_normal((19, k)) * scale_w).astype(np.float32)
         expected = oracle.linear_bf16(x, w, None, branches=4)
         got = CimLayer(w).linear_bf16(torch.from_numpy(x).to(DEV)).cpu().numpy()
         np.testing.assert_array_equal(bits(got), bits(expected))
@@ -300,8 +303,11 @@ def test_linear_int8_tensor_core_shapes(m, k, n):
     # CTA, and whole rows of zero groups
     (3000, 256, 96, 4, "rows"), (2048, 130, 64, 2, "rows")])
 def test_linear_bf16_tensor_core_bit_exact(m, k, n, branches, scale):
-    """Wide layers run the tcgen05 sign-split kernel (launch counter checked)."""
-    from cim22_b200.cim_ops import CimLayer
+    """Wide layers run the tcgen05 sign-split kernel (launch counter checked).
+    The prepare + contract form always takes it; one-tile layers of at most 64
+    lanes, which forward_bf16 runs as one thread-per-column kernel, are
+    checked through both."""
+    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace
     from cim22_b200.native import lib
 
     rng = np.random.default_rng(m + k + n)
@@ -320,11 +326,18 @@ def test_linear_bf16_tensor_core_bit_exact(m, k, n, branches, scale):
     b = rng.standard_normal(n).astype(np.float32)
     expected = oracle.linear_bf16(x, w, b, branches=4, threads=8)
     layer = CimLayer(w)
+    xt, bt = torch.from_numpy(x).to(DEV), torch.from_numpy(b).to(DEV)
+    ws, status = Workspace(torch.device(DEV)), StatusWord(torch.device(DEV))
+    out = torch.empty(m, n, device=DEV)
     before = lib().cim22_cuda_tensor_core_launches()
-    got = layer.linear_bf16(torch.from_numpy(x).to(DEV), bias=torch.from_numpy(b).to(DEV),
-                            branches=branches).cpu().numpy()
+    layer.prepare_bf16(xt, m, branches=branches, workspace=ws, status=status)
+    layer.contract_bf16(out, m, bias=bt, branches=branches, workspace=ws, status=status)
+    status.raise_if_set()
     assert lib().cim22_cuda_tensor_core_launches() == before + 1
-    np.testing.assert_array_equal(bits(got), bits(expected))
+    np.testing.assert_array_equal(bits(out.cpu().numpy()), bits(expected))
+    if layer.fused_forward:
+        got = layer.linear_bf16(xt, bias=bt, branches=branches).cpu().numpy()
+        np.testing.assert_array_equal(bits(got), bits(expected))
 
 
 @pytest.mark.parametrize("layout,n,c,h,f,kk,stride,pad,branches,pool", [
@@ -334,13 +347,17 @@ def test_linear_bf16_tensor_core_bit_exact(m, k, n, branches, scale):
     ("nchw", 16, 4, 10, 7, 3, 1, 0, 2, 2),    # fused 2x2 pool, K = 36
     ("nhwc", 8, 1, 12, 1, 7, 1, 3, 4, 2),     # K = 49, one lane
     ("nchw", 32, 2, 16, 12, 5, 1, 2, 4, 0),   # 12 lanes, K = 50: fused CUDA-core kernel
-    ("nchw", 32, 4, 12, 16, 5, 1, 2, 2, 0)])  # 16 lanes, K = 100: two tiles, fused
+    ("nchw", 32, 4, 12, 16, 5, 1, 2, 2, 0),   # 16 lanes, K = 100: two tiles, fused
+    ("nchw", 8, 2, 24, 32, 3, 1, 1, 2, 0),    # event-frame conv0: K = 18, 32 lanes, direct
+    ("nchw", 4, 1, 20, 64, 8, 1, 3, 4, 0),    # K = 64, 64 lanes
+    ("nhwc", 4, 3, 8, 40, 3, 2, 1, 4, 2),     # fused pool, K = 27, 40 lanes
+    ("nchw", 6, 5, 12, 48, 3, 1, 1, 2, 0)])   # K = 45, 48 lanes
 @pytest.mark.parametrize("out_layout", ["rows", "nchw"])
 def test_narrow_fused_layers_bit_exact(layout, n, c, h, f, kk, stride, pad, branches, pool,
                                        out_layout):
-    """Layers of at most 16 lanes and two K tiles run as one kernel (the
-    CUDA-core contraction building its own activation tiles): bit-exact
-    against the oracle."""
+    """Layers of one K tile and at most 64 lanes (one thread per column), or of
+    at most 16 lanes and two K tiles (the CUDA-core contraction building its
+    own activation tiles), run as one kernel: bit-exact against the oracle."""
     from cim22_b200 import abi
     from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace, conv_gather
 
@@ -366,19 +383,54 @@ def test_narrow_fused_layers_bit_exact(layout, n, c, h, f, kk, stride, pad, bran
     out = torch.empty(m, f, device=DEV)
     status = StatusWord(torch.device(DEV))
     pixels = g.out_h * g.out_w if out_layout == "nchw" else 0
+    # NCHW outputs take a fused ReLU (the branch-free epilogue of the direct kernel).
+    act = "relu" if out_layout == "nchw" else None
     layer.forward_bf16(xt, out, m, gather=g, bias=torch.from_numpy(b).to(DEV),
-                       branches=branches, out_pixels=pixels,
+                       activation=act, branches=branches, out_pixels=pixels,
                        workspace=Workspace(torch.device(DEV)), status=status)
     status.raise_if_set()
     if out_layout == "nchw":
         got = out.cpu().numpy().reshape(n, f, g.out_h, g.out_w)
+        expected = np.where(expected > 0, expected, np.float32(0))
     else:
         got = out.cpu().numpy().reshape(n, g.out_h, g.out_w, f).transpose(0, 3, 1, 2)
     np.testing.assert_array_equal(bits(got), bits(expected))
 
 
+@pytest.mark.parametrize("act", [None, "relu"])
+def test_direct_conv_dead_negative_branch(act):
+    """A 4-branch one-tile conv over binary event frames, with negative pixels
+    in some images: warps whose xn groups are all zero take the 2-branch merge,
+    the others all four branches; bit-exact either way."""
+    from cim22_b200 import abi
+    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace, conv_gather
+
+    rng = np.random.default_rng(11)
+    n, c, h, f = 6, 2, 40, 32
+    x = (rng.random((n, c, h, h)) < 0.05).astype(np.float32)
+    x[3] *= -1.0                 # an image of non-positive pixels
+    x[4, :, 10:20, :] -= 0.5     # negative rows inside an image
+    w = (rng.standard_normal((f, c, 3, 3)) * 0.3).astype(np.float32)
+    b = rng.standard_normal(f).astype(np.float32)
+    expected = oracle.conv2d_bf16(x, w, b, 1, 1, branches=4, threads=8)
+    if act == "relu":
+        expected = np.where(expected > 0, expected, np.float32(0))
+    layer = CimLayer(w.reshape(f, -1))
+    assert layer.fused_forward
+    g = conv_gather(abi.GATHER_CONV_NCHW, n, c, h, h, 3, 3, 1, 1)
+    m = n * h * h
+    out = torch.empty(m, f, device=DEV)
+    status = StatusWord(torch.device(DEV))
+    layer.forward_bf16(torch.from_numpy(x).to(DEV), out, m, gather=g,
+                       bias=torch.from_numpy(b).to(DEV), activation=act, branches=4,
+                       out_pixels=h * h, workspace=Workspace(torch.device(DEV)), status=status)
+    status.raise_if_set()
+    got = out.cpu().numpy().reshape(n, f, h, h)
+    np.testing.assert_array_equal(bits(got), bits(expected))
+
+
 @pytest.mark.parametrize("m,k,n,branches", [(300, 25, 6, 4), (129, 64, 8, 2), (77, 100, 10, 4),
-                                            (1000, 3, 1, 2)])
+                                            (1000, 3, 1, 2), (300, 64, 64, 2), (50, 40, 33, 4)])
 def test_narrow_fused_linear_bit_exact(m, k, n, branches):
     from cim22_b200.cim_ops import CimLayer
 
