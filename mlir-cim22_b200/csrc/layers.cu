@@ -248,9 +248,9 @@ __device__ __forceinline__ uint32_t branch_pair(uint32_t pair, int a) {
 }
 
 template <int kActBranches, bool kPool>
-__global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 1)
+__global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
     prepare_nchw_kernel(const float *__restrict__ x, Gather32 g, FastDiv div_chunks, int T,
-                        int m_pad, int k_pad, int8_t *__restrict__ A,
+                        int cols, int m_pad, int k_pad, int8_t *__restrict__ A,
                         int32_t *__restrict__ ex, int32_t *status) {
   pdl_launch_dependents();
   pdl_wait();
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 1)
   __shared__ unsigned long long sRows[kTapMasks + 1], sCols[kTapMasks + 1];
   const int blk = static_cast<int>(blockIdx.x);
   const int t = fdiv(blk, div_chunks);
-  const int m = (blk - t * static_cast<int>(div_chunks.d)) * 256 + static_cast<int>(threadIdx.x);
+  const int chunk0 = (blk - t * static_cast<int>(div_chunks.d)) * cols;
   const int kbeg = t * kTileK;
   if (threadIdx.x < kTileK) {
     const int k = kbeg + static_cast<int>(threadIdx.x);
@@ -283,8 +283,12 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 1)
     }
   }
   __syncthreads();
+  // The block's `cols` chunks of 256 consecutive columns, one column per
+  // thread and chunk.
+  for (int r = 0; r < cols; ++r) {
+  const int m = (chunk0 + r) * 256 + static_cast<int>(threadIdx.x);
   if (m >= m_pad)
-    return; // whole warps: m_pad is a multiple of 128
+    break; // whole warps: m_pad is a multiple of 128
   const float *img = x;
   int org = 0;
   unsigned long long inb = 0; // in-bounds elements of this column
@@ -393,6 +397,7 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 1)
     for (int q = 0; q < 4; ++q)
       dst[q] = make_uint4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
     ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax;
+  }
   }
 }
 
@@ -1868,12 +1873,18 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
   if (g.kind == CIM22_GATHER_CONV_NCHW && (g.pool_kernel == 0 || g.pool_kernel == 2) &&
       g.kernel_h <= kTapMasks && g.kernel_w <= kTapMasks &&
       ((m_pad + 255) / 256) * T >= 148 * 2) {
+    // Chunks of 256 columns per block: as many as (up to four) still give
+    // four waves of blocks on 148 SMs, to spread the block's tap table.
     const int64_t chunks = (m_pad + 255) / 256;
-    const FastDiv div_chunks = make_fastdiv(static_cast<uint32_t>(chunks));
-    const unsigned blocks = static_cast<unsigned>(chunks * T);
+    int per_block = 4;
+    while (per_block > 1 && ((chunks + per_block - 1) / per_block) * T < 148 * 4 * 4)
+      per_block /= 2;
+    const int64_t groups = (chunks + per_block - 1) / per_block;
+    const FastDiv div_chunks = make_fastdiv(static_cast<uint32_t>(groups));
+    const unsigned blocks = static_cast<unsigned>(groups * T);
     auto launch = [&](auto kernel) {
-      launch_pdl(kernel, blocks, 256, 0, s, x, dg, div_chunks, T, static_cast<int>(m_pad),
-                                    static_cast<int>(layer->k_pad), A, ex, status);
+      launch_pdl(kernel, blocks, 256, 0, s, x, dg, div_chunks, T, per_block,
+                 static_cast<int>(m_pad), static_cast<int>(layer->k_pad), A, ex, status);
     };
     const bool pool = g.pool_kernel > 0;
     if (ab == 1)
