@@ -231,6 +231,26 @@ __device__ __forceinline__ float exp2i(int e) {
                    : __uint_as_float(1u << (e + 149));
 }
 
+// Packed f32x2 arithmetic of sm_100: each half is an IEEE round-to-nearest
+// fma (or product) of its operands, as fmaf / __fmul_rn computes it.
+__device__ __forceinline__ void fma2(float a0, float a1, float b0, float b1, float c0, float c1,
+                                     float &d0, float &d1) {
+  asm("{\n\t.reg .b64 a, b, c, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+      "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+__device__ __forceinline__ void mul2(float a0, float a1, float b0, float b1, float &d0,
+                                     float &d1) {
+  asm("{\n\t.reg .b64 a, b, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // Q(p) as an exact f32 for 0 <= p < 2^23: the magic-number conversion is exact
 // and clearing the low 16 bits keeps the eight leading significant bits.
 __device__ __forceinline__ float trunc8f(int32_t p) {

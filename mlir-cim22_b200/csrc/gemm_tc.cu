@@ -397,10 +397,18 @@ __device__ __forceinline__ void restore_add(float (&acc)[kLT], const uint32_t (&
       const float4 s4 = *reinterpret_cast<const float4 *>(sw + j4);
       const float s[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float v = __fmaf_rn(__uint_as_float(p[j4 + j] | kDotBias), sx, nsx);
-        const float q = __uint_as_float(__float_as_uint(v) & 0xffff0000u);
-        acc[j4 + j] = kInit ? __fmul_rn(q, s[j]) : __fmaf_rn(q, s[j], acc[j4 + j]);
+      for (int j = 0; j < 4; j += 2) {
+        // Two dots per packed f32x2 operation (each half rounds as fmaf).
+        float v0, v1;
+        fma2(__uint_as_float(p[j4 + j] | kDotBias), __uint_as_float(p[j4 + j + 1] | kDotBias),
+             sx, sx, nsx, nsx, v0, v1);
+        const float q0 = __uint_as_float(__float_as_uint(v0) & 0xffff0000u);
+        const float q1 = __uint_as_float(__float_as_uint(v1) & 0xffff0000u);
+        if (kInit)
+          mul2(q0, q1, s[j], s[j + 1], acc[j4 + j], acc[j4 + j + 1]);
+        else
+          fma2(q0, q1, s[j], s[j + 1], acc[j4 + j], acc[j4 + j + 1], acc[j4 + j],
+               acc[j4 + j + 1]);
       }
     }
   } else {

@@ -867,21 +867,23 @@ __device__ __forceinline__ void direct_fast_lanes(
     const bool (&valid)[kCols], int64_t lane_stride) {
   for (int n = 0; n < N; ++n) {
     float br[kCols][kAB][2];
+    int p[2][kCols][kAB];
+    direct_dots<kBr>(Bs[0][n], aw, p[0]);
+    direct_dots<kBr>(Bs[1][n], aw, p[1]);
+    const float sw0 = sSw[0][n], sw1 = sSw[1][n];
 #pragma unroll
-    for (int w = 0; w < 2; ++w) {
-      int p[kCols][kAB];
-      direct_dots<kBr>(Bs[w][n], aw, p);
-      const float sw = sSw[w][n];
+    for (int c = 0; c < kCols; ++c)
 #pragma unroll
-      for (int c = 0; c < kCols; ++c)
-#pragma unroll
-        for (int a = 0; a < kBr; ++a) {
-          const float v =
-              __fmaf_rn(__uint_as_float(static_cast<uint32_t>(p[c][a]) | 0x4b000000u),
-                        sx[c][a], nsx[c][a]);
-          br[c][a][w] = __fmaf_rn(__uint_as_float(__float_as_uint(v) & 0xffff0000u), sw, 0.0f);
-        }
-    }
+      for (int a = 0; a < kBr; ++a) {
+        // The two weight signs of one column and branch as one f32x2 pair.
+        float v0, v1;
+        fma2(__uint_as_float(static_cast<uint32_t>(p[0][c][a]) | 0x4b000000u),
+             __uint_as_float(static_cast<uint32_t>(p[1][c][a]) | 0x4b000000u), sx[c][a],
+             sx[c][a], nsx[c][a], nsx[c][a], v0, v1);
+        fma2(__uint_as_float(__float_as_uint(v0) & 0xffff0000u),
+             __uint_as_float(__float_as_uint(v1) & 0xffff0000u), sw0, sw1, 0.0f, 0.0f,
+             br[c][a][0], br[c][a][1]);
+      }
     const float bn = sBias[n], sn = sScale[n], hn = sShift[n];
     const int64_t off = static_cast<int64_t>(n) * lane_stride;
 #pragma unroll
