@@ -501,12 +501,11 @@ int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float 
 /* 1 when cim22_cuda_layer_forward_bf16{,_ex} may run the layer as one kernel
  * that gathers, prealigns and contracts, so that its prepared columns never
  * leave the SM: one-tile layers (K <= 64) of at most 64 lanes (one thread per
- * column, preferred where measured faster: NCHW outputs of small enough
- * lanes x K x branches, rows outputs of at most 16 lanes and K <= 32) and
- * layers of at most 16 lanes and two K tiles (the CUDA-core contraction
- * building its own activation tiles). Such a call picks per gather and
- * output layout and otherwise runs the prepare and contract kernels itself.
- * 0: the caller runs prepare and contract. */
+ * column) and layers of at most 16 lanes and two K tiles (the CUDA-core
+ * contraction building its own activation tiles). Such a call picks, by the
+ * gather, output layout, branch count and column count, whichever was
+ * measured faster on B200, running the prepare and contract kernels itself
+ * where those win. 0: the caller runs prepare and contract. */
 int cim22_cuda_layer_fused_forward(const cim22_cuda_layer *layer);
 int cim22_cuda_layer_contract_bf16_ex(const cim22_cuda_layer *layer, int64_t m,
                                       int64_t out_pixels, const float *bias,

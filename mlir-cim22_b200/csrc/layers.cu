@@ -703,11 +703,13 @@ void launch_signsplit_simt(const int8_t *A, const int32_t *exA, int64_t m_pad,
 // in the multi-tile kernels.
 constexpr int kDirectLanes = 64;
 
-// Columns per thread: the aligned operand of all of them stays within 32
-// registers.
+// Columns per thread (at most 4): the aligned operand of all of them stays
+// within 48 registers.
 template <int kActBranches, int kWords>
 constexpr int direct_columns() {
-  return 32 / (kActBranches * kWords) >= 4 ? 4 : 32 / (kActBranches * kWords) >= 1 ? 32 / (kActBranches * kWords) : 1;
+  return 48 / (kActBranches * kWords) >= 4   ? 4
+         : 48 / (kActBranches * kWords) >= 1 ? 48 / (kActBranches * kWords)
+                                             : 1;
 }
 
 // The K elements of a one-tile layer as seen from a column's window origin,
@@ -1059,10 +1061,13 @@ bool direct_preferred(const cim22_cuda_layer *layer, int branches, int64_t out_p
   const int64_t words = (layer->k + 7) / 8 * 2, n = layer->n;
   if (out_pixels <= 0)
     return n <= 16 && words <= 8;
-  if (branches == 4)
-    return words * n <= 512 && !(words >= 16 && n >= 32);
-  return words * n <= 1024;
+  return words <= 8 || n <= 16 || (branches == 2 && n <= 32);
 }
+
+// The fused CUDA-core kernel of narrow layers (at most 16 lanes, two K
+// tiles) saves a launch, which pays up to about 2^17 columns; above that the
+// prepare and tensor-core contract kernels were measured faster.
+constexpr int64_t kFusedSimtColumns = int64_t{1} << 17;
 
 template <int kAB, int kMode>
 void launch_signsplit_direct(const cim22_cuda_layer *layer, const float *x, const Gather32 &g,
@@ -2044,7 +2049,7 @@ int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float 
       }
       return cuda_ok(cudaGetLastError(), "fused layer launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
     }
-    if (layer->n <= 16 && layer->tiles <= 2) {
+    if (layer->n <= 16 && layer->tiles <= 2 && m < kFusedSimtColumns) {
     // The CUDA-core contraction builds its own activation tiles.
     auto launch = [&](auto ab_tag, auto mode_tag) {
       constexpr int kAB = decltype(ab_tag)::value, kMode = decltype(mode_tag)::value;
