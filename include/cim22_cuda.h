@@ -513,6 +513,18 @@ int cim22_cuda_layer_contract_bf16_ex(const cim22_cuda_layer *layer, int64_t m,
                                       int32_t activation, int32_t branches, float *y,
                                       const void *workspace, size_t workspace_bytes,
                                       int32_t *status, void *stream);
+/* contract_bf16_ex with a residual add fused after the per-lane fma and
+ * before the activation: y = act(fma(merge + bias, post_scale, post_shift) +
+ * residual), one f32 add per element as the Host glue of a residual block
+ * (Conv -> BatchNorm -> add -> ReLU) computes it. residual is laid out like y
+ * (rows or NCHW planes, out_pixels as for y) and may be NULL. Sign-split
+ * layers only. */
+int cim22_cuda_layer_contract_bf16_res(const cim22_cuda_layer *layer, int64_t m,
+                                       int64_t out_pixels, const float *bias,
+                                       const float *post_scale, const float *post_shift,
+                                       const float *residual, int32_t activation,
+                                       int32_t branches, float *y, const void *workspace,
+                                       size_t workspace_bytes, int32_t *status, void *stream);
 
 /* INT8 layer: y[m, n] = sum over K tiles of the signed-i21 tile results,
  * accumulated in wrapping int32 (Passes.cpp:1054-1059). x is int8 [m, k]. */

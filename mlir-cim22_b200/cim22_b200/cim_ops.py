@@ -157,14 +157,21 @@ class CimLayer:
                       activation: str | None = None, branches: int = 4,
                       out_pixels: int = 0, post_scale: torch.Tensor | None = None,
                       post_shift: torch.Tensor | None = None,
+                      residual: torch.Tensor | None = None,
                       workspace: Workspace, status: StatusWord) -> None:
-        """Second kernel of forward_bf16: crossbar dots, restore, accumulate, merge."""
+        """Second kernel of forward_bf16: crossbar dots, restore, accumulate, merge.
+        residual (laid out like out) is added after the per-lane fma and before
+        the activation, as a Conv -> BatchNorm -> add -> ReLU block computes it."""
         _require(out, torch.float32, "out")
+        if residual is not None:
+            _require(residual, torch.float32, "residual")
+            if residual.numel() != out.numel():
+                raise ValueError("residual must have the output's shape")
         ws = workspace.get(self.workspace_bytes(m, branches))
-        check(lib().cim22_cuda_layer_contract_bf16_ex(
+        check(lib().cim22_cuda_layer_contract_bf16_res(
             self._handle, m, out_pixels, _ptr(bias), _ptr(post_scale), _ptr(post_shift),
-            ACT[activation], branches, _ptr(out), _ptr(ws), ws.numel(), _ptr(status.tensor),
-            _stream(out.device)),
+            _ptr(residual), ACT[activation], branches, _ptr(out), _ptr(ws), ws.numel(),
+            _ptr(status.tensor), _stream(out.device)),
             "cim22_cuda_layer_contract_bf16")
 
     def linear_bf16(self, x: torch.Tensor, bias=None, activation=None, branches: int = 4,

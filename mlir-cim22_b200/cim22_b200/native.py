@@ -81,6 +81,8 @@ _SIGNATURES = {
     "cim22_cuda_layer_compensation": (I32, [P]),
     "cim22_cuda_layer_contract_bf16_ex": (c.c_int, [P, I64, I64, P, P, P, I32, I32, P, P, SZ, P,
                                                     P]),
+    "cim22_cuda_layer_contract_bf16_res": (c.c_int, [P, I64, I64, P, P, P, P, I32, I32, P, P,
+                                                     SZ, P, P]),
     "cim22_cuda_layer_forward_bf16_noalloc": (c.c_int, [P, P, P, I64, P, I32, I32, P, P, P]),
     "cim22_cuda_layer_noalloc_scratch_bytes": (SZ, []),
     "cim22_cuda_relu": (c.c_int, [P, P, I64, P]),

@@ -618,6 +618,34 @@ class Program:
                 return user, (user.target, user.args, dict(user.kwargs))
         return None
 
+    def _fusable_residual(self, node, users, env, shape, layer):
+        """The add that is node's only user and whose other operand is an
+        image already computed, of the output's shape and this program's
+        layout, as (add node, that operand's Val), or None. The add folds into
+        node's contraction epilogue after the batch norm (f32 addition
+        commutes, so the operand computed last takes it: conv2 of an identity
+        block, the downsample conv of a projection block)."""
+        if not self.fuse or users[node] != 1 or layer.fused_forward or \
+                self.compensation != "sign-split":
+            return None
+        (user,) = node.users
+        if user.op == "call_function":
+            target, args, kwargs = user.target, user.args, user.kwargs
+        elif user.op == "call_method" and user.target == "add" and not user.kwargs:
+            target, args, kwargs = operator.add, user.args, {}
+        else:
+            return None
+        if target not in _ADD or len(args) != 2 or kwargs.get("alpha", 1) != 1:
+            return None
+        other = args[1] if args[0] is node else args[0] if args[1] is node else None
+        if not isinstance(other, fx.Node) or other is node or other not in env:
+            return None
+        v = env[other]
+        if v.kind != IMAGE or v.dtype != torch.float32 or v.flat_of is not None or \
+                tuple(v.shape) != tuple(shape) or v.layout != self.layout:
+            return None
+        return user, v
+
     def _bn_affine(self, args, kwargs, env):
         """Device (scale, shift) of an inference batch norm: y = x * scale + shift."""
         mean, var = self._const(env, args[1]), self._const(env, args[2])
@@ -675,6 +703,14 @@ class Program:
             post_scale, post_shift = self._bn_affine(bn_args, bn_kwargs, env)
             self._fused.add(bn_node)
             tail = bn_node
+        # A residual add of an image computed earlier folds in after that.
+        residual = None
+        res = self._fusable_residual(tail, users, env, (n, f, g.out_h, g.out_w), layer)
+        if res is not None:
+            add_node, other = res
+            residual = self._tensor(other)
+            self._fused.add(add_node)
+            tail = add_node
         act, out_node = self._epilogue(tail, users)
         nchw = self.layout == "nchw"
         out = self._new((n, f, g.out_h, g.out_w) if nchw else (n, g.out_h, g.out_w, f))
@@ -689,8 +725,8 @@ class Program:
         def run():
             layer.contract_bf16(out, m, bias=bias, activation=act, branches=branches,
                                 out_pixels=pixels, post_scale=post_scale,
-                                post_shift=post_shift, workspace=self.workspace,
-                                status=self.status)
+                                post_shift=post_shift, residual=residual,
+                                workspace=self.workspace, status=self.status)
 
         def fused():
             layer.forward_bf16(xt, out, m, gather=g, bias=bias, activation=act,
@@ -705,7 +741,7 @@ class Program:
             self.steps.append(Step(name + ".prepare", prepare))
         self.steps.append(Step(name, run, cim=True, meta=dict(
             kind="conv", x=xt, layout=x.layout, out_layout=self.layout,
-            post=None if post_scale is None else (post_scale, post_shift),
+            post=None if post_scale is None else (post_scale, post_shift), residual=residual,
             weight=torch.as_tensor(w).detach().float(),
             bias=None if b is None else torch.as_tensor(b).detach().float(), stride=stride[0],
             pad=pad[0], out=out, act=act, branches=branches)))

@@ -420,7 +420,8 @@ __device__ __forceinline__ void restore_add(float (&acc)[kLT], const uint32_t (&
 
 // Final merge of one output row's LT lanes: BF16 rounding of each branch sum
 // when there is more than one K tile, ((pp - pn) - np) + nn, bias, the
-// optional per-lane fma, the activation, then the store - rows, or NCHW
+// optional per-lane fma, the optional residual add, the activation, then the
+// store - rows, or NCHW
 // planes where a warp's 32 consecutive rows store 32 consecutive floats of a
 // lane. The branch sums are finite or infinite, never NaN, so the hardware
 // RNE conversion rounds them as the reference's truncf does.
@@ -428,7 +429,8 @@ template <int kAB, int LT>
 __device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, int lane0, int M,
                                            int N, int T, const float *__restrict__ bias,
                                            const float *__restrict__ post_scale,
-                                           const float *__restrict__ post_shift, int act,
+                                           const float *__restrict__ post_shift,
+                                           const float *__restrict__ residual, int act,
                                            int vec, int out_pixels, FastDiv div_pix,
                                            float *__restrict__ y) {
   if (row >= M)
@@ -476,6 +478,20 @@ __device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, in
       if (lane0 + j < N)
         o[j] = __fmaf_rn(o[j], __ldg(post_scale + lane0 + j), __ldg(post_shift + lane0 + j));
   }
+  if (residual != nullptr) {
+    // A residual add fused after the batch norm: the same element of a
+    // tensor laid out like y, one f32 add as the glue computes it.
+    int64_t base = static_cast<int64_t>(row) * N + lane0, lane_stride = 1;
+    if (out_pixels > 0) {
+      const int image = fdiv(row, div_pix);
+      base = (static_cast<int64_t>(image) * N + lane0) * out_pixels + (row - image * out_pixels);
+      lane_stride = out_pixels;
+    }
+#pragma unroll
+    for (int j = 0; j < LT; ++j)
+      if (lane0 + j < N)
+        o[j] = __fadd_rn(o[j], __ldg(residual + base + j * lane_stride));
+  }
   if (act == CIM22_ACT_RELU) {
 #pragma unroll
     for (int j = 0; j < LT; ++j)
@@ -515,7 +531,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
                         int m_pad, const int32_t *__restrict__ exB, int n_pad, int T, int M,
                         int N, FastDiv div_nb, const float *__restrict__ bias,
                         const float *__restrict__ post_scale,
-                        const float *__restrict__ post_shift, int act, int vec,
+                        const float *__restrict__ post_shift,
+                        const float *__restrict__ residual, int act, int vec,
                         int out_pixels, FastDiv div_pix, float *__restrict__ y,
                         int32_t *status) {
   using S = SSShape<kAB>;
@@ -729,7 +746,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
       if (!ok)
         break;
       store_tile<kAB, LT>(acc, m0 + row_local, lane0, M, N, T, bias, post_scale, post_shift,
-                          act, vec, out_pixels, div_pix, y);
+                          residual, act, vec, out_pixels, div_pix, y);
     }
     if (!ok) {
       *failed = 1;
@@ -1015,8 +1032,9 @@ bool int8_available() { return sm100(nullptr) && encode_fn() != nullptr; }
 bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const int8_t *B,
                       const int32_t *exB, int64_t n_pad, int64_t k_pad, int T, int64_t M,
                       int64_t N, const float *bias, const float *post_scale,
-                      const float *post_shift, int act, int act_branches,
-                      int64_t out_pixels, float *y, int32_t *status, cudaStream_t stream) {
+                      const float *post_shift, const float *residual, int act,
+                      int act_branches, int64_t out_pixels, float *y, int32_t *status,
+                      cudaStream_t stream) {
   // Layers of at most 8 lanes leave most of a 32- or 64-lane tile idle; the
   // CUDA-core kernel serves them. The exponent copies need 16-byte aligned
   // rows: m_pad and n_pad are multiples of 128 and both exponent arrays
@@ -1043,8 +1061,8 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
       return false;
     launch_pdl(kernel, grid, kSThreads, smem, stream, ta, tb, exA, static_cast<int>(m_pad), exB, static_cast<int>(n_pad), T,
         static_cast<int>(M), static_cast<int>(N),
-        make_fastdiv(static_cast<uint32_t>((N + L - 1) / L)), bias, post_scale, post_shift, act,
-        vec, static_cast<int>(out_pixels),
+        make_fastdiv(static_cast<uint32_t>((N + L - 1) / L)), bias, post_scale, post_shift,
+        residual, act, vec, static_cast<int>(out_pixels),
         make_fastdiv(static_cast<uint32_t>(out_pixels > 0 ? out_pixels : 1)), y, status);
     return true;
   };

@@ -25,8 +25,8 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad,
                       const int8_t *B, const int32_t *exB, int64_t n_pad,
                       int64_t k_pad, int T, int64_t M, int64_t N,
                       const float *bias, const float *post_scale,
-                      const float *post_shift, int act, int act_branches,
-                      int64_t out_pixels, float *y, int32_t *status,
+                      const float *post_shift, const float *residual, int act,
+                      int act_branches, int64_t out_pixels, float *y, int32_t *status,
                       cudaStream_t stream);
 
 // INT8 contraction with whole-K int32 accumulation (exact: range-proven

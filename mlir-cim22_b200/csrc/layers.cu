@@ -424,7 +424,8 @@ __global__ void __launch_bounds__(256)
                           int64_t k_pad, int T, int64_t M, int64_t N,
                           const float *__restrict__ bias,
                           const float *__restrict__ post_scale,
-                          const float *__restrict__ post_shift, int act, int64_t out_pixels,
+                          const float *__restrict__ post_shift,
+                          const float *__restrict__ residual, int act, int64_t out_pixels,
                           float *__restrict__ y, int32_t *status,
                           const float *__restrict__ x, Gather32 g, int k_logical) {
   pdl_launch_dependents();
@@ -648,6 +649,8 @@ __global__ void __launch_bounds__(256)
         out = __fadd_rn(out, bias[lane]);
       if (post_scale != nullptr && lane < N)
         out = __fmaf_rn(out, post_scale[lane], post_shift[lane]);
+      if (residual != nullptr && row < M && lane < N)
+        out = __fadd_rn(out, residual[base + lane * lane_stride]);
       out = apply_act(out, act);
       if (row < M && lane < N)
         y[base + lane * lane_stride] = out;
@@ -663,13 +666,13 @@ void launch_signsplit_simt(const int8_t *A, const int32_t *exA, int64_t m_pad,
                            const int8_t *B, const int32_t *exB, int64_t n_pad,
                            int64_t k_pad, int T, int64_t M, int64_t N,
                            const float *bias, const float *post_scale,
-                           const float *post_shift, int act, int64_t out_pixels, float *y,
-                           int32_t *status, cudaStream_t s, int k_logical,
-                           const float *x = nullptr, Gather32 g = Gather32{}) {
+                           const float *post_shift, const float *residual, int act,
+                           int64_t out_pixels, float *y, int32_t *status, cudaStream_t s,
+                           int k_logical, const float *x = nullptr, Gather32 g = Gather32{}) {
   const int64_t target = 2 * 148;
   auto go = [&](auto kernel, int64_t rows_per_cta, unsigned ny) {
-    launch_pdl(kernel, dim3(static_cast<unsigned>(m_pad / rows_per_cta), ny), 256, 0, s, A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift, act,
-        out_pixels, y, status, x, g, k_logical);
+    launch_pdl(kernel, dim3(static_cast<unsigned>(m_pad / rows_per_cta), ny), 256, 0, s, A, exA, m_pad, B, exB, n_pad, k_pad, T, M, N, bias, post_scale, post_shift,
+        residual, act, out_pixels, y, status, x, g, k_logical);
   };
   if (N <= 8) {
     go(signsplit_simt_kernel<kAB, 2, 1, kFuse>, 128, 1);
@@ -1947,16 +1950,17 @@ static int contract_mode(const cim22_cuda_layer *layer, int64_t m, int64_t out_p
   return cuda_ok(cudaGetLastError(), "mode contraction launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
 }
 
-int cim22_cuda_layer_contract_bf16_ex(const cim22_cuda_layer *layer, int64_t m,
-                                      int64_t out_pixels, const float *bias,
-                                      const float *post_scale, const float *post_shift,
-                                      int32_t activation, int32_t branches, float *y,
-                                      const void *workspace, size_t workspace_bytes,
-                                      int32_t *status, void *stream) {
+int cim22_cuda_layer_contract_bf16_res(const cim22_cuda_layer *layer, int64_t m,
+                                       int64_t out_pixels, const float *bias,
+                                       const float *post_scale, const float *post_shift,
+                                       const float *residual, int32_t activation,
+                                       int32_t branches, float *y, const void *workspace,
+                                       size_t workspace_bytes, int32_t *status, void *stream) {
   if (!layer || !layer->bf16 || !y || !status || m <= 0 ||
       (branches != 2 && branches != 4) || activation < 0 || activation > 2 ||
       !workspace || out_pixels < 0 || (out_pixels > 0 && m % out_pixels != 0) ||
       (post_scale == nullptr) != (post_shift == nullptr) ||
+      (residual != nullptr && layer->mode != CIM22_BF16_SIGN_SPLIT) ||
       workspace_bytes < cim22_cuda_layer_workspace_bf16(layer, m, branches)) {
     set_last_error("invalid arguments to cim22_cuda_layer_contract_bf16");
     return CIM22_STATUS_BAD_ARGUMENT;
@@ -1974,17 +1978,30 @@ int cim22_cuda_layer_contract_bf16_ex(const cim22_cuda_layer *layer, int64_t m,
   if (tc::signsplit_available() &&
       tc::launch_signsplit(A, ex, m_pad, layer->weights, layer->exponents,
                            layer->n_pad, layer->k_pad, T, m, layer->n, bias, post_scale,
-                           post_shift, activation, ab, out_pixels, y, status, s))
+                           post_shift, residual, activation, ab, out_pixels, y, status, s))
     return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
   if (ab == 1)
     launch_signsplit_simt<1>(A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
                              layer->k_pad, T, m, layer->n, bias, post_scale, post_shift,
-                             activation, out_pixels, y, status, s, static_cast<int>(layer->k));
+                             residual, activation, out_pixels, y, status, s,
+                             static_cast<int>(layer->k));
   else
     launch_signsplit_simt<2>(A, ex, m_pad, layer->weights, layer->exponents, layer->n_pad,
                              layer->k_pad, T, m, layer->n, bias, post_scale, post_shift,
-                             activation, out_pixels, y, status, s, static_cast<int>(layer->k));
+                             residual, activation, out_pixels, y, status, s,
+                             static_cast<int>(layer->k));
   return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+}
+
+int cim22_cuda_layer_contract_bf16_ex(const cim22_cuda_layer *layer, int64_t m,
+                                      int64_t out_pixels, const float *bias,
+                                      const float *post_scale, const float *post_shift,
+                                      int32_t activation, int32_t branches, float *y,
+                                      const void *workspace, size_t workspace_bytes,
+                                      int32_t *status, void *stream) {
+  return cim22_cuda_layer_contract_bf16_res(layer, m, out_pixels, bias, post_scale, post_shift,
+                                            nullptr, activation, branches, y, workspace,
+                                            workspace_bytes, status, stream);
 }
 
 int cim22_cuda_layer_contract_bf16(const cim22_cuda_layer *layer, int64_t m,
@@ -2055,9 +2072,9 @@ int cim22_cuda_layer_forward_bf16_ex(const cim22_cuda_layer *layer, const float 
       constexpr int kAB = decltype(ab_tag)::value, kMode = decltype(mode_tag)::value;
       launch_signsplit_simt<kAB, kMode>(nullptr, nullptr, m_pad, layer->weights,
                                         layer->exponents, layer->n_pad, layer->k_pad, T, m,
-                                        layer->n, bias, post_scale, post_shift, activation,
-                                        out_pixels, y, status, s, static_cast<int>(layer->k), x,
-                                        dg);
+                                        layer->n, bias, post_scale, post_shift, nullptr,
+                                        activation, out_pixels, y, status, s,
+                                        static_cast<int>(layer->k), x, dg);
     };
     using R = std::integral_constant<int, kPrepRows>;
     using C = std::integral_constant<int, kPrepConv>;

@@ -397,6 +397,39 @@ def test_narrow_fused_layers_bit_exact(layout, n, c, h, f, kk, stride, pad, bran
     np.testing.assert_array_equal(bits(got), bits(expected))
 
 
+@pytest.mark.parametrize("f,branches", [(6, 4), (40, 2), (96, 4)])
+def test_contract_residual_epilogue_bit_exact(f, branches):
+    """contract_bf16 with a residual: y = relu(conv + residual), bit-exact
+    against the oracle conv followed by the f32 glue (CUDA-core contraction
+    for 6 lanes, tcgen05 above). The batch norm before the add is covered by
+    the fused-versus-glue ResNet-18 program test."""
+    from cim22_b200 import abi
+    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace, conv_gather
+
+    rng = np.random.default_rng(f + branches)
+    n, c, h = 3, 8, 12
+    x = rng.standard_normal((n, c, h, h)).astype(np.float32)
+    if branches == 2:
+        x = np.maximum(x, 0)
+    w = (rng.standard_normal((f, c, 3, 3)) * 0.2).astype(np.float32)
+    res = rng.standard_normal((n, f, h, h)).astype(np.float32)
+    bn = oracle.conv2d_bf16(x, w, None, 1, 1, branches=4, threads=8)
+    expected = (bn + res).astype(np.float32)
+    expected = np.where(expected > 0, expected, np.float32(0))
+    layer = CimLayer(w.reshape(f, -1))
+    g = conv_gather(abi.GATHER_CONV_NCHW, n, c, h, h, 3, 3, 1, 1)
+    m = n * h * h
+    ws, status = Workspace(torch.device(DEV)), StatusWord(torch.device(DEV))
+    out = torch.empty(m, f, device=DEV)
+    layer.prepare_bf16(torch.from_numpy(x).to(DEV), m, gather=g, branches=branches,
+                       workspace=ws, status=status)
+    layer.contract_bf16(out, m, activation="relu", branches=branches, out_pixels=h * h,
+                        residual=torch.from_numpy(res).to(DEV), workspace=ws, status=status)
+    status.raise_if_set()
+    got = out.cpu().numpy().reshape(n, f, h, h)
+    np.testing.assert_array_equal(bits(got), bits(expected))
+
+
 @pytest.mark.parametrize("act", [None, "relu"])
 def test_direct_conv_dead_negative_branch(act):
     """A 4-branch one-tile conv over binary event frames, with negative pixels

@@ -82,6 +82,24 @@ def _check_layers(prog):
 
 
 @pytest.mark.parametrize("layout", ["nchw", "nhwc"])
+def test_residual_adds_fold_into_conv_epilogues(layout):
+    """Conv -> BatchNorm -> add -> ReLU of every residual block folds the add
+    into the contraction epilogue of the operand computed last (conv2 of an
+    identity block, the shortcut conv of a projection block); the outputs are
+    bit-identical to the unfused glue."""
+    from cim22_b200 import program, workloads
+
+    model, x = workloads.build("resnet18", 2)
+    fused = program.from_module(model, x, layout=layout)
+    assert not [s.name for s in fused.steps if s.name.startswith("add")]
+    assert sum(1 for s in fused.steps if s.cim and s.meta.get("residual") is not None) == 8
+    plain = program.from_module(model, x, fuse=False, layout=layout)
+    (a,) = run_program(fused, x)
+    (b,) = run_program(plain, x)
+    np.testing.assert_array_equal(bits(a), bits(b))
+
+
+@pytest.mark.parametrize("layout", ["nchw", "nhwc"])
 @pytest.mark.parametrize("name,batch,layers", [("resnet18", 1, 21), ("bf16_4x4096", 2, 4),
                                                ("event_cnn", 1, 5)])
 def test_every_cim_layer_bit_exact_on_recorded_inputs(name, batch, layers, layout):
