@@ -638,6 +638,10 @@ class Program:
         if target not in _ADD or len(args) != 2 or kwargs.get("alpha", 1) != 1:
             return None
         other = args[1] if args[0] is node else args[0] if args[1] is node else None
+        # An identity shortcut (nn.Identity, detach, contiguous) not lowered yet
+        # stands for its input.
+        while isinstance(other, fx.Node) and other not in env and self._is_identity(other):
+            other = other.args[0]
         if not isinstance(other, fx.Node) or other is node or other not in env:
             return None
         v = env[other]
@@ -645,6 +649,16 @@ class Program:
                 tuple(v.shape) != tuple(shape) or v.layout != self.layout:
             return None
         return user, v
+
+    def _is_identity(self, node) -> bool:
+        """Whether node passes its first argument through unchanged."""
+        if not node.args or not isinstance(node.args[0], fx.Node):
+            return False
+        if node.op == "call_module":
+            return isinstance(self._modules.get(str(node.target)), torch.nn.Identity)
+        if node.op == "call_method":
+            return node.target in ("contiguous", "detach")
+        return node.op == "call_function" and node.target in _IDENTITY
 
     def _bn_affine(self, args, kwargs, env):
         """Device (scale, shift) of an inference batch norm: y = x * scale + shift."""

@@ -418,6 +418,37 @@ __device__ __forceinline__ void restore_add(float (&acc)[kLT], const uint32_t (&
   }
 }
 
+// Address of the residual addend of one output row's first lane (laid out
+// like y: rows, or NCHW planes) and the stride between lanes.
+__device__ __forceinline__ const float *residual_row(const float *residual, int row, int lane0,
+                                                     int N, int out_pixels, FastDiv div_pix,
+                                                     int64_t &lane_stride) {
+  int64_t base = static_cast<int64_t>(row) * N + lane0;
+  lane_stride = 1;
+  if (out_pixels > 0) {
+    const int image = fdiv(row, div_pix);
+    base = (static_cast<int64_t>(image) * N + lane0) * out_pixels + (row - image * out_pixels);
+    lane_stride = out_pixels;
+  }
+  return residual + base;
+}
+
+// Pull one output row's residual addends into L2 when its output tile
+// starts, so that the epilogue's loads of them do not wait on HBM.
+template <int LT>
+__device__ __forceinline__ void prefetch_residual(const float *residual, int row, int lane0,
+                                                  int M, int N, int out_pixels,
+                                                  FastDiv div_pix) {
+  if (residual == nullptr || row >= M)
+    return;
+  int64_t stride;
+  const float *p = residual_row(residual, row, lane0, N, out_pixels, div_pix, stride);
+#pragma unroll
+  for (int j = 0; j < LT; ++j)
+    if (lane0 + j < N)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p + j * stride));
+}
+
 // Final merge of one output row's LT lanes: BF16 rounding of each branch sum
 // when there is more than one K tile, ((pp - pn) - np) + nn, bias, the
 // optional per-lane fma, the optional residual add, the activation, then the
@@ -479,18 +510,14 @@ __device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, in
         o[j] = __fmaf_rn(o[j], __ldg(post_scale + lane0 + j), __ldg(post_shift + lane0 + j));
   }
   if (residual != nullptr) {
-    // A residual add fused after the batch norm: the same element of a
-    // tensor laid out like y, one f32 add as the glue computes it.
-    int64_t base = static_cast<int64_t>(row) * N + lane0, lane_stride = 1;
-    if (out_pixels > 0) {
-      const int image = fdiv(row, div_pix);
-      base = (static_cast<int64_t>(image) * N + lane0) * out_pixels + (row - image * out_pixels);
-      lane_stride = out_pixels;
-    }
+    // A residual add fused after the batch norm (prefetched into L2 when the
+    // output tile started): one f32 add as the glue computes it.
+    int64_t stride;
+    const float *p = residual_row(residual, row, lane0, N, out_pixels, div_pix, stride);
 #pragma unroll
     for (int j = 0; j < LT; ++j)
       if (lane0 + j < N)
-        o[j] = __fadd_rn(o[j], __ldg(residual + base + j * lane_stride));
+        o[j] = __fadd_rn(o[j], __ldg(p + j * stride));
   }
   if (act == CIM22_ACT_RELU) {
 #pragma unroll
@@ -675,6 +702,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
       const int mb = fdiv(ot, div_nb);
       const int m0 = mb * kSBM, n0 = (ot - mb * num_nb) * L;
       const int lane0 = n0 + sub * LT;
+      prefetch_residual<LT>(residual, m0 + row_local, lane0, M, N, out_pixels, div_pix);
       // Written by the first crossbar tile (restore with kInit).
       float acc[kAB][2][LT];
       for (int t = 0; t < T; ++t, ++gi) {
