@@ -385,7 +385,10 @@ __device__ __forceinline__ float act_tc(float v, int act) {
 // p holds the dots as read from TMEM.
 // kInit marks the first crossbar tile of an output tile: the sums start at
 // +0, and q * s (exact, nonnegative) is what fma(q, s, +0) gives.
-template <int kLT, bool kInit>
+// kAddBias writes the bias as an integer add rather than an OR (equal for
+// dots below 2^23), which lets the compiler balance the ALU and FMA pipes
+// differently: measured faster for 2-branch layers, slower for 4-branch ones.
+template <int kLT, bool kInit, bool kAddBias>
 __device__ __forceinline__ void restore_add(float (&acc)[kLT], const uint32_t (&p)[kLT],
                                             bool fast, float sx, float nsx,
                                             const float *__restrict__ sw,
@@ -400,7 +403,9 @@ __device__ __forceinline__ void restore_add(float (&acc)[kLT], const uint32_t (&
       for (int j = 0; j < 4; j += 2) {
         // Two dots per packed f32x2 operation (each half rounds as fmaf).
         float v0, v1;
-        fma2(__uint_as_float(p[j4 + j] | kDotBias), __uint_as_float(p[j4 + j + 1] | kDotBias),
+        const uint32_t b0 = kAddBias ? p[j4 + j] + kDotBias : p[j4 + j] | kDotBias;
+        const uint32_t b1 = kAddBias ? p[j4 + j + 1] + kDotBias : p[j4 + j + 1] | kDotBias;
+        fma2(__uint_as_float(b0), __uint_as_float(b1),
              sx, sx, nsx, nsx, v0, v1);
         const float q0 = __uint_as_float(__float_as_uint(v0) & 0xffff0000u);
         const float q1 = __uint_as_float(__float_as_uint(v1) & 0xffff0000u);
@@ -751,14 +756,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
           tmem_wait(p0);
           tmem_wait(p1);
           if (t == 0) {
-            restore_add<LT, true>(acc[a][0], p0, fast[a], sx[a], nsx[a], &e.w[0][sub * LT],
+            restore_add<LT, true, kAB == 1>(acc[a][0], p0, fast[a], sx[a], nsx[a], &e.w[0][sub * LT],
                                   exB, ew0, ex[a], status);
-            restore_add<LT, true>(acc[a][1], p1, fast[a], sx[a], nsx[a], &e.w[1][sub * LT],
+            restore_add<LT, true, kAB == 1>(acc[a][1], p1, fast[a], sx[a], nsx[a], &e.w[1][sub * LT],
                                   exB, ew1, ex[a], status);
           } else {
-            restore_add<LT, false>(acc[a][0], p0, fast[a], sx[a], nsx[a], &e.w[0][sub * LT],
+            restore_add<LT, false, kAB == 1>(acc[a][0], p0, fast[a], sx[a], nsx[a], &e.w[0][sub * LT],
                                    exB, ew0, ex[a], status);
-            restore_add<LT, false>(acc[a][1], p1, fast[a], sx[a], nsx[a], &e.w[1][sub * LT],
+            restore_add<LT, false, kAB == 1>(acc[a][1], p1, fast[a], sx[a], nsx[a], &e.w[1][sub * LT],
                                    exB, ew1, ex[a], status);
           }
         }

@@ -304,29 +304,38 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
     const int clo = min(max(-iw0, 0), g.KW), chi = max(min(g.W - iw0, g.KW), clo);
     inb = (sRows[rhi] & ~sRows[rlo]) & (sCols[chi] & ~sCols[clo]);
   }
-  // Pass 1: gather, round to signed BF16 pairs, track the raw maximum.
+  // Pass 1: gather, round to signed BF16 pairs, track the raw maximum. The
+  // loads of the next 16 elements are issued before the current 16 are
+  // converted, so that two chunks of loads are in flight.
   uint32_t signed_pairs[32];
   uint32_t raw_max = 0;
-#pragma unroll
-  for (int chunk = 0; chunk < kTileK; chunk += 16) {
-    float v[16];
+  auto load_chunk = [&](int chunk, float (&v)[16]) {
     if (kbeg + chunk >= g.K) {
       // K padding: zeros, no loads.
 #pragma unroll
       for (int e = 0; e < 16; ++e)
         v[e] = 0.0f;
-    } else {
-#pragma unroll
-      for (int e4 = 0; e4 < 16; e4 += 4) {
-        const int4 rel = *reinterpret_cast<const int4 *>(&sRel[chunk + e4]);
-        const int r4[4] = {rel.x, rel.y, rel.z, rel.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          v[e4 + e] = (inb >> (chunk + e4 + e)) & 1ull
-                          ? window_load<kMode, kPool>(img, g, org + r4[e])
-                          : 0.0f;
-      }
+      return;
     }
+#pragma unroll
+    for (int e4 = 0; e4 < 16; e4 += 4) {
+      const int4 rel = *reinterpret_cast<const int4 *>(&sRel[chunk + e4]);
+      const int r4[4] = {rel.x, rel.y, rel.z, rel.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        v[e4 + e] = (inb >> (chunk + e4 + e)) & 1ull
+                        ? window_load<kMode, kPool>(img, g, org + r4[e])
+                        : 0.0f;
+    }
+  };
+  float vbuf[2][16];
+  load_chunk(0, vbuf[0]);
+#pragma unroll
+  for (int c = 0; c < kTileK / 16; ++c) {
+    if (c + 1 < kTileK / 16)
+      load_chunk((c + 1) * 16, vbuf[(c + 1) & 1]);
+    const float(&v)[16] = vbuf[c & 1];
+    const int chunk = c * 16;
 #pragma unroll
     for (int e = 0; e < 16; e += 2) {
       const int q = (chunk + e) / 2;
@@ -882,8 +891,8 @@ __device__ __forceinline__ void direct_fast_lanes(
       for (int a = 0; a < kBr; ++a) {
         // The two weight signs of one column and branch as one f32x2 pair.
         float v0, v1;
-        fma2(__uint_as_float(static_cast<uint32_t>(p[0][c][a]) | 0x4b000000u),
-             __uint_as_float(static_cast<uint32_t>(p[1][c][a]) | 0x4b000000u), sx[c][a],
+        fma2(__uint_as_float(static_cast<uint32_t>(p[0][c][a]) + 0x4b000000u),
+             __uint_as_float(static_cast<uint32_t>(p[1][c][a]) + 0x4b000000u), sx[c][a],
              sx[c][a], nsx[c][a], nsx[c][a], v0, v1);
         fma2(__uint_as_float(__float_as_uint(v0) & 0xffff0000u),
              __uint_as_float(__float_as_uint(v1) & 0xffff0000u), sw0, sw1, 0.0f, 0.0f,
