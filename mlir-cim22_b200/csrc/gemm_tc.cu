@@ -556,7 +556,9 @@ __device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, in
   }
 }
 
-template <int kAB>
+// kRes: the layer has a residual addend (a separate instance, so that layers
+// without one keep the registers the residual path would take).
+template <int kAB, bool kRes>
 __global__ void __launch_bounds__(kSThreads, 1)
     signsplit_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const int32_t *__restrict__ exA,
@@ -564,9 +566,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
                         int N, FastDiv div_nb, const float *__restrict__ bias,
                         const float *__restrict__ post_scale,
                         const float *__restrict__ post_shift,
-                        const float *__restrict__ residual, int act, int vec,
+                        const float *__restrict__ residual_arg, int act, int vec,
                         int out_pixels, FastDiv div_pix, float *__restrict__ y,
                         int32_t *status) {
+  const float *residual = kRes ? residual_arg : nullptr;
   using S = SSShape<kAB>;
   constexpr int L = S::L, LT = S::LT, SN = S::N;
   extern __shared__ uint8_t smem_raw[];
@@ -1099,8 +1102,12 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
         make_fastdiv(static_cast<uint32_t>(out_pixels > 0 ? out_pixels : 1)), y, status);
     return true;
   };
-  if (!(act_branches == 2 ? launch(signsplit_tc_kernel<2>, smem_ss<2>())
-                          : launch(signsplit_tc_kernel<1>, smem_ss<1>())))
+  const bool res = residual != nullptr;
+  if (!(act_branches == 2
+            ? (res ? launch(signsplit_tc_kernel<2, true>, smem_ss<2>())
+                   : launch(signsplit_tc_kernel<2, false>, smem_ss<2>()))
+            : (res ? launch(signsplit_tc_kernel<1, true>, smem_ss<1>())
+                   : launch(signsplit_tc_kernel<1, false>, smem_ss<1>()))))
     return false;
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
   return true;
