@@ -247,6 +247,77 @@ __device__ __forceinline__ uint32_t branch_pair(uint32_t pair, int a) {
   return (a == 0 ? pair & ~neg : pair & neg) & 0x7fff7fffu;
 }
 
+// The rest of one (column m, K tile t) group once its 64 signed BF16 pairs
+// and raw maximum are known: branch maxima, the non-finite and
+// negative-input flags, ExpPrealign, the 64 aligned bytes per branch (four
+// 16-byte stores) and the group exponent.
+template <int kActBranches>
+__device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
+                                             uint32_t raw_max, int32_t *status,
+                                             int8_t *__restrict__ A, int32_t *__restrict__ ex,
+                                             int m_pad, int k_pad, int T, int t, int m,
+                                             int kbeg) {
+  uint32_t mx[2] = {0, 0};
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a) {
+    uint32_t m2 = 0;
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      m2 = __vmaxu2(m2, branch_pair<kActBranches>(signed_pairs[e], a));
+    mx[a] = max(m2 & 0xffffu, m2 >> 16);
+  }
+  // Non-finite groups: BF16 exponent 0xff in the 2-branch maximum, |x| of
+  // the raw inputs otherwise (the max with 0 drops NaN).
+  const bool nonfinite = kActBranches == 2 ? raw_max >= 0x7f7f8000u : mx[0] >= 0x7f80u;
+  if (nonfinite)
+    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
+  else if (kActBranches == 1 && raw_max > 0x80000000u)
+    atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
+  // Pass 2: align and store.
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a) {
+    const bool zero = mx[a] == 0 || nonfinite;
+    const int emax = zero ? kZeroGroup : effective_exponent(static_cast<uint16_t>(mx[a]));
+    uint32_t out[16];
+    if (zero) {
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        out[q] = 0;
+    } else if ((mx[a] >> 7) >= 8) {
+      const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax) << 23);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        uint32_t r[4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t pk = branch_pair<kActBranches>(signed_pairs[2 * q + h], a);
+          r[2 * h] = __float_as_uint(__fmaf_rz(__uint_as_float(pk << 16), scale, 8388608.0f));
+          r[2 * h + 1] =
+              __float_as_uint(__fmaf_rz(__uint_as_float(pk & 0xffff0000u), scale, 8388608.0f));
+        }
+        out[q] = pack_low_bytes(r[0], r[1], r[2], r[3]);
+      }
+    } else {
+      const int shift = 127 - emax;
+      for (int q = 0; q < 16; ++q) {
+        uint32_t word = 0;
+        for (int h = 0; h < 4; ++h)
+          word |= slow_align((branch_pair<kActBranches>(signed_pairs[2 * q + h / 2], a) >>
+                              (16 * (h & 1))) & 0xffffu,
+                             shift)
+                  << (8 * h);
+        out[q] = word;
+      }
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad +
+                                           kbeg);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      dst[q] = make_uint4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+    ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax;
+  }
+}
+
 template <int kActBranches, bool kPool>
 __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
     prepare_nchw_kernel(const float *__restrict__ x, Gather32 g, FastDiv div_chunks, int T,
@@ -348,65 +419,8 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
         raw_max = max(raw_max, max(__float_as_uint(v[e]), __float_as_uint(v[e + 1])));
     }
   }
-  uint32_t mx[2] = {0, 0};
-#pragma unroll
-  for (int a = 0; a < kActBranches; ++a) {
-    uint32_t m2 = 0;
-#pragma unroll
-    for (int e = 0; e < 32; ++e)
-      m2 = __vmaxu2(m2, branch_pair<kActBranches>(signed_pairs[e], a));
-    mx[a] = max(m2 & 0xffffu, m2 >> 16);
-  }
-  // Non-finite groups: BF16 exponent 0xff in the 2-branch maximum, |x| of
-  // the raw inputs otherwise (the max with 0 drops NaN).
-  const bool nonfinite = kActBranches == 2 ? raw_max >= 0x7f7f8000u : mx[0] >= 0x7f80u;
-  if (nonfinite)
-    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-  else if (kActBranches == 1 && raw_max > 0x80000000u)
-    atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
-  // Pass 2: align and store.
-#pragma unroll
-  for (int a = 0; a < kActBranches; ++a) {
-    const bool zero = mx[a] == 0 || nonfinite;
-    const int emax = zero ? kZeroGroup : effective_exponent(static_cast<uint16_t>(mx[a]));
-    uint32_t out[16];
-    if (zero) {
-#pragma unroll
-      for (int q = 0; q < 16; ++q)
-        out[q] = 0;
-    } else if ((mx[a] >> 7) >= 8) {
-      const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax) << 23);
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        uint32_t r[4];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t pk = branch_pair<kActBranches>(signed_pairs[2 * q + h], a);
-          r[2 * h] = __float_as_uint(__fmaf_rz(__uint_as_float(pk << 16), scale, 8388608.0f));
-          r[2 * h + 1] =
-              __float_as_uint(__fmaf_rz(__uint_as_float(pk & 0xffff0000u), scale, 8388608.0f));
-        }
-        out[q] = pack_low_bytes(r[0], r[1], r[2], r[3]);
-      }
-    } else {
-      const int shift = 127 - emax;
-      for (int q = 0; q < 16; ++q) {
-        uint32_t word = 0;
-        for (int h = 0; h < 4; ++h)
-          word |= slow_align((branch_pair<kActBranches>(signed_pairs[2 * q + h / 2], a) >>
-                              (16 * (h & 1))) & 0xffffu,
-                             shift)
-                  << (8 * h);
-        out[q] = word;
-      }
-    }
-    uint4 *dst = reinterpret_cast<uint4 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad +
-                                           kbeg);
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      dst[q] = make_uint4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
-    ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax;
-  }
+  finish_group<kActBranches>(signed_pairs, raw_max, status, A, ex, m_pad, k_pad, T, t, m,
+                             kbeg);
   }
 }
 
