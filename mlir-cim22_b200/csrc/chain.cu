@@ -56,6 +56,7 @@ struct ChainLayerDev {
   int row_stride;     // bytes per prepared column in shared memory
   int lanes_per_item; // lanes one contraction thread carries (1 .. kMaxLaneBlock)
   int many_groups;    // prepare one thread per group through the tap table
+  int direct;         // one thread per column (chain_direct)
 };
 
 struct ChainParams {
@@ -364,6 +365,73 @@ __device__ void chain_contract(const ChainLayerDev &L, int col0, int ch, const i
   }
 }
 
+// One-tile layers of few lanes (K <= kDirectMaxK, at most kDirectMaxLanes
+// lanes: the first convolution of LeNet). One thread per column gathers its
+// group from the shared-memory input, splits, rounds and prealigns it in
+// registers with the routines of the prepare passes (split8,
+// group_exponents, align8), and dots it with every lane's weight rows; the
+// restore and the merge are tile_add and finish. The result is the one the
+// staged passes give (elements past kDirectMaxK are K padding, zero in both
+// operands), without the prepared columns in shared memory and the barriers
+// between the passes.
+constexpr int kDirectMaxK = 32;
+constexpr int kDirectMaxLanes = 16;
+
+template <int kActBranches>
+__device__ void chain_direct(const float *in, const ChainLayerDev &L, float *out,
+                             int32_t *status) {
+  constexpr int kChunks = kDirectMaxK / 8;
+  const int cols = L.OH * L.OW;
+  for (int col = static_cast<int>(threadIdx.x); col < cols; col += kChainThreads) {
+    uint32_t packed[kChunks][2][4];
+    uint32_t mx[2] = {0, 0};
+    uint32_t flags = 0;
+#pragma unroll
+    for (int c8 = 0; c8 < kChunks; ++c8) {
+      float v[8];
+      chain_gather8(in, L, col, c8 * 8, v);
+      split8<kActBranches>(v, packed[c8], mx, flags);
+    }
+    int emax[2];
+    group_exponents<kActBranches>(mx, flags, true, status, emax);
+    uint32_t aw[kActBranches][2 * kChunks];
+    float sx[kActBranches];
+#pragma unroll
+    for (int a = 0; a < kActBranches; ++a) {
+#pragma unroll
+      for (int c8 = 0; c8 < kChunks; ++c8) {
+        const uint2 w2 = align8(packed[c8][a], mx[a], emax[a]);
+        aw[a][2 * c8] = w2.x;
+        aw[a][2 * c8 + 1] = w2.y;
+      }
+      sx[a] = emax[a] == kZeroGroup ? 0.0f : exp2i(emax[a] - 133);
+    }
+    for (int lane = 0; lane < L.N; ++lane) {
+      float acc[kActBranches][2];
+#pragma unroll
+      for (int w = 0; w < 2; ++w) {
+        const int4 *row = reinterpret_cast<const int4 *>(
+            L.B + (static_cast<int64_t>(w) * L.n_pad + lane) * L.k_pad);
+        const int4 b0 = __ldg(row), b1 = __ldg(row + 1);
+        const int bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        const int ew = __ldg(L.exB + w * L.n_pad + lane); // Ew[w][tile 0][lane]
+        const float sw = __ldg(L.sw + w * L.n_pad + lane);
+#pragma unroll
+        for (int a = 0; a < kActBranches; ++a) {
+          int p = 0;
+#pragma unroll
+          for (int q = 0; q < 2 * kChunks; ++q)
+            p = __dp4a(static_cast<int>(aw[a][q]), bw[q], p);
+          acc[a][w] = emax[a] != kZeroGroup // a zero group's tile adds +0
+                          ? tile_add(0.0f, p, emax[a], sx[a], ew, sw, status)
+                          : 0.0f;
+        }
+      }
+      out[lane * cols + col] = finish<kActBranches>(acc, L.T, L.bias, lane, L.act);
+    }
+  }
+}
+
 // 2x2 stride-2 max pool of [N][OH][OW] into [N][OH/2][OW/2], NaN propagating
 // in window order as torch.max_pool2d.
 __device__ void chain_pool(const float *src, const ChainLayerDev &L, float *dst) {
@@ -404,7 +472,13 @@ __global__ void __launch_bounds__(kChainThreads, 2)
       const float *in = buf[cur];
       float *out = buf[cur ^ 1];
       const int cols = L.OH * L.OW;
-      if (L.many_groups) {
+      if (L.direct) {
+        if (L.act_br == 2)
+          chain_direct<2>(in, L, out, status);
+        else
+          chain_direct<1>(in, L, out, status);
+        __syncthreads();
+      } else if (L.many_groups) {
         // Tap table: offset of K element k from the window origin, and its
         // kernel row and column.
         for (int k = static_cast<int>(threadIdx.x); k < L.K; k += kChainThreads) {
@@ -416,7 +490,7 @@ __global__ void __launch_bounds__(kChainThreads, 2)
         }
         __syncthreads();
       }
-      for (int col0 = 0; col0 < cols; col0 += L.chunk) {
+      for (int col0 = 0; col0 < cols && !L.direct; col0 += L.chunk) {
         const int ch = min(L.chunk, cols - col0);
         if (L.many_groups) {
           if (L.act_br == 2)
@@ -537,6 +611,9 @@ int cim22_cuda_chain_forward(const cim22_chain_layer *layers, int32_t n_layers, 
       }
     // One thread per prepare group once there are enough groups for the block.
     d.many_groups = static_cast<int64_t>(d.chunk) * d.T >= kChainThreads / 2 ? 1 : 0;
+    d.direct = d.T == 1 && d.K <= kDirectMaxK && d.N <= kDirectMaxLanes ? 1 : 0;
+    if (d.direct)
+      d.many_groups = 0;
     if (s.pool && (d.OH < 2 || d.OW < 2)) {
       set_last_error("chain pool needs an output of at least 2x2");
       return CIM22_STATUS_BAD_ARGUMENT;
