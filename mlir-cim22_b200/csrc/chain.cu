@@ -57,6 +57,7 @@ struct ChainLayerDev {
   int lanes_per_item; // lanes one contraction thread carries (1 .. kMaxLaneBlock)
   int many_groups;    // prepare one thread per group through the tap table
   int direct;         // one thread per column (chain_direct)
+  int split;          // one column, items per (lane, weight sign, tile): chain_contract_split
 };
 
 struct ChainParams {
@@ -300,6 +301,58 @@ __device__ void chain_contract_lane(const ChainLayerDev &L, int col0, int ch, co
   }
 }
 
+// Layers of one column (Linear) with fewer lanes than threads and several K
+// tiles: one item per (lane, weight sign, K tile) restores that tile's value
+// into shared memory (vals, after the layer's outputs in the output buffer),
+// then one thread per lane adds its tiles in tile order and finishes. Inside
+// the fast window tile_add's fma adds an exactly representable product, so
+// acc + (that product) rounds as the fma does; a zero group's tile is +0,
+// which leaves the (never -0) sum as it is; the slow path adds the same BF16
+// tile value. The result is the sequential chain_contract_lane's.
+template <int kActBranches>
+__device__ void chain_contract_split(const ChainLayerDev &L, const int8_t *As, const int *sEx,
+                                     float *out, int32_t *status) {
+  float *vals = out + ((L.N + 3) & ~3); // [branch][sign][lane][tile]
+  const int items = 2 * L.N * L.T;
+  for (int it = static_cast<int>(threadIdx.x); it < items; it += kChainThreads) {
+    const int t = it % L.T, lane = (it / L.T) % L.N, w = it / (L.T * L.N);
+    int4 bw[4];
+    load_weights(L, w, lane, t, bw);
+    const int ew = __ldg(L.exB + (w * L.T + t) * L.n_pad + lane);
+    const float sw = __ldg(L.sw + (w * L.T + t) * L.n_pad + lane);
+#pragma unroll
+    for (int a = 0; a < kActBranches; ++a) {
+      const int ex = sEx[(a * L.T + t) * L.chunk];
+      float v = 0.0f; // a zero group's tile adds +0
+      if (ex != kZeroGroup) {
+        int4 av[4];
+        const int4 *row = reinterpret_cast<const int4 *>(As + a * L.chunk * L.row_stride +
+                                                         t * kTileK);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          av[kk] = row[kk];
+        v = tile_add(0.0f, dot64(av, bw), ex, exp2i(ex - 133), ew, sw, status);
+      }
+      vals[((a * 2 + w) * L.N + lane) * L.T + t] = v;
+    }
+  }
+  __syncthreads();
+  for (int lane = static_cast<int>(threadIdx.x); lane < L.N; lane += kChainThreads) {
+    float acc[kActBranches][2];
+#pragma unroll
+    for (int a = 0; a < kActBranches; ++a)
+#pragma unroll
+      for (int w = 0; w < 2; ++w) {
+        const float *v = vals + ((a * 2 + w) * L.N + lane) * L.T;
+        float sum = 0.0f;
+        for (int t = 0; t < L.T; ++t)
+          sum = __fadd_rn(sum, v[t]);
+        acc[a][w] = sum;
+      }
+    out[lane] = finish<kActBranches>(acc, L.T, L.bias, lane, L.act);
+  }
+}
+
 // One thread per (column, block of up to kMaxLaneBlock lanes): per K tile the
 // column's prepared rows are read once, each lane's weight rows (the same for
 // the whole warp: a broadcast) are dotted with them, and each restored tile is
@@ -503,7 +556,12 @@ __global__ void __launch_bounds__(kChainThreads, 2)
           chain_prepare8<1>(in, L, col0, ch, As, sEx, status);
         }
         __syncthreads();
-        if (L.lanes_per_item == 1) {
+        if (L.split) {
+          if (L.act_br == 2)
+            chain_contract_split<2>(L, As, sEx, out, status);
+          else
+            chain_contract_split<1>(L, As, sEx, out, status);
+        } else if (L.lanes_per_item == 1) {
           if (L.act_br == 2)
             chain_contract_lane<2>(L, col0, ch, As, sEx, out, status);
           else
@@ -614,6 +672,12 @@ int cim22_cuda_chain_forward(const cim22_chain_layer *layers, int32_t n_layers, 
     d.direct = d.T == 1 && d.K <= kDirectMaxK && d.N <= kDirectMaxLanes ? 1 : 0;
     if (d.direct)
       d.many_groups = 0;
+    // One column over fewer lanes than threads and several tiles: per-tile
+    // items, their values after the outputs in the output buffer.
+    d.split = cols == 1 && d.T >= 2 && d.N < kChainThreads && !d.direct ? 1 : 0;
+    if (d.split)
+      buf = std::max<int64_t>(buf, (d.N + 3) / 4 * 4 +
+                                       2 * static_cast<int64_t>(d.N) * d.T * d.act_br);
     if (s.pool && (d.OH < 2 || d.OW < 2)) {
       set_last_error("chain pool needs an output of at least 2x2");
       return CIM22_STATUS_BAD_ARGUMENT;

@@ -81,12 +81,18 @@ def test_mixed_chain_matches_layers_and_oracle():
     assert np.max(np.abs(got - expected)) <= 1e-3 * np.max(np.abs(expected))
 
 
-def test_chain_wide_linear_stack():
+@pytest.mark.parametrize("widths", [(300, 300, 10), (120, 84, 10)])
+def test_chain_wide_linear_stack(widths):
+    """Linear stacks with an all-zero group, a subnormal input and a group
+    exponent above the fast window; layers of fewer lanes than threads (all
+    of the (120, 84, 10) stack) restore per (lane, sign, tile) and sum in tile
+    order."""
     from cim22_b200 import program
 
     torch.manual_seed(1)
-    model = nn.Sequential(nn.Flatten(), nn.Linear(1000, 300), nn.ReLU(), nn.Linear(300, 300),
-                          nn.ReLU(), nn.Linear(300, 10)).eval()
+    a, b, c = widths
+    model = nn.Sequential(nn.Flatten(), nn.Linear(1000, a), nn.ReLU(), nn.Linear(a, b),
+                          nn.ReLU(), nn.Linear(b, c)).eval()
     x = torch.randn(33, 1000)
     x[0, :64] = 0.0  # an all-zero group
     x[1, 5] = 1e-40  # subnormal input
