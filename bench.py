@@ -1,22 +1,35 @@
-"""Benchmark: CIM-simulation inferences/s of the LeNet workload on B200s.
+"""Benchmark: CIM-simulation inferences/s on B200s, headline ResNet-18 at batch 1024.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload lenet]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload resnet18]
     python bench.py --impl reference ...      # the CPU reference arm
 
 One step is one inference pass of the whole CIM-simulated network over one
-batch (LeNet: 256 images of 1x32x32, U[0,1], He-normal weights; every
-Linear/Conv runs as BF16 sign-split crossbar tiles, bit-exact with the
-reference simulator). With N GPUs (torchrun, one process per GPU) each rank
-runs its own batch: the work shards by batch with no collective (weak
+batch (default: CIFAR ResNet-18, 1024 images of 3x32x32 ~ N(0,1), He-normal
+weights; every Conv/Linear runs as BF16 sign-split crossbar tiles, bit-exact
+with the reference simulator, the batch norms, ReLUs, residual adds and the
+average pool as f32 glue). With N GPUs (torchrun, one process per GPU) each
+rank runs its own batch: the work shards by batch with no collective (weak
 scaling); ``value`` is the whole-job rate, timed on the device with CUDA
 events and taken as the maximum over ranks.
 
-Prints one JSON line (rank 0). ``e2e`` is the same metric through the public
-API (the torch.compile backend, runtime="cuda") with the batch in pinned host
-memory and the logits read back every step. ``roofline`` covers the kernel
-with the largest share of device time, timed per launch with CUDA events on
-its stream. ``cpu_baseline`` is the oracle port of the reference's software
-runner (oracle/), run on this host's cores over a bounded sample.
+Prints one JSON line (rank 0):
+  value / ms_per_step   CUDA-graph replays of the whole network, L2 flushed
+                        between steps outside the timed span.
+  e2e                   the same metric through the public API (the
+                        torch.compile backend, runtime="cuda") with the batch in
+                        pinned host memory and the logits + status word read
+                        back every step.
+  roofline              the kernel with the largest share of device time, timed
+                        per launch with CUDA events on its stream.
+  kernels               every kernel of the step with its device time and share.
+  clocks                nvidia-smi samples over a loaded window of >= 1 s (untimed
+                        replays just before the timed loop, then the loop).
+  configs               (N=1) the other four workloads at their own batches:
+                        value, e2e, dominant kernel and its roof fraction.
+  int8_sweep            (N=1) INT8 CIM MVM layers over an M x K=N grid: best TOPS
+                        and the fraction of the int8 tensor peak at 8192^3.
+  cpu_baseline          (N=1) the reference's CPU simulation on this host's
+                        cores over a bounded sample (one core and all cores).
 """
 
 from __future__ import annotations
@@ -24,6 +37,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -37,22 +51,25 @@ sys.path[:0] = [str(REPO / "mlir-cim22_b200"), str(REPO / "oracle")]
 METRIC = "CIM-sim inferences/sec"
 UNIT = "inferences/s"
 L2_FLUSH_BYTES = 256 << 20
+L2_NOTE = "flushed between steps (256 MiB write, outside the timed span)"
 REFERENCE_SECONDS = 90.0
+CLOCK_WINDOW_S = 1.5
+EXTRA_WORKLOADS = ("mlp", "lenet", "bf16_4x4096", "event_cnn")
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=3000)
-    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--workload", default="lenet")
+    p.add_argument("--workload", default="resnet18")
     p.add_argument("--batch", type=int, default=None)
-    p.add_argument("--cpu-sample", type=int, default=2048,
-                   help="images in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the other workloads and the INT8 sweep (N=1 adds them by default)")
     p.add_argument("--int8-sweep", action="store_true",
-                   help="INT8 CIM MVM sweep (M x K=N grid): TOPS vs the int8 tensor peak")
+                   help="only the INT8 CIM MVM sweep (M x K=N grid), one JSON row per point")
     p.add_argument("--sweep-m", default="1,16,128,1024,8192")
     p.add_argument("--sweep-kn", default="256,1024,4096,8192")
     p.add_argument("--parallel", default="batch", choices=["batch", "columns"],
@@ -73,8 +90,30 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
+def bench_config(workload: str, batch: int, world: int) -> dict:
+    """The workload a line measures; identical in both arms."""
+    from cim22_b200 import workloads
+
+    w = workloads.WORKLOADS[workload]
+    return {"workload": f"{workload}: {w.description}", "batch_per_gpu": batch,
+            "global_batch": batch * world, "parallelism": f"batch-sharded x{world}",
+            "l2": L2_NOTE,
+            "arithmetic": "BF16 sign-split: int8 mantissa crossbar dots, BF16 tiles, "
+                          "f32 K sums; f32 glue"}
+
+
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -89,7 +128,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except OSError:
@@ -100,7 +139,7 @@ class ClockSampler:
         for line in self.proc.stdout:
             parts = [s.strip() for s in line.split(",")]
             if len(parts) >= 9:
-                self.rows.append(parts)
+                self.rows.append((time.perf_counter(), parts))
 
     def __exit__(self, *exc):
         if self.proc:
@@ -110,22 +149,24 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
 
-    def summary(self):
-        rows = [r for r in self.rows if r[0].isdigit() and int(r[0]) in self.indices]
+    def summary(self, since: float | None = None):
+        rows = [r for t, r in self.rows
+                if (since is None or t >= since) and r[0].isdigit() and int(r[0]) in self.indices]
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "power_w_max": max(pw) if pw else None}
 
 
 def ncu_traffic(workload: str, batch: int, step: str):
     """DRAM bytes per launch (read + write) of a step's kernel from a committed
-    ncu launch-list summary (profiles/traffic.json), or (None, None)."""
+    ncu summary (profiles/traffic.json), or (None, None)."""
     try:
         table = json.loads((REPO / "profiles" / "traffic.json").read_text())
         entry = table[f"{workload}_b{batch}"]
@@ -134,110 +175,99 @@ def ncu_traffic(workload: str, batch: int, step: str):
         return None, None
 
 
-def cpu_baseline(workload: str, sample: int, threads: int, batch_seed: int = 0):
-    """Oracle port of the reference's software runner on host cores."""
+# ----------------------------------------------------------------- CPU legs
+
+
+def cpu_sample_rate(workload: str, images: int, threads: int, seed: int = 0):
+    """Images per second of the reference's CPU simulation of a workload over
+    a sample of `images` inputs (oracle/: the tile runner driven with 40-Work
+    transactions, plan reuse and weight residency; PyTorch CPU glue)."""
     import oracle
     from cim22_b200 import workloads
 
-    model, x = workloads.build(workload, sample, seed=batch_seed)
-    oracle.cim_forward(model, x[:2].numpy(), threads=threads, via_runner=True)  # warm
+    model, x = workloads.build(workload, images, seed=seed)
+    xs = x.numpy()
+    oracle.cim_forward(model, xs[:1], threads=threads, via_runner="auto",
+                       branches="reference")  # warm
     t0 = time.perf_counter()
-    oracle.cim_forward(model, x.numpy(), threads=threads, via_runner=True)
+    oracle.cim_forward(model, xs, threads=threads, via_runner="auto", branches="reference")
     dt = time.perf_counter() - t0
-    return sample / dt, dt
+    return images / dt, dt
+
+
+def runner_kind() -> tuple[str, str]:
+    import oracle
+
+    if oracle.reference_runner_available():
+        return "reference", ("the reference's own CIMSoftwareRunner + BF16Compensation, "
+                             "compiled unmodified into oracle/_ref")
+    return "port", "the oracle's restated CIMSoftwareRunner"
+
+
+def cpu_baseline(workload: str) -> dict:
+    """One-core and all-core CPU simulation rates over bounded samples."""
+    threads = os.cpu_count() or 1
+    kind, what = runner_kind()
+    # Size the samples from a short probe so each leg runs for about 10 s.
+    probe, _ = cpu_sample_rate(workload, max(1, min(threads, 4)), threads)
+    n_all = max(threads, min(4096, int(10.0 * probe)))
+    rate, dt = cpu_sample_rate(workload, n_all, threads)
+    n_one = max(1, min(1024, int(6.0 * probe / threads)))
+    rate1, dt1 = cpu_sample_rate(workload, n_one, 1)
+    return {"value": rate, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{n_all} {workload} images on {threads} host threads through {what} "
+                      f"(40-Work transactions, plan reuse, weight residency; branch counts "
+                      f"as the reference's lowering) + PyTorch CPU glue, {dt:.1f} s",
+            "single_core": {"value": rate1, "unit": UNIT, "cores": 1,
+                            "sample": f"{n_one} images, {dt1:.1f} s"},
+            "cpu_model": cpu_model()}
 
 
 def reference_arm(args) -> None:
+    """The reference's CPU simulation on this host's cores, in the GPU arm's
+    metric, unit and config; each step is a bounded sample of the workload."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     import oracle
     from cim22_b200 import workloads as wl
 
     threads = os.cpu_count() or 1
-    # Size each step's sample so the whole run takes about REFERENCE_SECONDS.
-    rate, _ = cpu_baseline(args.workload, 2 * threads, threads)
+    kind, what = runner_kind()
+    batch = args.batch or wl.WORKLOADS[args.workload].batch
+    rate, _ = cpu_sample_rate(args.workload, max(1, min(threads, 4)), threads)
     per_step = int(REFERENCE_SECONDS * rate / max(1, args.steps + args.warmup))
-    per_step = max(1, min(args.cpu_sample, 256, per_step))
+    per_step = max(1, min(batch, per_step))
     model, x = wl.build(args.workload, per_step, seed=0)
     xs = x.numpy()
     for _ in range(args.warmup):
-        oracle.cim_forward(model, xs, threads=threads, via_runner=True)
+        oracle.cim_forward(model, xs, threads=threads, via_runner="auto", branches="reference")
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        oracle.cim_forward(model, xs, threads=threads, via_runner=True)
+        oracle.cim_forward(model, xs, threads=threads, via_runner="auto", branches="reference")
         times.append(time.perf_counter() - t0)
     total = sum(times)
     value = per_step * args.steps / total
-    from cim22_b200 import workloads
-
-    w = workloads.WORKLOADS[args.workload]
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000 * total / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {w.description}",
-                   "batch_per_step": per_step, "parallelism": "host threads over columns"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{per_step} images per step through the oracle's "
-                                   "restated CIMSoftwareRunner (40-Work transactions, plan "
-                                   "reuse, weight residency) + PyTorch CPU glue"},
+        "config": bench_config(args.workload, batch, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"{per_step} images per step (of the {batch}-image batch) "
+                                   f"on {threads} host threads through {what} (40-Work "
+                                   "transactions, plan reuse, weight residency) + PyTorch "
+                                   "CPU glue; rate per inference",
+                         "cpu_model": cpu_model()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def int8_sweep(args) -> None:
-    """INT8 CIM MVM layers y = x W^T (int8 x int8 -> int32, exact), timed per
-    launch with CUDA events on the current stream, L2 flushed in between."""
-    import numpy as np
-    import torch
-
-    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace
-    from cim22_b200.native import lib
-
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    _, bf16_peak, peak_kind = peaks()
-    int8_peak = 2 * bf16_peak
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    ws, status = Workspace(dev), StatusWord(dev)
-    stream = torch.cuda.current_stream(dev)
-    rng = np.random.default_rng(1)
-    rows = []
-    for kn in [int(v) for v in args.sweep_kn.split(",")]:
-        w = rng.integers(-127, 128, (kn, kn)).astype(np.int8)
-        layer = CimLayer(w, kind="int8", device=dev)
-        for m in [int(v) for v in args.sweep_m.split(",")]:
-            x = torch.from_numpy(np.random.default_rng(0).integers(-128, 128, (m, kn))
-                                 .astype(np.int8)).to(dev)
-            out = torch.empty(m, kn, dtype=torch.int32, device=dev)
-            tc0 = lib().cim22_cuda_tensor_core_launches()
-            for _ in range(3):
-                layer_launch(layer, x, out, m, ws, status)
-            times = []
-            for _ in range(max(3, min(args.steps, 20))):
-                flush.zero_()
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                layer_launch(layer, x, out, m, ws, status)
-                b.record(stream)
-                b.synchronize()
-                times.append(a.elapsed_time(b))
-            status.raise_if_set()
-            tc = lib().cim22_cuda_tensor_core_launches() - tc0
-            ms = sorted(times)[len(times) // 2]
-            tops = 2.0 * m * kn * kn / (ms / 1e3) / 1e12
-            row = {"m": m, "k": kn, "n": kn, "ms": ms, "tops": tops,
-                   "frac_int8_peak": tops / int8_peak, "tensor_core": tc > 0}
-            rows.append(row)
-            print(json.dumps(row), flush=True)
-    best = max(rows, key=lambda r: r["tops"])
-    print(json.dumps({"metric": "int8 CIM MVM TOPS", "best": best,
-                      "int8_peak_tops": int8_peak,
-                      "peak_note": f"2 x {peak_kind} bf16 cuBLAS ({bf16_peak} TF/s)"}), flush=True)
+# ----------------------------------------------------------------- INT8 sweep
 
 
 def layer_launch(layer, x, out, m, ws, status):
@@ -252,6 +282,247 @@ def layer_launch(layer, x, out, m, ws, status):
         layer._handle, ctypes.c_void_p(x.data_ptr()), m, ctypes.c_void_p(out.data_ptr()),
         ctypes.c_void_p(buf.data_ptr()), buf.numel(), ctypes.c_void_p(status.tensor.data_ptr()),
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "forward_int8")
+
+
+def int8_sweep(ms, kns, iters: int, dev, flush, emit=None) -> dict:
+    """INT8 CIM MVM layers y = x W^T (int8 x int8 -> int32, exact), each point
+    timed per launch with CUDA events on the current stream (median), L2
+    flushed in between."""
+    import numpy as np
+    import torch
+
+    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace
+    from cim22_b200.native import lib
+
+    _, bf16_peak, peak_kind = peaks()
+    int8_peak = 2 * bf16_peak
+    ws, status = Workspace(dev), StatusWord(dev)
+    stream = torch.cuda.current_stream(dev)
+    rng = np.random.default_rng(1)
+    rows = []
+    for kn in kns:
+        w = rng.integers(-127, 128, (kn, kn)).astype(np.int8)
+        layer = CimLayer(w, kind="int8", device=dev)
+        for m in ms:
+            x = torch.from_numpy(np.random.default_rng(0).integers(-128, 128, (m, kn))
+                                 .astype(np.int8)).to(dev)
+            out = torch.empty(m, kn, dtype=torch.int32, device=dev)
+            tc0 = lib().cim22_cuda_tensor_core_launches()
+            for _ in range(3):
+                layer_launch(layer, x, out, m, ws, status)
+            times = []
+            for _ in range(iters):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                layer_launch(layer, x, out, m, ws, status)
+                b.record(stream)
+                b.synchronize()
+                times.append(a.elapsed_time(b))
+            status.raise_if_set()
+            tc = lib().cim22_cuda_tensor_core_launches() - tc0
+            ms_ = sorted(times)[len(times) // 2]
+            tops = 2.0 * m * kn * kn / (ms_ / 1e3) / 1e12
+            row = {"m": m, "k": kn, "n": kn, "ms": round(ms_, 5), "tops": round(tops, 2),
+                   "frac_int8_peak": round(tops / int8_peak, 4), "tensor_core": tc > 0}
+            rows.append(row)
+            if emit:
+                emit(row)
+        del layer
+    best = max(rows, key=lambda r: r["tops"])
+    top = next((r for r in rows if r["m"] == 8192 and r["k"] == 8192), None)
+    return {"grid": {"m": list(ms), "k=n": list(kns)}, "points": rows, "best": best,
+            "frac_at_8192_cubed": top["frac_int8_peak"] if top else None,
+            "int8_peak_tops": int8_peak,
+            "peak_note": f"derived int8 peak = 2 x {peak_kind} bf16 cuBLAS burst ({bf16_peak} "
+                         "TF/s); no int8 GEMM peak is measured on this pool",
+            "method": f"median of {iters} launches per point, L2 flushed between launches"}
+
+
+# ----------------------------------------------------------------- GPU arm
+
+
+def step_names(prog) -> list[str]:
+    names, seen = [], {}
+    for s in prog.steps:
+        seen[s.name] = seen.get(s.name, 0) + 1
+        names.append(s.name if seen[s.name] == 1 else f"{s.name}#{seen[s.name]}")
+    return names
+
+
+def kernel_times(prog, dev, flush, iters: int) -> dict:
+    """Per-step device time (eager launches, one CUDA event pair per step on
+    the current stream, L2 flushed before each pass), averaged over iters."""
+    import torch
+
+    stream = torch.cuda.current_stream(dev)
+    names = step_names(prog)
+    per = {n: [] for n in names}
+    for _ in range(iters):
+        flush.zero_()
+        prog.status.reset()
+        evs = []
+        for n, step in zip(names, prog.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            step.fn()
+            b.record(stream)
+            evs.append((n, a, b))
+        torch.cuda.synchronize(dev)
+        for n, a, b in evs:
+            per[n].append(a.elapsed_time(b))
+    prog.check_status()
+    return {n: sum(v) / len(v) for n, v in per.items()}
+
+
+def roofline(prog, workload: str, batch: int, avg: dict) -> dict:
+    """Both roofs of the dominant step: int8 MMA work on the (derived) int8
+    tensor peak and its algorithmic bytes on the measured HBM copy bandwidth;
+    `bound` names the one with the larger fraction."""
+    names = step_names(prog)
+    dominant = max(avg, key=avg.get)
+    step = prog.steps[names.index(dominant)]
+    info = next((l for l in prog.layers if dominant.split("#")[0] == l.name
+                 or dominant.startswith(l.name + ".")), None)
+    hbm_peak, bf16_peak, peak_kind = peaks()
+    int8_peak = 2 * bf16_peak
+    dur_s = avg[dominant] / 1000
+    tensor = hbm = None
+    if step.cim and step.meta and step.meta.get("kind") == "chain":
+        ops = 2 * prog.macs
+        nbytes = (4 * step.meta["x"].numel() + 4 * step.meta["out"].numel()
+                  + sum(2 * l.n * l.k for l in prog.layers))
+        what = ("whole-network chain: ops = 2 x MACs of every layer; bytes = input batch "
+                "+ logits + int8 weights of both signs")
+        tensor, hbm = ops, nbytes
+    elif step.cim and info is not None:
+        ops = 2 * info.macs
+        nbytes = info.in_bytes + 2 * info.n * info.k + 4 * info.m * info.n
+        what = ("CIM layer: ops = 2 x branches x M x K x N (unpadded); bytes = source read "
+                "once + int8 weights of both signs + f32 output")
+        tensor, hbm = ops, nbytes
+    elif info is not None and dominant.endswith(".prepare"):
+        ab = 1 if info.branches == 2 else 2
+        t_tiles = -(-info.k // 64)
+        m_pad = -(-info.m // 128) * 128
+        hbm = info.in_bytes + ab * m_pad * t_tiles * (64 + 4)
+        what = ("prepare: bytes = source read once + prepared int8 columns and group "
+                "exponents written")
+    else:
+        what = "glue kernel (bytes not modelled)"
+    roofs = []
+    if tensor is not None:
+        a = tensor / dur_s / 1e12
+        roofs.append({"bound": "tensor", "achieved": a, "peak": int8_peak, "unit": "TFLOP/s",
+                      "frac": a / int8_peak, "ops_per_launch": tensor,
+                      "peak_note": f"derived int8 dense peak = 2 x {peak_kind} bf16 cuBLAS "
+                                   f"burst ({bf16_peak} TF/s), of measured"})
+    if hbm is not None:
+        a = hbm / dur_s / 1e9
+        roofs.append({"bound": "hbm", "achieved": a, "peak": hbm_peak, "unit": "GB/s",
+                      "frac": a / hbm_peak, "bytes_per_launch": hbm,
+                      "peak_note": f"{peak_kind} HBM copy bandwidth"})
+    if not roofs:
+        roofs.append({"bound": "hbm", "achieved": None, "peak": hbm_peak, "unit": "GB/s",
+                      "frac": None, "peak_note": f"{peak_kind} HBM copy bandwidth"})
+    roofs.sort(key=lambda r: -(r["frac"] or 0))
+    roof = dict(roofs[0], kernel=dominant, launch_ms=avg[dominant], work=what)
+    if len(roofs) > 1:
+        roof["other_roof"] = {k: roofs[1][k] for k in ("bound", "achieved", "peak", "unit",
+                                                       "frac")}
+    roof["traffic"], roof["traffic_source"] = ncu_traffic(workload, batch, dominant)
+    return roof
+
+
+def run_workload(name: str, batch: int, *, world: int, rank: int, local: int, dev, flush,
+                 steps: int, warmup: int, clock_window: bool, barrier, reduce_max):
+    """Build, time and e2e-time one workload. Returns a dict of results."""
+    import torch
+
+    from cim22_b200 import backend, program, workloads
+
+    model, _ = workloads.build(name, batch, seed=0)
+    _, x = workloads.build(name, batch, seed=1000 + rank)  # per-rank batch
+    prog = program.from_module(model, x, device=local, name=name)
+    prog.inputs[0].tensor.copy_(x.to(dev))
+    prog.capture()
+    stream = torch.cuda.current_stream(dev)
+
+    for _ in range(warmup):
+        flush.zero_()
+        prog.replay()
+    prog.check_status()
+    barrier()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    clocks = None
+    with ClockSampler([local] if world == 1 else range(world)) as sampler:
+        if clock_window:
+            # Untimed replays so the clock record covers a loaded window of at
+            # least CLOCK_WINDOW_S before and through the timed loop.
+            t_load = time.perf_counter()
+            while time.perf_counter() - t_load < CLOCK_WINDOW_S:
+                for _ in range(8):
+                    flush.zero_()
+                    prog.replay()
+                torch.cuda.synchronize(dev)
+        barrier()
+        for i in range(steps):
+            flush.zero_()  # L2 flush between steps, outside the timed span
+            starts[i].record(stream)
+            prog.replay()
+            ends[i].record(stream)
+        barrier()
+        time.sleep(0.25 if clock_window else 0.0)
+        if clock_window:
+            clocks = sampler.summary(since=t_load)
+    prog.check_status()
+    elapsed_ms = reduce_max(sum(s.elapsed_time(e) for s, e in zip(starts, ends)))
+    value = world * batch * steps / (elapsed_ms / 1000)
+
+    avg = kernel_times(prog, dev, flush, max(3, min(steps, 10)))
+    total_kernel = sum(avg.values())
+    roof = roofline(prog, name, batch, avg)
+
+    # End to end through the public API (torch.compile, runtime="cuda").
+    bname = backend.register()
+    torch._dynamo.reset()
+    compiled = torch.compile(model, backend=bname, fullgraph=True, dynamic=False,
+                             options={"runtime": "cuda", "device": local,
+                                      "chain": prog.chained})
+    host = x.pin_memory()
+    with torch.inference_mode():
+        out = compiled(host)
+        for _ in range(warmup):
+            out = compiled(host)
+        barrier()
+        e_ms = 0.0
+        for _ in range(steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            out = compiled(host)
+            b.record(stream)
+            b.synchronize()
+            e_ms += a.elapsed_time(b)
+        barrier()
+    e_ms = reduce_max(e_ms)
+    e2e_value = world * batch * steps / (e_ms / 1000)
+    h2d = host.numel() * host.element_size()
+    d2h = out.numel() * out.element_size() + 4  # outputs + status word
+    return {
+        "value": value, "ms_per_step": elapsed_ms / steps, "macs_per_batch": prog.macs,
+        "gpu_launches": len(prog.steps) * steps,
+        "lowering": "fused layer chain (one persistent kernel)" if prog.chained
+                    else f"{len(prog.steps)} kernels per step (CUDA graph)",
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": roof,
+        "kernels": {n: {"ms": round(v, 5), "share": round(v / total_kernel, 4)}
+                    for n, v in avg.items()},
+        "clocks": clocks,
+    }
 
 
 def column_bench(args, world: int, rank: int, local: int, dev) -> None:
@@ -290,6 +561,12 @@ def column_bench(args, world: int, rank: int, local: int, dev) -> None:
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     with ClockSampler([local] if world == 1 else range(world)) as clocks:
+        t_load = time.perf_counter()
+        while time.perf_counter() - t_load < CLOCK_WINDOW_S:
+            for _ in range(8):
+                flush.zero_()
+                stack(xd)
+            torch.cuda.synchronize(dev)
         barrier()
         for i in range(args.steps):
             flush.zero_()
@@ -297,6 +574,7 @@ def column_bench(args, world: int, rank: int, local: int, dev) -> None:
             stack(xd)
             ends[i].record(stream)
         barrier()
+        time.sleep(0.25)
     stack.check_status()
     t = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts, ends))], device=dev,
                      dtype=torch.float64)
@@ -350,8 +628,7 @@ def column_bench(args, world: int, rank: int, local: int, dev) -> None:
             "config": {"workload": f"{args.workload}: {w.description}", "global_batch": rows,
                        "parallelism": f"column-sharded x{world} (lanes split, NCCL all-gather "
                                       f"per layer)",
-                       "l2": "flushed between steps (256 MiB write, outside the timed span)",
-                       "graph": "eager launches"},
+                       "l2": L2_NOTE},
             "gpu_launches": 3 * len(stack.layers) * args.steps,
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": host.numel() * host.element_size(),
@@ -359,9 +636,10 @@ def column_bench(args, world: int, rank: int, local: int, dev) -> None:
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": 2 * bf16_peak,
                          "unit": "TFLOP/s", "frac": achieved / (2 * bf16_peak), "traffic": None,
                          "kernel": "linear0 (local lanes)", "launch_ms": launch_ms,
-                         "peak_note": f"int8 dense = 2 x {peak_kind} bf16 cuBLAS"},
+                         "peak_note": f"derived int8 dense peak = 2 x {peak_kind} bf16 "
+                                      "cuBLAS burst"},
             "cpu_baseline": None,
-            "clocks": clocks.summary(),
+            "clocks": clocks.summary(since=t_load),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -374,9 +652,6 @@ def main() -> None:
     if args.impl == "reference":
         reference_arm(args)
         return
-    if args.int8_sweep:
-        int8_sweep(args)
-        return
 
     import torch
     import torch.distributed as dist
@@ -386,25 +661,29 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    if args.int8_sweep:
+        int8_sweep([int(v) for v in args.sweep_m.split(",")],
+                   [int(v) for v in args.sweep_kn.split(",")], max(3, min(args.steps, 20)),
+                   dev, flush, emit=lambda r: print(json.dumps(r), flush=True))
+        return
     if world > 1:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    from cim22_b200 import backend, program, workloads
-
     if args.parallel == "columns":
         column_bench(args, world, rank, local, dev)
         return
 
-    w = workloads.WORKLOADS[args.workload]
-    batch = args.batch or w.batch
-    model, x = workloads.build(args.workload, batch, seed=0)
-    _, x = workloads.build(args.workload, batch, seed=1000 + rank)  # per-rank batch
+    from cim22_b200 import program, workloads
 
-    prog = program.from_module(model, x, device=local, name=args.workload)
-    prog.inputs[0].tensor.copy_(x.to(dev))
+    batch = args.batch or workloads.WORKLOADS[args.workload].batch
     if args.profile:
+        model, x = workloads.build(args.workload, batch, seed=0)
+        prog = program.from_module(model, x, device=local, name=args.workload)
+        prog.inputs[0].tensor.copy_(x.to(dev))
         for _ in range(args.warmup + args.steps):
             prog.status.reset()
             prog.launch()
@@ -413,189 +692,63 @@ def main() -> None:
         print(json.dumps({"profile": args.workload, "passes": args.warmup + args.steps,
                           "kernels": [s.name for s in prog.steps]}))
         return
-    prog.capture()
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
     def barrier():
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
 
-    # Warm-up.
-    for _ in range(args.warmup):
-        flush.zero_()
-        prog.replay()
-    prog.check_status()
-    barrier()
+    def reduce_max(v: float) -> float:
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
-    stream = torch.cuda.current_stream(dev)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler([local] if world == 1 else range(world)) as clocks:
-        barrier()
-        for i in range(args.steps):
-            flush.zero_()  # L2 flush between steps, outside the timed span
-            starts[i].record(stream)
-            prog.replay()
-            ends[i].record(stream)
-        barrier()
-    prog.check_status()
-    elapsed_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms = float(t.item())
-    value = world * batch * args.steps / (elapsed_ms / 1000)
+    head = run_workload(args.workload, batch, world=world, rank=rank, local=local, dev=dev,
+                        flush=flush, steps=args.steps, warmup=args.warmup, clock_window=True,
+                        barrier=barrier, reduce_max=reduce_max)
 
-    # Per-kernel device time (eager launches, one event pair per kernel);
-    # repeated glue names get an ordinal ("add", "add#2", ...).
-    names, seen = [], {}
-    for s in prog.steps:
-        seen[s.name] = seen.get(s.name, 0) + 1
-        names.append(s.name if seen[s.name] == 1 else f"{s.name}#{seen[s.name]}")
-    per = {n: [] for n in names}
-    kernel_iters = max(3, min(args.steps, 20))
-    for _ in range(kernel_iters):
-        flush.zero_()
-        prog.status.reset()
-        evs = []
-        for n, step in zip(names, prog.steps):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            step.fn()
-            b.record(stream)
-            evs.append((n, a, b))
-        torch.cuda.synchronize(dev)
-        for n, a, b in evs:
-            per[n].append(a.elapsed_time(b))
-    prog.check_status()
-    avg = {n: sum(v) / len(v) for n, v in per.items()}
-    total_kernel = sum(avg.values())
-    dominant = max(avg, key=avg.get)
-    hbm_peak, bf16_peak, peak_kind = peaks()
-    step = prog.steps[names.index(dominant)]
-    info = next((l for l in prog.layers if dominant.startswith(l.name)), None)
-    dur_s = avg[dominant] / 1000
-    if step.cim and step.meta and step.meta.get("kind") == "chain":
-        # The whole network in one kernel: the MMA-equivalent work of every
-        # layer on the int8 tensor peak (the chain computes it with dp4a on
-        # CUDA cores), and on HBM the input images, the logits and each
-        # layer's int8 weights of both signs.
-        ops = 2 * prog.macs
-        achieved = ops / dur_s / 1e12
-        int8_peak = 2 * bf16_peak
-        chain_bytes = (4 * step.meta["x"].numel() + 4 * step.meta["out"].numel()
-                       + sum(2 * l.n * l.k for l in prog.layers))
-        gbs = chain_bytes / dur_s / 1e9
-        tensor = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
-                  "frac": achieved / int8_peak, "ops_per_launch": ops,
-                  "peak_note": f"int8 dense = 2 x {peak_kind} bf16 cuBLAS ({bf16_peak} TF/s); "
-                               "ops = 2 x branches x M x K x N of every layer (unpadded)"}
-        hbm = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
-               "frac": gbs / hbm_peak, "bytes_per_launch": chain_bytes,
-               "peak_note": f"{peak_kind} HBM copy bandwidth"}
-        first, other = (tensor, hbm) if tensor["frac"] >= hbm["frac"] else (hbm, tensor)
-        roof = dict(first, traffic=None, kernel=dominant, launch_ms=avg[dominant],
-                    other_roof={k: other[k] for k in ("bound", "achieved", "peak", "unit",
-                                                       "frac")})
-    elif step.cim and info is not None:
-        # Both roofs of a CIM layer step: the MMA work on the int8 tensor
-        # peak, and the bytes it must move (its source read once, int8
-        # weights of both signs, the f32 output) on HBM; the binding one is
-        # the one with the larger fraction.
-        ops = 2 * info.macs
-        achieved = ops / dur_s / 1e12
-        int8_peak = 2 * bf16_peak
-        layer_bytes = info.in_bytes + 2 * info.n * info.k + 4 * info.m * info.n
-        gbs = layer_bytes / dur_s / 1e9
-        tensor = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
-                  "frac": achieved / int8_peak, "ops_per_launch": ops,
-                  "peak_note": f"int8 dense = 2 x {peak_kind} bf16 cuBLAS ({bf16_peak} TF/s); "
-                               "ops = 2 x branches x M x K x N (unpadded) as TOPS"}
-        hbm = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
-               "frac": gbs / hbm_peak, "bytes_per_launch": layer_bytes,
-               "peak_note": f"{peak_kind} HBM copy bandwidth"}
-        first, other = (tensor, hbm) if tensor["frac"] >= hbm["frac"] else (hbm, tensor)
-        roof = dict(first, traffic=None, kernel=dominant, launch_ms=avg[dominant],
-                    other_roof={k: other[k] for k in ("bound", "achieved", "peak", "unit",
-                                                       "frac")})
-    else:
-        algo = None
-        if info is not None and dominant.endswith(".prepare"):
-            # Read the source tensor once; write the prepared int8 columns and
-            # their group exponents (m_pad x (k_pad + 4 T) per activation branch).
-            ab = 1 if info.branches == 2 else 2
-            t_tiles = -(-info.k // 64)
-            m_pad = -(-info.m // 128) * 128
-            algo = info.in_bytes + ab * m_pad * t_tiles * (64 + 4)
-        gbs = (algo / dur_s / 1e9) if algo else None
-        roof = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
-                "frac": (gbs / hbm_peak) if gbs else None, "traffic": None, "kernel": dominant,
-                "bytes_per_launch": algo, "launch_ms": avg[dominant],
-                "peak_note": f"{peak_kind} HBM copy bandwidth"}
-    roof["traffic"], roof["traffic_source"] = ncu_traffic(args.workload, batch, dominant)
-    kernel_table = {n: {"ms": round(avg[n], 5), "share": round(avg[n] / total_kernel, 4)}
-                    for n in names}
-
-    # End to end through the public API (torch.compile, runtime="cuda").
-    name = backend.register()
-    compiled = torch.compile(model, backend=name, fullgraph=True, dynamic=False,
-                             options={"runtime": "cuda", "device": local,
-                                      "chain": prog.chained})
-    host = x.pin_memory()
-    with torch.inference_mode():
-        out = compiled(host)
-        for _ in range(args.warmup):
-            out = compiled(host)
-        barrier()
-        e_ms = 0.0
-        for _ in range(args.steps):
-            flush.zero_()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            out = compiled(host)
-            b.record(stream)
-            b.synchronize()
-            e_ms += a.elapsed_time(b)
-        barrier()
-    et = torch.tensor([e_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(et, op=dist.ReduceOp.MAX)
-    e2e_value = world * batch * args.steps / (float(et.item()) / 1000)
-    h2d = host.numel() * host.element_size()
-    d2h = out.numel() * out.element_size() + 4  # logits + status word
-
-    cpu = None
+    extras = sweep = cpu = None
+    if world == 1 and not args.no_extras:
+        extras = {}
+        for name in EXTRA_WORKLOADS:
+            if name == args.workload:
+                continue
+            b = workloads.WORKLOADS[name].batch
+            r = run_workload(name, b, world=1, rank=0, local=local, dev=dev, flush=flush,
+                             steps=max(args.steps, 20), warmup=args.warmup, clock_window=False,
+                             barrier=barrier, reduce_max=reduce_max)
+            roof = r["roofline"]
+            extras[name] = {
+                "config": bench_config(name, b, 1), "value": r["value"], "unit": UNIT,
+                "ms_per_step": r["ms_per_step"], "e2e": r["e2e"], "lowering": r["lowering"],
+                "dominant_kernel": roof["kernel"], "dominant_ms": roof["launch_ms"],
+                "dominant_share": r["kernels"][roof["kernel"]]["share"],
+                "roofline": {k: roof.get(k) for k in ("bound", "achieved", "unit", "frac",
+                                                       "peak", "other_roof")},
+                "macs_per_batch": r["macs_per_batch"],
+            }
+        sweep = int8_sweep([1, 16, 128, 1024, 8192], [256, 1024, 4096, 8192], 10, dev, flush)
+        sweep.pop("points")
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        rate, dt = cpu_baseline(args.workload, args.cpu_sample, threads)
-        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{args.cpu_sample} {args.workload} images through the oracle's "
-                         f"restated CIMSoftwareRunner (40-Work transactions, plan reuse, "
-                         f"residency) + PyTorch CPU glue, {dt:.1f} s wall"}
+        cpu = cpu_baseline(args.workload)
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"{args.workload}: {w.description}", "batch_per_gpu": batch,
-                       "global_batch": batch * world, "parallelism": f"batch-sharded x{world}",
-                       "l2": "flushed between steps (256 MiB write, outside the timed span)",
-                       "graph": "CUDA graph replay", "cim_macs_per_batch": prog.macs,
-                       "lowering": "fused layer chain (one persistent kernel)" if prog.chained
-                                   else "per-layer kernels",
-                       "arithmetic": "BF16 sign-split: int8 mantissa crossbar dots, BF16 "
-                                     "tiles, f32 K sums"},
-            "gpu_launches": len(prog.steps) * args.steps,
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
-            "roofline": roof,
-            "kernels": kernel_table,
-            "cpu_baseline": cpu,
-            "clocks": clocks.summary(),
+            "metric": METRIC, "value": head["value"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": bench_config(args.workload, batch, world),
+            "graph": "CUDA graph replay of the whole network per step",
+            "lowering": head["lowering"], "cim_macs_per_batch": head["macs_per_batch"],
+            "gpu_launches": head["gpu_launches"], "e2e": head["e2e"],
+            "roofline": head["roofline"], "kernels": head["kernels"],
+            "cpu_baseline": cpu, "clocks": head["clocks"],
         }
+        if extras is not None:
+            line["configs"] = extras
+        if sweep is not None:
+            line["int8_sweep"] = sweep
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

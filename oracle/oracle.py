@@ -35,10 +35,12 @@ class OracleError(RuntimeError):
 
 
 def build(reference: bool = True) -> None:
-    """Compile liboracle.so (and the reference pieces when the source exists)."""
+    """Compile liboracle.so and, when the mlir-cim22 source tree is present
+    (the Makefile's REFERENCE, or CIM22_REFERENCE), the reference pieces in
+    oracle/_ref. The Makefile alone knows where that tree lives."""
     targets = ["oracle"]
-    if reference and Path(os.environ.get("CIM22_REFERENCE", "/root/reference")).is_dir():
-        targets.append("ref")
+    if reference:
+        targets.append("ref-if-present")
     env = dict(os.environ)
     if "CIM22_REFERENCE" in os.environ:
         env["REFERENCE"] = os.environ["CIM22_REFERENCE"]
@@ -103,6 +105,35 @@ def ref_lib() -> ctypes.CDLL | None:
         L.ref_prealign_tile.argtypes = [ctypes.c_void_p] * 3
         _REF = L
     return _REF
+
+
+_REF_RUNNER = None
+
+
+def ref_runner_lib() -> ctypes.CDLL | None:
+    """The reference's own CIMSoftwareRunner + BF16Compensation (with
+    BF16Support), compiled unmodified into oracle/_ref against the clean-room
+    LLVM support headers of oracle/llvm_shim, when that was built here."""
+    global _REF_RUNNER
+    if _REF_RUNNER is None:
+        path = HERE / "_ref" / "libref_runner.so"
+        if not path.exists():
+            return None
+        L = ctypes.CDLL(str(path))
+        c = ctypes
+        L.ref_linear_bf16_runner.argtypes = [c.c_void_p, c.c_int64, c.c_int64, c.c_void_p,
+                                             c.c_int64, c.c_void_p, c.c_int, c.c_void_p,
+                                             c.c_int, c.c_char_p, c.c_size_t]
+        L.ref_runner_create.restype = c.c_void_p
+        L.ref_runner_destroy.argtypes = [c.c_void_p]
+        L.ref_runner_run.argtypes = [c.c_void_p, c.c_void_p, c.c_int, c.c_void_p, c.c_int64,
+                                     c.c_void_p, c.c_int64, c.c_int, c.c_char_p, c.c_size_t]
+        _REF_RUNNER = L
+    return _REF_RUNNER
+
+
+def reference_runner_available() -> bool:
+    return ref_runner_lib() is not None
 
 
 def _err() -> ctypes.Array:
@@ -249,8 +280,13 @@ def linear_int8(x: np.ndarray, w: np.ndarray) -> np.ndarray:
 
 
 def linear_bf16(x: np.ndarray, w: np.ndarray, bias: np.ndarray | None = None,
-                branches: int = 4, threads: int = 1, via_runner: bool = False) -> np.ndarray:
-    """Sign-split BF16 CIM layer, y[m, n] for columns x[m, k] and weights w[n, k]."""
+                branches: int = 4, threads: int = 1, via_runner: bool | str = False) -> np.ndarray:
+    """Sign-split BF16 CIM layer, y[m, n] for columns x[m, k] and weights w[n, k].
+
+    via_runner: False computes the layer directly from the restated numerics;
+    True drives the restated CIMSoftwareRunner with 40-Work transactions;
+    "reference" drives the reference's own runner (oracle/_ref); "auto" the
+    reference's runner when it was built, else the restated one."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     w = np.ascontiguousarray(w, dtype=np.float32)
     m, k = x.shape
@@ -259,7 +295,17 @@ def linear_bf16(x: np.ndarray, w: np.ndarray, bias: np.ndarray | None = None,
     b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
     y = np.zeros((m, n), np.float32)
     err = _err()
-    fn = lib().oracle_linear_bf16_runner if via_runner else lib().oracle_linear_bf16
+    if via_runner == "reference":
+        ref = ref_runner_lib()
+        if ref is None:
+            raise OracleError("the reference runner was not built (oracle/_ref)")
+        fn = ref.ref_linear_bf16_runner
+    elif via_runner == "auto" and ref_runner_lib() is not None:
+        fn = ref_runner_lib().ref_linear_bf16_runner
+    elif via_runner:
+        fn = lib().oracle_linear_bf16_runner
+    else:
+        fn = lib().oracle_linear_bf16
     if fn(x.ctypes.data, m, k, w.ctypes.data, n, None if b is None else b.ctypes.data,
           branches, y.ctypes.data, threads, err, len(err)):
         raise OracleError(err.value.decode())
@@ -398,28 +444,60 @@ def conv2d_int8(x: np.ndarray, weight: np.ndarray, bias: np.ndarray | None = Non
     return y.reshape(x.shape[0], oh, ow, f).transpose(0, 3, 1, 2).copy()
 
 
-def cim_forward(model, x, *, branches: int = 4, threads: int = 1, via_runner: bool = False,
-                compensation: str = "sign-split"):
+def reference_branches(model) -> dict:
+    """Sign-split branch count of every Linear/Conv2d module of a model, as
+    the reference's lowering decides it: 2 when the layer's input is directly
+    the result of a ReLU (isNonnegativeFloat, Passes.cpp:2239-2303), else 4
+    (graph inputs, pools, flattens of pools, GELU, additions)."""
+    import torch
+    import torch.fx as fx
+    import torch.nn.functional as F
+
+    relu_calls = {F.relu, torch.relu}
+    gm = fx.symbolic_trace(model)
+    modules = dict(gm.named_modules())
+    out = {}
+    for node in gm.graph.nodes:
+        if node.op != "call_module":
+            continue
+        module = modules[str(node.target)]
+        if not isinstance(module, (torch.nn.Linear, torch.nn.Conv2d)):
+            continue
+        src = node.args[0]
+        relu = isinstance(src, fx.Node) and (
+            (src.op == "call_function" and src.target in relu_calls) or
+            (src.op == "call_method" and src.target == "relu") or
+            (src.op == "call_module" and isinstance(modules[str(src.target)], torch.nn.ReLU)))
+        out[module] = 2 if relu else 4
+    return out
+
+
+def cim_forward(model, x, *, branches: int | str = 4, threads: int = 1,
+                via_runner: bool = False, compensation: str = "sign-split"):
     """Run a torch model on CPU with every Linear/Conv2d computed by the oracle.
 
     Everything else runs as PyTorch CPU eager in f32, which is the reference's
     own oracle for the float glue. compensation "legacy" / "none" computes the
-    layers in those diagnostic modes. Returns a NumPy array.
+    layers in those diagnostic modes. branches: 4, 2, or "reference" for the
+    per-layer counts of the reference's lowering (reference_branches); the
+    results are the same bits, only the work differs. Returns a NumPy array.
     """
     import torch
 
     saved = {}
+    per_layer = reference_branches(model) if branches == "reference" else {}
 
-    def contract(cols, weight, bias):
+    def contract(cols, weight, bias, module):
         if compensation == "sign-split":
-            return linear_bf16(cols, weight, bias, branches, threads, via_runner)
+            return linear_bf16(cols, weight, bias, per_layer.get(module, branches), threads,
+                               via_runner)
         return linear_bf16_mode(cols, weight, bias, compensation)
 
     def linear_forward(module):
         def fn(inp):
             flat = inp.detach().float().reshape(-1, inp.shape[-1]).numpy()
             bias = None if module.bias is None else module.bias.detach().float().numpy()
-            y = contract(flat, module.weight.detach().float().numpy(), bias)
+            y = contract(flat, module.weight.detach().float().numpy(), bias, module)
             return torch.from_numpy(y).reshape(*inp.shape[:-1], y.shape[-1])
         return fn
 
@@ -433,7 +511,7 @@ def cim_forward(model, x, *, branches: int = 4, threads: int = 1, via_runner: bo
             f, c, kh, kw = weight.shape
             cols, oh, ow = im2col(inp.detach().float().numpy(), kh, kw, module.stride[0],
                                   module.padding[0])
-            y = contract(cols, weight.reshape(f, -1), bias)
+            y = contract(cols, weight.reshape(f, -1), bias, module)
             n = inp.shape[0]
             return torch.from_numpy(y.reshape(n, oh, ow, f).transpose(0, 3, 1, 2).copy())
         return fn

@@ -1,9 +1,10 @@
 """Generate the committed golden vectors under tests/golden/.
 
-Run in a container that has the mlir-cim22 source tree (default
-/root/reference, override with CIM22_REFERENCE):
+Run in a container that has the mlir-cim22 source tree, naming it by the
+CIM22_REFERENCE environment variable or the first argument:
 
-    python tests/golden/make_golden.py
+    CIM22_REFERENCE=<mlir-cim22 checkout> python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <mlir-cim22 checkout>
 
 Outputs:
   supplier_int8.json   The four supplier INT8 tile fixtures
@@ -41,7 +42,8 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REFERENCE = Path(os.environ.get("CIM22_REFERENCE", "/root/reference"))
+REFERENCE = Path(sys.argv[1] if len(sys.argv) > 1 and not sys.argv[1].startswith("-")
+                 else os.environ.get("CIM22_REFERENCE", ""))
 
 
 def supplier_int8() -> dict:
@@ -232,6 +234,9 @@ def int8_conv_ref() -> dict:
 
 
 def main() -> None:
+    if not (REFERENCE / "lib").is_dir():
+        raise SystemExit("name the mlir-cim22 source tree: CIM22_REFERENCE=<dir> or "
+                         "make_golden.py <dir>")
     data = supplier_int8()
     (HERE / "supplier_int8.json").write_text(json.dumps(data) + "\n", encoding="ascii")
     np.savez_compressed(HERE / "bf16_support_ref.npz", **bf16_support_ref())
