@@ -125,7 +125,9 @@ def ref_runner_lib() -> ctypes.CDLL | None:
                                              c.c_int64, c.c_void_p, c.c_int, c.c_void_p,
                                              c.c_int, c.c_char_p, c.c_size_t]
         L.ref_runner_create.restype = c.c_void_p
+        L.ref_runner_create.argtypes = [c.c_int]
         L.ref_runner_destroy.argtypes = [c.c_void_p]
+        L.ref_runner_stats.argtypes = [c.c_void_p, c.c_void_p, c.c_void_p]
         L.ref_runner_run.argtypes = [c.c_void_p, c.c_void_p, c.c_int, c.c_void_p, c.c_int64,
                                      c.c_void_p, c.c_int64, c.c_int, c.c_char_p, c.c_size_t]
         _REF_RUNNER = L
@@ -134,6 +136,47 @@ def ref_runner_lib() -> ctypes.CDLL | None:
 
 def reference_runner_available() -> bool:
     return ref_runner_lib() is not None
+
+
+class RefRunner:
+    """The reference's own CIMSoftwareRunner (oracle/_ref) in one compensation
+    mode, with a session-owned weight catalog and residency; the same run()
+    contract as Runner."""
+
+    def __init__(self, mode: int) -> None:
+        L = ref_runner_lib()
+        if L is None:
+            raise OracleError("the reference runner was not built (oracle/_ref)")
+        self._handle = L.ref_runner_create(mode)
+
+    def close(self) -> None:
+        if self._handle:
+            ref_runner_lib().ref_runner_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self) -> None:  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def stats(self) -> tuple[int, int]:
+        w, h = ctypes.c_uint64(), ctypes.c_uint64()
+        ref_runner_lib().ref_runner_stats(self._handle, ctypes.byref(w), ctypes.byref(h))
+        return w.value, h.value
+
+    def run(self, spec, inputs, outputs, *, batch: bool = False, residency: bool = False):
+        txn = spec.to_c()
+        in_ptrs = (ctypes.c_void_p * max(1, len(inputs)))(
+            *[None if a is None else a.ctypes.data for a in inputs])
+        out_ptrs = (ctypes.c_void_p * max(1, len(outputs)))(
+            *[None if a is None else a.ctypes.data for a in outputs])
+        err = _err()
+        rc = ref_runner_lib().ref_runner_run(self._handle, txn.pointer, int(batch), in_ptrs,
+                                             len(inputs), out_ptrs, len(outputs),
+                                             int(residency), err, len(err))
+        return err.value.decode() if rc else None
 
 
 def _err() -> ctypes.Array:
