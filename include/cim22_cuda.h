@@ -441,9 +441,10 @@ int cim22_cuda_layer_forward_bf16(const cim22_cuda_layer *layer, const float *x,
 
 /* No counterpart in the reference. The same BF16 sign-split layer as
  * cim22_cuda_layer_forward_bf16 for callers that cannot allocate device
- * memory: code running while a stream is captured into a CUDA graph (where
- * cudaMalloc/cudaFree are not allowed) and generated model code that owns only
- * stack buffers. The prepared-column scratch lives in a library-owned 16 MiB
+ * memory: generated model code that, like the reference's compiled Host code,
+ * owns only stack buffers and has no device allocator, and embedders whose
+ * device memory is owned and budgeted by another component. The
+ * prepared-column scratch lives in a library-owned 16 MiB
  * __device__ array (held by every GPU that loads the library until exit);
  * calls needing more (cim22_cuda_layer_workspace_bf16 > that size) are
  * rejected with CIM22_STATUS_BAD_ARGUMENT and a message in

@@ -2,12 +2,11 @@
 //
 // cim22_cuda_layer_forward_bf16 needs a workspace for the prepared activation
 // columns (int8 mantissas and per-group exponents). Some callers cannot
-// provide one: code that runs while a CUDA stream is being captured into a
-// graph (cudaMalloc and cudaFree are not legal there, and cudaFree would
-// synchronize the device), and generated model code that, like the
-// reference's Host code, only owns stack buffers and has no allocator of its
-// own. This entry point keeps that scratch in a fixed-size array in device
-// global memory that belongs to the library, so the call allocates nothing.
+// provide one: generated model code that, like the reference's compiled Host
+// code, only owns stack buffers and has no device allocator of its own, and
+// embedders whose device memory is owned and budgeted by another component.
+// This entry point keeps that scratch in a fixed-size array in device global
+// memory that belongs to the library, so the call allocates nothing.
 //
 // Facts a caller must know:
 //  * Every GPU that loads the library holds kScratchBytes of device memory

@@ -1,8 +1,9 @@
 """The allocation-free BF16 layer entry point, through the C ABI.
 
 cim22_cuda_layer_forward_bf16_noalloc serves callers that cannot allocate
-device memory (stream capture, generated code with only stack buffers); its
-scratch is a library-owned static device array. Its output must equal the
+device memory (generated model code that owns only stack buffers, embedders
+whose device memory another component budgets); its scratch is a
+library-owned static device array. Its output must equal the
 workspace-taking entry point's, bit for bit, on consecutive calls (the array
 keeps the previous call's contents, which must not leak into the next result),
 and sizes beyond the array are rejected before any launch. This file sorts
