@@ -81,8 +81,11 @@ def _is_mutated(node: torch.fx.Node) -> bool:
 
 
 def backend(gm: torch.fx.GraphModule, example_inputs: Sequence[torch.Tensor], *,
-            options: BackendOptions | None = None) -> Callable:
-    """Compile a static inference graph for torch.compile."""
+            options: BackendOptions | None = None,
+            _on_program: Callable[[Program], None] | None = None) -> Callable:
+    """Compile a static inference graph for torch.compile. _on_program receives
+    each compiled program (LayerOffload tracks its layers' programs with it, as
+    the reference's backend hands out sessions through _on_session)."""
     options = dict(options or {})
     _validate(options)
     if torch.is_grad_enabled():
@@ -119,6 +122,8 @@ def backend(gm: torch.fx.GraphModule, example_inputs: Sequence[torch.Tensor], *,
                       chain=options.get("chain", "auto"))
     if options.get("cuda_graph", True):
         program.capture()
+    if _on_program is not None:
+        _on_program(program)
     inputs = [i for i in range(len(placeholders)) if i not in frozen]
 
     def run(*values):

@@ -150,6 +150,7 @@ class Program:
         self._host = None  # pinned output staging for CPU callers
         self._host_status = None
         self.mutated_inputs: set[int] = set()  # inputs the graph writes (state)
+        self.invocation_count = 0  # calls through __call__
         frozen = frozen or set()
         self.chained = False
         if chain and fuse and layout == "nchw" and bf16_compensation == "sign-split":
@@ -1365,6 +1366,7 @@ class Program:
         """Run on inputs (CPU or CUDA). Returns outputs on the inputs' device."""
         if len(values) != len(self.inputs):
             raise ValueError("Input count differs from compiled signature")
+        self.invocation_count += 1
         on_cpu = any(v.device.type == "cpu" for v in values)
         for v, shape, dtype in zip(values, self.input_shapes, self.input_dtypes):
             if tuple(v.shape) != shape or v.dtype != dtype:
@@ -1396,6 +1398,11 @@ class Program:
     @property
     def macs(self) -> int:
         return sum(layer.macs for layer in self.layers)
+
+    @property
+    def cim_launch_count(self) -> int:
+        """CIM layer kernels one call runs (contractions, or the fused chain)."""
+        return sum(1 for step in self.steps if step.cim)
 
 
 def from_module(model: torch.nn.Module, example: torch.Tensor, device: int = 0,

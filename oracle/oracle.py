@@ -516,14 +516,18 @@ def reference_branches(model) -> dict:
 
 
 def cim_forward(model, x, *, branches: int | str = 4, threads: int = 1,
-                via_runner: bool = False, compensation: str = "sign-split"):
+                via_runner: bool | str = False, compensation: str = "sign-split",
+                layers=None):
     """Run a torch model on CPU with every Linear/Conv2d computed by the oracle.
 
     Everything else runs as PyTorch CPU eager in f32, which is the reference's
     own oracle for the float glue. compensation "legacy" / "none" computes the
     layers in those diagnostic modes. branches: 4, 2, or "reference" for the
     per-layer counts of the reference's lowering (reference_branches); the
-    results are the same bits, only the work differs. Returns a NumPy array.
+    results are the same bits, only the work differs. layers: names of the
+    Linear/Conv2d modules to compute as CIM layers (default: all of them); the
+    others run as PyTorch CPU eager, as LayerOffload leaves them. Returns a
+    NumPy array.
     """
     import torch
 
@@ -559,7 +563,11 @@ def cim_forward(model, x, *, branches: int | str = 4, threads: int = 1,
             return torch.from_numpy(y.reshape(n, oh, ow, f).transpose(0, 3, 1, 2).copy())
         return fn
 
+    selected = None if layers is None else {
+        module for name, module in model.named_modules() if name in set(layers)}
     for module in model.modules():
+        if selected is not None and module not in selected:
+            continue
         if isinstance(module, torch.nn.Linear):
             saved[module] = module.forward
             module.forward = linear_forward(module)
