@@ -346,6 +346,15 @@ const char *cim22_cuda_last_error(void);
  * far (diagnostics: shows which contraction path a layer took). */
 int64_t cim22_cuda_tensor_core_launches(void);
 
+/* No counterpart in the reference. Self-check of the bounded on-device wait
+ * that every tensor-core pipeline uses for its mbarriers: one CTA waits on a
+ * barrier that nothing completes, gives up after limit_ns nanoseconds of the
+ * GPU's global timer and ORs CIM22_STATUS_TIMEOUT into *status (a device
+ * int32). The kernel holds no TMEM and issues no copies, so the context stays
+ * usable. Returns 0, or CIM22_STATUS_BAD_ARGUMENT for a null status or a
+ * limit outside (0, 10 s]. Asynchronous on `stream`. */
+int cim22_cuda_check_wait_timeout(uint64_t limit_ns, int32_t *status, void *stream);
+
 /* sizeof of each structure above, in declaration order: frame_packet,
  * static_weight, input_binding, readback_binding, work, group, transaction,
  * trace_event, memref2d, gather. Returns the number of entries written. */

@@ -98,6 +98,20 @@ def validate_cim_layers(model: torch.nn.Module, selected: Sequence[str] | None
     return names
 
 
+def _leaf_call(module: torch.nn.Module) -> Callable:
+    """The leaf's call (hooks and forward) as a function of this package, so
+    that Dynamo traces it: the reference compiles the leaf with
+    module.compile(), but Dynamo skips the call frames of torch.nn's own
+    modules when they are compiled directly, and LayerOffload selects exactly
+    those (Conv2d, Linear). Installed as the module's compiled call, as
+    module.compile() installs its own."""
+
+    def call(*args, **kwargs):
+        return module._call_impl(*args, **kwargs)
+
+    return call
+
+
 class LayerOffload:
     """Compile selected leaves in place and run the outer model on CPU.
 
@@ -137,9 +151,11 @@ class LayerOffload:
                         module = model.get_submodule(name)
                         compiled_calls[module] = module._compiled_call_impl
                         started = time.perf_counter()
-                        module.compile(backend=partial(backend, _on_program=programs.append),
-                                       fullgraph=True, dynamic=False,
-                                       options={"runtime": runtime, "device": device})
+                        module._compiled_call_impl = torch.compile(
+                            _leaf_call(module),
+                            backend=partial(backend, _on_program=programs.append),
+                            fullgraph=True, dynamic=False,
+                            options={"runtime": runtime, "device": device})
                         if reset is not None:
                             reset(model)
                         previous = self._invocations()

@@ -28,6 +28,7 @@ _SIGNATURES = {
     "cim22_cuda_last_error": (CHARP, []),
     "cim22_cuda_abi_sizes": (c.c_int, [P, c.c_int]),
     "cim22_cuda_tensor_core_launches": (I64, []),
+    "cim22_cuda_check_wait_timeout": (c.c_int, [c.c_uint64, P, P]),
     "cim22_cuda_runner_create": (P, [c.c_int, CHARP, SZ]),
     "cim22_cuda_runner_destroy": (None, [P]),
     "cim22_cuda_plan_create": (P, [P, P, c.c_int, CHARP, SZ]),

@@ -11,10 +11,10 @@
 //                          4 MMAs per K-block, tcgen05.commit frees a stage
 //   warps 2-5             epilogue: tcgen05.ld 32x32b from TMEM, int32 stores
 //
-// Every mbarrier wait is bounded; a wait that runs out sets
-// CIM22_STATUS_TIMEOUT, the CTA stops issuing work, waits (bounded) for the
-// copies it has in flight, frees its TMEM and returns. Every load is a plain
-// per-CTA copy into this CTA's shared memory.
+// Every mbarrier wait is bounded in time (kWaitLimitNs of the global timer);
+// a wait that runs out sets CIM22_STATUS_TIMEOUT, the CTA stops issuing work,
+// waits (bounded) for the copies it has in flight, frees its TMEM and
+// returns. Every load is a plain per-CTA copy into this CTA's shared memory.
 #include "gemm_tc.h"
 
 #include "cim_internal.h"
@@ -33,7 +33,8 @@ namespace {
 
 constexpr int kBM = 128, kBN = 128, kBK = 128, kStages = 4;
 constexpr int kThreads = 192;
-constexpr uint32_t kSpinLimit = 1u << 24;
+// Longest any single mbarrier wait may take before the kernel gives up.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kTileBytes = kBM * kBK; // A and B tiles are the same size
 
 struct alignas(1024) SmemInt8 {
@@ -60,11 +61,20 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                : "memory");
 }
 
-// Wait for the phase with the given parity to complete, at most kSpinLimit
-// polls. Returns false when the limit was reached.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the phase with the given parity to complete, for at most
+// limit_ns of the global timer (read once every 32 polls). Returns false
+// when the limit was reached.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   const uint32_t addr = smem_u32(bar);
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  uint64_t start = 0;
+  for (uint32_t i = 1;; ++i) {
     uint32_t done;
     asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
                  " selp.u32 %0, 1, 0, p;\n}\n"
@@ -73,8 +83,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
                  : "memory");
     if (done)
       return true;
+    if ((i & 31) == 0) {
+      const uint64_t now = global_ns();
+      if (start == 0)
+        start = now;
+      else if (now - start > limit_ns)
+        return false;
+    }
   }
-  return false;
+}
+
+// Dynamic shared memory rounded up to a 1024-byte boundary (the 128-byte
+// swizzle atoms), derived from the extern array so that the compiler keeps
+// addressing it as shared memory.
+template <typename T> __device__ __forceinline__ T &smem_aligned(uint8_t *raw) {
+  return *reinterpret_cast<T *>(raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u));
 }
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar,
@@ -137,8 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const int32_t *__restrict__ bias, int64_t out_pixels, FastDiv div_pix,
                    int32_t *__restrict__ y, int32_t *status) {
   extern __shared__ uint8_t smem_raw[];
-  SmemInt8 &s = *reinterpret_cast<SmemInt8 *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
+  SmemInt8 &s = smem_aligned<SmemInt8>(smem_raw);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int m0 = static_cast<int>(blockIdx.x) * kBM;
   const int n0 = static_cast<int>(blockIdx.y) * kBN;
@@ -272,13 +294,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 //                          merges ((pp - pn) - np) + nn, adds the bias and
 //                          applies the activation
 //
-// Inside the normal window (7 <= Ex <= 237, 140 <= Ex + Ew <= 374 for every
-// weight exponent of the tile) the restore is exact in three f32 operations:
-// fma(2^23 + p, 2^(Ex-133), -2^23 * 2^(Ex-133)) = p * 2^(Ex-133) is a normal
-// f32, clearing its low 16 bits keeps Q(p), and the product with 2^(Ew-133)
-// is the exactly representable tile value, so one FMA adds it with the single
-// rounding of the reference's f32 add. Outside the window the integer path
-// (signsplit_tile) restores the tile.
+// Inside the fast window (kScaleShift + 7 <= Ex <= kScaleShift + 111,
+// 140 <= Ex + Ew <= 374 and Ew <= 260 - kScaleShift for every weight exponent
+// of the tile) the restore is exact in three f32 operations on the dot p as
+// read from TMEM: its bit pattern is the f32 subnormal p * 2^-149, so
+// p * 2^(Ex + 16 - kScaleShift) = p * 2^(Ex - 133 - kScaleShift) is an exact
+// normal f32; clearing its low 16 bits keeps Q(p) (the truncating INT21->BF16
+// converter); and the product with the stored weight scale
+// 2^(Ew - 133 + kScaleShift) is the exactly representable tile value
+// Q(p) * 2^(Ex + Ew - 266), so one FMA adds it with the single rounding of the
+// reference's f32 add. Outside the window the integer path (signsplit_tile)
+// restores the tile.
 constexpr int kSBM = 128, kSBK = 128, kSStages = 4;
 constexpr int kEpiWarps = 16;
 constexpr int kSThreads = 64 + 32 * kEpiWarps;
@@ -293,7 +319,7 @@ template <int kAB> struct SSShape {
 
 struct alignas(16) ExpSlot {
   int32_t a[2][kSBM]; // activation group exponents per branch
-  float w[2][64];     // weight scales 2^(Ew - 133), Wp then Wn
+  float w[2][64];     // weight scales 2^(Ew - 133 + kScaleShift), Wp then Wn
   int32_t range[8];   // {min, max, 0, 0} weight exponent per 32-lane block
 };
 
@@ -356,11 +382,6 @@ __device__ __forceinline__ void tmem_wait(uint32_t (&r)[16]) {
                  "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])::"memory");
 }
 
-// A crossbar dot of the sign-split kernel is a nonnegative int32 below 2^21
-// (prealigned magnitudes of at most 127 over 64 elements), so OR-ing in the
-// bit pattern of 2^23 gives the f32 2^23 + dot, ready for the exact restore.
-constexpr uint32_t kDotBias = 0x4b000000u;
-
 // Exact restore of one tile value outside the fast window (out of line).
 __device__ __noinline__ float tc_slow_tile_add(float acc, int p, int ew, int ex,
                                                int32_t *status) {
@@ -379,48 +400,42 @@ __device__ __forceinline__ float act_tc(float v, int act) {
 }
 
 // Add the restored dots of one (activation branch, weight branch) pair of a
-// crossbar tile to the branch sums: the exact three-operation form inside
-// the window (scales read from the exponent slot four at a time), the
-// integer path otherwise.
-// p holds the dots as read from TMEM.
+// crossbar tile to the branch sums, three f32 operations per dot:
+//   v = p_bits * sx      (p_bits: the dot's bit pattern, the subnormal
+//                         p * 2^-149; sx = 2^(Ex + 16 - kScaleShift)), exact
+//   q = v with its low 16 bits cleared = Q(p) * 2^(Ex - 133 - kScaleShift)
+//   acc = fma(q, sw, acc) (sw = 2^(Ew - 133 + kScaleShift)), one rounding
+// Rows outside the fast window carry sx = 0, so their sums gain exactly +0
+// here and restore_slow_rows then adds their tile values; all sums are >= +0.
+// sw points at the tile's weight scales in shared memory (16-byte aligned).
 // kInit marks the first crossbar tile of an output tile: the sums start at
-// +0, and q * s (exact, nonnegative) is what fma(q, s, +0) gives.
-// kAddBias writes the bias as an integer add rather than an OR (equal for
-// dots below 2^23), which lets the compiler balance the ALU and FMA pipes
-// differently: measured faster for 2-branch layers, slower for 4-branch ones.
-template <int kLT, bool kInit, bool kAddBias>
-__device__ __forceinline__ void restore_add(float (&acc)[kLT], const uint32_t (&p)[kLT],
-                                            bool fast, float sx, float nsx,
-                                            const float *__restrict__ sw,
-                                            const int32_t *__restrict__ exB, int64_t ew_index,
-                                            int ex, int32_t *status) {
-  if (fast) {
+// q * sw (exact, nonnegative), which is what fma(q, sw, +0) gives.
+template <int kLT, bool kInit>
+__device__ __forceinline__ void restore_fast(float (&acc)[kLT], const uint32_t (&p)[kLT],
+                                             float sx, const float *__restrict__ sw) {
 #pragma unroll
-    for (int j4 = 0; j4 < kLT; j4 += 4) {
-      const float4 s4 = *reinterpret_cast<const float4 *>(sw + j4);
-      const float s[4] = {s4.x, s4.y, s4.z, s4.w};
+  for (int j4 = 0; j4 < kLT; j4 += 4) {
+    const float4 s4 = *reinterpret_cast<const float4 *>(sw + j4);
+    const float s[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-      for (int j = 0; j < 4; j += 2) {
-        // Two dots per packed f32x2 operation (each half rounds as fmaf).
-        float v0, v1;
-        const uint32_t b0 = kAddBias ? p[j4 + j] + kDotBias : p[j4 + j] | kDotBias;
-        const uint32_t b1 = kAddBias ? p[j4 + j + 1] + kDotBias : p[j4 + j + 1] | kDotBias;
-        fma2(__uint_as_float(b0), __uint_as_float(b1),
-             sx, sx, nsx, nsx, v0, v1);
-        const float q0 = __uint_as_float(__float_as_uint(v0) & 0xffff0000u);
-        const float q1 = __uint_as_float(__float_as_uint(v1) & 0xffff0000u);
-        if (kInit)
-          mul2(q0, q1, s[j], s[j + 1], acc[j4 + j], acc[j4 + j + 1]);
-        else
-          fma2(q0, q1, s[j], s[j + 1], acc[j4 + j], acc[j4 + j + 1], acc[j4 + j],
-               acc[j4 + j + 1]);
-      }
+    for (int j = 0; j < 4; ++j) {
+      const float v = __fmul_rn(__uint_as_float(p[j4 + j]), sx);
+      const float q = __uint_as_float(__float_as_uint(v) & 0xffff0000u);
+      acc[j4 + j] = kInit ? __fmul_rn(q, s[j]) : __fmaf_rn(q, s[j], acc[j4 + j]);
     }
-  } else {
-    for (int j = 0; j < kLT; ++j)
-      acc[j] = tc_slow_tile_add(kInit ? 0.0f : acc[j], static_cast<int>(p[j]),
-                                exB[ew_index + j], ex, status);
   }
+}
+
+// The exact integer restore of the tile values of rows outside the fast
+// window (subnormal or overflowing tiles), added to sums that the fast pass
+// left unchanged for them.
+template <int kLT>
+__device__ __forceinline__ void restore_slow_rows(float (&acc)[kLT], const uint32_t (&p)[kLT],
+                                                  const int32_t *__restrict__ exB,
+                                                  int64_t ew_index, int ex, int32_t *status) {
+#pragma unroll
+  for (int j = 0; j < kLT; ++j)
+    acc[j] = tc_slow_tile_add(acc[j], static_cast<int>(p[j]), exB[ew_index + j], ex, status);
 }
 
 // Address of the residual addend of one output row's first lane (laid out
@@ -573,14 +588,16 @@ __global__ void __launch_bounds__(kSThreads, 1)
   using S = SSShape<kAB>;
   constexpr int L = S::L, LT = S::LT, SN = S::N;
   extern __shared__ uint8_t smem_raw[];
-  SmemSS<kAB> &s = *reinterpret_cast<SmemSS<kAB> *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
+  SmemSS<kAB> &s = smem_aligned<SmemSS<kAB>>(smem_raw);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int num_kb = (T + 1) / 2;
   const int num_nb = (N + L - 1) / L;
   const int num_tiles = ((M + kSBM - 1) / kSBM) * num_nb;
   const int32_t *ranges = exB + int64_t{2} * T * n_pad; // [T][n_pad / 32][4]
-  const float *scales = reinterpret_cast<const float *>(ranges + int64_t{n_pad / 32} * T * 4);
+  // The epilogue's weight scales 2^(Ew - 133 + kScaleShift) follow the plain
+  // scales 2^(Ew - 133) [2][T][n_pad] that the CUDA-core kernels read.
+  const float *scales =
+      reinterpret_cast<const float *>(ranges + int64_t{n_pad / 32} * T * 4) + 2 * T * n_pad;
   constexpr uint32_t kTmemCols = kTmemBufs * kBufCols;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSStages; ++i) {
@@ -726,8 +743,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
           hi = max(hi, e.range[5]);
         }
         // Fast window for this tile's weights: ex_lo <= Ex <= ex_hi.
-        const int ex_lo = max(7, 140 - lo), ex_hi = min(237, 374 - hi);
-        float sx[kAB], nsx[kAB];
+        const int ex_lo = max(kScaleShift + 7, 140 - lo);
+        const int ex_hi = hi <= 260 - kScaleShift ? min(kScaleShift + 111, 374 - hi) : -1;
+        float sx[kAB];
         bool fast[kAB];
         int ex[kAB];
 #pragma unroll
@@ -737,9 +755,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
           const bool window = ex[a] >= ex_lo && ex[a] <= ex_hi;
           fast[a] = zero || window;
           // 2^(Ex - 133), a normal f32 inside the window (Ex >= 7).
-          sx[a] = window && !zero ? __uint_as_float(static_cast<uint32_t>(ex[a] - 6) << 23)
-                                  : 0.0f;
-          nsx[a] = -8388608.0f * sx[a];
+          // 2^(Ex + 16 - kScaleShift), a normal f32 inside the window.
+          sx[a] = window && !zero
+                      ? __uint_as_float(static_cast<uint32_t>(ex[a] + 143 - kScaleShift) << 23)
+                      : 0.0f;
         }
         if (!mbar_wait(&s.dfull[buf], (gi / kTmemBufs) & 1) || *failed) {
           ok = false;
@@ -747,27 +766,53 @@ __global__ void __launch_bounds__(kSThreads, 1)
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t col0 = tmem + tlane + buf * kBufCols + sub * LT;
-        // Index of this thread's weight exponents exB[w][t][lane0] (exact path).
-        const int64_t ew0 = static_cast<int64_t>(t) * n_pad + lane0;
-        const int64_t ew1 = ew0 + static_cast<int64_t>(T) * n_pad;
-        // One activation branch at a time: 2 x LT dots in registers.
+        if constexpr (kAB == 1) {
+          // 2-branch layers (LT = 16): one weight sign at a time, 16 dots in
+          // registers (measured faster than both signs at once: fewer live
+          // registers under the 96-register budget of 576 threads).
 #pragma unroll
-        for (int a = 0; a < kAB; ++a) {
-          uint32_t p0[LT], p1[LT];
-          tmem_ld(col0 + a * SN, p0);
-          tmem_ld(col0 + a * SN + L, p1);
-          tmem_wait(p0);
-          tmem_wait(p1);
-          if (t == 0) {
-            restore_add<LT, true, kAB == 1>(acc[a][0], p0, fast[a], sx[a], nsx[a], &e.w[0][sub * LT],
-                                  exB, ew0, ex[a], status);
-            restore_add<LT, true, kAB == 1>(acc[a][1], p1, fast[a], sx[a], nsx[a], &e.w[1][sub * LT],
-                                  exB, ew1, ex[a], status);
-          } else {
-            restore_add<LT, false, kAB == 1>(acc[a][0], p0, fast[a], sx[a], nsx[a], &e.w[0][sub * LT],
-                                   exB, ew0, ex[a], status);
-            restore_add<LT, false, kAB == 1>(acc[a][1], p1, fast[a], sx[a], nsx[a], &e.w[1][sub * LT],
-                                   exB, ew1, ex[a], status);
+          for (int w = 0; w < 2; ++w) {
+            uint32_t p[LT];
+            tmem_ld(col0 + w * L, p);
+            tmem_wait(p);
+            if (t == 0)
+              restore_fast<LT, true>(acc[0][w], p, sx[0], &e.w[w][sub * LT]);
+            else
+              restore_fast<LT, false>(acc[0][w], p, sx[0], &e.w[w][sub * LT]);
+            // One warp-uniform test: rows outside the window (rare) add their
+            // exact tile values to the sums the fast pass kept.
+            if (__any_sync(0xffffffffu, !fast[0])) {
+              if (!fast[0])
+                restore_slow_rows<LT>(acc[0][w], p, exB,
+                                      (static_cast<int64_t>(w) * T + t) * n_pad + lane0, ex[0],
+                                      status);
+            }
+          }
+        } else {
+          // 4-branch layers (LT = 8): both weight signs of one activation
+          // branch at a time, 2 x 8 dots in registers.
+#pragma unroll
+          for (int a = 0; a < kAB; ++a) {
+            uint32_t p0[LT], p1[LT];
+            tmem_ld(col0 + a * SN, p0);
+            tmem_ld(col0 + a * SN + L, p1);
+            tmem_wait(p0);
+            tmem_wait(p1);
+            if (t == 0) {
+              restore_fast<LT, true>(acc[a][0], p0, sx[a], &e.w[0][sub * LT]);
+              restore_fast<LT, true>(acc[a][1], p1, sx[a], &e.w[1][sub * LT]);
+            } else {
+              restore_fast<LT, false>(acc[a][0], p0, sx[a], &e.w[0][sub * LT]);
+              restore_fast<LT, false>(acc[a][1], p1, sx[a], &e.w[1][sub * LT]);
+            }
+            if (__any_sync(0xffffffffu, !fast[a])) {
+              if (!fast[a]) {
+                const int64_t ew0 = static_cast<int64_t>(t) * n_pad + lane0;
+                restore_slow_rows<LT>(acc[a][0], p0, exB, ew0, ex[a], status);
+                restore_slow_rows<LT>(acc[a][1], p1, exB, ew0 + static_cast<int64_t>(T) * n_pad,
+                                      ex[a], status);
+              }
+            }
           }
         }
         // Hand the TMEM buffer and the exponent slot back once every lane
@@ -841,8 +886,7 @@ __global__ void __launch_bounds__(kIThreads, 1)
                            int out_pixels, FastDiv div_pix, int vec, int32_t *__restrict__ y,
                            int32_t *status) {
   extern __shared__ uint8_t smem_raw[];
-  SmemI8P &s = *reinterpret_cast<SmemI8P *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                            ~uintptr_t{1023});
+  SmemI8P &s = smem_aligned<SmemI8P>(smem_raw);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int num_tiles = num_mb * ((N + kIBN - 1) / kIBN);
   if (threadIdx.x == 0) {
@@ -1162,7 +1206,35 @@ bool launch_int8(const int8_t *A, int64_t a_rows, int64_t a_cols, const int8_t *
   return true;
 }
 
+// One CTA waits, with the pipelines' bounded wait, on an mbarrier that
+// nothing completes: the wait gives up after limit_ns and the kernel reports
+// CIM22_STATUS_TIMEOUT. It holds no TMEM and issues no copies, so its
+// return leaves nothing in flight.
+__global__ void wait_timeout_kernel(uint64_t limit_ns, int32_t *status) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const bool done = mbar_wait(&bar, 0, limit_ns);
+  if (!done && threadIdx.x == 0)
+    atomicOr(status, CIM22_STATUS_TIMEOUT);
+  __syncthreads();
+}
+
 } // namespace cim::tc
+
+extern "C" int cim22_cuda_check_wait_timeout(uint64_t limit_ns, int32_t *status, void *stream) {
+  if (!status || limit_ns == 0 || limit_ns > 10000000000ull) {
+    cim::set_last_error("cim22_cuda_check_wait_timeout: status must be a device int32 and "
+                        "0 < limit_ns <= 10 s");
+    return CIM22_STATUS_BAD_ARGUMENT;
+  }
+  cim::tc::wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns,
+                                                                               status);
+  return cim::cuda_ok(cudaGetLastError(), "wait check launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+}
 
 extern "C" int64_t cim22_cuda_tensor_core_launches(void) {
   return cim::tc::g_tc_launches.load(std::memory_order_relaxed);

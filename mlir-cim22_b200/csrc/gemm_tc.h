@@ -6,6 +6,13 @@
 
 namespace cim::tc {
 
+// The weight scales of the sign-split contraction are stored as
+// 2^(Ew - 133 + kScaleShift): the epilogue reads each crossbar dot p as the
+// f32 subnormal p * 2^-149 and multiplies it by 2^(Ex + 16 - kScaleShift),
+// which is exact and normal for 67 <= Ex <= 171, so the product with the
+// shifted weight scale is Q(p) * 2^(Ex + Ew - 266) as before.
+constexpr int kScaleShift = 60;
+
 // True when the tcgen05 kernels are compiled in and the current device is an
 // sm_100 part.
 bool signsplit_available();
@@ -16,7 +23,8 @@ bool int8_available();
 // [act_branches][T][m_pad], B int8 [2 * n_pad][k_pad] (Wp rows, then Wn),
 // exB int32 [2][T][n_pad] followed by the weight-exponent ranges
 // [T][n_pad / 32][4] = {min, max, 0, 0} over both signs of each tile and
-// 32-lane block, and by the f32 weight scales 2^(Ew - 133) [2][T][n_pad]. Returns false when the shape is not handled by the tensor-core
+// 32-lane block, by the f32 weight scales 2^(Ew - 133) [2][T][n_pad] and by
+// the epilogue's f32 scales 2^(Ew - 133 + kScaleShift) [2][T][n_pad]. Returns false when the shape is not handled by the tensor-core
 // kernel, in which case nothing was launched. out_pixels = 0 writes y as
 // rows [M][N]; out_pixels > 0 writes NCHW images [M / out_pixels][N][out_pixels].
 // A non-null post_scale applies fma(out, post_scale[n], post_shift[n]) after

@@ -1589,7 +1589,7 @@ static void prepare_bf16_weights(const float *w, int64_t n, int64_t k,
                                  std::vector<int8_t> &mant,
                                  std::vector<int32_t> &exps) {
   mant.assign(2 * n_pad * k_pad, 0);
-  exps.assign(2 * T * n_pad + (n_pad / 32) * T * 4 + 2 * T * n_pad, 127);
+  exps.assign(2 * T * n_pad + (n_pad / 32) * T * 4 + 4 * T * n_pad, 127);
   uint16_t group[kTileK];
   for (int b = 0; b < 2; ++b)
     for (int64_t lane = 0; lane < n; ++lane)
@@ -1638,11 +1638,17 @@ static void prepare_bf16_weights(const float *w, int64_t n, int64_t k,
       r[2] = r[3] = 0;
     }
   // The weight scales 2^(Ew - 133) as f32 bit patterns (exact: Ew - 133 lies
-  // in [-133, 121], inside f32's normal and subnormal range).
+  // in [-133, 121], inside f32's normal and subnormal range), then the
+  // tensor-core epilogue's 2^(Ew - 133 + kScaleShift) (normal for
+  // Ew <= 260 - kScaleShift; tiles with a larger exponent take the exact
+  // integer restore, so the clamp is never used).
   int32_t *scales = ranges + (n_pad / 32) * T * 4;
+  int32_t *tc_scales = scales + 2 * T * n_pad;
   for (int64_t i = 0; i < 2 * T * n_pad; ++i) {
     const float f = std::ldexp(1.0f, exps[i] - 133);
     std::memcpy(&scales[i], &f, 4);
+    const float g = std::ldexp(1.0f, std::min(exps[i] - 133 + tc::kScaleShift, 127));
+    std::memcpy(&tc_scales[i], &g, 4);
   }
 }
 

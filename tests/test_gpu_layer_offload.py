@@ -3,6 +3,8 @@ model run as CIM layers on the GPU, the rest of the model on CPU, and the
 outputs equal the oracle's forward that computes exactly those layers as CIM
 layers (the rest as PyTorch CPU eager) - bit for bit."""
 
+import copy
+
 import numpy as np
 import pytest
 import torch
@@ -19,18 +21,23 @@ def test_layer_offload_matches_oracle_on_selected_layers(name, selected):
     from cim22_b200 import layers, workloads
 
     model, x = workloads.build(name, 3, seed=5)
+    # The oracle runs on its own copy: the offloaded model's selected leaves
+    # are compiled in place (the reference asks for a separate instance too).
+    reference = copy.deepcopy(model)
     offload = layers.LayerOffload(model, selected, (x,))
     assert offload.cim_layers == tuple(selected)
     assert set(offload.layer_compile_seconds) == set(selected)
     got = offload(x)
     assert got.device.type == "cpu"
     assert offload.dispatch_count >= len(selected)
-    expected = oracle.cim_forward(model, x.numpy(), branches=4, threads=4, layers=selected)
+    expected = oracle.cim_forward(reference, x.numpy(), branches=4, threads=4,
+                                  layers=selected)
     np.testing.assert_array_equal(got.numpy().view(np.uint32), expected.view(np.uint32))
     # Another batch of the same shape reuses the compiled layers.
     _, x2 = workloads.build(name, 3, seed=6)
     got2 = offload(x2)
-    expected2 = oracle.cim_forward(model, x2.numpy(), branches=4, threads=4, layers=selected)
+    expected2 = oracle.cim_forward(reference, x2.numpy(), branches=4, threads=4,
+                                   layers=selected)
     np.testing.assert_array_equal(got2.numpy().view(np.uint32), expected2.view(np.uint32))
 
 
