@@ -266,12 +266,14 @@ __device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
       m2 = __vmaxu2(m2, branch_pair<kActBranches>(signed_pairs[e], a));
     mx[a] = max(m2 & 0xffffu, m2 >> 16);
   }
-  // Non-finite groups: BF16 exponent 0xff in the 2-branch maximum, |x| of
-  // the raw inputs otherwise (the max with 0 drops NaN).
-  const bool nonfinite = kActBranches == 2 ? raw_max >= 0x7f7f8000u : mx[0] >= 0x7f80u;
+  // Non-finite groups: BF16 exponent 0xff in a branch maximum (the two
+  // branches of a 4-branch layer hold every magnitude between them, NaNs
+  // included). A 2-branch layer flags a negative nonzero BF16 input, the
+  // reference's sign-split rejection (-0 is cleared to +0).
+  const bool nonfinite = max(mx[0], mx[1]) >= 0x7f80u;
   if (nonfinite)
     atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-  else if (kActBranches == 1 && raw_max > 0x80000000u)
+  else if (kActBranches == 1 && max(raw_max & 0xffffu, raw_max >> 16) > 0x8000u)
     atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
   // Pass 2: align and store.
 #pragma unroll
@@ -360,8 +362,7 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
   const int m = (chunk0 + r) * 256 + static_cast<int>(threadIdx.x);
   if (m >= m_pad)
     break; // whole warps: m_pad is a multiple of 128
-  const float *img = x;
-  int org = 0;
+  const float *base = x; // the column's window origin (may lie before the image)
   unsigned long long inb = 0; // in-bounds elements of this column
   if (m < g.M) {
     const int n = fdiv(m, g.div_ohw);
@@ -369,15 +370,16 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
     const int oh = fdiv(rm, g.div_ow);
     const int ow = rm - oh * g.OW;
     const int ih0 = oh * g.SH - g.PH, iw0 = ow * g.SW - g.PW;
-    img = x + static_cast<int64_t>(n) * g.image;
-    org = ih0 * g.sH + iw0 * g.sW;
+    base = x + static_cast<int64_t>(n) * g.image + (ih0 * g.sH + iw0 * g.sW);
     const int rlo = min(max(-ih0, 0), g.KH), rhi = max(min(g.H - ih0, g.KH), rlo);
     const int clo = min(max(-iw0, 0), g.KW), chi = max(min(g.W - iw0, g.KW), clo);
     inb = (sRows[rhi] & ~sRows[rlo]) & (sCols[chi] & ~sCols[clo]);
   }
-  // Pass 1: gather, round to signed BF16 pairs, track the raw maximum. The
-  // loads of the next 16 elements are issued before the current 16 are
-  // converted, so that two chunks of loads are in flight.
+  // Pass 1: gather and round to signed BF16 pairs (for a 2-branch layer,
+  // also their largest bit pattern as unsigned halves: above 0x8000 exactly
+  // when some BF16 input is negative and nonzero). The loads of the next 16
+  // elements are issued before the current 16 are converted, so that two
+  // chunks of loads are in flight.
   uint32_t signed_pairs[32];
   uint32_t raw_max = 0;
   auto load_chunk = [&](int chunk, float (&v)[16]) {
@@ -395,7 +397,7 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
 #pragma unroll
       for (int e = 0; e < 4; ++e)
         v[e4 + e] = (inb >> (chunk + e4 + e)) & 1ull
-                        ? window_load<kMode, kPool>(img, g, org + r4[e])
+                        ? window_load<kMode, kPool>(base, g, r4[e])
                         : 0.0f;
     }
   };
@@ -412,11 +414,8 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
       const int q = (chunk + e) / 2;
       const __nv_bfloat162 h = __floats2bfloat162_rn(v[e], v[e + 1]);
       signed_pairs[q] = *reinterpret_cast<const uint32_t *>(&h);
-      if (kActBranches == 2)
-        raw_max = max(raw_max, max(__float_as_uint(v[e]) & 0x7fffffffu,
-                                   __float_as_uint(v[e + 1]) & 0x7fffffffu));
-      else
-        raw_max = max(raw_max, max(__float_as_uint(v[e]), __float_as_uint(v[e + 1])));
+      if (kActBranches == 1)
+        raw_max = __vmaxu2(raw_max, signed_pairs[q]);
     }
   }
   finish_group<kActBranches>(signed_pairs, raw_max, status, A, ex, m_pad, k_pad, T, t, m,
@@ -820,11 +819,8 @@ __device__ __forceinline__ bool direct_prepare(const float *__restrict__ x, cons
     for (int e = 0; e < 8; e += 2) {
       const __nv_bfloat162 h = __floats2bfloat162_rn(v[e], v[e + 1]);
       signed_pairs[(chunk + e) / 2] = *reinterpret_cast<const uint32_t *>(&h);
-      if (kActBranches == 2)
-        raw_max = max(raw_max, max(__float_as_uint(v[e]) & 0x7fffffffu,
-                                   __float_as_uint(v[e + 1]) & 0x7fffffffu));
-      else
-        raw_max = max(raw_max, max(__float_as_uint(v[e]), __float_as_uint(v[e + 1])));
+      if (kActBranches == 1)
+        raw_max = __vmaxu2(raw_max, signed_pairs[(chunk + e) / 2]);
     }
   }
   uint32_t mx[2] = {0, 0};
@@ -836,12 +832,14 @@ __device__ __forceinline__ bool direct_prepare(const float *__restrict__ x, cons
       m2 = __vmaxu2(m2, branch_pair<kActBranches>(signed_pairs[e], a));
     mx[a] = max(m2 & 0xffffu, m2 >> 16);
   }
-  // Non-finite groups: BF16 exponent 0xff in the 2-branch maximum, |x| of
-  // the raw inputs otherwise (the max with 0 drops NaN).
-  const bool nonfinite = kActBranches == 2 ? raw_max >= 0x7f7f8000u : mx[0] >= 0x7f80u;
+  // Non-finite groups: BF16 exponent 0xff in a branch maximum (the two
+  // branches of a 4-branch layer hold every magnitude between them, NaNs
+  // included). A 2-branch layer flags a negative nonzero BF16 input, the
+  // reference's sign-split rejection (-0 is cleared to +0).
+  const bool nonfinite = max(mx[0], mx[1]) >= 0x7f80u;
   if (nonfinite)
     atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-  else if (kActBranches == 1 && raw_max > 0x80000000u)
+  else if (kActBranches == 1 && max(raw_max & 0xffffu, raw_max >> 16) > 0x8000u)
     atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
   bool fast = true;
 #pragma unroll

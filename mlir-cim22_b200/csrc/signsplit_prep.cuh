@@ -46,8 +46,10 @@ constexpr int kGroupThreads = 8;
 // activation branch a in pairs (element 2e in the low half), mx[a] their
 // maximum. flags accumulates what marks a group: for 4-branch layers the
 // largest |x| bit pattern (non-finite when >= 0x7f7f8000: NaN, infinity or a
-// value that rounds to BF16 infinity), for 2-branch layers the largest raw
-// bit pattern (negative when > 0x80000000).
+// value that rounds to BF16 infinity), for 2-branch layers the largest BF16
+// bit pattern of either half (above 0x8000 exactly when some input rounds to
+// a negative nonzero BF16 value, which the reference's sign split rejects;
+// -0 is cleared to +0).
 template <int kActBranches>
 __device__ __forceinline__ void split8(const float (&v)[8], uint32_t (&packed)[2][4],
                                        uint32_t (&mx)[2], uint32_t &flags) {
@@ -65,12 +67,11 @@ __device__ __forceinline__ void split8(const float (&v)[8], uint32_t (&packed)[2
     }
   } else {
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      flags = max(flags, __float_as_uint(v[e]));
-#pragma unroll
     for (int e = 0; e < 8; e += 2) {
       const __nv_bfloat162 hp = __floats2bfloat162_rn(v[e], v[e + 1]);
-      packed[0][e / 2] = *reinterpret_cast<const uint32_t *>(&hp) & 0x7fff7fffu;
+      const uint32_t bits = *reinterpret_cast<const uint32_t *>(&hp);
+      flags = __vmaxu2(flags, bits);
+      packed[0][e / 2] = bits & 0x7fff7fffu;
     }
   }
 #pragma unroll
@@ -92,7 +93,7 @@ __device__ __forceinline__ void group_exponents(uint32_t (&mx)[2], uint32_t flag
   const bool nonfinite = mx[0] >= 0x7f80u;
   if (report && nonfinite)
     atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-  if (kActBranches == 1 && flags > 0x80000000u && !nonfinite)
+  if (kActBranches == 1 && max(flags & 0xffffu, flags >> 16) > 0x8000u && !nonfinite)
     atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
 #pragma unroll
   for (int a = 0; a < kActBranches; ++a) {
