@@ -397,9 +397,23 @@ def roofline(prog, workload: str, batch: int, avg: dict) -> dict:
         tensor, hbm = ops, nbytes
     elif step.cim and info is not None:
         ops = 2 * info.macs
-        nbytes = info.in_bytes + 2 * info.n * info.k + 4 * info.m * info.n
-        what = ("CIM layer: ops = 2 x branches x M x K x N (unpadded); bytes = source read "
-                "once + int8 weights of both signs + f32 output")
+        ab = 1 if info.branches == 2 else 2
+        t_tiles = -(-info.k // 64)
+        m_pad = -(-info.m // 128) * 128
+        if step.meta.get("x") is not None and dominant.split("#")[0] + ".prepare" in names:
+            # The contraction of a two-kernel layer reads the prepared int8
+            # columns and their group exponents, not the source image.
+            src = ab * m_pad * t_tiles * (64 + 4)
+            what = ("CIM contraction: ops = 2 x branches x M x K x N (unpadded); bytes = "
+                    "prepared int8 columns + group exponents + int8 weights of both signs + "
+                    "f32 output (+ f32 residual addend)")
+        else:
+            src = info.in_bytes
+            what = ("CIM layer: ops = 2 x branches x M x K x N (unpadded); bytes = source read "
+                    "once + int8 weights of both signs + f32 output (+ f32 residual addend)")
+        nbytes = src + 2 * info.n * info.k + 4 * info.m * info.n
+        if step.meta.get("residual") is not None:
+            nbytes += 4 * info.m * info.n
         tensor, hbm = ops, nbytes
     elif info is not None and dominant.endswith(".prepare"):
         ab = 1 if info.branches == 2 else 2
