@@ -1073,6 +1073,27 @@ bool encode_int8_2d(CUtensorMap *map, const void *base, uint64_t rows, uint64_t 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+} // namespace
+
+// 4-D f32 tensor [N][C][H][W] (W contiguous, W % 4 == 0), box
+// [nb][cb][hb][wb], no swizzle; out-of-range elements of a box read as +0.
+bool encode_nchw_box(CUtensorMap *map, const float *x, uint64_t W, uint64_t H, uint64_t C,
+                     uint64_t N, uint32_t wb, uint32_t hb, uint32_t cb, uint32_t nb) {
+  auto fn = encode_fn();
+  if (!fn)
+    return false;
+  const cuuint64_t dims[4] = {W, H, C, N};
+  const cuuint64_t strides[3] = {W * 4, H * W * 4, C * H * W * 4};
+  const cuuint32_t box[4] = {wb, hb, cb, nb};
+  const cuuint32_t elem[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(x), dims, strides, box,
+            elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+namespace {
+
 bool sm100(cudaStream_t) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess)

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace cim::tc {
@@ -46,5 +47,11 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad,
 bool launch_int8(const int8_t *A, int64_t a_rows, int64_t a_cols, const int8_t *B,
                  int64_t n_pad, int64_t k_pad, int64_t M, int64_t N, const int32_t *bias,
                  int64_t out_pixels, int32_t *y, int32_t *status, cudaStream_t stream);
+
+// Tensor map of an f32 NCHW tensor [N][C][H][W] (W contiguous, W % 4 == 0,
+// 16-byte aligned) for per-CTA loads of [nb][cb][hb][wb] boxes; elements
+// outside the tensor read as +0. False when the driver rejects it.
+bool encode_nchw_box(CUtensorMap *map, const float *x, uint64_t W, uint64_t H, uint64_t C,
+                     uint64_t N, uint32_t wb, uint32_t hb, uint32_t cb, uint32_t nb);
 
 } // namespace cim::tc

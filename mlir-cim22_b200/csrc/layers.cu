@@ -21,6 +21,7 @@
 #include <cuda_bf16.h>
 #include "gemm_tc.h"
 #include "signsplit_prep.cuh"
+#include "tma_util.cuh"
 
 #include <algorithm>
 #include <climits>
@@ -424,6 +425,148 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
 }
 
 
+
+// NCHW convolution gathers staged by TMA: a block serves 256 consecutive
+// columns (whole output rows of one image, or whole images) and one K tile.
+// One bulk-tensor copy brings the input window those columns read - the
+// tile's channels, the rows and columns of its kernel windows, with the
+// padding - into shared memory; the copy reads the zero padding itself
+// (elements outside the image read as +0), so the gather has no bounds
+// tests and every element is one shared-memory load at a column base plus a
+// per-tile offset (the last K tile of a layer whose K is not a multiple of 64
+// takes zeros for the elements past K). Then the same split, rounding,
+// prealign and stores as prepare_nchw_kernel.
+struct BoxGather {
+  int wb, hb, cb, nb; // box extents: columns, rows, channels, images
+  int x0;             // first box column (a multiple of 4, <= -PW)
+  int words;          // wb * hb * cb * nb
+};
+
+template <int kActBranches>
+__global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
+    prepare_nchw_box_kernel(const __grid_constant__ CUtensorMap map, Gather32 g, BoxGather b,
+                            FastDiv div_chunks, int T, int m_pad, int k_pad,
+                            int8_t *__restrict__ A, int32_t *__restrict__ ex, int32_t *status) {
+  extern __shared__ __align__(128) unsigned char box_raw[];
+  // The copy's destination, rounded up to 128 bytes (the launch adds them).
+  float *sbox = reinterpret_cast<float *>(box_raw + ((128u - (shared_addr(box_raw) & 127u)) & 127u));
+  __shared__ __align__(16) int sRel[kTileK];
+  __shared__ __align__(8) uint64_t bar;
+  pdl_launch_dependents();
+  const int blk = static_cast<int>(blockIdx.x);
+  const int t = fdiv(blk, div_chunks);
+  const int m0 = (blk - t * static_cast<int>(div_chunks.d)) * 256;
+  const int kbeg = t * kTileK;
+  const int khw = g.KH * g.KW;
+  const int c0 = kbeg / khw;
+  const int hw = g.OH * g.OW;
+  const int n0 = fdiv(m0, g.div_ohw);
+  // First input row of the box: the block's first output row's window, or
+  // the image's top padding when the block holds whole images.
+  const int ih0 = hw >= 256 ? fdiv(m0 - n0 * hw, g.div_ow) * g.SH - g.PH : -g.PH;
+  if (threadIdx.x == 0)
+    barrier_init(&bar, 1);
+  if (threadIdx.x < kTileK) {
+    const int k = kbeg + static_cast<int>(threadIdx.x);
+    const int c = fdiv(k, g.div_khw);
+    const int rk = k - c * khw;
+    const int i = fdiv(rk, g.div_kw);
+    const int j = rk - i * g.KW;
+    sRel[threadIdx.x] = k < g.K ? ((c - c0) * b.hb + i) * b.wb + j : -1;
+  }
+  __syncthreads();
+  pdl_wait();
+  if (threadIdx.x == 0) {
+    barrier_expect_tx(&bar, static_cast<uint32_t>(b.words) * 4u);
+    tma_load_4d(sbox, &map, &bar, b.x0, ih0, c0, n0);
+  }
+  if (!barrier_wait(&bar, 0)) {
+    if (threadIdx.x == 0)
+      atomicOr(status, CIM22_STATUS_TIMEOUT);
+    return;
+  }
+  const int m = m0 + static_cast<int>(threadIdx.x);
+  if (m >= m_pad)
+    return; // whole warps: m_pad is a multiple of 128
+  uint32_t signed_pairs[32];
+  uint32_t raw_max = 0;
+  if (m < g.M) {
+    const int n = fdiv(m, g.div_ohw);
+    const int rm = m - n * hw;
+    const int oh = fdiv(rm, g.div_ow);
+    const int ow = rm - oh * g.OW;
+    const float *base = sbox + ((n - n0) * b.cb * b.hb + (oh * g.SH - g.PH - ih0)) * b.wb +
+                        (ow * g.SW - g.PW - b.x0);
+    auto convert4 = [&](int e4, float v0, float v1, float v2, float v3) {
+      const __nv_bfloat162 h0 = __floats2bfloat162_rn(v0, v1);
+      const __nv_bfloat162 h1 = __floats2bfloat162_rn(v2, v3);
+      signed_pairs[e4 / 2] = *reinterpret_cast<const uint32_t *>(&h0);
+      signed_pairs[e4 / 2 + 1] = *reinterpret_cast<const uint32_t *>(&h1);
+      if (kActBranches == 1)
+        raw_max = __vmaxu2(raw_max, __vmaxu2(signed_pairs[e4 / 2], signed_pairs[e4 / 2 + 1]));
+    };
+    if (kbeg + kTileK <= g.K) {
+#pragma unroll
+      for (int e4 = 0; e4 < kTileK; e4 += 4) {
+        const int4 rel = *reinterpret_cast<const int4 *>(&sRel[e4]);
+        convert4(e4, base[rel.x], base[rel.y], base[rel.z], base[rel.w]);
+      }
+    } else {
+      // The layer's last K tile with elements past K (offset -1): zeros.
+#pragma unroll
+      for (int e4 = 0; e4 < kTileK; e4 += 4) {
+        const int4 rel = *reinterpret_cast<const int4 *>(&sRel[e4]);
+        convert4(e4, rel.x < 0 ? 0.0f : base[rel.x], rel.y < 0 ? 0.0f : base[rel.y],
+                 rel.z < 0 ? 0.0f : base[rel.z], rel.w < 0 ? 0.0f : base[rel.w]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 32; ++q)
+      signed_pairs[q] = 0; // a padding column: an all-zero group
+  }
+  finish_group<kActBranches>(signed_pairs, raw_max, status, A, ex, m_pad, k_pad, T, t, m,
+                             kbeg);
+}
+
+// The box of the TMA-staged gather for a layer, or false when its columns do
+// not tile into whole output rows or whole images per 256-column block, the
+// image rows are not 16-byte multiples, or the box exceeds kBoxSmemLimit.
+constexpr int kBoxSmemLimit = 47 * 1024;
+
+static bool plan_box_gather(const Gather32 &g, const float *x, int T, BoxGather &b) {
+  if (g.kind != CIM22_GATHER_CONV_NCHW || g.PK != 0 || (g.W & 3) != 0 ||
+      (reinterpret_cast<uintptr_t>(x) & 15) != 0 || g.sW != 1 || g.sH != g.W ||
+      g.sC != g.H * g.W)
+    return false;
+  const int hw = g.OH * g.OW;
+  if (hw >= 256) {
+    if (256 % g.OW != 0 || hw % 256 != 0)
+      return false;
+    b.nb = 1;
+    b.hb = (256 / g.OW - 1) * g.SH + g.KH;
+  } else {
+    if (256 % hw != 0)
+      return false;
+    b.nb = 256 / hw;
+    b.hb = (g.OH - 1) * g.SH + g.KH;
+  }
+  b.x0 = -((g.PW + 3) / 4) * 4;
+  b.wb = (((g.OW - 1) * g.SW - g.PW + g.KW - b.x0) + 3) / 4 * 4;
+  const int khw = g.KH * g.KW;
+  b.cb = 0;
+  for (int t = 0; t < T; ++t) {
+    const int lo = t * kTileK / khw, hi = std::min(g.C - 1, (t * kTileK + kTileK - 1) / khw);
+    b.cb = std::max(b.cb, hi - lo + 1);
+  }
+  if (b.wb > 256 || b.hb > 256 || b.cb > 256 || b.nb > 256)
+    return false;
+  const int64_t words = int64_t{b.wb} * b.hb * b.cb * b.nb;
+  if (words * 4 + 128 > kBoxSmemLimit)
+    return false;
+  b.words = static_cast<int>(words);
+  return true;
+}
 
 // ---------------------------------------------------------------------------
 // Sign-split contraction on CUDA cores (dp4a). CTA tile kBM columns x kBN
@@ -1901,6 +2044,29 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
     else
       go(prepare_mode_kernel<kPrepConvPool>);
     return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+  }
+  // Convolutions whose 256-column blocks cover whole output rows or whole
+  // images gather from a TMA-staged window in shared memory.
+  BoxGather box{};
+  if (tc::signsplit_available() && plan_box_gather(dg, x, T, box)) {
+    CUtensorMap map;
+    const int n_images = static_cast<int>(g.batch);
+    if (tc::encode_nchw_box(&map, x, dg.W, dg.H, dg.C, n_images, box.wb, box.hb, box.cb,
+                            box.nb)) {
+      const int64_t chunks = (m_pad + 255) / 256;
+      const FastDiv div_chunks = make_fastdiv(static_cast<uint32_t>(chunks));
+      const unsigned blocks = static_cast<unsigned>(chunks * T);
+      const size_t smem = static_cast<size_t>(box.words) * sizeof(float) + 128;
+      auto launch = [&](auto kernel) {
+        launch_pdl(kernel, blocks, 256, smem, s, map, dg, box, div_chunks, T,
+                   static_cast<int>(m_pad), static_cast<int>(layer->k_pad), A, ex, status);
+      };
+      if (ab == 1)
+        launch(prepare_nchw_box_kernel<1>);
+      else
+        launch(prepare_nchw_box_kernel<2>);
+      return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+    }
   }
   // The thread-per-group NCHW kernel serves convolutions over enough columns
   // to fill the GPU (measured 1.3-1.6x faster than the kernel below on

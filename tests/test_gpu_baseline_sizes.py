@@ -180,19 +180,24 @@ def prepare_schedule(m, T):
     return per_block
 
 
-@pytest.mark.parametrize("batch,branches,pool,per_block", [
-    (140, 2, 0, 2), (264, 2, 0, 4), (264, 4, 0, 4), (264, 2, 2, 4), (140, 4, 2, 2)])
-def test_prepare_nchw_several_chunks_per_block(batch, branches, pool, per_block):
-    """A 64 -> 64 channel 3x3 conv over 32x32 outputs (ResNet-18's first
-    stage, T = 9) at batches that give the prepare kernel two or four chunks
-    of 256 columns per block, 2 and 4 branches, with and without a fused 2x2
-    max pool: the whole output equals the NHWC input path's (a different
-    prepare kernel) bit for bit, and sampled columns equal the oracle's."""
+@pytest.mark.parametrize("batch,h,branches,pool,per_block", [
+    (140, 32, 2, 0, 2), (264, 32, 2, 0, 4), (264, 32, 4, 0, 4),   # TMA-staged window
+    (264, 32, 2, 2, 4), (140, 32, 4, 2, 2),                       # fused 2x2 pool
+    (150, 30, 2, 0, 2), (300, 30, 4, 0, 4)])                      # rows not in 256 columns
+def test_prepare_nchw_large_layers(batch, h, branches, pool, per_block):
+    """A 64 -> 64 channel 3x3 conv (ResNet-18's first stage, T = 9) at
+    batches of 135 k - 270 k columns, 2 and 4 branches. 32x32 outputs without
+    a pool take the TMA-staged window gather (a block's 256 columns are eight
+    whole output rows); with a fused 2x2 max pool, or with 30x30 outputs
+    (rows that do not tile 256 columns), the thread-per-group kernel with two
+    or four 256-column chunks per block, a schedule only layers of
+    2,368 x chunks / T or more reach. The whole output equals the NHWC input
+    path's (a different prepare kernel) bit for bit, and sampled columns
+    equal the oracle's."""
     from cim22_b200 import abi
     from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace, conv_gather
 
     c = f = 64
-    h = 32
     m = batch * h * h
     assert prepare_schedule(m, 9) == per_block
     rng = np.random.default_rng(batch + branches + pool)
