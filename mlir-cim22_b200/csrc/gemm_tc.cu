@@ -310,6 +310,7 @@ constexpr int kEpiWarps = 16;
 constexpr int kSThreads = 64 + 32 * kEpiWarps;
 constexpr int kExpSlots = 16, kTmemBufs = 4;
 constexpr uint32_t kBufCols = 128;
+constexpr int kParamLanes = 512;
 
 template <int kAB> struct SSShape {
   static constexpr int L = kAB == 1 ? 64 : 32; // lanes per output tile
@@ -335,6 +336,9 @@ template <int kAB> struct alignas(1024) SmemSS {
   uint64_t dempty[kTmemBufs];
   uint32_t tmem;
   int failed;
+  // Bias, batch-norm scale and shift of every lane (layers of at most
+  // kParamLanes lanes), copied once per CTA for the output stores.
+  alignas(16) float lane_params[3][kParamLanes];
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
@@ -475,10 +479,12 @@ __device__ __forceinline__ void prefetch_residual(const float *residual, int row
 // store - rows, or NCHW
 // planes where a warp's 32 consecutive rows store 32 consecutive floats of a
 // lane. The branch sums are finite or infinite, never NaN, so the hardware
-// RNE conversion rounds them as the reference's truncf does.
+// RNE conversion rounds them as the reference's truncf does. cache, when not
+// null, holds the bias, scale and shift of every lane in shared memory.
 template <int kAB, int LT>
 __device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, int lane0, int M,
-                                           int N, int T, const float *__restrict__ bias,
+                                           int N, int T, const float (*cache)[kParamLanes],
+                                           const float *__restrict__ bias,
                                            const float *__restrict__ post_scale,
                                            const float *__restrict__ post_shift,
                                            const float *__restrict__ residual, int act,
@@ -507,7 +513,16 @@ __device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, in
   }
   const bool full = lane0 + LT <= N;
   if (bias != nullptr) {
-    if (full && (vec & 1)) {
+    if (cache != nullptr && full) {
+#pragma unroll
+      for (int j4 = 0; j4 < LT; j4 += 4) {
+        const float4 b = *reinterpret_cast<const float4 *>(&cache[0][lane0 + j4]);
+        o[j4] = __fadd_rn(o[j4], b.x);
+        o[j4 + 1] = __fadd_rn(o[j4 + 1], b.y);
+        o[j4 + 2] = __fadd_rn(o[j4 + 2], b.z);
+        o[j4 + 3] = __fadd_rn(o[j4 + 3], b.w);
+      }
+    } else if (full && (vec & 1)) {
 #pragma unroll
       for (int j4 = 0; j4 < LT; j4 += 4) {
         const float4 b = __ldg(reinterpret_cast<const float4 *>(bias + lane0 + j4));
@@ -524,10 +539,22 @@ __device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, in
     }
   }
   if (post_scale != nullptr) {
+    if (cache != nullptr && full) {
 #pragma unroll
-    for (int j = 0; j < LT; ++j)
-      if (lane0 + j < N)
-        o[j] = __fmaf_rn(o[j], __ldg(post_scale + lane0 + j), __ldg(post_shift + lane0 + j));
+      for (int j4 = 0; j4 < LT; j4 += 4) {
+        const float4 sc = *reinterpret_cast<const float4 *>(&cache[1][lane0 + j4]);
+        const float4 sh = *reinterpret_cast<const float4 *>(&cache[2][lane0 + j4]);
+        o[j4] = __fmaf_rn(o[j4], sc.x, sh.x);
+        o[j4 + 1] = __fmaf_rn(o[j4 + 1], sc.y, sh.y);
+        o[j4 + 2] = __fmaf_rn(o[j4 + 2], sc.z, sh.z);
+        o[j4 + 3] = __fmaf_rn(o[j4 + 3], sc.w, sh.w);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < LT; ++j)
+        if (lane0 + j < N)
+          o[j] = __fmaf_rn(o[j], __ldg(post_scale + lane0 + j), __ldg(post_shift + lane0 + j));
+    }
   }
   if (residual != nullptr) {
     // A residual add fused after the batch norm (prefetched into L2 when the
@@ -616,6 +643,15 @@ __global__ void __launch_bounds__(kSThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
+  // The per-lane epilogue parameters are resident constants of the layer
+  // (no earlier kernel writes them), so they are copied before the PDL wait.
+  const bool cached = N <= kParamLanes;
+  if (cached)
+    for (int i = threadIdx.x; i < N; i += kSThreads) {
+      s.lane_params[0][i] = bias ? bias[i] : 0.0f;
+      s.lane_params[1][i] = post_scale ? post_scale[i] : 0.0f;
+      s.lane_params[2][i] = post_shift ? post_shift[i] : 0.0f;
+    }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&s.tmem)),
@@ -732,7 +768,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
       float acc[kAB][2][LT];
       for (int t = 0; t < T; ++t, ++gi) {
         const int slot = gi % kExpSlots, buf = gi % kTmemBufs;
-        if (!mbar_wait(&s.exfull[slot], (gi / kExpSlots) & 1) || *failed) {
+        // A failure elsewhere in the CTA shows up here as a wait that runs
+        // out, so the per-tile waits do not poll the failure flag.
+        if (!mbar_wait(&s.exfull[slot], (gi / kExpSlots) & 1)) {
           ok = false;
           break;
         }
@@ -760,7 +798,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                       ? __uint_as_float(static_cast<uint32_t>(ex[a] + 143 - kScaleShift) << 23)
                       : 0.0f;
         }
-        if (!mbar_wait(&s.dfull[buf], (gi / kTmemBufs) & 1) || *failed) {
+        if (!mbar_wait(&s.dfull[buf], (gi / kTmemBufs) & 1)) {
           ok = false;
           break;
         }
@@ -826,7 +864,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
       }
       if (!ok)
         break;
-      store_tile<kAB, LT>(acc, m0 + row_local, lane0, M, N, T, bias, post_scale, post_shift,
+      store_tile<kAB, LT>(acc, m0 + row_local, lane0, M, N, T,
+                          cached ? s.lane_params : nullptr, bias, post_scale, post_shift,
                           residual, act, vec, out_pixels, div_pix, y);
     }
     if (!ok) {
