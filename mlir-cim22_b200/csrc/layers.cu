@@ -24,6 +24,7 @@
 #include "tma_util.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cmath>
 #include <cstring>
@@ -259,13 +260,21 @@ __device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
                                              int m_pad, int k_pad, int T, int t, int m,
                                              int kbeg) {
   uint32_t mx[2] = {0, 0};
+  // A 2-branch layer whose BF16 inputs carry no sign bit (the usual case:
+  // the layer reads a ReLU output) has the raw maximum as its maximum; a -0
+  // or a negative input takes the loop over the cleared magnitudes.
+  const uint32_t raw_half = max(raw_max & 0xffffu, raw_max >> 16);
+  if (kActBranches == 1 && raw_half < 0x8000u) {
+    mx[0] = raw_half;
+  } else {
 #pragma unroll
-  for (int a = 0; a < kActBranches; ++a) {
-    uint32_t m2 = 0;
+    for (int a = 0; a < kActBranches; ++a) {
+      uint32_t m2 = 0;
 #pragma unroll
-    for (int e = 0; e < 32; ++e)
-      m2 = __vmaxu2(m2, branch_pair<kActBranches>(signed_pairs[e], a));
-    mx[a] = max(m2 & 0xffffu, m2 >> 16);
+      for (int e = 0; e < 32; ++e)
+        m2 = __vmaxu2(m2, branch_pair<kActBranches>(signed_pairs[e], a));
+      mx[a] = max(m2 & 0xffffu, m2 >> 16);
+    }
   }
   // Non-finite groups: BF16 exponent 0xff in a branch maximum (the two
   // branches of a 4-branch layer hold every magnitude between them, NaNs
@@ -274,7 +283,7 @@ __device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
   const bool nonfinite = max(mx[0], mx[1]) >= 0x7f80u;
   if (nonfinite)
     atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-  else if (kActBranches == 1 && max(raw_max & 0xffffu, raw_max >> 16) > 0x8000u)
+  else if (kActBranches == 1 && raw_half > 0x8000u)
     atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
   // Pass 2: align and store.
 #pragma unroll
@@ -288,12 +297,16 @@ __device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
         out[q] = 0;
     } else if ((mx[a] >> 7) >= 8) {
       const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax) << 23);
+      // A 2-branch layer aligns the raw halves: -0 aligns to 0 as +0 does,
+      // and a negative nonzero input has failed the call already.
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
         uint32_t r[4];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const uint32_t pk = branch_pair<kActBranches>(signed_pairs[2 * q + h], a);
+          const uint32_t pk = kActBranches == 1
+                                  ? signed_pairs[2 * q + h]
+                                  : branch_pair<kActBranches>(signed_pairs[2 * q + h], a);
           r[2 * h] = __float_as_uint(__fmaf_rz(__uint_as_float(pk << 16), scale, 8388608.0f));
           r[2 * h + 1] =
               __float_as_uint(__fmaf_rz(__uint_as_float(pk & 0xffff0000u), scale, 8388608.0f));
@@ -426,7 +439,7 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
 
 
 
-// NCHW convolution gathers staged by TMA: a block serves 256 consecutive
+// NCHW convolution gathers staged by TMA: a work item is 256 consecutive
 // columns (whole output rows of one image, or whole images) and one K tile.
 // One bulk-tensor copy brings the input window those columns read - the
 // tile's channels, the rows and columns of its kernel windows, with the
@@ -436,103 +449,165 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
 // per-tile offset (the last K tile of a layer whose K is not a multiple of 64
 // takes zeros for the elements past K). Then the same split, rounding,
 // prealign and stores as prepare_nchw_kernel.
+//
+// The grid is persistent: block b takes items b, b + G, b + 2G, ... in
+// column-chunk-major order (the K tiles of a chunk, then the next chunk), so
+// the blocks resident at one time read neighbouring windows, which share
+// channels and halo rows in L2. Two window stages: the copy of the block's
+// next item is in flight while it converts the current one, and the offset
+// table of the next item is built alongside; one barrier per item hands
+// both over.
 struct BoxGather {
   int wb, hb, cb, nb; // box extents: columns, rows, channels, images
   int x0;             // first box column (a multiple of 4, <= -PW)
   int words;          // wb * hb * cb * nb
+  int stage_floats;   // one stage of the window ring: words rounded up to 128 bytes
 };
 
 template <int kActBranches>
-__global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
+__global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
     prepare_nchw_box_kernel(const __grid_constant__ CUtensorMap map, Gather32 g, BoxGather b,
-                            FastDiv div_chunks, int T, int m_pad, int k_pad,
+                            FastDiv div_T, int T, int items, int m_pad, int k_pad,
                             int8_t *__restrict__ A, int32_t *__restrict__ ex, int32_t *status) {
   extern __shared__ __align__(128) unsigned char box_raw[];
-  // The copy's destination, rounded up to 128 bytes (the launch adds them).
-  float *sbox = reinterpret_cast<float *>(box_raw + ((128u - (shared_addr(box_raw) & 127u)) & 127u));
-  __shared__ __align__(16) int sRel[kTileK];
-  __shared__ __align__(8) uint64_t bar;
+  // The ring's first stage, rounded up to 128 bytes (the launch adds them).
+  float *ring = reinterpret_cast<float *>(box_raw + ((128u - (shared_addr(box_raw) & 127u)) & 127u));
+  __shared__ __align__(16) int sRel[2][kTileK];
+  __shared__ __align__(8) uint64_t bar[2];
   pdl_launch_dependents();
-  const int blk = static_cast<int>(blockIdx.x);
-  const int t = fdiv(blk, div_chunks);
-  const int m0 = (blk - t * static_cast<int>(div_chunks.d)) * 256;
-  const int kbeg = t * kTileK;
   const int khw = g.KH * g.KW;
-  const int c0 = kbeg / khw;
   const int hw = g.OH * g.OW;
-  const int n0 = fdiv(m0, g.div_ohw);
-  // First input row of the box: the block's first output row's window, or
-  // the image's top padding when the block holds whole images.
-  const int ih0 = hw >= 256 ? fdiv(m0 - n0 * hw, g.div_ow) * g.SH - g.PH : -g.PH;
-  if (threadIdx.x == 0)
-    barrier_init(&bar, 1);
-  if (threadIdx.x < kTileK) {
-    const int k = kbeg + static_cast<int>(threadIdx.x);
-    const int c = fdiv(k, g.div_khw);
-    const int rk = k - c * khw;
-    const int i = fdiv(rk, g.div_kw);
-    const int j = rk - i * g.KW;
-    sRel[threadIdx.x] = k < g.K ? ((c - c0) * b.hb + i) * b.wb + j : -1;
+  const int grid = static_cast<int>(gridDim.x);
+  const int tid = static_cast<int>(threadIdx.x);
+  // Window offsets of the item's 64 K elements (-1 past K).
+  auto build_rel = [&](int item, int s) {
+    if (tid < kTileK) {
+      const int t = item - fdiv(item, div_T) * T;
+      const int kbeg = t * kTileK;
+      const int c0 = kbeg / khw;
+      const int k = kbeg + tid;
+      const int c = fdiv(k, g.div_khw);
+      const int rk = k - c * khw;
+      const int i = fdiv(rk, g.div_kw);
+      const int j = rk - i * g.KW;
+      sRel[s][tid] = k < g.K ? ((c - c0) * b.hb + i) * b.wb + j : -1;
+    }
+  };
+  // First input row of an item's box: its first output row's window, or the
+  // image's top padding when the 256 columns hold whole images.
+  auto issue = [&](int item, int s) {
+    const int chunk = fdiv(item, div_T);
+    const int t = item - chunk * T;
+    const int m0 = chunk * 256;
+    const int n0 = fdiv(m0, g.div_ohw);
+    const int ih0 = hw >= 256 ? fdiv(m0 - n0 * hw, g.div_ow) * g.SH - g.PH : -g.PH;
+    barrier_expect_tx(&bar[s], static_cast<uint32_t>(b.words) * 4u);
+    tma_load_4d(ring + s * b.stage_floats, &map, &bar[s], b.x0, ih0, (t * kTileK) / khw, n0);
+  };
+  int item = static_cast<int>(blockIdx.x);
+  if (tid == 0) {
+    barrier_init(&bar[0], 1);
+    barrier_init(&bar[1], 1);
   }
+  build_rel(item, 0);
   __syncthreads();
   pdl_wait();
-  if (threadIdx.x == 0) {
-    barrier_expect_tx(&bar, static_cast<uint32_t>(b.words) * 4u);
-    tma_load_4d(sbox, &map, &bar, b.x0, ih0, c0, n0);
-  }
-  if (!barrier_wait(&bar, 0)) {
-    if (threadIdx.x == 0)
-      atomicOr(status, CIM22_STATUS_TIMEOUT);
-    return;
-  }
-  const int m = m0 + static_cast<int>(threadIdx.x);
-  if (m >= m_pad)
-    return; // whole warps: m_pad is a multiple of 128
-  uint32_t signed_pairs[32];
-  uint32_t raw_max = 0;
-  if (m < g.M) {
-    const int n = fdiv(m, g.div_ohw);
-    const int rm = m - n * hw;
-    const int oh = fdiv(rm, g.div_ow);
-    const int ow = rm - oh * g.OW;
-    const float *base = sbox + ((n - n0) * b.cb * b.hb + (oh * g.SH - g.PH - ih0)) * b.wb +
-                        (ow * g.SW - g.PW - b.x0);
-    auto convert4 = [&](int e4, float v0, float v1, float v2, float v3) {
-      const __nv_bfloat162 h0 = __floats2bfloat162_rn(v0, v1);
-      const __nv_bfloat162 h1 = __floats2bfloat162_rn(v2, v3);
-      signed_pairs[e4 / 2] = *reinterpret_cast<const uint32_t *>(&h0);
-      signed_pairs[e4 / 2 + 1] = *reinterpret_cast<const uint32_t *>(&h1);
-      if (kActBranches == 1)
-        raw_max = __vmaxu2(raw_max, __vmaxu2(signed_pairs[e4 / 2], signed_pairs[e4 / 2 + 1]));
-    };
-    if (kbeg + kTileK <= g.K) {
-#pragma unroll
-      for (int e4 = 0; e4 < kTileK; e4 += 4) {
-        const int4 rel = *reinterpret_cast<const int4 *>(&sRel[e4]);
-        convert4(e4, base[rel.x], base[rel.y], base[rel.z], base[rel.w]);
-      }
-    } else {
-      // The layer's last K tile with elements past K (offset -1): zeros.
-#pragma unroll
-      for (int e4 = 0; e4 < kTileK; e4 += 4) {
-        const int4 rel = *reinterpret_cast<const int4 *>(&sRel[e4]);
-        convert4(e4, rel.x < 0 ? 0.0f : base[rel.x], rel.y < 0 ? 0.0f : base[rel.y],
-                 rel.z < 0 ? 0.0f : base[rel.z], rel.w < 0 ? 0.0f : base[rel.w]);
-      }
+  if (tid == 0)
+    issue(item, 0);
+  for (int i = 0; item < items; ++i, item += grid) {
+    const int s = i & 1;
+    const int next = item + grid;
+    if (next < items) {
+      // Stage s ^ 1 and its offsets were released by the barrier that ended
+      // the previous item.
+      if (tid == 0)
+        issue(next, s ^ 1);
+      build_rel(next, s ^ 1);
     }
-  } else {
+    const bool arrived = barrier_wait(&bar[s], (i >> 1) & 1);
+    const int chunk = fdiv(item, div_T);
+    const int t = item - chunk * T;
+    const int kbeg = t * kTileK;
+    const int m0 = chunk * 256;
+    const int m = m0 + tid;
+    if (arrived && m < m_pad) { // whole warps: m_pad is a multiple of 128
+      uint32_t signed_pairs[32];
+      uint32_t raw_max = 0;
+      if (m < g.M) {
+        const int n0 = fdiv(m0, g.div_ohw);
+        const int ih0 = hw >= 256 ? fdiv(m0 - n0 * hw, g.div_ow) * g.SH - g.PH : -g.PH;
+        const int n = fdiv(m, g.div_ohw);
+        const int rm = m - n * hw;
+        const int oh = fdiv(rm, g.div_ow);
+        const int ow = rm - oh * g.OW;
+        const float *base = ring + (s ? b.stage_floats : 0) +
+                            ((n - n0) * b.cb * b.hb + (oh * g.SH - g.PH - ih0)) * b.wb +
+                            (ow * g.SW - g.PW - b.x0);
+        const int *rel_tab = sRel[s];
+        auto convert4 = [&](int e4, float v0, float v1, float v2, float v3) {
+          const __nv_bfloat162 h0 = __floats2bfloat162_rn(v0, v1);
+          const __nv_bfloat162 h1 = __floats2bfloat162_rn(v2, v3);
+          signed_pairs[e4 / 2] = *reinterpret_cast<const uint32_t *>(&h0);
+          signed_pairs[e4 / 2 + 1] = *reinterpret_cast<const uint32_t *>(&h1);
+          if (kActBranches == 1)
+            raw_max =
+                __vmaxu2(raw_max, __vmaxu2(signed_pairs[e4 / 2], signed_pairs[e4 / 2 + 1]));
+        };
+        if (kbeg + kTileK <= g.K) {
 #pragma unroll
-    for (int q = 0; q < 32; ++q)
-      signed_pairs[q] = 0; // a padding column: an all-zero group
+          for (int e4 = 0; e4 < kTileK; e4 += 4) {
+            const int4 rel = *reinterpret_cast<const int4 *>(&rel_tab[e4]);
+            convert4(e4, base[rel.x], base[rel.y], base[rel.z], base[rel.w]);
+          }
+        } else {
+          // The layer's last K tile with elements past K (offset -1): zeros.
+#pragma unroll
+          for (int e4 = 0; e4 < kTileK; e4 += 4) {
+            const int4 rel = *reinterpret_cast<const int4 *>(&rel_tab[e4]);
+            convert4(e4, rel.x < 0 ? 0.0f : base[rel.x], rel.y < 0 ? 0.0f : base[rel.y],
+                     rel.z < 0 ? 0.0f : base[rel.z], rel.w < 0 ? 0.0f : base[rel.w]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 32; ++q)
+          signed_pairs[q] = 0; // a padding column: an all-zero group
+      }
+      finish_group<kActBranches>(signed_pairs, raw_max, status, A, ex, m_pad, k_pad, T, t, m,
+                                 kbeg);
+    }
+    // The barrier that releases this stage also makes a run-out wait the
+    // whole block's: it leaves together, after a bounded wait for the copy it
+    // issued for its next item.
+    if (__syncthreads_or(!arrived)) {
+      if (tid == 0) {
+        atomicOr(status, CIM22_STATUS_TIMEOUT);
+        if (next < items)
+          barrier_wait(&bar[s ^ 1], ((i + 1) >> 1) & 1);
+      }
+      return;
+    }
   }
-  finish_group<kActBranches>(signed_pairs, raw_max, status, A, ex, m_pad, k_pad, T, t, m,
-                             kbeg);
 }
 
 // The box of the TMA-staged gather for a layer, or false when its columns do
 // not tile into whole output rows or whole images per 256-column block, the
 // image rows are not 16-byte multiples, or the box exceeds kBoxSmemLimit.
 constexpr int kBoxSmemLimit = 47 * 1024;
+
+static int device_sms() {
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return 148;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      return 148;
+    cached[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
 
 static bool plan_box_gather(const Gather32 &g, const float *x, int T, BoxGather &b) {
   if (g.kind != CIM22_GATHER_CONV_NCHW || g.PK != 0 || (g.W & 3) != 0 ||
@@ -565,7 +640,9 @@ static bool plan_box_gather(const Gather32 &g, const float *x, int T, BoxGather 
   if (words * 4 + 128 > kBoxSmemLimit)
     return false;
   b.words = static_cast<int>(words);
-  return true;
+  b.stage_floats = (b.words + 31) / 32 * 32;
+  const int64_t items = (int64_t{g.M} + 255) / 256 * T;
+  return items < (int64_t{1} << 31);
 }
 
 // ---------------------------------------------------------------------------
@@ -967,13 +1044,19 @@ __device__ __forceinline__ bool direct_prepare(const float *__restrict__ x, cons
     }
   }
   uint32_t mx[2] = {0, 0};
+  // Inputs without a sign bit: the raw maximum is the maximum.
+  const uint32_t raw_half = max(raw_max & 0xffffu, raw_max >> 16);
+  if (kActBranches == 1 && raw_half < 0x8000u) {
+    mx[0] = raw_half;
+  } else {
 #pragma unroll
-  for (int a = 0; a < kActBranches; ++a) {
-    uint32_t m2 = 0;
+    for (int a = 0; a < kActBranches; ++a) {
+      uint32_t m2 = 0;
 #pragma unroll
-    for (int e = 0; e < kE / 2; ++e)
-      m2 = __vmaxu2(m2, branch_pair<kActBranches>(signed_pairs[e], a));
-    mx[a] = max(m2 & 0xffffu, m2 >> 16);
+      for (int e = 0; e < kE / 2; ++e)
+        m2 = __vmaxu2(m2, branch_pair<kActBranches>(signed_pairs[e], a));
+      mx[a] = max(m2 & 0xffffu, m2 >> 16);
+    }
   }
   // Non-finite groups: BF16 exponent 0xff in a branch maximum (the two
   // branches of a 4-branch layer hold every magnitude between them, NaNs
@@ -982,7 +1065,7 @@ __device__ __forceinline__ bool direct_prepare(const float *__restrict__ x, cons
   const bool nonfinite = max(mx[0], mx[1]) >= 0x7f80u;
   if (nonfinite)
     atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-  else if (kActBranches == 1 && max(raw_max & 0xffffu, raw_max >> 16) > 0x8000u)
+  else if (kActBranches == 1 && raw_half > 0x8000u)
     atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
   bool fast = true;
 #pragma unroll
@@ -2053,19 +2136,28 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
     const int n_images = static_cast<int>(g.batch);
     if (tc::encode_nchw_box(&map, x, dg.W, dg.H, dg.C, n_images, box.wb, box.hb, box.cb,
                             box.nb)) {
-      const int64_t chunks = (m_pad + 255) / 256;
-      const FastDiv div_chunks = make_fastdiv(static_cast<uint32_t>(chunks));
-      const unsigned blocks = static_cast<unsigned>(chunks * T);
-      const size_t smem = static_cast<size_t>(box.words) * sizeof(float) + 128;
+      const int items = static_cast<int>((m_pad + 255) / 256 * T);
+      const size_t smem = 2 * static_cast<size_t>(box.stage_floats) * sizeof(float) + 128;
+      // A persistent grid: as many blocks as fit on the SMs at once.
       auto launch = [&](auto kernel) {
-        launch_pdl(kernel, blocks, 256, smem, s, map, dg, box, div_chunks, T,
-                   static_cast<int>(m_pad), static_cast<int>(layer->k_pad), A, ex, status);
+        int per_sm = 0;
+        if (!cuda_ok(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem)),
+                     "prepare shared memory") ||
+            !cuda_ok(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, smem),
+                     "prepare occupancy") ||
+            per_sm < 1)
+          return false;
+        const int grid = static_cast<int>(std::min<int64_t>(items, int64_t{device_sms()} * per_sm));
+        launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), 256, smem, s, map, dg, box,
+                   make_fastdiv(static_cast<uint32_t>(T)), T, items, static_cast<int>(m_pad),
+                   static_cast<int>(layer->k_pad), A, ex, status);
+        return true;
       };
-      if (ab == 1)
-        launch(prepare_nchw_box_kernel<1>);
-      else
-        launch(prepare_nchw_box_kernel<2>);
-      return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+      const bool launched =
+          ab == 1 ? launch(prepare_nchw_box_kernel<1>) : launch(prepare_nchw_box_kernel<2>);
+      return launched && cuda_ok(cudaGetLastError(), "prepare launch") ? 0
+                                                                      : CIM22_STATUS_BAD_ARGUMENT;
     }
   }
   // The thread-per-group NCHW kernel serves convolutions over enough columns

@@ -538,3 +538,57 @@ def test_relu_propagates_nan_like_torch():
     x = torch.tensor([float("nan"), -1.0, 2.0, float("-inf"), float("inf"), -0.0])
     got = cim_ops.relu(x.to(DEV)).cpu()
     torch.testing.assert_close(got, torch.relu(x), equal_nan=True, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("layout,n,c,h,f,kk,stride,pad", [
+    ("nchw", 64, 16, 32, 64, 3, 1, 1),   # TMA-staged window gather
+    ("nchw", 64, 16, 30, 32, 3, 1, 1),   # thread-per-group NCHW gather
+    ("nhwc", 64, 16, 32, 64, 3, 1, 1),   # NHWC gather
+    ("nchw", 4, 1, 28, 6, 5, 1, 0),      # one-tile direct kernel
+    ("rows", 512, 256, 0, 128, 0, 0, 0)])  # Linear rows
+def test_two_branch_signed_zero_and_negative_input(layout, n, c, h, f, kk, stride, pad):
+    """A 2-branch layer (nonnegative input) clears -0 to +0, as the
+    reference's preparation does, and rejects a negative nonzero input with
+    the reference's error text, on every prepare path."""
+    from cim22_b200 import abi
+    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace, conv_gather
+
+    rng = np.random.default_rng(n + c + h + f)
+    shape = (n, c) if layout == "rows" else (n, c, h, h)
+    x = np.maximum(rng.standard_normal(shape), 0).astype(np.float32)
+    x[rng.random(x.shape) < 0.3] = 0
+    w = (rng.standard_normal((f, c * max(kk, 1) ** 2)) * 0.1).astype(np.float32)
+    b = rng.standard_normal(f).astype(np.float32)
+    if layout == "rows":
+        m, g, expected = n, None, oracle.linear_bf16(x, w, b, branches=2, threads=8)
+    else:
+        kind = abi.GATHER_CONV_NCHW if layout == "nchw" else abi.GATHER_CONV_NHWC
+        g = conv_gather(kind, n, c, h, h, kk, kk, stride, pad)
+        m = n * g.out_h * g.out_w
+        conv = oracle.conv2d_bf16(x, w.reshape(f, c, kk, kk), b, stride, pad, branches=2,
+                                  threads=8)
+        expected = conv.transpose(0, 2, 3, 1).reshape(m, f)
+    layer = CimLayer(w)
+    ws = Workspace(DEV)
+    bias = torch.from_numpy(b).to(DEV)
+
+    def run(values):
+        host = values if layout != "nhwc" else values.transpose(0, 2, 3, 1).copy()
+        out = torch.empty(m, f, device=DEV)
+        status = StatusWord(DEV)
+        layer.forward_bf16(torch.from_numpy(host).to(DEV), out, m, gather=g, bias=bias,
+                           branches=2, workspace=ws, status=status)
+        torch.cuda.synchronize()
+        return out.cpu().numpy(), status
+
+    signed = x.copy()
+    signed[(x == 0) & (rng.random(x.shape) < 0.5)] = -0.0
+    assert np.signbit(signed).any()
+    got, status = run(signed)
+    status.raise_if_set()
+    np.testing.assert_array_equal(bits(got), bits(expected))
+    negative = x.copy()
+    negative.flat[rng.integers(negative.size)] = -0.5
+    _, status = run(negative)
+    with pytest.raises(RuntimeError, match="rejects negative inputs"):
+        status.raise_if_set()
