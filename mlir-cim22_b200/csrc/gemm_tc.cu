@@ -379,6 +379,19 @@ __device__ __forceinline__ void tmem_wait(uint32_t (&r)[8]) {
                  "+r"(r[6]), "+r"(r[7])::"memory");
 }
 
+// tcgen05.ld of 16 columns and the wait for it in one statement, so the
+// registers are written once.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, "
+               "%9, %10, %11, %12, %13, %14, %15}, [%16];\n"
+               "tcgen05.wait::ld.sync.aligned;"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                 "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+               : "r"(taddr)
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait(uint32_t (&r)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
                : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
@@ -412,9 +425,10 @@ __device__ __forceinline__ float act_tc(float v, int act) {
 // Rows outside the fast window carry sx = 0, so their sums gain exactly +0
 // here and restore_slow_rows then adds their tile values; all sums are >= +0.
 // sw points at the tile's weight scales in shared memory (16-byte aligned).
-// kInit marks the first crossbar tile of an output tile: the sums start at
-// q * sw (exact, nonnegative), which is what fma(q, sw, +0) gives.
-template <int kLT, bool kInit>
+// The sums start at +0 for each output tile: fma(q, sw, +0) of the first
+// crossbar tile is the exact q * sw (one code path for every tile, measured
+// faster than a first-tile multiply).
+template <int kLT>
 __device__ __forceinline__ void restore_fast(float (&acc)[kLT], const uint32_t (&p)[kLT],
                                              float sx, const float *__restrict__ sw) {
 #pragma unroll
@@ -425,7 +439,7 @@ __device__ __forceinline__ void restore_fast(float (&acc)[kLT], const uint32_t (
     for (int j = 0; j < 4; ++j) {
       const float v = __fmul_rn(__uint_as_float(p[j4 + j]), sx);
       const float q = __uint_as_float(__float_as_uint(v) & 0xffff0000u);
-      acc[j4 + j] = kInit ? __fmul_rn(q, s[j]) : __fmaf_rn(q, s[j], acc[j4 + j]);
+      acc[j4 + j] = __fmaf_rn(q, s[j], acc[j4 + j]);
     }
   }
 }
@@ -764,8 +778,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
       const int m0 = mb * kSBM, n0 = (ot - mb * num_nb) * L;
       const int lane0 = n0 + sub * LT;
       prefetch_residual<LT>(residual, m0 + row_local, lane0, M, N, out_pixels, div_pix);
-      // Written by the first crossbar tile (restore with kInit).
       float acc[kAB][2][LT];
+#pragma unroll
+      for (int a = 0; a < kAB; ++a)
+#pragma unroll
+        for (int w = 0; w < 2; ++w)
+#pragma unroll
+          for (int j = 0; j < LT; ++j)
+            acc[a][w][j] = 0.0f;
       for (int t = 0; t < T; ++t, ++gi) {
         const int slot = gi % kExpSlots, buf = gi % kTmemBufs;
         // A failure elsewhere in the CTA shows up here as a wait that runs
@@ -775,14 +795,13 @@ __global__ void __launch_bounds__(kSThreads, 1)
           break;
         }
         const ExpSlot &e = s.ex[slot];
-        int lo = e.range[0], hi = e.range[1];
+        // Fast window for this tile's weights, ex_lo <= Ex <= ex_hi: the
+        // intersection of its 32-lane blocks' windows (tabulated at load).
+        int ex_lo = e.range[2], ex_hi = e.range[3];
         if (L == 64) {
-          lo = min(lo, e.range[4]);
-          hi = max(hi, e.range[5]);
+          ex_lo = max(ex_lo, e.range[6]);
+          ex_hi = min(ex_hi, e.range[7]);
         }
-        // Fast window for this tile's weights: ex_lo <= Ex <= ex_hi.
-        const int ex_lo = max(kScaleShift + 7, 140 - lo);
-        const int ex_hi = hi <= 260 - kScaleShift ? min(kScaleShift + 111, 374 - hi) : -1;
         float sx[kAB];
         bool fast[kAB];
         int ex[kAB];
@@ -811,12 +830,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
 #pragma unroll
           for (int w = 0; w < 2; ++w) {
             uint32_t p[LT];
-            tmem_ld(col0 + w * L, p);
-            tmem_wait(p);
-            if (t == 0)
-              restore_fast<LT, true>(acc[0][w], p, sx[0], &e.w[w][sub * LT]);
-            else
-              restore_fast<LT, false>(acc[0][w], p, sx[0], &e.w[w][sub * LT]);
+            tmem_ld_wait(col0 + w * L, p);
+            restore_fast<LT>(acc[0][w], p, sx[0], &e.w[w][sub * LT]);
             // One warp-uniform test: rows outside the window (rare) add their
             // exact tile values to the sums the fast pass kept.
             if (__any_sync(0xffffffffu, !fast[0])) {
@@ -836,13 +851,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
             tmem_ld(col0 + a * SN + L, p1);
             tmem_wait(p0);
             tmem_wait(p1);
-            if (t == 0) {
-              restore_fast<LT, true>(acc[a][0], p0, sx[a], &e.w[0][sub * LT]);
-              restore_fast<LT, true>(acc[a][1], p1, sx[a], &e.w[1][sub * LT]);
-            } else {
-              restore_fast<LT, false>(acc[a][0], p0, sx[a], &e.w[0][sub * LT]);
-              restore_fast<LT, false>(acc[a][1], p1, sx[a], &e.w[1][sub * LT]);
-            }
+            restore_fast<LT>(acc[a][0], p0, sx[a], &e.w[0][sub * LT]);
+            restore_fast<LT>(acc[a][1], p1, sx[a], &e.w[1][sub * LT]);
             if (__any_sync(0xffffffffu, !fast[a])) {
               if (!fast[a]) {
                 const int64_t ew0 = static_cast<int64_t>(t) * n_pad + lane0;

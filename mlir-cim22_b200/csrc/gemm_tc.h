@@ -23,8 +23,9 @@ bool int8_available();
 // layers.cu): A int8 [act_branches * m_pad][k_pad], exA int32
 // [act_branches][T][m_pad], B int8 [2 * n_pad][k_pad] (Wp rows, then Wn),
 // exB int32 [2][T][n_pad] followed by the weight-exponent ranges
-// [T][n_pad / 32][4] = {min, max, 0, 0} over both signs of each tile and
-// 32-lane block, by the f32 weight scales 2^(Ew - 133) [2][T][n_pad] and by
+// [T][n_pad / 32][4] = {min, max, ex_lo, ex_hi} over both signs of each tile
+// and 32-lane block (ex_lo..ex_hi: the activation exponents the epilogue
+// restores on its fast path), by the f32 weight scales 2^(Ew - 133) [2][T][n_pad] and by
 // the epilogue's f32 scales 2^(Ew - 133 + kScaleShift) [2][T][n_pad]. Returns false when the shape is not handled by the tensor-core
 // kernel, in which case nothing was launched. out_pixels = 0 writes y as
 // rows [M][N]; out_pixels > 0 writes NCHW images [M / out_pixels][N][out_pixels].

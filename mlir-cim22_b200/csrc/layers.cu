@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
   const int hw = g.OH * g.OW;
   const int grid = static_cast<int>(gridDim.x);
   const int tid = static_cast<int>(threadIdx.x);
-  // Window offsets of the item's 64 K elements (-1 past K).
+  // Window byte offsets of the item's 64 K elements (-1 past K).
   auto build_rel = [&](int item, int s) {
     if (tid < kTileK) {
       const int t = item - fdiv(item, div_T) * T;
@@ -490,7 +490,7 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
       const int rk = k - c * khw;
       const int i = fdiv(rk, g.div_kw);
       const int j = rk - i * g.KW;
-      sRel[s][tid] = k < g.K ? ((c - c0) * b.hb + i) * b.wb + j : -1;
+      sRel[s][tid] = k < g.K ? 4 * (((c - c0) * b.hb + i) * b.wb + j) : -1;
     }
   };
   // First input row of an item's box: its first output row's window, or the
@@ -540,9 +540,13 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
         const int rm = m - n * hw;
         const int oh = fdiv(rm, g.div_ow);
         const int ow = rm - oh * g.OW;
-        const float *base = ring + (s ? b.stage_floats : 0) +
-                            ((n - n0) * b.cb * b.hb + (oh * g.SH - g.PH - ih0)) * b.wb +
-                            (ow * g.SW - g.PW - b.x0);
+        // 32-bit shared-memory byte addresses: the column's window origin
+        // plus the element's byte offset.
+        const uint32_t base =
+            shared_addr(ring) +
+            4u * static_cast<uint32_t>((s ? b.stage_floats : 0) +
+                                       ((n - n0) * b.cb * b.hb + (oh * g.SH - g.PH - ih0)) * b.wb +
+                                       (ow * g.SW - g.PW - b.x0));
         const int *rel_tab = sRel[s];
         auto convert4 = [&](int e4, float v0, float v1, float v2, float v3) {
           const __nv_bfloat162 h0 = __floats2bfloat162_rn(v0, v1);
@@ -557,15 +561,18 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
 #pragma unroll
           for (int e4 = 0; e4 < kTileK; e4 += 4) {
             const int4 rel = *reinterpret_cast<const int4 *>(&rel_tab[e4]);
-            convert4(e4, base[rel.x], base[rel.y], base[rel.z], base[rel.w]);
+            convert4(e4, lds_f32(base + rel.x), lds_f32(base + rel.y), lds_f32(base + rel.z),
+                     lds_f32(base + rel.w));
           }
         } else {
           // The layer's last K tile with elements past K (offset -1): zeros.
 #pragma unroll
           for (int e4 = 0; e4 < kTileK; e4 += 4) {
             const int4 rel = *reinterpret_cast<const int4 *>(&rel_tab[e4]);
-            convert4(e4, rel.x < 0 ? 0.0f : base[rel.x], rel.y < 0 ? 0.0f : base[rel.y],
-                     rel.z < 0 ? 0.0f : base[rel.z], rel.w < 0 ? 0.0f : base[rel.w]);
+            convert4(e4, rel.x < 0 ? 0.0f : lds_f32(base + rel.x),
+                     rel.y < 0 ? 0.0f : lds_f32(base + rel.y),
+                     rel.z < 0 ? 0.0f : lds_f32(base + rel.z),
+                     rel.w < 0 ? 0.0f : lds_f32(base + rel.w));
           }
         }
       } else {
@@ -1856,10 +1863,16 @@ static void prepare_bf16_weights(const float *w, int64_t n, int64_t k,
           lo = std::min(lo, e);
           hi = std::max(hi, e);
         }
+      // With them, the block's window of activation group exponents Ex for
+      // the epilogue's exact fast restore (Ex + 16 - kScaleShift and
+      // Ew - 133 + kScaleShift normal, Ex + Ew in [140, 374]; empty when an
+      // exponent exceeds 260 - kScaleShift).
+      constexpr int X = tc::kScaleShift;
       int32_t *r = ranges + (t * (n_pad / 32) + nb) * 4;
       r[0] = lo;
       r[1] = hi;
-      r[2] = r[3] = 0;
+      r[2] = std::max(X + 7, 140 - lo);
+      r[3] = hi <= 260 - X ? std::min(X + 111, 374 - hi) : -1;
     }
   // The weight scales 2^(Ew - 133) as f32 bit patterns (exact: Ew - 133 lies
   // in [-133, 121], inside f32's normal and subnormal range), then the

@@ -50,6 +50,13 @@ __device__ __forceinline__ bool barrier_wait(uint64_t *bar, uint32_t parity,
   }
 }
 
+// One f32 from a shared-memory byte address.
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+
 // A 4-D tiled bulk-tensor load into this CTA's shared memory (no cluster
 // multicast). The innermost coordinate x must be a multiple of 4 floats.
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar,
