@@ -297,6 +297,9 @@ __device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
         out[q] = 0;
     } else if ((mx[a] >> 7) >= 8) {
       const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax) << 23);
+      const uint64_t scale2 = (static_cast<uint64_t>(__float_as_uint(scale)) << 32) |
+                              __float_as_uint(scale);
+      const uint64_t magic2 = 0x4b0000004b000000ull; // 2^23 in both halves
       // A 2-branch layer aligns the raw halves: -0 aligns to 0 as +0 does,
       // and a negative nonzero input has failed the call already.
 #pragma unroll
@@ -307,9 +310,12 @@ __device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
           const uint32_t pk = kActBranches == 1
                                   ? signed_pairs[2 * q + h]
                                   : branch_pair<kActBranches>(signed_pairs[2 * q + h], a);
-          r[2 * h] = __float_as_uint(__fmaf_rz(__uint_as_float(pk << 16), scale, 8388608.0f));
-          r[2 * h + 1] =
-              __float_as_uint(__fmaf_rz(__uint_as_float(pk & 0xffff0000u), scale, 8388608.0f));
+          // Both halves in one packed f32x2 fma (each half rounds toward zero
+          // as __fmaf_rz).
+          asm("{\n\t.reg .b64 a, d;\n\tmov.b64 a, {%2, %3};\n\t"
+              "fma.rz.f32x2 d, a, %4, %5;\n\tmov.b64 {%0, %1}, d;\n\t}"
+              : "=r"(r[2 * h]), "=r"(r[2 * h + 1])
+              : "r"(pk << 16), "r"(pk & 0xffff0000u), "l"(scale2), "l"(magic2));
         }
         out[q] = pack_low_bytes(r[0], r[1], r[2], r[3]);
       }
