@@ -57,8 +57,8 @@ __device__ __forceinline__ float lds_f32(uint32_t addr) {
   return v;
 }
 
-// A 4-D tiled bulk-tensor load into this CTA's shared memory (no cluster
-// multicast). The innermost coordinate x must be a multiple of 4 floats.
+// A 4-D tiled bulk-tensor load into this CTA's own shared memory only. The
+// innermost coordinate x must be a multiple of 4 floats.
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar,
                                             int x, int y, int z, int w) {
   asm volatile(
