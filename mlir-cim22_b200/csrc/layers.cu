@@ -456,13 +456,15 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
 // takes zeros for the elements past K). Then the same split, rounding,
 // prealign and stores as prepare_nchw_kernel.
 //
-// The grid is persistent: block b takes items b, b + G, b + 2G, ... in
+// Block b takes a run of consecutive items [b * run, (b + 1) * run) in
 // column-chunk-major order (the K tiles of a chunk, then the next chunk), so
 // the blocks resident at one time read neighbouring windows, which share
 // channels and halo rows in L2. Two window stages: the copy of the block's
 // next item is in flight while it converts the current one, and the offset
 // table of the next item is built alongside; one barrier per item hands
-// both over.
+// both over. Runs of up to eight items keep several waves of blocks, so the
+// hardware scheduler fills SMs as the neighbouring kernels' blocks leave
+// (programmatic dependent launch overlaps the tails).
 struct BoxGather {
   int wb, hb, cb, nb; // box extents: columns, rows, channels, images
   int x0;             // first box column (a multiple of 4, <= -PW)
@@ -473,7 +475,7 @@ struct BoxGather {
 template <int kActBranches>
 __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
     prepare_nchw_box_kernel(const __grid_constant__ CUtensorMap map, Gather32 g, BoxGather b,
-                            FastDiv div_T, int T, int items, int m_pad, int k_pad,
+                            FastDiv div_T, int T, int items, int run, int m_pad, int k_pad,
                             int8_t *__restrict__ A, int32_t *__restrict__ ex, int32_t *status) {
   extern __shared__ __align__(128) unsigned char box_raw[];
   // The ring's first stage, rounded up to 128 bytes (the launch adds them).
@@ -483,7 +485,6 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
   pdl_launch_dependents();
   const int khw = g.KH * g.KW;
   const int hw = g.OH * g.OW;
-  const int grid = static_cast<int>(gridDim.x);
   const int tid = static_cast<int>(threadIdx.x);
   // Window byte offsets of the item's 64 K elements (-1 past K).
   auto build_rel = [&](int item, int s) {
@@ -510,7 +511,8 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
     barrier_expect_tx(&bar[s], static_cast<uint32_t>(b.words) * 4u);
     tma_load_4d(ring + s * b.stage_floats, &map, &bar[s], b.x0, ih0, (t * kTileK) / khw, n0);
   };
-  int item = static_cast<int>(blockIdx.x);
+  int item = static_cast<int>(blockIdx.x) * run;
+  const int end = min(item + run, items);
   if (tid == 0) {
     barrier_init(&bar[0], 1);
     barrier_init(&bar[1], 1);
@@ -520,10 +522,10 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
   pdl_wait();
   if (tid == 0)
     issue(item, 0);
-  for (int i = 0; item < items; ++i, item += grid) {
+  for (int i = 0; item < end; ++i, ++item) {
     const int s = i & 1;
-    const int next = item + grid;
-    if (next < items) {
+    const int next = item + 1;
+    if (next < end) {
       // Stage s ^ 1 and its offsets were released by the barrier that ended
       // the previous item.
       if (tid == 0)
@@ -595,7 +597,7 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
     if (__syncthreads_or(!arrived)) {
       if (tid == 0) {
         atomicOr(status, CIM22_STATUS_TIMEOUT);
-        if (next < items)
+        if (next < end)
           barrier_wait(&bar[s ^ 1], ((i + 1) >> 1) & 1);
       }
       return;
@@ -2157,7 +2159,7 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
                             box.nb)) {
       const int items = static_cast<int>((m_pad + 255) / 256 * T);
       const size_t smem = 2 * static_cast<size_t>(box.stage_floats) * sizeof(float) + 128;
-      // A persistent grid: as many blocks as fit on the SMs at once.
+      // Runs of items per block: up to eight, keeping at least four waves.
       auto launch = [&](auto kernel) {
         int per_sm = 0;
         if (!cuda_ok(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -2167,9 +2169,11 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
                      "prepare occupancy") ||
             per_sm < 1)
           return false;
-        const int grid = static_cast<int>(std::min<int64_t>(items, int64_t{device_sms()} * per_sm));
+        const int64_t resident = int64_t{device_sms()} * per_sm;
+        const int run = static_cast<int>(std::clamp<int64_t>(items / (4 * resident), 1, 8));
+        const int grid = (items + run - 1) / run;
         launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), 256, smem, s, map, dg, box,
-                   make_fastdiv(static_cast<uint32_t>(T)), T, items, static_cast<int>(m_pad),
+                   make_fastdiv(static_cast<uint32_t>(T)), T, items, run, static_cast<int>(m_pad),
                    static_cast<int>(layer->k_pad), A, ex, status);
         return true;
       };
