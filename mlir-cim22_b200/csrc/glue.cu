@@ -364,6 +364,28 @@ __global__ void gap_nchw_kernel(const float *__restrict__ x, float *__restrict__
     y[plane] = sum / static_cast<float>(hw);
 }
 
+// Mean of each small plane (at most 64 elements, a multiple of 4, 16-byte
+// aligned): one thread per plane, 128-bit loads, the elements summed in
+// order; a warp's 32 planes are contiguous.
+__global__ void gap_nchw_small_kernel(const float4 *__restrict__ x, float *__restrict__ y,
+                                      int64_t planes, int quads) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t plane = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (plane >= planes)
+    return;
+  const float4 *p = x + plane * quads;
+  float sum = 0.0f;
+  for (int i = 0; i < quads; ++i) {
+    const float4 v = __ldg(p + i);
+    sum += v.x;
+    sum += v.y;
+    sum += v.z;
+    sum += v.w;
+  }
+  y[plane] = sum / static_cast<float>(4 * quads);
+}
+
 // Per-channel affine over NCHW planes, 128-bit accesses: planes of a
 // multiple of 4 elements, flat index below 2^31 quads.
 __global__ void affine_nchw_vec_kernel(const float4 *__restrict__ x,
@@ -630,8 +652,15 @@ int cim22_cuda_global_avgpool_nchw(const float *x, float *y, int32_t n,
   if (!x || !y || n <= 0 || h <= 0 || w <= 0 || c <= 0)
     return bad("cim22_cuda_global_avgpool_nchw");
   const int64_t planes = static_cast<int64_t>(n) * c;
+  const int64_t hw = static_cast<int64_t>(h) * w;
+  if (hw <= 64 && hw % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    launch_pdl(gap_nchw_small_kernel, static_cast<unsigned>((planes + 255) / 256), 256, 0,
+               static_cast<cudaStream_t>(stream), reinterpret_cast<const float4 *>(x), y,
+               planes, static_cast<int>(hw / 4));
+    return launched("global_avgpool");
+  }
   const unsigned blocks = static_cast<unsigned>((planes * 32 + 255) / 256);
-  launch_pdl(gap_nchw_kernel, blocks, 256, 0, static_cast<cudaStream_t>(stream), x, y, planes, static_cast<int64_t>(h) * w);
+  launch_pdl(gap_nchw_kernel, blocks, 256, 0, static_cast<cudaStream_t>(stream), x, y, planes, hw);
   return launched("global_avgpool");
 }
 

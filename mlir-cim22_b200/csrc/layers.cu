@@ -459,10 +459,13 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
 // Block b takes a run of consecutive items [b * run, (b + 1) * run) in
 // column-chunk-major order (the K tiles of a chunk, then the next chunk), so
 // the blocks resident at one time read neighbouring windows, which share
-// channels and halo rows in L2. Two window stages: the copy of the block's
-// next item is in flight while it converts the current one, and the offset
-// table of the next item is built alongside; one barrier per item hands
-// both over. Runs of up to eight items keep several waves of blocks, so the
+// channels and halo rows in L2. A ring of three window stages: the copies
+// of the block's next two items are in flight while it converts the
+// current one; a stage's full barrier completes with its copy, its empty
+// barrier when all eight warps have read it. The window offsets of the 64
+// elements of a tile depend only on the tile's first element modulo KH * KW,
+// so one table per phase is built when the block starts. Runs of up to
+// eight items keep several waves of blocks, so the
 // hardware scheduler fills SMs as the neighbouring kernels' blocks leave
 // (programmatic dependent launch overlaps the tails).
 struct BoxGather {
@@ -470,7 +473,11 @@ struct BoxGather {
   int x0;             // first box column (a multiple of 4, <= -PW)
   int words;          // wb * hb * cb * nb
   int stage_floats;   // one stage of the window ring: words rounded up to 128 bytes
+  int stages;         // window stages in the ring (at most kBoxStages)
 };
+
+constexpr int kBoxStages = 3;
+constexpr int kBoxWarps = 8; // 256 threads
 
 template <int kActBranches>
 __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
@@ -478,67 +485,67 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
                             FastDiv div_T, int T, int items, int run, int m_pad, int k_pad,
                             int8_t *__restrict__ A, int32_t *__restrict__ ex, int32_t *status) {
   extern __shared__ __align__(128) unsigned char box_raw[];
-  // The ring's first stage, rounded up to 128 bytes (the launch adds them).
+  // The ring's first stage, rounded up to 128 bytes (the launch adds them),
+  // then the offset table.
   float *ring = reinterpret_cast<float *>(box_raw + ((128u - (shared_addr(box_raw) & 127u)) & 127u));
-  __shared__ __align__(16) int sRel[2][kTileK];
-  __shared__ __align__(8) uint64_t bar[2];
+  int *rel_table = reinterpret_cast<int *>(ring + b.stages * b.stage_floats);
+  __shared__ __align__(8) uint64_t full[kBoxStages], empty[kBoxStages];
   pdl_launch_dependents();
   const int khw = g.KH * g.KW;
   const int hw = g.OH * g.OW;
   const int tid = static_cast<int>(threadIdx.x);
-  // Window byte offsets of the item's 64 K elements (-1 past K).
-  auto build_rel = [&](int item, int s) {
-    if (tid < kTileK) {
-      const int t = item - fdiv(item, div_T) * T;
-      const int kbeg = t * kTileK;
-      const int c0 = kbeg / khw;
-      const int k = kbeg + tid;
-      const int c = fdiv(k, g.div_khw);
-      const int rk = k - c * khw;
-      const int i = fdiv(rk, g.div_kw);
-      const int j = rk - i * g.KW;
-      sRel[s][tid] = k < g.K ? 4 * (((c - c0) * b.hb + i) * b.wb + j) : -1;
+  const int item0 = static_cast<int>(blockIdx.x) * run;
+  const int n_items = min(run, items - item0);
+  if (tid == 0)
+    for (int s = 0; s < b.stages; ++s) {
+      barrier_init(&full[s], 1);
+      barrier_init(&empty[s], kBoxWarps);
     }
-  };
+  // Window byte offsets of the 64 K elements of a tile for every phase
+  // ph = kbeg mod (KH * KW): element e is k = c0 * KH * KW + ph + e.
+  for (int idx = tid; idx < khw * kTileK; idx += 256) {
+    const int r = idx / kTileK + idx % kTileK; // ph + e
+    const int c = r / khw, rk = r - c * khw;
+    const int i = rk / g.KW, j = rk - i * g.KW;
+    rel_table[idx] = 4 * ((c * b.hb + i) * b.wb + j);
+  }
+  __syncthreads();
+  pdl_wait();
   // First input row of an item's box: its first output row's window, or the
   // image's top padding when the 256 columns hold whole images.
-  auto issue = [&](int item, int s) {
+  auto issue = [&](int i) {
+    const int item = item0 + i, s = i % b.stages;
     const int chunk = fdiv(item, div_T);
     const int t = item - chunk * T;
     const int m0 = chunk * 256;
     const int n0 = fdiv(m0, g.div_ohw);
     const int ih0 = hw >= 256 ? fdiv(m0 - n0 * hw, g.div_ow) * g.SH - g.PH : -g.PH;
-    barrier_expect_tx(&bar[s], static_cast<uint32_t>(b.words) * 4u);
-    tma_load_4d(ring + s * b.stage_floats, &map, &bar[s], b.x0, ih0, (t * kTileK) / khw, n0);
+    barrier_expect_tx(&full[s], static_cast<uint32_t>(b.words) * 4u);
+    tma_load_4d(ring + s * b.stage_floats, &map, &full[s], b.x0, ih0, (t * kTileK) / khw, n0);
   };
-  int item = static_cast<int>(blockIdx.x) * run;
-  const int end = min(item + run, items);
-  if (tid == 0) {
-    barrier_init(&bar[0], 1);
-    barrier_init(&bar[1], 1);
-  }
-  build_rel(item, 0);
-  __syncthreads();
-  pdl_wait();
+  int issued = 0;
   if (tid == 0)
-    issue(item, 0);
-  for (int i = 0; item < end; ++i, ++item) {
-    const int s = i & 1;
-    const int next = item + 1;
-    if (next < end) {
-      // Stage s ^ 1 and its offsets were released by the barrier that ended
-      // the previous item.
-      if (tid == 0)
-        issue(next, s ^ 1);
-      build_rel(next, s ^ 1);
+    for (; issued < min(b.stages - 1, n_items); ++issued)
+      issue(issued);
+  int i = 0; // items this thread has seen arrive
+  for (; i < n_items; ++i) {
+    const int s = i % b.stages;
+    if (tid == 0 && issued < n_items) {
+      // The stage of item i + stages - 1 last held item i - 1: every warp
+      // has left it when its empty barrier completes.
+      if (i >= 1 && !barrier_wait(&empty[issued % b.stages], ((i - 1) / b.stages) & 1))
+        break;
+      issue(issued++);
     }
-    const bool arrived = barrier_wait(&bar[s], (i >> 1) & 1);
+    if (!barrier_wait(&full[s], (i / b.stages) & 1))
+      break;
+    const int item = item0 + i;
     const int chunk = fdiv(item, div_T);
     const int t = item - chunk * T;
     const int kbeg = t * kTileK;
     const int m0 = chunk * 256;
     const int m = m0 + tid;
-    if (arrived && m < m_pad) { // whole warps: m_pad is a multiple of 128
+    if (m < m_pad) { // whole warps: m_pad is a multiple of 128
       uint32_t signed_pairs[32];
       uint32_t raw_max = 0;
       if (m < g.M) {
@@ -552,10 +559,10 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
         // plus the element's byte offset.
         const uint32_t base =
             shared_addr(ring) +
-            4u * static_cast<uint32_t>((s ? b.stage_floats : 0) +
+            4u * static_cast<uint32_t>(s * b.stage_floats +
                                        ((n - n0) * b.cb * b.hb + (oh * g.SH - g.PH - ih0)) * b.wb +
                                        (ow * g.SW - g.PW - b.x0));
-        const int *rel_tab = sRel[s];
+        const int *rel = rel_table + (kbeg - (kbeg / khw) * khw) * kTileK;
         auto convert4 = [&](int e4, float v0, float v1, float v2, float v3) {
           const __nv_bfloat162 h0 = __floats2bfloat162_rn(v0, v1);
           const __nv_bfloat162 h1 = __floats2bfloat162_rn(v2, v3);
@@ -568,19 +575,20 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
         if (kbeg + kTileK <= g.K) {
 #pragma unroll
           for (int e4 = 0; e4 < kTileK; e4 += 4) {
-            const int4 rel = *reinterpret_cast<const int4 *>(&rel_tab[e4]);
-            convert4(e4, lds_f32(base + rel.x), lds_f32(base + rel.y), lds_f32(base + rel.z),
-                     lds_f32(base + rel.w));
+            const int4 r4 = *reinterpret_cast<const int4 *>(&rel[e4]);
+            convert4(e4, lds_f32(base + r4.x), lds_f32(base + r4.y), lds_f32(base + r4.z),
+                     lds_f32(base + r4.w));
           }
         } else {
-          // The layer's last K tile with elements past K (offset -1): zeros.
+          // The layer's last K tile: zeros for the elements past K.
+          const int kv = g.K - kbeg;
 #pragma unroll
           for (int e4 = 0; e4 < kTileK; e4 += 4) {
-            const int4 rel = *reinterpret_cast<const int4 *>(&rel_tab[e4]);
-            convert4(e4, rel.x < 0 ? 0.0f : lds_f32(base + rel.x),
-                     rel.y < 0 ? 0.0f : lds_f32(base + rel.y),
-                     rel.z < 0 ? 0.0f : lds_f32(base + rel.z),
-                     rel.w < 0 ? 0.0f : lds_f32(base + rel.w));
+            const int4 r4 = *reinterpret_cast<const int4 *>(&rel[e4]);
+            convert4(e4, e4 < kv ? lds_f32(base + r4.x) : 0.0f,
+                     e4 + 1 < kv ? lds_f32(base + r4.y) : 0.0f,
+                     e4 + 2 < kv ? lds_f32(base + r4.z) : 0.0f,
+                     e4 + 3 < kv ? lds_f32(base + r4.w) : 0.0f);
           }
         }
       } else {
@@ -591,17 +599,19 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
       finish_group<kActBranches>(signed_pairs, raw_max, status, A, ex, m_pad, k_pad, T, t, m,
                                  kbeg);
     }
-    // The barrier that releases this stage also makes a run-out wait the
-    // whole block's: it leaves together, after a bounded wait for the copy it
-    // issued for its next item.
-    if (__syncthreads_or(!arrived)) {
-      if (tid == 0) {
-        atomicOr(status, CIM22_STATUS_TIMEOUT);
-        if (next < end)
-          barrier_wait(&bar[s ^ 1], ((i + 1) >> 1) & 1);
-      }
-      return;
-    }
+    // This warp is done with the stage.
+    __syncwarp();
+    if ((tid & 31) == 0)
+      barrier_arrive(&empty[s]);
+  }
+  if (i < n_items) {
+    // A wait ran out: report it; the issuing thread waits (bounded) for the
+    // copies it issued that it has not seen complete (at most one per stage,
+    // so each is its stage's current phase).
+    atomicOr(status, CIM22_STATUS_TIMEOUT);
+    if (tid == 0)
+      for (int j = i; j < issued; ++j)
+        barrier_wait(&full[j % b.stages], (j / b.stages) & 1, 100000000ull);
   }
 }
 
@@ -622,6 +632,15 @@ static int device_sms() {
     cached[dev].store(n, std::memory_order_relaxed);
   }
   return n;
+}
+
+// Dynamic shared memory of prepare_nchw_box_kernel: the window ring (one
+// stage rounded up to 128 bytes, plus 128 bytes for the ring's alignment) and
+// the offset table of every kernel-window phase.
+static size_t box_smem(const BoxGather &b, int khw) {
+  return (static_cast<size_t>(b.stages) * b.stage_floats + static_cast<size_t>(khw) * kTileK) *
+             sizeof(float) +
+         128;
 }
 
 static bool plan_box_gather(const Gather32 &g, const float *x, int T, BoxGather &b) {
@@ -657,7 +676,11 @@ static bool plan_box_gather(const Gather32 &g, const float *x, int T, BoxGather 
   b.words = static_cast<int>(words);
   b.stage_floats = (b.words + 31) / 32 * 32;
   const int64_t items = (int64_t{g.M} + 255) / 256 * T;
-  return items < (int64_t{1} << 31);
+  // Three stages (the copies of the next two items in flight): measured
+  // faster on ResNet-18's convolutions than two, also where the third stage
+  // costs a resident block (a stride-2 convolution's larger window).
+  b.stages = kBoxStages;
+  return items < (int64_t{1} << 31) && box_smem(b, khw) <= 200 * 1024;
 }
 
 // ---------------------------------------------------------------------------
@@ -2158,7 +2181,7 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
     if (tc::encode_nchw_box(&map, x, dg.W, dg.H, dg.C, n_images, box.wb, box.hb, box.cb,
                             box.nb)) {
       const int items = static_cast<int>((m_pad + 255) / 256 * T);
-      const size_t smem = 2 * static_cast<size_t>(box.stage_floats) * sizeof(float) + 128;
+      const size_t smem = box_smem(box, dg.KH * dg.KW);
       // Runs of items per block: up to eight, keeping at least four waves.
       auto launch = [&](auto kernel) {
         int per_sm = 0;

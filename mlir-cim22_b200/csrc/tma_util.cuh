@@ -24,6 +24,10 @@ __device__ __forceinline__ void barrier_expect_tx(uint64_t *bar, uint32_t bytes)
                : "memory");
 }
 
+__device__ __forceinline__ void barrier_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(shared_addr(bar)) : "memory");
+}
+
 // Wait for the phase with the given parity, for at most limit_ns of the
 // global timer (read once every 32 polls). Returns false when it ran out.
 __device__ __forceinline__ bool barrier_wait(uint64_t *bar, uint32_t parity,

@@ -219,6 +219,11 @@ def test_glue_against_torch_cpu():
     torch.testing.assert_close(cim_ops.avgpool2d_nchw(nd, 2, 2).cpu(),
                                torch.nn.functional.avg_pool2d(nchw, 2, 2), **tol)
     torch.testing.assert_close(cim_ops.global_avgpool_nchw(nd).cpu(), nchw.mean((2, 3)), **tol)
+    # Planes of at most 64 elements (one thread per plane), ResNet-18's 4x4 among them.
+    for shape in [(64, 512, 4, 4), (3, 5, 2, 6), (2, 3, 8, 8)]:
+        small = torch.from_numpy(rng.standard_normal(shape).astype(np.float32))
+        torch.testing.assert_close(cim_ops.global_avgpool_nchw(small.to(DEV)).cpu(),
+                                   small.mean((2, 3)), **tol)
     torch.testing.assert_close(
         cim_ops.channel_affine_nchw(nd, scale.to(DEV), shift.to(DEV), "relu").cpu(),
         torch.relu(nchw * scale[:, None, None] + shift[:, None, None]), **tol)
