@@ -116,6 +116,11 @@ class CimLayer:
     def range_safe(self) -> bool:
         return bool(lib().cim22_cuda_layer_range_safe(self._handle))
 
+    @property
+    def bf16_operands(self) -> bool:
+        """Whether the weights admit the contraction with BF16 operands."""
+        return bool(lib().cim22_cuda_layer_bf16_operands(self._handle))
+
     def workspace_bytes(self, m: int, branches: int = 4) -> int:
         if self.kind == "bf16":
             return int(lib().cim22_cuda_layer_workspace_bf16(self._handle, m, branches))

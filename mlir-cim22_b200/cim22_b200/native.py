@@ -65,6 +65,7 @@ _SIGNATURES = {
     "cim22_cuda_layer_create_int8": (P, [c.c_int, P, I64, I64, CHARP, SZ]),
     "cim22_cuda_layer_destroy": (None, [P]),
     "cim22_cuda_layer_range_safe": (c.c_int, [P]),
+    "cim22_cuda_layer_bf16_operands": (c.c_int, [P]),
     "cim22_cuda_layer_n": (I64, [P]),
     "cim22_cuda_layer_k": (I64, [P]),
     "cim22_cuda_layer_workspace_bf16": (SZ, [P, I64, I32]),

@@ -112,4 +112,31 @@ struct cim22_cuda_layer {
   // flag for a lane of all -128 mantissas. INT8: int8 [n_pad][k_pad].
   int8_t *weights = nullptr;
   int32_t *exponents = nullptr;
+  // BF16 sign-split layers of at least kOperandMinLanes lanes whose nonzero
+  // weight lanes all have exponents in [kOperandEwMin, kOperandEwMax]: the
+  // scaled BF16 operands b * 2^(Ew - 133)
+  // [2][n_pad][k_pad] of the tensor-core contraction with BF16 operands, and
+  // the window [ex_lo, ex_hi] of activation group exponents whose prepared
+  // values a * 2^(Ex - 133) it multiplies exactly (null / empty otherwise).
+  uint16_t *operands = nullptr;
+  int32_t ex_lo = 1, ex_hi = 0;
 };
+
+namespace cim {
+// Layers of at least this many output lanes take BF16 operands. Measured on
+// B200: the contraction with BF16 operands is faster wherever it runs, but its
+// prepare writes two bytes per element instead of one, which outweighs the
+// gain for narrow layers over many columns (ResNet-18's 64- and 128-channel
+// convolutions) and pays off from 256 lanes on (its 256- and 512-channel
+// convolutions, the 4096-wide Linear stack).
+constexpr int64_t kOperandMinLanes = 256;
+// The weight exponents that BF16 operands admit: every nonzero scaled weight
+// b * 2^(Ew - 133) (1 <= b <= 127) is a normal BF16 value, and a dot p < 2^20
+// of unscaled activation mantissas times them stays a finite normal f32.
+constexpr int kOperandEwMin = 8, kOperandEwMax = 241;
+// Activation group exponents with scaled operands: a * 2^(Ex - 133) normal
+// (Ex >= 8), the preparation's offset 2^(Ex - 110) finite (Ex <= 237), and
+// for every weight exponent of the layer 140 <= Ex + Ew <= 374, so that a
+// dot's f32 value p * 2^(Ex + Ew - 266) is normal and finite.
+constexpr int kOperandExMin = 8, kOperandExMax = 237;
+} // namespace cim

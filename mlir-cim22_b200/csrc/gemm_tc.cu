@@ -881,6 +881,333 @@ __global__ void __launch_bounds__(kSThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// BF16 sign-split contraction with BF16 operands. The prepare stores each
+// activation group as BF16 values a * 2^(Ex - 133) (a: the ExpPrealign
+// mantissas, 0..127) and the layer stores its weights as b * 2^(Ew - 133);
+// every product a * b * 2^(Ex + Ew - 266) and every partial sum is then an
+// integer multiple of 2^(Ex + Ew - 266) below 2^20 of them, which the
+// tensor core's f32 accumulation holds exactly. So a tcgen05.mma kind::f16
+// leaves each crossbar dot in TMEM as the exact f32 value
+// v = p * 2^(Ex + Ew - 266), normal and finite inside the layer's window
+// (ex_lo <= Ex <= ex_hi, which the layer derives from its weight exponents
+// so that 140 <= Ex + Ew <= 374 for every lane). The restore of the
+// reference - RNE_bf16(Q(p) * 2^(Ew + Ex - 266)), Q keeping the top 8 bits of
+// p - is then v with its low 16 bits cleared (exactly representable), and
+// the tile-order f32 sum adds it with one rounding: two operations per dot,
+// no per-tile scales.
+//
+// Groups outside the window are stored unscaled (a itself), so their dots
+// arrive as p * 2^(Ew - 133) (exact: the layer's weight exponents lie in
+// [kOperandEwMin, kOperandEwMax]); a row of such a group takes the exact
+// integer restore for that tile. The epilogue tells them apart by the group
+// exponents, which the producer copies per tile into a 16-slot ring that the
+// epilogue releases (a load per tile from global memory would put its
+// latency on every tile).
+//
+// Same warp roles, TMEM buffers and output stores as signsplit_tc_kernel; the
+// ring holds one crossbar tile per stage (128 bytes of K per row) and the MMA
+// warp issues four K=16 MMAs per activation branch and tile.
+template <int kAB> struct SBShape {
+  static constexpr int kStages = kAB == 1 ? 6 : 4;
+  static constexpr int kExSlots = 16;                       // activation exponent ring
+  static constexpr int kATile = kSBM * 64;                  // BF16 elements per branch
+  static constexpr int kBTile = SSShape<kAB>::N * 64;       // BF16 elements
+};
+
+template <int kAB> struct alignas(1024) SmemSB {
+  uint16_t a[SBShape<kAB>::kStages][kAB][SBShape<kAB>::kATile];
+  uint16_t b[SBShape<kAB>::kStages][SBShape<kAB>::kBTile];
+  int32_t exa[SBShape<kAB>::kExSlots][kAB][kSBM];
+  uint64_t full[SBShape<kAB>::kStages];
+  uint64_t empty[SBShape<kAB>::kStages];
+  uint64_t exfull[SBShape<kAB>::kExSlots];
+  uint64_t exempty[SBShape<kAB>::kExSlots];
+  uint64_t dfull[kTmemBufs];
+  uint64_t dempty[kTmemBufs];
+  uint32_t tmem;
+  int failed;
+  alignas(16) float lane_params[3][kParamLanes];
+};
+
+// Instruction descriptor of tcgen05.mma .kind::f16 with BF16 A and B and an
+// f32 accumulator: D format (bits [4,6)) 1 = F32, A and B formats (bits
+// [7,10), [10,13)) 1 = BF16, both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+               " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+               "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Add one (activation branch, weight sign) slice of a crossbar tile to the
+// branch sums: q = v with its low 16 bits cleared, acc += q (the sums start
+// at +0 for each output tile).
+template <int kLT>
+__device__ __forceinline__ void restore_b16(float (&acc)[kLT], const uint32_t (&v)[kLT]) {
+#pragma unroll
+  for (int j = 0; j < kLT; ++j)
+    acc[j] = __fadd_rn(acc[j], __uint_as_float(v[j] & 0xffff0000u));
+}
+
+// The same slice when some row of the warp holds an unscaled group: this
+// thread's row restores p = v * 2^(133 - Ew) exactly through the integer path
+// when `raw`, else as restore_b16.
+template <int kLT>
+__device__ __forceinline__ void restore_b16_raw(float (&acc)[kLT], const uint32_t (&v)[kLT],
+                                             bool raw, const int32_t *__restrict__ exB,
+                                             int64_t ew_index, int ex, int32_t *status) {
+  if (!raw) {
+    restore_b16<kLT>(acc, v);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < kLT; ++j) {
+    const int ew = exB[ew_index + j];
+    const float unscale = __uint_as_float(static_cast<uint32_t>(260 - ew) << 23);
+    const int p = __float2int_rn(__fmul_rn(__uint_as_float(v[j]), unscale));
+    acc[j] = tc_slow_tile_add(acc[j], p, ew, ex, status);
+  }
+}
+
+template <int kAB, bool kRes>
+__global__ void __launch_bounds__(kSThreads, 1)
+    signsplit_b16_kernel(const __grid_constant__ CUtensorMap tmA,
+                         const __grid_constant__ CUtensorMap tmB,
+                         const int32_t *__restrict__ exA, int m_pad,
+                         const int32_t *__restrict__ exB, int n_pad, int T, int M, int N,
+                         int ex_lo, int ex_hi, FastDiv div_nb, const float *__restrict__ bias,
+                         const float *__restrict__ post_scale,
+                         const float *__restrict__ post_shift,
+                         const float *__restrict__ residual_arg, int act, int vec,
+                         int out_pixels, FastDiv div_pix, float *__restrict__ y,
+                         int32_t *status) {
+  const float *residual = kRes ? residual_arg : nullptr;
+  using S = SSShape<kAB>;
+  constexpr int L = S::L, LT = S::LT, SN = S::N;
+  constexpr int kStages = SBShape<kAB>::kStages, kExSlots = SBShape<kAB>::kExSlots;
+  extern __shared__ uint8_t smem_raw[];
+  SmemSB<kAB> &s = smem_aligned<SmemSB<kAB>>(smem_raw);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int num_nb = (N + L - 1) / L;
+  const int num_tiles = ((M + kSBM - 1) / kSBM) * num_nb;
+  constexpr uint32_t kTmemCols = kTmemBufs * kBufCols;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < kExSlots; ++i) {
+      mbar_init(&s.exfull[i], 1);
+      mbar_init(&s.exempty[i], kEpiWarps);
+    }
+    for (int i = 0; i < kTmemBufs; ++i) {
+      mbar_init(&s.dfull[i], 1);
+      mbar_init(&s.dempty[i], kEpiWarps);
+    }
+    s.failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  // Resident per-lane epilogue parameters, copied before the PDL wait.
+  const bool cached = N <= kParamLanes;
+  if (cached)
+    for (int i = threadIdx.x; i < N; i += kSThreads) {
+      s.lane_params[0][i] = bias ? bias[i] : 0.0f;
+      s.lane_params[1][i] = post_scale ? post_scale[i] : 0.0f;
+      s.lane_params[2][i] = post_shift ? post_shift[i] : 0.0f;
+    }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s.tmem)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = s.tmem;
+  volatile int *failed = &s.failed;
+  pdl_launch_dependents();
+  pdl_wait();
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer: per crossbar tile the activation tile of each branch
+    // and the stacked Wp / Wn tile into the stage ring, the tile's activation
+    // exponents of the 128 rows into the exponent ring.
+    uint32_t it = 0;
+    bool ok = true;
+    for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
+      const int mb = fdiv(ot, div_nb);
+      const int m0 = mb * kSBM, nb = ot - mb * num_nb, n0 = nb * L;
+      for (int t = 0; t < T; ++t, ++it) {
+        const int stage = it % kStages, slot = it % kExSlots;
+        if (!mbar_wait(&s.empty[stage], ((it / kStages) & 1) ^ 1) ||
+            !mbar_wait(&s.exempty[slot], ((it / kExSlots) & 1) ^ 1) || *failed) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&s.full[stage], (kAB * SBShape<kAB>::kATile + SBShape<kAB>::kBTile) * 2);
+#pragma unroll
+        for (int a = 0; a < kAB; ++a)
+          tma_load_2d(s.a[stage][a], &tmA, &s.full[stage], t * 64, a * m_pad + m0);
+        tma_load_2d(s.b[stage], &tmB, &s.full[stage], t * 64, n0);
+        tma_load_2d(s.b[stage] + L * 64, &tmB, &s.full[stage], t * 64, n_pad + n0);
+        mbar_expect_tx(&s.exfull[slot], kAB * kSBM * 4);
+#pragma unroll
+        for (int a = 0; a < kAB; ++a)
+          bulk_load(s.exa[slot][a], exA + (static_cast<int64_t>(a) * T + t) * m_pad + m0,
+                    kSBM * 4, &s.exfull[slot]);
+      }
+    }
+    if (!ok)
+      *failed = 1;
+    // Never leave with copies in flight: wait (bounded) for the last use of
+    // every stage and exponent slot this thread filled (`it` counts the
+    // filled tiles; a wait that failed filled none).
+    for (uint32_t i = it > static_cast<uint32_t>(kStages) ? it - kStages : 0; i < it; ++i)
+      mbar_wait(&s.full[i % kStages], (i / kStages) & 1);
+    for (uint32_t i = it > static_cast<uint32_t>(kExSlots) ? it - kExSlots : 0; i < it; ++i)
+      mbar_wait(&s.exfull[i % kExSlots], (i / kExSlots) & 1);
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer: four K=16 MMAs per activation branch and crossbar tile.
+    constexpr uint32_t idesc = idesc_bf16(kSBM, SN);
+    uint32_t gi = 0;
+    bool ok = true;
+    for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
+      for (int t = 0; t < T; ++t, ++gi) {
+        const int stage = gi % kStages, buf = gi % kTmemBufs;
+        if (!mbar_wait(&s.full[stage], (gi / kStages) & 1) ||
+            !mbar_wait(&s.dempty[buf], ((gi / kTmemBufs) & 1) ^ 1) || *failed) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t bdesc = sw128_desc(s.b[stage]);
+#pragma unroll
+        for (int a = 0; a < kAB; ++a) {
+          const uint64_t adesc = sw128_desc(s.a[stage][a]);
+          const uint32_t d = tmem + buf * kBufCols + a * SN;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_bf16(d, adesc + 2 * k, bdesc + 2 * k, idesc, k > 0 ? 1u : 0u);
+        }
+        mma_commit(&s.dfull[buf]);
+        mma_commit(&s.empty[stage]);
+      }
+    }
+    if (!ok)
+      *failed = 1;
+    // Let the last MMAs land before TMEM is freed.
+    if (gi > 0)
+      mbar_wait(&s.dfull[(gi - 1) % kTmemBufs], ((gi - 1) / kTmemBufs) & 1);
+  } else if (warp >= 2) {
+    // Epilogue.
+    const int quad = warp % 4, sub = (warp - 2) / 4;
+    const int row_local = quad * 32 + lane;
+    const uint32_t tlane = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t span = static_cast<uint32_t>(ex_hi - ex_lo);
+    uint32_t gi = 0;
+    bool ok = true;
+    for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
+      const int mb = fdiv(ot, div_nb);
+      const int m0 = mb * kSBM, n0 = (ot - mb * num_nb) * L;
+      const int lane0 = n0 + sub * LT;
+      const int row = m0 + row_local; // < m_pad
+      prefetch_residual<LT>(residual, row, lane0, M, N, out_pixels, div_pix);
+      float acc[kAB][2][LT];
+#pragma unroll
+      for (int a = 0; a < kAB; ++a)
+#pragma unroll
+        for (int w = 0; w < 2; ++w)
+#pragma unroll
+          for (int j = 0; j < LT; ++j)
+            acc[a][w][j] = 0.0f;
+      for (int t = 0; t < T; ++t, ++gi) {
+        const int buf = gi % kTmemBufs, slot = gi % kExSlots;
+        // A failure elsewhere in the CTA shows up here as a wait that runs out.
+        if (!mbar_wait(&s.exfull[slot], (gi / kExSlots) & 1)) {
+          ok = false;
+          break;
+        }
+        int ex[kAB];
+        bool raw[kAB];
+#pragma unroll
+        for (int a = 0; a < kAB; ++a) {
+          ex[a] = s.exa[slot][a][row_local];
+          raw[a] = ex[a] != kZeroGroup && static_cast<uint32_t>(ex[a] - ex_lo) > span;
+        }
+        if (!mbar_wait(&s.dfull[buf], (gi / kTmemBufs) & 1)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t col0 = tmem + tlane + buf * kBufCols + sub * LT;
+        if constexpr (kAB == 1) {
+          const bool any_raw = __any_sync(0xffffffffu, raw[0]);
+#pragma unroll
+          for (int w = 0; w < 2; ++w) {
+            uint32_t v[LT];
+            tmem_ld_wait(col0 + w * L, v);
+            if (any_raw)
+              restore_b16_raw<LT>(acc[0][w], v, raw[0], exB,
+                                  (static_cast<int64_t>(w) * T + t) * n_pad + lane0, ex[0],
+                                  status);
+            else
+              restore_b16<LT>(acc[0][w], v);
+          }
+        } else {
+#pragma unroll
+          for (int a = 0; a < kAB; ++a) {
+            uint32_t v0[LT], v1[LT];
+            tmem_ld(col0 + a * SN, v0);
+            tmem_ld(col0 + a * SN + L, v1);
+            tmem_wait(v0);
+            tmem_wait(v1);
+            if (__any_sync(0xffffffffu, raw[a])) {
+              const int64_t ew0 = static_cast<int64_t>(t) * n_pad + lane0;
+              restore_b16_raw<LT>(acc[a][0], v0, raw[a], exB, ew0, ex[a], status);
+              restore_b16_raw<LT>(acc[a][1], v1, raw[a], exB,
+                                  ew0 + static_cast<int64_t>(T) * n_pad, ex[a], status);
+            } else {
+              restore_b16<LT>(acc[a][0], v0);
+              restore_b16<LT>(acc[a][1], v1);
+            }
+          }
+        }
+        // Hand the TMEM buffer and the exponent slot back once every lane
+        // has read them.
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&s.dempty[buf]);
+          mbar_arrive(&s.exempty[slot]);
+        }
+      }
+      if (!ok)
+        break;
+      store_tile<kAB, LT>(acc, row, lane0, M, N, T, cached ? s.lane_params : nullptr, bias,
+                          post_scale, post_shift, residual, act, vec, out_pixels, div_pix, y);
+    }
+    if (!ok) {
+      *failed = 1;
+      if (lane == 0)
+        atomicOr(status, CIM22_STATUS_TIMEOUT);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols));
+  }
+}
+
+// ---------------------------------------------------------------------------
 // INT8 contraction, persistent: 128 x 256 output tiles (one tcgen05.mma
 // kind::i8 of M=128, N=256, K=32 per 32 bytes of K), a 4-stage TMA ring of
 // 128-byte K blocks (16 KB of A and 32 KB of B per stage), and two 256-column
@@ -1109,6 +1436,23 @@ bool encode_int8_2d(CUtensorMap *map, const void *base, uint64_t rows, uint64_t 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D BF16 tensor [rows][cols] (cols contiguous), box 64 x box_rows (128
+// bytes of a row: one crossbar tile), 128B swizzle.
+bool encode_bf16_2d(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                    uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn)
+    return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
+            box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 } // namespace
 
 // 4-D f32 tensor [N][C][H][W] (W contiguous, W % 4 == 0), box
@@ -1209,6 +1553,52 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
                    : launch(signsplit_tc_kernel<2, false>, smem_ss<2>()))
             : (res ? launch(signsplit_tc_kernel<1, true>, smem_ss<1>())
                    : launch(signsplit_tc_kernel<1, false>, smem_ss<1>()))))
+    return false;
+  g_tc_launches.fetch_add(1, std::memory_order_relaxed);
+  return true;
+}
+
+template <int kAB> constexpr size_t smem_sb() { return sizeof(SmemSB<kAB>) + 1024; }
+static_assert(smem_sb<1>() <= 232448 && smem_sb<2>() <= 232448,
+              "the BF16 operand ring must fit the 227 KB of dynamic shared memory per CTA");
+
+bool launch_signsplit_b16(const uint16_t *A, const int32_t *exA, int64_t m_pad,
+                          const uint16_t *B, const int32_t *exB, int64_t n_pad, int64_t k_pad,
+                          int T, int64_t M, int64_t N, int ex_lo, int ex_hi, const float *bias,
+                          const float *post_scale, const float *post_shift,
+                          const float *residual, int act, int act_branches, int64_t out_pixels,
+                          float *y, int32_t *status, cudaStream_t stream) {
+  const int L = act_branches == 2 ? SSShape<2>::L : SSShape<1>::L;
+  if (M < 1 || N <= 8 || m_pad % kSBM || n_pad % 128 || k_pad % 64 || ex_lo > ex_hi ||
+      static_cast<int64_t>(act_branches) * m_pad >= (int64_t{1} << 31) ||
+      (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
+      (reinterpret_cast<uintptr_t>(exA) & 15) || (reinterpret_cast<uintptr_t>(exB) & 15))
+    return false;
+  CUtensorMap ta, tb;
+  if (!encode_bf16_2d(&ta, A, act_branches * m_pad, k_pad, kSBM) ||
+      !encode_bf16_2d(&tb, B, 2 * n_pad, k_pad, static_cast<uint32_t>(L)))
+    return false;
+  const int vec = (N % 4 == 0 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0 ? 1 : 0) |
+                  (N % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 ? 2 : 0);
+  const int64_t tiles = ((M + kSBM - 1) / kSBM) * ((N + L - 1) / L);
+  const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, sm_count())));
+  auto launch = [&](auto kernel, size_t smem) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return false;
+    launch_pdl(kernel, grid, kSThreads, smem, stream, ta, tb, exA, static_cast<int>(m_pad), exB,
+               static_cast<int>(n_pad), T, static_cast<int>(M), static_cast<int>(N), ex_lo,
+               ex_hi, make_fastdiv(static_cast<uint32_t>((N + L - 1) / L)), bias, post_scale,
+               post_shift, residual, act, vec, static_cast<int>(out_pixels),
+               make_fastdiv(static_cast<uint32_t>(out_pixels > 0 ? out_pixels : 1)), y, status);
+    return true;
+  };
+  const bool res = residual != nullptr;
+  if (!(act_branches == 2
+            ? (res ? launch(signsplit_b16_kernel<2, true>, smem_sb<2>())
+                   : launch(signsplit_b16_kernel<2, false>, smem_sb<2>()))
+            : (res ? launch(signsplit_b16_kernel<1, true>, smem_sb<1>())
+                   : launch(signsplit_b16_kernel<1, false>, smem_sb<1>()))))
     return false;
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
   return true;

@@ -39,6 +39,22 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad,
                       int act_branches, int64_t out_pixels, float *y, int32_t *status,
                       cudaStream_t stream);
 
+// The sign-split contraction with BF16 operands: A holds the prepared
+// activation groups as BF16 values [act_branches * m_pad][k_pad] - a * 2^(Ex -
+// 133) for groups whose exponent Ex lies in [ex_lo, ex_hi], the unscaled
+// mantissas a otherwise - and exA their exponents [act_branches][T][m_pad];
+// B holds the weights b * 2^(Ew - 133) [2 * n_pad][k_pad] (Wp rows, then Wn)
+// and exB the lane exponents [2][T][n_pad] of launch_signsplit's layout. The
+// tcgen05 MMAs (kind::f16, f32 accumulation) then give each crossbar dot as
+// the exact f32 value p * 2^(Ex + Ew - 266) (p * 2^(Ew - 133) for unscaled
+// groups). Same outputs, options and return convention as launch_signsplit.
+bool launch_signsplit_b16(const uint16_t *A, const int32_t *exA, int64_t m_pad,
+                          const uint16_t *B, const int32_t *exB, int64_t n_pad, int64_t k_pad,
+                          int T, int64_t M, int64_t N, int ex_lo, int ex_hi, const float *bias,
+                          const float *post_scale, const float *post_shift,
+                          const float *residual, int act, int act_branches, int64_t out_pixels,
+                          float *y, int32_t *status, cudaStream_t stream);
+
 // INT8 contraction with whole-K int32 accumulation (exact: range-proven
 // layers, or unproven ones computed as the Host computes them).
 // A is int8 [a_rows][a_cols] (a_cols <= k_pad, a multiple of 16; rows >= M),

@@ -189,11 +189,11 @@ __device__ __forceinline__ void gather8(const float *__restrict__ x, const Gathe
 }
 
 
-template <int kActBranches, int kMode>
+template <int kActBranches, int kMode, bool kB16>
 __global__ void __launch_bounds__(256)
     prepare_kernel(const float *__restrict__ x, Gather32 g, FastDiv div_chunks, int T, int cols,
                    int m_pad, int k_pad, int8_t *__restrict__ A, int32_t *__restrict__ ex,
-                   int32_t *status) {
+                   int32_t *status, int win_lo, int win_hi) {
   pdl_launch_dependents();
   pdl_wait();
   const int blk = static_cast<int>(blockIdx.x);
@@ -210,16 +210,26 @@ __global__ void __launch_bounds__(256)
       break; // uniform per 8-lane subgroup
     float v[8];
     gather8<kMode>(x, g, tp, m, kbeg, v);
-    uint2 out[2];
     int emax[2];
-    convert8<kActBranches>(v, mask, sub, status, out, emax);
+    if constexpr (kB16) {
+      uint4 out[2];
+      convert8_b16<kActBranches>(v, mask, sub, status, win_lo, win_hi, out, emax);
 #pragma unroll
-    for (int a = 0; a < kActBranches; ++a) {
-      *reinterpret_cast<uint2 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) =
-          out[a];
+      for (int a = 0; a < kActBranches; ++a)
+        *reinterpret_cast<uint4 *>(A + ((static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) *
+                                           2) = out[a];
+    } else {
+      uint2 out[2];
+      convert8<kActBranches>(v, mask, sub, status, out, emax);
+#pragma unroll
+      for (int a = 0; a < kActBranches; ++a)
+        *reinterpret_cast<uint2 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) =
+            out[a];
+    }
+#pragma unroll
+    for (int a = 0; a < kActBranches; ++a)
       if (sub == 0)
         ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax[a];
-    }
   }
 }
 
@@ -251,14 +261,16 @@ __device__ __forceinline__ uint32_t branch_pair(uint32_t pair, int a) {
 
 // The rest of one (column m, K tile t) group once its 64 signed BF16 pairs
 // and raw maximum are known: branch maxima, the non-finite and
-// negative-input flags, ExpPrealign, the 64 aligned bytes per branch (four
-// 16-byte stores) and the group exponent.
-template <int kActBranches>
+// negative-input flags, ExpPrealign, the group exponent and the prepared
+// group of each branch - 64 aligned int8 mantissas (four 16-byte stores), or
+// with kB16 the 64 scaled BF16 operand values (eight 16-byte stores; scaled
+// for groups whose exponent lies in [win_lo, win_hi], unscaled otherwise).
+template <int kActBranches, bool kB16 = false>
 __device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
                                              uint32_t raw_max, int32_t *status,
                                              int8_t *__restrict__ A, int32_t *__restrict__ ex,
                                              int m_pad, int k_pad, int T, int t, int m,
-                                             int kbeg) {
+                                             int kbeg, int win_lo = 1, int win_hi = 0) {
   uint32_t mx[2] = {0, 0};
   // A 2-branch layer whose BF16 inputs carry no sign bit (the usual case:
   // the layer reads a ReLU output) has the raw maximum as its maximum; a -0
@@ -286,20 +298,24 @@ __device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
   else if (kActBranches == 1 && raw_half > 0x8000u)
     atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
   // Pass 2: align and store.
+  constexpr int kWords = kB16 ? 32 : 16;
 #pragma unroll
   for (int a = 0; a < kActBranches; ++a) {
     const bool zero = mx[a] == 0 || nonfinite;
     const int emax = zero ? kZeroGroup : effective_exponent(static_cast<uint16_t>(mx[a]));
-    uint32_t out[16];
+    uint32_t out[kWords];
     if (zero) {
 #pragma unroll
-      for (int q = 0; q < 16; ++q)
+      for (int q = 0; q < kWords; ++q)
         out[q] = 0;
     } else if ((mx[a] >> 7) >= 8) {
       const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax) << 23);
       const uint64_t scale2 = (static_cast<uint64_t>(__float_as_uint(scale)) << 32) |
                               __float_as_uint(scale);
       const uint64_t magic2 = 0x4b0000004b000000ull; // 2^23 in both halves
+      uint64_t s2 = 0, off2 = 0;
+      if (kB16)
+        operand_scale(emax, win_lo, win_hi, s2, off2);
       // A 2-branch layer aligns the raw halves: -0 aligns to 0 as +0 does,
       // and a negative nonzero input has failed the call already.
 #pragma unroll
@@ -317,34 +333,50 @@ __device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
               : "=r"(r[2 * h]), "=r"(r[2 * h + 1])
               : "r"(pk << 16), "r"(pk & 0xffff0000u), "l"(scale2), "l"(magic2));
         }
-        out[q] = pack_low_bytes(r[0], r[1], r[2], r[3]);
+        if constexpr (kB16) {
+          const uint2 w = scale_pairs(r, s2, off2);
+          out[2 * q] = w.x;
+          out[2 * q + 1] = w.y;
+        } else {
+          out[q] = pack_low_bytes(r[0], r[1], r[2], r[3]);
+        }
       }
     } else {
+      // Tiny maxima (exponent < 8): exact alignment; with kB16 the unscaled
+      // mantissas (such a group is outside every window).
       const int shift = 127 - emax;
       for (int q = 0; q < 16; ++q) {
-        uint32_t word = 0;
+        uint32_t bytes[4];
         for (int h = 0; h < 4; ++h)
-          word |= slow_align((branch_pair<kActBranches>(signed_pairs[2 * q + h / 2], a) >>
-                              (16 * (h & 1))) & 0xffffu,
-                             shift)
-                  << (8 * h);
-        out[q] = word;
+          bytes[h] = slow_align((branch_pair<kActBranches>(signed_pairs[2 * q + h / 2], a) >>
+                                 (16 * (h & 1))) & 0xffffu,
+                                shift);
+        if constexpr (kB16) {
+          out[2 * q] = static_cast<uint32_t>(f32_to_bf16(static_cast<float>(bytes[0]))) |
+                       (static_cast<uint32_t>(f32_to_bf16(static_cast<float>(bytes[1]))) << 16);
+          out[2 * q + 1] =
+              static_cast<uint32_t>(f32_to_bf16(static_cast<float>(bytes[2]))) |
+              (static_cast<uint32_t>(f32_to_bf16(static_cast<float>(bytes[3]))) << 16);
+        } else {
+          out[q] = bytes[0] | (bytes[1] << 8) | (bytes[2] << 16) | (bytes[3] << 24);
+        }
       }
     }
-    uint4 *dst = reinterpret_cast<uint4 *>(A + (static_cast<int64_t>(a) * m_pad + m) * k_pad +
-                                           kbeg);
+    constexpr int kElemBytes = kB16 ? 2 : 1;
+    uint4 *dst = reinterpret_cast<uint4 *>(
+        A + ((static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) * kElemBytes);
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
+    for (int q = 0; q < kWords / 4; ++q)
       dst[q] = make_uint4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
     ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax;
   }
 }
 
-template <int kActBranches, bool kPool>
+template <int kActBranches, bool kPool, bool kB16>
 __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
     prepare_nchw_kernel(const float *__restrict__ x, Gather32 g, FastDiv div_chunks, int T,
                         int cols, int m_pad, int k_pad, int8_t *__restrict__ A,
-                        int32_t *__restrict__ ex, int32_t *status) {
+                        int32_t *__restrict__ ex, int32_t *status, int win_lo, int win_hi) {
   pdl_launch_dependents();
   pdl_wait();
   constexpr int kMode = kPool ? kPrepConvPool : kPrepConv;
@@ -438,8 +470,8 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 4)
         raw_max = __vmaxu2(raw_max, signed_pairs[q]);
     }
   }
-  finish_group<kActBranches>(signed_pairs, raw_max, status, A, ex, m_pad, k_pad, T, t, m,
-                             kbeg);
+  finish_group<kActBranches, kB16>(signed_pairs, raw_max, status, A, ex, m_pad, k_pad, T, t,
+                                   m, kbeg, win_lo, win_hi);
   }
 }
 
@@ -479,11 +511,12 @@ struct BoxGather {
 constexpr int kBoxStages = 3;
 constexpr int kBoxWarps = 8; // 256 threads
 
-template <int kActBranches>
+template <int kActBranches, bool kB16>
 __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
     prepare_nchw_box_kernel(const __grid_constant__ CUtensorMap map, Gather32 g, BoxGather b,
                             FastDiv div_T, int T, int items, int run, int m_pad, int k_pad,
-                            int8_t *__restrict__ A, int32_t *__restrict__ ex, int32_t *status) {
+                            int8_t *__restrict__ A, int32_t *__restrict__ ex, int32_t *status,
+                            int win_lo, int win_hi) {
   extern __shared__ __align__(128) unsigned char box_raw[];
   // The ring's first stage, rounded up to 128 bytes (the launch adds them),
   // then the offset table.
@@ -596,8 +629,8 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
         for (int q = 0; q < 32; ++q)
           signed_pairs[q] = 0; // a padding column: an all-zero group
       }
-      finish_group<kActBranches>(signed_pairs, raw_max, status, A, ex, m_pad, k_pad, T, t, m,
-                                 kbeg);
+      finish_group<kActBranches, kB16>(signed_pairs, raw_max, status, A, ex, m_pad, k_pad, T,
+                                       t, m, kbeg, win_lo, win_hi);
     }
     // This warp is done with the stage.
     __syncwarp();
@@ -1849,7 +1882,9 @@ __global__ void __launch_bounds__(256)
 static void prepare_bf16_weights(const float *w, int64_t n, int64_t k,
                                  int64_t n_pad, int64_t k_pad, int64_t T,
                                  std::vector<int8_t> &mant,
-                                 std::vector<int32_t> &exps) {
+                                 std::vector<int32_t> &exps,
+                                 std::vector<uint16_t> &operands, int32_t &ex_lo,
+                                 int32_t &ex_hi) {
   mant.assign(2 * n_pad * k_pad, 0);
   exps.assign(2 * T * n_pad + (n_pad / 32) * T * 4 + 4 * T * n_pad, 127);
   uint16_t group[kTileK];
@@ -1918,6 +1953,45 @@ static void prepare_bf16_weights(const float *w, int64_t n, int64_t k,
     const float g = std::ldexp(1.0f, std::min(exps[i] - 133 + tc::kScaleShift, 127));
     std::memcpy(&tc_scales[i], &g, 4);
   }
+  // Scaled BF16 operands b * 2^(Ew - 133) (exact: b has at most 7 significant
+  // bits and the value is normal for Ew >= kOperandEwMin), for layers of at
+  // least kOperandMinLanes lanes whose lanes with a nonzero mantissa all have
+  // an admitted exponent; the activation window then follows from the
+  // extreme exponents of those lanes.
+  operands.clear();
+  ex_lo = 1;
+  ex_hi = 0;
+  int ew_min = 1 << 30, ew_max = -(1 << 30);
+  for (int b = 0; b < 2; ++b)
+    for (int64_t t = 0; t < T; ++t)
+      for (int64_t lane = 0; lane < n; ++lane) {
+        const int8_t *src = mant.data() + (b * n_pad + lane) * k_pad + t * kTileK;
+        if (std::any_of(src, src + kTileK, [](int8_t v) { return v != 0; })) {
+          const int e = exps[(b * T + t) * n_pad + lane];
+          ew_min = std::min(ew_min, e);
+          ew_max = std::max(ew_max, e);
+        }
+      }
+  if (ew_min > ew_max) { // no nonzero weight: every dot is 0
+    ew_min = kOperandEwMin;
+    ew_max = kOperandEwMin;
+  }
+  const int lo = std::max(kOperandExMin, 140 - ew_min);
+  const int hi = std::min(kOperandExMax, 374 - ew_max);
+  if (n < kOperandMinLanes || ew_min < kOperandEwMin || ew_max > kOperandEwMax || lo > hi)
+    return;
+  operands.assign(2 * n_pad * k_pad, 0);
+  for (int b = 0; b < 2; ++b)
+    for (int64_t lane = 0; lane < n; ++lane)
+      for (int64_t t = 0; t < T; ++t) {
+        const int e = exps[(b * T + t) * n_pad + lane];
+        const int64_t off = (b * n_pad + lane) * k_pad + t * kTileK;
+        for (int i = 0; i < kTileK; ++i)
+          if (mant[off + i] != 0)
+            operands[off + i] = f32_to_bf16(std::ldexp(static_cast<float>(mant[off + i]), e - 133));
+      }
+  ex_lo = lo;
+  ex_hi = hi;
 }
 
 static bool int8_range_proof(const int8_t *w, int64_t n, int64_t k) {
@@ -1966,8 +2040,9 @@ cim22_cuda_layer *cim22_cuda_layer_create_bf16(int device, const float *weight,
   layer->tiles = layer->k_pad / kTileK;
   std::vector<int8_t> mant;
   std::vector<int32_t> exps;
+  std::vector<uint16_t> operands;
   prepare_bf16_weights(weight, n, k, layer->n_pad, layer->k_pad, layer->tiles,
-                       mant, exps);
+                       mant, exps, operands, layer->ex_lo, layer->ex_hi);
   if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice") ||
       !cuda_ok(cudaMalloc(&layer->weights, mant.size()), "cudaMalloc") ||
       !cuda_ok(cudaMalloc(&layer->exponents, exps.size() * sizeof(int32_t)),
@@ -1977,7 +2052,13 @@ cim22_cuda_layer *cim22_cuda_layer_create_bf16(int device, const float *weight,
                "cudaMemcpy") ||
       !cuda_ok(cudaMemcpy(layer->exponents, exps.data(),
                           exps.size() * sizeof(int32_t), cudaMemcpyHostToDevice),
-               "cudaMemcpy")) {
+               "cudaMemcpy") ||
+      (!operands.empty() &&
+       (!cuda_ok(cudaMalloc(&layer->operands, operands.size() * sizeof(uint16_t)),
+                 "cudaMalloc") ||
+        !cuda_ok(cudaMemcpy(layer->operands, operands.data(),
+                            operands.size() * sizeof(uint16_t), cudaMemcpyHostToDevice),
+                 "cudaMemcpy")))) {
     copy_error(last_error(), error, error_capacity);
     cim22_cuda_layer_destroy(layer);
     return nullptr;
@@ -2096,11 +2177,16 @@ void cim22_cuda_layer_destroy(cim22_cuda_layer *layer) {
     cudaFree(layer->weights);
   if (layer->exponents)
     cudaFree(layer->exponents);
+  if (layer->operands)
+    cudaFree(layer->operands);
   delete layer;
 }
 
 int cim22_cuda_layer_range_safe(const cim22_cuda_layer *layer) {
   return layer && layer->range_safe ? 1 : 0;
+}
+int cim22_cuda_layer_bf16_operands(const cim22_cuda_layer *layer) {
+  return layer && layer->operands ? 1 : 0;
 }
 int64_t cim22_cuda_layer_n(const cim22_cuda_layer *layer) { return layer ? layer->n : -1; }
 int64_t cim22_cuda_layer_k(const cim22_cuda_layer *layer) { return layer ? layer->k : -1; }
@@ -2114,7 +2200,9 @@ size_t cim22_cuda_layer_workspace_bf16(const cim22_cuda_layer *layer,
     return static_cast<size_t>(round_up(m_pad * layer->k_pad, 256) +
                                2 * layer->tiles * m_pad * 4);
   const int64_t ab = branches == 2 ? 1 : 2;
-  const int64_t a_bytes = round_up(ab * m_pad * layer->k_pad, 256);
+  // Room for the BF16 operand values wherever the layer admits them.
+  const int64_t elem = layer->operands ? 2 : 1;
+  const int64_t a_bytes = round_up(ab * m_pad * layer->k_pad * elem, 256);
   return static_cast<size_t>(a_bytes + ab * layer->tiles * m_pad * 4);
 }
 
@@ -2122,6 +2210,22 @@ size_t cim22_cuda_layer_workspace_int8(const cim22_cuda_layer *layer, int64_t m)
   if (!layer || m <= 0)
     return 0;
   return static_cast<size_t>(round_up(m, kColumnPad) * layer->k_pad);
+}
+
+// The prepared-column format of a sign-split call, decided the same way by
+// the prepare and the contraction: scaled BF16 operand values for the
+// tensor-core contraction with BF16 operands where the layer holds BF16
+// operands (at least kOperandMinLanes lanes, weight exponents in the operand
+// range) and that kernel runs (sm_100, a 16-byte aligned workspace); int8
+// mantissas otherwise.
+static bool bf16_operands(const cim22_cuda_layer *layer, const void *workspace) {
+  return layer->operands != nullptr && layer->mode == CIM22_BF16_SIGN_SPLIT && layer->n > 8 &&
+         (reinterpret_cast<uintptr_t>(workspace) & 15) == 0 && tc::signsplit_available();
+}
+
+// Byte offset of the group exponents in a sign-split workspace.
+static int64_t exponent_offset(const cim22_cuda_layer *layer, int64_t m_pad, int ab, bool b16) {
+  return round_up(ab * m_pad * layer->k_pad * (b16 ? 2 : 1), 256);
 }
 
 int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
@@ -2148,8 +2252,10 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
     return CIM22_STATUS_BAD_ARGUMENT;
   }
   int8_t *A = static_cast<int8_t *>(workspace);
-  int32_t *ex = reinterpret_cast<int32_t *>(
-      static_cast<char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
+  const bool b16 = bf16_operands(layer, workspace);
+  int32_t *ex = reinterpret_cast<int32_t *>(static_cast<char *>(workspace) +
+                                            exponent_offset(layer, m_pad, ab, b16));
+  const int win_lo = layer->ex_lo, win_hi = layer->ex_hi;
   const Gather32 dg = to_device_gather(g, m, layer->k, x);
   if (layer->mode != CIM22_BF16_SIGN_SPLIT) {
     // Legacy / None: one thread per (column, K tile) group.
@@ -2197,11 +2303,14 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
         const int grid = (items + run - 1) / run;
         launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), 256, smem, s, map, dg, box,
                    make_fastdiv(static_cast<uint32_t>(T)), T, items, run, static_cast<int>(m_pad),
-                   static_cast<int>(layer->k_pad), A, ex, status);
+                   static_cast<int>(layer->k_pad), A, ex, status, win_lo, win_hi);
         return true;
       };
       const bool launched =
-          ab == 1 ? launch(prepare_nchw_box_kernel<1>) : launch(prepare_nchw_box_kernel<2>);
+          ab == 1 ? (b16 ? launch(prepare_nchw_box_kernel<1, true>)
+                         : launch(prepare_nchw_box_kernel<1, false>))
+                  : (b16 ? launch(prepare_nchw_box_kernel<2, true>)
+                         : launch(prepare_nchw_box_kernel<2, false>));
       return launched && cuda_ok(cudaGetLastError(), "prepare launch") ? 0
                                                                       : CIM22_STATUS_BAD_ARGUMENT;
     }
@@ -2225,13 +2334,21 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
     const unsigned blocks = static_cast<unsigned>(groups * T);
     auto launch = [&](auto kernel) {
       launch_pdl(kernel, blocks, 256, 0, s, x, dg, div_chunks, T, per_block,
-                 static_cast<int>(m_pad), static_cast<int>(layer->k_pad), A, ex, status);
+                 static_cast<int>(m_pad), static_cast<int>(layer->k_pad), A, ex, status, win_lo,
+                 win_hi);
     };
     const bool pool = g.pool_kernel > 0;
-    if (ab == 1)
-      launch(pool ? prepare_nchw_kernel<1, true> : prepare_nchw_kernel<1, false>);
-    else
-      launch(pool ? prepare_nchw_kernel<2, true> : prepare_nchw_kernel<2, false>);
+    if (ab == 1) {
+      if (b16)
+        launch(pool ? prepare_nchw_kernel<1, true, true> : prepare_nchw_kernel<1, false, true>);
+      else
+        launch(pool ? prepare_nchw_kernel<1, true, false> : prepare_nchw_kernel<1, false, false>);
+    } else {
+      if (b16)
+        launch(pool ? prepare_nchw_kernel<2, true, true> : prepare_nchw_kernel<2, false, true>);
+      else
+        launch(pool ? prepare_nchw_kernel<2, true, false> : prepare_nchw_kernel<2, false, false>);
+    }
     return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
   }
   // Columns per group thread: as many as still give four waves of 256-thread
@@ -2247,16 +2364,21 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
                                                : kPrepConv;
   auto launch = [&](auto kernel) {
     launch_pdl(kernel, blocks, 256, 0, s, x, dg, div_chunks, T, cols, static_cast<int>(m_pad),
-                                  static_cast<int>(layer->k_pad), A, ex, status);
+               static_cast<int>(layer->k_pad), A, ex, status, win_lo, win_hi);
+  };
+  auto pick = [&](auto ab_tag, auto b16_tag) {
+    constexpr int kAB = decltype(ab_tag)::value;
+    constexpr bool kB = decltype(b16_tag)::value;
+    launch(mode == kPrepRows   ? prepare_kernel<kAB, kPrepRows, kB>
+           : mode == kPrepConv ? prepare_kernel<kAB, kPrepConv, kB>
+                               : prepare_kernel<kAB, kPrepConvPool, kB>);
   };
   if (ab == 1)
-    launch(mode == kPrepRows   ? prepare_kernel<1, kPrepRows>
-           : mode == kPrepConv ? prepare_kernel<1, kPrepConv>
-                               : prepare_kernel<1, kPrepConvPool>);
+    b16 ? pick(std::integral_constant<int, 1>{}, std::true_type{})
+        : pick(std::integral_constant<int, 1>{}, std::false_type{});
   else
-    launch(mode == kPrepRows   ? prepare_kernel<2, kPrepRows>
-           : mode == kPrepConv ? prepare_kernel<2, kPrepConv>
-                               : prepare_kernel<2, kPrepConvPool>);
+    b16 ? pick(std::integral_constant<int, 2>{}, std::true_type{})
+        : pick(std::integral_constant<int, 2>{}, std::false_type{});
   return cuda_ok(cudaGetLastError(), "prepare launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
 }
 
@@ -2304,8 +2426,23 @@ int cim22_cuda_layer_contract_bf16_res(const cim22_cuda_layer *layer, int64_t m,
   const int ab = branches == 2 ? 1 : 2;
   const int T = static_cast<int>(layer->tiles);
   const int8_t *A = static_cast<const int8_t *>(workspace);
-  const int32_t *ex = reinterpret_cast<const int32_t *>(
-      static_cast<const char *>(workspace) + round_up(ab * m_pad * layer->k_pad, 256));
+  const bool b16 = bf16_operands(layer, workspace);
+  const int32_t *ex = reinterpret_cast<const int32_t *>(static_cast<const char *>(workspace) +
+                                                        exponent_offset(layer, m_pad, ab, b16));
+  if (b16) {
+    // The prepare wrote BF16 operand values: only the contraction with BF16
+    // operands reads them.
+    if (!tc::launch_signsplit_b16(reinterpret_cast<const uint16_t *>(A), ex, m_pad,
+                                  layer->operands, layer->exponents, layer->n_pad, layer->k_pad, T,
+                                  m, layer->n, layer->ex_lo, layer->ex_hi, bias, post_scale,
+                                  post_shift, residual, activation, ab, out_pixels, y, status,
+                                  s)) {
+      set_last_error("cim22_cuda_layer_contract_bf16: the contraction with BF16 operands "
+                     "did not launch");
+      return CIM22_STATUS_BAD_ARGUMENT;
+    }
+    return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+  }
   if (tc::signsplit_available() &&
       tc::launch_signsplit(A, ex, m_pad, layer->weights, layer->exponents,
                            layer->n_pad, layer->k_pad, T, m, layer->n, bias, post_scale,

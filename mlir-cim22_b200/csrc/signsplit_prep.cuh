@@ -132,6 +132,74 @@ __device__ __forceinline__ uint2 align8(const uint32_t (&packed)[4], uint32_t mx
   return make_uint2(lo, hi);
 }
 
+// Scaled BF16 operand values of four aligned elements for the contraction
+// with BF16 operands: r holds 2^23 + a for each aligned mantissa a (the bit
+// patterns of the alignment fma); one packed fma per pair computes
+// a * s = r * s + off (off = -2^23 * s, exact), rounded to BF16 exactly (a has
+// at most 7 significant bits). s = 2^(Ex - 133) inside the layer's window,
+// else 1: the unscaled mantissa, restored exactly by the epilogue.
+__device__ __forceinline__ uint2 scale_pairs(const uint32_t (&r)[4], uint64_t s2,
+                                             uint64_t off2) {
+  uint32_t y[4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    asm("{\n\t.reg .b64 a, d;\n\tmov.b64 a, {%2, %3};\n\t"
+        "fma.rn.f32x2 d, a, %4, %5;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=r"(y[2 * h]), "=r"(y[2 * h + 1])
+        : "r"(r[2 * h]), "r"(r[2 * h + 1]), "l"(s2), "l"(off2));
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(__uint_as_float(y[0]), __uint_as_float(y[1]));
+  const __nv_bfloat162 hi = __floats2bfloat162_rn(__uint_as_float(y[2]), __uint_as_float(y[3]));
+  return make_uint2(*reinterpret_cast<const uint32_t *>(&lo),
+                    *reinterpret_cast<const uint32_t *>(&hi));
+}
+
+// The pair {s, s} and {off, off} of scale_pairs for a group of exponent emax
+// (the fast alignment path: emax >= 8).
+__device__ __forceinline__ void operand_scale(int emax, int win_lo, int win_hi, uint64_t &s2,
+                                              uint64_t &off2) {
+  const bool in = emax >= win_lo && emax <= win_hi;
+  const uint32_t s = in ? static_cast<uint32_t>(emax - 6) << 23 : 0x3f800000u;
+  const uint32_t off = in ? 0x80000000u | (static_cast<uint32_t>(emax + 17) << 23) : 0xcb000000u;
+  s2 = (static_cast<uint64_t>(s) << 32) | s;
+  off2 = (static_cast<uint64_t>(off) << 32) | off;
+}
+
+// align8 for the contraction with BF16 operands: the eight elements as
+// scaled BF16 operand values (scale_pairs; unscaled for a group outside
+// [win_lo, win_hi] and for tiny maxima, whose exponent lies below every
+// window), zeros for a zero group.
+__device__ __forceinline__ uint4 align8_b16(const uint32_t (&packed)[4], uint32_t mx, int emax,
+                                            int win_lo, int win_hi) {
+  if (emax == kZeroGroup)
+    return make_uint4(0, 0, 0, 0);
+  if ((mx >> 7) >= 8) {
+    const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax) << 23);
+    uint32_t r[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      r[2 * e] =
+          __float_as_uint(__fmaf_rz(__uint_as_float(packed[e] << 16), scale, 8388608.0f));
+      r[2 * e + 1] = __float_as_uint(
+          __fmaf_rz(__uint_as_float(packed[e] & 0xffff0000u), scale, 8388608.0f));
+    }
+    uint64_t s2, off2;
+    operand_scale(emax, win_lo, win_hi, s2, off2);
+    const uint32_t r0[4] = {r[0], r[1], r[2], r[3]}, r1[4] = {r[4], r[5], r[6], r[7]};
+    const uint2 lo = scale_pairs(r0, s2, off2), hi = scale_pairs(r1, s2, off2);
+    return make_uint4(lo.x, lo.y, hi.x, hi.y);
+  }
+  const int shift = 127 - emax;
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const uint32_t b0 = slow_align(packed[e] & 0xffffu, shift);
+    const uint32_t b1 = slow_align(packed[e] >> 16, shift);
+    w[e] = static_cast<uint32_t>(f32_to_bf16(static_cast<float>(b0))) |
+           (static_cast<uint32_t>(f32_to_bf16(static_cast<float>(b1))) << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 // ExpPrealign of four BF16 magnitudes (packed in pairs) against a group of
 // maximum mx and exponent emax, as bytes of one word; 0 for a zero group
 // (emax == kZeroGroup), which never enters the exact path.
@@ -173,6 +241,29 @@ __device__ __forceinline__ void convert8(const float (&v)[8], unsigned mask, int
 #pragma unroll
   for (int a = 0; a < kActBranches; ++a)
     out[a] = emax[a] == kZeroGroup ? make_uint2(0, 0) : align8(packed[a], mx[a], emax[a]);
+}
+
+// convert8 with the eight elements of each branch as scaled BF16 operand
+// values (align8_b16).
+template <int kActBranches>
+__device__ __forceinline__ void convert8_b16(const float (&v)[8], unsigned mask, int sub,
+                                             int32_t *status, int win_lo, int win_hi,
+                                             uint4 (&out)[2], int (&emax)[2]) {
+  uint32_t packed[2][4];
+  uint32_t mx[2] = {0, 0};
+  uint32_t flags = 0;
+  split8<kActBranches>(v, packed, mx, flags);
+  if (kActBranches == 2 && flags >= 0x7f7f8000u)
+    mx[0] = 0xffffu;
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a)
+#pragma unroll
+    for (int o = 4; o; o >>= 1)
+      mx[a] = max(mx[a], __shfl_xor_sync(mask, mx[a], o, kGroupThreads));
+  group_exponents<kActBranches>(mx, kActBranches == 2 ? 0u : flags, sub == 0, status, emax);
+#pragma unroll
+  for (int a = 0; a < kActBranches; ++a)
+    out[a] = align8_b16(packed[a], mx[a], emax[a], win_lo, win_hi);
 }
 
 __device__ __forceinline__ float apply_act(float v, int act) {

@@ -60,6 +60,33 @@ def test_linear_bf16_extreme_exponents_slow_path():
         np.testing.assert_array_equal(bits(got), bits(expected))
 
 
+@pytest.mark.parametrize("scale_w", [1e-37, 1e36])
+def test_wide_layer_with_extreme_weights_keeps_int8_operands(scale_w):
+    """A 300-lane layer whose weight exponents fall outside the BF16 operand
+    range (below 8: |w| < 2^-119; above 241: |w| >= 2^114) keeps int8
+    mantissas and the int8 tensor-core kernel, bit-exact with the oracle."""
+    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace
+    from cim22_b200.native import lib
+
+    rng = np.random.default_rng(5)
+    m, k, n = 600, 200, 300
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    x *= (1e-10 if scale_w > 1 else 1e10)  # keep the tile values finite and normal
+    w = (rng.standard_normal((n, k)) * scale_w).astype(np.float32)
+    expected = oracle.linear_bf16(x, w, None, branches=4, threads=8)
+    layer = CimLayer(w)
+    assert not layer.bf16_operands
+    xt = torch.from_numpy(x).to(DEV)
+    ws, status = Workspace(torch.device(DEV)), StatusWord(torch.device(DEV))
+    out = torch.empty(m, n, device=DEV)
+    before = lib().cim22_cuda_tensor_core_launches()
+    layer.prepare_bf16(xt, m, branches=4, workspace=ws, status=status)
+    layer.contract_bf16(out, m, branches=4, workspace=ws, status=status)
+    status.raise_if_set()
+    assert lib().cim22_cuda_tensor_core_launches() == before + 1
+    np.testing.assert_array_equal(bits(out.cpu().numpy()), bits(expected))
+
+
 def test_linear_bf16_overflow_and_nan_status():
     from cim22_b200.cim_ops import CimLayer
 
@@ -110,7 +137,14 @@ def test_conv_bf16_bit_exact(layout, c, h, f, kk, stride, pad):
     ("nhwc", 32, 8, 34, 48, 3, 2, 0, 2, 0),
     ("nchw", 40, 6, 14, 16, 5, 1, 0, 2, 2),    # LeNet conv2 shape over a fused pool
     ("nchw", 64, 32, 16, 32, 3, 1, 1, 4, 2),
-    ("nhwc", 64, 32, 16, 32, 3, 1, 1, 4, 2)])  # fused 2x2 max pool over 32x32
+    ("nhwc", 64, 32, 16, 32, 3, 1, 1, 4, 2),   # fused 2x2 max pool over 32x32
+    # 256 lanes: BF16 operand values from every prepare kernel (TMA-staged
+    # whole rows and whole images, thread per group over a fused pool, eight
+    # threads per group) into the contraction with BF16 operands
+    ("nchw", 16, 64, 16, 256, 3, 1, 1, 2, 0),
+    ("nchw", 8, 32, 16, 256, 3, 2, 1, 4, 0),
+    ("nchw", 16, 32, 8, 256, 3, 1, 1, 2, 2),
+    ("nhwc", 16, 32, 16, 256, 3, 1, 1, 4, 0)])
 @pytest.mark.parametrize("out_layout", ["rows", "nchw"])
 def test_conv_bf16_large_batch_bit_exact(layout, n, c, h, f, kk, stride, pad, branches, pool,
                                          out_layout):
@@ -132,6 +166,7 @@ def test_conv_bf16_large_batch_bit_exact(layout, n, c, h, f, kk, stride, pad, br
     b = rng.standard_normal(f).astype(np.float32)
     expected = oracle.conv2d_bf16(pooled, w, b, stride, pad, branches=4, threads=8)
     layer = CimLayer(w.reshape(f, -1))
+    assert layer.bf16_operands == (f >= 256)
     kind = abi.GATHER_CONV_NCHW if layout == "nchw" else abi.GATHER_CONV_NHWC
     g = conv_gather(kind, n, c, h, h, kk, kk, stride, pad)
     if pool:
@@ -306,10 +341,15 @@ def test_linear_int8_tensor_core_shapes(m, k, n):
     (5000, 300, 160, 4, 1.0),
     # per-row scales from 1e-38 to 1e30: fast and exact-path rows share a
     # CTA, and whole rows of zero groups
-    (3000, 256, 96, 4, "rows"), (2048, 130, 64, 2, "rows")])
+    (3000, 256, 96, 4, "rows"), (2048, 130, 64, 2, "rows"),
+    # 256 lanes and more: BF16 operands, with unscaled groups (rows outside
+    # the layer's exponent window) restored exactly
+    (3000, 256, 300, 4, "rows"), (2048, 130, 256, 2, "rows"), (700, 640, 260, 4, 1.0),
+    (512, 4096, 512, 2, 1.0), (600, 200, 320, 4, 1e-30), (512, 64, 256, 4, 1e18)])
 def test_linear_bf16_tensor_core_bit_exact(m, k, n, branches, scale):
-    """Wide layers run the tcgen05 sign-split kernel (launch counter checked).
-    The prepare + contract form always takes it; one-tile layers of at most 64
+    """Wide layers run a tcgen05 sign-split kernel (launch counter checked):
+    int8 mantissas below 256 lanes, BF16 operands from 256 lanes on. The
+    prepare + contract form always takes it; one-tile layers of at most 64
     lanes, which forward_bf16 runs as one thread-per-column kernel, are
     checked through both."""
     from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace
@@ -331,6 +371,7 @@ def test_linear_bf16_tensor_core_bit_exact(m, k, n, branches, scale):
     b = rng.standard_normal(n).astype(np.float32)
     expected = oracle.linear_bf16(x, w, b, branches=4, threads=8)
     layer = CimLayer(w)
+    assert layer.bf16_operands == (n >= 256)
     xt, bt = torch.from_numpy(x).to(DEV), torch.from_numpy(b).to(DEV)
     ws, status = Workspace(torch.device(DEV)), StatusWord(torch.device(DEV))
     out = torch.empty(m, n, device=DEV)
