@@ -556,9 +556,17 @@ def column_bench(args, world: int, rank: int, local: int, dev) -> None:
         raise SystemExit("--parallel columns is defined for the bf16_4x4096 Linear stack")
     linears = [m for m in model.modules() if isinstance(m, torch.nn.Linear)]
     acts = ["gelu"] * (len(linears) - 1) + [None]  # GELU between the layers
-    stack = ColumnShardedStack([l.weight.detach() for l in linears],
-                               [None if l.bias is None else l.bias.detach() for l in linears],
-                               acts, rows, device=local)
+    weights = [l.weight.detach() for l in linears]
+    biases = [None if l.bias is None else l.bias.detach() for l in linears]
+    try:
+        # Peer stores in the contraction epilogue + a device barrier per layer
+        # (every rank's lane block takes BF16 operands).
+        stack = ColumnShardedStack(weights, biases, acts, rows, device=local, fused=True)
+        exchange = "each rank's lanes stored into every rank's output by the contraction " \
+                   "epilogue over NVLink (CUDA IPC), device barrier per layer"
+    except ValueError:
+        stack = ColumnShardedStack(weights, biases, acts, rows, device=local)
+        exchange = "NCCL all-gather per layer"
     xd = x.to(dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -640,8 +648,7 @@ def column_bench(args, world: int, rank: int, local: int, dev) -> None:
             "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"{args.workload}: {w.description}", "global_batch": rows,
-                       "parallelism": f"column-sharded x{world} (lanes split, NCCL all-gather "
-                                      f"per layer)",
+                       "parallelism": f"column-sharded x{world} (lanes split; {exchange})",
                        "l2": L2_NOTE},
             "gpu_launches": 3 * len(stack.layers) * args.steps,
             "e2e": {"value": e2e_value, "unit": UNIT,
@@ -656,6 +663,7 @@ def column_bench(args, world: int, rank: int, local: int, dev) -> None:
             "clocks": clocks.summary(since=t_load),
         }
         print(json.dumps(line), flush=True)
+    stack.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

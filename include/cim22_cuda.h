@@ -677,6 +677,68 @@ int cim22_cuda_slice_copy(const void *src, void *dst, int64_t blocks, int64_t in
  * (trailing blocks may be padded: columns at or past total are dropped). */
 int cim22_cuda_unshard_columns(const float *src, float *dst, int32_t ranks, int64_t rows,
                                int64_t cols, int64_t total, void *stream);
+/* No counterpart in the reference (it runs on one host): peer memory for a
+ * layer whose output lanes are split over the GPUs of one node, so that the
+ * contraction's epilogue writes each rank's lane block straight into every
+ * rank's full output over NVLink (the compute step and the all-gather in one
+ * kernel), and a device-side barrier orders the layers.
+ *
+ * cim22_cuda_device_alloc returns zero-filled device memory of its own
+ * cudaMalloc (an IPC handle covers a whole allocation, so buffers to share
+ * are allocated here); cim22_cuda_ipc_get_handle writes the
+ * CIM22_IPC_HANDLE_BYTES-byte handle of such a buffer, and another process
+ * on the same node maps it with cim22_cuda_ipc_open_handle (peer access
+ * enabled lazily) and unmaps it with cim22_cuda_ipc_close_handle. */
+#define CIM22_IPC_HANDLE_BYTES 64
+#define CIM22_MAX_PEERS 8
+int cim22_cuda_device_alloc(size_t bytes, void **ptr);
+int cim22_cuda_device_free(void *ptr);
+int cim22_cuda_ipc_get_handle(const void *base, void *handle);
+int cim22_cuda_ipc_open_handle(const void *handle, void **base);
+int cim22_cuda_ipc_close_handle(void *base);
+
+/* Where a column-sharded layer's outputs go: out[p] is rank p's full
+ * [rows][row_stride] f32 output as mapped on this device (out[rank] the
+ * local one); this rank's lanes land in columns lane_offset .. lane_offset +
+ * lanes - 1 of every out[p] (the layer's further lanes are padding and are
+ * not stored). */
+typedef struct cim22_peer_outputs {
+  float *out[CIM22_MAX_PEERS];
+  int32_t ranks;
+  int64_t row_stride;
+  int64_t lane_offset;
+  int64_t lanes;
+} cim22_peer_outputs;
+
+/* cim22_cuda_layer_contract_bf16 for a layer with BF16 operands
+ * (cim22_cuda_layer_bf16_operands) whose outputs are rows: the epilogue
+ * stores every output value into all peers' buffers of `peers` (float4
+ * stores where row_stride, lane_offset and the buffers allow) and makes
+ * them visible system-wide before the kernel ends. Prepare with
+ * cim22_cuda_layer_prepare_bf16 into the same workspace first. */
+int cim22_cuda_layer_contract_bf16_peers(const cim22_cuda_layer *layer, int64_t m,
+                                         const float *bias, int32_t activation,
+                                         int32_t branches, const cim22_peer_outputs *peers,
+                                         const void *workspace, size_t workspace_bytes,
+                                         int32_t *status, void *stream);
+
+/* A barrier of `ranks` GPUs in one launch per rank: flags[p] is rank p's
+ * array of ranks + 1 int32 words (zero-filled at allocation) as mapped on
+ * this device. One thread raises this rank's epoch (the last word of its own
+ * array), makes every earlier write of the stream visible system-wide,
+ * stores the epoch into word `rank` of every rank's array and waits until
+ * every word of its own array holds at least that epoch. A wait that runs
+ * out after limit_ns of the GPU's global timer ORs CIM22_STATUS_TIMEOUT into
+ * *status and returns (the outputs of the step are then invalid). Every rank
+ * makes the same sequence of barrier calls. */
+typedef struct cim22_peer_flags {
+  int32_t *flags[CIM22_MAX_PEERS];
+  int32_t ranks;
+  int32_t rank;
+} cim22_peer_flags;
+int cim22_cuda_peer_barrier(const cim22_peer_flags *flags, uint64_t limit_ns, int32_t *status,
+                            void *stream);
+
 /* The pooling and affine glue on NCHW batches [n, c, h, w]. */
 int cim22_cuda_maxpool2d_nchw(const float *x, float *y, int32_t n, int32_t c,
                               int32_t h, int32_t w, int32_t kernel,

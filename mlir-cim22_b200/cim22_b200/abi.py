@@ -210,6 +210,32 @@ class ChainLayer(ctypes.Structure):
 CHAIN_LINEAR = 0
 CHAIN_CONV = 1
 
+MAX_PEERS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class PeerOutputs(ctypes.Structure):
+    """cim22_peer_outputs: each rank's full [rows][row_stride] output as mapped
+    on this device, and this rank's lane block within a row."""
+    _fields_ = [
+        ("out", ctypes.c_void_p * MAX_PEERS),
+        ("ranks", ctypes.c_int32),
+        ("row_stride", ctypes.c_int64),
+        ("lane_offset", ctypes.c_int64),
+        ("lanes", ctypes.c_int64),
+    ]
+
+
+class PeerFlags(ctypes.Structure):
+    """cim22_peer_flags: each rank's barrier words (ranks + 1 int32) as mapped
+    on this device, the world size and this rank."""
+    _fields_ = [
+        ("flags", ctypes.c_void_p * MAX_PEERS),
+        ("ranks", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+    ]
+
+
 ABI_STRUCTS = (
     FramePacket,
     StaticWeight,
@@ -222,6 +248,8 @@ ABI_STRUCTS = (
     Memref2D,
     Gather,
     ChainLayer,
+    PeerOutputs,
+    PeerFlags,
 )
 
 

@@ -66,6 +66,13 @@ _SIGNATURES = {
     "cim22_cuda_layer_destroy": (None, [P]),
     "cim22_cuda_layer_range_safe": (c.c_int, [P]),
     "cim22_cuda_layer_bf16_operands": (c.c_int, [P]),
+    "cim22_cuda_device_alloc": (c.c_int, [SZ, c.POINTER(c.c_void_p)]),
+    "cim22_cuda_device_free": (c.c_int, [P]),
+    "cim22_cuda_ipc_get_handle": (c.c_int, [P, P]),
+    "cim22_cuda_ipc_open_handle": (c.c_int, [P, c.POINTER(c.c_void_p)]),
+    "cim22_cuda_ipc_close_handle": (c.c_int, [P]),
+    "cim22_cuda_layer_contract_bf16_peers": (c.c_int, [P, I64, P, I32, I32, P, P, SZ, P, P]),
+    "cim22_cuda_peer_barrier": (c.c_int, [P, c.c_uint64, P, P]),
     "cim22_cuda_layer_n": (I64, [P]),
     "cim22_cuda_layer_k": (I64, [P]),
     "cim22_cuda_layer_workspace_bf16": (SZ, [P, I64, I32]),

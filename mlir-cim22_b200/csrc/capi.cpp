@@ -58,7 +58,8 @@ int cim22_cuda_abi_sizes(int64_t *sizes, int capacity) {
       sizeof(cim22_work),          sizeof(cim22_group),
       sizeof(cim22_transaction),   sizeof(cim22_trace_event),
       sizeof(cim22_memref2d),      sizeof(cim22_gather),
-      sizeof(cim22_chain_layer)};
+      sizeof(cim22_chain_layer),   sizeof(cim22_peer_outputs),
+      sizeof(cim22_peer_flags)};
   const int n = static_cast<int>(sizeof(all) / sizeof(all[0]));
   if (sizes)
     for (int i = 0; i < std::min(n, capacity); ++i)

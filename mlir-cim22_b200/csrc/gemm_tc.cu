@@ -480,16 +480,13 @@ __device__ __forceinline__ void prefetch_residual(const float *residual, int row
 // RNE conversion rounds them as the reference's truncf does. cache, when not
 // null, holds the bias, scale and shift of every lane in shared memory.
 template <int kAB, int LT>
-__device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, int lane0, int M,
-                                           int N, int T, const float (*cache)[kParamLanes],
-                                           const float *__restrict__ bias,
-                                           const float *__restrict__ post_scale,
-                                           const float *__restrict__ post_shift,
-                                           const float *__restrict__ residual, int act,
-                                           int vec, int out_pixels, FastDiv div_pix,
-                                           float *__restrict__ y) {
-  if (row >= M)
-    return;
+__device__ __forceinline__ void tile_values(float (&acc)[kAB][2][LT], int row, int lane0, int N,
+                                            int T, const float (*cache)[kParamLanes],
+                                            const float *__restrict__ bias,
+                                            const float *__restrict__ post_scale,
+                                            const float *__restrict__ post_shift,
+                                            const float *__restrict__ residual, int act, int vec,
+                                            int out_pixels, FastDiv div_pix, float (&o)[LT]) {
   if (T > 1) {
 #pragma unroll
     for (int a = 0; a < kAB; ++a)
@@ -502,7 +499,6 @@ __device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, in
           acc[a][w][j + 1] = __high2float(h);
         }
   }
-  float o[LT];
 #pragma unroll
   for (int j = 0; j < LT; ++j) {
     o[j] = __fsub_rn(acc[0][0][j], acc[0][1][j]);
@@ -573,6 +569,23 @@ __device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, in
     for (int j = 0; j < LT; ++j)
       o[j] = act_tc(o[j], CIM22_ACT_GELU);
   }
+}
+
+template <int kAB, int LT>
+__device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, int lane0, int M,
+                                           int N, int T, const float (*cache)[kParamLanes],
+                                           const float *__restrict__ bias,
+                                           const float *__restrict__ post_scale,
+                                           const float *__restrict__ post_shift,
+                                           const float *__restrict__ residual, int act,
+                                           int vec, int out_pixels, FastDiv div_pix,
+                                           float *__restrict__ y) {
+  if (row >= M)
+    return;
+  float o[LT];
+  tile_values<kAB, LT>(acc, row, lane0, N, T, cache, bias, post_scale, post_shift, residual, act,
+                       vec, out_pixels, div_pix, o);
+  const bool full = lane0 + LT <= N;
   if (out_pixels > 0) {
     const int image = fdiv(row, div_pix);
     float *dst = y + (static_cast<int64_t>(image) * N + lane0) * out_pixels +
@@ -591,6 +604,41 @@ __device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, in
 #pragma unroll
       for (int j = 0; j < LT; ++j)
         if (lane0 + j < N)
+          dst[j] = o[j];
+    }
+  }
+}
+
+// store_tile for a column-sharded layer: the row's LT lanes go into every
+// rank's full output (peer memory mapped on this device) at the rank's lane
+// offset; lanes at or past peers.lanes are padding and are not stored.
+// vec4: row_stride, lane_offset and every output base allow float4 stores.
+template <int kAB, int LT>
+__device__ __forceinline__ void store_tile_peers(float (&acc)[kAB][2][LT], int row, int lane0,
+                                                 int M, int N, int T,
+                                                 const float (*cache)[kParamLanes],
+                                                 const float *__restrict__ bias,
+                                                 const float *__restrict__ post_scale,
+                                                 const float *__restrict__ post_shift, int act,
+                                                 int vec, const cim22_peer_outputs &peers,
+                                                 bool vec4) {
+  if (row >= M)
+    return;
+  float o[LT];
+  tile_values<kAB, LT>(acc, row, lane0, N, T, cache, bias, post_scale, post_shift, nullptr, act,
+                       vec, 0, FastDiv{1, 0, 0}, o);
+  const int64_t off = static_cast<int64_t>(row) * peers.row_stride + peers.lane_offset + lane0;
+  const bool full = lane0 + LT <= peers.lanes;
+  for (int p = 0; p < peers.ranks; ++p) {
+    float *dst = peers.out[p] + off;
+    if (full && vec4) {
+#pragma unroll
+      for (int j4 = 0; j4 < LT; j4 += 4)
+        *reinterpret_cast<float4 *>(dst + j4) = make_float4(o[j4], o[j4 + 1], o[j4 + 2], o[j4 + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < LT; ++j)
+        if (lane0 + j < peers.lanes)
           dst[j] = o[j];
     }
   }
@@ -974,7 +1022,9 @@ __device__ __forceinline__ void restore_b16_raw(float (&acc)[kLT], const uint32_
   }
 }
 
-template <int kAB, bool kRes>
+// kPeer: a column-sharded layer whose rows go to every rank's full output
+// (store_tile_peers), made visible system-wide before the CTA ends.
+template <int kAB, bool kRes, bool kPeer>
 __global__ void __launch_bounds__(kSThreads, 1)
     signsplit_b16_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB,
@@ -985,7 +1035,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
                          const float *__restrict__ post_shift,
                          const float *__restrict__ residual_arg, int act, int vec,
                          int out_pixels, FastDiv div_pix, float *__restrict__ y,
-                         int32_t *status) {
+                         int32_t *status, const __grid_constant__ cim22_peer_outputs peers,
+                         int peer_vec4) {
   const float *residual = kRes ? residual_arg : nullptr;
   using S = SSShape<kAB>;
   constexpr int L = S::L, LT = S::LT, SN = S::N;
@@ -1189,14 +1240,20 @@ __global__ void __launch_bounds__(kSThreads, 1)
       }
       if (!ok)
         break;
-      store_tile<kAB, LT>(acc, row, lane0, M, N, T, cached ? s.lane_params : nullptr, bias,
-                          post_scale, post_shift, residual, act, vec, out_pixels, div_pix, y);
+      if constexpr (kPeer)
+        store_tile_peers<kAB, LT>(acc, row, lane0, M, N, T, cached ? s.lane_params : nullptr,
+                                  bias, post_scale, post_shift, act, vec, peers, peer_vec4 != 0);
+      else
+        store_tile<kAB, LT>(acc, row, lane0, M, N, T, cached ? s.lane_params : nullptr, bias,
+                            post_scale, post_shift, residual, act, vec, out_pixels, div_pix, y);
     }
     if (!ok) {
       *failed = 1;
       if (lane == 0)
         atomicOr(status, CIM22_STATUS_TIMEOUT);
     }
+    if constexpr (kPeer)
+      __threadfence_system();
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -1567,8 +1624,25 @@ bool launch_signsplit_b16(const uint16_t *A, const int32_t *exA, int64_t m_pad,
                           int T, int64_t M, int64_t N, int ex_lo, int ex_hi, const float *bias,
                           const float *post_scale, const float *post_shift,
                           const float *residual, int act, int act_branches, int64_t out_pixels,
-                          float *y, int32_t *status, cudaStream_t stream) {
+                          float *y, int32_t *status, cudaStream_t stream,
+                          const cim22_peer_outputs *peers) {
   const int L = act_branches == 2 ? SSShape<2>::L : SSShape<1>::L;
+  cim22_peer_outputs none{};
+  const bool peer = peers != nullptr;
+  if (peer && (out_pixels != 0 || residual != nullptr || peers->ranks < 1 ||
+               peers->ranks > CIM22_MAX_PEERS || peers->lanes < 1 || peers->lanes > N ||
+               peers->lane_offset < 0 || peers->lane_offset + peers->lanes > peers->row_stride))
+    return false;
+  int peer_vec4 = 0;
+  if (peer) {
+    peer_vec4 = peers->row_stride % 4 == 0 && peers->lane_offset % 4 == 0;
+    for (int p = 0; p < peers->ranks; ++p) {
+      if (!peers->out[p])
+        return false;
+      if (reinterpret_cast<uintptr_t>(peers->out[p]) & 15)
+        peer_vec4 = 0;
+    }
+  }
   if (M < 1 || N <= 8 || m_pad % kSBM || n_pad % 128 || k_pad % 64 || ex_lo > ex_hi ||
       static_cast<int64_t>(act_branches) * m_pad >= (int64_t{1} << 31) ||
       (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
@@ -1590,15 +1664,22 @@ bool launch_signsplit_b16(const uint16_t *A, const int32_t *exA, int64_t m_pad,
                static_cast<int>(n_pad), T, static_cast<int>(M), static_cast<int>(N), ex_lo,
                ex_hi, make_fastdiv(static_cast<uint32_t>((N + L - 1) / L)), bias, post_scale,
                post_shift, residual, act, vec, static_cast<int>(out_pixels),
-               make_fastdiv(static_cast<uint32_t>(out_pixels > 0 ? out_pixels : 1)), y, status);
+               make_fastdiv(static_cast<uint32_t>(out_pixels > 0 ? out_pixels : 1)), y, status,
+               peer ? *peers : none, peer_vec4);
     return true;
   };
   const bool res = residual != nullptr;
-  if (!(act_branches == 2
-            ? (res ? launch(signsplit_b16_kernel<2, true>, smem_sb<2>())
-                   : launch(signsplit_b16_kernel<2, false>, smem_sb<2>()))
-            : (res ? launch(signsplit_b16_kernel<1, true>, smem_sb<1>())
-                   : launch(signsplit_b16_kernel<1, false>, smem_sb<1>()))))
+  bool launched;
+  if (peer)
+    launched = act_branches == 2 ? launch(signsplit_b16_kernel<2, false, true>, smem_sb<2>())
+                                 : launch(signsplit_b16_kernel<1, false, true>, smem_sb<1>());
+  else
+    launched = act_branches == 2
+                   ? (res ? launch(signsplit_b16_kernel<2, true, false>, smem_sb<2>())
+                          : launch(signsplit_b16_kernel<2, false, false>, smem_sb<2>()))
+                   : (res ? launch(signsplit_b16_kernel<1, true, false>, smem_sb<1>())
+                          : launch(signsplit_b16_kernel<1, false, false>, smem_sb<1>()));
+  if (!launched)
     return false;
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
   return true;

@@ -5,6 +5,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "../../include/cim22_cuda.h"
+
 namespace cim::tc {
 
 // The weight scales of the sign-split contraction are stored as
@@ -48,12 +50,15 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad,
 // tcgen05 MMAs (kind::f16, f32 accumulation) then give each crossbar dot as
 // the exact f32 value p * 2^(Ex + Ew - 266) (p * 2^(Ew - 133) for unscaled
 // groups). Same outputs, options and return convention as launch_signsplit.
+// With peers (rows output, no residual) every output row is stored into all
+// ranks' full outputs instead of y (see cim22_cuda_layer_contract_bf16_peers).
 bool launch_signsplit_b16(const uint16_t *A, const int32_t *exA, int64_t m_pad,
                           const uint16_t *B, const int32_t *exB, int64_t n_pad, int64_t k_pad,
                           int T, int64_t M, int64_t N, int ex_lo, int ex_hi, const float *bias,
                           const float *post_scale, const float *post_shift,
                           const float *residual, int act, int act_branches, int64_t out_pixels,
-                          float *y, int32_t *status, cudaStream_t stream);
+                          float *y, int32_t *status, cudaStream_t stream,
+                          const cim22_peer_outputs *peers = nullptr);
 
 // INT8 contraction with whole-K int32 accumulation (exact: range-proven
 // layers, or unproven ones computed as the Host computes them).

@@ -2461,6 +2461,39 @@ int cim22_cuda_layer_contract_bf16_res(const cim22_cuda_layer *layer, int64_t m,
   return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
 }
 
+int cim22_cuda_layer_contract_bf16_peers(const cim22_cuda_layer *layer, int64_t m,
+                                         const float *bias, int32_t activation,
+                                         int32_t branches, const cim22_peer_outputs *peers,
+                                         const void *workspace, size_t workspace_bytes,
+                                         int32_t *status, void *stream) {
+  if (!layer || !layer->bf16 || !peers || !status || m <= 0 ||
+      (branches != 2 && branches != 4) || activation < 0 || activation > 2 || !workspace ||
+      workspace_bytes < cim22_cuda_layer_workspace_bf16(layer, m, branches)) {
+    set_last_error("invalid arguments to cim22_cuda_layer_contract_bf16_peers");
+    return CIM22_STATUS_BAD_ARGUMENT;
+  }
+  if (!bf16_operands(layer, workspace)) {
+    set_last_error("cim22_cuda_layer_contract_bf16_peers: the layer does not take BF16 "
+                   "operands (see cim22_cuda_layer_bf16_operands)");
+    return CIM22_STATUS_BAD_ARGUMENT;
+  }
+  const int64_t m_pad = round_up(m, kColumnPad);
+  const int ab = branches == 2 ? 1 : 2;
+  const uint16_t *A = static_cast<const uint16_t *>(workspace);
+  const int32_t *ex = reinterpret_cast<const int32_t *>(static_cast<const char *>(workspace) +
+                                                        exponent_offset(layer, m_pad, ab, true));
+  if (!tc::launch_signsplit_b16(A, ex, m_pad, layer->operands, layer->exponents, layer->n_pad,
+                                layer->k_pad, static_cast<int>(layer->tiles), m, layer->n,
+                                layer->ex_lo, layer->ex_hi, bias, nullptr, nullptr, nullptr,
+                                activation, ab, 0, nullptr, status,
+                                static_cast<cudaStream_t>(stream), peers)) {
+    set_last_error("cim22_cuda_layer_contract_bf16_peers: invalid peer outputs (1 to 8 "
+                   "ranks, lanes within the layer, columns within row_stride)");
+    return CIM22_STATUS_BAD_ARGUMENT;
+  }
+  return cuda_ok(cudaGetLastError(), "signsplit launch") ? 0 : CIM22_STATUS_BAD_ARGUMENT;
+}
+
 int cim22_cuda_layer_contract_bf16_ex(const cim22_cuda_layer *layer, int64_t m,
                                       int64_t out_pixels, const float *bias,
                                       const float *post_scale, const float *post_shift,
