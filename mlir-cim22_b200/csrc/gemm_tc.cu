@@ -318,10 +318,18 @@ template <int kAB> struct SSShape {
   static constexpr int N = 2 * L;              // MMA N: Wp and Wn rows
 };
 
+// One kScaleBlockWords weight record: the epilogue scales
+// 2^(Ew - 133 + kScaleShift) of a 32-lane block's Wp and Wn lanes and the
+// block's weight-exponent range {min, max, ex_lo, ex_hi}.
+struct alignas(16) ExpBlock {
+  float w[2][32];
+  int32_t range[4];
+};
+static_assert(sizeof(ExpBlock) == kScaleBlockWords * 4, "weight record layout");
+
 struct alignas(16) ExpSlot {
   int32_t a[2][kSBM]; // activation group exponents per branch
-  float w[2][64];     // weight scales 2^(Ew - 133 + kScaleShift), Wp then Wn
-  int32_t range[8];   // {min, max, 0, 0} weight exponent per 32-lane block
+  ExpBlock blk[2];    // the tile's weight records of the output tile's 32-lane blocks
 };
 
 template <int kAB> struct alignas(1024) SmemSS {
@@ -671,6 +679,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
   // scales 2^(Ew - 133) [2][T][n_pad] that the CUDA-core kernels read.
   const float *scales =
       reinterpret_cast<const float *>(ranges + int64_t{n_pad / 32} * T * 4) + 2 * T * n_pad;
+  // Then the per-(tile, 32-lane block) weight records.
+  const int32_t *wrecs = reinterpret_cast<const int32_t *>(scales) + 2 * T * n_pad;
   constexpr uint32_t kTmemCols = kTmemBufs * kBufCols;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSStages; ++i) {
@@ -714,14 +724,17 @@ __global__ void __launch_bounds__(kSThreads, 1)
   pdl_wait();
 
   if (warp == 0 && lane == 0) {
-    uint32_t kbi = 0, gi = 0;
+    // Ring positions and phase parities advance incrementally (this
+    // thread's per-tile instruction chain is on the kernel's critical path);
+    // a failure elsewhere shows up as a bounded wait that runs out.
+    uint32_t kbi = 0, gi = 0, stage = 0, sphase = 0, slot = 0, xphase = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
       const int mb = fdiv(ot, div_nb);
       const int m0 = mb * kSBM, nb = ot - mb * num_nb, n0 = nb * L;
+      const int32_t *wrec = wrecs + static_cast<int64_t>(n0 / 32) * kScaleBlockWords;
       for (int kb = 0; kb < num_kb; ++kb, ++kbi) {
-        const int stage = kbi % kSStages;
-        if (!mbar_wait(&s.empty[stage], ((kbi / kSStages) & 1) ^ 1) || *failed) {
+        if (!mbar_wait(&s.empty[stage], sphase ^ 1)) {
           ok = false;
           break;
         }
@@ -731,24 +744,27 @@ __global__ void __launch_bounds__(kSThreads, 1)
           tma_load_2d(s.a[stage][a], &tmA, &s.full[stage], kb * kSBK, a * m_pad + m0);
         tma_load_2d(s.b[stage], &tmB, &s.full[stage], kb * kSBK, n0);
         tma_load_2d(s.b[stage] + L * kSBK, &tmB, &s.full[stage], kb * kSBK, n_pad + n0);
+        if (++stage == kSStages) {
+          stage = 0;
+          sphase ^= 1;
+        }
         for (int t = 2 * kb; t < 2 * kb + 2 && t < T; ++t, ++gi) {
-          const int slot = gi % kExpSlots;
-          if (!mbar_wait(&s.exempty[slot], ((gi / kExpSlots) & 1) ^ 1) || *failed) {
+          if (!mbar_wait(&s.exempty[slot], xphase ^ 1)) {
             ok = false;
             break;
           }
           ExpSlot &e = s.ex[slot];
-          mbar_expect_tx(&s.exfull[slot], kAB * kSBM * 4 + 2 * L * 4 + (L / 32) * 16);
+          mbar_expect_tx(&s.exfull[slot], kAB * kSBM * 4 + (L / 32) * kScaleBlockWords * 4);
 #pragma unroll
           for (int a = 0; a < kAB; ++a)
             bulk_load(e.a[a], exA + (static_cast<int64_t>(a) * T + t) * m_pad + m0, kSBM * 4,
                       &s.exfull[slot]);
-#pragma unroll
-          for (int w = 0; w < 2; ++w)
-            bulk_load(e.w[w], scales + (static_cast<int64_t>(w) * T + t) * n_pad + n0, L * 4,
-                      &s.exfull[slot]);
-          bulk_load(e.range, ranges + (static_cast<int64_t>(t) * (n_pad / 32) + n0 / 32) * 4,
-                    (L / 32) * 16, &s.exfull[slot]);
+          bulk_load(e.blk, wrec + static_cast<int64_t>(t) * (n_pad / 32) * kScaleBlockWords,
+                    (L / 32) * kScaleBlockWords * 4, &s.exfull[slot]);
+          if (++slot == kExpSlots) {
+            slot = 0;
+            xphase ^= 1;
+          }
         }
         if (!ok) {
           ++kbi;
@@ -766,22 +782,26 @@ __global__ void __launch_bounds__(kSThreads, 1)
       mbar_wait(&s.exfull[i % kExpSlots], (i / kExpSlots) & 1);
   } else if (warp == 1 && lane == 0) {
     // MMA issuer: two K=32 MMAs per branch per crossbar tile.
+    // The kernel's critical path: ring positions advance incrementally and
+    // the descriptors step by constant strides.
     constexpr uint32_t idesc = idesc_i8(kSBM, SN);
-    uint32_t kbi = 0, gi = 0;
+    constexpr uint64_t kAStep = sizeof(s.a[0]) >> 4, kBStep = sizeof(s.b[0]) >> 4;
+    const uint64_t adesc0 = sw128_desc(s.a[0][0]), bdesc0 = sw128_desc(s.b[0]);
+    uint32_t kbi = 0, gi = 0, stage = 0, sphase = 0, buf = 0, dphase = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
       for (int t = 0; t < T; ++t, ++gi) {
-        const int half = t % 2, stage = kbi % kSStages, buf = gi % kTmemBufs;
-        if ((half == 0 && !mbar_wait(&s.full[stage], (kbi / kSStages) & 1)) ||
-            !mbar_wait(&s.dempty[buf], ((gi / kTmemBufs) & 1) ^ 1) || *failed) {
+        const int half = t & 1;
+        if ((half == 0 && !mbar_wait(&s.full[stage], sphase)) ||
+            !mbar_wait(&s.dempty[buf], dphase ^ 1)) {
           ok = false;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint64_t bdesc = sw128_desc(s.b[stage]) + half * 4;
+        const uint64_t bdesc = bdesc0 + stage * kBStep + half * 4;
 #pragma unroll
         for (int a = 0; a < kAB; ++a) {
-          const uint64_t adesc = sw128_desc(s.a[stage][a]) + half * 4;
+          const uint64_t adesc = adesc0 + stage * kAStep + a * (kSBM * kSBK >> 4) + half * 4;
           const uint32_t d = tmem + buf * kBufCols + a * SN;
           mma_i8(d, adesc, bdesc, idesc, 0u);
           mma_i8(d, adesc + 2, bdesc + 2, idesc, 1u);
@@ -790,6 +810,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
         if (half == 1 || t == T - 1) {
           mma_commit(&s.empty[stage]);
           ++kbi;
+          if (++stage == kSStages) {
+            stage = 0;
+            sphase ^= 1;
+          }
+        }
+        if (++buf == kTmemBufs) {
+          buf = 0;
+          dphase ^= 1;
         }
       }
     }
@@ -803,7 +831,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
     const int quad = warp % 4, sub = (warp - 2) / 4;
     const int row_local = quad * 32 + lane;
     const uint32_t tlane = static_cast<uint32_t>(quad * 32) << 16;
-    uint32_t gi = 0;
+    // The thread's lanes within the output tile: record (sub * LT) / 32 of
+    // a tile's weight records, from lane (sub * LT) % 32 on.
+    const int rec = (sub * LT) >> 5, rec_lane = (sub * LT) & 31;
+    uint32_t gi = 0, buf = 0, dphase = 0, slot = 0, xphase = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
       const int mb = fdiv(ot, div_nb);
@@ -822,20 +853,19 @@ __global__ void __launch_bounds__(kSThreads, 1)
       // faster there; 2-branch layers run slower unrolled).
 #pragma unroll(kAB == 2 ? 2 : 1)
       for (int t = 0; t < T; ++t, ++gi) {
-        const int slot = gi % kExpSlots, buf = gi % kTmemBufs;
         // A failure elsewhere in the CTA shows up here as a wait that runs
         // out, so the per-tile waits do not poll the failure flag.
-        if (!mbar_wait(&s.exfull[slot], (gi / kExpSlots) & 1)) {
+        if (!mbar_wait(&s.exfull[slot], xphase)) {
           ok = false;
           break;
         }
         const ExpSlot &e = s.ex[slot];
         // Fast window for this tile's weights, ex_lo <= Ex <= ex_hi: the
         // intersection of its 32-lane blocks' windows (tabulated at load).
-        int ex_lo = e.range[2], ex_hi = e.range[3];
+        int ex_lo = e.blk[0].range[2], ex_hi = e.blk[0].range[3];
         if (L == 64) {
-          ex_lo = max(ex_lo, e.range[6]);
-          ex_hi = min(ex_hi, e.range[7]);
+          ex_lo = max(ex_lo, e.blk[1].range[2]);
+          ex_hi = min(ex_hi, e.blk[1].range[3]);
         }
         float sx[kAB];
         bool fast[kAB];
@@ -852,7 +882,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                       ? __uint_as_float(static_cast<uint32_t>(ex[a] + 143 - kScaleShift) << 23)
                       : 0.0f;
         }
-        if (!mbar_wait(&s.dfull[buf], (gi / kTmemBufs) & 1)) {
+        if (!mbar_wait(&s.dfull[buf], dphase)) {
           ok = false;
           break;
         }
@@ -866,7 +896,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
           for (int w = 0; w < 2; ++w) {
             uint32_t p[LT];
             tmem_ld_wait(col0 + w * L, p);
-            restore_fast<LT>(acc[0][w], p, sx[0], &e.w[w][sub * LT]);
+            restore_fast<LT>(acc[0][w], p, sx[0], &e.blk[rec].w[w][rec_lane]);
             // One warp-uniform test: rows outside the window (rare) add their
             // exact tile values to the sums the fast pass kept.
             if (__any_sync(0xffffffffu, !fast[0])) {
@@ -886,8 +916,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
             tmem_ld(col0 + a * SN + L, p1);
             tmem_wait(p0);
             tmem_wait(p1);
-            restore_fast<LT>(acc[a][0], p0, sx[a], &e.w[0][sub * LT]);
-            restore_fast<LT>(acc[a][1], p1, sx[a], &e.w[1][sub * LT]);
+            restore_fast<LT>(acc[a][0], p0, sx[a], &e.blk[rec].w[0][rec_lane]);
+            restore_fast<LT>(acc[a][1], p1, sx[a], &e.blk[rec].w[1][rec_lane]);
             if (__any_sync(0xffffffffu, !fast[a])) {
               if (!fast[a]) {
                 const int64_t ew0 = static_cast<int64_t>(t) * n_pad + lane0;
@@ -905,6 +935,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
         if (lane == 0) {
           mbar_arrive(&s.dempty[buf]);
           mbar_arrive(&s.exempty[slot]);
+        }
+        if (++buf == kTmemBufs) {
+          buf = 0;
+          dphase ^= 1;
+        }
+        if (++slot == kExpSlots) {
+          slot = 0;
+          xphase ^= 1;
         }
       }
       if (!ok)
@@ -1089,15 +1127,18 @@ __global__ void __launch_bounds__(kSThreads, 1)
     // TMA producer: per crossbar tile the activation tile of each branch
     // and the stacked Wp / Wn tile into the stage ring, the tile's activation
     // exponents of the 128 rows into the exponent ring.
-    uint32_t it = 0;
+    // Ring positions and phase parities advance incrementally: this thread
+    // is the ring's only producer, and its per-tile instruction chain (not
+    // the copies) is on the kernel's critical path. A failure elsewhere
+    // shows up as a bounded wait that runs out.
+    uint32_t it = 0, stage = 0, sphase = 0, slot = 0, xphase = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
       const int mb = fdiv(ot, div_nb);
       const int m0 = mb * kSBM, nb = ot - mb * num_nb, n0 = nb * L;
       for (int t = 0; t < T; ++t, ++it) {
-        const int stage = it % kStages, slot = it % kExSlots;
-        if (!mbar_wait(&s.empty[stage], ((it / kStages) & 1) ^ 1) ||
-            !mbar_wait(&s.exempty[slot], ((it / kExSlots) & 1) ^ 1) || *failed) {
+        if (!mbar_wait(&s.empty[stage], sphase ^ 1) ||
+            !mbar_wait(&s.exempty[slot], xphase ^ 1)) {
           ok = false;
           break;
         }
@@ -1112,6 +1153,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
         for (int a = 0; a < kAB; ++a)
           bulk_load(s.exa[slot][a], exA + (static_cast<int64_t>(a) * T + t) * m_pad + m0,
                     kSBM * 4, &s.exfull[slot]);
+        if (++stage == kStages) {
+          stage = 0;
+          sphase ^= 1;
+        }
+        if (++slot == kExSlots) {
+          slot = 0;
+          xphase ^= 1;
+        }
       }
     }
     if (!ok)
@@ -1125,22 +1174,24 @@ __global__ void __launch_bounds__(kSThreads, 1)
       mbar_wait(&s.exfull[i % kExSlots], (i / kExSlots) & 1);
   } else if (warp == 1 && lane == 0) {
     // MMA issuer: four K=16 MMAs per activation branch and crossbar tile.
+    // The critical path of the kernel: ring positions advance incrementally
+    // and the descriptors step by constant strides.
     constexpr uint32_t idesc = idesc_bf16(kSBM, SN);
-    uint32_t gi = 0;
+    constexpr uint64_t kAStep = sizeof(s.a[0]) >> 4, kBStep = sizeof(s.b[0]) >> 4;
+    const uint64_t adesc0 = sw128_desc(s.a[0][0]), bdesc0 = sw128_desc(s.b[0]);
+    uint32_t gi = 0, stage = 0, sphase = 0, buf = 0, dphase = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
       for (int t = 0; t < T; ++t, ++gi) {
-        const int stage = gi % kStages, buf = gi % kTmemBufs;
-        if (!mbar_wait(&s.full[stage], (gi / kStages) & 1) ||
-            !mbar_wait(&s.dempty[buf], ((gi / kTmemBufs) & 1) ^ 1) || *failed) {
+        if (!mbar_wait(&s.full[stage], sphase) || !mbar_wait(&s.dempty[buf], dphase ^ 1)) {
           ok = false;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint64_t bdesc = sw128_desc(s.b[stage]);
+        const uint64_t bdesc = bdesc0 + stage * kBStep;
 #pragma unroll
         for (int a = 0; a < kAB; ++a) {
-          const uint64_t adesc = sw128_desc(s.a[stage][a]);
+          const uint64_t adesc = adesc0 + stage * kAStep + a * (kSBM * 64 * 2 >> 4);
           const uint32_t d = tmem + buf * kBufCols + a * SN;
 #pragma unroll
           for (int k = 0; k < 4; ++k)
@@ -1148,6 +1199,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
         }
         mma_commit(&s.dfull[buf]);
         mma_commit(&s.empty[stage]);
+        if (++stage == kStages) {
+          stage = 0;
+          sphase ^= 1;
+        }
+        if (++buf == kTmemBufs) {
+          buf = 0;
+          dphase ^= 1;
+        }
       }
     }
     if (!ok)
@@ -1161,7 +1220,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
     const int row_local = quad * 32 + lane;
     const uint32_t tlane = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t span = static_cast<uint32_t>(ex_hi - ex_lo);
-    uint32_t gi = 0;
+    uint32_t gi = 0, buf = 0, dphase = 0, slot = 0, xphase = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
       const int mb = fdiv(ot, div_nb);
@@ -1178,9 +1237,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
           for (int j = 0; j < LT; ++j)
             acc[a][w][j] = 0.0f;
       for (int t = 0; t < T; ++t, ++gi) {
-        const int buf = gi % kTmemBufs, slot = gi % kExSlots;
         // A failure elsewhere in the CTA shows up here as a wait that runs out.
-        if (!mbar_wait(&s.exfull[slot], (gi / kExSlots) & 1)) {
+        if (!mbar_wait(&s.exfull[slot], xphase)) {
           ok = false;
           break;
         }
@@ -1191,7 +1249,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
           ex[a] = s.exa[slot][a][row_local];
           raw[a] = ex[a] != kZeroGroup && static_cast<uint32_t>(ex[a] - ex_lo) > span;
         }
-        if (!mbar_wait(&s.dfull[buf], (gi / kTmemBufs) & 1)) {
+        if (!mbar_wait(&s.dfull[buf], dphase)) {
           ok = false;
           break;
         }
@@ -1236,6 +1294,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
         if (lane == 0) {
           mbar_arrive(&s.dempty[buf]);
           mbar_arrive(&s.exempty[slot]);
+        }
+        if (++buf == kTmemBufs) {
+          buf = 0;
+          dphase ^= 1;
+        }
+        if (++slot == kExSlots) {
+          slot = 0;
+          xphase ^= 1;
         }
       }
       if (!ok)

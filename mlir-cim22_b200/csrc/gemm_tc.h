@@ -16,6 +16,11 @@ namespace cim::tc {
 // shifted weight scale is Q(p) * 2^(Ex + Ew - 266) as before.
 constexpr int kScaleShift = 60;
 
+// Words of one per-(K tile, 32-lane block) weight record of the sign-split
+// contraction: the Wp and Wn epilogue scales of the block's 32 lanes, then
+// its exponent range {min, max, ex_lo, ex_hi}.
+constexpr int kScaleBlockWords = 32 + 32 + 4;
+
 // True when the tcgen05 kernels are compiled in and the current device is an
 // sm_100 part.
 bool signsplit_available();
@@ -28,7 +33,9 @@ bool int8_available();
 // [T][n_pad / 32][4] = {min, max, ex_lo, ex_hi} over both signs of each tile
 // and 32-lane block (ex_lo..ex_hi: the activation exponents the epilogue
 // restores on its fast path), by the f32 weight scales 2^(Ew - 133) [2][T][n_pad] and by
-// the epilogue's f32 scales 2^(Ew - 133 + kScaleShift) [2][T][n_pad]. Returns false when the shape is not handled by the tensor-core
+// the epilogue's f32 scales 2^(Ew - 133 + kScaleShift) [2][T][n_pad] and by
+// the same scales and ranges as records [T][n_pad / 32][kScaleBlockWords].
+// Returns false when the shape is not handled by the tensor-core
 // kernel, in which case nothing was launched. out_pixels = 0 writes y as
 // rows [M][N]; out_pixels > 0 writes NCHW images [M / out_pixels][N][out_pixels].
 // A non-null post_scale applies fma(out, post_scale[n], post_shift[n]) after

@@ -1886,7 +1886,9 @@ static void prepare_bf16_weights(const float *w, int64_t n, int64_t k,
                                  std::vector<uint16_t> &operands, int32_t &ex_lo,
                                  int32_t &ex_hi) {
   mant.assign(2 * n_pad * k_pad, 0);
-  exps.assign(2 * T * n_pad + (n_pad / 32) * T * 4 + 4 * T * n_pad, 127);
+  exps.assign(2 * T * n_pad + (n_pad / 32) * T * 4 + 4 * T * n_pad +
+                  T * (n_pad / 32) * tc::kScaleBlockWords,
+              127);
   uint16_t group[kTileK];
   for (int b = 0; b < 2; ++b)
     for (int64_t lane = 0; lane < n; ++lane)
@@ -1953,6 +1955,17 @@ static void prepare_bf16_weights(const float *w, int64_t n, int64_t k,
     const float g = std::ldexp(1.0f, std::min(exps[i] - 133 + tc::kScaleShift, 127));
     std::memcpy(&tc_scales[i], &g, 4);
   }
+  // The same epilogue scales and windows per (K tile, 32-lane block) in one
+  // record {Wp scales [32], Wn scales [32], range [4]}, so that the
+  // tensor-core kernel fetches a tile's weight data with one bulk copy.
+  int32_t *blocks = tc_scales + 2 * T * n_pad;
+  for (int64_t t = 0; t < T; ++t)
+    for (int64_t nb = 0; nb < n_pad / 32; ++nb) {
+      int32_t *rec = blocks + (t * (n_pad / 32) + nb) * tc::kScaleBlockWords;
+      for (int b = 0; b < 2; ++b)
+        std::memcpy(rec + 32 * b, tc_scales + (b * T + t) * n_pad + nb * 32, 32 * 4);
+      std::memcpy(rec + 64, ranges + (t * (n_pad / 32) + nb) * 4, 4 * 4);
+    }
   // Scaled BF16 operands b * 2^(Ew - 133) (exact: b has at most 7 significant
   // bits and the value is normal for Ew >= kOperandEwMin), for layers of at
   // least kOperandMinLanes lanes whose lanes with a nonzero mantissa all have
