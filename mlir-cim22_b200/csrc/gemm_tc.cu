@@ -1595,6 +1595,21 @@ bool encode_nchw_box(CUtensorMap *map, const float *x, uint64_t W, uint64_t H, u
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encode_prepared_store(CUtensorMap *map, void *base, uint64_t rows, uint64_t k_pad,
+                           bool b16) {
+  auto fn = encode_fn();
+  if (!fn)
+    return false;
+  const cuuint64_t dims[2] = {k_pad, rows};
+  const cuuint64_t strides[1] = {k_pad * (b16 ? 2 : 1)};
+  const cuuint32_t box[2] = {64, 32};
+  const cuuint32_t elem[2] = {1, 1};
+  return fn(map, b16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base,
+            dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            b16 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 namespace {
 
 bool sm100(cudaStream_t) {

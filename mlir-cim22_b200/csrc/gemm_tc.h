@@ -83,4 +83,11 @@ bool launch_int8(const int8_t *A, int64_t a_rows, int64_t a_cols, const int8_t *
 bool encode_nchw_box(CUtensorMap *map, const float *x, uint64_t W, uint64_t H, uint64_t C,
                      uint64_t N, uint32_t wb, uint32_t hb, uint32_t cb, uint32_t nb);
 
+// Tensor map of prepared activation columns [rows][k_pad] (int8, or BF16
+// with b16) for TMA stores of 32-row x 64-element boxes from a swizzled
+// shared-memory tile: 64-byte swizzle for int8 rows, 128-byte for BF16 rows.
+// False when the driver rejects it.
+bool encode_prepared_store(CUtensorMap *map, void *base, uint64_t rows, uint64_t k_pad,
+                           bool b16);
+
 } // namespace cim::tc

@@ -265,12 +265,26 @@ __device__ __forceinline__ uint32_t branch_pair(uint32_t pair, int a) {
 // group of each branch - 64 aligned int8 mantissas (four 16-byte stores), or
 // with kB16 the 64 scaled BF16 operand values (eight 16-byte stores; scaled
 // for groups whose exponent lies in [win_lo, win_hi], unscaled otherwise).
-template <int kActBranches, bool kB16 = false>
+// kStaged: the warp's 32 columns (consecutive, all in the call) are written
+// into the warp's shared-memory tile `stage` (per branch 32 rows of 64 or
+// 128 bytes, 16-byte chunks swizzled as `omap` describes) and leave with one
+// TMA store per branch, so that whole lines reach global memory.
+template <int kActBranches, bool kB16 = false, bool kStaged = false>
 __device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
                                              uint32_t raw_max, int32_t *status,
                                              int8_t *__restrict__ A, int32_t *__restrict__ ex,
                                              int m_pad, int k_pad, int T, int t, int m,
-                                             int kbeg, int win_lo = 1, int win_hi = 0) {
+                                             int kbeg, int win_lo = 1, int win_hi = 0,
+                                             uint8_t *stage = nullptr,
+                                             const CUtensorMap *omap = nullptr) {
+  constexpr int kRowBytes = kB16 ? 128 : 64;
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  if constexpr (kStaged) {
+    // The tile's previous stores must have read it before it is rewritten.
+    if (lane == 0)
+      bulk_wait_read();
+    __syncwarp();
+  }
   uint32_t mx[2] = {0, 0};
   // A 2-branch layer whose BF16 inputs carry no sign bit (the usual case:
   // the layer reads a ReLU output) has the raw maximum as its maximum; a -0
@@ -362,13 +376,34 @@ __device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
         }
       }
     }
-    constexpr int kElemBytes = kB16 ? 2 : 1;
-    uint4 *dst = reinterpret_cast<uint4 *>(
-        A + ((static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) * kElemBytes);
+    if constexpr (kStaged) {
+      // Row `lane` of the branch's tile; chunk q at q ^ (the swizzle's row
+      // bits): lane & 7 for 128-byte rows, (lane >> 1) & 3 for 64-byte rows.
+      uint8_t *row = stage + (a * 32 + lane) * kRowBytes;
+      const int swz = kB16 ? (lane & 7) : ((lane >> 1) & 3);
 #pragma unroll
-    for (int q = 0; q < kWords / 4; ++q)
-      dst[q] = make_uint4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+      for (int q = 0; q < kWords / 4; ++q)
+        *reinterpret_cast<uint4 *>(row + ((q ^ swz) << 4)) =
+            make_uint4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+    } else {
+      constexpr int kElemBytes = kB16 ? 2 : 1;
+      uint4 *dst = reinterpret_cast<uint4 *>(
+          A + ((static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) * kElemBytes);
+#pragma unroll
+      for (int q = 0; q < kWords / 4; ++q)
+        dst[q] = make_uint4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+    }
     ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax;
+  }
+  if constexpr (kStaged) {
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+#pragma unroll
+      for (int a = 0; a < kActBranches; ++a)
+        tma_store_2d(omap, stage + a * 32 * kRowBytes, kbeg, a * m_pad + (m - lane));
+      bulk_commit();
+    }
   }
 }
 
@@ -513,14 +548,19 @@ constexpr int kBoxWarps = 8; // 256 threads
 
 template <int kActBranches, bool kB16>
 __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
-    prepare_nchw_box_kernel(const __grid_constant__ CUtensorMap map, Gather32 g, BoxGather b,
+    prepare_nchw_box_kernel(const __grid_constant__ CUtensorMap map,
+                            const __grid_constant__ CUtensorMap omap, Gather32 g, BoxGather b,
                             FastDiv div_T, int T, int items, int run, int m_pad, int k_pad,
                             int8_t *__restrict__ A, int32_t *__restrict__ ex, int32_t *status,
                             int win_lo, int win_hi) {
-  extern __shared__ __align__(128) unsigned char box_raw[];
-  // The ring's first stage, rounded up to 128 bytes (the launch adds them),
-  // then the offset table.
-  float *ring = reinterpret_cast<float *>(box_raw + ((128u - (shared_addr(box_raw) & 127u)) & 127u));
+  extern __shared__ __align__(1024) unsigned char box_raw[];
+  // Each warp's output tiles first (1024-byte aligned for the swizzle; the
+  // launch adds the alignment slack), then the window ring, then the offset
+  // table.
+  constexpr int kOutTile = kActBranches * 32 * (kB16 ? 128 : 64);
+  uint8_t *out_tiles = box_raw + ((1024u - (shared_addr(box_raw) & 1023u)) & 1023u);
+  uint8_t *my_tile = out_tiles + (threadIdx.x >> 5) * kOutTile;
+  float *ring = reinterpret_cast<float *>(out_tiles + kBoxWarps * kOutTile);
   int *rel_table = reinterpret_cast<int *>(ring + b.stages * b.stage_floats);
   __shared__ __align__(8) uint64_t full[kBoxStages], empty[kBoxStages];
   pdl_launch_dependents();
@@ -629,8 +669,9 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
         for (int q = 0; q < 32; ++q)
           signed_pairs[q] = 0; // a padding column: an all-zero group
       }
-      finish_group<kActBranches, kB16>(signed_pairs, raw_max, status, A, ex, m_pad, k_pad, T,
-                                       t, m, kbeg, win_lo, win_hi);
+      finish_group<kActBranches, kB16, true>(signed_pairs, raw_max, status, A, ex, m_pad,
+                                             k_pad, T, t, m, kbeg, win_lo, win_hi, my_tile,
+                                             &omap);
     }
     // This warp is done with the stage.
     __syncwarp();
@@ -646,6 +687,9 @@ __global__ void __launch_bounds__(256, kActBranches == 2 ? 2 : 3)
       for (int j = i; j < issued; ++j)
         barrier_wait(&full[j % b.stages], (j / b.stages) & 1, 100000000ull);
   }
+  // The warp's output stores complete before the block leaves.
+  if ((tid & 31) == 0)
+    bulk_wait();
 }
 
 // The box of the TMA-staged gather for a layer, or false when its columns do
@@ -670,10 +714,12 @@ static int device_sms() {
 // Dynamic shared memory of prepare_nchw_box_kernel: the window ring (one
 // stage rounded up to 128 bytes, plus 128 bytes for the ring's alignment) and
 // the offset table of every kernel-window phase.
-static size_t box_smem(const BoxGather &b, int khw) {
-  return (static_cast<size_t>(b.stages) * b.stage_floats + static_cast<size_t>(khw) * kTileK) *
+static size_t box_smem(const BoxGather &b, int khw, int act_branches, bool b16) {
+  const size_t out_tiles = static_cast<size_t>(kBoxWarps) * act_branches * 32 * (b16 ? 128 : 64);
+  return out_tiles +
+         (static_cast<size_t>(b.stages) * b.stage_floats + static_cast<size_t>(khw) * kTileK) *
              sizeof(float) +
-         128;
+         1024;
 }
 
 static bool plan_box_gather(const Gather32 &g, const float *x, int T, BoxGather &b) {
@@ -713,7 +759,8 @@ static bool plan_box_gather(const Gather32 &g, const float *x, int T, BoxGather 
   // faster on ResNet-18's convolutions than two, also where the third stage
   // costs a resident block (a stride-2 convolution's larger window).
   b.stages = kBoxStages;
-  return items < (int64_t{1} << 31) && box_smem(b, khw) <= 200 * 1024;
+  // The largest output tiles (4-branch, BF16 operands) must fit beside them.
+  return items < (int64_t{1} << 31) && box_smem(b, khw, 2, true) <= 200 * 1024;
 }
 
 // ---------------------------------------------------------------------------
@@ -2295,12 +2342,14 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
   // images gather from a TMA-staged window in shared memory.
   BoxGather box{};
   if (tc::signsplit_available() && plan_box_gather(dg, x, T, box)) {
-    CUtensorMap map;
+    CUtensorMap map, omap;
     const int n_images = static_cast<int>(g.batch);
     if (tc::encode_nchw_box(&map, x, dg.W, dg.H, dg.C, n_images, box.wb, box.hb, box.cb,
-                            box.nb)) {
+                            box.nb) &&
+        tc::encode_prepared_store(&omap, A, static_cast<uint64_t>(ab) * m_pad, layer->k_pad,
+                                  b16)) {
       const int items = static_cast<int>((m_pad + 255) / 256 * T);
-      const size_t smem = box_smem(box, dg.KH * dg.KW);
+      const size_t smem = box_smem(box, dg.KH * dg.KW, ab, b16);
       // Runs of items per block: up to eight, keeping at least four waves.
       auto launch = [&](auto kernel) {
         int per_sm = 0;
@@ -2314,7 +2363,7 @@ int cim22_cuda_layer_prepare_bf16(const cim22_cuda_layer *layer,
         const int64_t resident = int64_t{device_sms()} * per_sm;
         const int run = static_cast<int>(std::clamp<int64_t>(items / (4 * resident), 1, 8));
         const int grid = (items + run - 1) / run;
-        launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), 256, smem, s, map, dg, box,
+        launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), 256, smem, s, map, omap, dg, box,
                    make_fastdiv(static_cast<uint32_t>(T)), T, items, run, static_cast<int>(m_pad),
                    static_cast<int>(layer->k_pad), A, ex, status, win_lo, win_hi);
         return true;

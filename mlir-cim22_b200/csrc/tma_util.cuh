@@ -73,5 +73,36 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
+// A 2-D tiled bulk-tensor store from this CTA's shared memory (the layout
+// the map's swizzle describes) to global memory, in the thread's bulk async
+// group. The innermost coordinate x must be 16-byte aligned in bytes.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x,
+                                             int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::
+                   "l"(reinterpret_cast<uint64_t>(map)),
+               "r"(shared_addr(src)), "r"(x), "r"(y)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until the thread's committed bulk stores have read their shared
+// memory (the source may then be rewritten).
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Wait until the thread's committed bulk stores have completed.
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Make this thread's shared-memory writes visible to the async proxy (TMA).
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 } // namespace
 } // namespace cim
