@@ -385,7 +385,7 @@ cim22_cuda_layer *cim22_cuda_layer_create_int8(int device, const int8_t *weight,
                                                size_t error_capacity);
 void cim22_cuda_layer_destroy(cim22_cuda_layer *layer);
 int cim22_cuda_layer_range_safe(const cim22_cuda_layer *layer);
-/* 1 when a BF16 sign-split layer takes BF16 operands: at least 256 output
+/* 1 when a BF16 sign-split layer takes BF16 operands: at least 64 output
  * lanes, and every lane with a nonzero mantissa has a weight exponent in
  * [8, 241]. On sm_100 its prepare then stores scaled BF16 operand values
  * (twice the workspace bytes of int8 mantissas) and its contraction runs the

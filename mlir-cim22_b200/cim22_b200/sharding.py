@@ -206,7 +206,7 @@ class ColumnShardedStack:
         if fused:
             if not all(layer.bf16_operands for layer in self.layers):
                 raise ValueError("the fused column shard needs every rank's lane block to take "
-                                 "BF16 operands (at least 256 lanes with admitted weights)")
+                                 "BF16 operands (at least 64 lanes with admitted weights)")
             for plan in self.plans:
                 buf = PeerBuffer((rows, plan.lanes), torch.float32, self.device, group)
                 self.peer_out.append(buf)

@@ -124,12 +124,11 @@ struct cim22_cuda_layer {
 
 namespace cim {
 // Layers of at least this many output lanes take BF16 operands. Measured on
-// B200: the contraction with BF16 operands is faster wherever it runs, but its
-// prepare writes two bytes per element instead of one, which outweighs the
-// gain for narrow layers over many columns (ResNet-18's 64- and 128-channel
-// convolutions) and pays off from 256 lanes on (its 256- and 512-channel
-// convolutions, the 4096-wide Linear stack).
-constexpr int64_t kOperandMinLanes = 256;
+// B200: the contraction with BF16 operands is faster wherever it runs, and
+// with the TMA-stored prepare its two bytes per element cost less than that
+// gain from 64 lanes on (every ResNet-18 and event-CNN convolution after the
+// first, the Linear stacks); narrower layers stay on int8 mantissas.
+constexpr int64_t kOperandMinLanes = 64;
 // The weight exponents that BF16 operands admit: every nonzero scaled weight
 // b * 2^(Ew - 133) (1 <= b <= 127) is a normal BF16 value, and a dot p < 2^20
 // of unscaled activation mantissas times them stays a finite normal f32.

@@ -1,7 +1,7 @@
 // layers_noalloc.cu - BF16 sign-split CIM layer without caller scratch.
 //
 // cim22_cuda_layer_forward_bf16 needs a workspace for the prepared activation
-// columns (int8 mantissas, or BF16 operand values for layers of 256 lanes and
+// columns (int8 mantissas, or BF16 operand values for layers of 64 lanes and
 // more, and per-group exponents). Some callers cannot
 // provide one: generated model code that, like the reference's compiled Host
 // code, only owns stack buffers and has no device allocator of its own, and

@@ -140,7 +140,8 @@ def test_conv_bf16_bit_exact(layout, c, h, f, kk, stride, pad):
     ("nhwc", 64, 32, 16, 32, 3, 1, 1, 4, 2),   # fused 2x2 max pool over 32x32
     # 256 lanes: BF16 operand values from every prepare kernel (TMA-staged
     # whole rows and whole images, thread per group over a fused pool, eight
-    # threads per group) into the contraction with BF16 operands
+    # threads per group) into the contraction with BF16 operands, several
+    # lane blocks per output row
     ("nchw", 16, 64, 16, 256, 3, 1, 1, 2, 0),
     ("nchw", 8, 32, 16, 256, 3, 2, 1, 4, 0),
     ("nchw", 16, 32, 8, 256, 3, 1, 1, 2, 2),
@@ -166,7 +167,7 @@ def test_conv_bf16_large_batch_bit_exact(layout, n, c, h, f, kk, stride, pad, br
     b = rng.standard_normal(f).astype(np.float32)
     expected = oracle.conv2d_bf16(pooled, w, b, stride, pad, branches=4, threads=8)
     layer = CimLayer(w.reshape(f, -1))
-    assert layer.bf16_operands == (f >= 256)
+    assert layer.bf16_operands == (f >= 64)
     kind = abi.GATHER_CONV_NCHW if layout == "nchw" else abi.GATHER_CONV_NHWC
     g = conv_gather(kind, n, c, h, h, kk, kk, stride, pad)
     if pool:
@@ -341,14 +342,15 @@ def test_linear_int8_tensor_core_shapes(m, k, n):
     (5000, 300, 160, 4, 1.0),
     # per-row scales from 1e-38 to 1e30: fast and exact-path rows share a
     # CTA, and whole rows of zero groups
-    (3000, 256, 96, 4, "rows"), (2048, 130, 64, 2, "rows"),
-    # 256 lanes and more: BF16 operands, with unscaled groups (rows outside
-    # the layer's exponent window) restored exactly
+    (3000, 256, 96, 4, "rows"), (2048, 130, 64, 2, "rows"), (3000, 256, 48, 4, "rows"),
+    (2048, 130, 40, 2, "rows"),
+    # BF16 operands over many output tiles, with unscaled groups (rows
+    # outside the layer's exponent window) restored exactly
     (3000, 256, 300, 4, "rows"), (2048, 130, 256, 2, "rows"), (700, 640, 260, 4, 1.0),
     (512, 4096, 512, 2, 1.0), (600, 200, 320, 4, 1e-30), (512, 64, 256, 4, 1e18)])
 def test_linear_bf16_tensor_core_bit_exact(m, k, n, branches, scale):
     """Wide layers run a tcgen05 sign-split kernel (launch counter checked):
-    int8 mantissas below 256 lanes, BF16 operands from 256 lanes on. The
+    int8 mantissas below 64 lanes, BF16 operands from 64 lanes on. The
     prepare + contract form always takes it; one-tile layers of at most 64
     lanes, which forward_bf16 runs as one thread-per-column kernel, are
     checked through both."""
@@ -371,7 +373,7 @@ def test_linear_bf16_tensor_core_bit_exact(m, k, n, branches, scale):
     b = rng.standard_normal(n).astype(np.float32)
     expected = oracle.linear_bf16(x, w, b, branches=4, threads=8)
     layer = CimLayer(w)
-    assert layer.bf16_operands == (n >= 256)
+    assert layer.bf16_operands == (n >= 64)
     xt, bt = torch.from_numpy(x).to(DEV), torch.from_numpy(b).to(DEV)
     ws, status = Workspace(torch.device(DEV)), StatusWord(torch.device(DEV))
     out = torch.empty(m, n, device=DEV)
