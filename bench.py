@@ -400,18 +400,20 @@ def roofline(prog, workload: str, batch: int, avg: dict) -> dict:
         ab = 1 if info.branches == 2 else 2
         t_tiles = -(-info.k // 64)
         m_pad = -(-info.m // 128) * 128
+        eb = info.operand_bytes
+        kind = "BF16 operand" if eb == 2 else "int8"
         if step.meta.get("x") is not None and dominant.split("#")[0] + ".prepare" in names:
-            # The contraction of a two-kernel layer reads the prepared int8
-            # columns and their group exponents, not the source image.
-            src = ab * m_pad * t_tiles * (64 + 4)
+            # The contraction of a two-kernel layer reads the prepared columns
+            # and their group exponents, not the source image.
+            src = ab * m_pad * t_tiles * (64 * eb + 4)
             what = ("CIM contraction: ops = 2 x branches x M x K x N (unpadded); bytes = "
-                    "prepared int8 columns + group exponents + int8 weights of both signs + "
-                    "f32 output (+ f32 residual addend)")
+                    f"prepared {kind} columns + group exponents + {kind} weights of both signs "
+                    "+ f32 output (+ f32 residual addend)")
         else:
             src = info.in_bytes
             what = ("CIM layer: ops = 2 x branches x M x K x N (unpadded); bytes = source read "
-                    "once + int8 weights of both signs + f32 output (+ f32 residual addend)")
-        nbytes = src + 2 * info.n * info.k + 4 * info.m * info.n
+                    f"once + {kind} weights of both signs + f32 output (+ f32 residual addend)")
+        nbytes = src + 2 * eb * info.n * info.k + 4 * info.m * info.n
         if step.meta.get("residual") is not None:
             nbytes += 4 * info.m * info.n
         tensor, hbm = ops, nbytes
@@ -419,8 +421,9 @@ def roofline(prog, workload: str, batch: int, avg: dict) -> dict:
         ab = 1 if info.branches == 2 else 2
         t_tiles = -(-info.k // 64)
         m_pad = -(-info.m // 128) * 128
-        hbm = info.in_bytes + ab * m_pad * t_tiles * (64 + 4)
-        what = ("prepare: bytes = source read once + prepared int8 columns and group "
+        hbm = info.in_bytes + ab * m_pad * t_tiles * (64 * info.operand_bytes + 4)
+        what = ("prepare: bytes = source read once + prepared "
+                f"{'BF16 operand' if info.operand_bytes == 2 else 'int8'} columns and group "
                 "exponents written")
     else:
         what = "glue kernel (bytes not modelled)"

@@ -83,6 +83,7 @@ class LayerInfo:
     branches: int
     macs: int
     in_bytes: int = 0  # bytes of the source tensor the prepare kernel gathers from
+    operand_bytes: int = 1  # bytes per prepared element: 2 with BF16 operands, else 1
 
 
 _CONV = {torch.conv2d, F.conv2d}
@@ -762,7 +763,8 @@ class Program:
             pad=pad[0], out=out, act=act, branches=branches)))
         self.layers.append(LayerInfo(name, "conv", m, c * kh * kw, f, branches,
                                      branches * m * c * kh * kw * f,
-                                     xt.numel() * xt.element_size()))
+                                     xt.numel() * xt.element_size(),
+                                     2 if layer.bf16_operands else 1))
         env[out_node] = Val(IMAGE, (n, f, g.out_h, g.out_w), out, self.layout,
                             nonneg=act == "relu")
 
@@ -818,7 +820,8 @@ class Program:
             bias=None if b is None else torch.as_tensor(b).detach().float(), out=out, act=act,
             branches=branches)))
         self.layers.append(LayerInfo(name, "linear", m, k, n, branches, branches * m * k * n,
-                                     xt.numel() * xt.element_size()))
+                                     xt.numel() * xt.element_size(),
+                                     2 if layer.bf16_operands else 1))
         if len(lead) == 1:
             env[out_node] = Val(MATRIX, (m, n), out, nonneg=act == "relu")
         else:

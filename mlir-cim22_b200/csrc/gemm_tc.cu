@@ -494,7 +494,9 @@ __device__ __forceinline__ void tile_values(float (&acc)[kAB][2][LT], int row, i
                                             const float *__restrict__ post_scale,
                                             const float *__restrict__ post_shift,
                                             const float *__restrict__ residual, int act, int vec,
-                                            int out_pixels, FastDiv div_pix, float (&o)[LT]) {
+                                            int out_pixels, FastDiv div_pix, float (&o)[LT],
+                                            const float *res_tile = nullptr,
+                                            int res_stride = 0) {
   if (T > 1) {
 #pragma unroll
     for (int a = 0; a < kAB; ++a)
@@ -558,7 +560,14 @@ __device__ __forceinline__ void tile_values(float (&acc)[kAB][2][LT], int row, i
           o[j] = __fmaf_rn(o[j], __ldg(post_scale + lane0 + j), __ldg(post_shift + lane0 + j));
     }
   }
-  if (residual != nullptr) {
+  if (res_tile != nullptr) {
+    // The residual addends of the row's lanes, staged in shared memory by
+    // TMA while the output tile was computed: one f32 add as the glue.
+#pragma unroll
+    for (int j = 0; j < LT; ++j)
+      if (lane0 + j < N)
+        o[j] = __fadd_rn(o[j], res_tile[j * res_stride]);
+  } else if (residual != nullptr) {
     // A residual add fused after the batch norm (prefetched into L2 when the
     // output tile started): one f32 add as the glue computes it.
     int64_t stride;
@@ -587,12 +596,14 @@ __device__ __forceinline__ void store_tile(float (&acc)[kAB][2][LT], int row, in
                                            const float *__restrict__ post_shift,
                                            const float *__restrict__ residual, int act,
                                            int vec, int out_pixels, FastDiv div_pix,
-                                           float *__restrict__ y) {
+                                           float *__restrict__ y,
+                                           const float *res_tile = nullptr,
+                                           int res_stride = 0) {
   if (row >= M)
     return;
   float o[LT];
   tile_values<kAB, LT>(acc, row, lane0, N, T, cache, bias, post_scale, post_shift, residual, act,
-                       vec, out_pixels, div_pix, o);
+                       vec, out_pixels, div_pix, o, res_tile, res_stride);
   const bool full = lane0 + LT <= N;
   if (out_pixels > 0) {
     const int image = fdiv(row, div_pix);
@@ -993,27 +1004,46 @@ __global__ void __launch_bounds__(kSThreads, 1)
 // Same warp roles, TMEM buffers and output stores as signsplit_tc_kernel; the
 // ring holds one crossbar tile per stage (128 bytes of K per row) and the MMA
 // warp issues four K=16 MMAs per activation branch and tile.
-template <int kAB> struct SBShape {
-  static constexpr int kStages = kAB == 1 ? 6 : 4;
+// kRes: the layer has a residual addend, which one epilogue thread loads per
+// output tile into shared memory by TMA (NCHW outputs whose 128-row tiles
+// cover whole images or runs of one image); the ring gives up a stage for it
+// where shared memory is short.
+template <int kAB, bool kRes> struct SBShape {
+  static constexpr int kStages = kAB == 1 ? (kRes ? 5 : 6) : 4;
   static constexpr int kExSlots = 16;                       // activation exponent ring
   static constexpr int kATile = kSBM * 64;                  // BF16 elements per branch
   static constexpr int kBTile = SSShape<kAB>::N * 64;       // BF16 elements
+  static constexpr int kResTile = kRes ? kSBM * SSShape<kAB>::L : 4; // f32 addends
 };
 
-template <int kAB> struct alignas(1024) SmemSB {
-  uint16_t a[SBShape<kAB>::kStages][kAB][SBShape<kAB>::kATile];
-  uint16_t b[SBShape<kAB>::kStages][SBShape<kAB>::kBTile];
-  int32_t exa[SBShape<kAB>::kExSlots][kAB][kSBM];
-  uint64_t full[SBShape<kAB>::kStages];
-  uint64_t empty[SBShape<kAB>::kStages];
-  uint64_t exfull[SBShape<kAB>::kExSlots];
-  uint64_t exempty[SBShape<kAB>::kExSlots];
+template <int kAB, bool kRes> struct alignas(1024) SmemSB {
+  using Shape = SBShape<kAB, kRes>;
+  uint16_t a[Shape::kStages][kAB][Shape::kATile];
+  uint16_t b[Shape::kStages][Shape::kBTile];
+  int32_t exa[Shape::kExSlots][kAB][kSBM];
+  alignas(128) float res[Shape::kResTile]; // [images][lanes][pixels] of the tile
+  uint64_t full[Shape::kStages];
+  uint64_t empty[Shape::kStages];
+  uint64_t exfull[Shape::kExSlots];
+  uint64_t exempty[Shape::kExSlots];
   uint64_t dfull[kTmemBufs];
   uint64_t dempty[kTmemBufs];
+  uint64_t rfull, rempty;
   uint32_t tmem;
   int failed;
   alignas(16) float lane_params[3][kParamLanes];
 };
+
+// A 3-D tiled bulk-tensor load into this CTA's shared memory (no cluster
+// forms); x must be 16-byte aligned in bytes.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                            int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 
 // Instruction descriptor of tcgen05.mma .kind::f16 with BF16 A and B and an
 // f32 accumulator: D format (bits [4,6)) 1 = F32, A and B formats (bits
@@ -1074,13 +1104,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
                          const float *__restrict__ residual_arg, int act, int vec,
                          int out_pixels, FastDiv div_pix, float *__restrict__ y,
                          int32_t *status, const __grid_constant__ cim22_peer_outputs peers,
-                         int peer_vec4) {
+                         int peer_vec4, const __grid_constant__ CUtensorMap tmR, int res_bp) {
   const float *residual = kRes ? residual_arg : nullptr;
   using S = SSShape<kAB>;
   constexpr int L = S::L, LT = S::LT, SN = S::N;
-  constexpr int kStages = SBShape<kAB>::kStages, kExSlots = SBShape<kAB>::kExSlots;
+  using Shape = SBShape<kAB, kRes>;
+  constexpr int kStages = Shape::kStages, kExSlots = Shape::kExSlots;
   extern __shared__ uint8_t smem_raw[];
-  SmemSB<kAB> &s = smem_aligned<SmemSB<kAB>>(smem_raw);
+  SmemSB<kAB, kRes> &s = smem_aligned<SmemSB<kAB, kRes>>(smem_raw);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int num_nb = (N + L - 1) / L;
   const int num_tiles = ((M + kSBM - 1) / kSBM) * num_nb;
@@ -1098,6 +1129,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
       mbar_init(&s.dfull[i], 1);
       mbar_init(&s.dempty[i], kEpiWarps);
     }
+    mbar_init(&s.rfull, 1);
+    mbar_init(&s.rempty, kEpiWarps);
     s.failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1142,7 +1175,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
           ok = false;
           break;
         }
-        mbar_expect_tx(&s.full[stage], (kAB * SBShape<kAB>::kATile + SBShape<kAB>::kBTile) * 2);
+        mbar_expect_tx(&s.full[stage], (kAB * Shape::kATile + Shape::kBTile) * 2);
 #pragma unroll
         for (int a = 0; a < kAB; ++a)
           tma_load_2d(s.a[stage][a], &tmA, &s.full[stage], t * 64, a * m_pad + m0);
@@ -1221,13 +1254,35 @@ __global__ void __launch_bounds__(kSThreads, 1)
     const uint32_t tlane = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t span = static_cast<uint32_t>(ex_hi - ex_lo);
     uint32_t gi = 0, buf = 0, dphase = 0, slot = 0, xphase = 0;
+    // Residual tiles by TMA: output tiles this CTA has started (the loads
+    // warp 2's lane 0 issued) and finished (whose addends every warp read).
+    const bool res_tma = kRes && res_bp > 0;
+    const bool res_issuer = res_tma && warp == 2 && lane == 0;
+    uint32_t res_started = 0, res_done = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
       const int mb = fdiv(ot, div_nb);
       const int m0 = mb * kSBM, n0 = (ot - mb * num_nb) * L;
       const int lane0 = n0 + sub * LT;
       const int row = m0 + row_local; // < m_pad
-      prefetch_residual<LT>(residual, row, lane0, M, N, out_pixels, div_pix);
+      if (res_tma) {
+        if (res_issuer) {
+          // The previous tile's addends have been read by every warp; this
+          // tile's arrive while its crossbar tiles are computed. The box is
+          // res_bp pixels x L lanes x (128 / res_bp) images from pixel
+          // m0 mod HW of image m0 / HW.
+          if (res_started > 0 && !mbar_wait(&s.rempty, (res_started - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          const int img0 = fdiv(m0, div_pix);
+          mbar_expect_tx(&s.rfull, Shape::kResTile * 4);
+          tma_load_3d(s.res, &tmR, &s.rfull, m0 - img0 * out_pixels, n0, img0);
+        }
+        ++res_started;
+      } else {
+        prefetch_residual<LT>(residual, row, lane0, M, N, out_pixels, div_pix);
+      }
       float acc[kAB][2][LT];
 #pragma unroll
       for (int a = 0; a < kAB; ++a)
@@ -1306,13 +1361,33 @@ __global__ void __launch_bounds__(kSThreads, 1)
       }
       if (!ok)
         break;
-      if constexpr (kPeer)
+      if constexpr (kPeer) {
         store_tile_peers<kAB, LT>(acc, row, lane0, M, N, T, cached ? s.lane_params : nullptr,
                                   bias, post_scale, post_shift, act, vec, peers, peer_vec4 != 0);
-      else
+      } else if (res_tma) {
+        if (!mbar_wait(&s.rfull, res_done & 1)) {
+          ok = false;
+          break;
+        }
+        // Row r of the tile is pixel r mod res_bp of the tile's image
+        // r / res_bp; lane j of the thread sits res_bp floats further on.
+        const float *res_row =
+            s.res + ((row_local / res_bp) * L + sub * LT) * res_bp + row_local % res_bp;
+        store_tile<kAB, LT>(acc, row, lane0, M, N, T, cached ? s.lane_params : nullptr, bias,
+                            post_scale, post_shift, residual, act, vec, out_pixels, div_pix, y,
+                            res_row, res_bp);
+        __syncwarp();
+        if (lane == 0)
+          mbar_arrive(&s.rempty);
+        ++res_done;
+      } else {
         store_tile<kAB, LT>(acc, row, lane0, M, N, T, cached ? s.lane_params : nullptr, bias,
                             post_scale, post_shift, residual, act, vec, out_pixels, div_pix, y);
+      }
     }
+    // Never leave with the residual copy in flight (bounded).
+    if (res_issuer && res_started > res_done)
+      mbar_wait(&s.rfull, (res_started - 1) & 1);
     if (!ok) {
       *failed = 1;
       if (lane == 0)
@@ -1696,8 +1771,11 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
   return true;
 }
 
-template <int kAB> constexpr size_t smem_sb() { return sizeof(SmemSB<kAB>) + 1024; }
-static_assert(smem_sb<1>() <= 232448 && smem_sb<2>() <= 232448,
+template <int kAB, bool kRes> constexpr size_t smem_sb() {
+  return sizeof(SmemSB<kAB, kRes>) + 1024;
+}
+static_assert(smem_sb<1, false>() <= 232448 && smem_sb<2, false>() <= 232448 &&
+                  smem_sb<1, true>() <= 232448 && smem_sb<2, true>() <= 232448,
               "the BF16 operand ring must fit the 227 KB of dynamic shared memory per CTA");
 
 bool launch_signsplit_b16(const uint16_t *A, const int32_t *exA, int64_t m_pad,
@@ -1735,6 +1813,28 @@ bool launch_signsplit_b16(const uint16_t *A, const int32_t *exA, int64_t m_pad,
     return false;
   const int vec = (N % 4 == 0 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0 ? 1 : 0) |
                   (N % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 ? 2 : 0);
+  // NCHW residual addends whose 128-row tiles cover whole images or runs of
+  // one image come as one TMA box per output tile: res_bp pixels x L lanes x
+  // 128 / res_bp images (lanes and images past the tensor read as +0).
+  CUtensorMap tr{};
+  int res_bp = 0;
+  if (residual != nullptr && out_pixels > 0 && out_pixels % 4 == 0 && M % out_pixels == 0 &&
+      (out_pixels % kSBM == 0 || kSBM % out_pixels == 0) &&
+      (reinterpret_cast<uintptr_t>(residual) & 15) == 0) {
+    auto fn = encode_fn();
+    const uint32_t bp = static_cast<uint32_t>(std::min<int64_t>(out_pixels, kSBM));
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(out_pixels), static_cast<cuuint64_t>(N),
+                                static_cast<cuuint64_t>(M / out_pixels)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(out_pixels) * 4,
+                                   static_cast<cuuint64_t>(N * out_pixels) * 4};
+    const cuuint32_t box[3] = {bp, static_cast<cuuint32_t>(L), kSBM / bp};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    if (fn && fn(&tr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(residual), dims,
+                 strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+      res_bp = static_cast<int>(bp);
+  }
   const int64_t tiles = ((M + kSBM - 1) / kSBM) * ((N + L - 1) / L);
   const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, sm_count())));
   auto launch = [&](auto kernel, size_t smem) {
@@ -1746,20 +1846,21 @@ bool launch_signsplit_b16(const uint16_t *A, const int32_t *exA, int64_t m_pad,
                ex_hi, make_fastdiv(static_cast<uint32_t>((N + L - 1) / L)), bias, post_scale,
                post_shift, residual, act, vec, static_cast<int>(out_pixels),
                make_fastdiv(static_cast<uint32_t>(out_pixels > 0 ? out_pixels : 1)), y, status,
-               peer ? *peers : none, peer_vec4);
+               peer ? *peers : none, peer_vec4, tr, res_bp);
     return true;
   };
   const bool res = residual != nullptr;
   bool launched;
   if (peer)
-    launched = act_branches == 2 ? launch(signsplit_b16_kernel<2, false, true>, smem_sb<2>())
-                                 : launch(signsplit_b16_kernel<1, false, true>, smem_sb<1>());
+    launched = act_branches == 2
+                   ? launch(signsplit_b16_kernel<2, false, true>, smem_sb<2, false>())
+                   : launch(signsplit_b16_kernel<1, false, true>, smem_sb<1, false>());
   else
     launched = act_branches == 2
-                   ? (res ? launch(signsplit_b16_kernel<2, true, false>, smem_sb<2>())
-                          : launch(signsplit_b16_kernel<2, false, false>, smem_sb<2>()))
-                   : (res ? launch(signsplit_b16_kernel<1, true, false>, smem_sb<1>())
-                          : launch(signsplit_b16_kernel<1, false, false>, smem_sb<1>()));
+                   ? (res ? launch(signsplit_b16_kernel<2, true, false>, smem_sb<2, true>())
+                          : launch(signsplit_b16_kernel<2, false, false>, smem_sb<2, false>()))
+                   : (res ? launch(signsplit_b16_kernel<1, true, false>, smem_sb<1, true>())
+                          : launch(signsplit_b16_kernel<1, false, false>, smem_sb<1, false>()));
   if (!launched)
     return false;
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
