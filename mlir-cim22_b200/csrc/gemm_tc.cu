@@ -1008,6 +1008,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
 // output tile into shared memory by TMA (NCHW outputs whose 128-row tiles
 // cover whole images or runs of one image); the ring gives up a stage for it
 // where shared memory is short.
+// The TMA producer and the MMA issuer are two threads each (warps 0 and 18,
+// warps 1 and 19), taking the even and the odd crossbar tiles of the CTA's
+// sequence: the per-tile instruction chain of one issuing thread (two waits,
+// four MMAs, two commits) is longer than the tensor pipe's work on a
+// 128 x 128 x 64 tile, so one thread alone bounds the layer.
+constexpr int kSBIssuers = 2;
+constexpr int kSBThreads = 32 * (2 * kSBIssuers + kEpiWarps);
+
 template <int kAB, bool kRes> struct SBShape {
   static constexpr int kStages = kAB == 1 ? (kRes ? 5 : 6) : 4;
   static constexpr int kExSlots = 16;                       // activation exponent ring
@@ -1093,7 +1101,7 @@ __device__ __forceinline__ void restore_b16_raw(float (&acc)[kLT], const uint32_
 // kPeer: a column-sharded layer whose rows go to every rank's full output
 // (store_tile_peers), made visible system-wide before the CTA ends.
 template <int kAB, bool kRes, bool kPeer>
-__global__ void __launch_bounds__(kSThreads, 1)
+__global__ void __launch_bounds__(kSBThreads, 1)
     signsplit_b16_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB,
                          const int32_t *__restrict__ exA, int m_pad,
@@ -1138,7 +1146,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
   // Resident per-lane epilogue parameters, copied before the PDL wait.
   const bool cached = N <= kParamLanes;
   if (cached)
-    for (int i = threadIdx.x; i < N; i += kSThreads) {
+    for (int i = threadIdx.x; i < N; i += kSBThreads) {
       s.lane_params[0][i] = bias ? bias[i] : 0.0f;
       s.lane_params[1][i] = post_scale ? post_scale[i] : 0.0f;
       s.lane_params[2][i] = post_shift ? post_shift[i] : 0.0f;
@@ -1155,21 +1163,33 @@ __global__ void __launch_bounds__(kSThreads, 1)
   volatile int *failed = &s.failed;
   pdl_launch_dependents();
   pdl_wait();
+  // Warps 0 and 18 produce, warps 1 and 19 issue MMAs; issuer q takes the
+  // crossbar tiles gi with gi % kSBIssuers == q of the CTA's sequence.
+  constexpr int kEpiEnd = 2 + kEpiWarps;
+  const int role_q = warp >= kEpiEnd ? (warp - kEpiEnd) / 2 + 1 : 0;
+  const bool producer = lane == 0 && (warp == 0 || (warp >= kEpiEnd && (warp - kEpiEnd) % 2 == 0));
+  const bool issuer = lane == 0 && (warp == 1 || (warp >= kEpiEnd && (warp - kEpiEnd) % 2 == 1));
+  static_assert(kStages >= kSBIssuers && kExSlots % kSBIssuers == 0 &&
+                    kTmemBufs % kSBIssuers == 0,
+                "each issuer steps every ring by kSBIssuers positions");
 
-  if (warp == 0 && lane == 0) {
+  if (producer) {
     // TMA producer: per crossbar tile the activation tile of each branch
     // and the stacked Wp / Wn tile into the stage ring, the tile's activation
     // exponents of the 128 rows into the exponent ring.
-    // Ring positions and phase parities advance incrementally: this thread
-    // is the ring's only producer, and its per-tile instruction chain (not
-    // the copies) is on the kernel's critical path. A failure elsewhere
-    // shows up as a bounded wait that runs out.
-    uint32_t it = 0, stage = 0, sphase = 0, slot = 0, xphase = 0;
+    // Ring positions and phase parities advance incrementally by the number
+    // of producers: the per-tile instruction chain of this thread (not the
+    // copies) is on the kernel's critical path. A failure elsewhere shows up
+    // as a bounded wait that runs out.
+    const uint32_t q = static_cast<uint32_t>(role_q);
+    uint32_t it = 0, stage = q, sphase = 0, slot = q, xphase = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
       const int mb = fdiv(ot, div_nb);
       const int m0 = mb * kSBM, nb = ot - mb * num_nb, n0 = nb * L;
       for (int t = 0; t < T; ++t, ++it) {
+        if (it % kSBIssuers != q)
+          continue;
         if (!mbar_wait(&s.empty[stage], sphase ^ 1) ||
             !mbar_wait(&s.exempty[slot], xphase ^ 1)) {
           ok = false;
@@ -1186,36 +1206,46 @@ __global__ void __launch_bounds__(kSThreads, 1)
         for (int a = 0; a < kAB; ++a)
           bulk_load(s.exa[slot][a], exA + (static_cast<int64_t>(a) * T + t) * m_pad + m0,
                     kSBM * 4, &s.exfull[slot]);
-        if (++stage == kStages) {
-          stage = 0;
+        if ((stage += kSBIssuers) >= kStages) {
+          stage -= kStages;
           sphase ^= 1;
         }
-        if (++slot == kExSlots) {
-          slot = 0;
+        if ((slot += kSBIssuers) >= kExSlots) {
+          slot -= kExSlots;
           xphase ^= 1;
         }
       }
     }
     if (!ok)
       *failed = 1;
-    // Never leave with copies in flight: wait (bounded) for the last use of
-    // every stage and exponent slot this thread filled (`it` counts the
-    // filled tiles; a wait that failed filled none).
+    // Never leave with copies in flight: wait (bounded) for this thread's
+    // fills among the last kStages tiles of the sequence it walked (`it`
+    // tiles; a wait that failed filled none). Older fills completed before
+    // their stage was refilled. The window is the sequence's, not this
+    // thread's own last kStages fills: with an odd stage count the other
+    // producer refills this thread's older stages, and a parity wait on a
+    // stage filled twice since would not end.
     for (uint32_t i = it > static_cast<uint32_t>(kStages) ? it - kStages : 0; i < it; ++i)
-      mbar_wait(&s.full[i % kStages], (i / kStages) & 1);
+      if (i % kSBIssuers == q)
+        mbar_wait(&s.full[i % kStages], (i / kStages) & 1);
     for (uint32_t i = it > static_cast<uint32_t>(kExSlots) ? it - kExSlots : 0; i < it; ++i)
-      mbar_wait(&s.exfull[i % kExSlots], (i / kExSlots) & 1);
-  } else if (warp == 1 && lane == 0) {
+      if (i % kSBIssuers == q)
+        mbar_wait(&s.exfull[i % kExSlots], (i / kExSlots) & 1);
+  } else if (issuer) {
     // MMA issuer: four K=16 MMAs per activation branch and crossbar tile.
     // The critical path of the kernel: ring positions advance incrementally
-    // and the descriptors step by constant strides.
+    // and the descriptors step by constant strides. Issuer q owns the TMEM
+    // buffers b with b % kSBIssuers == q.
     constexpr uint32_t idesc = idesc_bf16(kSBM, SN);
     constexpr uint64_t kAStep = sizeof(s.a[0]) >> 4, kBStep = sizeof(s.b[0]) >> 4;
     const uint64_t adesc0 = sw128_desc(s.a[0][0]), bdesc0 = sw128_desc(s.b[0]);
-    uint32_t gi = 0, stage = 0, sphase = 0, buf = 0, dphase = 0;
+    const uint32_t q = static_cast<uint32_t>(role_q);
+    uint32_t gi = 0, stage = q, sphase = 0, buf = q, dphase = 0, issued = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
       for (int t = 0; t < T; ++t, ++gi) {
+        if (gi % kSBIssuers != q)
+          continue;
         if (!mbar_wait(&s.full[stage], sphase) || !mbar_wait(&s.dempty[buf], dphase ^ 1)) {
           ok = false;
           break;
@@ -1232,22 +1262,24 @@ __global__ void __launch_bounds__(kSThreads, 1)
         }
         mma_commit(&s.dfull[buf]);
         mma_commit(&s.empty[stage]);
-        if (++stage == kStages) {
-          stage = 0;
+        issued = gi + 1;
+        if ((stage += kSBIssuers) >= kStages) {
+          stage -= kStages;
           sphase ^= 1;
         }
-        if (++buf == kTmemBufs) {
-          buf = 0;
+        if ((buf += kSBIssuers) >= kTmemBufs) {
+          buf -= kTmemBufs;
           dphase ^= 1;
         }
       }
     }
     if (!ok)
       *failed = 1;
-    // Let the last MMAs land before TMEM is freed.
-    if (gi > 0)
-      mbar_wait(&s.dfull[(gi - 1) % kTmemBufs], ((gi - 1) / kTmemBufs) & 1);
-  } else if (warp >= 2) {
+    // Let this thread's last MMAs land before TMEM is freed (its commit
+    // covers every MMA it issued).
+    if (issued > 0)
+      mbar_wait(&s.dfull[(issued - 1) % kTmemBufs], ((issued - 1) / kTmemBufs) & 1);
+  } else if (warp >= 2 && warp < kEpiEnd) {
     // Epilogue.
     const int quad = warp % 4, sub = (warp - 2) / 4;
     const int row_local = quad * 32 + lane;
@@ -1841,7 +1873,7 @@ bool launch_signsplit_b16(const uint16_t *A, const int32_t *exA, int64_t m_pad,
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
       return false;
-    launch_pdl(kernel, grid, kSThreads, smem, stream, ta, tb, exA, static_cast<int>(m_pad), exB,
+    launch_pdl(kernel, grid, kSBThreads, smem, stream, ta, tb, exA, static_cast<int>(m_pad), exB,
                static_cast<int>(n_pad), T, static_cast<int>(M), static_cast<int>(N), ex_lo,
                ex_hi, make_fastdiv(static_cast<uint32_t>((N + L - 1) / L)), bias, post_scale,
                post_shift, residual, act, vec, static_cast<int>(out_pixels),

@@ -478,6 +478,45 @@ def test_contract_residual_epilogue_bit_exact(f, branches):
     np.testing.assert_array_equal(bits(got), bits(expected))
 
 
+@pytest.mark.parametrize("f,n", [(64, 3), (128, 2)])
+def test_residual_bf16_operand_conv_many_tiles(f, n):
+    """A 64-channel 3x3 residual conv (9 crossbar tiles per output tile, BF16
+    operands, 2 branches): the residual instance's odd stage ring is split
+    between two TMA producers. Bit-exact against the oracle, and the launch
+    ends in well under the pipelines' 2 s wait limit (a producer whose exit
+    drain waited on a stage refilled by the other one ran the limit out)."""
+    from cim22_b200 import abi
+    from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace, conv_gather
+
+    rng = np.random.default_rng(f * 7 + n)
+    c, h = 64, 8
+    x = np.maximum(rng.standard_normal((n, c, h, h)), 0).astype(np.float32)
+    w = (rng.standard_normal((f, c, 3, 3)) * 0.1).astype(np.float32)
+    res = rng.standard_normal((n, f, h, h)).astype(np.float32)
+    conv = oracle.conv2d_bf16(x, w, None, 1, 1, branches=4, threads=8)
+    expected = (conv + res).astype(np.float32)
+    expected = np.where(expected > 0, expected, np.float32(0))
+    layer = CimLayer(w.reshape(f, -1))
+    g = conv_gather(abi.GATHER_CONV_NCHW, n, c, h, h, 3, 3, 1, 1)
+    m = n * h * h
+    dev = torch.device(DEV)
+    ws, status = Workspace(dev), StatusWord(dev)
+    out = torch.empty(m, f, device=DEV)
+    xt, rt = torch.from_numpy(x).to(DEV), torch.from_numpy(res).to(DEV)
+    layer.prepare_bf16(xt, m, gather=g, branches=2, workspace=ws, status=status)
+    assert layer.bf16_operands
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    layer.contract_bf16(out, m, activation="relu", branches=2, out_pixels=h * h, residual=rt,
+                        workspace=ws, status=status)
+    end.record()
+    torch.cuda.synchronize()
+    status.raise_if_set()
+    assert start.elapsed_time(end) < 500.0
+    got = out.cpu().numpy().reshape(n, f, h, h)
+    np.testing.assert_array_equal(bits(got), bits(expected))
+
+
 @pytest.mark.parametrize("act", [None, "relu"])
 def test_direct_conv_dead_negative_branch(act):
     """A 4-branch one-tile conv over binary event frames, with negative pixels
