@@ -242,6 +242,15 @@ __device__ __forceinline__ void fma2(float a0, float a1, float b0, float b1, flo
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
 }
 
+__device__ __forceinline__ void add2(float a0, float a1, float b0, float b1, float &d0,
+                                     float &d1) {
+  asm("{\n\t.reg .b64 a, b, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 __device__ __forceinline__ void mul2(float a0, float a1, float b0, float b1, float &d0,
                                      float &d1) {
   asm("{\n\t.reg .b64 a, b, d;\n\t"
