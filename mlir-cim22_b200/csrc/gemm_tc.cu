@@ -19,7 +19,6 @@
 
 #include "cim_internal.h"
 #include "cim_numeric.cuh"
-#include "signsplit_prep.cuh"
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -1009,36 +1008,22 @@ __global__ void __launch_bounds__(kSThreads, 1)
 // output tile into shared memory by TMA (NCHW outputs whose 128-row tiles
 // cover whole images or runs of one image); the ring gives up a stage for it
 // where shared memory is short.
-// The TMA producer and the MMA issuer are two threads each (warps 0 and 18,
-// warps 1 and 19), taking the even and the odd crossbar tiles of the CTA's
-// sequence: the per-tile instruction chain of one issuing thread (two waits,
-// four MMAs, two commits) is longer than the tensor pipe's work on a
-// 128 x 128 x 64 tile, so one thread alone bounds the layer.
-constexpr int kSBIssuers = 2;
-constexpr int kSBThreads = 32 * (2 * kSBIssuers + kEpiWarps);
-// kConv (launch_signsplit_b16_conv): one producer, one MMA issuer and
-// kPrepWarps warps that prepare each crossbar tile's 128 activation rows in
-// shared memory (one row per thread).
-constexpr int kPrepWarps = 4;
-constexpr int kConvThreads = 32 * (2 + kEpiWarps + kPrepWarps);
-
-template <int kAB, bool kRes, bool kConv = false> struct SBShape {
-  static constexpr int kStages = kConv ? 4 : kAB == 1 ? (kRes ? 5 : 6) : 4;
+template <int kAB, bool kRes> struct SBShape {
+  static constexpr int kStages = kAB == 1 ? (kRes ? 5 : 6) : 4;
   static constexpr int kExSlots = 16;                       // activation exponent ring
   static constexpr int kATile = kSBM * 64;                  // BF16 elements per branch
   static constexpr int kBTile = SSShape<kAB>::N * 64;       // BF16 elements
   static constexpr int kResTile = kRes ? kSBM * SSShape<kAB>::L : 4; // f32 addends
 };
 
-template <int kAB, bool kRes, bool kConv = false> struct alignas(1024) SmemSB {
-  using Shape = SBShape<kAB, kRes, kConv>;
+template <int kAB, bool kRes> struct alignas(1024) SmemSB {
+  using Shape = SBShape<kAB, kRes>;
   uint16_t a[Shape::kStages][kAB][Shape::kATile];
   uint16_t b[Shape::kStages][Shape::kBTile];
   int32_t exa[Shape::kExSlots][kAB][kSBM];
   alignas(128) float res[Shape::kResTile]; // [images][lanes][pixels] of the tile
   uint64_t full[Shape::kStages];
   uint64_t empty[Shape::kStages];
-  uint64_t wfull[Shape::kStages]; // kConv: the stage's input window has landed
   uint64_t exfull[Shape::kExSlots];
   uint64_t exempty[Shape::kExSlots];
   uint64_t dfull[kTmemBufs];
@@ -1117,14 +1102,8 @@ __device__ __forceinline__ void restore_b16_raw(float (&acc)[kLT], const uint32_
 
 // kPeer: a column-sharded layer whose rows go to every rank's full output
 // (store_tile_peers), made visible system-wide before the CTA ends.
-// kConv: a 2-branch convolution of at most 64 lanes whose activation tiles
-// the kernel prepares (launch_signsplit_b16_conv): the producer copies each
-// crossbar tile's input window (tmX, one box of ct) into a window ring behind
-// the shared-memory struct, and warps 18-21 gather, round and prealign the
-// tile's 128 rows into the stage (finish_group's operand-tile store) and its
-// exponents into the exponent ring.
-template <int kAB, bool kRes, bool kPeer, bool kConv = false>
-__global__ void __launch_bounds__(kConv ? kConvThreads : kSBThreads, 1)
+template <int kAB, bool kRes, bool kPeer>
+__global__ void __launch_bounds__(kSThreads, 1)
     signsplit_b16_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB,
                          const int32_t *__restrict__ exA, int m_pad,
@@ -1135,35 +1114,25 @@ __global__ void __launch_bounds__(kConv ? kConvThreads : kSBThreads, 1)
                          const float *__restrict__ residual_arg, int act, int vec,
                          int out_pixels, FastDiv div_pix, float *__restrict__ y,
                          int32_t *status, const __grid_constant__ cim22_peer_outputs peers,
-                         int peer_vec4, const __grid_constant__ CUtensorMap tmR, int res_bp,
-                         const __grid_constant__ CUtensorMap tmX, const ConvTile ct) {
+                         int peer_vec4, const __grid_constant__ CUtensorMap tmR, int res_bp) {
   const float *residual = kRes ? residual_arg : nullptr;
   using S = SSShape<kAB>;
   constexpr int L = S::L, LT = S::LT, SN = S::N;
-  using Shape = SBShape<kAB, kRes, kConv>;
+  using Shape = SBShape<kAB, kRes>;
   constexpr int kStages = Shape::kStages, kExSlots = Shape::kExSlots;
-  constexpr int kThreads = kConv ? kConvThreads : kSBThreads;
-  constexpr int kIssuers = kConv ? 1 : kSBIssuers;
-  static_assert(!kConv || (kAB == 1 && !kPeer), "the fused convolution is 2-branch, one rank");
   extern __shared__ uint8_t smem_raw[];
-  SmemSB<kAB, kRes, kConv> &s = smem_aligned<SmemSB<kAB, kRes, kConv>>(smem_raw);
-  // kConv: the window ring and the window offset table behind the struct.
-  float *win_ring = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(&s) +
-                                              sizeof(SmemSB<kAB, kRes, kConv>));
-  int *rel_table = reinterpret_cast<int *>(win_ring + kStages * ct.stage_floats);
+  SmemSB<kAB, kRes> &s = smem_aligned<SmemSB<kAB, kRes>>(smem_raw);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int num_nb = (N + L - 1) / L;
   const int num_tiles = ((M + kSBM - 1) / kSBM) * num_nb;
   constexpr uint32_t kTmemCols = kTmemBufs * kBufCols;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
-      // kConv: the producer's weight copy and every prepare warp's rows.
-      mbar_init(&s.full[i], kConv ? 1 + kPrepWarps : 1);
+      mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
-      mbar_init(&s.wfull[i], 1);
     }
     for (int i = 0; i < kExSlots; ++i) {
-      mbar_init(&s.exfull[i], kConv ? kPrepWarps : 1);
+      mbar_init(&s.exfull[i], 1);
       mbar_init(&s.exempty[i], kEpiWarps);
     }
     for (int i = 0; i < kTmemBufs; ++i) {
@@ -1179,23 +1148,11 @@ __global__ void __launch_bounds__(kConv ? kConvThreads : kSBThreads, 1)
   // Resident per-lane epilogue parameters, copied before the PDL wait.
   const bool cached = N <= kParamLanes;
   if (cached)
-    for (int i = threadIdx.x; i < N; i += kThreads) {
+    for (int i = threadIdx.x; i < N; i += kSThreads) {
       s.lane_params[0][i] = bias ? bias[i] : 0.0f;
       s.lane_params[1][i] = post_scale ? post_scale[i] : 0.0f;
       s.lane_params[2][i] = post_shift ? post_shift[i] : 0.0f;
     }
-  if constexpr (kConv) {
-    // Window byte offsets of the 64 K elements of a tile for every phase
-    // ph = kbeg mod (KH * KW): element e is k = c0 * KH * KW + ph + e, at
-    // relative channel c, kernel row i and column j of the window box.
-    const int khw = ct.KH * ct.KW;
-    for (int idx = threadIdx.x; idx < khw * kTileK; idx += kThreads) {
-      const int r = idx / kTileK + idx % kTileK;
-      const int c = r / khw, rk = r - c * khw;
-      const int i = rk / ct.KW, j = rk - i * ct.KW;
-      rel_table[idx] = 4 * ((c * ct.hb + i) * ct.wb + j);
-    }
-  }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&s.tmem)),
@@ -1208,158 +1165,21 @@ __global__ void __launch_bounds__(kConv ? kConvThreads : kSBThreads, 1)
   volatile int *failed = &s.failed;
   pdl_launch_dependents();
   pdl_wait();
-  // Warps 0 and 18 produce, warps 1 and 19 issue MMAs; issuer q takes the
-  // crossbar tiles gi with gi % kIssuers == q of the CTA's sequence. kConv:
-  // warps 0 and 1 alone, warps 18 to 21 prepare.
-  constexpr int kEpiEnd = 2 + kEpiWarps;
-  const int role_q = warp >= kEpiEnd ? (warp - kEpiEnd) / 2 + 1 : 0;
-  const bool producer =
-      lane == 0 && (warp == 0 || (!kConv && warp >= kEpiEnd && (warp - kEpiEnd) % 2 == 0));
-  const bool issuer =
-      lane == 0 && (warp == 1 || (!kConv && warp >= kEpiEnd && (warp - kEpiEnd) % 2 == 1));
-  static_assert(kStages >= kIssuers && kExSlots % kIssuers == 0 && kTmemBufs % kIssuers == 0,
-                "each issuer steps every ring by kIssuers positions");
 
-  if (kConv && producer) {
-    // Producer of the fused convolution: per crossbar tile the stage's input
-    // window (wfull, for the prepare warps) and the stacked Wp / Wn tile (one
-    // arrival of full, which the prepare warps complete). The stage is free
-    // once the MMAs of its previous tile have completed (empty).
-    uint32_t it = 0, stage = 0, sphase = 0;
-    bool ok = true;
-    for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
-      const int m0 = ot * kSBM; // one lane block: tile ot is row block ot
-      const int n0 = fdiv(m0, ct.div_hw);
-      const int ih0 = ct.hw >= kSBM ? fdiv(m0 - n0 * ct.hw, ct.div_ow) * ct.SH - ct.PH : -ct.PH;
-      for (int t = 0; t < T; ++t, ++it) {
-        if (!mbar_wait(&s.empty[stage], sphase ^ 1)) {
-          ok = false;
-          break;
-        }
-        mbar_expect_tx(&s.wfull[stage], static_cast<uint32_t>(ct.words) * 4u);
-        tma_load_4d(win_ring + stage * ct.stage_floats, &tmX, &s.wfull[stage], ct.x0, ih0,
-                    fdiv(t * kTileK, ct.div_khw), n0);
-        mbar_expect_tx(&s.full[stage], Shape::kBTile * 2);
-        tma_load_2d(s.b[stage], &tmB, &s.full[stage], t * 64, 0);
-        tma_load_2d(s.b[stage] + L * 64, &tmB, &s.full[stage], t * 64, n_pad);
-        if (++stage == kStages) {
-          stage = 0;
-          sphase ^= 1;
-        }
-      }
-    }
-    if (!ok)
-      *failed = 1;
-    // Never leave with copies in flight: the last kStages tiles' windows and
-    // weight tiles (older ones completed before their stage was refilled).
-    for (uint32_t i = it > static_cast<uint32_t>(kStages) ? it - kStages : 0; i < it; ++i) {
-      mbar_wait(&s.wfull[i % kStages], (i / kStages) & 1);
-      mbar_wait(&s.full[i % kStages], (i / kStages) & 1);
-    }
-  } else if (kConv && warp >= kEpiEnd) {
-    // Prepare warps: thread r of the 128 builds row r of each crossbar tile
-    // (column m0 + r) from the staged window, as prepare_nchw_box_kernel
-    // does, into the stage's operand tile and the exponent ring.
-    const int pw = warp - kEpiEnd;
-    const int r = pw * 32 + lane;
-    uint32_t stage = 0, sphase = 0, slot = 0, xphase = 0;
-    const int khw = ct.KH * ct.KW;
-    bool ok = true;
-    for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
-      const int m0 = ot * kSBM, m = m0 + r;
-      const int n0 = fdiv(m0, ct.div_hw);
-      const int ih0 = ct.hw >= kSBM ? fdiv(m0 - n0 * ct.hw, ct.div_ow) * ct.SH - ct.PH : -ct.PH;
-      // The column's window origin within a stage (columns past M: zeros).
-      uint32_t origin = 0;
-      if (m < M) {
-        const int n = fdiv(m, ct.div_hw);
-        const int rm = m - n * ct.hw;
-        const int oh = fdiv(rm, ct.div_ow);
-        const int ow = rm - oh * ct.OW;
-        origin = 4u * static_cast<uint32_t>(
-                          ((n - n0) * ct.cb * ct.hb + (oh * ct.SH - ct.PH - ih0)) * ct.wb +
-                          (ow * ct.SW - ct.PW - ct.x0));
-      }
-      for (int t = 0; t < T; ++t) {
-        if (!mbar_wait(&s.wfull[stage], sphase) || !mbar_wait(&s.exempty[slot], xphase ^ 1)) {
-          ok = false;
-          break;
-        }
-        const int kbeg = t * kTileK;
-        uint32_t signed_pairs[32];
-        uint32_t raw_max = 0;
-        if (m < M) {
-          const uint32_t base = smem_u32(win_ring + stage * ct.stage_floats) + origin;
-          const int *rel = rel_table + (kbeg - fdiv(kbeg, ct.div_khw) * khw) * kTileK;
-          const int kv = ct.K - kbeg; // elements of this tile below K
-          auto convert4 = [&](int e4, float v0, float v1, float v2, float v3) {
-            const __nv_bfloat162 h0 = __floats2bfloat162_rn(v0, v1);
-            const __nv_bfloat162 h1 = __floats2bfloat162_rn(v2, v3);
-            signed_pairs[e4 / 2] = *reinterpret_cast<const uint32_t *>(&h0);
-            signed_pairs[e4 / 2 + 1] = *reinterpret_cast<const uint32_t *>(&h1);
-            raw_max = __vmaxu2(raw_max, __vmaxu2(signed_pairs[e4 / 2], signed_pairs[e4 / 2 + 1]));
-          };
-          if (kv >= kTileK) {
-#pragma unroll
-            for (int e4 = 0; e4 < kTileK; e4 += 4) {
-              const int4 r4 = *reinterpret_cast<const int4 *>(&rel[e4]);
-              convert4(e4, lds_f32(base + r4.x), lds_f32(base + r4.y), lds_f32(base + r4.z),
-                       lds_f32(base + r4.w));
-            }
-          } else {
-#pragma unroll
-            for (int e4 = 0; e4 < kTileK; e4 += 4) {
-              const int4 r4 = *reinterpret_cast<const int4 *>(&rel[e4]);
-              convert4(e4, e4 < kv ? lds_f32(base + r4.x) : 0.0f,
-                       e4 + 1 < kv ? lds_f32(base + r4.y) : 0.0f,
-                       e4 + 2 < kv ? lds_f32(base + r4.z) : 0.0f,
-                       e4 + 3 < kv ? lds_f32(base + r4.w) : 0.0f);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < 32; ++q)
-            signed_pairs[q] = 0; // a column past M: an all-zero group
-        }
-        finish_group<1, true, kStoreOperand>(
-            signed_pairs, raw_max, status, nullptr, s.exa[slot][0], 0, 0, 0, t, r, kbeg, ex_lo,
-            ex_hi, reinterpret_cast<uint8_t *>(s.a[stage][0]) + pw * 32 * 128);
-        // The rows are read by the tensor cores (async proxy).
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&s.full[stage]);
-          mbar_arrive(&s.exfull[slot]);
-        }
-        if (++stage == kStages) {
-          stage = 0;
-          sphase ^= 1;
-        }
-        if (++slot == kExSlots) {
-          slot = 0;
-          xphase ^= 1;
-        }
-      }
-    }
-    if (!ok)
-      *failed = 1;
-  } else if (producer) {
+  if (warp == 0 && lane == 0) {
     // TMA producer: per crossbar tile the activation tile of each branch
     // and the stacked Wp / Wn tile into the stage ring, the tile's activation
     // exponents of the 128 rows into the exponent ring.
-    // Ring positions and phase parities advance incrementally by the number
-    // of producers: the per-tile instruction chain of this thread (not the
-    // copies) is on the kernel's critical path. A failure elsewhere shows up
-    // as a bounded wait that runs out.
-    const uint32_t q = static_cast<uint32_t>(role_q);
-    uint32_t it = 0, stage = q, sphase = 0, slot = q, xphase = 0;
+    // Ring positions and phase parities advance incrementally: this thread
+    // is the ring's only producer, and its per-tile instruction chain (not
+    // the copies) is on the kernel's critical path. A failure elsewhere
+    // shows up as a bounded wait that runs out.
+    uint32_t it = 0, stage = 0, sphase = 0, slot = 0, xphase = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
       const int mb = fdiv(ot, div_nb);
       const int m0 = mb * kSBM, nb = ot - mb * num_nb, n0 = nb * L;
       for (int t = 0; t < T; ++t, ++it) {
-        if (it % kIssuers != q)
-          continue;
         if (!mbar_wait(&s.empty[stage], sphase ^ 1) ||
             !mbar_wait(&s.exempty[slot], xphase ^ 1)) {
           ok = false;
@@ -1376,46 +1196,36 @@ __global__ void __launch_bounds__(kConv ? kConvThreads : kSBThreads, 1)
         for (int a = 0; a < kAB; ++a)
           bulk_load(s.exa[slot][a], exA + (static_cast<int64_t>(a) * T + t) * m_pad + m0,
                     kSBM * 4, &s.exfull[slot]);
-        if ((stage += kIssuers) >= kStages) {
-          stage -= kStages;
+        if (++stage == kStages) {
+          stage = 0;
           sphase ^= 1;
         }
-        if ((slot += kIssuers) >= kExSlots) {
-          slot -= kExSlots;
+        if (++slot == kExSlots) {
+          slot = 0;
           xphase ^= 1;
         }
       }
     }
     if (!ok)
       *failed = 1;
-    // Never leave with copies in flight: wait (bounded) for this thread's
-    // fills among the last kStages tiles of the sequence it walked (`it`
-    // tiles; a wait that failed filled none). Older fills completed before
-    // their stage was refilled. The window is the sequence's, not this
-    // thread's own last kStages fills: with an odd stage count the other
-    // producer refills this thread's older stages, and a parity wait on a
-    // stage filled twice since would not end.
+    // Never leave with copies in flight: wait (bounded) for the last use of
+    // every stage and exponent slot this thread filled (`it` counts the
+    // filled tiles; a wait that failed filled none).
     for (uint32_t i = it > static_cast<uint32_t>(kStages) ? it - kStages : 0; i < it; ++i)
-      if (i % kIssuers == q)
-        mbar_wait(&s.full[i % kStages], (i / kStages) & 1);
+      mbar_wait(&s.full[i % kStages], (i / kStages) & 1);
     for (uint32_t i = it > static_cast<uint32_t>(kExSlots) ? it - kExSlots : 0; i < it; ++i)
-      if (i % kIssuers == q)
-        mbar_wait(&s.exfull[i % kExSlots], (i / kExSlots) & 1);
-  } else if (issuer) {
+      mbar_wait(&s.exfull[i % kExSlots], (i / kExSlots) & 1);
+  } else if (warp == 1 && lane == 0) {
     // MMA issuer: four K=16 MMAs per activation branch and crossbar tile.
     // The critical path of the kernel: ring positions advance incrementally
-    // and the descriptors step by constant strides. Issuer q owns the TMEM
-    // buffers b with b % kIssuers == q.
+    // and the descriptors step by constant strides.
     constexpr uint32_t idesc = idesc_bf16(kSBM, SN);
     constexpr uint64_t kAStep = sizeof(s.a[0]) >> 4, kBStep = sizeof(s.b[0]) >> 4;
     const uint64_t adesc0 = sw128_desc(s.a[0][0]), bdesc0 = sw128_desc(s.b[0]);
-    const uint32_t q = static_cast<uint32_t>(role_q);
-    uint32_t gi = 0, stage = q, sphase = 0, buf = q, dphase = 0, issued = 0;
+    uint32_t gi = 0, stage = 0, sphase = 0, buf = 0, dphase = 0;
     bool ok = true;
     for (int ot = blockIdx.x; ot < num_tiles && ok; ot += gridDim.x) {
       for (int t = 0; t < T; ++t, ++gi) {
-        if (gi % kIssuers != q)
-          continue;
         if (!mbar_wait(&s.full[stage], sphase) || !mbar_wait(&s.dempty[buf], dphase ^ 1)) {
           ok = false;
           break;
@@ -1432,24 +1242,22 @@ __global__ void __launch_bounds__(kConv ? kConvThreads : kSBThreads, 1)
         }
         mma_commit(&s.dfull[buf]);
         mma_commit(&s.empty[stage]);
-        issued = gi + 1;
-        if ((stage += kIssuers) >= kStages) {
-          stage -= kStages;
+        if (++stage == kStages) {
+          stage = 0;
           sphase ^= 1;
         }
-        if ((buf += kIssuers) >= kTmemBufs) {
-          buf -= kTmemBufs;
+        if (++buf == kTmemBufs) {
+          buf = 0;
           dphase ^= 1;
         }
       }
     }
     if (!ok)
       *failed = 1;
-    // Let this thread's last MMAs land before TMEM is freed (its commit
-    // covers every MMA it issued).
-    if (issued > 0)
-      mbar_wait(&s.dfull[(issued - 1) % kTmemBufs], ((issued - 1) / kTmemBufs) & 1);
-  } else if (warp >= 2 && warp < kEpiEnd) {
+    // Let the last MMAs land before TMEM is freed.
+    if (gi > 0)
+      mbar_wait(&s.dfull[(gi - 1) % kTmemBufs], ((gi - 1) / kTmemBufs) & 1);
+  } else if (warp >= 2) {
     // Epilogue.
     const int quad = warp % 4, sub = (warp - 2) / 4;
     const int row_local = quad * 32 + lane;
@@ -1973,20 +1781,9 @@ bool launch_signsplit(const int8_t *A, const int32_t *exA, int64_t m_pad, const 
   return true;
 }
 
-template <int kAB, bool kRes, bool kConv = false> constexpr size_t smem_sb() {
-  return sizeof(SmemSB<kAB, kRes, kConv>) + 1024;
+template <int kAB, bool kRes> constexpr size_t smem_sb() {
+  return sizeof(SmemSB<kAB, kRes>) + 1024;
 }
-
-// The fused convolution's shared memory: the struct, then the window ring
-// and the window offset table of every kernel phase (KH * KW <= 25).
-constexpr int kConvMaxTaps = 25;
-constexpr int kConvTableInts = kConvMaxTaps * kTileK;
-template <bool kRes> constexpr size_t smem_conv() {
-  return smem_sb<1, kRes, true>() + (SBShape<1, kRes, true>::kStages * kConvWindowFloats +
-                                     kConvTableInts) * 4;
-}
-static_assert(smem_conv<false>() <= 232448 && smem_conv<true>() <= 232448,
-              "the fused convolution's rings must fit 227 KB of shared memory per CTA");
 static_assert(smem_sb<1, false>() <= 232448 && smem_sb<2, false>() <= 232448 &&
                   smem_sb<1, true>() <= 232448 && smem_sb<2, true>() <= 232448,
               "the BF16 operand ring must fit the 227 KB of dynamic shared memory per CTA");
@@ -2054,12 +1851,12 @@ bool launch_signsplit_b16(const uint16_t *A, const int32_t *exA, int64_t m_pad,
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
       return false;
-    launch_pdl(kernel, grid, kSBThreads, smem, stream, ta, tb, exA, static_cast<int>(m_pad), exB,
+    launch_pdl(kernel, grid, kSThreads, smem, stream, ta, tb, exA, static_cast<int>(m_pad), exB,
                static_cast<int>(n_pad), T, static_cast<int>(M), static_cast<int>(N), ex_lo,
                ex_hi, make_fastdiv(static_cast<uint32_t>((N + L - 1) / L)), bias, post_scale,
                post_shift, residual, act, vec, static_cast<int>(out_pixels),
                make_fastdiv(static_cast<uint32_t>(out_pixels > 0 ? out_pixels : 1)), y, status,
-               peer ? *peers : none, peer_vec4, tr, res_bp, tr, ConvTile{});
+               peer ? *peers : none, peer_vec4, tr, res_bp);
     return true;
   };
   const bool res = residual != nullptr;
@@ -2074,119 +1871,6 @@ bool launch_signsplit_b16(const uint16_t *A, const int32_t *exA, int64_t m_pad,
                           : launch(signsplit_b16_kernel<2, false, false>, smem_sb<2, false>()))
                    : (res ? launch(signsplit_b16_kernel<1, true, false>, smem_sb<1, true>())
                           : launch(signsplit_b16_kernel<1, false, false>, smem_sb<1, false>()));
-  if (!launched)
-    return false;
-  g_tc_launches.fetch_add(1, std::memory_order_relaxed);
-  return true;
-}
-
-bool plan_conv_tile(int W, int H, int C, int images, int OH, int OW, int KH, int KW, int S,
-                    int P, int K, int T, int64_t M, int64_t N, const float *x, ConvTile &ct) {
-  const int64_t hw = int64_t{OH} * OW;
-  if (N > SSShape<1>::L || N <= 8 || (W & 3) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) ||
-      S < 1 || P < 0 || KH < 1 || KW < 1 || KH * KW > kConvMaxTaps || M != hw * images ||
-      M >= (int64_t{1} << 31) - kSBM || K != C * KH * KW || T != (K + kTileK - 1) / kTileK)
-    return false;
-  ct = ConvTile{};
-  if (hw >= kSBM) {
-    if (kSBM % OW != 0 || hw % kSBM != 0)
-      return false;
-    ct.nb = 1;
-    ct.hb = (kSBM / OW - 1) * S + KH;
-  } else {
-    if (kSBM % hw != 0)
-      return false;
-    ct.nb = static_cast<int>(kSBM / hw);
-    ct.hb = (OH - 1) * S + KH;
-  }
-  ct.x0 = -((P + 3) / 4) * 4;
-  ct.wb = (((OW - 1) * S - P + KW - ct.x0) + 3) / 4 * 4;
-  const int khw = KH * KW;
-  ct.cb = 0;
-  for (int t = 0; t < T; ++t) {
-    const int lo = t * kTileK / khw, hi = std::min(C - 1, (t * kTileK + kTileK - 1) / khw);
-    ct.cb = std::max(ct.cb, hi - lo + 1);
-  }
-  if (ct.wb > 256 || ct.hb > 256 || ct.cb > 256 || ct.nb > 256)
-    return false;
-  const int64_t words = int64_t{ct.wb} * ct.hb * ct.cb * ct.nb;
-  if (words > kConvWindowFloats)
-    return false;
-  ct.words = static_cast<int>(words);
-  ct.stage_floats = (ct.words + 31) / 32 * 32;
-  ct.W = W;
-  ct.H = H;
-  ct.C = C;
-  ct.images = images;
-  ct.OW = OW;
-  ct.hw = static_cast<int>(hw);
-  ct.SH = ct.SW = S;
-  ct.PH = ct.PW = P;
-  ct.KH = KH;
-  ct.KW = KW;
-  ct.K = K;
-  ct.div_ow = make_fastdiv(static_cast<uint32_t>(OW));
-  ct.div_hw = make_fastdiv(static_cast<uint32_t>(hw));
-  ct.div_khw = make_fastdiv(static_cast<uint32_t>(khw));
-  return true;
-}
-
-bool launch_signsplit_b16_conv(const float *x, const ConvTile &ct, const uint16_t *B,
-                               const int32_t *exB, int64_t n_pad, int64_t k_pad, int T,
-                               int64_t M, int64_t N, int ex_lo, int ex_hi, const float *bias,
-                               const float *post_scale, const float *post_shift,
-                               const float *residual, int act, int64_t out_pixels, float *y,
-                               int32_t *status, cudaStream_t stream) {
-  constexpr int L = SSShape<1>::L;
-  if (M < 1 || N <= 8 || N > L || n_pad % 128 || k_pad % 64 || ex_lo > ex_hi ||
-      int64_t{T} * kTileK > k_pad || ct.words < 1 || ct.words > kConvWindowFloats ||
-      ct.KH * ct.KW > kConvMaxTaps || (reinterpret_cast<uintptr_t>(B) & 15) ||
-      (reinterpret_cast<uintptr_t>(exB) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
-    return false;
-  CUtensorMap tb, tx;
-  if (!encode_bf16_2d(&tb, B, 2 * n_pad, k_pad, static_cast<uint32_t>(L)) ||
-      !encode_nchw_box(&tx, x, ct.W, ct.H, ct.C, ct.images, ct.wb, ct.hb, ct.cb, ct.nb))
-    return false;
-  const int vec = (N % 4 == 0 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0 ? 1 : 0) |
-                  (N % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 ? 2 : 0);
-  // Residual addends by TMA, as launch_signsplit_b16 loads them.
-  CUtensorMap tr{};
-  int res_bp = 0;
-  if (residual != nullptr && out_pixels > 0 && out_pixels % 4 == 0 && M % out_pixels == 0 &&
-      (out_pixels % kSBM == 0 || kSBM % out_pixels == 0) &&
-      (reinterpret_cast<uintptr_t>(residual) & 15) == 0) {
-    auto fn = encode_fn();
-    const uint32_t bp = static_cast<uint32_t>(std::min<int64_t>(out_pixels, kSBM));
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(out_pixels), static_cast<cuuint64_t>(N),
-                                static_cast<cuuint64_t>(M / out_pixels)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(out_pixels) * 4,
-                                   static_cast<cuuint64_t>(N * out_pixels) * 4};
-    const cuuint32_t box[3] = {bp, static_cast<cuuint32_t>(L), kSBM / bp};
-    const cuuint32_t elem[3] = {1, 1, 1};
-    if (fn && fn(&tr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(residual), dims,
-                 strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                 CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
-      res_bp = static_cast<int>(bp);
-  }
-  const int64_t tiles = (M + kSBM - 1) / kSBM;
-  const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, sm_count())));
-  cim22_peer_outputs none{};
-  auto launch = [&](auto kernel, size_t smem) {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-      return false;
-    launch_pdl(kernel, grid, kConvThreads, smem, stream, tx, tb, nullptr, 0, exB,
-               static_cast<int>(n_pad), T, static_cast<int>(M), static_cast<int>(N), ex_lo, ex_hi,
-               make_fastdiv(1u), bias, post_scale, post_shift, residual, act, vec,
-               static_cast<int>(out_pixels),
-               make_fastdiv(static_cast<uint32_t>(out_pixels > 0 ? out_pixels : 1)), y, status,
-               none, 0, tr, res_bp, tx, ct);
-    return true;
-  };
-  const bool launched = residual != nullptr
-                            ? launch(signsplit_b16_kernel<1, true, false, true>, smem_conv<true>())
-                            : launch(signsplit_b16_kernel<1, false, false, true>, smem_conv<false>());
   if (!launched)
     return false;
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);

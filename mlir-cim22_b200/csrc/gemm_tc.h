@@ -6,7 +6,6 @@
 #include <cuda_runtime.h>
 
 #include "../../include/cim22_cuda.h"
-#include "cim_internal.h"
 
 namespace cim::tc {
 
@@ -67,46 +66,6 @@ bool launch_signsplit_b16(const uint16_t *A, const int32_t *exA, int64_t m_pad,
                           const float *residual, int act, int act_branches, int64_t out_pixels,
                           float *y, int32_t *status, cudaStream_t stream,
                           const cim22_peer_outputs *peers = nullptr);
-
-// A convolution whose activation tiles the contraction with BF16 operands
-// prepares itself: f32 NCHW input [images][C][H][W] (W % 4 == 0, 16-byte
-// aligned), 128-column output tiles that cover 128 / OW whole output rows of
-// one image or 128 / hw whole images; the input window that the 64 K
-// elements of one crossbar tile read in one output tile is one TMA box
-// [nb][cb][hb][wb] from (x0, first input row, first channel, first image),
-// with the padding read as +0.
-struct ConvTile {
-  int W, H, C, images;     // input extents
-  int wb, hb, cb, nb;      // window box extents: columns, rows, channels, images
-  int x0;                  // first box column (a multiple of 4, <= -PW)
-  int words;               // wb * hb * cb * nb
-  int stage_floats;        // one window stage: words rounded up to 32 floats
-  int OW, hw, SH, SW, PH, PW, KH, KW, K;
-  FastDiv div_ow, div_hw, div_khw;
-};
-
-// Largest window stage of the fused convolution contraction, in floats.
-constexpr int kConvWindowFloats = 2048;
-
-// Whether a convolution of this geometry can run as
-// launch_signsplit_b16_conv (fills ct): NCHW f32 input, no fused pool, more
-// than 8 and at most 64 lanes (one lane block), tiles of whole output rows
-// or images, at most 25 kernel taps.
-bool plan_conv_tile(int W, int H, int C, int images, int OH, int OW, int KH, int KW, int S,
-                    int P, int K, int T, int64_t M, int64_t N, const float *x, ConvTile &ct);
-
-// launch_signsplit_b16 for a 2-branch convolution whose activation tiles are
-// prepared inside the kernel from the input x (no prepare kernel, no
-// prepared columns in global memory): per crossbar tile four warps gather
-// the window, round to BF16, take the group maxima and ExpPrealign, and
-// write the scaled BF16 operand values straight into the tile's
-// shared-memory stage (the operand window is the layer's ex_lo..ex_hi).
-bool launch_signsplit_b16_conv(const float *x, const ConvTile &ct, const uint16_t *B,
-                               const int32_t *exB, int64_t n_pad, int64_t k_pad, int T,
-                               int64_t M, int64_t N, int ex_lo, int ex_hi, const float *bias,
-                               const float *post_scale, const float *post_shift,
-                               const float *residual, int act, int64_t out_pixels, float *y,
-                               int32_t *status, cudaStream_t stream);
 
 // INT8 contraction with whole-K int32 accumulation (exact: range-proven
 // layers, or unproven ones computed as the Host computes them).

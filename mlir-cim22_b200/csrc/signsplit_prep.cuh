@@ -1,14 +1,12 @@
 // signsplit_prep.cuh - device routines shared by the sign-split layer
-// kernels (layers.cu), the contraction that prepares its own operand tiles
-// (gemm_tc.cu) and the fused layer-chain kernel (chain.cu): the 8-thread group
-// preparation of activations (split, RNE to BF16, group maximum,
-// ExpPrealign), the thread-per-group finish of a prepared group and its
-// stores, the exact slow restore of one tile and the epilogue activations.
+// kernels (layers.cu) and the fused layer-chain kernel (chain.cu): the
+// 8-thread group preparation of activations (split, RNE to BF16, group
+// maximum, ExpPrealign), the exact slow restore of one tile and the
+// epilogue activations.
 #pragma once
 
 #include "cim_internal.h"
 #include "cim_numeric.cuh"
-#include "tma_util.cuh"
 
 #include <cuda_bf16.h>
 
@@ -286,182 +284,6 @@ __device__ __noinline__ float slow_tile_add(float acc, int p, int ew, int ex, in
   if (tile == kBF16Inf)
     atomicOr(status, CIM22_STATUS_TILE_OVERFLOW);
   return __fadd_rn(acc, bf16_to_f32(tile));
-}
-
-// Branch a of two signed BF16 halves, sign cleared: for a 2-branch layer the
-// value itself (its sign is flagged separately); for a 4-branch layer xp =
-// max(v, 0) (a = 0) or xn = max(-v, 0) (a = 1).
-template <int kActBranches>
-__device__ __forceinline__ uint32_t branch_pair(uint32_t pair, int a) {
-  if (kActBranches == 1)
-    return pair & 0x7fff7fffu;
-  const uint32_t neg = ((pair >> 15) & 0x00010001u) * 0xffffu; // halves with the sign set
-  return (a == 0 ? pair & ~neg : pair & neg) & 0x7fff7fffu;
-}
-
-// The rest of one (column m, K tile t) group once its 64 signed BF16 pairs
-// and raw maximum are known: branch maxima, the non-finite and
-// negative-input flags, ExpPrealign, the group exponent and the prepared
-// group of each branch - 64 aligned int8 mantissas (four 16-byte stores), or
-// with kB16 the 64 scaled BF16 operand values (eight 16-byte stores; scaled
-// for groups whose exponent lies in [win_lo, win_hi], unscaled otherwise).
-// kStore: where the prepared group goes.
-//   kStoreGlobal  16-byte stores into A (the workspace), the exponent into ex
-//   kStoreStaged  the warp's 32 columns (consecutive, all in the call) are
-//                 written into the warp's shared-memory tile `stage` (per
-//                 branch 32 rows of 64 or 128 bytes, 16-byte chunks swizzled
-//                 as `omap` describes) and leave with one TMA store per
-//                 branch, so that whole lines reach global memory
-//   kStoreOperand the same swizzled rows, left in shared memory as the warp's
-//                 32 rows of a contraction's 128-row operand tile (1-branch
-//                 BF16 operands, 128-byte swizzle); the exponent goes to
-//                 ex[m] (a shared-memory ring slot). The caller fences the
-//                 writes for the tensor cores (async proxy) and signals them.
-constexpr int kStoreGlobal = 0, kStoreStaged = 1, kStoreOperand = 2;
-
-template <int kActBranches, bool kB16 = false, int kStore = kStoreGlobal>
-__device__ __forceinline__ void finish_group(const uint32_t (&signed_pairs)[32],
-                                             uint32_t raw_max, int32_t *status,
-                                             int8_t *__restrict__ A, int32_t *__restrict__ ex,
-                                             int m_pad, int k_pad, int T, int t, int m,
-                                             int kbeg, int win_lo = 1, int win_hi = 0,
-                                             uint8_t *stage = nullptr,
-                                             const CUtensorMap *omap = nullptr) {
-  constexpr bool kStaged = kStore == kStoreStaged;
-  constexpr bool kShared = kStore != kStoreGlobal;
-  static_assert(kStore != kStoreOperand || (kActBranches == 1 && kB16),
-                "operand tiles hold one branch of BF16 operand values");
-  constexpr int kRowBytes = kB16 ? 128 : 64;
-  const int lane = static_cast<int>(threadIdx.x & 31);
-  if constexpr (kStaged) {
-    // The tile's previous stores must have read it before it is rewritten.
-    if (lane == 0)
-      bulk_wait_read();
-    __syncwarp();
-  }
-  uint32_t mx[2] = {0, 0};
-  // A 2-branch layer whose BF16 inputs carry no sign bit (the usual case:
-  // the layer reads a ReLU output) has the raw maximum as its maximum; a -0
-  // or a negative input takes the loop over the cleared magnitudes.
-  const uint32_t raw_half = max(raw_max & 0xffffu, raw_max >> 16);
-  if (kActBranches == 1 && raw_half < 0x8000u) {
-    mx[0] = raw_half;
-  } else {
-#pragma unroll
-    for (int a = 0; a < kActBranches; ++a) {
-      uint32_t m2 = 0;
-#pragma unroll
-      for (int e = 0; e < 32; ++e)
-        m2 = __vmaxu2(m2, branch_pair<kActBranches>(signed_pairs[e], a));
-      mx[a] = max(m2 & 0xffffu, m2 >> 16);
-    }
-  }
-  // Non-finite groups: BF16 exponent 0xff in a branch maximum (the two
-  // branches of a 4-branch layer hold every magnitude between them, NaNs
-  // included). A 2-branch layer flags a negative nonzero BF16 input, the
-  // reference's sign-split rejection (-0 is cleared to +0).
-  const bool nonfinite = max(mx[0], mx[1]) >= 0x7f80u;
-  if (nonfinite)
-    atomicOr(status, CIM22_STATUS_INPUT_NOT_FINITE);
-  else if (kActBranches == 1 && raw_half > 0x8000u)
-    atomicOr(status, CIM22_STATUS_NEGATIVE_INPUT);
-  // Pass 2: align and store.
-  constexpr int kWords = kB16 ? 32 : 16;
-#pragma unroll
-  for (int a = 0; a < kActBranches; ++a) {
-    const bool zero = mx[a] == 0 || nonfinite;
-    const int emax = zero ? kZeroGroup : effective_exponent(static_cast<uint16_t>(mx[a]));
-    uint32_t out[kWords];
-    if (zero) {
-#pragma unroll
-      for (int q = 0; q < kWords; ++q)
-        out[q] = 0;
-    } else if ((mx[a] >> 7) >= 8) {
-      const float scale = __uint_as_float(static_cast<uint32_t>(260 - emax) << 23);
-      const uint64_t scale2 = (static_cast<uint64_t>(__float_as_uint(scale)) << 32) |
-                              __float_as_uint(scale);
-      const uint64_t magic2 = 0x4b0000004b000000ull; // 2^23 in both halves
-      uint64_t s2 = 0, off2 = 0;
-      if (kB16)
-        operand_scale(emax, win_lo, win_hi, s2, off2);
-      // A 2-branch layer aligns the raw halves: -0 aligns to 0 as +0 does,
-      // and a negative nonzero input has failed the call already.
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        uint32_t r[4];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t pk = kActBranches == 1
-                                  ? signed_pairs[2 * q + h]
-                                  : branch_pair<kActBranches>(signed_pairs[2 * q + h], a);
-          // Both halves in one packed f32x2 fma (each half rounds toward zero
-          // as __fmaf_rz).
-          asm("{\n\t.reg .b64 a, d;\n\tmov.b64 a, {%2, %3};\n\t"
-              "fma.rz.f32x2 d, a, %4, %5;\n\tmov.b64 {%0, %1}, d;\n\t}"
-              : "=r"(r[2 * h]), "=r"(r[2 * h + 1])
-              : "r"(pk << 16), "r"(pk & 0xffff0000u), "l"(scale2), "l"(magic2));
-        }
-        if constexpr (kB16) {
-          const uint2 w = scale_pairs(r, s2, off2);
-          out[2 * q] = w.x;
-          out[2 * q + 1] = w.y;
-        } else {
-          out[q] = pack_low_bytes(r[0], r[1], r[2], r[3]);
-        }
-      }
-    } else {
-      // Tiny maxima (exponent < 8): exact alignment; with kB16 the unscaled
-      // mantissas (such a group is outside every window).
-      const int shift = 127 - emax;
-      for (int q = 0; q < 16; ++q) {
-        uint32_t bytes[4];
-        for (int h = 0; h < 4; ++h)
-          bytes[h] = slow_align((branch_pair<kActBranches>(signed_pairs[2 * q + h / 2], a) >>
-                                 (16 * (h & 1))) & 0xffffu,
-                                shift);
-        if constexpr (kB16) {
-          out[2 * q] = static_cast<uint32_t>(f32_to_bf16(static_cast<float>(bytes[0]))) |
-                       (static_cast<uint32_t>(f32_to_bf16(static_cast<float>(bytes[1]))) << 16);
-          out[2 * q + 1] =
-              static_cast<uint32_t>(f32_to_bf16(static_cast<float>(bytes[2]))) |
-              (static_cast<uint32_t>(f32_to_bf16(static_cast<float>(bytes[3]))) << 16);
-        } else {
-          out[q] = bytes[0] | (bytes[1] << 8) | (bytes[2] << 16) | (bytes[3] << 24);
-        }
-      }
-    }
-    if constexpr (kShared) {
-      // Row `lane` of the branch's tile; chunk q at q ^ (the swizzle's row
-      // bits): lane & 7 for 128-byte rows, (lane >> 1) & 3 for 64-byte rows.
-      uint8_t *row = stage + (a * 32 + lane) * kRowBytes;
-      const int swz = kB16 ? (lane & 7) : ((lane >> 1) & 3);
-#pragma unroll
-      for (int q = 0; q < kWords / 4; ++q)
-        *reinterpret_cast<uint4 *>(row + ((q ^ swz) << 4)) =
-            make_uint4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
-    } else {
-      constexpr int kElemBytes = kB16 ? 2 : 1;
-      uint4 *dst = reinterpret_cast<uint4 *>(
-          A + ((static_cast<int64_t>(a) * m_pad + m) * k_pad + kbeg) * kElemBytes);
-#pragma unroll
-      for (int q = 0; q < kWords / 4; ++q)
-        dst[q] = make_uint4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
-    }
-    if constexpr (kStore == kStoreOperand)
-      ex[m] = emax;
-    else
-      ex[(static_cast<int64_t>(a) * T + t) * m_pad + m] = emax;
-  }
-  if constexpr (kStaged) {
-    fence_proxy_async();
-    __syncwarp();
-    if (lane == 0) {
-#pragma unroll
-      for (int a = 0; a < kActBranches; ++a)
-        tma_store_2d(omap, stage + a * 32 * kRowBytes, kbeg, a * m_pad + (m - lane));
-      bulk_commit();
-    }
-  }
 }
 
 } // namespace
