@@ -1063,8 +1063,7 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64
 // Add one (activation branch, weight sign) slice of a crossbar tile to the
 // branch sums: q = v with its low 16 bits cleared, acc += q (the sums start
 // at +0 for each output tile). kPacked: two lanes per packed f32x2 add, each
-// half rounding as the scalar f32 add (measured faster for 4-branch tiles,
-// slower for 2-branch ones).
+// half rounding as the scalar f32 add.
 template <int kLT, bool kPacked>
 __device__ __forceinline__ void restore_b16(float (&acc)[kLT], const uint32_t (&v)[kLT]) {
   static_assert(kLT % 2 == 0, "lanes come in pairs");
@@ -1322,16 +1321,38 @@ __global__ void __launch_bounds__(kSThreads, 1)
         const uint32_t col0 = tmem + tlane + buf * kBufCols + sub * LT;
         if constexpr (kAB == 1) {
           const bool any_raw = __any_sync(0xffffffffu, raw[0]);
+          if (any_raw) {
 #pragma unroll
-          for (int w = 0; w < 2; ++w) {
-            uint32_t v[LT];
-            tmem_ld_wait(col0 + w * L, v);
-            if (any_raw)
+            for (int w = 0; w < 2; ++w) {
+              uint32_t v[LT];
+              tmem_ld_wait(col0 + w * L, v);
               restore_b16_raw<LT>(acc[0][w], v, raw[0], exB,
                                   (static_cast<int64_t>(w) * T + t) * n_pad + lane0, ex[0],
                                   status);
-            else
-              restore_b16<LT, false>(acc[0][w], v);
+            }
+          } else {
+            // Both weight signs' columns in flight before one wait, then
+            // packed adds (with one load and wait per sign the packed form
+            // measured slower than scalar adds).
+            static_assert(LT == 16, "two 8-column halves per weight sign");
+            uint32_t v[2][2][8];
+#pragma unroll
+            for (int w = 0; w < 2; ++w) {
+              tmem_ld(col0 + w * L, v[w][0]);
+              tmem_ld(col0 + w * L + 8, v[w][1]);
+            }
+#pragma unroll
+            for (int w = 0; w < 2; ++w) {
+              tmem_wait(v[w][0]);
+              tmem_wait(v[w][1]);
+            }
+#pragma unroll
+            for (int w = 0; w < 2; ++w)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                float(&a8)[8] = *reinterpret_cast<float(*)[8]>(&acc[0][w][8 * h]);
+                restore_b16<8, true>(a8, v[w][h]);
+              }
           }
         } else {
 #pragma unroll
