@@ -481,10 +481,11 @@ def test_contract_residual_epilogue_bit_exact(f, branches):
 @pytest.mark.parametrize("f,n", [(64, 3), (128, 2)])
 def test_residual_bf16_operand_conv_many_tiles(f, n):
     """A 64-channel 3x3 residual conv (9 crossbar tiles per output tile, BF16
-    operands, 2 branches): the residual instance's odd stage ring is split
-    between two TMA producers. Bit-exact against the oracle, and the launch
-    ends in well under the pipelines' 2 s wait limit (a producer whose exit
-    drain waited on a stage refilled by the other one ran the limit out)."""
+    operands, 2 branches) through the residual instance, whose stage ring has
+    an odd number of stages. Bit-exact against the oracle, and the launch
+    ends in well under the pipelines' 2 s wait limit: an exit drain that
+    waits on a stage parity it will never see shows up as a launch of about
+    2 s, not as a wrong result."""
     from cim22_b200 import abi
     from cim22_b200.cim_ops import CimLayer, StatusWord, Workspace, conv_gather
 
